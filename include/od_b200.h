@@ -1,0 +1,181 @@
+/*
+ * od_b200.h - C ABI of libod_b200.so, the sm_100a kernels of the OpenDecider decision forward pass.
+ *
+ * Conventions (the same as the reference's own ctypes C ABI, deploy/llamacpp/od_llama.cpp:13-23 and
+ * src/opendecider/llamacpp.py:37-52):
+ *   - every entry point returns an int status: OD_OK (0) on success, a negative OD_E* code on error;
+ *     od_last_error() returns a message for the calling thread's last error. No C++ exception crosses the ABI.
+ *   - all pointers are DEVICE pointers unless the name says host; buffers are owned by the caller.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = the legacy default stream). No compute entry point
+ *     synchronises the host or allocates device memory (od_gemm_w8a8 encodes its TMA descriptors on the host and
+ *     passes them as kernel parameters).
+ *   - dtype codes: OD_BF16, OD_F16, OD_F32 (see below).
+ *   - shapes are int64; strides are in ELEMENTS.
+ *
+ * Layouts (the reference's, kept unchanged so the kernels read the reference's buffers as they are):
+ *   int8 weight      qweight (N, K) int8 row-major + scale (N) in the weight dtype  (quant.py:122-127)
+ *   int8 KV cache    q (S, Hkv, T, D) int8 + scale (S, Hkv, T) in the source dtype  (backbone.py:446, quant.py:37-41)
+ *   activations      (M, K) row-major, bf16
+ */
+#ifndef OD_B200_H
+#define OD_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define OD_API __attribute__((visibility("default")))
+#else
+#define OD_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  OD_OK = 0,
+  OD_EINVAL = -1,      /* bad argument (shape, dtype, alignment, null pointer) */
+  OD_ECUDA = -2,       /* a CUDA runtime/driver call failed */
+  OD_EUNSUPPORTED = -3,/* a valid configuration this build does not implement */
+  OD_ETIMEOUT = -4     /* a bounded device-side wait gave up (see od_device_error) */
+};
+
+enum { OD_BF16 = 0, OD_F16 = 1, OD_F32 = 2 };
+
+/* Message of the calling thread's last error ("" if none). */
+OD_API const char* od_last_error(void);
+
+/* Library version string, e.g. "od_b200 0.1 sm_100a". */
+OD_API const char* od_version(void);
+
+/* Device-side error word written by kernels whose bounded waits give up (0 = none). Reads and clears it.
+ * Synchronises `stream`. Not a hot-path call. */
+OD_API int od_device_error(void* stream, int32_t* host_code);
+
+/* ---------------------------------------------------------------------------------------------------------------
+ * A1 / A5 / A6: per-row symmetric int8 quantisation, Int8Tensor.quantize (quant.py:37-41) and the weight quantiser
+ * of Int8Linear.__init__ (quant.py:124-127):
+ *     s = max(max_k |x[m,k]|, 1e-8) / 127   (fp32, IEEE division)
+ *     q = clamp(rint(x / s), -127, 127)     (fp32 IEEE division, round half to even)
+ *     scale[m] = s rounded to `scale_dtype`
+ * x (M, K) of `x_dtype` with row stride ldx (elements). Optional inv_s (K,) bf16: x is first multiplied by inv_s in
+ * bf16 (SmoothedLinear.forward, quant.py:328-329: bf16(x * inv_s)) before quantising.
+ * Replaces: Int8Tensor.quantize, Int8Linear.__init__'s quantiser, and GemLite A8W8's dynamic activation quant.
+ */
+OD_API int od_quant_rows_i8(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, const void* inv_s,
+                     int8_t* q, void* scale, int scale_dtype, void* stream);
+
+/* Row-wise dequantisation, Int8Tensor.dequantize (quant.py:43-45): y = out_dtype(out_dtype(q) * out_dtype(s)).
+ * q (M, K) int8, scale (M) of scale_dtype, y (M, K) of out_dtype. */
+OD_API int od_dequant_rows_i8(const int8_t* q, const void* scale, int scale_dtype, int64_t M, int64_t K,
+                       void* y, int out_dtype, void* stream);
+
+/* ---------------------------------------------------------------------------------------------------------------
+ * A6: int8 KV-cache append. New keys/values k, v of `t` tokens per state, bf16 or fp16, addressed as
+ * k[s*ks_s + j*ks_t + h*ks_h + d] (any strides, d contiguous), are quantised per (state, head, token) over D exactly
+ * as Int8Tensor.quantize and written at token offset t0 of the cache:
+ *     kq[s, h, t0 + j, :], ksc[s, h, t0 + j]    (cache: (S, Hkv, T_cap, D) int8 + (S, Hkv, T_cap) scales)
+ * Scales are stored in the dtype of k/v (as Int8Tensor does). Replaces PackedCache.pack's per-layer
+ * maybe_quantize (backbone.py:446) and PrefixCache._take's new-slice quantisation (state_cache.py:79).
+ */
+OD_API int od_kv_append_i8(const void* k, const void* v, int kv_dtype, int64_t S, int64_t t, int Hkv, int D,
+                    int64_t ks_s, int64_t ks_t, int64_t ks_h, int64_t vs_s, int64_t vs_t, int64_t vs_h,
+                    int8_t* kq, int8_t* vq, void* ksc, void* vsc, int64_t T_cap, int64_t t0, void* stream);
+
+/* ---------------------------------------------------------------------------------------------------------------
+ * A3 + A4 + A5: residual add + Qwen3.5 RMSNorm + (optional SmoothQuant multiply) + per-token int8 quantisation.
+ *     h   = res_in ? bf16(x + res_in) : x                    (decoder residual add, modeling_qwen3_5.py:768/781)
+ *     y   = bf16(float(h) * rsqrt(mean(float(h)^2) + eps) * (1 + float(w)))   (Qwen3_5RMSNorm, :720-725)
+ *     y'  = inv_s ? bf16(y * inv_s) : y                      (SmoothedLinear, quant.py:328-329)
+ *     q,s = quantise(y') as od_quant_rows_i8 with fp32 scales
+ * x, res_in, res_out, y_out: (M, H) bf16. res_out (may alias x) receives h when res_in is given. y_out (optional)
+ * receives y' in bf16. q (M, H) int8 and s (M) fp32 are optional (both or neither).
+ */
+OD_API int od_rmsnorm_res_quant(const void* x, const void* res_in, void* res_out, const void* w, const void* inv_s,
+                         float eps, int64_t M, int H, void* y_out, int8_t* q, float* s, void* stream);
+
+/* ---------------------------------------------------------------------------------------------------------------
+ * A2: W8A8 GEMM on the 5th-generation tensor cores (tcgen05.mma kind::i8, int32 accumulators in TMEM, TMA loads).
+ *     acc[m, n] = sum_k A[m, k] * W[n, k]          (int32, exact)
+ * epilogue OD_EPI_BF16:   Y[m, n] = bf16((float(acc) * sa[m]) * float(sw[n]))            Y (M, N) bf16, ldy = N
+ * epilogue OD_EPI_SWIGLU: W rows are interleaved in blocks of 128 (gate_0..127, up_0..127, gate_128.., ...);
+ *                         g = bf16(acc_gate...), u = bf16(acc_up...), Y[m, j] = bf16(bf16(silu(g)) * u)
+ *                         (Qwen3_5MLP.forward: act_fn(gate_proj(x)) * up_proj(x)), Y (M, N/2) bf16
+ * epilogue OD_EPI_INT32:  Y[m, n] = acc (int32) - the bit-exact parity mode
+ * A (M, K) int8 row-major, sa (M) fp32 (per-token activation scales), W (N, K) int8 row-major (Int8Linear.qweight),
+ * sw (N) bf16 (Int8Linear.scale). K % 128 == 0, N % 256 == 0 (OD_EPI_SWIGLU: N % 256 == 0), M >= 1 (any).
+ * A, W 16-byte aligned. Replaces GemLite A8W8 (quant.py:302-314) and the dequant+cuBLAS path (quant.py:149-157).
+ */
+enum { OD_EPI_BF16 = 0, OD_EPI_SWIGLU = 1, OD_EPI_INT32 = 2 };
+OD_API int od_gemm_w8a8(const int8_t* A, const float* sa, const int8_t* W, const void* sw, void* Y,
+                 int64_t M, int64_t N, int64_t K, int epilogue, void* stream);
+
+/* ---------------------------------------------------------------------------------------------------------------
+ * Embedding lookup of an int8 table, Int8Embedding.forward (quant.py:199-200):
+ *     out[i, :] = bf16(bf16(qweight[ids[i], :]) * scale[ids[i]])
+ * ids (n) int64, qweight (V, H) int8, scale (V) bf16, out (n, H) bf16.
+ */
+OD_API int od_embed_i8(const int64_t* ids, int64_t n, const int8_t* qweight, const void* scale, int64_t V, int H,
+                void* out, void* stream);
+
+/* ---------------------------------------------------------------------------------------------------------------
+ * Attention pre-processing on the fused q/k/v projection output (Qwen3_5Attention.forward, modeling_qwen3_5.py:
+ * 647-668 and prefix_attn.py:84-90): per token, q_proj's gated layout [head h: q (D) | gate (D)] is split,
+ * q and k get the per-head RMSNorm (1 + w), then rotate-half RoPE with the cos/sin tables:
+ *     q' = bf16(bf16(q * cos) + bf16(rotate_half(q) * sin))   (bf16 tables, the HF rounding points)
+ * qkv (M, Hq*2D + 2*Hkv*D) bf16 row-major; pos (M) int32 position of every token; cos, sin (P, D) bf16 tables.
+ * Outputs: q_out (M, Hq, D), k_out (M, Hkv, D), v_out (M, Hkv, D) bf16. The gate stays in qkv.
+ */
+OD_API int od_qk_norm_rope(const void* qkv, const int32_t* pos, const void* cos, const void* sin, int64_t P,
+                    const void* qnorm_w, const void* knorm_w, float eps, int64_t M, int Hq, int Hkv, int D,
+                    void* q_out, void* k_out, void* v_out, void* stream);
+
+/* Output gate + per-token quantisation of the o_proj input (Qwen3_5Attention.forward :666-668):
+ *     g = bf16(o * bf16(sigmoid(gate))),  then q, s = quantise(g) (fp32 scales)
+ * o (M, Hq*D) bf16; gate read from qkv (M, ldqkv) at column h*2D + D + d for head h. */
+OD_API int od_gate_quant(const void* o, const void* qkv, int64_t ldqkv, int64_t M, int Hq, int D,
+                  int8_t* q, float* s, void* stream);
+
+/* ---------------------------------------------------------------------------------------------------------------
+ * A9/A10: branched shared-prefix attention (Hydragen split, prefix_attn.py:43-76, merged exactly by log-sum-exp).
+ * Every query row r (a question or option row, t tokens, Hq heads) attends, in ONE online softmax:
+ *   1. the int8 state prefix of state st = row_state[r]: keys p in [p_lo[st], p_hi[st]) of Kp/Vp (S, Hkv, T, D) int8
+ *      with per-token scales ksc/vsc (S, Hkv, T); keys with pmask[st, p] == 0 are skipped (pmask may be NULL).
+ *      Dequantised in shared memory exactly as materialize() does (bf16(q * s); fp16 scales: bf16(fp16(q * s))).
+ *   2. optionally a second bf16 prefix level (the question cache, prefix_attn.py:94-99): keys j < q_len[qr] of
+ *      Kq/Vq (NQ, Lq, Hkv, D) for question qr = row_q[r].
+ *   3. its own k/v (R, t, Hkv, D) bf16 causally: key j visible to query i iff j <= i and j < row_len[r].
+ * Output o (R, t, Hq, D) bf16 and optionally lse (R, Hq, t) fp32 (natural log, -inf when no key is visible; such
+ * rows output 0, wide_attention.py:62-67). q (R, t, Hq, D) bf16. GQA: query head h reads kv head h / (Hq / Hkv).
+ * Every row sees the same key layout whatever its index: outputs do not depend on row order.
+ */
+typedef struct {
+  int64_t R, t, S, T, NQ, Lq;   /* rows, tokens per row, states, prefix capacity, questions, question length */
+  int Hq, Hkv, D;
+  int scale_dtype;              /* dtype of ksc/vsc: OD_BF16 or OD_F16 */
+  float sm_scale;               /* softmax scale (head_dim ** -0.5) */
+} od_attn_dims;
+
+OD_API int od_prefix_attn(const void* q, const int8_t* Kp, const int8_t* Vp, const void* ksc, const void* vsc,
+                   const int32_t* row_state, const int32_t* p_lo, const int32_t* p_hi, const uint8_t* pmask,
+                   const void* Kq, const void* Vq, const int32_t* row_q, const int32_t* q_len,
+                   const void* k_own, const void* v_own, const int32_t* row_len,
+                   void* o, float* lse, od_attn_dims dims, void* stream);
+
+/* ---------------------------------------------------------------------------------------------------------------
+ * A13: option readout, Decider._probs (decider.py:255-257):
+ *     p[i, :] = softmax(logits[i, :] / T[i] + bias[i, :]) * mask[i, :]
+ * logits (N, K) fp32, T (N) fp32, bias (N, K) fp32 or NULL, mask (N, K) uint8; probs (N, K) fp32.
+ * If none_col (N) int32 is given (the explicit `none` text option, decider.py:296-303; -1 = absent), also writes
+ * renorm (N, K) fp64: the probabilities clamped at 0 and renormalised over the caller's options 0..none_col-1
+ * (all K columns when none_col[i] == -1) in fp64 (decider._normalize, :26-29; other columns 0), and p_none (N) =
+ * p[i, none_col] (or 0).
+ */
+OD_API int od_readout(const float* logits, const float* T, const float* bias, const uint8_t* mask,
+               const int32_t* none_col, int64_t N, int64_t K, float* probs, double* renorm, float* p_none,
+               void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* OD_B200_H */

@@ -1,0 +1,240 @@
+"""ctypes binding of libod_b200.so (the C ABI declared in include/od_b200.h) and thin tensor-level wrappers.
+
+The library is the only implementation of the hot path: there is no CPU or PyTorch fallback. Loading fails loudly
+when the shared object is missing (build it with `python -m opendecider_b200.build`), and every wrapper raises
+ODError with the library's own message when a call returns a non-zero status. Wrappers launch on PyTorch's current
+CUDA stream and never synchronise.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from ctypes import POINTER, c_double, c_float, c_int, c_int32, c_int64, c_uint8, c_void_p
+
+import torch
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libod_b200.so")
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "od_b200.h")
+
+OD_BF16, OD_F16, OD_F32 = 0, 1, 2
+OD_EPI_BF16, OD_EPI_SWIGLU, OD_EPI_INT32 = 0, 1, 2
+_DT = {torch.bfloat16: OD_BF16, torch.float16: OD_F16, torch.float32: OD_F32}
+
+
+class ODError(RuntimeError):
+    """A libod_b200 call returned an error status."""
+
+
+class AttnDims(ctypes.Structure):
+    _fields_ = [("R", c_int64), ("t", c_int64), ("S", c_int64), ("T", c_int64), ("NQ", c_int64), ("Lq", c_int64),
+                ("Hq", c_int), ("Hkv", c_int), ("D", c_int), ("scale_dtype", c_int), ("sm_scale", c_float)]
+
+
+# exported symbol -> argument types (the declarations of include/od_b200.h)
+SIGNATURES = {
+    "od_last_error": [],
+    "od_version": [],
+    "od_device_error": [c_void_p, POINTER(c_int32)],
+    "od_quant_rows_i8": [c_void_p, c_int, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_int, c_void_p],
+    "od_dequant_rows_i8": [c_void_p, c_void_p, c_int, c_int64, c_int64, c_void_p, c_int, c_void_p],
+    "od_kv_append_i8": [c_void_p, c_void_p, c_int, c_int64, c_int64, c_int, c_int, c_int64, c_int64, c_int64,
+                        c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64,
+                        c_void_p],
+    "od_rmsnorm_res_quant": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_int64, c_int, c_void_p,
+                             c_void_p, c_void_p, c_void_p],
+    "od_gemm_w8a8": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int, c_void_p],
+    "od_embed_i8": [c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int, c_void_p, c_void_p],
+    "od_qk_norm_rope": [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_float, c_int64, c_int,
+                        c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p],
+    "od_gate_quant": [c_void_p, c_void_p, c_int64, c_int64, c_int, c_int, c_void_p, c_void_p, c_void_p],
+    "od_prefix_attn": [c_void_p] * 18 + [AttnDims, c_void_p],
+    "od_readout": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p,
+                   c_void_p],
+}
+
+_lib = None
+
+
+def load(path: str = LIB_PATH) -> ctypes.CDLL:
+    """Load the shared library once (raises if it is missing: the product has no fallback path)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(path):
+            raise ODError(f"{path} is missing: build it with `python -m opendecider_b200.build` (no fallback path)")
+        lib = ctypes.CDLL(path)
+        for name, args in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.argtypes = args
+            fn.restype = ctypes.c_char_p if name in ("od_last_error", "od_version") else c_int
+        _lib = lib
+    return _lib
+
+
+def _check(rc: int, what: str) -> None:
+    if rc != 0:
+        msg = load().od_last_error().decode(errors="replace")
+        raise ODError(f"{what}: status {rc}: {msg}")
+
+
+def _p(t: torch.Tensor | None):
+    return None if t is None else c_void_p(t.data_ptr())
+
+
+def _stream(device: torch.device) -> c_void_p:
+    return c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _need_cuda(*ts: torch.Tensor | None) -> torch.device:
+    dev = None
+    for t in ts:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise ODError("libod_b200 kernels take CUDA tensors only (there is no CPU path)")
+        if dev is None:
+            dev = t.device
+    return dev
+
+
+def device_error(device: torch.device | None = None) -> int:
+    """Reads and clears the device-side error word (bounded waits that gave up, out-of-range ids). Synchronises."""
+    device = device or torch.device("cuda", torch.cuda.current_device())
+    v = c_int32(0)
+    _check(load().od_device_error(_stream(device), ctypes.byref(v)), "od_device_error")
+    return v.value
+
+
+# ------------------------------------------------------------------------------------------------ wrappers
+def quant_rows(x: torch.Tensor, scale_dtype: torch.dtype | None = None, inv_s: torch.Tensor | None = None,
+               q: torch.Tensor | None = None, scale: torch.Tensor | None = None):
+    """Int8Tensor.quantize over the last dim of a 2-D (row-strided) tensor: returns (q int8 (M, K), scale (M, 1))."""
+    dev = _need_cuda(x, inv_s)
+    assert x.dim() == 2 and x.stride(1) == 1, "x must be (M, K) with a contiguous last dim"
+    M, K = x.shape
+    sdt = scale_dtype or (x.dtype if x.dtype != torch.float32 else torch.float32)
+    q = torch.empty(M, K, dtype=torch.int8, device=dev) if q is None else q
+    scale = torch.empty(M, 1, dtype=sdt, device=dev) if scale is None else scale
+    _check(load().od_quant_rows_i8(_p(x), _DT[x.dtype], M, K, x.stride(0), _p(inv_s), _p(q), _p(scale), _DT[sdt],
+                                   _stream(dev)), "od_quant_rows_i8")
+    return q, scale
+
+
+def dequant_rows(q: torch.Tensor, scale: torch.Tensor, out_dtype: torch.dtype) -> torch.Tensor:
+    dev = _need_cuda(q, scale)
+    M, K = q.reshape(-1, q.shape[-1]).shape
+    y = torch.empty(q.shape, dtype=out_dtype, device=dev)
+    _check(load().od_dequant_rows_i8(_p(q), _p(scale), _DT[scale.dtype], M, K, _p(y), _DT[out_dtype], _stream(dev)),
+           "od_dequant_rows_i8")
+    return y
+
+
+def kv_append(k: torch.Tensor, v: torch.Tensor, kq: torch.Tensor, vq: torch.Tensor, ksc: torch.Tensor,
+              vsc: torch.Tensor, t0: int) -> None:
+    """Quantise new keys/values k, v (S, t, Hkv, D) (any strides, last dim contiguous) into the int8 cache
+    kq/vq (S, Hkv, T_cap, D) + ksc/vsc (S, Hkv, T_cap) at token offset t0."""
+    dev = _need_cuda(k, v, kq, vq, ksc, vsc)
+    S, t, Hkv, D = k.shape
+    assert k.stride(3) == 1 and v.stride(3) == 1 and kq.is_contiguous() and vq.is_contiguous()
+    assert ksc.dtype == k.dtype and vsc.dtype == v.dtype and k.dtype == v.dtype
+    _check(load().od_kv_append_i8(_p(k), _p(v), _DT[k.dtype], S, t, Hkv, D, k.stride(0), k.stride(1), k.stride(2),
+                                  v.stride(0), v.stride(1), v.stride(2), _p(kq), _p(vq), _p(ksc), _p(vsc),
+                                  kq.shape[2], t0, _stream(dev)), "od_kv_append_i8")
+
+
+def rmsnorm_res_quant(x: torch.Tensor, w: torch.Tensor, eps: float, res_in: torch.Tensor | None = None,
+                      res_out: torch.Tensor | None = None, inv_s: torch.Tensor | None = None,
+                      y_out: torch.Tensor | None = None, want_q: bool = True, q: torch.Tensor | None = None,
+                      s: torch.Tensor | None = None):
+    """Residual add + RMSNorm (1+w) + optional smoothing + per-token int8. Returns (q, s) (or (None, None))."""
+    dev = _need_cuda(x, w, res_in, inv_s)
+    M, H = x.shape
+    if want_q:
+        q = torch.empty(M, H, dtype=torch.int8, device=dev) if q is None else q
+        s = torch.empty(M, dtype=torch.float32, device=dev) if s is None else s
+    _check(load().od_rmsnorm_res_quant(_p(x), _p(res_in), _p(res_out), _p(w), _p(inv_s), eps, M, H, _p(y_out),
+                                       _p(q) if want_q else None, _p(s) if want_q else None, _stream(dev)),
+           "od_rmsnorm_res_quant")
+    return (q, s) if want_q else (None, None)
+
+
+def gemm_w8a8(a: torch.Tensor, sa: torch.Tensor | None, w: torch.Tensor, sw: torch.Tensor | None,
+              epilogue: int = OD_EPI_BF16, out: torch.Tensor | None = None) -> torch.Tensor:
+    """int8 (M, K) x int8 (N, K)^T on tcgen05: bf16 (M, N) / SwiGLU bf16 (M, N/2) / int32 (M, N)."""
+    dev = _need_cuda(a, w, sa, sw)
+    M, K = a.shape
+    N = w.shape[0]
+    if out is None:
+        if epilogue == OD_EPI_INT32:
+            out = torch.empty(M, N, dtype=torch.int32, device=dev)
+        elif epilogue == OD_EPI_SWIGLU:
+            out = torch.empty(M, N // 2, dtype=torch.bfloat16, device=dev)
+        else:
+            out = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+    _check(load().od_gemm_w8a8(_p(a), _p(sa), _p(w), _p(sw), _p(out), M, N, K, epilogue, _stream(dev)),
+           "od_gemm_w8a8")
+    return out
+
+
+def embed_i8(ids: torch.Tensor, qweight: torch.Tensor, scale: torch.Tensor, out: torch.Tensor | None = None):
+    dev = _need_cuda(ids, qweight, scale)
+    ids = ids.reshape(-1).to(torch.int64).contiguous()
+    V, H = qweight.shape
+    out = torch.empty(ids.numel(), H, dtype=torch.bfloat16, device=dev) if out is None else out
+    _check(load().od_embed_i8(_p(ids), ids.numel(), _p(qweight), _p(scale), V, H, _p(out), _stream(dev)),
+           "od_embed_i8")
+    return out
+
+
+def qk_norm_rope(qkv: torch.Tensor, pos: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, qnorm_w: torch.Tensor,
+                 knorm_w: torch.Tensor, eps: float, Hq: int, Hkv: int, D: int, q_out=None, k_out=None, v_out=None):
+    dev = _need_cuda(qkv, pos, cos, sin)
+    M = qkv.shape[0]
+    q_out = torch.empty(M, Hq, D, dtype=torch.bfloat16, device=dev) if q_out is None else q_out
+    k_out = torch.empty(M, Hkv, D, dtype=torch.bfloat16, device=dev) if k_out is None else k_out
+    v_out = torch.empty(M, Hkv, D, dtype=torch.bfloat16, device=dev) if v_out is None else v_out
+    _check(load().od_qk_norm_rope(_p(qkv), _p(pos), _p(cos), _p(sin), cos.shape[0], _p(qnorm_w), _p(knorm_w), eps, M,
+                                  Hq, Hkv, D, _p(q_out), _p(k_out), _p(v_out), _stream(dev)), "od_qk_norm_rope")
+    return q_out, k_out, v_out
+
+
+def gate_quant(o: torch.Tensor, qkv: torch.Tensor, Hq: int, D: int, q=None, s=None):
+    dev = _need_cuda(o, qkv)
+    M = o.shape[0]
+    q = torch.empty(M, Hq * D, dtype=torch.int8, device=dev) if q is None else q
+    s = torch.empty(M, dtype=torch.float32, device=dev) if s is None else s
+    _check(load().od_gate_quant(_p(o), _p(qkv), qkv.stride(0), M, Hq, D, _p(q), _p(s), _stream(dev)),
+           "od_gate_quant")
+    return q, s
+
+
+def prefix_attn(q: torch.Tensor, k_own: torch.Tensor, v_own: torch.Tensor, sm_scale: float, *,
+                Kp=None, Vp=None, ksc=None, vsc=None, row_state=None, p_lo=None, p_hi=None, pmask=None,
+                Kq=None, Vq=None, row_q=None, q_len=None, row_len=None, out=None, want_lse: bool = False):
+    """q (R, t, Hq, D), own k/v (R, t, Hkv, D) bf16; int8 prefix Kp/Vp (S, Hkv, T, D) + scales (S, Hkv, T[, 1]);
+    optional bf16 question prefix Kq/Vq (NQ, Lq, Hkv, D). Returns o (R, t, Hq, D) [, lse (R, Hq, t)]."""
+    dev = _need_cuda(q, k_own, v_own, Kp, Kq)
+    R, t, Hq, D = q.shape
+    Hkv = k_own.shape[2]
+    out = torch.empty_like(q) if out is None else out
+    lse = torch.empty(R, Hq, t, dtype=torch.float32, device=dev) if want_lse else None
+    S, T = (Kp.shape[0], Kp.shape[2]) if Kp is not None else (0, 0)
+    NQ, Lq = (Kq.shape[0], Kq.shape[1]) if Kq is not None else (0, 0)
+    sdt = _DT[ksc.dtype] if ksc is not None else OD_BF16
+    dims = AttnDims(R, t, S, T, NQ, Lq, Hq, Hkv, D, sdt, sm_scale)
+    _check(load().od_prefix_attn(_p(q), _p(Kp), _p(Vp), _p(ksc), _p(vsc), _p(row_state), _p(p_lo), _p(p_hi),
+                                 _p(pmask), _p(Kq), _p(Vq), _p(row_q), _p(q_len), _p(k_own), _p(v_own), _p(row_len),
+                                 _p(out), _p(lse), dims, _stream(dev)), "od_prefix_attn")
+    return (out, lse) if want_lse else out
+
+
+def readout(logits: torch.Tensor, T: torch.Tensor, mask: torch.Tensor, bias: torch.Tensor | None = None,
+            none_col: torch.Tensor | None = None, want_renorm: bool = True):
+    """softmax(logits / T + bias) * mask -> probs (N, K) fp32; renorm (N, K) fp64; p_none (N,) fp32."""
+    dev = _need_cuda(logits, T, mask, bias, none_col)
+    N, K = logits.shape
+    probs = torch.empty(N, K, dtype=torch.float32, device=dev)
+    renorm = torch.empty(N, K, dtype=torch.float64, device=dev) if want_renorm else None
+    p_none = torch.empty(N, dtype=torch.float32, device=dev) if none_col is not None else None
+    _check(load().od_readout(_p(logits), _p(T), _p(bias), _p(mask), _p(none_col), N, K, _p(probs), _p(renorm),
+                             _p(p_none), _stream(dev)), "od_readout")
+    return probs, renorm, p_none

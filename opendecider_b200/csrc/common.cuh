@@ -1,0 +1,98 @@
+// Shared helpers of libod_b200: status codes, the per-thread error message, dtype conversions with the exact
+// rounding points of PyTorch's bf16/fp16 elementwise ops (compute in fp32, round to nearest even once per op).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+#include <stdarg.h>
+
+#include "../../include/od_b200.h"
+
+namespace od {
+
+// Records a printf-style message as the calling thread's last error and returns `code`.
+int fail(int code, const char* fmt, ...);
+// Clears the last error and returns OD_OK.
+int ok();
+// Device address of the library's device-side error word on the current device (set by bounded waits).
+int32_t* device_error_word();
+
+#define OD_CUDA_TRY(call)                                                                   \
+  do {                                                                                      \
+    cudaError_t e_ = (call);                                                                \
+    if (e_ != cudaSuccess) return ::od::fail(OD_ECUDA, "%s failed: %s (%s:%d)", #call,      \
+                                             cudaGetErrorString(e_), __FILE__, __LINE__);   \
+  } while (0)
+
+#define OD_REQUIRE(cond, ...)                                                               \
+  do {                                                                                      \
+    if (!(cond)) return ::od::fail(OD_EINVAL, __VA_ARGS__);                                 \
+  } while (0)
+
+// After a launch: report configuration errors synchronously (no device sync).
+#define OD_LAUNCH_CHECK()                                                                   \
+  do {                                                                                      \
+    cudaError_t e_ = cudaGetLastError();                                                    \
+    if (e_ != cudaSuccess) return ::od::fail(OD_ECUDA, "kernel launch failed: %s (%s:%d)",  \
+                                             cudaGetErrorString(e_), __FILE__, __LINE__);   \
+  } while (0)
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ------------------------------------------------------------------------------------------------ element types
+template <typename T> struct Elem;
+template <> struct Elem<__nv_bfloat16> {
+  static __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+  static __device__ __forceinline__ __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
+};
+template <> struct Elem<__half> {
+  static __device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
+  static __device__ __forceinline__ __half from_f(float v) { return __float2half_rn(v); }
+};
+template <> struct Elem<float> {
+  static __device__ __forceinline__ float to_f(float v) { return v; }
+  static __device__ __forceinline__ float from_f(float v) { return v; }
+};
+
+// Round through a storage dtype: the value PyTorch holds after one op on that dtype.
+__device__ __forceinline__ float rbf(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+__device__ __forceinline__ float rhf(float v) { return __half2float(__float2half_rn(v)); }
+
+// Int8Tensor.quantize's scale from a row's absmax: max(amax, 1e-8) / 127 in IEEE fp32.
+__device__ __forceinline__ float quant_scale(float amax) { return __fdiv_rn(fmaxf(amax, 1e-8f), 127.0f); }
+
+// Int8Tensor.quantize's value: clamp(round_half_even(x / s), -127, 127).
+__device__ __forceinline__ int8_t quant_val(float x, float s) {
+  float r = rintf(__fdiv_rn(x, s));
+  r = fminf(fmaxf(r, -127.0f), 127.0f);
+  return static_cast<int8_t>(static_cast<int>(r));
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Store a scale in the requested dtype.
+__device__ __forceinline__ void store_scale(void* p, int64_t i, float s, int dtype) {
+  if (dtype == OD_BF16) reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(s);
+  else if (dtype == OD_F16) reinterpret_cast<__half*>(p)[i] = __float2half_rn(s);
+  else reinterpret_cast<float*>(p)[i] = s;
+}
+__device__ __forceinline__ float load_scale(const void* p, int64_t i, int dtype) {
+  if (dtype == OD_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+  if (dtype == OD_F16) return __half2float(reinterpret_cast<const __half*>(p)[i]);
+  return reinterpret_cast<const float*>(p)[i];
+}
+
+}  // namespace od

@@ -1,0 +1,516 @@
+// Bandwidth-bound row kernels of the decision forward pass: per-row int8 quantisation (weights, activations, KV),
+// dequantisation, the int8 KV-cache append, fused residual + RMSNorm + quantisation, the int8 embedding lookup,
+// the attention output gate + quantisation, and the option readout softmax.
+//
+// Every kernel reads its input once from HBM and keeps the row in registers between the reduction and the write,
+// with 16-byte vector accesses that are coalesced across the threads of a row block. Rounding follows the
+// reference's PyTorch ops one op at a time (see the comments at each step).
+#include "common.cuh"
+
+namespace od {
+namespace {
+
+constexpr int kRowThreads = 128;  // one CTA per row; a row of K elements is K / 8 vectors of 8
+
+// ---------------------------------------------------------------------------------------------- vector I/O
+template <typename T> __device__ __forceinline__ void load8(const T* p, float (&v)[8]);
+template <> __device__ __forceinline__ void load8<__nv_bfloat16>(const __nv_bfloat16* p, float (&v)[8]) {
+  uint4 raw = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+template <> __device__ __forceinline__ void load8<__half>(const __half* p, float (&v)[8]) {
+  uint4 raw = *reinterpret_cast<const uint4*>(p);
+  const __half2* h = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 f = __half22float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+template <> __device__ __forceinline__ void load8<float>(const float* p, float (&v)[8]) {
+  float4 a = *reinterpret_cast<const float4*>(p);
+  float4 b = *reinterpret_cast<const float4*>(p + 4);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+template <typename T> __device__ __forceinline__ void store8(T* p, const float (&v)[8]);
+template <> __device__ __forceinline__ void store8<__nv_bfloat16>(__nv_bfloat16* p, const float (&v)[8]) {
+  uint4 raw;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&raw);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+  *reinterpret_cast<uint4*>(p) = raw;
+}
+
+__device__ __forceinline__ void store8_i8(int8_t* p, const float (&v)[8], float s) {
+  uint2 raw;
+  int8_t* b = reinterpret_cast<int8_t*>(&raw);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) b[i] = quant_val(v[i], s);
+  *reinterpret_cast<uint2*>(p) = raw;
+}
+
+// Round a value to the precision of T (the dtype a PyTorch op on T tensors stores).
+template <typename T> __device__ __forceinline__ float round_to(float v) { return Elem<T>::to_f(Elem<T>::from_f(v)); }
+
+// Block-wide reductions over kRowThreads threads.
+__device__ __forceinline__ float block_max(float v, float* red) {
+  v = warp_max(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float r = red[0];
+#pragma unroll
+  for (int i = 1; i < kRowThreads / 32; ++i) r = fmaxf(r, red[i]);
+  __syncthreads();
+  return r;
+}
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float r = red[0];
+#pragma unroll
+  for (int i = 1; i < kRowThreads / 32; ++i) r += red[i];
+  __syncthreads();
+  return r;
+}
+
+// ---------------------------------------------------------------------------------------------- quantise rows
+// Int8Tensor.quantize (quant.py:37-41) per row; optional SmoothedLinear multiply first (quant.py:328-329).
+template <typename T, int VPT>
+__global__ void __launch_bounds__(kRowThreads) quant_rows_kernel(const T* __restrict__ x, int64_t K, int64_t ldx,
+                                                                 const __nv_bfloat16* __restrict__ inv_s,
+                                                                 int8_t* __restrict__ q, void* scale,
+                                                                 int scale_dtype) {
+  __shared__ float red[kRowThreads / 32];
+  const int64_t row = blockIdx.x;
+  const T* xr = x + row * ldx;
+  float v[VPT][8];
+  float amax = 0.f;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int64_t e = (static_cast<int64_t>(j) * kRowThreads + threadIdx.x) * 8;
+    if (e < K) {
+      load8<T>(xr + e, v[j]);
+      if (inv_s) {
+        float w[8];
+        load8<__nv_bfloat16>(inv_s + e, w);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[j][i] = round_to<T>(v[j][i] * round_to<T>(w[i]));
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[j][i]));
+    }
+  }
+  amax = block_max(amax, red);
+  const float s = quant_scale(amax);
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int64_t e = (static_cast<int64_t>(j) * kRowThreads + threadIdx.x) * 8;
+    if (e < K) store8_i8(q + row * K + e, v[j], s);
+  }
+  if (threadIdx.x == 0) store_scale(scale, row, s, scale_dtype);
+}
+
+template <typename T>
+int launch_quant_rows(const T* x, int64_t M, int64_t K, int64_t ldx, const __nv_bfloat16* inv_s, int8_t* q,
+                      void* scale, int scale_dtype, cudaStream_t st) {
+  const int64_t vecs = (K / 8 + kRowThreads - 1) / kRowThreads;
+  dim3 grid(static_cast<unsigned>(M)), block(kRowThreads);
+#define OD_QR(V) quant_rows_kernel<T, V><<<grid, block, 0, st>>>(x, K, ldx, inv_s, q, scale, scale_dtype)
+  if (vecs <= 1) OD_QR(1);
+  else if (vecs <= 2) OD_QR(2);
+  else if (vecs <= 4) OD_QR(4);
+  else if (vecs <= 8) OD_QR(8);
+  else if (vecs <= 12) OD_QR(12);
+  else if (vecs <= 16) OD_QR(16);
+  else return fail(OD_EUNSUPPORTED, "od_quant_rows_i8: K=%lld above 16384", (long long)K);
+#undef OD_QR
+  OD_LAUNCH_CHECK();
+  return ok();
+}
+
+// ---------------------------------------------------------------------------------------------- dequantise rows
+template <typename TO>
+__global__ void dequant_rows_kernel(const int8_t* __restrict__ q, const void* scale, int scale_dtype, int64_t M,
+                                    int64_t K, TO* __restrict__ y) {
+  const int64_t n = M * K;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / K;
+    // Int8Tensor.dequantize: q.to(dt) * scale.to(dt), one rounding of the product to dt
+    const float s = round_to<TO>(load_scale(scale, r, scale_dtype));
+    y[i] = Elem<TO>::from_f(static_cast<float>(q[i]) * s);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------- KV append
+// One warp per (state, new token, head) row of D elements; EPL = D / 32 contiguous elements per lane.
+template <typename T, int EPL>
+__global__ void kv_append_kernel(const T* __restrict__ k, const T* __restrict__ v, int64_t S, int64_t t, int Hkv,
+                                 int64_t ks_s, int64_t ks_t, int64_t ks_h, int64_t vs_s, int64_t vs_t, int64_t vs_h,
+                                 int8_t* __restrict__ kq, int8_t* __restrict__ vq, T* __restrict__ ksc,
+                                 T* __restrict__ vsc, int64_t T_cap, int64_t t0) {
+  constexpr int D = EPL * 32;
+  const int64_t item = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t rows = S * t * Hkv;
+  if (item >= rows) return;
+  const int h = static_cast<int>(item % Hkv);
+  const int64_t j = (item / Hkv) % t;
+  const int64_t s = item / (Hkv * t);
+  const int64_t dst = ((s * Hkv + h) * T_cap + t0 + j);
+#pragma unroll
+  for (int which = 0; which < 2; ++which) {
+    const T* src = which == 0 ? k + s * ks_s + j * ks_t + h * ks_h : v + s * vs_s + j * vs_t + h * vs_h;
+    float x[EPL];
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) {
+      x[i] = Elem<T>::to_f(src[lane * EPL + i]);
+      amax = fmaxf(amax, fabsf(x[i]));
+    }
+    amax = warp_max(amax);
+    const float sc = quant_scale(amax);
+    int8_t* out = (which == 0 ? kq : vq) + dst * D + lane * EPL;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) out[i] = quant_val(x[i], sc);
+    if (lane == 0) (which == 0 ? ksc : vsc)[dst] = Elem<T>::from_f(sc);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------- norm + quant
+// Residual add + Qwen3_5RMSNorm + optional SmoothQuant multiply + per-token quantisation, one row per CTA.
+template <int VPT>
+__global__ void __launch_bounds__(kRowThreads) rmsnorm_res_quant_kernel(
+    const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ res_in, __nv_bfloat16* res_out,
+    const __nv_bfloat16* __restrict__ w, const __nv_bfloat16* __restrict__ inv_s, float eps, int H,
+    __nv_bfloat16* __restrict__ y_out, int8_t* __restrict__ q, float* __restrict__ s_out) {
+  __shared__ float red[kRowThreads / 32];
+  const int64_t row = blockIdx.x;
+  const int64_t base = row * H;
+  float v[VPT][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int e = (j * kRowThreads + threadIdx.x) * 8;
+    if (e < H) {
+      load8<__nv_bfloat16>(x + base + e, v[j]);
+      if (res_in) {  // hidden = residual + hidden, one bf16 rounding
+        float r[8];
+        load8<__nv_bfloat16>(res_in + base + e, r);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[j][i] = rbf(r[i] + v[j][i]);
+        store8<__nv_bfloat16>(res_out + base + e, v[j]);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss += v[j][i] * v[j][i];
+    }
+  }
+  ss = block_sum(ss, red);
+  // torch.rsqrt(x.pow(2).mean(-1) + eps): mean in fp32, then 1 / sqrt (the CPU reference rounds twice)
+  const float var = __fdiv_rn(ss, static_cast<float>(H));
+  const float rs = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+  float amax = 0.f;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int e = (j * kRowThreads + threadIdx.x) * 8;
+    if (e < H) {
+      float wv[8];
+      load8<__nv_bfloat16>(w + e, wv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[j][i] = rbf(__fmul_rn(__fmul_rn(v[j][i], rs), __fadd_rn(1.0f, wv[i])));
+      if (inv_s) {
+        float is[8];
+        load8<__nv_bfloat16>(inv_s + e, is);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[j][i] = rbf(v[j][i] * is[i]);
+      }
+      if (y_out) store8<__nv_bfloat16>(y_out + base + e, v[j]);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[j][i]));
+    }
+  }
+  if (!q) return;
+  amax = block_max(amax, red);
+  const float sc = quant_scale(amax);
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int e = (j * kRowThreads + threadIdx.x) * 8;
+    if (e < H) store8_i8(q + base + e, v[j], sc);
+  }
+  if (threadIdx.x == 0) s_out[row] = sc;
+}
+
+// ---------------------------------------------------------------------------------------------- embedding
+__global__ void embed_i8_kernel(const int64_t* __restrict__ ids, const int8_t* __restrict__ qw,
+                                const __nv_bfloat16* __restrict__ scale, int64_t V, int H,
+                                __nv_bfloat16* __restrict__ out, int32_t* err) {
+  const int64_t tok = blockIdx.x;
+  int64_t id = ids[tok];
+  if (id < 0 || id >= V) {  // out-of-range id: record it and write zeros instead of reading out of bounds
+    if (threadIdx.x == 0) atomicCAS(err, 0, 0x1D0000 | 1);
+    id = -1;
+  }
+  const float s = id >= 0 ? __bfloat162float(scale[id]) : 0.f;
+  for (int e = threadIdx.x * 8; e < H; e += blockDim.x * 8) {
+    float v[8];
+    if (id >= 0) {
+      uint2 raw = *reinterpret_cast<const uint2*>(qw + id * H + e);
+      const int8_t* b = reinterpret_cast<const int8_t*>(&raw);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = rbf(static_cast<float>(b[i]) * s);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = 0.f;
+    }
+    store8<__nv_bfloat16>(out + tok * H + e, v);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------- gate + quant
+// o * sigmoid(gate) (Qwen3_5Attention.forward) then per-token quantisation of the o_proj input.
+template <int VPT>
+__global__ void __launch_bounds__(kRowThreads) gate_quant_kernel(const __nv_bfloat16* __restrict__ o,
+                                                                 const __nv_bfloat16* __restrict__ qkv,
+                                                                 int64_t ldqkv, int Hq, int D,
+                                                                 int8_t* __restrict__ q, float* __restrict__ s_out) {
+  __shared__ float red[kRowThreads / 32];
+  const int64_t row = blockIdx.x;
+  const int W = Hq * D;
+  float v[VPT][8];
+  float amax = 0.f;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int e = (j * kRowThreads + threadIdx.x) * 8;
+    if (e < W) {
+      const int h = e / D, d = e % D;
+      float g[8];
+      load8<__nv_bfloat16>(o + row * W + e, v[j]);
+      load8<__nv_bfloat16>(qkv + row * ldqkv + static_cast<int64_t>(h) * 2 * D + D + d, g);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float sg = rbf(__fdiv_rn(1.0f, 1.0f + expf(-g[i])));
+        v[j][i] = rbf(v[j][i] * sg);
+        amax = fmaxf(amax, fabsf(v[j][i]));
+      }
+    }
+  }
+  amax = block_max(amax, red);
+  const float sc = quant_scale(amax);
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int e = (j * kRowThreads + threadIdx.x) * 8;
+    if (e < W) store8_i8(q + row * W + e, v[j], sc);
+  }
+  if (threadIdx.x == 0) s_out[row] = sc;
+}
+
+// ---------------------------------------------------------------------------------------------- readout
+// Decider._probs softmax (decider.py:255-257) and _normalize (:26-29), one warp per question.
+__global__ void readout_kernel(const float* __restrict__ logits, const float* __restrict__ T,
+                               const float* __restrict__ bias, const uint8_t* __restrict__ mask,
+                               const int32_t* __restrict__ none_col, int64_t N, int64_t K, float* __restrict__ probs,
+                               double* __restrict__ renorm, float* __restrict__ p_none) {
+  const int64_t i = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (i >= N) return;
+  const float ti = T[i];
+  float m = -INFINITY;
+  for (int64_t k = lane; k < K; k += 32) {
+    float z = __fdiv_rn(logits[i * K + k], ti);
+    if (bias) z = __fadd_rn(z, bias[i * K + k]);
+    m = fmaxf(m, z);
+  }
+  m = warp_max(m);
+  float sum = 0.f;
+  for (int64_t k = lane; k < K; k += 32) {
+    float z = __fdiv_rn(logits[i * K + k], ti);
+    if (bias) z = __fadd_rn(z, bias[i * K + k]);
+    sum += expf(z - m);
+  }
+  sum = warp_sum(sum);
+  const int nc = none_col ? none_col[i] : -1;
+  const int64_t Kc = nc >= 0 ? nc : K;
+  double dsum = 0.0;
+  for (int64_t k = lane; k < K; k += 32) {
+    float z = __fdiv_rn(logits[i * K + k], ti);
+    if (bias) z = __fadd_rn(z, bias[i * K + k]);
+    const float p = __fdiv_rn(expf(z - m), sum) * static_cast<float>(mask[i * K + k] != 0);
+    probs[i * K + k] = p;
+    if (k < Kc) dsum += fmax(static_cast<double>(p), 0.0);
+    if (p_none && k == nc) p_none[i] = p;
+  }
+  if (p_none && nc < 0 && lane == 0) p_none[i] = 0.f;
+  if (!renorm) return;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) dsum += __shfl_xor_sync(0xffffffffu, dsum, o);
+  for (int64_t k = lane; k < K; k += 32) {
+    const double p = fmax(static_cast<double>(probs[i * K + k]), 0.0);
+    renorm[i * K + k] = k < Kc ? p / dsum : 0.0;
+  }
+}
+
+}  // namespace
+}  // namespace od
+
+using namespace od;
+
+extern "C" int od_quant_rows_i8(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, const void* inv_s,
+                                int8_t* q, void* scale, int scale_dtype, void* stream) {
+  OD_REQUIRE(x && q && scale, "od_quant_rows_i8: null pointer");
+  OD_REQUIRE(M >= 0 && K > 0 && K % 8 == 0 && ldx >= K && ldx % 8 == 0, "od_quant_rows_i8: bad shape M=%lld K=%lld ldx=%lld",
+             (long long)M, (long long)K, (long long)ldx);
+  OD_REQUIRE(aligned16(x) && aligned16(q) && (!inv_s || aligned16(inv_s)), "od_quant_rows_i8: pointers must be 16-byte aligned");
+  OD_REQUIRE(scale_dtype >= OD_BF16 && scale_dtype <= OD_F32, "od_quant_rows_i8: bad scale dtype");
+  if (M == 0) return ok();
+  cudaStream_t st = as_stream(stream);
+  const __nv_bfloat16* is = static_cast<const __nv_bfloat16*>(inv_s);
+  switch (x_dtype) {
+    case OD_BF16: return launch_quant_rows(static_cast<const __nv_bfloat16*>(x), M, K, ldx, is, q, scale, scale_dtype, st);
+    case OD_F16: return launch_quant_rows(static_cast<const __half*>(x), M, K, ldx, is, q, scale, scale_dtype, st);
+    case OD_F32: return launch_quant_rows(static_cast<const float*>(x), M, K, ldx, is, q, scale, scale_dtype, st);
+    default: return fail(OD_EINVAL, "od_quant_rows_i8: bad x dtype %d", x_dtype);
+  }
+}
+
+extern "C" int od_dequant_rows_i8(const int8_t* q, const void* scale, int scale_dtype, int64_t M, int64_t K, void* y,
+                                  int out_dtype, void* stream) {
+  OD_REQUIRE(q && scale && y, "od_dequant_rows_i8: null pointer");
+  OD_REQUIRE(M >= 0 && K > 0, "od_dequant_rows_i8: bad shape");
+  OD_REQUIRE(scale_dtype >= OD_BF16 && scale_dtype <= OD_F32, "od_dequant_rows_i8: bad scale dtype");
+  if (M == 0) return ok();
+  cudaStream_t st = as_stream(stream);
+  const int64_t n = M * K;
+  const int blocks = static_cast<int>(n / 256 + 1 < 148 * 32 ? n / 256 + 1 : 148 * 32);
+  switch (out_dtype) {
+    case OD_BF16: dequant_rows_kernel<<<blocks, 256, 0, st>>>(q, scale, scale_dtype, M, K, static_cast<__nv_bfloat16*>(y)); break;
+    case OD_F16: dequant_rows_kernel<<<blocks, 256, 0, st>>>(q, scale, scale_dtype, M, K, static_cast<__half*>(y)); break;
+    case OD_F32: dequant_rows_kernel<<<blocks, 256, 0, st>>>(q, scale, scale_dtype, M, K, static_cast<float*>(y)); break;
+    default: return fail(OD_EINVAL, "od_dequant_rows_i8: bad out dtype %d", out_dtype);
+  }
+  OD_LAUNCH_CHECK();
+  return ok();
+}
+
+extern "C" int od_kv_append_i8(const void* k, const void* v, int kv_dtype, int64_t S, int64_t t, int Hkv, int D,
+                               int64_t ks_s, int64_t ks_t, int64_t ks_h, int64_t vs_s, int64_t vs_t, int64_t vs_h,
+                               int8_t* kq, int8_t* vq, void* ksc, void* vsc, int64_t T_cap, int64_t t0, void* stream) {
+  OD_REQUIRE(k && v && kq && vq && ksc && vsc, "od_kv_append_i8: null pointer");
+  OD_REQUIRE(S >= 0 && t >= 0 && Hkv > 0 && t0 >= 0 && t0 + t <= T_cap, "od_kv_append_i8: bad shape (t0 + t > T_cap?)");
+  OD_REQUIRE(D == 64 || D == 128 || D == 256, "od_kv_append_i8: head_dim %d not in {64, 128, 256}", D);
+  if (S == 0 || t == 0) return ok();
+  cudaStream_t st = as_stream(stream);
+  const int64_t rows = S * t * Hkv;
+  const int threads = 256;
+  const unsigned blocks = static_cast<unsigned>((rows * 32 + threads - 1) / threads);
+#define OD_KV(T_, E)                                                                                           \
+  kv_append_kernel<T_, E><<<blocks, threads, 0, st>>>(static_cast<const T_*>(k), static_cast<const T_*>(v), S, t, \
+                                                      Hkv, ks_s, ks_t, ks_h, vs_s, vs_t, vs_h, kq, vq,          \
+                                                      static_cast<T_*>(ksc), static_cast<T_*>(vsc), T_cap, t0)
+  if (kv_dtype == OD_BF16) {
+    if (D == 64) OD_KV(__nv_bfloat16, 2); else if (D == 128) OD_KV(__nv_bfloat16, 4); else OD_KV(__nv_bfloat16, 8);
+  } else if (kv_dtype == OD_F16) {
+    if (D == 64) OD_KV(__half, 2); else if (D == 128) OD_KV(__half, 4); else OD_KV(__half, 8);
+  } else if (kv_dtype == OD_F32) {
+    if (D == 64) OD_KV(float, 2); else if (D == 128) OD_KV(float, 4); else OD_KV(float, 8);
+  } else {
+    return fail(OD_EINVAL, "od_kv_append_i8: bad dtype %d", kv_dtype);
+  }
+#undef OD_KV
+  OD_LAUNCH_CHECK();
+  return ok();
+}
+
+extern "C" int od_rmsnorm_res_quant(const void* x, const void* res_in, void* res_out, const void* w, const void* inv_s,
+                                    float eps, int64_t M, int H, void* y_out, int8_t* q, float* s, void* stream) {
+  OD_REQUIRE(x && w, "od_rmsnorm_res_quant: null pointer");
+  OD_REQUIRE(!res_in || res_out, "od_rmsnorm_res_quant: res_in needs res_out");
+  OD_REQUIRE((q == nullptr) == (s == nullptr), "od_rmsnorm_res_quant: q and s go together");
+  OD_REQUIRE(y_out || q, "od_rmsnorm_res_quant: nothing to write");
+  OD_REQUIRE(M >= 0 && H > 0 && H % 8 == 0, "od_rmsnorm_res_quant: bad shape M=%lld H=%d", (long long)M, H);
+  OD_REQUIRE(aligned16(x) && aligned16(w) && (!res_in || (aligned16(res_in) && aligned16(res_out))) &&
+             (!y_out || aligned16(y_out)) && (!q || aligned16(q)) && (!inv_s || aligned16(inv_s)),
+             "od_rmsnorm_res_quant: pointers must be 16-byte aligned");
+  if (M == 0) return ok();
+  cudaStream_t st = as_stream(stream);
+  const int vecs = (H / 8 + kRowThreads - 1) / kRowThreads;
+  dim3 grid(static_cast<unsigned>(M)), block(kRowThreads);
+  auto X = static_cast<const __nv_bfloat16*>(x);
+  auto RI = static_cast<const __nv_bfloat16*>(res_in);
+  auto RO = static_cast<__nv_bfloat16*>(res_out);
+  auto Wt = static_cast<const __nv_bfloat16*>(w);
+  auto IS = static_cast<const __nv_bfloat16*>(inv_s);
+  auto Y = static_cast<__nv_bfloat16*>(y_out);
+#define OD_RN(V) rmsnorm_res_quant_kernel<V><<<grid, block, 0, st>>>(X, RI, RO, Wt, IS, eps, H, Y, q, s)
+  if (vecs <= 1) OD_RN(1);
+  else if (vecs <= 2) OD_RN(2);
+  else if (vecs <= 4) OD_RN(4);
+  else if (vecs <= 8) OD_RN(8);
+  else if (vecs <= 16) OD_RN(16);
+  else return fail(OD_EUNSUPPORTED, "od_rmsnorm_res_quant: H=%d above 16384", H);
+#undef OD_RN
+  OD_LAUNCH_CHECK();
+  return ok();
+}
+
+extern "C" int od_embed_i8(const int64_t* ids, int64_t n, const int8_t* qweight, const void* scale, int64_t V, int H,
+                           void* out, void* stream) {
+  OD_REQUIRE(ids && qweight && scale && out, "od_embed_i8: null pointer");
+  OD_REQUIRE(n >= 0 && V > 0 && H > 0 && H % 8 == 0, "od_embed_i8: bad shape");
+  OD_REQUIRE(aligned16(out) && (reinterpret_cast<uintptr_t>(qweight) & 7) == 0, "od_embed_i8: misaligned pointers");
+  if (n == 0) return ok();
+  int32_t* err = device_error_word();
+  if (!err) return fail(OD_ECUDA, "od_embed_i8: no device error word");
+  embed_i8_kernel<<<static_cast<unsigned>(n), 128, 0, as_stream(stream)>>>(
+      ids, qweight, static_cast<const __nv_bfloat16*>(scale), V, H, static_cast<__nv_bfloat16*>(out), err);
+  OD_LAUNCH_CHECK();
+  return ok();
+}
+
+extern "C" int od_gate_quant(const void* o, const void* qkv, int64_t ldqkv, int64_t M, int Hq, int D, int8_t* q,
+                             float* s, void* stream) {
+  OD_REQUIRE(o && qkv && q && s, "od_gate_quant: null pointer");
+  OD_REQUIRE(M >= 0 && Hq > 0 && D % 8 == 0 && ldqkv % 8 == 0 && ldqkv >= 2LL * Hq * D, "od_gate_quant: bad shape");
+  OD_REQUIRE(aligned16(o) && aligned16(qkv) && aligned16(q), "od_gate_quant: pointers must be 16-byte aligned");
+  if (M == 0) return ok();
+  cudaStream_t st = as_stream(stream);
+  const int W = Hq * D;
+  const int vecs = (W / 8 + kRowThreads - 1) / kRowThreads;
+  dim3 grid(static_cast<unsigned>(M)), block(kRowThreads);
+  auto O = static_cast<const __nv_bfloat16*>(o);
+  auto G = static_cast<const __nv_bfloat16*>(qkv);
+#define OD_GQ(V) gate_quant_kernel<V><<<grid, block, 0, st>>>(O, G, ldqkv, Hq, D, q, s)
+  if (vecs <= 1) OD_GQ(1);
+  else if (vecs <= 2) OD_GQ(2);
+  else if (vecs <= 4) OD_GQ(4);
+  else if (vecs <= 8) OD_GQ(8);
+  else if (vecs <= 16) OD_GQ(16);
+  else return fail(OD_EUNSUPPORTED, "od_gate_quant: Hq*D=%d above 16384", W);
+#undef OD_GQ
+  OD_LAUNCH_CHECK();
+  return ok();
+}
+
+extern "C" int od_readout(const float* logits, const float* T, const float* bias, const uint8_t* mask,
+                          const int32_t* none_col, int64_t N, int64_t K, float* probs, double* renorm, float* p_none,
+                          void* stream) {
+  OD_REQUIRE(logits && T && mask && probs, "od_readout: null pointer");
+  OD_REQUIRE(N >= 0 && K > 0, "od_readout: bad shape");
+  if (N == 0) return ok();
+  const int threads = 256;
+  const unsigned blocks = static_cast<unsigned>((N * 32 + threads - 1) / threads);
+  readout_kernel<<<blocks, threads, 0, as_stream(stream)>>>(logits, T, bias, mask, none_col, N, K, probs, renorm, p_none);
+  OD_LAUNCH_CHECK();
+  return ok();
+}

@@ -1,0 +1,316 @@
+"""Parity of every libod_b200 kernel (called through the C ABI) with the CPU oracle and the reference's golden
+outputs. Bytes, scales and int32 accumulators must match bit-exactly; floating-point outputs within the tolerance
+written at each assert."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import ops
+from opendecider_b200 import _lib
+from opendecider_b200 import synthetic as syn
+from tests.conftest import from_bits
+
+pytestmark = pytest.mark.gpu
+
+
+def bf(a) -> torch.Tensor:
+    return torch.as_tensor(np.asarray(a, dtype=np.float32)).to(torch.bfloat16)
+
+
+# ------------------------------------------------------------------------------------------------ quantisers
+def test_quant_rows_golden(cuda, golden):
+    gc = syn.gemm_case(M=64, N=256, K=512, seed=1)
+    for name, x, tdt in (("bf16", gc.x, torch.bfloat16), ("f16", gc.x.float().to(torch.float16), torch.float16),
+                         ("f32", gc.x.float(), torch.float32)):
+        q, s = _lib.quant_rows(x.to(cuda))
+        assert np.array_equal(q.cpu().numpy(), golden[f"quant.{name}.q"]), name
+        gs = golden[f"quant.{name}.scale"]
+        gs = torch.from_numpy(gs) if tdt == torch.float32 else from_bits(gs, tdt)
+        assert torch.equal(s.cpu().view(-1), gs.view(-1)), name
+    q, s = _lib.quant_rows(gc.w.to(cuda))                      # A1: the weight quantiser
+    assert np.array_equal(q.cpu().numpy(), golden["gemm.qweight"])
+    assert torch.equal(s.cpu().view(-1), from_bits(golden["gemm.wscale"], torch.bfloat16).view(-1))
+
+
+@pytest.mark.parametrize("M,K", [(1, 8), (7, 64), (513, 4096), (300, 12288), (2, 16384)])
+def test_quant_rows_shapes(cuda, M, K):
+    g = syn.gen(M * 7 + K)
+    x = (torch.randn(M, K, generator=g) * torch.rand(M, 1, generator=g) * 10).to(torch.bfloat16)
+    x[0, : min(K, 5)] = 0
+    if M > 2:
+        x[1] = 0                                                 # all-zero row: scale = 1e-8 / 127
+    q, s = _lib.quant_rows(x.to(cuda), scale_dtype=torch.float32)
+    qo, _, so = ops.quantize_rows(x.float().numpy(), "f32")
+    assert np.array_equal(q.cpu().numpy(), qo)
+    assert np.array_equal(s.cpu().numpy(), so)
+
+
+def test_quant_rows_smoothquant_and_stride(cuda):
+    """SmoothedLinear's bf16(x * inv_s) before quantisation, on a row-strided view."""
+    g = syn.gen(11)
+    big = torch.randn(50, 1024, generator=g).to(torch.bfloat16)
+    x = big[:, 256:768]
+    inv_s = (torch.rand(512, generator=g) + 0.5).to(torch.bfloat16)
+    q, s = _lib.quant_rows(big.to(cuda)[:, 256:768], scale_dtype=torch.float32, inv_s=inv_s.to(cuda))
+    xs = ops.rbf(x.float().numpy() * inv_s.float().numpy())
+    qo, _, so = ops.quantize_rows(xs, "f32")
+    assert np.array_equal(q.cpu().numpy(), qo) and np.array_equal(s.cpu().numpy(), so)
+
+
+def test_dequant_rows(cuda, golden):
+    q = torch.from_numpy(golden["kv.kq"]).reshape(-1, 128)
+    s = from_bits(golden["kv.ks"], torch.float16).reshape(-1, 1)
+    for dt, name in ((torch.bfloat16, "bf16"), (torch.float16, "f16"), (torch.float32, "f32")):
+        y = _lib.dequant_rows(q.to(cuda), s.to(cuda), dt).cpu().float().numpy()
+        ref = ops.dequantize_rows(q.numpy(), s.float().numpy(), name)
+        assert np.array_equal(y, ref), name
+
+
+def test_kv_append_golden(cuda, golden):
+    """A6: the fp16 state's K/V appended in two slices at token offsets equal Int8Tensor.quantize byte for byte."""
+    ac = syn.attn_case(S=2, T=160, rows=2, t=16, Hq=8, Hkv=2, D=128, seed=2)
+    S, Hkv, T, D = ac.K16.shape
+    kq = torch.zeros(S, Hkv, T, D, dtype=torch.int8, device=cuda)
+    vq = torch.zeros_like(kq)
+    ksc = torch.zeros(S, Hkv, T, dtype=torch.float16, device=cuda)
+    vsc = torch.zeros_like(ksc)
+    k = ac.K16.transpose(1, 2).to(cuda)                          # (S, T, Hkv, D) strided view of the cache layout
+    v = ac.V16.transpose(1, 2).to(cuda)
+    _lib.kv_append(k[:, :100], v[:, :100], kq, vq, ksc, vsc, t0=0)
+    _lib.kv_append(k[:, 100:], v[:, 100:], kq, vq, ksc, vsc, t0=100)
+    assert np.array_equal(kq.cpu().numpy(), golden["kv.kq"])
+    assert np.array_equal(vq.cpu().numpy(), golden["kv.vq"])
+    assert torch.equal(ksc.cpu().view(torch.int16).reshape(-1), torch.from_numpy(golden["kv.ks"]).reshape(-1))
+    assert torch.equal(vsc.cpu().view(torch.int16).reshape(-1), torch.from_numpy(golden["kv.vs"]).reshape(-1))
+
+
+# ------------------------------------------------------------------------------------------------ norm + quant
+@pytest.mark.parametrize("M,H", [(40, 256), (333, 4096)])
+def test_rmsnorm_res_quant(cuda, M, H):
+    g = syn.gen(M + H)
+    x = torch.randn(M, H, generator=g).to(torch.bfloat16)
+    res = (torch.randn(M, H, generator=g) * 3).to(torch.bfloat16)
+    w = (torch.randn(H, generator=g) * 0.1).to(torch.bfloat16)
+    inv_s = (torch.rand(H, generator=g) + 0.5).to(torch.bfloat16)
+    for use_s in (False, True):
+        res_out = torch.empty(M, H, dtype=torch.bfloat16, device=cuda)
+        y = torch.empty(M, H, dtype=torch.bfloat16, device=cuda)
+        q, s = _lib.rmsnorm_res_quant(x.to(cuda), w.to(cuda), 1e-6, res_in=res.to(cuda), res_out=res_out,
+                                      inv_s=inv_s.to(cuda) if use_s else None, y_out=y)
+        h, yo, _, _ = ops.rmsnorm_res_quant(x.float().numpy(), w.float().numpy(), 1e-6, res=res.float().numpy(),
+                                            inv_s=inv_s.float().numpy() if use_s else None)
+        assert np.array_equal(res_out.cpu().float().numpy(), h)
+        yk = y.cpu().float().numpy()
+        # the sum of squares is reduced in a different order than torch's: y may differ by one bf16 ulp rarely
+        assert np.mean(yk != yo) < 0.005 and np.all(np.abs(yk - yo) <= 2 ** -7 * np.abs(yo) + 1e-30)
+        # the int8 bytes and scales are exactly the quantisation of the kernel's own normalised row
+        qo, _, so = ops.quantize_rows(yk, "f32")
+        assert np.array_equal(q.cpu().numpy(), qo) and np.array_equal(s.cpu().numpy(), so[:, 0])
+
+
+def test_rmsnorm_golden(cuda, golden):
+    g = syn.gen(3)
+    x = torch.randn(40, 256, generator=g).to(torch.bfloat16)
+    res_in = torch.randn(40, 256, generator=g).to(torch.bfloat16)
+    nw = (torch.randn(256, generator=g) * 0.1).to(torch.bfloat16)
+    res_out = torch.empty(40, 256, dtype=torch.bfloat16, device=cuda)
+    y = torch.empty(40, 256, dtype=torch.bfloat16, device=cuda)
+    _lib.rmsnorm_res_quant(x.to(cuda), nw.to(cuda), 1e-6, res_in=res_in.to(cuda), res_out=res_out, y_out=y,
+                           want_q=False)
+    assert torch.equal(res_out.cpu().view(torch.int16), from_bits(golden["norm.h"], torch.bfloat16).view(torch.int16))
+    ref = from_bits(golden["norm.y"], torch.bfloat16).float()
+    assert (y.cpu().float() != ref).float().mean() < 0.005
+
+
+# ------------------------------------------------------------------------------------------------ W8A8 GEMM
+def test_gemm_int32_golden(cuda, golden):
+    a = torch.from_numpy(golden["quant.bf16.q"]).to(cuda)
+    w = torch.from_numpy(golden["gemm.qweight"]).to(cuda)
+    acc = _lib.gemm_w8a8(a, None, w, None, _lib.OD_EPI_INT32)
+    assert np.array_equal(acc.cpu().numpy(), golden["gemm.acc"])
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 256, 128), (127, 512, 384), (300, 768, 1024), (1000, 1280, 2048)])
+def test_gemm_shapes_vs_oracle(cuda, M, N, K):
+    g = syn.gen(M + N + K)
+    a = torch.randint(-127, 128, (M, K), generator=g, dtype=torch.int8)
+    w = torch.randint(-127, 128, (N, K), generator=g, dtype=torch.int8)
+    sa = torch.rand(M, generator=g) * 0.01
+    sw = (torch.rand(N, generator=g) * 0.01).to(torch.bfloat16)
+    acc = _lib.gemm_w8a8(a.to(cuda), None, w.to(cuda), None, _lib.OD_EPI_INT32)
+    ref = ops.gemm_i32(a.numpy(), w.numpy())
+    assert np.array_equal(acc.cpu().numpy(), ref)
+    y = _lib.gemm_w8a8(a.to(cuda), sa.to(cuda), w.to(cuda), sw.to(cuda), _lib.OD_EPI_BF16)
+    yo = ops.gemm_w8a8_bf16(ref, sa.numpy(), sw.float().numpy())
+    assert np.array_equal(y.cpu().float().numpy(), yo)
+
+
+@pytest.mark.parametrize("M,N,K", [(512, 4096, 4096), (2048, 12288, 4096), (8192, 4096, 12288)])
+def test_gemm_config2_int32_exact(cuda, M, N, K):
+    """Config 2 shapes at full size: int32 accumulators equal cuBLASLt's exact int8 GEMM (torch._int_mm)."""
+    gc = syn.gemm_case(M, N, K, seed=0)
+    xq, sx = _lib.quant_rows(gc.x.to(cuda), scale_dtype=torch.float32)
+    wq = gc.qweight.to(cuda)
+    acc = _lib.gemm_w8a8(xq, None, wq, None, _lib.OD_EPI_INT32)
+    ref = torch._int_mm(xq, wq.t())
+    assert torch.equal(acc, ref)
+    y = _lib.gemm_w8a8(xq, sx, wq, gc.wscale.to(cuda), _lib.OD_EPI_BF16)
+    yo = ((ref.float() * sx.view(-1, 1)) * gc.wscale.to(cuda).float().view(1, -1)).to(torch.bfloat16)
+    assert torch.equal(y, yo)
+
+
+def test_gemm_swiglu(cuda):
+    g = syn.gen(5)
+    M, F, K = 200, 384, 512
+    a = torch.randint(-127, 128, (M, K), generator=g, dtype=torch.int8)
+    wg = torch.randint(-127, 128, (F, K), generator=g, dtype=torch.int8)
+    wu = torch.randint(-127, 128, (F, K), generator=g, dtype=torch.int8)
+    sa = torch.rand(M, generator=g) * 0.002
+    sg = (torch.rand(F, generator=g) * 0.002).to(torch.bfloat16)
+    su = (torch.rand(F, generator=g) * 0.002).to(torch.bfloat16)
+    w = torch.from_numpy(ops.interleave_gate_up(wg.numpy(), wu.numpy()))
+    s = torch.from_numpy(ops.interleave_gate_up(sg.float().numpy()[:, None], su.float().numpy()[:, None])[:, 0])
+    y = _lib.gemm_w8a8(a.to(cuda), sa.to(cuda), w.to(cuda), s.to(torch.bfloat16).to(cuda), _lib.OD_EPI_SWIGLU)
+    gq = ops.gemm_w8a8_bf16(ops.gemm_i32(a.numpy(), wg.numpy()), sa.numpy(), sg.float().numpy())
+    uq = ops.gemm_w8a8_bf16(ops.gemm_i32(a.numpy(), wu.numpy()), sa.numpy(), su.float().numpy())
+    ref = ops.silu_mul(gq, uq)
+    yk = y.cpu().float().numpy()
+    # exp() of two libraries may differ by an fp32 ulp: bf16 results equal except for rare one-ulp flips
+    assert np.mean(yk != ref) < 0.01 and np.all(np.abs(yk - ref) <= 2 ** -7 * np.abs(ref) + 1e-6)
+
+
+# ------------------------------------------------------------------------------------------------ small kernels
+def test_embed(cuda, golden):
+    qw = torch.from_numpy(golden["embed.qweight"]).to(cuda)
+    sc = from_bits(golden["embed.scale"], torch.bfloat16).reshape(-1).to(cuda)
+    g = syn.gen(3)
+    for shape in [(40, 256), (40, 256), (256,)]:
+        torch.randn(*shape, generator=g)
+    torch.randn(24, 4 * 128 + 2 * 2 * 64, generator=g); torch.randn(64, generator=g); torch.randn(64, generator=g)
+    torch.randint(0, 300, (24,), generator=g); torch.randn(24, 4 * 64, generator=g)
+    torch.randn(100, 64, generator=g)
+    ids = torch.randint(0, 100, (33,), generator=g)
+    out = _lib.embed_i8(ids.to(cuda), qw, sc)
+    assert torch.equal(out.cpu().view(torch.int16), from_bits(golden["embed.out"], torch.bfloat16).view(torch.int16))
+    assert _lib.device_error() == 0
+
+
+def test_qk_norm_rope_and_gate(cuda, golden):
+    g = syn.gen(3)
+    torch.randn(40, 256, generator=g); torch.randn(40, 256, generator=g); torch.randn(256, generator=g)
+    Hq, Hkv, D, M = 4, 2, 64, 24
+    qkv = torch.randn(M, Hq * 2 * D + 2 * Hkv * D, generator=g).to(torch.bfloat16)
+    qw = (torch.randn(D, generator=g) * 0.1).to(torch.bfloat16)
+    kw = (torch.randn(D, generator=g) * 0.1).to(torch.bfloat16)
+    pos = torch.randint(0, 300, (M,), generator=g)
+    cos, sin = ops.rope_tables(D, 1e6, 300)
+    q, k, v = _lib.qk_norm_rope(qkv.to(cuda), pos.to(torch.int32).to(cuda), cos.to(cuda), sin.to(cuda), qw.to(cuda),
+                                kw.to(cuda), 1e-6, Hq, Hkv, D)
+    rq = from_bits(golden["rope.q"], torch.bfloat16).float()
+    rk = from_bits(golden["rope.k"], torch.bfloat16).float()
+    assert (q.cpu().float() != rq).float().mean() < 0.01
+    assert (k.cpu().float() != rk).float().mean() < 0.01
+    assert torch.allclose(q.cpu().float(), rq, atol=2e-2, rtol=0) and torch.allclose(k.cpu().float(), rk, atol=2e-2)
+    assert torch.equal(v.cpu().float().reshape(M, -1), qkv[:, Hq * 2 * D + Hkv * D:].float())
+    o = torch.randn(M, Hq * D, generator=g).to(torch.bfloat16)
+    qo, so = _lib.gate_quant(o.to(cuda), qkv.to(cuda), Hq, D)
+    gg, qr, sr = ops.gate_quant(o.float().numpy(), qkv.float().numpy(), Hq, D)
+    ref = from_bits(golden["gate.g"], torch.bfloat16).float().numpy()
+    assert np.mean(gg != ref) < 0.01
+    # bytes equal the oracle's quantisation of the oracle's gated row wherever the gated row agrees
+    assert np.mean(qo.cpu().numpy() != qr) < 0.01 and np.allclose(so.cpu().numpy(), sr, rtol=1e-2)
+
+
+def test_readout(cuda, golden):
+    logits = torch.from_numpy(golden["readout.logits"]).to(cuda)
+    T = torch.from_numpy(golden["readout.T"]).to(cuda)
+    mask = torch.from_numpy(golden["readout.mask"]).to(torch.uint8).to(cuda)
+    nc = torch.from_numpy(golden["readout.none_col"]).to(cuda)
+    p, ren, pn = _lib.readout(logits, T, mask, none_col=nc)
+    assert np.allclose(p.cpu().numpy(), golden["readout.p"], atol=1e-6, rtol=0)
+    assert np.allclose(ren.cpu().numpy(), golden["readout.renorm"], atol=1e-6, rtol=0)
+    for i, c in enumerate(golden["readout.none_col"]):
+        if c >= 0:
+            assert abs(pn[i].item() - golden["readout.p"][i, c]) < 1e-6
+
+
+# ------------------------------------------------------------------------------------------------ attention
+def _attn_inputs(cuda, ac):
+    Kq, Vq = ac.Kq.to(cuda), ac.Vq.to(cuda)
+    ks, vs = ac.ks.reshape(ac.Kq.shape[:3]).to(cuda), ac.vs.reshape(ac.Kq.shape[:3]).to(cuda)
+    return Kq, Vq, ks, vs
+
+
+def test_prefix_attn_golden(cuda, golden):
+    """A9: int8 prefix (with a left pad run and a hole on state 1) + causal own keys vs the reference's
+    _split_attention. bf16 P.V rounding: the reference's own GPU test allows 2e-2 (tests/test_wide_attention.py)."""
+    ac = syn.attn_case(S=2, T=160, rows=2, t=16, Hq=8, Hkv=2, D=128, seed=2)
+    Kq, Vq, ks, vs = _attn_inputs(cuda, ac)
+    pm = torch.from_numpy(golden["attn.pm"])
+    pmask = torch.stack([torch.ones_like(pm), pm]).to(torch.uint8).to(cuda)
+    o, lse = _lib.prefix_attn(ac.q.to(cuda), ac.k.to(cuda), ac.v.to(cuda), 128 ** -0.5, Kp=Kq, Vp=Vq, ksc=ks,
+                              vsc=vs, row_state=ac.row_state.to(cuda), pmask=pmask, want_lse=True)
+    ref = from_bits(golden["attn.o"], torch.bfloat16).float()
+    got = o.cpu().float()
+    assert (got - ref).abs().max() < 2e-2
+    assert (got - ref).norm() / ref.norm() < 5e-3
+    # the same rows through p_lo (leading pads sliced, as the reference does) give the same result
+    p_lo = torch.tensor([0, 7], dtype=torch.int32, device=cuda)
+    o2 = _lib.prefix_attn(ac.q.to(cuda), ac.k.to(cuda), ac.v.to(cuda), 128 ** -0.5, Kp=Kq, Vp=Vq, ksc=ks, vsc=vs,
+                          row_state=ac.row_state.to(cuda), pmask=pmask, p_lo=p_lo)
+    assert (o2.cpu().float() - ref).abs().max() < 2e-2
+
+
+def test_prefix_attn_row_order_invariant(cuda):
+    """Every row sees the same key layout: permuting the rows permutes the outputs bit for bit."""
+    ac = syn.attn_case(S=3, T=300, rows=5, t=12, Hq=32, Hkv=8, D=128, seed=7)
+    Kq, Vq, ks, vs = _attn_inputs(cuda, ac)
+    perm = torch.randperm(ac.q.shape[0], generator=syn.gen(1))
+    args = dict(Kp=Kq, Vp=Vq, ksc=ks, vsc=vs)
+    o = _lib.prefix_attn(ac.q.to(cuda), ac.k.to(cuda), ac.v.to(cuda), 128 ** -0.5, row_state=ac.row_state.to(cuda),
+                         **args)
+    op = _lib.prefix_attn(ac.q[perm].to(cuda), ac.k[perm].to(cuda), ac.v[perm].to(cuda), 128 ** -0.5,
+                          row_state=ac.row_state[perm].to(cuda), **args)
+    assert torch.equal(o[perm.to(cuda)], op)
+
+
+def test_prefix_attn_question_level_and_causal(cuda):
+    """Two-level prefix (state int8 + question bf16, right-padded questions) and a prefix-free causal pass, vs the
+    oracle's split attention over the concatenated prefix (prefix_attn.py:94-99)."""
+    g = syn.gen(9)
+    S, T, Hq, Hkv, D, t = 2, 96, 4, 2, 64, 8
+    ac = syn.attn_case(S=S, T=T, rows=3, t=t, Hq=Hq, Hkv=Hkv, D=D, seed=9)
+    NQ, Lq = 3, 20
+    q_len = torch.tensor([20, 13, 5], dtype=torch.int32)
+    q_state = torch.tensor([0, 1, 1])
+    Kqn = torch.randn(NQ, Lq, Hkv, D, generator=g).to(torch.bfloat16)
+    Vqn = torch.randn(NQ, Lq, Hkv, D, generator=g).to(torch.bfloat16)
+    R = ac.q.shape[0]
+    row_q = torch.tensor([0, 1, 2, 1, 0, 2][:R], dtype=torch.int32)
+    row_state = q_state[row_q.long()].to(torch.int32)
+    Kq, Vq, ks, vs = _attn_inputs(cuda, ac)
+    o = _lib.prefix_attn(ac.q.to(cuda), ac.k.to(cuda), ac.v.to(cuda), D ** -0.5, Kp=Kq, Vp=Vq, ksc=ks, vsc=vs,
+                         row_state=row_state.to(cuda), Kq=Kqn.to(cuda), Vq=Vqn.to(cuda), row_q=row_q.to(cuda),
+                         q_len=q_len.to(cuda)).cpu().float()
+    Kp = ops.materialize_int8(ac.Kq, ac.ks)
+    Vp = ops.materialize_int8(ac.Vq, ac.vs)
+    for r in range(R):
+        qr, s = int(row_q[r]), int(row_state[r])
+        Kc = torch.cat([Kp[s], Kqn[qr].transpose(0, 1)], 1)
+        Vc = torch.cat([Vp[s], Vqn[qr].transpose(0, 1)], 1)
+        pm = torch.cat([torch.ones(T, dtype=torch.bool), torch.arange(Lq) < q_len[qr]])
+        ref = ops.split_attention(ac.q[r:r + 1].transpose(1, 2), ac.k[r:r + 1].transpose(1, 2),
+                                  ac.v[r:r + 1].transpose(1, 2), Kc, Vc, pm, D ** -0.5).transpose(1, 2)[0]
+        assert (o[r] - ref).abs().max() < 2e-2, r
+    # prefix-free causal attention (the state pass): rows of 200 tokens, no int8 prefix
+    q = torch.randn(2, 200, Hq, D, generator=g).to(torch.bfloat16)
+    k = torch.randn(2, 200, Hkv, D, generator=g).to(torch.bfloat16)
+    v = torch.randn(2, 200, Hkv, D, generator=g).to(torch.bfloat16)
+    o = _lib.prefix_attn(q.to(cuda), k.to(cuda), v.to(cuda), D ** -0.5).cpu().float()
+    rep = Hq // Hkv
+    for r in range(2):
+        qh, kh, vh = q[r].float().transpose(0, 1), k[r].float().transpose(0, 1), v[r].float().transpose(0, 1)
+        sc = torch.einsum("htd,hsd->hts", qh, kh.repeat_interleave(rep, 0)) * D ** -0.5
+        sc = sc.masked_fill(~torch.ones(200, 200, dtype=torch.bool).tril(), float("-inf"))
+        ref = (torch.softmax(sc, -1) @ vh.repeat_interleave(rep, 0)).transpose(0, 1)
+        assert (o[r] - ref).abs().max() < 2e-2
