@@ -144,7 +144,8 @@ OD_API int od_gate_quant(const void* o, const void* qkv, int64_t ldqkv, int64_t 
  *      Dequantised in shared memory exactly as materialize() does (bf16(q * s); fp16 scales: bf16(fp16(q * s))).
  *   2. optionally a second bf16 prefix level (the question cache, prefix_attn.py:94-99): keys j < q_len[qr] of
  *      Kq/Vq (NQ, Lq, Hkv, D) for question qr = row_q[r].
- *   3. its own k/v (R, t, Hkv, D) bf16 causally: key j visible to query i iff j <= i and j < row_len[r].
+ *   3. its own k/v (R, t, Hkv, D) bf16 causally: key j visible to query i iff j <= i and
+ *      own_lo[r] <= j < own_hi[r] (own_lo / own_hi may be NULL: 0 / t; left-padded rows set own_lo).
  * Output o (R, t, Hq, D) bf16 and optionally lse (R, Hq, t) fp32 (natural log, -inf when no key is visible; such
  * rows output 0, wide_attention.py:62-67). q (R, t, Hq, D) bf16. GQA: query head h reads kv head h / (Hq / Hkv).
  * Every row sees the same key layout whatever its index: outputs do not depend on row order.
@@ -157,10 +158,10 @@ typedef struct {
 } od_attn_dims;
 
 OD_API int od_prefix_attn(const void* q, const int8_t* Kp, const int8_t* Vp, const void* ksc, const void* vsc,
-                   const int32_t* row_state, const int32_t* p_lo, const int32_t* p_hi, const uint8_t* pmask,
-                   const void* Kq, const void* Vq, const int32_t* row_q, const int32_t* q_len,
-                   const void* k_own, const void* v_own, const int32_t* row_len,
-                   void* o, float* lse, od_attn_dims dims, void* stream);
+                          const int32_t* row_state, const int32_t* p_lo, const int32_t* p_hi, const uint8_t* pmask,
+                          const void* Kq, const void* Vq, const int32_t* row_q, const int32_t* q_len,
+                          const void* k_own, const void* v_own, const int32_t* own_lo, const int32_t* own_hi,
+                          void* o, float* lse, od_attn_dims dims, void* stream);
 
 /* ---------------------------------------------------------------------------------------------------------------
  * A13: option readout, Decider._probs (decider.py:255-257):

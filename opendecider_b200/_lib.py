@@ -47,7 +47,7 @@ SIGNATURES = {
     "od_qk_norm_rope": [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_float, c_int64, c_int,
                         c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p],
     "od_gate_quant": [c_void_p, c_void_p, c_int64, c_int64, c_int, c_int, c_void_p, c_void_p, c_void_p],
-    "od_prefix_attn": [c_void_p] * 18 + [AttnDims, c_void_p],
+    "od_prefix_attn": [c_void_p] * 19 + [AttnDims, c_void_p],
     "od_readout": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p,
                    c_void_p],
 }
@@ -209,9 +209,10 @@ def gate_quant(o: torch.Tensor, qkv: torch.Tensor, Hq: int, D: int, q=None, s=No
 
 def prefix_attn(q: torch.Tensor, k_own: torch.Tensor, v_own: torch.Tensor, sm_scale: float, *,
                 Kp=None, Vp=None, ksc=None, vsc=None, row_state=None, p_lo=None, p_hi=None, pmask=None,
-                Kq=None, Vq=None, row_q=None, q_len=None, row_len=None, out=None, want_lse: bool = False):
+                Kq=None, Vq=None, row_q=None, q_len=None, own_lo=None, own_hi=None, out=None, want_lse: bool = False):
     """q (R, t, Hq, D), own k/v (R, t, Hkv, D) bf16; int8 prefix Kp/Vp (S, Hkv, T, D) + scales (S, Hkv, T[, 1]);
-    optional bf16 question prefix Kq/Vq (NQ, Lq, Hkv, D). Returns o (R, t, Hq, D) [, lse (R, Hq, t)]."""
+    optional bf16 question prefix Kq/Vq (NQ, Lq, Hkv, D); own keys valid in [own_lo[r], own_hi[r]) and causal.
+    Returns o (R, t, Hq, D) [, lse (R, Hq, t)]."""
     dev = _need_cuda(q, k_own, v_own, Kp, Kq)
     R, t, Hq, D = q.shape
     Hkv = k_own.shape[2]
@@ -222,7 +223,8 @@ def prefix_attn(q: torch.Tensor, k_own: torch.Tensor, v_own: torch.Tensor, sm_sc
     sdt = _DT[ksc.dtype] if ksc is not None else OD_BF16
     dims = AttnDims(R, t, S, T, NQ, Lq, Hq, Hkv, D, sdt, sm_scale)
     _check(load().od_prefix_attn(_p(q), _p(Kp), _p(Vp), _p(ksc), _p(vsc), _p(row_state), _p(p_lo), _p(p_hi),
-                                 _p(pmask), _p(Kq), _p(Vq), _p(row_q), _p(q_len), _p(k_own), _p(v_own), _p(row_len),
+                                 _p(pmask), _p(Kq), _p(Vq), _p(row_q), _p(q_len), _p(k_own), _p(v_own), _p(own_lo),
+                                 _p(own_hi),
                                  _p(out), _p(lse), dims, _stream(dev)), "od_prefix_attn")
     return (out, lse) if want_lse else out
 

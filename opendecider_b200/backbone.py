@@ -1,0 +1,298 @@
+"""The frozen backbone of the decision forward pass on B200: a dense Qwen3.5 decoder (every layer full attention)
+whose every op runs in libod_b200 (C ABI, sm_100a kernels). PyTorch only owns the buffers and the stream.
+
+Mirrors the reference's backbone seam (src/opendecider/backbone.py): the same int8 weight layout (Int8Linear's
+qweight (N, K) int8 + scale (N,) in the weight dtype, quant.py:122-127), the same int8 KV layout
+(PackedCache.tensors[(layer, "keys"|"values", None)] = Int8Tensor q (S, Hkv, T, D) + scale, backbone.py:436-468), the
+same LEFT-padded batched state pass (prefix_cache_batch, backbone.py:347-368) and the same positions (padded column
+index; continuations start at the padded state length).
+
+Per decoder layer (Qwen3_5DecoderLayer, modeling_qwen3_5.py:744-783) on M tokens:
+    od_rmsnorm_res_quant   residual add + input RMSNorm + per-token int8         (A3/A4/A5)
+    od_gemm_w8a8           fused q/k/v projection (the reference's three Int8Linear weights stacked by rows)
+    od_qk_norm_rope        gated-q split, q/k RMSNorm, RoPE
+    od_prefix_attn         causal / shared-prefix attention (int8 state prefix, bf16 question prefix, own keys)
+    od_kv_append_i8        int8 KV cache write (state pass)                      (A6)
+    od_gate_quant          o * sigmoid(gate) + per-token int8
+    od_gemm_w8a8           o_proj
+    od_rmsnorm_res_quant   residual add + post-attention RMSNorm + int8
+    od_gemm_w8a8 SWIGLU    gate/up (rows interleaved in blocks of 128) with SiLU(gate)*up in the epilogue
+    od_quant_rows_i8       per-token int8 of the MLP activation
+    od_gemm_w8a8           down_proj
+Stacking q/k/v (and gate/up) rows is exact: per-output-channel scales and int32 dot products of a row do not depend
+on the other rows, and all three projections quantise the same normalised activation.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import torch
+
+from . import _lib
+from .quant import Int8Tensor, quantize_weight
+
+GU_BLOCK = 128   # gate/up row interleave of the SwiGLU epilogue
+
+
+@dataclass
+class DecoderConfig:
+    """Shape of a dense Qwen3.5-style GQA decoder (Qwen3_5TextConfig with every layer `full_attention`)."""
+    vocab: int
+    hidden: int
+    layers: int
+    heads: int
+    kv_heads: int
+    head_dim: int
+    ffn: int
+    eps: float = 1e-6
+    rope_theta: float = 1e6
+    max_pos: int = 32768
+    feature_layers: tuple = ("final",)
+    dtype: torch.dtype = torch.bfloat16
+
+    @property
+    def ffn_pad(self) -> int:
+        return -(-self.ffn // GU_BLOCK) * GU_BLOCK
+
+    @property
+    def qkv_out(self) -> int:
+        return self.heads * self.head_dim * 2 + 2 * self.kv_heads * self.head_dim
+
+    @classmethod
+    def tiny(cls, **kw) -> "DecoderConfig":
+        """4 layers, hidden 256, 4 q / 2 kv heads, head_dim 64, SwiGLU 688, vocab 1024."""
+        return cls(vocab=1024, hidden=256, layers=4, heads=4, kv_heads=2, head_dim=64, ffn=688, max_pos=4096, **kw)
+
+    @classmethod
+    def nine_b(cls, **kw) -> "DecoderConfig":
+        """BASELINE configs 4/5: 36 layers, hidden 4096, 32 q / 8 kv heads, head_dim 128, SwiGLU 12288, vocab 151936."""
+        return cls(vocab=151936, hidden=4096, layers=36, heads=32, kv_heads=8, head_dim=128, ffn=12288,
+                   max_pos=32768, **kw)
+
+
+def hf_weight_names(cfg: DecoderConfig) -> list[tuple[str, tuple]]:
+    """(name, shape) of every float weight in Qwen3_5TextModel order (the names HF's state dict uses)."""
+    H, D, Hq, Hkv, F = cfg.hidden, cfg.head_dim, cfg.heads, cfg.kv_heads, cfg.ffn
+    out = [("embed_tokens.weight", (cfg.vocab, H))]
+    for i in range(cfg.layers):
+        p = f"layers.{i}."
+        out += [(p + "input_layernorm.weight", (H,)), (p + "self_attn.q_proj.weight", (Hq * D * 2, H)),
+                (p + "self_attn.k_proj.weight", (Hkv * D, H)), (p + "self_attn.v_proj.weight", (Hkv * D, H)),
+                (p + "self_attn.o_proj.weight", (H, Hq * D)), (p + "self_attn.q_norm.weight", (D,)),
+                (p + "self_attn.k_norm.weight", (D,)), (p + "post_attention_layernorm.weight", (H,)),
+                (p + "mlp.gate_proj.weight", (F, H)), (p + "mlp.up_proj.weight", (F, H)),
+                (p + "mlp.down_proj.weight", (H, F))]
+    out.append(("norm.weight", (H,)))
+    return out
+
+
+def synthetic_weights(cfg: DecoderConfig, seed: int = 0, device="cpu") -> dict[str, torch.Tensor]:
+    """Random-init float weights (bf16) of the decoder, drawn in hf_weight_names order from one seeded generator:
+    matrices ~ N(0, 0.02) (HF's initializer_range), RMSNorm weights ~ N(0, 0.1) (non-zero so the (1 + w) form is
+    exercised; HF initialises them to 0)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    out = {}
+    for name, shape in hf_weight_names(cfg):
+        std = 0.1 if name.endswith("norm.weight") else 0.02
+        out[name] = (torch.randn(*shape, generator=g, device=device) * std).to(cfg.dtype)
+    return out
+
+
+@dataclass
+class Layer:
+    ln1: torch.Tensor
+    ln2: torch.Tensor
+    qkv: Int8Tensor          # (Hq*2D + 2*Hkv*D, H)
+    q_norm: torch.Tensor
+    k_norm: torch.Tensor
+    o: Int8Tensor            # (H, Hq*D)
+    gate_up: Int8Tensor      # (2*F_pad, H) rows interleaved in blocks of GU_BLOCK
+    down: Int8Tensor         # (H, F_pad) columns >= F are zero
+
+
+@dataclass
+class KVCache:
+    """int8 state K/V of every layer in the reference's PackedCache layout: q (S, Hkv, T, D) int8 + scale
+    (S, Hkv, T) in the activation dtype, plus the left padding of each state (p_lo) and the padded length T."""
+    k: list                  # per layer Int8Tensor
+    v: list
+    p_lo: torch.Tensor       # (S,) int32: first real token of each state (left padding)
+    T: int
+    lens: list = field(default_factory=list)   # real tokens per state (CPU ints)
+
+    @property
+    def S(self) -> int:
+        return self.p_lo.numel()
+
+    def nbytes(self) -> int:
+        return sum(t.nbytes() for t in self.k + self.v)
+
+
+@dataclass
+class PassSpec:
+    """One backbone pass over R rows of t tokens (rectangular, row-major token order).
+    ids/pos (R, t) on the device; own_lo/own_hi (R,) valid own-key range (None = all); prefix levels optional."""
+    ids: torch.Tensor
+    pos: torch.Tensor
+    own_lo: torch.Tensor | None = None
+    own_hi: torch.Tensor | None = None
+    cache: KVCache | None = None           # level-1 int8 state prefix
+    row_state: torch.Tensor | None = None  # (R,) int32 state of each row
+    qkv_prefix: list | None = None         # level-2 bf16 prefix: per layer (K, V) (NQ, Lq, Hkv, D)
+    row_q: torch.Tensor | None = None      # (R,) int32 question of each row
+    q_len: torch.Tensor | None = None      # (NQ,) int32 real tokens of each question
+    write_cache: KVCache | None = None     # state pass: append this pass's K/V (rows = states) at offset 0
+    capture: bool = False                  # keep every layer's post-RoPE (k, v) (R, t, Hkv, D)
+    features: tuple = ()                   # feature layers to return ("final" or 1-based layer numbers)
+    kv_only_last: bool = False             # state pass: the last layer only needs its K/V
+
+
+class Backbone:
+    """Int8 weights on the device + the pass driver. Construct with from_float_weights / from_int8 / random."""
+
+    def __init__(self, cfg: DecoderConfig, embed: Int8Tensor, layers: list, final_norm: torch.Tensor,
+                 device: torch.device):
+        self.cfg, self.embed, self.layers, self.final_norm, self.device = cfg, embed, layers, final_norm, device
+        from .rope import rope_tables
+        self.cos, self.sin = rope_tables(cfg.head_dim, cfg.rope_theta, cfg.max_pos, cfg.dtype, device)
+        self.pad_id = 0
+
+    # ------------------------------------------------------------------------------------------ construction
+    @classmethod
+    def from_int8(cls, cfg: DecoderConfig, q: dict, norms: dict, device) -> "Backbone":
+        """From the reference's int8 layout: q maps 'embed_tokens' and every 'layers.{i}.{self_attn|mlp}.{proj}' to
+        (qweight int8 (N, K), scale (N,) or (N, 1)); norms maps the RMSNorm weight names to float tensors."""
+        dev = torch.device(device)
+        D, F, Fp, H = cfg.head_dim, cfg.ffn, cfg.ffn_pad, cfg.hidden
+        dt = cfg.dtype
+
+        def qt(name):
+            w, s = q[name]
+            return w.to(dev).contiguous(), s.reshape(-1).to(dev, dt).contiguous()
+
+        layers = []
+        for i in range(cfg.layers):
+            p = f"layers.{i}."
+            parts = [qt(p + "self_attn." + n) for n in ("q_proj", "k_proj", "v_proj")]
+            qkv = Int8Tensor(torch.cat([w for w, _ in parts]), torch.cat([s for _, s in parts]), dt)
+            gw, gs = qt(p + "mlp.gate_proj")
+            uw, us = qt(p + "mlp.up_proj")
+            if Fp != F:                                   # zero rows: SiLU(0) * 0 = 0 outputs, exact padding
+                gw = torch.cat([gw, gw.new_zeros(Fp - F, H)]); uw = torch.cat([uw, uw.new_zeros(Fp - F, H)])
+                gs = torch.cat([gs, gs.new_ones(Fp - F)]); us = torch.cat([us, us.new_ones(Fp - F)])
+            gu_w = torch.stack([gw.view(Fp // GU_BLOCK, GU_BLOCK, H), uw.view(Fp // GU_BLOCK, GU_BLOCK, H)], 1)
+            gu_s = torch.stack([gs.view(-1, GU_BLOCK), us.view(-1, GU_BLOCK)], 1)
+            dw, ds = qt(p + "mlp.down_proj")
+            if Fp != F:                                   # zero columns: the padded activations contribute 0
+                dw = torch.cat([dw, dw.new_zeros(H, Fp - F)], 1)
+            ow, os_ = qt(p + "self_attn.o_proj")
+            layers.append(Layer(
+                ln1=norms[p + "input_layernorm.weight"].to(dev, dt).contiguous(),
+                ln2=norms[p + "post_attention_layernorm.weight"].to(dev, dt).contiguous(),
+                qkv=qkv,
+                q_norm=norms[p + "self_attn.q_norm.weight"].to(dev, dt).contiguous(),
+                k_norm=norms[p + "self_attn.k_norm.weight"].to(dev, dt).contiguous(),
+                o=Int8Tensor(ow, os_, dt),
+                gate_up=Int8Tensor(gu_w.reshape(2 * Fp, H).contiguous(), gu_s.reshape(-1).contiguous(), dt),
+                down=Int8Tensor(dw.contiguous(), ds, dt)))
+        ew, es = qt("embed_tokens")
+        return cls(cfg, Int8Tensor(ew, es, dt), layers, norms["norm.weight"].to(dev, dt).contiguous(), dev)
+
+    @classmethod
+    def from_float_weights(cls, cfg: DecoderConfig, sd: dict, device) -> "Backbone":
+        """Quantise float weights exactly as the reference does at load (quantize_int8_ / Int8Embedding,
+        quant.py:122-127, 186-191: per-output-row absmax int8, scale in the weight dtype), on the device."""
+        dev = torch.device(device)
+        q, norms = {}, {}
+        for name, w in sd.items():
+            if name.endswith("norm.weight"):
+                norms[name] = w
+            else:
+                q[name[: -len(".weight")]] = quantize_weight(w.to(dev))
+        return cls.from_int8(cfg, q, norms, dev)
+
+    @classmethod
+    def random(cls, cfg: DecoderConfig, seed: int = 0, device="cuda", gen_device="cpu") -> "Backbone":
+        return cls.from_float_weights(cfg, synthetic_weights(cfg, seed, gen_device), device)
+
+    # ------------------------------------------------------------------------------------------ passes
+    def run(self, spec: PassSpec):
+        """One pass. Returns (features (R, t, nL*H) bf16 or None, captured [(k, v)] per layer or None)."""
+        cfg, dev = self.cfg, self.device
+        R, t = spec.ids.shape
+        M = R * t
+        H, D, Hq, Hkv = cfg.hidden, cfg.head_dim, cfg.heads, cfg.kv_heads
+        pos = spec.pos.reshape(-1).to(torch.int32).contiguous()
+        x = _lib.embed_i8(spec.ids.reshape(-1), self.embed.q, self.embed.scale)     # (M, H): layer 0 input
+        r = x                                                                          # residual stream
+        feats = {}
+        want = [f for f in spec.features]
+        captured = [] if spec.capture else None
+        d = None
+        cache = spec.cache
+        for li, L in enumerate(self.layers):
+            last = li == cfg.layers - 1
+            if li == 0:
+                hq, hs = _lib.rmsnorm_res_quant(r, L.ln1, cfg.eps)
+            else:
+                hq, hs = _lib.rmsnorm_res_quant(d, L.ln1, cfg.eps, res_in=r, res_out=r)
+                if li in want:                              # output of decoder layer li (1-based feature number)
+                    feats[li] = r.clone()
+            qkv = _lib.gemm_w8a8(hq, hs, L.qkv.q, L.qkv.scale, _lib.OD_EPI_BF16)
+            q, k, v = _lib.qk_norm_rope(qkv, pos, self.cos, self.sin, L.q_norm, L.k_norm, cfg.eps, Hq, Hkv, D)
+            k4, v4 = k.view(R, t, Hkv, D), v.view(R, t, Hkv, D)
+            if spec.write_cache is not None:
+                wc = spec.write_cache
+                _lib.kv_append(k4, v4, wc.k[li].q, wc.v[li].q, wc.k[li].scale, wc.v[li].scale, t0=0)
+            if captured is not None:
+                captured.append((k4, v4))
+            if last and spec.kv_only_last:
+                break
+            o = _lib.prefix_attn(
+                q.view(R, t, Hq, D), k4, v4, D ** -0.5,
+                Kp=cache.k[li].q if cache else None, Vp=cache.v[li].q if cache else None,
+                ksc=cache.k[li].scale if cache else None, vsc=cache.v[li].scale if cache else None,
+                row_state=spec.row_state, p_lo=cache.p_lo if cache else None,
+                Kq=spec.qkv_prefix[li][0] if spec.qkv_prefix else None,
+                Vq=spec.qkv_prefix[li][1] if spec.qkv_prefix else None, row_q=spec.row_q, q_len=spec.q_len,
+                own_lo=spec.own_lo, own_hi=spec.own_hi)
+            oq, os_ = _lib.gate_quant(o.view(M, Hq * D), qkv, Hq, D)
+            a = _lib.gemm_w8a8(oq, os_, L.o.q, L.o.scale, _lib.OD_EPI_BF16)
+            mq, ms = _lib.rmsnorm_res_quant(a, L.ln2, cfg.eps, res_in=r, res_out=r)
+            hm = _lib.gemm_w8a8(mq, ms, L.gate_up.q, L.gate_up.scale, _lib.OD_EPI_SWIGLU)
+            dq, dsc = _lib.quant_rows(hm, scale_dtype=torch.float32)
+            d = _lib.gemm_w8a8(dq, dsc.view(-1), L.down.q, L.down.scale, _lib.OD_EPI_BF16)
+        out = None
+        if want and not spec.kv_only_last:
+            y = torch.empty(M, H, dtype=cfg.dtype, device=dev)
+            _lib.rmsnorm_res_quant(d, self.final_norm, cfg.eps, res_in=r, res_out=r, y_out=y, want_q=False)
+            if cfg.layers in want:
+                feats[cfg.layers] = r
+            feats["final"] = y
+            out = torch.cat([feats[f if f == "final" else int(f)].view(R, t, H) for f in want], -1)
+        return out, captured
+
+    # ------------------------------------------------------------------------------------------ state pass
+    def new_cache(self, S: int, T: int) -> KVCache:
+        cfg, dev = self.cfg, self.device
+        mk = lambda: Int8Tensor(torch.empty(S, cfg.kv_heads, T, cfg.head_dim, dtype=torch.int8, device=dev),
+                                torch.empty(S, cfg.kv_heads, T, dtype=cfg.dtype, device=dev), cfg.dtype)
+        return KVCache([mk() for _ in range(cfg.layers)], [mk() for _ in range(cfg.layers)],
+                       torch.zeros(S, dtype=torch.int32, device=dev), T)
+
+    def prefix_cache_batch(self, seqs) -> KVCache:
+        """ONE pass over all states, LEFT-padded so continuations follow each state's last real token
+        (Backbone.prefix_cache_batch, backbone.py:347-368); the int8 K/V of every layer is written by
+        od_kv_append_i8 (PackedCache.pack's Int8Tensor.quantize, backbone.py:446). Returns the cache."""
+        lens = [len(s) for s in seqs]
+        S, T = len(seqs), max(lens)
+        ids = torch.tensor([[self.pad_id] * (T - n) + list(s) for s, n in zip(seqs, lens)], dtype=torch.long)
+        pad = torch.tensor([T - n for n in lens], dtype=torch.int32)
+        cache = self.new_cache(S, T)
+        cache.p_lo.copy_(pad)
+        cache.lens = lens
+        pos = torch.arange(T, dtype=torch.int32).expand(S, T)
+        spec = PassSpec(ids=ids.to(self.device, non_blocking=True), pos=pos.to(self.device, non_blocking=True),
+                        own_lo=pad.to(self.device, non_blocking=True), write_cache=cache, kv_only_last=True)
+        self.run(spec)
+        return cache

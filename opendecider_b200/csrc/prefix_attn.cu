@@ -67,7 +67,8 @@ struct Params {
   const int32_t* q_len;
   const __nv_bfloat16* k_own;
   const __nv_bfloat16* v_own;
-  const int32_t* row_len;
+  const int32_t* own_lo;
+  const int32_t* own_hi;
   __nv_bfloat16* o;
   float* lse;
   int64_t R, t, S, T, NQ, Lq;
@@ -205,10 +206,11 @@ __device__ __forceinline__ void stage_int8_block(uint8_t* sK, uint8_t* sV, float
   }
 }
 
-// Stage 64 bf16 keys+values; key j of the block is row (j0 + j) at stride `ld` elements; keys >= n are invalid.
+// Stage 64 bf16 keys+values; key j of the block is row (j0 + j) at stride `ld` elements; keys outside [lo, n) are
+// invalid (zero-filled and masked).
 template <int D>
 __device__ __forceinline__ void stage_bf16_block(uint8_t* sK, uint8_t* sV, float* bias, const __nv_bfloat16* Kb,
-                                                 const __nv_bfloat16* Vb, int64_t ld, int j0, int n) {
+                                                 const __nv_bfloat16* Vb, int64_t ld, int j0, int lo, int n) {
   // 64 keys x D/8 chunks of 8 bf16 per matrix
   constexpr int CPR = D / 8;
 #pragma unroll
@@ -216,14 +218,15 @@ __device__ __forceinline__ void stage_bf16_block(uint8_t* sK, uint8_t* sV, float
     const int c = threadIdx.x + it * kThreads;
     const int key = c / CPR, ch = c % CPR;
     const int j = j0 + key;
+    const bool in = j >= lo && j < n;
     uint4 kraw = make_uint4(0, 0, 0, 0), vraw = make_uint4(0, 0, 0, 0);
-    if (j < n) {
+    if (in) {
       kraw = *reinterpret_cast<const uint4*>(Kb + j * ld + ch * 8);
       vraw = *reinterpret_cast<const uint4*>(Vb + j * ld + ch * 8);
     }
     *reinterpret_cast<uint4*>(sK + swz<D>(key, ch)) = kraw;
     *reinterpret_cast<uint4*>(sV + swz<D>(key, ch)) = vraw;
-    if (ch == 0) bias[key] = j < n ? 0.f : -INFINITY;
+    if (ch == 0) bias[key] = in ? 0.f : -INFINITY;
   }
 }
 
@@ -296,7 +299,7 @@ __global__ void __launch_bounds__(kThreads) prefix_attn_kernel(Params P) {
     const __nv_bfloat16* Kb = P.Kq + (static_cast<int64_t>(qr) * P.Lq * P.Hkv + g) * D;
     const __nv_bfloat16* Vb = P.Vq + (static_cast<int64_t>(qr) * P.Lq * P.Hkv + g) * D;
     for (int j0 = 0; j0 < n; j0 += BN) {
-      stage_bf16_block<D>(sK, sV, bias, Kb, Vb, ld, j0, n);
+      stage_bf16_block<D>(sK, sV, bias, Kb, Vb, ld, j0, 0, n);
       __syncthreads();
       attend_block<D, false>(st, qf, sKa, sVa, bias, P.scale_log2, 0, qtok, lane);
       __syncthreads();
@@ -304,13 +307,14 @@ __global__ void __launch_bounds__(kThreads) prefix_attn_kernel(Params P) {
   }
   // ---- segment 3: own keys, causal
   {
-    const int n = P.row_len ? P.row_len[r] : static_cast<int>(P.t);
+    const int lo = P.own_lo ? P.own_lo[r] : 0;
+    const int n = P.own_hi ? P.own_hi[r] : static_cast<int>(P.t);
     const int last = min(static_cast<int>(P.t), i0 + tok_per_tile);  // keys past the tile's last token are never visible
     const int64_t ld = static_cast<int64_t>(P.Hkv) * D;
     const __nv_bfloat16* Kb = P.k_own + (r * P.t * P.Hkv + g) * D;
     const __nv_bfloat16* Vb = P.v_own + (r * P.t * P.Hkv + g) * D;
-    for (int j0 = 0; j0 < last; j0 += BN) {
-      stage_bf16_block<D>(sK, sV, bias, Kb, Vb, ld, j0, min(n, last));
+    for (int j0 = (lo / BN) * BN; j0 < last; j0 += BN) {
+      stage_bf16_block<D>(sK, sV, bias, Kb, Vb, ld, j0, lo, min(n, last));
       __syncthreads();
       attend_block<D, true>(st, qf, sKa, sVa, bias, P.scale_log2, j0, qtok, lane);
       __syncthreads();
@@ -365,7 +369,8 @@ using namespace od;
 extern "C" int od_prefix_attn(const void* q, const int8_t* Kp, const int8_t* Vp, const void* ksc, const void* vsc,
                               const int32_t* row_state, const int32_t* p_lo, const int32_t* p_hi, const uint8_t* pmask,
                               const void* Kq, const void* Vq, const int32_t* row_q, const int32_t* q_len,
-                              const void* k_own, const void* v_own, const int32_t* row_len, void* o, float* lse,
+                              const void* k_own, const void* v_own, const int32_t* own_lo, const int32_t* own_hi,
+                              void* o, float* lse,
                               od_attn_dims dims, void* stream) {
   OD_REQUIRE(q && k_own && v_own && o, "od_prefix_attn: null pointer");
   OD_REQUIRE(dims.D == 64 || dims.D == 128, "od_prefix_attn: head_dim %d not in {64, 128}", dims.D);
@@ -397,7 +402,8 @@ extern "C" int od_prefix_attn(const void* q, const int8_t* Kp, const int8_t* Vp,
   P.q_len = q_len;
   P.k_own = static_cast<const __nv_bfloat16*>(k_own);
   P.v_own = static_cast<const __nv_bfloat16*>(v_own);
-  P.row_len = row_len;
+  P.own_lo = own_lo;
+  P.own_hi = own_hi;
   P.o = static_cast<__nv_bfloat16*>(o);
   P.lse = lse;
   P.R = dims.R; P.t = dims.t; P.S = dims.S; P.T = dims.T; P.NQ = dims.NQ; P.Lq = dims.Lq;

@@ -74,3 +74,99 @@ def attn_case(S: int, T: int, rows: int, t: int, Hq: int, Hkv: int, D: int, seed
     v = torch.randn(R, t, Hkv, D, generator=g).to(torch.bfloat16)
     row_state = torch.arange(S, dtype=torch.int32).repeat_interleave(rows)
     return AttnCase(q, k, v, K16, V16, Kq, Vq, ks.to(torch.float16), vs.to(torch.float16), row_state)
+
+
+# ------------------------------------------------------------------------------------------------ decision requests
+class SyntheticTokenizer:
+    """Deterministic word-level tokenizer standing in for the Qwen tokenizer (absent: no network) on synthetic
+    workloads. A word `t<id>` is token id (mod vocab), a newline is 1, any other word (the templates' fixed words)
+    is 2 + crc32(word) % 14; ids 16.. are free for random content. Has the HF tokenizer surface the reference uses:
+    __call__(texts, add_special_tokens=False)["input_ids"], pad_token_id, __len__."""
+
+    pad_token_id = 0
+
+    def __init__(self, vocab: int):
+        self.vocab = vocab
+
+    def __len__(self) -> int:
+        return self.vocab
+
+    def encode(self, text: str) -> list:
+        import re
+        import zlib
+        out = []
+        for m in re.finditer(r"\n|[^\s]+", text):
+            w = m.group(0)
+            if w == "\n":
+                out.append(1)
+            elif re.fullmatch(r"t\d+", w):
+                out.append(int(w[1:]) % self.vocab)
+            else:
+                out.append(2 + zlib.crc32(w.encode()) % 14)
+        return out
+
+    def __call__(self, texts, add_special_tokens: bool = False):
+        if isinstance(texts, str):
+            return {"input_ids": self.encode(texts)}
+        return {"input_ids": [self.encode(t) for t in texts]}
+
+
+def words(ids) -> str:
+    return " ".join(f"t{int(i)}" for i in ids)
+
+
+@dataclass
+class Request:
+    """One decision request: a state and its questions (the atomic part of the reference's DecideRequest)."""
+    state: str
+    questions: list
+
+
+def _ids(g, n, vocab):
+    return torch.randint(16, vocab, (n,), generator=g).tolist()
+
+
+def _distinct_options(g, k, n_tok, vocab):
+    seen, out = set(), []
+    while len(out) < k:
+        o = words(_ids(g, n_tok, vocab))
+        if o not in seen:
+            seen.add(o)
+            out.append(o)
+    return out
+
+
+def decision_requests(config: int, seed: int = 0, n_requests: int | None = None, vocab: int | None = None,
+                      state_tokens: int | None = None, n_options: int | None = None):
+    """Seeded requests of BASELINE configs 1, 4 and 5 (states of random ids; state_text() adds 3 template tokens,
+    so the random part is state_tokens - 3 ids and the tokenised state is exactly state_tokens long).
+      1: 4 requests, 256-token states, one choice question: prompt 16 ids, 8 options x 8 ids
+      4: 64 requests, 2048-token states, three questions: choice 16 options x 12 ids, yes/no, score 5 levels x
+         2 ids; prompts 16 ids
+      5: 512 requests, 16384-token states (+512 appended record ids), one choice question 255 options x 12 ids
+    Returns (requests, tokenizer)."""
+    from .batching import Question
+    g = gen(seed)
+    if config == 1:
+        n, V, T, K = n_requests or 4, vocab or 1024, state_tokens or 256, n_options or 8
+    elif config == 4:
+        n, V, T, K = n_requests or 64, vocab or 151936, state_tokens or 2048, n_options or 16
+    elif config == 5:
+        n, V, T, K = n_requests or 512, vocab or 151936, state_tokens or 16384, n_options or 255
+    else:
+        raise ValueError(config)
+    tok = SyntheticTokenizer(V)
+    reqs = []
+    for i in range(n):
+        state = words(_ids(g, T - 3, V))
+        qs = []
+        if config == 1:
+            qs.append(Question(words(_ids(g, 16, V)), _distinct_options(g, K, 8, V), "choice", name="q0"))
+        elif config == 4:
+            qs.append(Question(words(_ids(g, 16, V)), _distinct_options(g, K, 12, V), "choice", name="choice"))
+            qs.append(Question.noul(words(_ids(g, 16, V)), name="yesno"))
+            qs.append(Question.score(words(_ids(g, 16, V)), _distinct_options(g, 5, 2, V), name="score"))
+        else:
+            qs.append(Question(words(_ids(g, 16, V)), _distinct_options(g, K, 12, V), "choice", name="choice"))
+        reqs.append(Request(state, qs))
+    return reqs, tok

@@ -1,0 +1,82 @@
+"""End-to-end parity of the B200 decision forward (every backbone op through the C ABI) with the reference's own
+Decider.decide_many on BASELINE config 1 (tests/golden/e2e_config1.npz, made by tests/golden/make_golden_e2e.py).
+Tolerance: probabilities within 1e-3 absolute (the north star's bar), trunk logits within 2e-2."""
+import numpy as np
+import pytest
+import torch
+
+from opendecider_b200 import synthetic as syn
+from opendecider_b200.backbone import Backbone, DecoderConfig
+from opendecider_b200.decider import Decider
+from opendecider_b200.v3 import TrunkConfig, V3Model, V3Trunk, trunk_state_dict
+
+pytestmark = pytest.mark.gpu
+
+FEATURE_LAYERS = (1, 3, "final")
+TRUNK = dict(d_model=64, n_heads=4, decision_layers=2)
+TEMPS = {"choice": 1.4978350400924683, "noul": 1.2169979810714722, "score": 1.5226973295211792}
+
+
+def make_decider(cuda, qcache=True):
+    cfg = DecoderConfig.tiny(feature_layers=FEATURE_LAYERS)
+    bb = Backbone.random(cfg, seed=0, device=cuda, gen_device="cpu")
+    tc = TrunkConfig(d_feat=cfg.hidden, n_feat_layers=len(FEATURE_LAYERS), **TRUNK)
+    trunk = V3Trunk(tc, trunk_state_dict(tc, seed=0), cuda)
+    reqs, tok = syn.decision_requests(1, seed=0)
+    model = V3Model(bb, trunk, tok, question_cache=qcache, qcache_min_rows=32)
+    return Decider(model, temperature=1.419344425201416, temperature_by_type=TEMPS), reqs
+
+
+def _collect(ans):
+    K = max(len(a["q0"]["probs_list"]) for a in ans)
+    p = np.zeros((len(ans), K))
+    for i, a in enumerate(ans):
+        p[i, : len(a["q0"]["probs_list"])] = a["q0"]["probs_list"]
+    return p, np.array([a["q0"]["none"] for a in ans])
+
+
+@pytest.mark.parametrize("qcache", [True, False])
+def test_config1_matches_reference_decide_many(cuda, qcache):
+    g = np.load("tests/golden/e2e_config1.npz")
+    tag = "qcache" if qcache else "rows"
+    dec, reqs = make_decider(cuda, qcache)
+    ans = dec.decide_many(reqs)
+    p, none = _collect(ans)
+    assert np.abs(p - g[f"{tag}.probs"]).max() < 1e-3, np.abs(p - g[f"{tag}.probs"]).max()
+    assert np.abs(none - g[f"{tag}.none"]).max() < 1e-3
+    # logits of the trunk (one per option + none), before the readout
+    questions = []
+    for i, r in enumerate(reqs):
+        for q in r.questions:
+            import copy
+            q2 = copy.copy(q)
+            q2.state_idx = i
+            questions.append(dec._with_none(q2))
+    cache = dec.encode_states([r.state for r in reqs])
+    logits, _ = dec.model.run(questions, cache)
+    ref = torch.from_numpy(g[f"{tag}.logits"])
+    assert (logits.cpu() - ref).abs().max() < 2e-2
+
+
+def test_option_order_invariance(cuda):
+    """Reversing the options permutes the probabilities (the reordering-invariance property, <= 2e-7 TV)."""
+    dec, reqs = make_decider(cuda)
+    ans = dec.decide_many(reqs)
+    rev = []
+    for r in reqs:
+        q = r.questions[0]
+        rev.append(syn.Request(r.state, [type(q)(q.prompt, list(reversed(q.options)), q.type, name=q.name)]))
+    ans_r = dec.decide_many(rev)
+    for a, b in zip(ans, ans_r):
+        pa = np.array(a["q0"]["probs_list"])
+        pb = np.array(b["q0"]["probs_list"])[::-1]
+        assert 0.5 * np.abs(pa - pb).sum() <= 2e-7
+        assert abs(a["q0"]["none"] - b["q0"]["none"]) <= 2e-7
+
+
+def test_batch_invariance(cuda):
+    """A request decided alone equals the same request inside the batch (state isolation, left padding)."""
+    dec, reqs = make_decider(cuda)
+    ans = dec.decide_many(reqs)
+    one = dec.decide_many(reqs[1:2])
+    assert np.abs(np.array(ans[1]["q0"]["probs_list"]) - np.array(one[0]["q0"]["probs_list"])).max() < 1e-3
