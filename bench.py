@@ -1,0 +1,339 @@
+"""Benchmark of the B200 decision forward pass (BASELINE config 4 by default).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--config 4|1]
+    python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 --master-port P \\
+        bench.py --gpus N --steps K --warmup W
+
+Workload (config 4): a 9B-class dense Qwen3.5-style decoder (36 layers, hidden 4096, 32/8 heads, head_dim 128, SwiGLU
+12288, vocab 151936, random-init int8 weights, int8 KV) under the V3 trunk (d_model 512, 8 heads, 4 layers, feature
+layers 8/16/24/final); per GPU 64 requests, each a 2048-token random-id state with three questions (choice 16 x 12
+tokens, yes/no, score 5 x 2 tokens), each + the `none` option: 192 decisions per GPU per step. One step = the whole
+decision forward of that batch (state pass, question-cache row passes, trunk, readout). Requests are independent:
+N GPUs run N batches (weak scaling) and gather the probabilities over NCCL.
+
+Printed: one JSON line on rank 0. `value` = decisions/s over all GPUs with the batch's inputs resident in HBM
+(device time, CUDA events, max over ranks); `e2e` = the same metric through the public API Decider.decide_many
+(tokenisation, one pinned host->device copy, kernels, the device->host read of the answers); `roofline` = the W8A8
+GEMM (the dominant kernel) timed per launch with CUDA events inside the timed region; `cpu_baseline` = the CPU oracle
+of the same path (oracle/model.py) on a bounded sample, extrapolated.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+TEMPS = {"choice": 1.4978350400924683, "noul": 1.2169979810714722, "score": 1.5226973295211792}
+TEMPERATURE = 1.419344425201416
+METRIC = "decisions/sec"
+
+
+def workload(config: int):
+    """(DecoderConfig, TrunkConfig kwargs, qcache threshold, description) of a bench configuration."""
+    from opendecider_b200.backbone import DecoderConfig
+    if config == 4:
+        cfg = DecoderConfig.nine_b(feature_layers=(8, 16, 24, "final"))
+        return cfg, dict(d_model=512, n_heads=8, decision_layers=4), 12, \
+            "config4: 9B-class dense decoder, 64 requests/GPU x 2048-token state, 3 questions (+none)"
+    cfg = DecoderConfig.tiny(feature_layers=(1, 3, "final"))
+    return cfg, dict(d_model=64, n_heads=4, decision_layers=2), 32, \
+        "config1: tiny decoder, 4 requests x 256-token state, 1 choice question x 8 options (+none)"
+
+
+# ------------------------------------------------------------------------------------------------ clocks
+class Clocks:
+    """nvidia-smi sampled every 200 ms during the timed region (rank 0, all GPUs of the run)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, n_gpus: int):
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        ids = ",".join(str(i) for i in range(n_gpus))
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", ids, f"--query-gpu={self.FIELDS}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
+                                      stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+
+    def stop(self) -> dict:
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.p.terminate()
+        self.p.wait()
+        self.f.seek(0)
+        rows = [l.strip().split(", ") for l in self.f.read().splitlines() if l.strip()]
+        os.unlink(self.f.name)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx.append(float(r[2]))
+                for n, v in zip(names, r[5:9]):
+                    if v.strip() == "Active":
+                        reasons.add(n)
+            except (ValueError, IndexError):
+                continue
+        load = [s for s in sm if mx and s > 0.3 * max(mx)] or sm
+        return {"sm_mhz": statistics.median(load) if load else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------------------------------ CPU oracle
+class CpuSample:
+    """The CPU oracle (oracle/model.py) timed on one request of the workload with as many decoder layers as fit a
+    time budget, extrapolated linearly to all layers. With fewer layers than the feature layers need, the last
+    sampled layer's normed output stands in for each feature layer (same shapes and trunk work)."""
+
+    def __init__(self, config: int, budget_s: float, seed: int = 0):
+        from oracle.model import OracleDecision
+        from opendecider_b200 import synthetic as syn
+        from opendecider_b200.backbone import synthetic_weights
+        from opendecider_b200.v3 import TrunkConfig, V3Trunk, trunk_state_dict
+        torch.set_num_threads(os.cpu_count() or 1)
+        cfg, tk, qmin, _ = workload(config)
+        self.cfg, self.n_layers_total = cfg, cfg.layers
+        self.reqs, tok = syn.decision_requests(config, seed=seed, n_requests=1)
+        tc = TrunkConfig(d_feat=cfg.hidden, n_feat_layers=len(cfg.feature_layers), **tk)
+        trunk = V3Trunk(tc, trunk_state_dict(tc, seed=0), "cpu")
+        sd = synthetic_weights(cfg, seed=0, layers=1)
+        self.feats = cfg.feature_layers
+        cfg.feature_layers = ("final",) * len(self.feats)
+        mk = lambda n: OracleDecision(cfg, self._alias(sd, n), trunk, tok, TEMPS, TEMPERATURE, layers=n,
+                                      qcache_min_rows=qmin)
+        t1 = self._time(mk(1))                      # calibration with one layer
+        self.n = max(1, min(cfg.layers, int(budget_s / max(t1, 1e-3))))
+        self.od = mk(self.n)
+
+    @staticmethod
+    def _alias(sd, n):
+        """Layers 1..n-1 reuse layer 0's weights (timing only: the sample is not checked for parity)."""
+        out = dict(sd)
+        for k, v in sd.items():
+            if k.startswith("layers.0."):
+                for i in range(1, n):
+                    out[k.replace("layers.0.", f"layers.{i}.", 1)] = v
+        return out
+
+    def _time(self, od) -> float:
+        t0 = time.perf_counter()
+        od.decide(self.reqs)
+        return time.perf_counter() - t0
+
+    def step(self):
+        """One timed sample. Returns (decisions/s extrapolated, threads, description)."""
+        t = self._time(self.od)
+        nd = sum(len(r.questions) for r in self.reqs)
+        per_request = t * self.n_layers_total / self.n
+        desc = (f"oracle/model.py (PyTorch CPU, bf16 + int8 _int_mm) on 1 request ({nd} decisions): {self.n} of "
+                f"{self.n_layers_total} decoder layers timed ({t:.1f} s), extrapolated linearly to all layers")
+        return nd / per_request, torch.get_num_threads(), desc
+
+
+def cpu_oracle_sample(config: int, budget_s: float):
+    return CpuSample(config, budget_s).step()
+
+
+def run_reference(args, rank: int) -> None:
+    """--impl reference: the reference path's CPU implementation (the oracle port) on the host cores."""
+    if rank != 0:
+        return
+    cfg, _, _, desc = workload(args.config)
+    per_step = max(3.0, 120.0 / max(1, args.steps + args.warmup))
+    cs = CpuSample(args.config, per_step)
+    vals = []
+    for i in range(args.warmup + args.steps):
+        v, cores, sample = cs.step()
+        if i >= args.warmup:
+            vals.append(v)
+    value = statistics.mean(vals)
+    print(json.dumps({
+        "metric": METRIC, "value": value, "unit": "decisions/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8", "data": "synthetic", "impl": "reference",
+        "config": {"workload": desc, "global_batch": None},
+        "cpu_baseline": {"value": value, "unit": "decisions/s", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "decisions/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+
+
+# ------------------------------------------------------------------------------------------------ B200 arm
+def traffic_per_launch():
+    """DRAM bytes per W8A8 GEMM launch from the committed ncu summary (profiles/gemm_w8a8_qkv.md), else None."""
+    path = os.path.join(ROOT, "profiles", "gemm_w8a8_qkv.md")
+    if not os.path.exists(path):
+        return None
+    for line in open(path):
+        if line.startswith("dram_bytes_per_launch_full_size:"):
+            try:
+                return float(line.split(":", 1)[1].split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--config", type=int, default=4, choices=[1, 4])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+
+    import torch.distributed as dist
+    from datetime import timedelta
+    from opendecider_b200 import _lib
+    from opendecider_b200 import synthetic as syn
+    from opendecider_b200.backbone import Backbone
+    from opendecider_b200.decider import Decider
+    from opendecider_b200.v3 import TrunkConfig, V3Model, V3Trunk, trunk_state_dict
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    cfg, tk, qmin, desc = workload(args.config)
+    bb = Backbone.random(cfg, seed=0, device=dev, gen_device=dev)
+    torch.cuda.empty_cache()
+    tc = TrunkConfig(d_feat=cfg.hidden, n_feat_layers=len(cfg.feature_layers), **tk)
+    trunk = V3Trunk(tc, trunk_state_dict(tc, seed=0), dev)
+    reqs, tok = syn.decision_requests(args.config, seed=rank)
+    decider = Decider(V3Model(bb, trunk, tok, qcache_min_rows=qmin), TEMPERATURE, TEMPS)
+
+    def gather(probs):
+        if world > 1:
+            p = probs[0]
+            out = torch.empty(world * p.shape[0], p.shape[1], dtype=p.dtype, device=dev)
+            dist.all_gather_into_tensor(out, p.contiguous())
+            return out
+        return probs[0]
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- value: device-resident inputs (the plan uploaded once), K timed steps
+    plan = decider.plan(reqs)
+    n_dec_local = len(plan["questions"])
+    cache = None
+    for _ in range(args.warmup):
+        probs, cache = decider.execute(plan, cache)
+        gather(probs)
+    torch.cuda.synchronize()
+    assert _lib.device_error(dev) == 0, "a kernel reported a device-side error"
+    barrier()
+    clocks = Clocks(world) if rank == 0 else None
+    _lib.GEMM_PROBE = []
+    l0 = _lib.LAUNCHES[0]
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        probs, cache = decider.execute(plan, cache)
+        gather(probs)
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    launches = (_lib.LAUNCHES[0] - l0) // max(1, args.steps)
+    probe, _lib.GEMM_PROBE = _lib.GEMM_PROBE, None
+    clk = clocks.stop() if clocks else None
+    t_dev = max_over_ranks(e0.elapsed_time(e1) / 1e3)
+    gemm_ms = sum(a.elapsed_time(b) for a, b, _, _ in probe)
+    gemm_ops = sum(o for _, _, o, _ in probe)
+    gemm_launches = len(probe) // max(1, args.steps)
+    decisions = n_dec_local * world * args.steps
+    value = decisions / t_dev
+
+    # ---- e2e: the public API per step (tokenise, plan, one pinned H2D copy, kernels, gather, D2H answers)
+    for _ in range(1):
+        ans = decider.decide_many(reqs)
+    torch.cuda.synchronize()
+    barrier()
+    h2d = d2h = 0
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for _ in range(args.steps):
+        p = decider.plan(reqs)
+        pr, _ = decider.execute(p)
+        g = gather(pr)
+        ans = decider.answers(p, pr)
+        if world > 1:
+            g.cpu()
+        h2d = p["h2d_bytes"]
+        d2h = sum(t.numel() * t.element_size() for t in pr) + (g.numel() * g.element_size() if world > 1 else 0)
+    f1.record()
+    torch.cuda.synchronize()
+    barrier()
+    t_e2e = max_over_ranks(f0.elapsed_time(f1) / 1e3)
+    assert len(ans) == len(reqs)
+
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    # ---- roofline of the dominant kernel (W8A8 GEMM, int8 tensor pipe)
+    peaks = {}
+    pk = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(pk):
+        peaks = json.load(open(pk))
+    if peaks.get("bf16_tflops_sustained"):
+        peak = 2.0 * peaks["bf16_tflops_sustained"]
+        peak_note = "2 x measured sustained bf16 TFLOP/s (MEASURED_PEAKS.json): the dense int8 rate is twice bf16's"
+    else:
+        peak = 2.0 * 1400.0
+        peak_note = "2 x fallback sustained bf16 1.4 PFLOP/s"
+    achieved = gemm_ops / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else None
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        v, cores, sample = cpu_oracle_sample(args.config, 20.0)
+        cpu = {"value": v, "unit": "decisions/s", "cores": cores, "kind": "port", "sample": sample}
+    out = {
+        "metric": METRIC, "value": value, "unit": "decisions/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1e3 * t_dev / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded random-id states, random-init weights)",
+        "config": {"workload": desc, "global_batch": n_dec_local * world, "requests_per_gpu": len(reqs),
+                   "state_tokens": plan["state"]["T"], "parallelism": f"dp{world} (requests sharded, NCCL gather)",
+                   "l2": "inputs larger than L2 (7.6 GB of int8 weights and a 9.7 GB KV cache stream every step)"},
+        "e2e": {"value": decisions / t_e2e, "unit": "decisions/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": 1e3 * t_e2e / args.steps},
+        "roofline": {"bound": "tensor", "kernel": "od_gemm_w8a8 (tcgen05 kind::i8)", "achieved": achieved,
+                     "peak": peak, "unit": "TOP/s (int8)", "frac": (achieved / peak) if achieved else None,
+                     "peak_source": peak_note, "traffic": traffic_per_launch(),
+                     "launches_per_step": gemm_launches, "share_of_step": gemm_ms / 1e3 / args.steps /
+                     (t_dev / args.steps) if t_dev else None},
+        "cpu_baseline": cpu, "clocks": clk, "gpu_launches": launches * args.steps,
+        "gpu_launches_per_step": launches}
+    print(json.dumps(out))
+
+
+if __name__ == "__main__":
+    main()

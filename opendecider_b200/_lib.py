@@ -54,6 +54,11 @@ SIGNATURES = {
 
 _lib = None
 
+# kernel launches issued through this module (every compute wrapper launches exactly one kernel)
+LAUNCHES = [0]
+# optional per-launch timing of od_gemm_w8a8: a list that receives (start event, end event, int ops) per launch
+GEMM_PROBE: list | None = None
+
 
 def load(path: str = LIB_PATH) -> ctypes.CDLL:
     """Load the shared library once (raises if it is missing: the product has no fallback path)."""
@@ -71,6 +76,7 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
 
 
 def _check(rc: int, what: str) -> None:
+    LAUNCHES[0] += 1
     if rc != 0:
         msg = load().od_last_error().decode(errors="replace")
         raise ODError(f"{what}: status {rc}: {msg}")
@@ -100,7 +106,9 @@ def device_error(device: torch.device | None = None) -> int:
     """Reads and clears the device-side error word (bounded waits that gave up, out-of-range ids). Synchronises."""
     device = device or torch.device("cuda", torch.cuda.current_device())
     v = c_int32(0)
-    _check(load().od_device_error(_stream(device), ctypes.byref(v)), "od_device_error")
+    rc = load().od_device_error(_stream(device), ctypes.byref(v))
+    if rc != 0:
+        raise ODError(f"od_device_error: status {rc}: {load().od_last_error().decode(errors='replace')}")
     return v.value
 
 
@@ -170,8 +178,15 @@ def gemm_w8a8(a: torch.Tensor, sa: torch.Tensor | None, w: torch.Tensor, sw: tor
             out = torch.empty(M, N // 2, dtype=torch.bfloat16, device=dev)
         else:
             out = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+    probe = GEMM_PROBE
+    if probe is not None:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
     _check(load().od_gemm_w8a8(_p(a), _p(sa), _p(w), _p(sw), _p(out), M, N, K, epilogue, _stream(dev)),
            "od_gemm_w8a8")
+    if probe is not None:
+        e1.record()
+        probe.append((e0, e1, 2 * M * N * K, M * K + N * K + out.numel() * out.element_size() + 4 * M + 2 * N))
     return out
 
 

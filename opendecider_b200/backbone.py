@@ -86,13 +86,17 @@ def hf_weight_names(cfg: DecoderConfig) -> list[tuple[str, tuple]]:
     return out
 
 
-def synthetic_weights(cfg: DecoderConfig, seed: int = 0, device="cpu") -> dict[str, torch.Tensor]:
+def synthetic_weights(cfg: DecoderConfig, seed: int = 0, device="cpu", layers: int | None = None) \
+        -> dict[str, torch.Tensor]:
     """Random-init float weights (bf16) of the decoder, drawn in hf_weight_names order from one seeded generator:
     matrices ~ N(0, 0.02) (HF's initializer_range), RMSNorm weights ~ N(0, 0.1) (non-zero so the (1 + w) form is
-    exercised; HF initialises them to 0)."""
+    exercised; HF initialises them to 0). layers: only the embedding, the first `layers` layers and the final norm
+    (for a sampled CPU baseline)."""
     g = torch.Generator(device=device).manual_seed(seed)
     out = {}
     for name, shape in hf_weight_names(cfg):
+        if layers is not None and name.startswith("layers.") and int(name.split(".")[1]) >= layers:
+            continue
         std = 0.1 if name.endswith("norm.weight") else 0.02
         out[name] = (torch.randn(*shape, generator=g, device=device) * std).to(cfg.dtype)
     return out
@@ -280,19 +284,30 @@ class Backbone:
         return KVCache([mk() for _ in range(cfg.layers)], [mk() for _ in range(cfg.layers)],
                        torch.zeros(S, dtype=torch.int32, device=dev), T)
 
-    def prefix_cache_batch(self, seqs) -> KVCache:
-        """ONE pass over all states, LEFT-padded so continuations follow each state's last real token
-        (Backbone.prefix_cache_batch, backbone.py:347-368); the int8 K/V of every layer is written by
-        od_kv_append_i8 (PackedCache.pack's Int8Tensor.quantize, backbone.py:446). Returns the cache."""
+    def plan_state(self, seqs, up=None) -> dict:
+        """Host layout of the batched state pass (Backbone.prefix_cache_batch, backbone.py:347-368): states LEFT-padded
+        to the longest, positions = padded column index, uploaded once."""
         lens = [len(s) for s in seqs]
         S, T = len(seqs), max(lens)
         ids = torch.tensor([[self.pad_id] * (T - n) + list(s) for s, n in zip(seqs, lens)], dtype=torch.long)
         pad = torch.tensor([T - n for n in lens], dtype=torch.int32)
-        cache = self.new_cache(S, T)
-        cache.p_lo.copy_(pad)
-        cache.lens = lens
-        pos = torch.arange(T, dtype=torch.int32).expand(S, T)
-        spec = PassSpec(ids=ids.to(self.device, non_blocking=True), pos=pos.to(self.device, non_blocking=True),
-                        own_lo=pad.to(self.device, non_blocking=True), write_cache=cache, kv_only_last=True)
-        self.run(spec)
+        pos = torch.arange(T, dtype=torch.int32).expand(S, T).contiguous()
+        up = up or (lambda x: x.to(self.device, non_blocking=True))
+        return {"S": S, "T": T, "lens": lens, "ids": up(ids), "pos": up(pos), "pad": up(pad)}
+
+    def run_state(self, plan: dict, cache: KVCache | None = None) -> KVCache:
+        """ONE pass over all states; every layer's int8 K/V is written by od_kv_append_i8 (PackedCache.pack's
+        Int8Tensor.quantize, backbone.py:446). The last layer stops after its K/V projection: nothing downstream
+        reads its attention or MLP output (the state pass keeps no hidden states, v3.py:317)."""
+        S, T = plan["S"], plan["T"]
+        if cache is None or cache.S != S or cache.T != T:
+            cache = self.new_cache(S, T)
+        cache.p_lo.copy_(plan["pad"])
+        cache.lens = plan["lens"]
+        self.run(PassSpec(ids=plan["ids"], pos=plan["pos"], own_lo=plan["pad"], write_cache=cache,
+                          kv_only_last=True))
         return cache
+
+    def prefix_cache_batch(self, seqs) -> KVCache:
+        """Backbone.prefix_cache_batch (backbone.py:347-368) on B200: returns the int8 KV cache of all states."""
+        return self.run_state(self.plan_state(seqs))

@@ -17,6 +17,7 @@ import torch
 from . import _lib
 from .backbone import KVCache
 from .batching import MAX_OPTIONS, Question, state_text
+from .staging import Staging
 
 # option rows per call from which the question cache is used (decider.py:85-88, keyed by backbone hidden size)
 QCACHE_MIN_ROWS = {2048: 64, 4096: 12}
@@ -31,6 +32,7 @@ class Decider:
         # the explicit `none` option appended as text to every question (decider.py:133-135)
         self.none_text = os.environ.get("OPENDECIDER_NONE_TEXT", "none of the above") if none_text is None \
             else none_text
+        self.staging = Staging(model.backbone.device)
 
     def _with_none(self, q: Question) -> Question:
         """Copy of q with `none` appended, unless at the 255-option cap (decider.py:296-303)."""
@@ -43,14 +45,46 @@ class Decider:
 
     def encode_states(self, states) -> KVCache:
         """The batched state pass: state_text() of every request, tokenised, one left-padded pass."""
+        return self.model.backbone.run_state(self._plan_states(states))
+
+    def _plan_states(self, states, up=None) -> dict:
         texts = [state_text(s) for s in states]
         seqs = self.model.tok(texts, add_special_tokens=False)["input_ids"]
-        return self.model.backbone.prefix_cache_batch(seqs)
+        return self.model.backbone.plan_state(seqs, up)
+
+    def plan(self, requests) -> dict:
+        """Everything host-side of one decide_many call (tokenisation, layouts, readout constants), staged in one
+        pinned buffer and uploaded by one copy. The plan's device views stay valid until the next plan()."""
+        self.staging.begin()
+        up = self.staging.put
+        st = self._plan_states([r.state for r in requests], up)
+        batch, owner = [], []
+        for i, r in enumerate(requests):
+            for q in r.questions:
+                q2 = copy.copy(q)
+                q2.state_idx = i
+                q2.name = f"{i}\x1f{q.name}"
+                batch.append(self._with_none(q2) if self.none_text else q2)
+                owner.append(i)
+        T = up(torch.tensor([self.temperature_by_type.get(q.type, self.temperature) for q in batch],
+                            dtype=torch.float32))
+        nc = up(torch.tensor([getattr(q, "none_col", -1) for q in batch], dtype=torch.int32))
+        mplan = self.model.plan(batch, st["T"], st["lens"], up)
+        h2d = self.staging.commit()
+        return {"state": st, "model": mplan, "questions": batch, "owner": owner, "n_requests": len(requests),
+                "T": T, "none_col": nc, "h2d_bytes": h2d}
+
+    def execute(self, plan: dict, cache: KVCache | None = None):
+        """The device work of one call: state pass, row passes, trunk, od_readout. Returns device tensors
+        (probs (N, K) fp32, renorm (N, K) fp64, p_none (N,) fp32) and the cache."""
+        cache = self.model.backbone.run_state(plan["state"], cache)
+        logits, opt_mask = self.model.execute(plan["model"], cache)
+        probs = _lib.readout(logits.contiguous(), plan["T"], opt_mask.to(torch.uint8), none_col=plan["none_col"])
+        return probs, cache
 
     def probs(self, questions, cache: KVCache):
-        """Decider._probs (decider.py:236-284) without calibration profiles / sampler: logits / T -> softmax * mask,
-        the caller-option renormalisation in fp64 and P(none), all in od_readout. Returns device tensors
-        (probs (N, K) fp32, renorm (N, K) fp64, p_none (N,) fp32)."""
+        """Decider._probs (decider.py:236-284) without calibration profiles / sampler for questions reading
+        `cache`: logits / T -> softmax * mask, caller-option renormalisation (fp64) and P(none) in od_readout."""
         logits, opt_mask = self.model.run(questions, cache)
         dev = logits.device
         T = torch.tensor([self.temperature_by_type.get(q.type, self.temperature) for q in questions],
@@ -83,21 +117,17 @@ class Decider:
             out[q.name] = a
         return out
 
+    def answers(self, plan: dict, probs) -> list:
+        """Host answers from the device results (one device->host read of probs, renorm and P(none))."""
+        got = self._answers(plan["questions"], *probs)
+        out = [{} for _ in range(plan["n_requests"])]
+        for q, i in zip(plan["questions"], plan["owner"]):
+            out[i][q.name.split("\x1f", 1)[1]] = got[q.name]
+        return out
+
     def decide_many(self, requests) -> list:
         """Independent requests in one batch: ONE state pass over all states and ONE row pass over all questions,
         each question reading its own request's state (decider.py:438-484). Returns per request {name: answer}."""
-        cache = self.encode_states([r.state for r in requests])
-        batch, owner = [], []
-        for i, r in enumerate(requests):
-            for q in r.questions:
-                q2 = copy.copy(q)
-                q2.state_idx = i
-                q2.name = f"{i}\x1f{q.name}"
-                batch.append(self._with_none(q2) if self.none_text else q2)
-                owner.append(i)
-        probs, renorm, p_none = self.probs(batch, cache)
-        got = self._answers(batch, probs, renorm, p_none)
-        out = [{} for _ in requests]
-        for q, i in zip(batch, owner):
-            out[i][q.name.split("\x1f", 1)[1]] = got[q.name]
-        return out
+        plan = self.plan(requests)
+        probs, _ = self.execute(plan)
+        return self.answers(plan, probs)

@@ -144,65 +144,74 @@ class V3Trunk:
         w = torch.softmax(self.p["layer_mix"].float(), 0)
         return torch.einsum("l,mld->md", w, f.float().view(f.shape[0], n, d)).float()
 
-    @torch.no_grad()
-    def forward(self, q_flat, q_lens, o_flat, o_lens, n_opt, opt_mask, state_lens):
-        """V3.forward (v3.py:606-709) for the state-free trunk. q_flat (sum lq, nL*d) question-token features,
-        o_flat (sum lo, nL*d) option-token features; q_lens/o_lens/n_opt/state_lens CPU longs (state_lens = the
-        state length of each question's state); opt_mask (N, K) bool on the device. Returns logits (N, K) fp32."""
-        p, dev = self.p, self.device
-        h, dm, df = self.cfg.n_heads, self.cfg.d_model, self.cfg.d_feat
-        N, K = opt_mask.shape
+    def prepare(self, q_lens, o_lens, n_opt, state_lens, up=None) -> dict:
+        """Host-side layout of V3.forward (v3.py:606-662) for the state-free trunk, uploaded once: option-token and
+        question-token destinations, option ids and positions, masks and additive biases. q_lens / o_lens / n_opt /
+        state_lens are CPU longs (state_lens: the real length of each question's state)."""
+        dev = self.device
+        N = n_opt.numel()
+        K = int(n_opt.max())
+        opt_mask = torch.arange(K)[None, :] < n_opt[:, None]
         opt_q = torch.repeat_interleave(torch.arange(N), n_opt)
         opt_k = torch.arange(int(n_opt.sum())) - torch.repeat_interleave(torch.cumsum(n_opt, 0) - n_opt, n_opt)
-        # ---- options -> (N, P, d)
         row, col, seg, pos, row_len = segment_layout(o_lens, opt_q, N)
         P = int(row_len.max())
-        rc = (row.to(dev), col.to(dev))
-        X = torch.zeros(N, P, df, device=dev)
-        X[rc] = self.mix(o_flat)
-        opt_id = torch.full((N, P), -1, dtype=torch.long, device=dev)
-        opt_id[rc] = opt_k[seg].to(dev)
-        opos = torch.zeros(N, P, dtype=torch.long, device=dev)
-        opos[rc] = pos.to(dev)
+        opt_id = torch.full((N, P), -1, dtype=torch.long)
+        opt_id[row, col] = opt_k[seg]
+        opos = torch.zeros(N, P, dtype=torch.long)
+        opos[row, col] = pos
         x_pad = opt_id < 0
-        # ---- context = question tokens only, positioned after the state (state-free trunk)
         Tc = int(q_lens.max())
-        C = torch.zeros(N, Tc, df, device=dev)
         qrow, qcol, _, _, _ = segment_layout(q_lens, torch.arange(N), N)
-        C[(qrow.to(dev), qcol.to(dev))] = self.mix(q_flat)
         t = torch.arange(Tc)[None, :]
         in_q = t < q_lens[:, None]
-        cpos = (t + state_lens[:, None]).to(dev)
-        c_pad = (~in_q).to(dev)
+        cpos = t + state_lens[:, None]
+        c_pad = ~in_q
+        up = up or (lambda x: x.to(dev, non_blocking=True))
+        return {"N": N, "K": K, "P": P, "Tc": Tc, "rc": (up(row), up(col)), "qrc": (up(qrow), up(qcol)),
+                "opt_id": up(opt_id), "opos": up(opos), "in_q": up(in_q), "cpos": up(cpos), "c_pad": up(c_pad),
+                "opt_mask": up(opt_mask)}
+
+    @torch.no_grad()
+    def run(self, plan: dict, q_flat: torch.Tensor, o_flat: torch.Tensor) -> torch.Tensor:
+        """V3.forward's device part (v3.py:627-709): option/context stacks, decision layers, CLS readout, score.
+        q_flat (sum lq, nL*d), o_flat (sum lo, nL*d) token features. Returns logits (N, K) fp32, NEG at pads."""
+        p, dev = self.p, self.device
+        h, dm, df = self.cfg.n_heads, self.cfg.d_model, self.cfg.d_feat
+        N, K, P, Tc = plan["N"], plan["K"], plan["P"], plan["Tc"]
+        opt_id, c_pad = plan["opt_id"], plan["c_pad"]
+        x_pad = opt_id < 0
+        same = ((opt_id[:, :, None] == opt_id[:, None, :]) & ~x_pad[:, :, None]).float()
+        b_cross = torch.zeros(c_pad.shape, device=dev).masked_fill(c_pad, NEG)[:, None, None, :]
+        own = opt_id[:, None, :] == torch.arange(K, device=dev)[None, :, None]
+        b_cls = torch.zeros(own.shape, device=dev).masked_fill(~own, NEG)[:, None]
+        X = torch.zeros(N, P, df, device=dev)
+        X[plan["rc"]] = self.mix(o_flat)
+        C = torch.zeros(N, Tc, df, device=dev)
+        C[plan["qrc"]] = self.mix(q_flat)
         C = C * (~c_pad)[..., None]
-        # ---- stack inputs
         x = F.linear(_scalenorm(X, p["in_norm.g"]), p["proj_option.weight"], p["proj_option.bias"])
         cin = _scalenorm(C, p["in_norm.g"])
-        c = torch.where(in_q.to(dev)[..., None], F.linear(cin, p["proj_question.weight"], p["proj_question.bias"]),
+        c = torch.where(plan["in_q"][..., None], F.linear(cin, p["proj_question.weight"], p["proj_question.bias"]),
                         F.linear(cin, p["proj_state.weight"], p["proj_state.bias"]))
-        same = (opt_id[:, :, None] == opt_id[:, None, :]) & ~x_pad[:, :, None]
-        b_cross = torch.zeros(c_pad.shape, device=dev).masked_fill(c_pad, NEG)[:, None, None, :]
+        opos, cpos = plan["opos"], plan["cpos"]
         for i in range(self.cfg.decision_layers):
             L = f"layers.{i}."
-            b_self = p[L + "same_bias"].view(1, h, 1, 1) * same[:, None].float()
+            b_self = p[L + "same_bias"].view(1, h, 1, 1) * same[:, None]
             b_self = b_self.masked_fill(x_pad[:, None, None, :], NEG)
             hx = _scalenorm(x, p[L + "n1.g"])
             x = x + _mha(p, L + "self_attn", h, hx, hx, b_self, opos, opos)
-            x = x + _mha(p, L + "cross", h, _scalenorm(x, p[L + "n2.g"]), _scalenorm(c, p[L + "n2c.g"]), b_cross,
-                         None, cpos)
+            x = x + _mha(p, L + "cross", h, _scalenorm(x, p[L + "n2.g"]), _scalenorm(c, p[L + "n2c.g"]),
+                         b_cross, None, cpos)
             x = x + _xatglu(p, L + "ff", _scalenorm(x, p[L + "n3.g"]))
-        # ---- CLS readout: one query per option attends only to that option's tokens
-        own = opt_id[:, None, :] == torch.arange(K, device=dev)[None, :, None]
-        b = torch.zeros(own.shape, device=dev).masked_fill(~own, NEG)[:, None]
         hc = p["cls.weight"].expand(N, K, dm)
-        hc = hc + _mha(p, "cls_attn", h, _scalenorm(hc, p["cls_nq.g"]), _scalenorm(x, p["cls_nkv.g"]), b, None, opos)
+        hc = hc + _mha(p, "cls_attn", h, _scalenorm(hc, p["cls_nq.g"]), _scalenorm(x, p["cls_nkv.g"]),
+                       b_cls, None, opos)
         hc = hc + _xatglu(p, "cls_ff", _scalenorm(hc, p["cls_nf.g"]))
         hc = _scalenorm(hc, p["final_norm.g"])
         logits = F.linear(hc, p["score.weight"], p["score.bias"]).squeeze(-1).float()
-        return logits.masked_fill(~opt_mask, NEG)
-
-
-# ------------------------------------------------------------------------------------------------ row passes
+        return logits.masked_fill(~plan["opt_mask"], NEG)
+# ------------------------------------------------------------------------------------------------ row plans
 def _rect(tok_lists, pad_id, width=None):
     lens = torch.tensor([len(t) for t in tok_lists], dtype=torch.long)
     L = width or max(1, int(lens.max()))
@@ -212,89 +221,121 @@ def _rect(tok_lists, pad_id, width=None):
     return ids, lens
 
 
-def branched_feats_qcache(bb: Backbone, tok, questions, cache: KVCache, list_cap: int = 16, chunk: int = 4096):
-    """Question cache path (v3.py:446-534). Returns (q_flat, lq, o_flat, lo): features of every question token and
-    every option token in question / option order, (tokens, nL*H) bf16 on the device; lengths on the CPU."""
-    dev, feats = bb.device, bb.cfg.feature_layers
+@dataclass
+class RowPass:
+    """One rectangular backbone pass over option (or question) rows, with the scatter of its real tokens."""
+    spec: PassSpec
+    dst: torch.Tensor | None = None     # destination index of each real token in the flat feature array
+    keep: torch.Tensor | None = None    # (R, w) bool: real tokens of the pass
+
+
+@dataclass
+class RowPlan:
+    """Everything the row passes of one call need, built on the host and uploaded once (no host sync later)."""
+    qcache: bool
+    question: RowPass | None            # question pass (question cache) with the flat question-token mask
+    options: list                       # RowPass per option chunk (or per [question ; option] chunk)
+    n_q_tok: int
+    n_o_tok: int
+    q_lens: torch.Tensor                # CPU
+    o_lens: torch.Tensor                # CPU
+    q_src: tuple | None = None          # rows-path: (row, col) of question tokens in the first row of each question
+
+
+def plan_rows(bb: Backbone, tok, questions, T: int, qcache: bool, list_cap: int = 16, chunk: int = 4096,
+              up=None) -> RowPlan:
+    """Host layout of the branched row passes. qcache: V3._branched_feats_qcache (v3.py:446-534) - one right-padded
+    question pass continuing each question's state at positions T + j, capturing its K/V, then option rows of
+    their own answer tokens (sorted by length, chunks as wide as their longest option, positions after their own
+    question). Otherwise V3._branched_feats (v3.py:393-444) - one row [question ; option] per option."""
+    dev = bb.device
+    up = up or (lambda x: x.to(dev, non_blocking=True))
     N = len(questions)
     q_tok = tok([answer_row_prefix(q.prompt, q.options, list_cap) for q in questions],
                 add_special_tokens=False)["input_ids"]
     o_tok = tok([answer_option_text(o) for q in questions for o in q.options], add_special_tokens=False)["input_ids"]
     n_opt = torch.tensor([len(q.options) for q in questions])
     row_q = torch.repeat_interleave(torch.arange(N), n_opt)
-    Qids, lq = _rect(q_tok, bb.pad_id)
-    Lq = Qids.shape[1]
     sidx = torch.tensor([q.state_idx for q in questions], dtype=torch.int32)
-    T = cache.T
-    # ---- question pass: right-padded, continuing each question's state (positions T + j)
-    qpos = (T + torch.arange(Lq, dtype=torch.int32)).expand(N, Lq)
-    spec = PassSpec(ids=Qids.to(dev), pos=qpos.to(dev), own_hi=lq.to(torch.int32).to(dev), cache=cache,
-                    row_state=sidx.to(dev), capture=True, features=tuple(feats))
-    fq, cap = bb.run(spec)
-    qm = (torch.arange(Lq)[None, :] < lq[:, None])
-    q_flat = fq[qm.to(dev)]
-    # ---- option rows: own answer tokens only, sorted by length, chunks as wide as their longest option
-    lo = torch.tensor([len(t) for t in o_tok], dtype=torch.long)
-    M = lo.numel()
-    o_flat = torch.empty(int(lo.sum()), fq.shape[-1], dtype=fq.dtype, device=dev)
-    o_start = torch.cumsum(lo, 0) - lo
-    order = torch.argsort(lo, stable=True)
-    q_len_dev = lq.to(torch.int32).to(dev)
-    for a in range(0, M, chunk):
-        rows = order[a:a + chunk]
-        w = max(2, int(lo[rows].max()))
-        ids, ln = _rect([o_tok[i] for i in rows.tolist()], bb.pad_id, w)
-        rq = row_q[rows]
-        pos = (T + lq[rq])[:, None].to(torch.int32) + torch.arange(w, dtype=torch.int32)[None, :]
-        spec = PassSpec(ids=ids.to(dev), pos=pos.to(dev), own_hi=ln.to(torch.int32).to(dev), cache=cache,
-                        row_state=sidx[rq].to(dev), qkv_prefix=cap, row_q=rq.to(torch.int32).to(dev),
-                        q_len=q_len_dev, features=tuple(feats))
-        fo, _ = bb.run(spec)
-        om = torch.arange(w)[None, :] < ln[:, None]
-        # scatter each row's real tokens back to its place in option order
-        dst = (o_start[rows][:, None] + torch.arange(w)[None, :])[om]
-        o_flat[dst.to(dev)] = fo[om.to(dev)]
-    return q_flat, lq, o_flat, lo
-
-
-def branched_feats(bb: Backbone, tok, questions, cache: KVCache, list_cap: int = 16, chunk: int = 4096):
-    """One row [question ; option] per option continuing the state (v3.py:393-444), for calls with few option rows.
-    Question features come from each question's first row. Returns (q_flat, lq, o_flat, lo)."""
-    dev, feats = bb.device, bb.cfg.feature_layers
-    N = len(questions)
-    q_tok = tok([answer_row_prefix(q.prompt, q.options, list_cap) for q in questions],
-                add_special_tokens=False)["input_ids"]
-    o_tok = tok([answer_option_text(o) for q in questions for o in q.options], add_special_tokens=False)["input_ids"]
-    n_opt = torch.tensor([len(q.options) for q in questions])
-    row_q = torch.repeat_interleave(torch.arange(N), n_opt)
     lq = torch.tensor([len(t) for t in q_tok], dtype=torch.long)
     lo = torch.tensor([len(t) for t in o_tok], dtype=torch.long)
-    rows_tok = [q_tok[int(row_q[i])] + o_tok[i] for i in range(len(o_tok))]
+    feats = tuple(bb.cfg.feature_layers)
+    M = lo.numel()
+    if qcache:
+        Qids, _ = _rect(q_tok, bb.pad_id)
+        Lq = Qids.shape[1]
+        qpos = (T + torch.arange(Lq, dtype=torch.int32)).expand(N, Lq).contiguous()
+        qkeep = torch.arange(Lq)[None, :] < lq[:, None]
+        qpass = RowPass(PassSpec(ids=up(Qids), pos=up(qpos), own_hi=up(lq.to(torch.int32)), row_state=up(sidx),
+                                 capture=True, features=feats), keep=up(qkeep))
+        o_start = torch.cumsum(lo, 0) - lo
+        order = torch.argsort(lo, stable=True)
+        q_len_dev = up(lq.to(torch.int32))
+        passes = []
+        for a in range(0, M, chunk):
+            rows = order[a:a + chunk]
+            w = max(2, int(lo[rows].max()))
+            ids, ln = _rect([o_tok[i] for i in rows.tolist()], bb.pad_id, w)
+            rq = row_q[rows]
+            pos = (T + lq[rq])[:, None].to(torch.int32) + torch.arange(w, dtype=torch.int32)[None, :]
+            keep = torch.arange(w)[None, :] < ln[:, None]
+            dst = (o_start[rows][:, None] + torch.arange(w)[None, :])[keep]
+            passes.append(RowPass(PassSpec(ids=up(ids), pos=up(pos), own_hi=up(ln.to(torch.int32)),
+                                           row_state=up(sidx[rq]), row_q=up(rq.to(torch.int32)), q_len=q_len_dev,
+                                           features=feats), dst=up(dst), keep=up(keep)))
+        return RowPlan(True, qpass, passes, int(lq.sum()), int(lo.sum()), lq, lo)
+    rows_tok = [q_tok[int(row_q[i])] + o_tok[i] for i in range(M)]
     ids, ln = _rect(rows_tok, bb.pad_id)
     W = ids.shape[1]
-    sidx = torch.tensor([q.state_idx for q in questions], dtype=torch.int32)
-    T = cache.T
-    fl = []
-    for a in range(0, len(rows_tok), chunk):
-        sl = slice(a, a + chunk)
-        pos = (T + torch.arange(W, dtype=torch.int32)).expand(ids[sl].shape[0], W)
-        spec = PassSpec(ids=ids[sl].to(dev), pos=pos.to(dev), own_hi=ln[sl].to(torch.int32).to(dev), cache=cache,
-                        row_state=sidx[row_q[sl]].to(dev), features=tuple(feats))
-        fl.append(bb.run(spec)[0])
-    Fr = torch.cat(fl, 0)
+    passes = []
+    o_dst_start = torch.cumsum(lo, 0) - lo
+    for a in range(0, M, chunk):
+        sl = slice(a, min(a + chunk, M))
+        R = sl.stop - sl.start
+        pos = (T + torch.arange(W, dtype=torch.int32)).expand(R, W).contiguous()
+        # option tokens of these rows: columns [lq, lq + lo) of each row
+        rr = torch.arange(sl.start, sl.stop)
+        cols = torch.arange(W)[None, :]
+        keep = (cols >= lq[row_q[rr]][:, None]) & (cols < (lq[row_q[rr]] + lo[rr])[:, None])
+        dst = (o_dst_start[rr][:, None] + cols - lq[row_q[rr]][:, None])[keep]
+        passes.append(RowPass(PassSpec(ids=up(ids[sl]), pos=up(pos), own_hi=up(ln[sl].to(torch.int32)),
+                                       row_state=up(sidx[row_q[sl]]), features=feats), dst=up(dst), keep=up(keep)))
     first = torch.cumsum(n_opt, 0) - n_opt
     qr, qc, _, _, _ = segment_layout(lq, torch.arange(N), N)
-    q_flat = Fr[(first[qr].to(dev), qc.to(dev))]
-    r2, c2, _, _, _ = segment_layout(lo, torch.arange(len(o_tok)), len(o_tok))
-    o_flat = Fr[(r2.to(dev), (lq[row_q][r2] + c2).to(dev))]
-    return q_flat, lq, o_flat, lo
+    return RowPlan(False, None, passes, int(lq.sum()), int(lo.sum()), lq, lo, (up(first[qr]), up(qc)))
+
+
+def run_rows(bb: Backbone, plan: RowPlan, cache: KVCache):
+    """Device part of the row passes. Returns (q_flat, o_flat) features (tokens, nL*H) bf16."""
+    dev = bb.device
+    nf = len(bb.cfg.feature_layers) * bb.cfg.hidden
+    o_flat = torch.empty(plan.n_o_tok, nf, dtype=bb.cfg.dtype, device=dev)
+    if plan.qcache:
+        qspec = plan.question.spec
+        qspec.cache = cache
+        fq, cap = bb.run(qspec)
+        q_flat = fq[plan.question.keep]
+        for rp in plan.options:
+            rp.spec.cache, rp.spec.qkv_prefix = cache, cap
+            fo, _ = bb.run(rp.spec)
+            o_flat[rp.dst] = fo[rp.keep]
+        return q_flat, o_flat
+    q_flat = None
+    first_rows = []
+    for rp in plan.options:
+        rp.spec.cache = cache
+        fo, _ = bb.run(rp.spec)
+        o_flat[rp.dst] = fo[rp.keep]
+        first_rows.append(fo)
+    Fr = torch.cat(first_rows, 0) if len(first_rows) > 1 else first_rows[0]
+    q_flat = Fr[plan.q_src]
+    return q_flat, o_flat
 
 
 # ------------------------------------------------------------------------------------------------ model
 class V3Model:
-    """Backbone rows + trunk: run(questions, cache) -> (logits (N, K) fp32, opt_mask (N, K) bool), the
-    DecisionModel.run surface (v3.py:588-590) for the branched answer-row configuration.
-    question_cache / qcache_min_rows: the serving switch of prepare_inference_ (decider.py:111-116)."""
+    """Backbone rows + trunk, the DecisionModel.run surface (v3.py:588-590) for the branched answer-row
+    configuration. question_cache / qcache_min_rows: the serving switch of prepare_inference_ (decider.py:111-116)."""
 
     def __init__(self, backbone: Backbone, trunk: V3Trunk, tokenizer, list_cap: int = 16,
                  question_cache: bool = True, qcache_min_rows: int = 12, chunk: int = 4096):
@@ -302,17 +343,18 @@ class V3Model:
         self.list_cap, self.question_cache, self.qcache_min_rows, self.chunk = (list_cap, question_cache,
                                                                                 qcache_min_rows, chunk)
 
-    def features(self, questions, cache: KVCache):
-        if self.question_cache and sum(len(q.options) for q in questions) >= self.qcache_min_rows:
-            return branched_feats_qcache(self.backbone, self.tok, questions, cache, self.list_cap, self.chunk)
-        return branched_feats(self.backbone, self.tok, questions, cache, self.list_cap, self.chunk)
+    def plan(self, questions, T: int, state_lens: list, up=None):
+        qc = self.question_cache and sum(len(q.options) for q in questions) >= self.qcache_min_rows
+        rows = plan_rows(self.backbone, self.tok, questions, T, qc, self.list_cap, self.chunk, up)
+        n_opt = torch.tensor([len(q.options) for q in questions])
+        sl = torch.tensor([state_lens[q.state_idx] for q in questions], dtype=torch.long)
+        return rows, self.trunk.prepare(rows.q_lens, rows.o_lens, n_opt, sl, up)
+
+    def execute(self, plan, cache: KVCache):
+        rows, tplan = plan
+        q_flat, o_flat = run_rows(self.backbone, rows, cache)
+        return self.trunk.run(tplan, q_flat, o_flat), tplan["opt_mask"]
 
     def run(self, questions, cache: KVCache):
-        dev = self.backbone.device
-        n_opt = torch.tensor([len(q.options) for q in questions])
-        K = int(n_opt.max())
-        opt_mask = (torch.arange(K)[None, :] < n_opt[:, None]).to(dev)
-        q_flat, lq, o_flat, lo = self.features(questions, cache)
-        state_lens = torch.tensor([cache.lens[q.state_idx] for q in questions], dtype=torch.long)
-        logits = self.trunk.forward(q_flat, lq, o_flat, lo, n_opt, opt_mask, state_lens)
-        return logits, opt_mask
+        """(logits (N, K) fp32, opt_mask (N, K) bool) for questions reading `cache`."""
+        return self.execute(self.plan(questions, cache.T, cache.lens), cache)

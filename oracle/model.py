@@ -1,0 +1,226 @@
+"""CPU oracle of the whole decision forward pass - TEST INFRASTRUCTURE and the timed CPU baseline, never the product.
+
+A PyTorch-CPU restatement of the reference's path with its bf16 rounding points (what src/opendecider computes with
+the transformers Qwen3.5 modules on a bf16 CPU model):
+  decoder        Qwen3_5DecoderLayer / Qwen3_5Attention / Qwen3_5MLP / Qwen3_5RMSNorm
+                 (transformers models/qwen3_5/modeling_qwen3_5.py:620-783), every linear through the A8W8 arithmetic
+                 installed at the reference's Int8Linear._fused seam (quant.py:150-152): per-token int8 activations by
+                 Int8Tensor.quantize's formula (quant.py:37-41, fp32 scale), exact int32 products (torch._int_mm),
+                 bf16((acc * s_x) * s_w); weights quantised as Int8Linear does (quant.py:124-127)
+  state pass     Backbone.prefix_cache_batch (backbone.py:347-368): left-padded, causal, the cache quantised per
+                 (state, head, token) by Int8Tensor.quantize (backbone.py:446)
+  row passes     V3._branched_feats_qcache / _branched_feats (v3.py:393-534) with shared_prefix_attention's
+                 _split_attention CPU branch (prefix_attn.py:58-76) over the materialised int8 state K/V
+  trunk/readout  the trunk of opendecider_b200.v3 on the CPU (plain PyTorch, the same code the GPU path runs, pinned
+                 to the reference by tests/golden/e2e_config1.npz) and Decider._probs' softmax (decider.py:255-257)
+Only tests/, __graft_entry__.smoke() and bench.py (cpu_baseline, --impl reference) may import this module.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import ops
+
+BF = torch.bfloat16
+
+
+def _quant_w(w: torch.Tensor):
+    wf = w.float()
+    s = wf.abs().amax(1, keepdim=True).clamp_min(1e-8) / 127.0
+    return torch.round(wf / s).clamp_(-127, 127).to(torch.int8), s.to(w.dtype)
+
+
+def a8w8(x: torch.Tensor, qw: torch.Tensor, sw: torch.Tensor) -> torch.Tensor:
+    """bf16 x (M, K) through the W8A8 arithmetic; qw (N, K) int8, sw (N, 1) bf16 -> bf16 (M, N)."""
+    xf = x.float()
+    s = xf.abs().amax(-1, keepdim=True).clamp_min(1e-8) / 127.0
+    q = torch.round(xf / s).clamp_(-127, 127).to(torch.int8)
+    M = q.shape[0]
+    if M <= 16:                                                 # _int_mm wants more than 16 rows: zero rows are exact
+        q = torch.cat([q, q.new_zeros(17 - M, q.shape[1])])
+    acc = torch._int_mm(q, qw.t())[:M]
+    return ((acc.float() * s) * sw.float().view(1, -1)).to(BF)
+
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    xf = x.float()
+    out = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
+    return (out * (1.0 + w.float())).to(x.dtype)
+
+
+def _rot(x, cos, sin):
+    D = x.shape[-1]
+    rh = torch.cat([-x[..., D // 2:], x[..., : D // 2]], -1)
+    return (x * cos) + (rh * sin)
+
+
+class OracleDecoder:
+    """The int8 decoder on the CPU. sd: float (bf16) weights under HF's Qwen3_5TextModel names; `layers` limits the
+    pass to the first n layers (the timed baseline samples a few layers and extrapolates)."""
+
+    def __init__(self, cfg, sd: dict, layers: int | None = None):
+        self.cfg = cfg
+        self.n = layers or cfg.layers
+        self.q = {}
+        for name, w in sd.items():
+            if not name.endswith("norm.weight"):
+                self.q[name[: -len(".weight")]] = _quant_w(w)
+        self.norm = {k: v for k, v in sd.items() if k.endswith("norm.weight")}
+        self.cos, self.sin = ops.rope_tables(cfg.head_dim, cfg.rope_theta, cfg.max_pos)
+
+    def embed(self, ids):
+        qw, s = self.q["embed_tokens"]
+        return qw[ids].to(BF) * s[ids]
+
+    def layer(self, i, x, pos, attend):
+        """One decoder layer on (R, t, H) bf16; attend(i, q, k, v) -> (R, t, Hq*D) bf16. Returns (x, k, v)."""
+        cfg, p = self.cfg, f"layers.{i}."
+        R, t, H = x.shape
+        D, Hq, Hkv = cfg.head_dim, cfg.heads, cfg.kv_heads
+        h = rmsnorm(x, self.norm[p + "input_layernorm.weight"], cfg.eps).reshape(R * t, H)
+        qg = a8w8(h, *self.q[p + "self_attn.q_proj"]).view(R, t, Hq, 2 * D)
+        q, gate = qg[..., :D], qg[..., D:].reshape(R, t, Hq * D)
+        k = a8w8(h, *self.q[p + "self_attn.k_proj"]).view(R, t, Hkv, D)
+        v = a8w8(h, *self.q[p + "self_attn.v_proj"]).view(R, t, Hkv, D)
+        q = rmsnorm(q, self.norm[p + "self_attn.q_norm.weight"], cfg.eps)
+        k = rmsnorm(k, self.norm[p + "self_attn.k_norm.weight"], cfg.eps)
+        c, s = self.cos[pos][:, :, None, :], self.sin[pos][:, :, None, :]
+        q, k = _rot(q, c, s), _rot(k, c, s)
+        o = attend(i, q, k, v) * torch.sigmoid(gate)
+        x = x + a8w8(o.reshape(R * t, Hq * D), *self.q[p + "self_attn.o_proj"]).view(R, t, H)
+        h2 = rmsnorm(x, self.norm[p + "post_attention_layernorm.weight"], cfg.eps).reshape(R * t, H)
+        g = a8w8(h2, *self.q[p + "mlp.gate_proj"])
+        u = a8w8(h2, *self.q[p + "mlp.up_proj"])
+        m = torch.nn.functional.silu(g) * u
+        x = x + a8w8(m, *self.q[p + "mlp.down_proj"]).view(R, t, H)
+        return x, k, v
+
+    def run(self, ids, pos, attend, features=()):
+        """Rows (R, t) -> per-layer (k, v) and the requested features (R, t, nL*H) bf16."""
+        x = self.embed(ids)
+        feats, kv = {}, []
+        for i in range(self.n):
+            x, k, v = self.layer(i, x, pos, attend)
+            kv.append((k, v))
+            feats[i + 1] = x
+        out = None
+        if features:
+            feats["final"] = rmsnorm(x, self.norm["norm.weight"], self.cfg.eps)
+            out = torch.cat([feats[f if f == "final" else int(f)] for f in features], -1)
+        return out, kv
+
+
+def causal_attend(pad):
+    """Causal attention of the state pass with left padding (keys before pad[r] masked), fp32 math."""
+    def f(i, q, k, v):
+        R, t, Hq, D = q.shape
+        g = Hq // k.shape[2]
+        qf = q.float().transpose(1, 2)
+        kf = k.float().repeat_interleave(g, 2).transpose(1, 2)
+        vf = v.float().repeat_interleave(g, 2).transpose(1, 2)
+        s = qf @ kf.transpose(-1, -2) * D ** -0.5
+        j = torch.arange(t)
+        ok = (j[None, :] <= j[:, None])[None] & (j[None, None, :] >= pad.view(-1, 1, 1))
+        s = s.masked_fill(~ok[:, None], float("-inf"))
+        o = torch.softmax(s, -1).nan_to_num(0.0) @ vf
+        return o.transpose(1, 2).reshape(R, t, Hq * D).to(BF)
+    return f
+
+
+class OracleDecision:
+    """decide_many on the CPU: state pass, question-cache row passes, trunk, readout."""
+
+    def __init__(self, cfg, sd, trunk, tok, temps: dict, temperature: float, layers: int | None = None,
+                 list_cap: int = 16, qcache_min_rows: int = 12, none_text: str = "none of the above"):
+        self.dec = OracleDecoder(cfg, sd, layers)
+        self.cfg, self.trunk, self.tok, self.temps, self.temperature = cfg, trunk, tok, temps, temperature
+        self.list_cap, self.qcache_min_rows, self.none_text = list_cap, qcache_min_rows, none_text
+
+    def state_pass(self, states):
+        from opendecider_b200.batching import state_text
+        seqs = self.tok([state_text(s) for s in states], add_special_tokens=False)["input_ids"]
+        lens = [len(s) for s in seqs]
+        S, T = len(seqs), max(lens)
+        ids = torch.tensor([[0] * (T - n) + list(s) for s, n in zip(seqs, lens)])
+        pad = torch.tensor([T - n for n in lens])
+        pos = torch.arange(T).expand(S, T)
+        _, kv = self.dec.run(ids, pos, causal_attend(pad))
+        cache = []
+        for k, v in kv:                                   # Int8Tensor.quantize then materialize(): bf16 prefix
+            kq, ks, _ = ops.quantize_rows(k.transpose(1, 2).float().numpy(), "bf16")
+            vq, vs, _ = ops.quantize_rows(v.transpose(1, 2).float().numpy(), "bf16")
+            cache.append((ops.materialize_int8(torch.from_numpy(kq), torch.from_numpy(ks).to(BF)),
+                          ops.materialize_int8(torch.from_numpy(vq), torch.from_numpy(vs).to(BF))))
+        return cache, pad, T, lens
+
+    def decide(self, requests):
+        """Returns (probs (N, K), renorm (N, K) fp64, p_none (N,)) numpy, questions in request order."""
+        import copy
+        from opendecider_b200.batching import MAX_OPTIONS, answer_option_text, answer_row_prefix
+        cache, pad, T, lens = self.state_pass([r.state for r in requests])
+        qs = []
+        for i, r in enumerate(requests):
+            for q in r.questions:
+                q2 = copy.copy(q)
+                q2.state_idx = i
+                if len(q.options) < MAX_OPTIONS:
+                    q2.options = list(q.options) + [self.none_text]
+                    q2.none_col = len(q.options)
+                qs.append(q2)
+        N = len(qs)
+        q_tok = self.tok([answer_row_prefix(q.prompt, q.options, self.list_cap) for q in qs])["input_ids"]
+        o_tok = self.tok([answer_option_text(o) for q in qs for o in q.options])["input_ids"]
+        n_opt = torch.tensor([len(q.options) for q in qs])
+        row_q = torch.repeat_interleave(torch.arange(N), n_opt)
+        lq = torch.tensor([len(t) for t in q_tok])
+        lo = torch.tensor([len(t) for t in o_tok])
+        sidx = torch.tensor([q.state_idx for q in qs])
+        feats = tuple(self.cfg.feature_layers)
+        Lq = int(lq.max())
+        Qids = torch.zeros(N, Lq, dtype=torch.long)
+        for j, t in enumerate(q_tok):
+            Qids[j, : len(t)] = torch.tensor(t)
+        pm_state = torch.arange(T)[None, :] >= pad[:, None]
+
+        def attend_q(i, q, k, v):                         # question pass: state prefix + own (causal)
+            Kp, Vp = cache[i]
+            out = torch.empty(q.shape[0], q.shape[1], q.shape[2] * q.shape[3], dtype=BF)
+            for j in range(q.shape[0]):
+                s = int(sidx[j])
+                o = ops.split_attention(q[j:j + 1].transpose(1, 2), k[j:j + 1].transpose(1, 2),
+                                        v[j:j + 1].transpose(1, 2), Kp[s], Vp[s], pm_state[s], q.shape[3] ** -0.5)
+                out[j] = o.to(BF).transpose(1, 2).reshape(q.shape[1], -1)
+            return out
+
+        qpos = (T + torch.arange(Lq)).expand(N, Lq)
+        fq, qkv = self.dec.run(Qids, qpos, attend_q, feats)
+        q_flat = fq[torch.arange(Lq)[None, :] < lq[:, None]]
+        o_flat = torch.empty(int(lo.sum()), fq.shape[-1], dtype=fq.dtype)
+        o_start = torch.cumsum(lo, 0) - lo
+        for m in range(lo.numel()):                       # option rows, one at a time (width >= 2)
+            w = max(2, int(lo[m]))
+            ids = torch.zeros(1, w, dtype=torch.long)
+            ids[0, : lo[m]] = torch.tensor(o_tok[m])
+            qj = int(row_q[m])
+            s = int(sidx[qj])
+
+            def attend_o(i, q, k, v, qj=qj, s=s):
+                Kp, Vp = cache[i]
+                Kq, Vq = qkv[i]
+                Kc = torch.cat([Kp[s], Kq[qj].transpose(0, 1)], 1)
+                Vc = torch.cat([Vp[s], Vq[qj].transpose(0, 1)], 1)
+                pmc = torch.cat([pm_state[s], torch.arange(Lq) < lq[qj]])
+                o = ops.split_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), Kc, Vc, pmc,
+                                        q.shape[3] ** -0.5)
+                return o.to(BF).transpose(1, 2).reshape(1, q.shape[1], -1)
+
+            pos = (T + lq[qj] + torch.arange(w))[None, :]
+            fo, _ = self.dec.run(ids, pos, attend_o, feats)
+            o_flat[o_start[m]: o_start[m] + lo[m]] = fo[0, : lo[m]]
+        sl = torch.tensor([lens[q.state_idx] for q in qs])
+        tplan = self.trunk.prepare(lq, lo, n_opt, sl)
+        logits = self.trunk.run(tplan, q_flat, o_flat)
+        Tq = [self.temps.get(q.type, self.temperature) for q in qs]
+        nc = [getattr(q, "none_col", -1) for q in qs]
+        probs, ren, pn = ops.readout(logits.numpy(), Tq, tplan["opt_mask"].numpy(), none_col=nc)
+        return probs, ren, pn, logits

@@ -1,0 +1,27 @@
+"""The CPU oracle of the whole decision forward (oracle/model.py, the timed CPU baseline) reproduces the reference's
+own Decider.decide_many on config 1 (tests/golden/e2e_config1.npz): probabilities within 1e-3."""
+import numpy as np
+
+from oracle.model import OracleDecision
+from opendecider_b200 import synthetic as syn
+from opendecider_b200.backbone import DecoderConfig, synthetic_weights
+from opendecider_b200.v3 import TrunkConfig, V3Trunk, trunk_state_dict
+
+FEATURE_LAYERS = (1, 3, "final")
+TRUNK = dict(d_model=64, n_heads=4, decision_layers=2)
+TEMPS = {"choice": 1.4978350400924683, "noul": 1.2169979810714722, "score": 1.5226973295211792}
+
+
+def test_oracle_decide_matches_reference():
+    cfg = DecoderConfig.tiny(feature_layers=FEATURE_LAYERS)
+    tc = TrunkConfig(d_feat=cfg.hidden, n_feat_layers=len(FEATURE_LAYERS), **TRUNK)
+    trunk = V3Trunk(tc, trunk_state_dict(tc, seed=0), "cpu")
+    reqs, tok = syn.decision_requests(1, seed=0)
+    od = OracleDecision(cfg, synthetic_weights(cfg, seed=0), trunk, tok, TEMPS, 1.419344425201416,
+                        qcache_min_rows=32)
+    probs, ren, pn, logits = od.decide(reqs)
+    g = np.load("tests/golden/e2e_config1.npz")
+    K = g["qcache.probs"].shape[1]
+    assert np.abs(ren[:, :K] - g["qcache.probs"]).max() < 1e-3
+    assert np.abs(pn - g["qcache.none"]).max() < 1e-3
+    assert np.abs(logits.numpy() - g["qcache.logits"]).max() < 2e-2
