@@ -185,6 +185,99 @@ def traffic_per_launch():
     return None
 
 
+def _peaks():
+    pk = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    return json.load(open(pk)) if os.path.exists(pk) else {}
+
+
+def _flush_l2(buf):
+    buf.add_(1)                                                # writes 256 MB: more than the 126 MB L2
+
+
+def op_gemm(args):
+    """the W8A8 GEMM at M in {512, 2048, 8192} x (K, N) in {(4096, 4096), (4096, 12288),
+    (12288, 4096)}; one JSON line per shape (TOP/s vs 2 x measured bf16, GB/s of the algorithmic bytes,
+    cuBLASLt's int8 GEMM (torch._int_mm) on the same operands for context). L2 flushed between iterations."""
+    from opendecider_b200 import _lib
+    from opendecider_b200 import synthetic as syn
+    dev = torch.device("cuda", 0)
+    shapes = [tuple(int(v) for v in x.split("x")) for x in args.shapes.split(",")] if args.shapes else \
+        [(m, n, k) for m in (512, 2048, 8192) for (k, n) in ((4096, 4096), (4096, 12288), (12288, 4096))]
+    peak = 2.0 * _peaks().get("bf16_tflops", 1590.0)            # burst: a kernel timed alone
+    flush = torch.zeros(64 << 20, dtype=torch.float32, device=dev)
+    for (M, N, K) in shapes:
+        gc = syn.gemm_case(M, N, K, seed=0)
+        xq, sx = _lib.quant_rows(gc.x.to(dev), scale_dtype=torch.float32)
+        wq, sw = gc.qweight.to(dev), gc.wscale.to(dev).view(-1)
+        y = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+        ts, tc = [], []
+        for i in range(args.warmup + args.steps):
+            _flush_l2(flush)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            _lib.gemm_w8a8(xq, sx.view(-1), wq, sw, _lib.OD_EPI_BF16, out=y)
+            b.record()
+            _flush_l2(flush)
+            c, d = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            c.record()
+            torch._int_mm(xq, wq.t())
+            d.record()
+            torch.cuda.synchronize()
+            if i >= args.warmup:
+                ts.append(a.elapsed_time(b))
+                tc.append(c.elapsed_time(d))
+        t = statistics.median(ts) / 1e3
+        ops = 2.0 * M * N * K
+        byts = M * K + N * K + 2 * M * N + 4 * M + 2 * N
+        print(json.dumps({"op": "gemm_w8a8", "shape": {"M": M, "N": N, "K": K}, "ms": t * 1e3,
+                          "tops": ops / t / 1e12, "peak_tops": peak, "frac": ops / t / 1e12 / peak,
+                          "gbs": byts / t / 1e9, "cublaslt_int8_tops": ops / (statistics.median(tc) / 1e3) / 1e12,
+                          "l2": "flushed between iterations"}))
+
+
+def op_attn(args):
+    """branched shared-prefix attention, 32 requests x 4096-token int8 state (fp16 scales),
+    32 q / 8 kv heads, D 128, 64 option rows x 16 tokens per request; plus the diagnostic bandwidth-bound shape
+    (3 rows x 2 tokens per request). GB/s of the algorithmic bytes and TFLOP/s."""
+    from opendecider_b200 import _lib
+    dev = torch.device("cuda", 0)
+    peaks = _peaks()
+    for S, rows, t in ((32, 64, 16), (32, 3, 2)):
+        T, Hq, Hkv, D = 4096, 32, 8, 128
+        g = torch.Generator(device=dev).manual_seed(0)
+        K16 = torch.randn(S, Hkv, T, D, generator=g, device=dev).to(torch.float16)
+        V16 = torch.randn(S, Hkv, T, D, generator=g, device=dev).to(torch.float16)
+        Kq, ks = _lib.quant_rows(K16.view(-1, D))
+        Vq, vs = _lib.quant_rows(V16.view(-1, D))
+        del K16, V16
+        R = S * rows
+        q = torch.randn(R, t, Hq, D, generator=g, device=dev).to(torch.bfloat16)
+        k = torch.randn(R, t, Hkv, D, generator=g, device=dev).to(torch.bfloat16)
+        v = torch.randn(R, t, Hkv, D, generator=g, device=dev).to(torch.bfloat16)
+        row_state = torch.arange(S, dtype=torch.int32, device=dev).repeat_interleave(rows)
+        kw = dict(Kp=Kq.view(S, Hkv, T, D), Vp=Vq.view(S, Hkv, T, D), ksc=ks.view(S, Hkv, T),
+                  vsc=vs.view(S, Hkv, T), row_state=row_state)
+        out = torch.empty_like(q)
+        ts = []
+        for i in range(args.warmup + args.steps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            _lib.prefix_attn(q, k, v, D ** -0.5, out=out, **kw)
+            b.record()
+            torch.cuda.synchronize()
+            if i >= args.warmup:
+                ts.append(a.elapsed_time(b))
+        tm = statistics.median(ts) / 1e3
+        flops = R * t * Hq * (T + (t + 1) / 2) * D * 4.0
+        byts = S * Hkv * T * (2 * D + 2 * 2) + 2 * R * t * Hq * D * 2 + 2 * R * t * Hkv * D * 2
+        print(json.dumps({"op": "prefix_attn", "shape": {"requests": S, "state_tokens": T, "rows": rows, "t": t,
+                                                         "Hq": Hq, "Hkv": Hkv, "D": D},
+                          "ms": tm * 1e3, "tflops": flops / tm / 1e12, "gbs": byts / tm / 1e9,
+                          "frac_hbm": byts / tm / 1e9 / peaks.get("hbm_gbs", 6650.0),
+                          "frac_bf16": flops / tm / 1e12 / peaks.get("bf16_tflops", 1590.0),
+                          "flop_per_byte": flops / byts}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -193,7 +286,15 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--config", type=int, default=4, choices=[1, 4])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--op", default="decide", choices=["decide", "gemm", "attn"],
+                    help="decide: the headline decision throughput; gemm / attn: operator configs 2 / 3")
+    ap.add_argument("--shapes", default="", help="--op gemm: comma-separated MxNxK list")
+    ap.add_argument("--breakdown", action="store_true", help="print per-kernel device time of one step to stderr")
     args = ap.parse_args()
+    if args.op == "gemm":
+        return op_gemm(args)
+    if args.op == "attn":
+        return op_attn(args)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -256,11 +357,13 @@ def main():
     torch.cuda.synchronize()
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("od_timed")
     e0.record()
     for _ in range(args.steps):
         probs, cache = decider.execute(plan, cache)
         gather(probs)
     e1.record()
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     barrier()
     launches = (_lib.LAUNCHES[0] - l0) // max(1, args.steps)
@@ -272,6 +375,21 @@ def main():
     gemm_launches = len(probe) // max(1, args.steps)
     decisions = n_dec_local * world * args.steps
     value = decisions / t_dev
+
+    if args.breakdown and rank == 0:
+        _lib.KERNEL_PROBE = {}
+        torch.cuda.synchronize()
+        b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        b0.record()
+        probs, cache = decider.execute(plan, cache)
+        b1.record()
+        torch.cuda.synchronize()
+        summ = _lib.probe_summary(_lib.KERNEL_PROBE)
+        _lib.KERNEL_PROBE = None
+        tot = b0.elapsed_time(b1)
+        for k, (n, ms) in sorted(summ.items(), key=lambda kv: -kv[1][1]):
+            print(f"breakdown {k:20s} launches {n:5d}  {ms:9.2f} ms  {100 * ms / tot:5.1f} %", file=sys.stderr)
+        print(f"breakdown step {tot:.2f} ms, kernels {sum(v[1] for v in summ.values()):.2f} ms", file=sys.stderr)
 
     # ---- e2e: the public API per step (tokenise, plan, one pinned H2D copy, kernels, gather, D2H answers)
     for _ in range(1):

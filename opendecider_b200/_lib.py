@@ -58,6 +58,31 @@ _lib = None
 LAUNCHES = [0]
 # optional per-launch timing of od_gemm_w8a8: a list that receives (start event, end event, int ops) per launch
 GEMM_PROBE: list | None = None
+# optional per-launch timing of every wrapper: dict name -> list of (start event, end event)
+KERNEL_PROBE: dict | None = None
+
+
+def _probed(fn):
+    """Record CUDA events around a wrapper's launch when KERNEL_PROBE is set (diagnostics; off by default)."""
+    import functools
+
+    @functools.wraps(fn)
+    def w(*a, **k):
+        probe = KERNEL_PROBE
+        if probe is None:
+            return fn(*a, **k)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        out = fn(*a, **k)
+        e1.record()
+        probe.setdefault(fn.__name__, []).append((e0, e1))
+        return out
+    return w
+
+
+def probe_summary(probe: dict) -> dict:
+    """{wrapper: (launches, total ms)} of a KERNEL_PROBE after synchronisation."""
+    return {k: (len(v), sum(a.elapsed_time(b) for a, b in v)) for k, v in probe.items()}
 
 
 def load(path: str = LIB_PATH) -> ctypes.CDLL:
@@ -113,6 +138,7 @@ def device_error(device: torch.device | None = None) -> int:
 
 
 # ------------------------------------------------------------------------------------------------ wrappers
+@_probed
 def quant_rows(x: torch.Tensor, scale_dtype: torch.dtype | None = None, inv_s: torch.Tensor | None = None,
                q: torch.Tensor | None = None, scale: torch.Tensor | None = None):
     """Int8Tensor.quantize over the last dim of a 2-D (row-strided) tensor: returns (q int8 (M, K), scale (M, 1))."""
@@ -127,6 +153,7 @@ def quant_rows(x: torch.Tensor, scale_dtype: torch.dtype | None = None, inv_s: t
     return q, scale
 
 
+@_probed
 def dequant_rows(q: torch.Tensor, scale: torch.Tensor, out_dtype: torch.dtype) -> torch.Tensor:
     dev = _need_cuda(q, scale)
     M, K = q.reshape(-1, q.shape[-1]).shape
@@ -136,6 +163,7 @@ def dequant_rows(q: torch.Tensor, scale: torch.Tensor, out_dtype: torch.dtype) -
     return y
 
 
+@_probed
 def kv_append(k: torch.Tensor, v: torch.Tensor, kq: torch.Tensor, vq: torch.Tensor, ksc: torch.Tensor,
               vsc: torch.Tensor, t0: int) -> None:
     """Quantise new keys/values k, v (S, t, Hkv, D) (any strides, last dim contiguous) into the int8 cache
@@ -149,6 +177,7 @@ def kv_append(k: torch.Tensor, v: torch.Tensor, kq: torch.Tensor, vq: torch.Tens
                                   kq.shape[2], t0, _stream(dev)), "od_kv_append_i8")
 
 
+@_probed
 def rmsnorm_res_quant(x: torch.Tensor, w: torch.Tensor, eps: float, res_in: torch.Tensor | None = None,
                       res_out: torch.Tensor | None = None, inv_s: torch.Tensor | None = None,
                       y_out: torch.Tensor | None = None, want_q: bool = True, q: torch.Tensor | None = None,
@@ -165,6 +194,7 @@ def rmsnorm_res_quant(x: torch.Tensor, w: torch.Tensor, eps: float, res_in: torc
     return (q, s) if want_q else (None, None)
 
 
+@_probed
 def gemm_w8a8(a: torch.Tensor, sa: torch.Tensor | None, w: torch.Tensor, sw: torch.Tensor | None,
               epilogue: int = OD_EPI_BF16, out: torch.Tensor | None = None) -> torch.Tensor:
     """int8 (M, K) x int8 (N, K)^T on tcgen05: bf16 (M, N) / SwiGLU bf16 (M, N/2) / int32 (M, N)."""
@@ -190,6 +220,7 @@ def gemm_w8a8(a: torch.Tensor, sa: torch.Tensor | None, w: torch.Tensor, sw: tor
     return out
 
 
+@_probed
 def embed_i8(ids: torch.Tensor, qweight: torch.Tensor, scale: torch.Tensor, out: torch.Tensor | None = None):
     dev = _need_cuda(ids, qweight, scale)
     ids = ids.reshape(-1).to(torch.int64).contiguous()
@@ -200,6 +231,7 @@ def embed_i8(ids: torch.Tensor, qweight: torch.Tensor, scale: torch.Tensor, out:
     return out
 
 
+@_probed
 def qk_norm_rope(qkv: torch.Tensor, pos: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, qnorm_w: torch.Tensor,
                  knorm_w: torch.Tensor, eps: float, Hq: int, Hkv: int, D: int, q_out=None, k_out=None, v_out=None):
     dev = _need_cuda(qkv, pos, cos, sin)
@@ -212,6 +244,7 @@ def qk_norm_rope(qkv: torch.Tensor, pos: torch.Tensor, cos: torch.Tensor, sin: t
     return q_out, k_out, v_out
 
 
+@_probed
 def gate_quant(o: torch.Tensor, qkv: torch.Tensor, Hq: int, D: int, q=None, s=None):
     dev = _need_cuda(o, qkv)
     M = o.shape[0]
@@ -222,6 +255,7 @@ def gate_quant(o: torch.Tensor, qkv: torch.Tensor, Hq: int, D: int, q=None, s=No
     return q, s
 
 
+@_probed
 def prefix_attn(q: torch.Tensor, k_own: torch.Tensor, v_own: torch.Tensor, sm_scale: float, *,
                 Kp=None, Vp=None, ksc=None, vsc=None, row_state=None, p_lo=None, p_hi=None, pmask=None,
                 Kq=None, Vq=None, row_q=None, q_len=None, own_lo=None, own_hi=None, out=None, want_lse: bool = False):
@@ -244,6 +278,7 @@ def prefix_attn(q: torch.Tensor, k_own: torch.Tensor, v_own: torch.Tensor, sm_sc
     return (out, lse) if want_lse else out
 
 
+@_probed
 def readout(logits: torch.Tensor, T: torch.Tensor, mask: torch.Tensor, bias: torch.Tensor | None = None,
             none_col: torch.Tensor | None = None, want_renorm: bool = True):
     """softmax(logits / T + bias) * mask -> probs (N, K) fp32; renorm (N, K) fp64; p_none (N,) fp32."""

@@ -52,6 +52,18 @@ class Decider:
         seqs = self.model.tok(texts, add_special_tokens=False)["input_ids"]
         return self.model.backbone.plan_state(seqs, up)
 
+    def plan_questions(self, requests) -> dict:
+        """The host-only part of a plan (the question list and owners) for building answers from gathered results."""
+        batch, owner = [], []
+        for i, r in enumerate(requests):
+            for q in r.questions:
+                q2 = copy.copy(q)
+                q2.state_idx = i
+                q2.name = f"{i}\x1f{q.name}"
+                batch.append(self._with_none(q2) if self.none_text else q2)
+                owner.append(i)
+        return {"questions": batch, "owner": owner, "n_requests": len(requests)}
+
     def plan(self, requests) -> dict:
         """Everything host-side of one decide_many call (tokenisation, layouts, readout constants), staged in one
         pinned buffer and uploaded by one copy. The plan's device views stay valid until the next plan()."""
