@@ -242,7 +242,10 @@ def op_attn(args):
     from opendecider_b200 import _lib
     dev = torch.device("cuda", 0)
     peaks = _peaks()
-    for S, rows, t in ((32, 64, 16), (32, 3, 2)):
+    shapes = ((args.requests or 32, 64, 16), (args.requests or 32, 3, 2))
+    if args.shapes:
+        shapes = tuple(tuple(int(v) for v in x.split("x")) for x in args.shapes.split(","))
+    for S, rows, t in shapes:
         T, Hq, Hkv, D = 4096, 32, 8, 128
         g = torch.Generator(device=dev).manual_seed(0)
         K16 = torch.randn(S, Hkv, T, D, generator=g, device=dev).to(torch.float16)
@@ -257,6 +260,10 @@ def op_attn(args):
         row_state = torch.arange(S, dtype=torch.int32, device=dev).repeat_interleave(rows)
         kw = dict(Kp=Kq.view(S, Hkv, T, D), Vp=Vq.view(S, Hkv, T, D), ksc=ks.view(S, Hkv, T),
                   vsc=vs.view(S, Hkv, T), row_state=row_state)
+        per = max(1, min(rows, 128 // (t * (Hq // Hkv))))      # rows of one request share a 128-slot tile
+        starts = [(s * rows + a, min(per, rows - a)) for s in range(S) for a in range(0, rows, per)]
+        kw["row_groups"] = torch.tensor(starts, dtype=torch.int32, device=dev)
+        kw["max_group_rows"] = per
         out = torch.empty_like(q)
         ts = []
         for i in range(args.warmup + args.steps):
@@ -288,7 +295,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--op", default="decide", choices=["decide", "gemm", "attn"],
                     help="decide: the headline decision throughput; gemm / attn: operator configs 2 / 3")
-    ap.add_argument("--shapes", default="", help="--op gemm: comma-separated MxNxK list")
+    ap.add_argument("--shapes", default="", help="--op gemm: MxNxK list; --op attn: requestsxrowsxt list")
+    ap.add_argument("--requests", type=int, default=0, help="--op attn: requests (default 32)")
     ap.add_argument("--breakdown", action="store_true", help="print per-kernel device time of one step to stderr")
     args = ap.parse_args()
     if args.op == "gemm":

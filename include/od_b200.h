@@ -148,20 +148,26 @@ OD_API int od_gate_quant(const void* o, const void* qkv, int64_t ldqkv, int64_t 
  *      own_lo[r] <= j < own_hi[r] (own_lo / own_hi may be NULL: 0 / t; left-padded rows set own_lo).
  * Output o (R, t, Hq, D) bf16 and optionally lse (R, Hq, t) fp32 (natural log, -inf when no key is visible; such
  * rows output 0, wide_attention.py:62-67). q (R, t, Hq, D) bf16. GQA: query head h reads kv head h / (Hq / Hkv).
- * Every row sees the same key layout whatever its index: outputs do not depend on row order.
+ * row_groups (G, 2) int32 [first row, rows] (optional; NULL = every row alone): consecutive rows that share their
+ * state and question and are processed together in one 128-slot tensor-core tile (rows x t x Hq/Hkv <= 128 when a
+ * group has more than one row); they still attend only their own keys.
+ * Every row sees the same key layout whatever its index or group: outputs do not depend on row order.
+ * Runs on tcgen05 (S = Q K^T and O += P V in TMEM); head_dim 64 or 128.
  */
 typedef struct {
   int64_t R, t, S, T, NQ, Lq;   /* rows, tokens per row, states, prefix capacity, questions, question length */
   int Hq, Hkv, D;
   int scale_dtype;              /* dtype of ksc/vsc: OD_BF16 or OD_F16 */
   float sm_scale;               /* softmax scale (head_dim ** -0.5) */
+  int64_t G;                    /* number of row groups (used when row_groups != NULL) */
+  int max_group_rows;           /* largest group (used when row_groups != NULL) */
 } od_attn_dims;
 
 OD_API int od_prefix_attn(const void* q, const int8_t* Kp, const int8_t* Vp, const void* ksc, const void* vsc,
                           const int32_t* row_state, const int32_t* p_lo, const int32_t* p_hi, const uint8_t* pmask,
                           const void* Kq, const void* Vq, const int32_t* row_q, const int32_t* q_len,
                           const void* k_own, const void* v_own, const int32_t* own_lo, const int32_t* own_hi,
-                          void* o, float* lse, od_attn_dims dims, void* stream);
+                          const int32_t* row_groups, void* o, float* lse, od_attn_dims dims, void* stream);
 
 /* ---------------------------------------------------------------------------------------------------------------
  * A13: option readout, Decider._probs (decider.py:255-257):

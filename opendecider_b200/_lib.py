@@ -27,7 +27,8 @@ class ODError(RuntimeError):
 
 class AttnDims(ctypes.Structure):
     _fields_ = [("R", c_int64), ("t", c_int64), ("S", c_int64), ("T", c_int64), ("NQ", c_int64), ("Lq", c_int64),
-                ("Hq", c_int), ("Hkv", c_int), ("D", c_int), ("scale_dtype", c_int), ("sm_scale", c_float)]
+                ("Hq", c_int), ("Hkv", c_int), ("D", c_int), ("scale_dtype", c_int), ("sm_scale", c_float),
+                ("G", c_int64), ("max_group_rows", c_int)]
 
 
 # exported symbol -> argument types (the declarations of include/od_b200.h)
@@ -47,7 +48,7 @@ SIGNATURES = {
     "od_qk_norm_rope": [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_float, c_int64, c_int,
                         c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p],
     "od_gate_quant": [c_void_p, c_void_p, c_int64, c_int64, c_int, c_int, c_void_p, c_void_p, c_void_p],
-    "od_prefix_attn": [c_void_p] * 19 + [AttnDims, c_void_p],
+    "od_prefix_attn": [c_void_p] * 20 + [AttnDims, c_void_p],
     "od_readout": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p,
                    c_void_p],
 }
@@ -258,10 +259,12 @@ def gate_quant(o: torch.Tensor, qkv: torch.Tensor, Hq: int, D: int, q=None, s=No
 @_probed
 def prefix_attn(q: torch.Tensor, k_own: torch.Tensor, v_own: torch.Tensor, sm_scale: float, *,
                 Kp=None, Vp=None, ksc=None, vsc=None, row_state=None, p_lo=None, p_hi=None, pmask=None,
-                Kq=None, Vq=None, row_q=None, q_len=None, own_lo=None, own_hi=None, out=None, want_lse: bool = False):
+                Kq=None, Vq=None, row_q=None, q_len=None, own_lo=None, own_hi=None, row_groups=None,
+                max_group_rows: int = 1, out=None, want_lse: bool = False):
     """q (R, t, Hq, D), own k/v (R, t, Hkv, D) bf16; int8 prefix Kp/Vp (S, Hkv, T, D) + scales (S, Hkv, T[, 1]);
-    optional bf16 question prefix Kq/Vq (NQ, Lq, Hkv, D); own keys valid in [own_lo[r], own_hi[r]) and causal.
-    Returns o (R, t, Hq, D) [, lse (R, Hq, t)]."""
+    optional bf16 question prefix Kq/Vq (NQ, Lq, Hkv, D); own keys valid in [own_lo[r], own_hi[r]) and causal;
+    row_groups (G, 2) int32 [first row, rows] of consecutive rows sharing state and question, processed together
+    (max_group_rows = the largest). Returns o (R, t, Hq, D) [, lse (R, Hq, t)]."""
     dev = _need_cuda(q, k_own, v_own, Kp, Kq)
     R, t, Hq, D = q.shape
     Hkv = k_own.shape[2]
@@ -270,10 +273,11 @@ def prefix_attn(q: torch.Tensor, k_own: torch.Tensor, v_own: torch.Tensor, sm_sc
     S, T = (Kp.shape[0], Kp.shape[2]) if Kp is not None else (0, 0)
     NQ, Lq = (Kq.shape[0], Kq.shape[1]) if Kq is not None else (0, 0)
     sdt = _DT[ksc.dtype] if ksc is not None else OD_BF16
-    dims = AttnDims(R, t, S, T, NQ, Lq, Hq, Hkv, D, sdt, sm_scale)
+    G = row_groups.shape[0] if row_groups is not None else R
+    dims = AttnDims(R, t, S, T, NQ, Lq, Hq, Hkv, D, sdt, sm_scale, G, max_group_rows if row_groups is not None else 1)
     _check(load().od_prefix_attn(_p(q), _p(Kp), _p(Vp), _p(ksc), _p(vsc), _p(row_state), _p(p_lo), _p(p_hi),
                                  _p(pmask), _p(Kq), _p(Vq), _p(row_q), _p(q_len), _p(k_own), _p(v_own), _p(own_lo),
-                                 _p(own_hi),
+                                 _p(own_hi), _p(row_groups),
                                  _p(out), _p(lse), dims, _stream(dev)), "od_prefix_attn")
     return (out, lse) if want_lse else out
 

@@ -145,6 +145,8 @@ class PassSpec:
     qkv_prefix: list | None = None         # level-2 bf16 prefix: per layer (K, V) (NQ, Lq, Hkv, D)
     row_q: torch.Tensor | None = None      # (R,) int32 question of each row
     q_len: torch.Tensor | None = None      # (NQ,) int32 real tokens of each question
+    row_groups: torch.Tensor | None = None # (G, 2) int32 [first row, rows]: consecutive rows sharing state + question
+    max_group_rows: int = 1
     write_cache: KVCache | None = None     # state pass: append this pass's K/V (rows = states) at offset 0
     capture: bool = False                  # keep every layer's post-RoPE (k, v) (R, t, Hkv, D)
     features: tuple = ()                   # feature layers to return ("final" or 1-based layer numbers)
@@ -259,7 +261,8 @@ class Backbone:
                 row_state=spec.row_state, p_lo=cache.p_lo if cache else None,
                 Kq=spec.qkv_prefix[li][0] if spec.qkv_prefix else None,
                 Vq=spec.qkv_prefix[li][1] if spec.qkv_prefix else None, row_q=spec.row_q, q_len=spec.q_len,
-                own_lo=spec.own_lo, own_hi=spec.own_hi)
+                own_lo=spec.own_lo, own_hi=spec.own_hi, row_groups=spec.row_groups,
+                max_group_rows=spec.max_group_rows)
             oq, os_ = _lib.gate_quant(o.view(M, Hq * D), qkv, Hq, D)
             a = _lib.gemm_w8a8(oq, os_, L.o.q, L.o.scale, _lib.OD_EPI_BF16)
             mq, ms = _lib.rmsnorm_res_quant(a, L.ln2, cfg.eps, res_in=r, res_out=r)

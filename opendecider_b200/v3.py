@@ -242,6 +242,32 @@ class RowPlan:
     q_src: tuple | None = None          # rows-path: (row, col) of question tokens in the first row of each question
 
 
+def width_chunks(lengths: torch.Tensor, chunk: int, waste: float = 0.25) -> list:
+    """Split rows sorted by length (ascending) into chunks: a new chunk starts at `chunk` rows or when padding the
+    chunk to a longer row would waste more than `waste` of its tokens. Returns [(start, end)] over the sorted rows."""
+    out, a, w = [], 0, 0
+    for i, L in enumerate(lengths.tolist()):
+        n = i - a
+        if n and (n >= chunk or (L > w and (L - w) * n > waste * n * w)):
+            out.append((a, i))
+            a, n, w = i, 0, 0
+        w = max(w, L)
+    if a < lengths.numel():
+        out.append((a, lengths.numel()))
+    return out
+
+
+def row_groups(owner: torch.Tensor, max_rows: int) -> torch.Tensor:
+    """(G, 2) [first row, rows] runs of consecutive rows with the same owner (question), at most max_rows each."""
+    groups, a = [], 0
+    o = owner.tolist()
+    for i in range(1, len(o) + 1):
+        if i == len(o) or o[i] != o[a] or i - a == max_rows:
+            groups.append((a, i - a))
+            a = i
+    return torch.tensor(groups, dtype=torch.int32).view(-1, 2)
+
+
 def plan_rows(bb: Backbone, tok, questions, T: int, qcache: bool, list_cap: int = 16, chunk: int = 4096,
               up=None) -> RowPlan:
     """Host layout of the branched row passes. qcache: V3._branched_feats_qcache (v3.py:446-534) - one right-padded
@@ -272,16 +298,21 @@ def plan_rows(bb: Backbone, tok, questions, T: int, qcache: bool, list_cap: int 
         order = torch.argsort(lo, stable=True)
         q_len_dev = up(lq.to(torch.int32))
         passes = []
-        for a in range(0, M, chunk):
-            rows = order[a:a + chunk]
+        rep = bb.cfg.heads // bb.cfg.kv_heads
+        for a, b in width_chunks(lo[order], chunk):
+            rows = order[a:b]
             w = max(2, int(lo[rows].max()))
             ids, ln = _rect([o_tok[i] for i in rows.tolist()], bb.pad_id, w)
             rq = row_q[rows]
             pos = (T + lq[rq])[:, None].to(torch.int32) + torch.arange(w, dtype=torch.int32)[None, :]
             keep = torch.arange(w)[None, :] < ln[:, None]
             dst = (o_start[rows][:, None] + torch.arange(w)[None, :])[keep]
+            # rows of one question (consecutive after the stable length sort) share a tensor-core tile
+            mg = max(1, 128 // (w * rep))
+            grp = row_groups(rq, mg)
             passes.append(RowPass(PassSpec(ids=up(ids), pos=up(pos), own_hi=up(ln.to(torch.int32)),
                                            row_state=up(sidx[rq]), row_q=up(rq.to(torch.int32)), q_len=q_len_dev,
+                                           row_groups=up(grp), max_group_rows=int(grp[:, 1].max()),
                                            features=feats), dst=up(dst), keep=up(keep)))
         return RowPlan(True, qpass, passes, int(lq.sum()), int(lo.sum()), lq, lo)
     rows_tok = [q_tok[int(row_q[i])] + o_tok[i] for i in range(M)]

@@ -314,3 +314,27 @@ def test_prefix_attn_question_level_and_causal(cuda):
         sc = sc.masked_fill(~torch.ones(200, 200, dtype=torch.bool).tril(), float("-inf"))
         ref = (torch.softmax(sc, -1) @ vh.repeat_interleave(rep, 0)).transpose(0, 1)
         assert (o[r] - ref).abs().max() < 2e-2
+
+
+def test_prefix_attn_row_groups(cuda):
+    """Rows of one question processed together in one tensor-core tile equal the rows processed alone (each row
+    still attends only its own keys); groups of 1-3 rows, option rows of 5 tokens, 32 / 8 heads."""
+    g = syn.gen(21)
+    S, T, Hq, Hkv, D, t = 2, 200, 32, 8, 128, 5
+    ac = syn.attn_case(S=S, T=T, rows=3, t=t, Hq=Hq, Hkv=Hkv, D=D, seed=21)
+    Kq, Vq, ks, vs = _attn_inputs(cuda, ac)
+    NQ, Lq = 2, 30
+    Kqn = torch.randn(NQ, Lq, Hkv, D, generator=g).to(torch.bfloat16).to(cuda)
+    Vqn = torch.randn(NQ, Lq, Hkv, D, generator=g).to(torch.bfloat16).to(cuda)
+    row_q = torch.tensor([0, 0, 0, 1, 1, 1], dtype=torch.int32, device=cuda)
+    q_len = torch.tensor([30, 17], dtype=torch.int32, device=cuda)
+    own_hi = torch.tensor([5, 3, 4, 1, 5, 2], dtype=torch.int32, device=cuda)
+    args = dict(Kp=Kq, Vp=Vq, ksc=ks, vsc=vs, row_state=ac.row_state.to(cuda), Kq=Kqn, Vq=Vqn, row_q=row_q,
+                q_len=q_len, own_hi=own_hi)
+    q, k, v = ac.q.to(cuda), ac.k.to(cuda), ac.v.to(cuda)
+    alone = _lib.prefix_attn(q, k, v, D ** -0.5, **args)
+    groups = torch.tensor([[0, 3], [3, 2], [5, 1]], dtype=torch.int32, device=cuda)
+    together = _lib.prefix_attn(q, k, v, D ** -0.5, row_groups=groups, max_group_rows=3, **args)
+    for r in range(6):
+        n = int(own_hi[r])
+        assert (together[r, :n].float() - alone[r, :n].float()).abs().max() < 1e-2, r
