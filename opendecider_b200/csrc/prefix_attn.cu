@@ -1,19 +1,23 @@
 // Branched shared-prefix attention on the sm_100a tensor cores (the Hydragen split of prefix_attn._split_attention,
 // merged exactly by log-sum-exp, here as one online softmax over the three key segments of a query row).
 //
-// One CTA = 128 query slots (one per softmax thread and per TMEM lane) of one KV head: the slots are (row, token,
-// head of the GQA group) of a row group - one long row (the state pass: 32 tokens x 4 heads per CTA) or several
-// short rows of the same question (option rows), so the tensor-core tile is filled and each prefix block staged once
-// serves all of them. Keys run in blocks of 64 through a warp-specialised pipeline:
-//   producer warps (4)   stage K and V of block j into a 2-stage shared-memory ring in the 128-byte-swizzled UMMA
-//                        layout: the int8 state prefix is dequantised there exactly as materialize() rounds
-//                        (bf16(q * s); fp16 scales: bf16(fp16(q * s))), the bf16 question prefix and own keys are
-//                        copied; a per-key bias marks padding / holes
+// One CTA = 128 query slots (one per TMEM lane) of one KV head: the slots are (row, token, head of the GQA group) of
+// a row group - one long row (the state pass: 32 tokens x 4 heads per CTA) or several short rows of the same question
+// (option rows), so the tensor-core tile is filled and each prefix block staged once serves all of them. Keys run in
+// blocks of 128 through a warp-specialised pipeline:
+//   producer warps (4)   stage K_j (2-deep ring, freed when S_j completes) and V_j (2-deep ring, freed when
+//                        P_j V_j completes) in the 128-byte-swizzled UMMA layout: the int8 state prefix arrives
+//                        by TMA in a raw staging buffer and is dequantised from there exactly as materialize()
+//                        rounds (bf16(q * s); fp16 scales: bf16(fp16(q * s))), the bf16 question prefix and own
+//                        keys arrive by TMA directly; one visibility bit per key (padding, holes, segment ends)
+//                        goes to a 4-deep mask ring
 //   MMA warp (1 thread)  S_{j+1} = Q K_{j+1}^T into the other half of a double-buffered S in TMEM while the softmax
-//                        works on S_j, then O += P_j V_j (V as an MN-major operand) with O in TMEM
-//   softmax warps (4)    read the slot's S row from TMEM, mask (causal and same-row for own keys), online softmax in
-//                        the exp2 domain with a lazy rescale of O only when the max grows by more than 2^8, P (bf16)
-//                        into a double-buffered shared-memory tile; at the end O / l and the natural-log LSE
+//                        works on S_j, then O += P_j V_j with P read from TMEM (A operand) and V as an MN-major
+//                        shared-memory operand, O accumulating in TMEM
+//   softmax warps (8)    warp w owns TMEM lane quarter w % 4 and keys [64 (w / 4), +64) of each block: causal and
+//                        same-row masks on own keys, the row max exchanged with the partner warp of the other key
+//                        half, online softmax in the exp2 domain with a lazy rescale of O only when the max grows
+//                        by more than 2^8, P (bf16) into TMEM; at the end O / l and the natural-log LSE
 // Every mbarrier wait is bounded; a time-out ends the kernel with an error code, never a hang.
 // Each slot's math does not depend on the other slots: outputs do not depend on row order.
 #include <cudaTypedefs.h>
@@ -28,37 +32,44 @@ namespace od {
 namespace {
 using namespace sm100;
 
-constexpr int kSoftmaxWarps = 4;     // warps 0-3: thread = query slot = TMEM lane
-constexpr int kMmaWarp = 4;          // warp 4: TMEM allocation and the single MMA-issuing thread
-constexpr int kProducerWarps = 4;    // warps 5-8: stage K/V blocks
+constexpr int kSoftmaxWarps = 8;     // warps 0-7: lane quarter w % 4, key half w / 4
+constexpr int kMmaWarp = 8;          // warp 8: TMEM allocation and the single MMA-issuing thread
+constexpr int kProducerWarps = 4;    // warps 9-12: stage Q, then K/V blocks
+constexpr int kProducer0 = 32 * (kSoftmaxWarps + 1);
 constexpr int kProducers = 32 * kProducerWarps;
 constexpr int kThreads = 32 * (kSoftmaxWarps + 1 + kProducerWarps);
 constexpr int BM = 128;              // query slots per CTA
-constexpr int BN = 64;               // keys per block
-constexpr int kStages = 3;           // K/V ring depth
-constexpr uint32_t kTmemCols = 256;  // S buffers at columns 0 and 64 (64 fp32 each), O at column 128 (D fp32)
-constexpr uint32_t kTmemO = 128;
+constexpr int BN = 128;              // keys per block (one per producer thread)
+constexpr int KS = 2;                // K ring depth
+constexpr int VS = 2;                // V ring depth
+constexpr int MS = 4;                // mask ring depth (a block's bits are rewritten only after its softmax ended)
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTmemS = 0;       // S buffers at columns 0 and BN (BN fp32 each)
+constexpr uint32_t kTmemP = 2 * BN;  // P: BN / 2 columns of bf16 pairs
+constexpr uint32_t kTmemO = 384;     // O: D fp32 columns
 constexpr int32_t kErrAttn = 0x5A0000;
+static_assert(BN == kProducers, "one key of a block per producer thread");
 
 template <int D>
 struct Layout {
-  static constexpr int Q = 0;                        // BM x D bf16: D/64 atoms of BM rows x 128 B
-  static constexpr int Q_ATOM = BM * 128;
-  static constexpr int KV_ATOM = BN * 128;           // a K or V block: D/64 atoms of BN rows x 128 B
-  static constexpr int KV_BYTES = BN * D * 2;
-  static constexpr int KV0 = Q + BM * D * 2;         // stage b: K at KV0 + 2b*KV_BYTES, V right after
-  static constexpr int P0 = KV0 + 2 * kStages * KV_BYTES;  // P buffer b: BM x BN bf16 (one atom)
-  static constexpr int BIAS0 = P0 + 2 * BM * BN * 2; // bias of stage b: BN floats at BIAS0 + b*BN*4
-  static constexpr int BAR = BIAS0 + kStages * BN * 4;  // mbarriers + TMEM holder + abort flag
-  static constexpr int BYTES = BAR + 128 + 1024;     // + alignment slack
-  static __host__ __device__ constexpr int K(int b) { return KV0 + 2 * b * KV_BYTES; }
-  static __host__ __device__ constexpr int V(int b) { return KV0 + (2 * b + 1) * KV_BYTES; }
-  static __host__ __device__ constexpr int P(int b) { return P0 + b * BM * BN * 2; }
-  static __host__ __device__ constexpr int BIAS(int b) { return BIAS0 + b * BN * 4; }
+  static constexpr int ATOM = 128 * 128;             // 128 rows x 128 B: one 64-column swizzle atom of a tile
+  static constexpr int TILE = ATOM * (D / 64);       // 128 rows x D bf16 (Q, a K block or a V block)
+  static constexpr int Q = 0;
+  static constexpr int K0 = Q + TILE;
+  static constexpr int V0 = K0 + KS * TILE;
+  static constexpr int RAWK = V0 + VS * TILE;        // int8 K / V block staging: BN rows x D bytes, row-major
+  static constexpr int RAWV = RAWK + BN * D;
+  static constexpr int MASK0 = RAWV + BN * D;        // MS x 4 words: bit k of word w = key 32 w + k visible
+  static constexpr int XCH = MASK0 + MS * 16;        // 3 x 2 x BM floats: row max (2 parities), then l
+  static constexpr int BAR = XCH + 3 * 2 * BM * 4;   // mbarriers + TMEM holder + abort flag
+  static constexpr int BYTES = BAR + 256 + 1024;     // + alignment slack
+  static __host__ __device__ constexpr int K(int b) { return K0 + b * TILE; }
+  static __host__ __device__ constexpr int V(int b) { return V0 + b * TILE; }
 };
 
 struct Params {
-  CUtensorMap map_ko, map_vo, map_kq, map_vq;   // bf16 (rows, Hkv*D) views of own / question K and V, 64x64 boxes
+  CUtensorMap map_ko, map_vo, map_kq, map_vq;   // bf16 (rows, Hkv*D) views of own / question K and V, 64x128 boxes
+  CUtensorMap map_kp, map_vp;                   // int8 (S*Hkv*T, D) views of the state prefix, D x 128 boxes
   const __nv_bfloat16* q;
   const int8_t* Kp;
   const int8_t* Vp;
@@ -98,76 +109,85 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// One producer thread's share of an int8 K/V block held in registers between its load and its dequantising store,
-// so the next blocks' loads are in flight while this one is converted.
+// Four int8 (one 32-bit word) -> two bf16 pairs of RN(x * s), s a bf16 pair; equal to rounding float(x) * s to bf16,
+// since the product of two 8-bit significands is exact. Integer path without the conversion pipe: the byte
+// (x ^ 0x80) = x + 128 placed under the exponent of 2^23 gives the float 2^23 + x + 128 exactly; subtracting
+// 2^23 + 128 leaves x, whose upper 16 bits are its exact bf16 (|x| <= 128 has at most 8 significant bits).
+__device__ __forceinline__ void dequant4_bf16(uint32_t w, uint32_t s2, uint32_t& lo, uint32_t& hi) {
+  const uint32_t u = w ^ 0x80808080u;
+  const float2 off = make_float2(-8388736.f, -8388736.f);
+  const float2 f01 = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7650)),
+                                            __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7651))), off);
+  const float2 f23 = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7652)),
+                                            __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7653))), off);
+  const uint32_t x01 = __byte_perm(__float_as_uint(f01.x), __float_as_uint(f01.y), 0x7632);
+  const uint32_t x23 = __byte_perm(__float_as_uint(f23.x), __float_as_uint(f23.y), 0x7632);
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(lo) : "r"(x01), "r"(s2));
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(hi) : "r"(x23), "r"(s2));
+}
+
+// A producer thread's share of an int8 block: chunks c = pt + it * kProducers (16 bytes each, key c / (D / 16)).
 template <int D>
-struct RawInt8 {
-  static constexpr int N = BN * (D / 16) / kProducers;   // 16-byte chunks per thread per matrix
-  int4 k[N], v[N];
-  float ks[N], vs[N];
+struct Piece {
+  static constexpr int N = BN * (D / 16) / kProducers;
 };
 
-template <typename TS, int D>
-__device__ __forceinline__ void load_int8(RawInt8<D>& r, int pt, const int8_t* Kb, const int8_t* Vb, const TS* ks,
-                                          const TS* vs, int p0, int p_hi) {
+// The scales of the thread's chunks, raw 16-bit patterns (nothing consumes them until the piece is converted, so
+// the loads stay in flight meanwhile); keys past the segment get 0.
+template <int D>
+__device__ __forceinline__ void load_scales(uint32_t (&sc)[Piece<D>::N], int pt, const void* base, int p0,
+                                            int p_hi) {
   constexpr int CPR = D / 16;
 #pragma unroll
-  for (int it = 0; it < RawInt8<D>::N; ++it) {
-    const int c = pt + it * kProducers;
-    const int key = c / CPR, ch = c % CPR;
-    const int p = p0 + key;
-    if (p < p_hi) {
-      r.k[it] = __ldg(reinterpret_cast<const int4*>(Kb + static_cast<int64_t>(p) * D) + ch);
-      r.v[it] = __ldg(reinterpret_cast<const int4*>(Vb + static_cast<int64_t>(p) * D) + ch);
-      r.ks[it] = Elem<TS>::to_f(ks[p]);
-      r.vs[it] = Elem<TS>::to_f(vs[p]);
-    } else {
-      r.k[it] = r.v[it] = make_int4(0, 0, 0, 0);
-      r.ks[it] = r.vs[it] = 0.f;
-    }
+  for (int it = 0; it < Piece<D>::N; ++it) {
+    const int p = p0 + (pt + it * kProducers) / CPR;
+    sc[it] = p < p_hi ? static_cast<uint32_t>(__ldg(static_cast<const unsigned short*>(base) + p)) : 0u;
   }
 }
 
-// Dequantise a held block into the stage exactly as materialize() rounds; keys >= p_hi or masked by pmask get
-// bias -inf (their data is zero).
+// Dequantise a staged int8 block (row-major, D bytes per key) into a bf16 stage exactly as materialize() rounds.
 template <typename TS, int D>
-__device__ __forceinline__ void store_int8(const RawInt8<D>& r, uint8_t* sK, uint8_t* sV, float* bias, int pt,
-                                           const uint8_t* pm, int p0, int p_hi) {
-  using L = Layout<D>;
+__device__ __forceinline__ void convert_piece(const uint8_t* raw, const uint32_t (&sc)[Piece<D>::N], uint8_t* dst,
+                                              int pt) {
   constexpr int CPR = D / 16;
+  constexpr int ATOM = Layout<D>::ATOM;
 #pragma unroll
-  for (int it = 0; it < RawInt8<D>::N; ++it) {
+  for (int it = 0; it < Piece<D>::N; ++it) {
     const int c = pt + it * kProducers;
     const int key = c / CPR, ch = c % CPR;
-    const int p = p0 + key;
-    const int8_t* kb = reinterpret_cast<const int8_t*>(&r.k[it]);
-    const int8_t* vb = reinterpret_cast<const int8_t*>(&r.v[it]);
-    uint32_t kw[8], vw[8];
+    const uint4 q = *reinterpret_cast<const uint4*>(raw + key * D + ch * 16);
+    uint32_t w[8];
+    if (std::is_same<TS, __nv_bfloat16>::value) {
+      const uint32_t s2 = sc[it] | (sc[it] << 16);
+      dequant4_bf16(q.x, s2, w[0], w[1]);
+      dequant4_bf16(q.y, s2, w[2], w[3]);
+      dequant4_bf16(q.z, s2, w[4], w[5]);
+      dequant4_bf16(q.w, s2, w[6], w[7]);
+    } else {
+      const float sf = __half2float(__ushort_as_half(static_cast<unsigned short>(sc[it])));
+      const int8_t* qb = reinterpret_cast<const int8_t*>(&q);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      float k0 = static_cast<float>(kb[2 * e]) * r.ks[it], k1 = static_cast<float>(kb[2 * e + 1]) * r.ks[it];
-      float v0 = static_cast<float>(vb[2 * e]) * r.vs[it], v1 = static_cast<float>(vb[2 * e + 1]) * r.vs[it];
-      if (std::is_same<TS, __half>::value) {
-        k0 = rhf(k0); k1 = rhf(k1); v0 = rhf(v0); v1 = rhf(v1);
-      }
-      kw[e] = pack_bf16(k0, k1);
-      vw[e] = pack_bf16(v0, v1);
+      for (int e = 0; e < 8; ++e)
+        w[e] = pack_bf16(rhf(static_cast<float>(qb[2 * e]) * sf), rhf(static_cast<float>(qb[2 * e + 1]) * sf));
     }
     // the 16 int8 values of chunk ch are bf16 chunks 2ch and 2ch+1 of the row
-    *reinterpret_cast<uint4*>(sK + swz(key, 2 * ch, L::KV_ATOM)) = make_uint4(kw[0], kw[1], kw[2], kw[3]);
-    *reinterpret_cast<uint4*>(sK + swz(key, 2 * ch + 1, L::KV_ATOM)) = make_uint4(kw[4], kw[5], kw[6], kw[7]);
-    *reinterpret_cast<uint4*>(sV + swz(key, 2 * ch, L::KV_ATOM)) = make_uint4(vw[0], vw[1], vw[2], vw[3]);
-    *reinterpret_cast<uint4*>(sV + swz(key, 2 * ch + 1, L::KV_ATOM)) = make_uint4(vw[4], vw[5], vw[6], vw[7]);
-    if (ch == 0) bias[key] = (p < p_hi && (!pm || pm[p])) ? 0.f : -INFINITY;
+    *reinterpret_cast<uint4*>(dst + swz(key, 2 * ch, ATOM)) = make_uint4(w[0], w[1], w[2], w[3]);
+    *reinterpret_cast<uint4*>(dst + swz(key, 2 * ch + 1, ATOM)) = make_uint4(w[4], w[5], w[6], w[7]);
   }
 }
 
-// Warp-uniform bounded wait (the softmax warps issue warp-collective TMEM loads after it).
+// Warp-uniform bounded wait (the softmax warps issue warp-collective TMEM accesses after it).
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int32_t* err,
                                           int32_t code) {
   return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, err, code));
@@ -181,14 +201,24 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
   // compiler, so accesses compile to shared-memory instructions rather than generic ones
   uint8_t* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::BAR);
-  uint64_t* kv_full = bars;                    // [kStages] producers -> MMA / softmax (count 128)
-  uint64_t* kv_empty = bars + kStages;         // [kStages] MMA (after PV_j) -> producers
-  uint64_t* s_full = bars + 2 * kStages;       // [2] MMA (after S_j) -> softmax
-  uint64_t* p_full = s_full + 2;               // [2] softmax (P_j written) -> MMA (count 128)
-  uint64_t* pv_done = s_full + 4;              // [2] MMA (after PV_j) -> softmax
-  uint64_t* drain = s_full + 6;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(s_full + 7);
+  uint64_t* kfull = bars;                  // [KS] producers (+ TMA bytes) -> MMA
+  uint64_t* kempty = kfull + KS;           // [KS] MMA (S_j complete) -> producers
+  uint64_t* vfull = kempty + KS;           // [VS] producers (+ TMA bytes) -> MMA
+  uint64_t* vempty = vfull + VS;           // [VS] MMA (P_j V_j complete) -> producers
+  uint64_t* mfull = vempty + VS;           // [MS] producer warps (mask words written) -> softmax
+  uint64_t* s_full = mfull + MS;           // [2] MMA (S_j complete) -> softmax
+  uint64_t* p_full = s_full + 2;           // softmax (P_j in TMEM, O rescaled) -> MMA
+  uint64_t* pv_done = p_full + 1;          // MMA (P_j V_j complete) -> softmax
+  uint64_t* xbar = pv_done + 1;            // [4] the two softmax warps of a lane quarter exchanged their values
+  uint64_t* rawk_full = xbar + 4;          // TMA (raw int8 K block) -> producers
+  uint64_t* rawk_empty = rawk_full + 1;    // producers (raw K converted) -> the TMA-issuing producer
+  uint64_t* rawv_full = rawk_full + 2;
+  uint64_t* rawv_empty = rawk_full + 3;
+  uint64_t* drain = rawk_full + 4;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  uint32_t* masks = reinterpret_cast<uint32_t*>(sm + L::MASK0);
+  float* xch = reinterpret_cast<float*>(sm + L::XCH);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int tile = blockIdx.x % P.tiles_per_group;
@@ -203,15 +233,23 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
   if (s0 >= slots) return;                            // uniform: before any barrier or allocation
 
   if (tid == 0) {
-    for (int b = 0; b < kStages; ++b) {
-      mbar_init(&kv_full[b], kProducers);
-      mbar_init(&kv_empty[b], 1);
+    for (int b = 0; b < KS; ++b) {
+      mbar_init(&kfull[b], kProducers);
+      mbar_init(&kempty[b], 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&s_full[b], 1);
-      mbar_init(&p_full[b], 32 * kSoftmaxWarps);
-      mbar_init(&pv_done[b], 1);
+    for (int b = 0; b < VS; ++b) {
+      mbar_init(&vfull[b], kProducers);
+      mbar_init(&vempty[b], 1);
     }
+    for (int b = 0; b < MS; ++b) mbar_init(&mfull[b], kProducerWarps);
+    for (int b = 0; b < 2; ++b) mbar_init(&s_full[b], 1);
+    mbar_init(p_full, 32 * kSoftmaxWarps);
+    mbar_init(pv_done, 1);
+    for (int b = 0; b < 4; ++b) mbar_init(&xbar[b], 64);
+    mbar_init(rawk_full, 1);
+    mbar_init(rawk_empty, kProducers);
+    mbar_init(rawv_full, 1);
+    mbar_init(rawv_empty, kProducers);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -249,9 +287,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
   const int nb3 = own_end > own_begin ? (own_end - own_begin + BN - 1) / BN : 0;
   const int nblk = nb1 + nb2 + nb3;
 
-  if (warp >= kSoftmaxWarps + 1) {
+  if (warp > kMmaWarp) {
     // ================================================================== producers: Q, then K/V blocks
-    const int pt = tid - 32 * (kSoftmaxWarps + 1);
+    const int pt = tid - kProducer0, pw = pt >> 5;
     {
       constexpr int CPR = D / 8;
 #pragma unroll 4
@@ -264,109 +302,150 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
           v = __ldg(reinterpret_cast<const uint4*>(
                         P.q + ((static_cast<int64_t>(row0 + a) * t + i) * P.Hq + g * rep + hh) * D) + ch);
         }
-        *reinterpret_cast<uint4*>(sm + L::Q + swz(r, ch, L::Q_ATOM)) = v;
+        *reinterpret_cast<uint4*>(sm + L::Q + swz(r, ch, L::ATOM)) = v;
       }
+      fence_proxy_async_smem();                       // Q is read by the first S MMA
     }
-    const int8_t* Kb1 = nullptr;
-    const int8_t* Vb1 = nullptr;
     const TS* ks1 = nullptr;
     const TS* vs1 = nullptr;
     const uint8_t* pm1 = nullptr;
+    int prow = 0;                                     // row of key 0 in the (S*Hkv*T, D) int8 views
     if (P.Kp) {
       const int64_t base = (static_cast<int64_t>(st) * P.Hkv + g) * P.T;
-      Kb1 = P.Kp + base * D;
-      Vb1 = P.Vp + base * D;
+      prow = static_cast<int>(base);
       ks1 = static_cast<const TS*>(P.ksc) + base;
       vs1 = static_cast<const TS*>(P.vsc) + base;
       pm1 = P.pmask ? P.pmask + static_cast<int64_t>(st) * P.T : nullptr;
     }
-    // int8 blocks run a 2-deep register pipeline: blocks j+1 and j+2 are being loaded while block j is converted
-    RawInt8<D> ra, rb;
-    if (nb1 > 0) load_int8<TS, D>(ra, pt, Kb1, Vb1, ks1, vs1, lo1, hi1);
-    if (nb1 > 1) load_int8<TS, D>(rb, pt, Kb1, Vb1, ks1, vs1, lo1 + BN, hi1);
-    for (int j = 0; j < nblk; ++j) {
-      const int b = j % kStages;
-      if (j >= kStages && !mbar_wait(&kv_empty[b], ((j / kStages) - 1) & 1, abort_flag, P.err, kErrAttn | 1)) break;
-      uint8_t* sK = sm + L::K(b);
-      uint8_t* sV = sm + L::V(b);
-      float* bias = reinterpret_cast<float*>(sm + L::BIAS(b));
-      if (j < nb1) {
-        store_int8<TS, D>(ra, sK, sV, bias, pt, pm1, lo1 + j * BN, hi1);
-        ra = rb;
-        if (j + 2 < nb1) load_int8<TS, D>(rb, pt, Kb1, Vb1, ks1, vs1, lo1 + (j + 2) * BN, hi1);
-      } else {
-        // bf16 block: TMA straight into the swizzled UMMA layout; every producer thread writes a key's bias first
-        const bool q_seg = j < nb1 + nb2;
-        const int k0 = q_seg ? (j - nb1) * BN : own_begin + (j - nb1 - nb2) * BN;
-        if (pt < BN) {
-          const int idx = k0 + pt;
-          bool ok;
-          if (q_seg) {
-            ok = idx < n2;
-          } else {
-            const int a = idx / t, jj = idx - a * t;
-            const int r = row0 + a;
-            ok = idx < own_end && a < nr && jj >= (P.own_lo ? P.own_lo[r] : 0) && jj < (P.own_hi ? P.own_hi[r] : t);
-          }
-          bias[pt] = ok ? 0.f : -INFINITY;
-        }
-        if (pt == 0) {
-          const CUtensorMap* mk = q_seg ? &P.map_kq : &P.map_ko;
-          const CUtensorMap* mv = q_seg ? &P.map_vq : &P.map_vo;
-          const int y = (q_seg ? qr * static_cast<int>(P.Lq) : row0 * t) + k0;
-          mbar_arrive_expect_tx(&kv_full[b], 2 * L::KV_BYTES);
-#pragma unroll
-          for (int h = 0; h < D / 64; ++h) {
-            tma_load_2d(sK + h * L::KV_ATOM, mk, &kv_full[b], g * D + h * 64, y);
-            tma_load_2d(sV + h * L::KV_ATOM, mv, &kv_full[b], g * D + h * 64, y);
-          }
-        } else {
-          mbar_arrive(&kv_full[b]);
-        }
-        continue;
+    uint32_t skc[Piece<D>::N], svc[Piece<D>::N];     // scales of the next int8 K / V piece to convert
+    if (nb1 > 0) {
+      load_scales<D>(skc, pt, ks1, lo1, hi1);
+      load_scales<D>(svc, pt, vs1, lo1, hi1);
+      if (pt == 0) {
+        mbar_arrive_expect_tx(rawk_full, BN * D);
+        tma_load_2d(sm + L::RAWK, &P.map_kp, rawk_full, 0, prow + lo1);
+        mbar_arrive_expect_tx(rawv_full, BN * D);
+        tma_load_2d(sm + L::RAWV, &P.map_vp, rawv_full, 0, prow + lo1);
       }
-      fence_proxy_async_smem();
-      mbar_arrive(&kv_full[b]);
+    }
+    for (int j = 0; j < nblk; ++j) {
+      const bool i8 = j < nb1;
+      const bool q_seg = !i8 && j < nb1 + nb2;
+      const int k0 = i8 ? lo1 + j * BN : q_seg ? (j - nb1) * BN : own_begin + (j - nb1 - nb2) * BN;
+      // ---- K_j and the block's visibility bits (a mask slot is reused 4 blocks later: by then this producer has
+      // passed the V stage wait of block j+3, which follows the softmax of block j+1)
+      const int bk = j % KS;
+      if (j >= KS && !mbar_wait(&kempty[bk], ((j / KS) - 1) & 1, abort_flag, P.err, kErrAttn | 1)) break;
+      bool vis;
+      {
+        const int idx = k0 + pt;
+        if (i8) {
+          vis = idx < hi1 && (!pm1 || pm1[idx]);
+        } else if (q_seg) {
+          vis = idx < n2;
+        } else {
+          const int a = idx / t, jj = idx - a * t;
+          const int r = row0 + a;
+          vis = idx < own_end && a < nr && jj >= (P.own_lo ? P.own_lo[r] : 0) && jj < (P.own_hi ? P.own_hi[r] : t);
+        }
+      }
+      const uint32_t word = __ballot_sync(0xffffffffu, vis);
+      if (lane == 0) {
+        masks[4 * (j % MS) + pw] = word;
+        mbar_arrive(&mfull[j % MS]);
+      }
+      uint8_t* sK = sm + L::K(bk);
+      if (i8) {
+        if (!mbar_wait(rawk_full, j & 1, abort_flag, P.err, kErrAttn | 13)) break;
+        convert_piece<TS, D>(sm + L::RAWK, skc, sK, pt);
+        mbar_arrive(rawk_empty);
+        if (j + 1 < nb1) {
+          load_scales<D>(skc, pt, ks1, k0 + BN, hi1);
+          if (pt == 0) {                              // refill the staging once every thread has converted it
+            if (!mbar_wait(rawk_empty, j & 1, abort_flag, P.err, kErrAttn | 14)) break;
+            mbar_arrive_expect_tx(rawk_full, BN * D);
+            tma_load_2d(sm + L::RAWK, &P.map_kp, rawk_full, 0, prow + k0 + BN);
+          }
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&kfull[bk]);
+      } else if (pt == 0) {
+        const CUtensorMap* mk = q_seg ? &P.map_kq : &P.map_ko;
+        const int y = (q_seg ? qr * static_cast<int>(P.Lq) : row0 * t) + k0;
+        mbar_arrive_expect_tx(&kfull[bk], L::TILE);
+#pragma unroll
+        for (int h = 0; h < D / 64; ++h) tma_load_2d(sK + h * L::ATOM, mk, &kfull[bk], g * D + h * 64, y);
+      } else {
+        mbar_arrive(&kfull[bk]);
+      }
+      // ---- V_j
+      const int bv = j % VS;
+      if (j >= VS && !mbar_wait(&vempty[bv], ((j / VS) - 1) & 1, abort_flag, P.err, kErrAttn | 2)) break;
+      uint8_t* sV = sm + L::V(bv);
+      if (i8) {
+        if (!mbar_wait(rawv_full, j & 1, abort_flag, P.err, kErrAttn | 15)) break;
+        convert_piece<TS, D>(sm + L::RAWV, svc, sV, pt);
+        mbar_arrive(rawv_empty);
+        if (j + 1 < nb1) {
+          load_scales<D>(svc, pt, vs1, k0 + BN, hi1);
+          if (pt == 0) {
+            if (!mbar_wait(rawv_empty, j & 1, abort_flag, P.err, kErrAttn | 16)) break;
+            mbar_arrive_expect_tx(rawv_full, BN * D);
+            tma_load_2d(sm + L::RAWV, &P.map_vp, rawv_full, 0, prow + k0 + BN);
+          }
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&vfull[bv]);
+      } else if (pt == 0) {
+        const CUtensorMap* mv = q_seg ? &P.map_vq : &P.map_vo;
+        const int y = (q_seg ? qr * static_cast<int>(P.Lq) : row0 * t) + k0;
+        mbar_arrive_expect_tx(&vfull[bv], L::TILE);
+#pragma unroll
+        for (int h = 0; h < D / 64; ++h) tma_load_2d(sV + h * L::ATOM, mv, &vfull[bv], g * D + h * 64, y);
+      } else {
+        mbar_arrive(&vfull[bv]);
+      }
     }
   } else if (warp == kMmaWarp) {
     // ================================================================== MMA issue (one thread)
     if (lane == 0 && nblk > 0) {
-      constexpr uint32_t idesc_qk = idesc_bf16(BM, BN, false);
-      constexpr uint32_t idesc_pv = idesc_bf16(BM, D, true);
+      constexpr uint32_t idesc_s = idesc_bf16(BM, BN, false);
+      constexpr uint32_t idesc_o = idesc_bf16(BM, D, true);
       const uint32_t sQ = smem_u32(sm + L::Q);
       auto issue_s = [&](int j) {
-        const int b = j & 1;
-        const uint32_t sK = smem_u32(sm + L::K(j % kStages));
+        const uint32_t sK = smem_u32(sm + L::K(j % KS));
 #pragma unroll
         for (int kd = 0; kd < D / 16; ++kd) {
-          const uint32_t qa = sQ + (kd >> 2) * L::Q_ATOM + (kd & 3) * 32;
-          const uint32_t ka = sK + (kd >> 2) * L::KV_ATOM + (kd & 3) * 32;
-          mma_f16(tmem + b * BN, desc_sw128(qa, 16, 1024), desc_sw128(ka, 16, 1024), idesc_qk, kd > 0 ? 1u : 0u);
+          const uint32_t off = (kd >> 2) * L::ATOM + (kd & 3) * 32;
+          mma_f16(tmem + kTmemS + (j & 1) * BN, desc_sw128(sQ + off, 16, 1024), desc_sw128(sK + off, 16, 1024),
+                  idesc_s, kd > 0 ? 1u : 0u);
         }
-        mma_commit(&s_full[b]);
+        mma_commit(&s_full[j & 1]);
+        mma_commit(&kempty[j % KS]);
       };
-      bool live = mbar_wait(&kv_full[0], 0, abort_flag, P.err, kErrAttn | 2);
+      bool live = mbar_wait(&kfull[0], 0, abort_flag, P.err, kErrAttn | 3);
       if (live) {
         tc_fence_after();
         issue_s(0);
       }
       for (int j = 0; j < nblk && live; ++j) {
+        // S buffer (j+1) & 1 was last read by the softmax of block j-1, whose P_{j-1} was waited for below
         if (j + 1 < nblk) {
-          const int b1 = (j + 1) % kStages;
-          if (!mbar_wait(&kv_full[b1], ((j + 1) / kStages) & 1, abort_flag, P.err, kErrAttn | 3)) break;
+          if (!mbar_wait(&kfull[(j + 1) % KS], ((j + 1) / KS) & 1, abort_flag, P.err, kErrAttn | 4)) break;
           tc_fence_after();
           issue_s(j + 1);
         }
-        const int b = j & 1;
-        if (!mbar_wait(&p_full[b], (j >> 1) & 1, abort_flag, P.err, kErrAttn | 4)) break;
+        if (!mbar_wait(&vfull[j % VS], (j / VS) & 1, abort_flag, P.err, kErrAttn | 5) ||
+            !mbar_wait(p_full, j & 1, abort_flag, P.err, kErrAttn | 6))
+          break;
         tc_fence_after();
-        const uint32_t sP = smem_u32(sm + L::P(b)), sV = smem_u32(sm + L::V(j % kStages));
+        const uint32_t sV = smem_u32(sm + L::V(j % VS));
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk)
-          mma_f16(tmem + kTmemO, desc_sw128(sP + kk * 32, 16, 1024),
-                  desc_sw128(sV + kk * 16 * 128, L::KV_ATOM, 1024), idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
-        mma_commit(&kv_empty[j % kStages]);
-        mma_commit(&pv_done[b]);
+          mma_f16_ts(tmem + kTmemO, tmem + kTmemP + kk * 8, desc_sw128(sV + kk * 16 * 128, L::ATOM, 1024), idesc_o,
+                     (j > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(pv_done);
+        mma_commit(&vempty[j % VS]);
       }
       // every MMA issued here has completed before TMEM is released (immediate unless aborted)
       mma_commit(drain);
@@ -375,29 +454,31 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
       }
     }
   } else {
-    // ================================================================== softmax (thread = slot = TMEM lane)
-    const int slot = s0 + tid;
+    // ================================================================== softmax (lane quarter q4, key half h)
+    const int q4 = warp & 3, h = warp >> 2;
+    const int tt = 32 * q4 + lane;                    // slot of the tile = TMEM lane
+    const int slot = s0 + tt;
     const bool my_valid = slot < slots;
     const int a_my = my_valid ? slot / slots_row : 0;
     const int i_my = my_valid ? (slot % slots_row) / rep : 0;
     const int hh_my = slot % rep;
-    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
-    float m_used = -INFINITY, l_sum = 0.f;
+    const uint32_t lane_off = static_cast<uint32_t>(32 * q4) << 16;
+    const float scale = P.scale_log2;
+    float m_used = -INFINITY, l_part = 0.f;
     bool live = true;
     for (int j = 0; j < nblk; ++j) {
       const int b = j & 1;
-      const uint32_t ph = (j >> 1) & 1;
-      if (!warp_wait(&s_full[b], ph, abort_flag, P.err, kErrAttn | 5) ||
-          !warp_wait(&kv_full[j % kStages], (j / kStages) & 1, abort_flag, P.err, kErrAttn | 6)) {
+      if (!warp_wait(&s_full[b], (j >> 1) & 1, abort_flag, P.err, kErrAttn | 7) ||
+          !warp_wait(&mfull[j % MS], (j / MS) & 1, abort_flag, P.err, kErrAttn | 8)) {
         live = false;
         break;
       }
       tc_fence_after();
-      float s[BN];
+      float s[64];
       {
         uint32_t r0[32], r1[32];
-        tmem_ld_32x32b_x32(tmem + lane_off + b * BN, r0);
-        tmem_ld_32x32b_x32(tmem + lane_off + b * BN + 32, r1);
+        tmem_ld_32x32b_x32(tmem + lane_off + kTmemS + b * BN + 64 * h, r0);
+        tmem_ld_32x32b_x32(tmem + lane_off + kTmemS + b * BN + 64 * h + 32, r1);
         tmem_ld_wait();
 #pragma unroll
         for (int k = 0; k < 32; ++k) {
@@ -405,109 +486,112 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
           s[k + 32] = __uint_as_float(r1[k]);
         }
       }
-      float bias[BN];
-      {
-        const float4* bsrc = reinterpret_cast<const float4*>(sm + L::BIAS(j % kStages));
+      const uint32_t mw0 = masks[4 * (j % MS) + 2 * h], mw1 = masks[4 * (j % MS) + 2 * h + 1];
+      // own keys visible to this slot form one range of the flattened (row, token) index: its own row's tokens up
+      // to its own position; in block-local key numbers of this warp's half: [vis_lo, vis_hi]
+      int vis_lo = -(1 << 30), vis_hi = 1 << 30;
+      if (j >= nb1 + nb2) {
+        const int key0 = own_begin + (j - nb1 - nb2) * BN + 64 * h;
+        vis_lo = a_my * t - key0;
+        vis_hi = a_my * t + i_my - key0;
+      }
+      const bool fast = (mw0 & mw1) == 0xffffffffu && vis_lo <= 0 && vis_hi >= 63;
+      if (!__all_sync(0xffffffffu, fast)) {
 #pragma unroll
-        for (int k = 0; k < BN / 4; ++k) {
-          const float4 b4 = bsrc[k];
-          bias[4 * k] = b4.x;
-          bias[4 * k + 1] = b4.y;
-          bias[4 * k + 2] = b4.z;
-          bias[4 * k + 3] = b4.w;
+        for (int k = 0; k < 64; ++k) {
+          const uint32_t bit = ((k < 32 ? mw0 : mw1) >> (k & 31)) & 1u;
+          if (!bit || k < vis_lo || k > vis_hi) s[k] = -INFINITY;
         }
       }
-      const bool own = j >= nb1 + nb2;
-      const float scale = P.scale_log2;
       float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-      if (!own) {
 #pragma unroll
-        for (int k = 0; k < BN; ++k) {
-          s[k] = fmaf(s[k], scale, bias[k]);
-          mq[k & 3] = fmaxf(mq[k & 3], s[k]);
-        }
-      } else {
-        // own keys visible to this slot form one range of the flattened (row, token) index: its own row's tokens
-        // up to its own position (padding inside the row is already in the bias)
-        const int key0 = own_begin + (j - nb1 - nb2) * BN;
-        const int vis_lo = a_my * t - key0, vis_hi = a_my * t + i_my - key0;
-#pragma unroll
-        for (int k = 0; k < BN; ++k) {
-          s[k] = (k < vis_lo || k > vis_hi) ? -INFINITY : fmaf(s[k], scale, bias[k]);
-          mq[k & 3] = fmaxf(mq[k & 3], s[k]);
-        }
+      for (int k = 0; k < 64; k += 8) {
+        mq[0] = fmax3(mq[0], s[k], s[k + 1]);
+        mq[1] = fmax3(mq[1], s[k + 2], s[k + 3]);
+        mq[2] = fmax3(mq[2], s[k + 4], s[k + 5]);
+        mq[3] = fmax3(mq[3], s[k + 6], s[k + 7]);
       }
-      const float mb = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
+      const float mloc = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
+      // the row max of the whole block: exchange with the warp holding the other key half of these slots
+      float* xm = xch + (j & 1) * 2 * BM;
+      xm[h * BM + tt] = mloc;
+      mbar_arrive(&xbar[q4]);
+      if (!warp_wait(&xbar[q4], j & 1, abort_flag, P.err, kErrAttn | 9)) {
+        live = false;
+        break;
+      }
+      const float mb = fmaxf(mloc, xm[(1 - h) * BM + tt]) * scale;
       float alpha = 1.f;
       bool resc = false;
       if (m_used == -INFINITY) {
         m_used = mb;                                   // nothing accumulated yet: O and l are 0
       } else if (mb > m_used + 8.f) {
         alpha = ex2_approx(m_used - mb);
-        l_sum *= alpha;
+        l_part *= alpha;
         m_used = mb;
         resc = true;
       }
-      uint32_t pw[BN / 2];
-      float rq[4] = {0.f, 0.f, 0.f, 0.f};
+      uint32_t pw[32];
+      float rs = 0.f;
       if (m_used == -INFINITY) {                       // no visible key so far: every weight is 0
 #pragma unroll
-        for (int k = 0; k < BN / 2; ++k) pw[k] = 0u;
+        for (int c = 0; c < 32; ++c) pw[c] = 0u;
       } else {
+        const float2 sc2 = make_float2(scale, scale), nm2 = make_float2(-m_used, -m_used);
+        float2 acc[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
-        for (int k = 0; k < BN; k += 2) {
-          const float p0 = ex2_approx(s[k] - m_used);
-          const float p1 = ex2_approx(s[k + 1] - m_used);
-          rq[(k >> 1) & 3] += p0 + p1;
-          pw[k / 2] = pack_bf16(p0, p1);
+        for (int c = 0; c < 32; ++c) {
+          const float2 x = __ffma2_rn(make_float2(s[2 * c], s[2 * c + 1]), sc2, nm2);
+          const float2 p = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+          acc[c & 1] = __fadd2_rn(acc[c & 1], p);
+          pw[c] = pack_bf16(p.x, p.y);
         }
+        rs = (acc[0].x + acc[0].y) + (acc[1].x + acc[1].y);
       }
-      const float rs = (rq[0] + rq[1]) + (rq[2] + rq[3]);
-      l_sum += rs;
-      // P buffer b is free once PV_{j-2} completed
-      if (j >= 2 && !warp_wait(&pv_done[b], ((j >> 1) - 1) & 1, abort_flag, P.err, kErrAttn | 7)) {
+      l_part += rs;
+      // P (one buffer) and O are free once P_{j-1} V_{j-1} completed
+      if (j >= 1 && !warp_wait(pv_done, (j - 1) & 1, abort_flag, P.err, kErrAttn | 10)) {
         live = false;
         break;
       }
-      if (__any_sync(0xffffffffu, resc)) {           // lazy rescale of this warp's O rows once PV_{j-1} is done
-        if (!warp_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag, P.err, kErrAttn | 8)) {
-          live = false;
-          break;
-        }
-        tc_fence_after();
+      tc_fence_after();
+      if (__any_sync(0xffffffffu, resc)) {             // lazy rescale of this warp's half of the O row
 #pragma unroll 1
-        for (int dc = 0; dc < D / 32; ++dc) {
+        for (int dc = 0; dc < D / 64; ++dc) {
           uint32_t o[32];
-          tmem_ld_32x32b_x32(tmem + lane_off + kTmemO + dc * 32, o);
+          const uint32_t ta = tmem + lane_off + kTmemO + h * (D / 2) + dc * 32;
+          tmem_ld_32x32b_x32(ta, o);
           tmem_ld_wait();
 #pragma unroll
           for (int k = 0; k < 32; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * alpha);
-          tmem_st_32x32b_x32(tmem + lane_off + kTmemO + dc * 32, o);
+          tmem_st_32x32b_x32(ta, o);
         }
-        tmem_st_wait();
       }
-      uint8_t* sP = sm + L::P(b);
-#pragma unroll
-      for (int c = 0; c < BN / 8; ++c)
-        *reinterpret_cast<uint4*>(sP + swz(tid, c, BM * 128)) =
-            make_uint4(pw[4 * c], pw[4 * c + 1], pw[4 * c + 2], pw[4 * c + 3]);
-      fence_proxy_async_smem();
+      tmem_st_32x32b_x32(tmem + lane_off + kTmemP + 32 * h, pw);
+      tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&p_full[b]);
+      mbar_arrive(p_full);
     }
     // ---- epilogue: O / l, natural-log LSE (nothing is written after a time-out; the error word says why).
     // TMEM loads are warp-collective: every lane loads, valid slots store.
     if (live && nblk > 0)
-      live = warp_wait(&pv_done[(nblk - 1) & 1], ((nblk - 1) >> 1) & 1, abort_flag, P.err, kErrAttn | 9);
+      live = warp_wait(pv_done, (nblk - 1) & 1, abort_flag, P.err, kErrAttn | 11);
+    if (live) {
+      float* xl = xch + 4 * BM;
+      xl[h * BM + tt] = l_part;
+      mbar_arrive(&xbar[q4]);
+      live = warp_wait(&xbar[q4], nblk & 1, abort_flag, P.err, kErrAttn | 12);
+    }
     if (live) {
       tc_fence_after();
+      const float l_sum = l_part + xch[4 * BM + (1 - h) * BM + tt];
       const float inv = l_sum > 0.f ? 1.0f / l_sum : 0.f;
       const int64_t orow = ((static_cast<int64_t>(row0 + a_my) * t + i_my) * P.Hq + g * rep + hh_my) * D;
 #pragma unroll 1
-      for (int dc = 0; dc < D / 32; ++dc) {
+      for (int dc = 0; dc < D / 64; ++dc) {
         uint32_t o[32];
         if (nblk > 0) {
-          tmem_ld_32x32b_x32(tmem + lane_off + kTmemO + dc * 32, o);
+          tmem_ld_32x32b_x32(tmem + lane_off + kTmemO + h * (D / 2) + dc * 32, o);
           tmem_ld_wait();
         } else {
 #pragma unroll
@@ -518,12 +602,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
 #pragma unroll
           for (int k = 0; k < 16; ++k)
             w[k] = pack_bf16(__uint_as_float(o[2 * k]) * inv, __uint_as_float(o[2 * k + 1]) * inv);
-          uint4* dst = reinterpret_cast<uint4*>(P.o + orow + dc * 32);
+          uint4* dst = reinterpret_cast<uint4*>(P.o + orow + h * (D / 2) + dc * 32);
 #pragma unroll
           for (int k = 0; k < 4; ++k) dst[k] = make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
         }
       }
-      if (P.lse && my_valid)
+      if (P.lse && my_valid && h == 0)
         P.lse[(static_cast<int64_t>(row0 + a_my) * P.Hq + g * rep + hh_my) * t + i_my] =
             l_sum > 0.f ? (m_used + log2f(l_sum)) * 0.6931471805599453f : -INFINITY;
     }
@@ -548,7 +632,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// (rows, cols) bf16 row-major view tiled into 64 x 64 boxes with the 128-byte swizzle of the UMMA layout
+// (rows, cols) bf16 row-major view tiled into 64-column x BN-row boxes with the 128-byte swizzle of the UMMA layout
 int make_map_bf16(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows) {
   auto fn = encode_fn();
   if (!fn) return fail(OD_ECUDA, "cuTensorMapEncodeTiled is unavailable");
@@ -560,6 +644,21 @@ int make_map_bf16(CUtensorMap* map, const void* base, uint64_t cols, uint64_t ro
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(OD_ECUDA, "cuTensorMapEncodeTiled (bf16) failed (%d)", static_cast<int>(r));
+  return OD_OK;
+}
+
+// (rows, D) int8 row-major view tiled into D x BN boxes, no swizzle (the producers read it row by row)
+int make_map_i8(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows) {
+  auto fn = encode_fn();
+  if (!fn) return fail(OD_ECUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(cols), static_cast<cuuint32_t>(BN)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(OD_ECUDA, "cuTensorMapEncodeTiled (int8) failed (%d)", static_cast<int>(r));
   return OD_OK;
 }
 
@@ -650,6 +749,12 @@ extern "C" int od_prefix_attn(const void* q, const int8_t* Kp, const int8_t* Vp,
     if (!Kq) {
       P.map_kq = P.map_ko;
       P.map_vq = P.map_vo;
+    }
+    if (!rc && Kp) {
+      const uint64_t prows = static_cast<uint64_t>(dims.S) * dims.Hkv * dims.T;
+      OD_REQUIRE(prows < (1ULL << 31), "od_prefix_attn: S * Hkv * T must be below 2^31");
+      rc = make_map_i8(&P.map_kp, Kp, static_cast<uint64_t>(dims.D), prows);
+      if (!rc) rc = make_map_i8(&P.map_vp, Vp, static_cast<uint64_t>(dims.D), prows);
     }
     if (rc) return rc;
   }

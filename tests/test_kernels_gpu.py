@@ -338,3 +338,33 @@ def test_prefix_attn_row_groups(cuda):
     for r in range(6):
         n = int(own_hi[r])
         assert (together[r, :n].float() - alone[r, :n].float()).abs().max() < 1e-2, r
+
+
+@pytest.mark.gpu
+def test_prefix_attn_int8_dequant_exact(cuda):
+    """One visible prefix key per state (p_hi = p_lo + 1, no own key visible): its softmax weight is exactly 1, so
+    every output equals that key's dequantised V, bf16(vq * vs), bit for bit - the materialize() rounding of the
+    reference (quant.py:43-45), over every int8 value and scales across many binades."""
+    g = syn.gen(33)
+    S, T, Hq, Hkv, D, t = 4, 256, 8, 2, 128, 3
+    Vq = torch.randint(-128, 128, (S, Hkv, T, D), generator=g, dtype=torch.int8)
+    Kq = torch.randint(-128, 128, (S, Hkv, T, D), generator=g, dtype=torch.int8)
+    vs = (torch.rand(S, Hkv, T, generator=g) *
+          torch.pow(2.0, torch.randint(-30, 10, (S, Hkv, T), generator=g).float())).to(torch.bfloat16)
+    ks = torch.full((S, Hkv, T), 0.01).to(torch.bfloat16)
+    row_state = torch.tensor([0, 1, 2, 3, 1], dtype=torch.int32)
+    R = row_state.shape[0]
+    p_lo = torch.tensor([0, 5, 100, 255], dtype=torch.int32)
+    q = torch.randn(R, t, Hq, D, generator=g).to(torch.bfloat16)
+    k = torch.randn(R, t, Hkv, D, generator=g).to(torch.bfloat16)
+    zeros = torch.zeros(R, dtype=torch.int32, device=cuda)
+    o = _lib.prefix_attn(q.to(cuda), k.to(cuda), k.to(cuda), D ** -0.5, Kp=Kq.to(cuda), Vp=Vq.to(cuda),
+                         ksc=ks.to(cuda), vsc=vs.to(cuda), row_state=row_state.to(cuda), p_lo=p_lo.to(cuda),
+                         p_hi=(p_lo + 1).to(cuda), own_lo=zeros, own_hi=zeros).cpu()
+    deq = (Vq.float() * vs.float()[..., None]).to(torch.bfloat16)              # (S, Hkv, T, D)
+    rep = Hq // Hkv
+    for r in range(R):
+        s = int(row_state[r])
+        want = deq[s, :, int(p_lo[s]), :].repeat_interleave(rep, 0)           # (Hq, D)
+        for i in range(t):
+            assert torch.equal(o[r, i].view(torch.int16), want.view(torch.int16)), (r, i)
