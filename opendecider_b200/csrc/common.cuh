@@ -65,11 +65,28 @@ __device__ __forceinline__ float rhf(float v) { return __half2float(__float2half
 // Int8Tensor.quantize's scale from a row's absmax: max(amax, 1e-8) / 127 in IEEE fp32.
 __device__ __forceinline__ float quant_scale(float amax) { return __fdiv_rn(fmaxf(amax, 1e-8f), 127.0f); }
 
-// Int8Tensor.quantize's value: clamp(round_half_even(x / s), -127, 127).
-__device__ __forceinline__ int8_t quant_val(float x, float s) {
-  float r = rintf(__fdiv_rn(x, s));
-  r = fminf(fmaxf(r, -127.0f), 127.0f);
-  return static_cast<int8_t>(static_cast<int>(r));
+// RN(1 / s), computed once per row for quant_val.
+__device__ __forceinline__ float quant_recip(float s) { return __frcp_rn(s); }
+
+// Int8Tensor.quantize's value: clamp(round_half_even(x / s), -127, 127) with x / s the IEEE fp32 quotient, bit for
+// bit, given r = RN(1 / s) and |x / s| <= 128 (x is an element of the row whose absmax gave s). y = RN(x * r) lies
+// within 2.3e-5 of RN(x / s) (two roundings of relative size 2^-24 on a value of at most 128), so the two round to
+// the same integer unless y is within 1e-4 of a half-integer; only then is the quotient formed. Rounding to
+// nearest-even is the addition of 1.5 * 2^23 (exact for |y| < 2^22), whose low mantissa bits are the integer.
+__device__ __forceinline__ int quant_int(float x, float s, float r) {
+  constexpr float kMagic = 12582912.0f;       // 1.5 * 2^23, bit pattern 0x4B400000
+  const float y = __fmul_rn(x, r);
+  float t = __fadd_rn(y, kMagic);
+  if (fabsf(__fsub_rn(y, __fsub_rn(t, kMagic))) > 0.4999f) t = __fadd_rn(__fdiv_rn(x, s), kMagic);
+  return min(max(__float_as_int(t) - 0x4B400000, -127), 127);
+}
+__device__ __forceinline__ int8_t quant_val(float x, float s, float r) {
+  return static_cast<int8_t>(quant_int(x, s, r));
+}
+// four quantised values packed little-endian into one word
+__device__ __forceinline__ uint32_t quant4(float a, float b, float c, float d, float s, float r) {
+  return (static_cast<uint32_t>(quant_int(a, s, r)) & 0xFFu) | ((static_cast<uint32_t>(quant_int(b, s, r)) & 0xFFu) << 8) |
+         ((static_cast<uint32_t>(quant_int(c, s, r)) & 0xFFu) << 16) | (static_cast<uint32_t>(quant_int(d, s, r)) << 24);
 }
 
 __device__ __forceinline__ float warp_max(float v) {

@@ -10,7 +10,7 @@
 namespace od {
 namespace {
 
-constexpr int kRowThreads = 128;  // one CTA per row; a row of K elements is K / 8 vectors of 8
+constexpr int kRowThreads = 256;  // one CTA per row; a row of K elements is K / 8 vectors of 8
 
 // ---------------------------------------------------------------------------------------------- vector I/O
 template <typename T> __device__ __forceinline__ void load8(const T* p, float (&v)[8]);
@@ -50,12 +50,9 @@ template <> __device__ __forceinline__ void store8<__nv_bfloat16>(__nv_bfloat16*
   *reinterpret_cast<uint4*>(p) = raw;
 }
 
-__device__ __forceinline__ void store8_i8(int8_t* p, const float (&v)[8], float s) {
-  uint2 raw;
-  int8_t* b = reinterpret_cast<int8_t*>(&raw);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) b[i] = quant_val(v[i], s);
-  *reinterpret_cast<uint2*>(p) = raw;
+__device__ __forceinline__ void store8_i8(int8_t* p, const float (&v)[8], float s, float r) {
+  *reinterpret_cast<uint2*>(p) =
+      make_uint2(quant4(v[0], v[1], v[2], v[3], s, r), quant4(v[4], v[5], v[6], v[7], s, r));
 }
 
 // Round a value to the precision of T (the dtype a PyTorch op on T tensors stores).
@@ -113,11 +110,11 @@ __global__ void __launch_bounds__(kRowThreads) quant_rows_kernel(const T* __rest
     }
   }
   amax = block_max(amax, red);
-  const float s = quant_scale(amax);
+  const float s = quant_scale(amax), rs = quant_recip(s);
 #pragma unroll
   for (int j = 0; j < VPT; ++j) {
     const int64_t e = (static_cast<int64_t>(j) * kRowThreads + threadIdx.x) * 8;
-    if (e < K) store8_i8(q + row * K + e, v[j], s);
+    if (e < K) store8_i8(q + row * K + e, v[j], s, rs);
   }
   if (threadIdx.x == 0) store_scale(scale, row, s, scale_dtype);
 }
@@ -130,11 +127,13 @@ int launch_quant_rows(const T* x, int64_t M, int64_t K, int64_t ldx, const __nv_
 #define OD_QR(V) quant_rows_kernel<T, V><<<grid, block, 0, st>>>(x, K, ldx, inv_s, q, scale, scale_dtype)
   if (vecs <= 1) OD_QR(1);
   else if (vecs <= 2) OD_QR(2);
+  else if (vecs <= 3) OD_QR(3);
   else if (vecs <= 4) OD_QR(4);
+  else if (vecs <= 6) OD_QR(6);
   else if (vecs <= 8) OD_QR(8);
   else if (vecs <= 12) OD_QR(12);
   else if (vecs <= 16) OD_QR(16);
-  else return fail(OD_EUNSUPPORTED, "od_quant_rows_i8: K=%lld above 16384", (long long)K);
+  else return fail(OD_EUNSUPPORTED, "od_quant_rows_i8: K=%lld above %d", (long long)K, 16 * 8 * kRowThreads);
 #undef OD_QR
   OD_LAUNCH_CHECK();
   return ok();
@@ -181,10 +180,10 @@ __global__ void kv_append_kernel(const T* __restrict__ k, const T* __restrict__ 
       amax = fmaxf(amax, fabsf(x[i]));
     }
     amax = warp_max(amax);
-    const float sc = quant_scale(amax);
+    const float sc = quant_scale(amax), rs = quant_recip(sc);
     int8_t* out = (which == 0 ? kq : vq) + dst * D + lane * EPL;
 #pragma unroll
-    for (int i = 0; i < EPL; ++i) out[i] = quant_val(x[i], sc);
+    for (int i = 0; i < EPL; ++i) out[i] = quant_val(x[i], sc, rs);
     if (lane == 0) (which == 0 ? ksc : vsc)[dst] = Elem<T>::from_f(sc);
   }
 }
@@ -243,11 +242,11 @@ __global__ void __launch_bounds__(kRowThreads) rmsnorm_res_quant_kernel(
   }
   if (!q) return;
   amax = block_max(amax, red);
-  const float sc = quant_scale(amax);
+  const float sc = quant_scale(amax), rq = quant_recip(sc);
 #pragma unroll
   for (int j = 0; j < VPT; ++j) {
     const int e = (j * kRowThreads + threadIdx.x) * 8;
-    if (e < H) store8_i8(q + base + e, v[j], sc);
+    if (e < H) store8_i8(q + base + e, v[j], sc, rq);
   }
   if (threadIdx.x == 0) s_out[row] = sc;
 }
@@ -279,6 +278,18 @@ __global__ void embed_i8_kernel(const int64_t* __restrict__ ids, const int8_t* _
 }
 
 // ---------------------------------------------------------------------------------------------- gate + quant
+// sigmoid(g) = 1 / (1 + exp(-g)) in fp32 (expf, IEEE division), rounded to bf16. A fast value from the hardware
+// exp2 / reciprocal approximations (relative error below 1.4e-6 for |g| < 16) rounds to the same bf16 unless it lies
+// within 64 fp32 ulps (relative 3.8e-6) of a bf16 rounding boundary; then, and for |g| >= 16, the fp32 formula decides.
+__device__ __forceinline__ float sigmoid_bf16(float g) {
+  float e, v;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(g * -1.4426950408889634f));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(v) : "f"(1.0f + e));
+  const int lo = static_cast<int>(__float_as_uint(v) & 0xFFFFu);
+  if (fabsf(g) >= 16.0f || abs(lo - 0x8000) < 64 || lo < 64 || lo > 0xFFFF - 64) v = __fdiv_rn(1.0f, 1.0f + expf(-g));
+  return rbf(v);
+}
+
 // o * sigmoid(gate) (Qwen3_5Attention.forward) then per-token quantisation of the o_proj input.
 template <int VPT>
 __global__ void __launch_bounds__(kRowThreads) gate_quant_kernel(const __nv_bfloat16* __restrict__ o,
@@ -300,18 +311,18 @@ __global__ void __launch_bounds__(kRowThreads) gate_quant_kernel(const __nv_bflo
       load8<__nv_bfloat16>(qkv + row * ldqkv + static_cast<int64_t>(h) * 2 * D + D + d, g);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const float sg = rbf(__fdiv_rn(1.0f, 1.0f + expf(-g[i])));
+        const float sg = sigmoid_bf16(g[i]);
         v[j][i] = rbf(v[j][i] * sg);
         amax = fmaxf(amax, fabsf(v[j][i]));
       }
     }
   }
   amax = block_max(amax, red);
-  const float sc = quant_scale(amax);
+  const float sc = quant_scale(amax), rs = quant_recip(sc);
 #pragma unroll
   for (int j = 0; j < VPT; ++j) {
     const int e = (j * kRowThreads + threadIdx.x) * 8;
-    if (e < W) store8_i8(q + row * W + e, v[j], sc);
+    if (e < W) store8_i8(q + row * W + e, v[j], sc, rs);
   }
   if (threadIdx.x == 0) s_out[row] = sc;
 }
@@ -455,10 +466,12 @@ extern "C" int od_rmsnorm_res_quant(const void* x, const void* res_in, void* res
 #define OD_RN(V) rmsnorm_res_quant_kernel<V><<<grid, block, 0, st>>>(X, RI, RO, Wt, IS, eps, H, Y, q, s)
   if (vecs <= 1) OD_RN(1);
   else if (vecs <= 2) OD_RN(2);
+  else if (vecs <= 3) OD_RN(3);
   else if (vecs <= 4) OD_RN(4);
+  else if (vecs <= 6) OD_RN(6);
   else if (vecs <= 8) OD_RN(8);
   else if (vecs <= 16) OD_RN(16);
-  else return fail(OD_EUNSUPPORTED, "od_rmsnorm_res_quant: H=%d above 16384", H);
+  else return fail(OD_EUNSUPPORTED, "od_rmsnorm_res_quant: H=%d above %d", H, 16 * 8 * kRowThreads);
 #undef OD_RN
   OD_LAUNCH_CHECK();
   return ok();
@@ -493,10 +506,12 @@ extern "C" int od_gate_quant(const void* o, const void* qkv, int64_t ldqkv, int6
 #define OD_GQ(V) gate_quant_kernel<V><<<grid, block, 0, st>>>(O, G, ldqkv, Hq, D, q, s)
   if (vecs <= 1) OD_GQ(1);
   else if (vecs <= 2) OD_GQ(2);
+  else if (vecs <= 3) OD_GQ(3);
   else if (vecs <= 4) OD_GQ(4);
+  else if (vecs <= 6) OD_GQ(6);
   else if (vecs <= 8) OD_GQ(8);
   else if (vecs <= 16) OD_GQ(16);
-  else return fail(OD_EUNSUPPORTED, "od_gate_quant: Hq*D=%d above 16384", W);
+  else return fail(OD_EUNSUPPORTED, "od_gate_quant: Hq*D=%d above %d", W, 16 * 8 * kRowThreads);
 #undef OD_GQ
   OD_LAUNCH_CHECK();
   return ok();

@@ -45,6 +45,45 @@ def test_quant_rows_shapes(cuda, M, K):
     assert np.array_equal(s.cpu().numpy(), so)
 
 
+def test_quant_rows_near_ties_exact(cuda):
+    """Values at and one ulp either side of half-integer multiples of the scale - where rounding x * (1/s) instead of
+    the IEEE quotient x / s would pick the other integer - quantise exactly as clamp(rint(fp32(x / s)), -127, 127)
+    (Int8Tensor.quantize, quant.py:37-41), over scales spanning 30 binades; fp32 rows, so any value is reachable."""
+    rng = np.random.default_rng(5)
+    M, K = 96, 4096
+    x = np.empty((M, K), dtype=np.float32)
+    for m in range(M):
+        amax = np.float32(2.0 ** rng.integers(-20, 10)) * np.float32(rng.uniform(1, 2))
+        s = np.float32(max(amax, np.float32(1e-8)) / np.float32(127))
+        n = rng.integers(-127, 127, K).astype(np.float32) + np.float32(0.5)
+        v = (n * s).astype(np.float32)
+        k = rng.integers(-1, 2, K)
+        v = np.where(k > 0, np.nextafter(v, np.float32(np.inf)), np.where(k < 0, np.nextafter(v, np.float32(-np.inf)), v))
+        v[0] = amax
+        x[m] = v
+    xt = torch.from_numpy(x)
+    q, sc = _lib.quant_rows(xt.to(cuda), scale_dtype=torch.float32)
+    amax = np.abs(x).max(axis=1, keepdims=True)
+    s_ref = (np.maximum(amax, np.float32(1e-8)) / np.float32(127)).astype(np.float32)
+    q_ref = np.clip(np.rint((x / s_ref).astype(np.float32)), -127, 127).astype(np.int8)
+    assert np.array_equal(sc.cpu().numpy(), s_ref)
+    assert np.array_equal(q.cpu().numpy(), q_ref)
+
+
+@pytest.mark.parametrize("M,K", [(5, 12288), (3, 9216), (7, 2048)])
+def test_quant_rows_wide_rows(cuda, M, K):
+    """Rows wider than one pass of the row's threads (several 8-value vectors per thread, ragged tails) against the
+    fp32 formula."""
+    x = torch.randn(M, K, generator=torch.Generator().manual_seed(K)) * 3
+    xb = x.to(torch.bfloat16)
+    q, sc = _lib.quant_rows(xb.to(cuda), scale_dtype=torch.float32)
+    xf = xb.float().numpy()
+    s_ref = (np.maximum(np.abs(xf).max(axis=1, keepdims=True), np.float32(1e-8)) / np.float32(127)).astype(np.float32)
+    q_ref = np.clip(np.rint((xf / s_ref).astype(np.float32)), -127, 127).astype(np.int8)
+    assert np.array_equal(sc.cpu().numpy(), s_ref)
+    assert np.array_equal(q.cpu().numpy(), q_ref)
+
+
 def test_quant_rows_smoothquant_and_stride(cuda):
     """SmoothedLinear's bf16(x * inv_s) before quantisation, on a row-strided view."""
     g = syn.gen(11)
