@@ -42,6 +42,7 @@ int32_t* device_error_word();
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline bool aligned8(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 7u) == 0; }
 
 // ------------------------------------------------------------------------------------------------ element types
 template <typename T> struct Elem;
@@ -87,6 +88,66 @@ __device__ __forceinline__ int8_t quant_val(float x, float s, float r) {
 __device__ __forceinline__ uint32_t quant4(float a, float b, float c, float d, float s, float r) {
   return (static_cast<uint32_t>(quant_int(a, s, r)) & 0xFFu) | ((static_cast<uint32_t>(quant_int(b, s, r)) & 0xFFu) << 8) |
          ((static_cast<uint32_t>(quant_int(c, s, r)) & 0xFFu) << 16) | (static_cast<uint32_t>(quant_int(d, s, r)) << 24);
+}
+
+// ---- bf16 pairs (two bf16 in one 32-bit word, lower element in the low half)
+// RN of the exact product / sum of two bf16 values: equal to rounding the fp32 result to bf16 (a product of two 8-bit
+// significands is exact in fp32; a sum is exact unless the exponents differ by more than 16, and then both forms round
+// to the larger operand).
+__device__ __forceinline__ uint32_t bmul2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t badd2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+// elementwise max of |a| and |b| (exact; NaN operands are ignored as fmaxf does)
+__device__ __forceinline__ uint32_t babsmax2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("max.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a & 0x7FFF7FFFu), "r"(b & 0x7FFF7FFFu));
+  return d;
+}
+__device__ __forceinline__ float bmax_halves(uint32_t a) {
+  return fmaxf(__uint_as_float(a << 16), __uint_as_float(a & 0xFFFF0000u));
+}
+__device__ __forceinline__ uint32_t pack_rn(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ float2 unpack2(uint32_t w) {
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w));
+}
+__device__ __forceinline__ void unpack8(const uint4& w, float (&v)[8]) {
+  const float2 a = unpack2(w.x), b = unpack2(w.y), c = unpack2(w.z), d = unpack2(w.w);
+  v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y; v[4] = c.x; v[5] = c.y; v[6] = d.x; v[7] = d.y;
+}
+__device__ __forceinline__ uint32_t babsmax4(const uint4& w, uint32_t acc) {
+  return babsmax2(acc, babsmax2(babsmax2(w.x, w.y), babsmax2(w.z, w.w)));
+}
+
+// Eight quantised values of a row (quant_int's rounding, two pairs at a time), packed little-endian in two words.
+// The byte of round(y) is the low byte of the bits of y + 1.5 * 2^23. No clamp: every element x of the row whose
+// absmax gave s has |x / s| <= 127 * (1 + 2^-23), which rounds into [-127, 127].
+__device__ __forceinline__ uint2 quant8(const float (&v)[8], float s, float r) {
+  constexpr float kMagic = 12582912.0f;
+  const float2 r2 = make_float2(r, r), m2 = make_float2(kMagic, kMagic), nm2 = make_float2(-kMagic, -kMagic);
+  uint32_t b[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 y = __fmul2_rn(make_float2(v[2 * i], v[2 * i + 1]), r2);
+    float2 t = __fadd2_rn(y, m2);
+    const float2 n = __fadd2_rn(t, nm2);
+    const float2 d = __fadd2_rn(y, make_float2(-n.x, -n.y));
+    if (fabsf(d.x) > 0.4999f) t.x = __fadd_rn(__fdiv_rn(v[2 * i], s), kMagic);
+    if (fabsf(d.y) > 0.4999f) t.y = __fadd_rn(__fdiv_rn(v[2 * i + 1], s), kMagic);
+    b[2 * i] = __float_as_uint(t.x);
+    b[2 * i + 1] = __float_as_uint(t.y);
+  }
+  return make_uint2(__byte_perm(__byte_perm(b[0], b[1], 0x0040), __byte_perm(b[2], b[3], 0x0040), 0x5410),
+                    __byte_perm(__byte_perm(b[4], b[5], 0x0040), __byte_perm(b[6], b[7], 0x0040), 0x5410));
 }
 
 __device__ __forceinline__ float warp_max(float v) {

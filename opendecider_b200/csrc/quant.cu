@@ -51,8 +51,7 @@ template <> __device__ __forceinline__ void store8<__nv_bfloat16>(__nv_bfloat16*
 }
 
 __device__ __forceinline__ void store8_i8(int8_t* p, const float (&v)[8], float s, float r) {
-  *reinterpret_cast<uint2*>(p) =
-      make_uint2(quant4(v[0], v[1], v[2], v[3], s, r), quant4(v[4], v[5], v[6], v[7], s, r));
+  *reinterpret_cast<uint2*>(p) = quant8(v, s, r);
 }
 
 // Round a value to the precision of T (the dtype a PyTorch op on T tensors stores).
@@ -119,11 +118,56 @@ __global__ void __launch_bounds__(kRowThreads) quant_rows_kernel(const T* __rest
   if (threadIdx.x == 0) store_scale(scale, row, s, scale_dtype);
 }
 
+// The bf16 form without SmoothQuant (the activation path): the row stays packed, absmax by bf16 pair max.
+template <int VPT>
+__global__ void __launch_bounds__(kRowThreads) quant_rows_bf16_kernel(const __nv_bfloat16* __restrict__ x, int64_t K,
+                                                                      int64_t ldx, int8_t* __restrict__ q, void* scale,
+                                                                      int scale_dtype) {
+  __shared__ float red[kRowThreads / 32];
+  const int64_t row = blockIdx.x;
+  const __nv_bfloat16* xr = x + row * ldx;
+  uint4 v[VPT];
+  uint32_t am = 0u;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int64_t e = (static_cast<int64_t>(j) * kRowThreads + threadIdx.x) * 8;
+    v[j] = e < K ? __ldg(reinterpret_cast<const uint4*>(xr + e)) : make_uint4(0, 0, 0, 0);
+    am = babsmax4(v[j], am);
+  }
+  const float amax = block_max(bmax_halves(am), red);
+  const float s = quant_scale(amax), rs = quant_recip(s);
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int64_t e = (static_cast<int64_t>(j) * kRowThreads + threadIdx.x) * 8;
+    if (e < K) {
+      float f[8];
+      unpack8(v[j], f);
+      *reinterpret_cast<uint2*>(q + row * K + e) = quant8(f, s, rs);
+    }
+  }
+  if (threadIdx.x == 0) store_scale(scale, row, s, scale_dtype);
+}
+
 template <typename T>
 int launch_quant_rows(const T* x, int64_t M, int64_t K, int64_t ldx, const __nv_bfloat16* inv_s, int8_t* q,
                       void* scale, int scale_dtype, cudaStream_t st) {
   const int64_t vecs = (K / 8 + kRowThreads - 1) / kRowThreads;
   dim3 grid(static_cast<unsigned>(M)), block(kRowThreads);
+  if (std::is_same<T, __nv_bfloat16>::value && !inv_s && vecs <= 16 && ldx % 8 == 0) {
+    const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(x);
+#define OD_QB(V) quant_rows_bf16_kernel<V><<<grid, block, 0, st>>>(xb, K, ldx, q, scale, scale_dtype)
+    if (vecs <= 1) OD_QB(1);
+    else if (vecs <= 2) OD_QB(2);
+    else if (vecs <= 3) OD_QB(3);
+    else if (vecs <= 4) OD_QB(4);
+    else if (vecs <= 6) OD_QB(6);
+    else if (vecs <= 8) OD_QB(8);
+    else if (vecs <= 12) OD_QB(12);
+    else OD_QB(16);
+#undef OD_QB
+    OD_LAUNCH_CHECK();
+    return ok();
+  }
 #define OD_QR(V) quant_rows_kernel<T, V><<<grid, block, 0, st>>>(x, K, ldx, inv_s, q, scale, scale_dtype)
   if (vecs <= 1) OD_QR(1);
   else if (vecs <= 2) OD_QR(2);
@@ -154,36 +198,46 @@ __global__ void dequant_rows_kernel(const int8_t* __restrict__ q, const void* sc
 }
 
 // ---------------------------------------------------------------------------------------------- KV append
-// One warp per (state, new token, head) row of D elements; EPL = D / 32 contiguous elements per lane.
+// One warp per (state, new token, head) row of D elements; EPL = D / 32 contiguous elements per lane. The grid's y
+// index is the state, x covers the (token, head) rows of one state (32-bit index arithmetic).
 template <typename T, int EPL>
 __global__ void kv_append_kernel(const T* __restrict__ k, const T* __restrict__ v, int64_t S, int64_t t, int Hkv,
                                  int64_t ks_s, int64_t ks_t, int64_t ks_h, int64_t vs_s, int64_t vs_t, int64_t vs_h,
                                  int8_t* __restrict__ kq, int8_t* __restrict__ vq, T* __restrict__ ksc,
-                                 T* __restrict__ vsc, int64_t T_cap, int64_t t0) {
+                                 T* __restrict__ vsc, int64_t T_cap, int64_t t0, bool vec) {
   constexpr int D = EPL * 32;
-  const int64_t item = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
+  const int item = static_cast<int>((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
   const int lane = threadIdx.x & 31;
-  const int64_t rows = S * t * Hkv;
-  if (item >= rows) return;
-  const int h = static_cast<int>(item % Hkv);
-  const int64_t j = (item / Hkv) % t;
-  const int64_t s = item / (Hkv * t);
+  if (item >= static_cast<int>(t) * Hkv) return;
+  const int64_t j = item / Hkv;
+  const int h = item - static_cast<int>(j) * Hkv;
+  const int64_t s = blockIdx.y;
   const int64_t dst = ((s * Hkv + h) * T_cap + t0 + j);
 #pragma unroll
   for (int which = 0; which < 2; ++which) {
-    const T* src = which == 0 ? k + s * ks_s + j * ks_t + h * ks_h : v + s * vs_s + j * vs_t + h * vs_h;
+    const T* src = (which == 0 ? k + s * ks_s + j * ks_t + h * ks_h : v + s * vs_s + j * vs_t + h * vs_h) + lane * EPL;
     float x[EPL];
+    if (EPL == 4 && sizeof(T) == 2 && vec) {             // one 8-byte load per lane
+      const uint2 raw = __ldg(reinterpret_cast<const uint2*>(src));
+      const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) x[i] = Elem<T>::to_f(e[i]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < EPL; ++i) x[i] = Elem<T>::to_f(src[i]);
+    }
     float amax = 0.f;
 #pragma unroll
-    for (int i = 0; i < EPL; ++i) {
-      x[i] = Elem<T>::to_f(src[lane * EPL + i]);
-      amax = fmaxf(amax, fabsf(x[i]));
-    }
+    for (int i = 0; i < EPL; ++i) amax = fmaxf(amax, fabsf(x[i]));
     amax = warp_max(amax);
     const float sc = quant_scale(amax), rs = quant_recip(sc);
     int8_t* out = (which == 0 ? kq : vq) + dst * D + lane * EPL;
+    if (EPL == 4 && vec) {                                // one 4-byte store per lane
+      *reinterpret_cast<uint32_t*>(out) = quant4(x[0], x[1], x[2], x[3], sc, rs);
+    } else {
 #pragma unroll
-    for (int i = 0; i < EPL; ++i) out[i] = quant_val(x[i], sc, rs);
+      for (int i = 0; i < EPL; ++i) out[i] = quant_val(x[i], sc, rs);
+    }
     if (lane == 0) (which == 0 ? ksc : vsc)[dst] = Elem<T>::from_f(sc);
   }
 }
@@ -198,55 +252,68 @@ __global__ void __launch_bounds__(kRowThreads) rmsnorm_res_quant_kernel(
   __shared__ float red[kRowThreads / 32];
   const int64_t row = blockIdx.x;
   const int64_t base = row * H;
-  float v[VPT][8];
+  uint4 hv[VPT];                                      // the row (hidden, then y), packed bf16
   float ss = 0.f;
 #pragma unroll
   for (int j = 0; j < VPT; ++j) {
     const int e = (j * kRowThreads + threadIdx.x) * 8;
+    hv[j] = make_uint4(0, 0, 0, 0);
     if (e < H) {
-      load8<__nv_bfloat16>(x + base + e, v[j]);
+      uint4 xv = __ldg(reinterpret_cast<const uint4*>(x + base + e));
       if (res_in) {  // hidden = residual + hidden, one bf16 rounding
-        float r[8];
-        load8<__nv_bfloat16>(res_in + base + e, r);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) v[j][i] = rbf(r[i] + v[j][i]);
-        store8<__nv_bfloat16>(res_out + base + e, v[j]);
+        const uint4 rv = __ldg(reinterpret_cast<const uint4*>(res_in + base + e));
+        xv = make_uint4(badd2(rv.x, xv.x), badd2(rv.y, xv.y), badd2(rv.z, xv.z), badd2(rv.w, xv.w));
+        *reinterpret_cast<uint4*>(res_out + base + e) = xv;
       }
+      hv[j] = xv;
+      float f[8];
+      unpack8(xv, f);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) ss += v[j][i] * v[j][i];
+      for (int i = 0; i < 8; ++i) ss += f[i] * f[i];
     }
   }
   ss = block_sum(ss, red);
   // torch.rsqrt(x.pow(2).mean(-1) + eps): mean in fp32, then 1 / sqrt (the CPU reference rounds twice)
   const float var = __fdiv_rn(ss, static_cast<float>(H));
   const float rs = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
-  float amax = 0.f;
+  const float2 rs2 = make_float2(rs, rs), one2 = make_float2(1.0f, 1.0f);
+  uint32_t am = 0u;
 #pragma unroll
   for (int j = 0; j < VPT; ++j) {
     const int e = (j * kRowThreads + threadIdx.x) * 8;
     if (e < H) {
-      float wv[8];
-      load8<__nv_bfloat16>(w + e, wv);
+      const uint4 wv = __ldg(reinterpret_cast<const uint4*>(w + e));
+      const uint32_t* hw = &hv[j].x;
+      const uint32_t* ww = &wv.x;
+      uint32_t y[4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) v[j][i] = rbf(__fmul_rn(__fmul_rn(v[j][i], rs), __fadd_rn(1.0f, wv[i])));
-      if (inv_s) {
-        float is[8];
-        load8<__nv_bfloat16>(inv_s + e, is);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) v[j][i] = rbf(v[j][i] * is[i]);
+      for (int i = 0; i < 4; ++i) {               // y = bf16((h * rs) * (1 + w))
+        const float2 v = __fmul2_rn(__fmul2_rn(unpack2(hw[i]), rs2), __fadd2_rn(one2, unpack2(ww[i])));
+        y[i] = pack_rn(v.x, v.y);
       }
-      if (y_out) store8<__nv_bfloat16>(y_out + base + e, v[j]);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[j][i]));
+      if (inv_s) {                                 // SmoothQuant: bf16(y * inv_s)
+        const uint4 is = __ldg(reinterpret_cast<const uint4*>(inv_s + e));
+        y[0] = bmul2(y[0], is.x);
+        y[1] = bmul2(y[1], is.y);
+        y[2] = bmul2(y[2], is.z);
+        y[3] = bmul2(y[3], is.w);
+      }
+      hv[j] = make_uint4(y[0], y[1], y[2], y[3]);
+      if (y_out) *reinterpret_cast<uint4*>(y_out + base + e) = hv[j];
+      am = babsmax4(hv[j], am);
     }
   }
   if (!q) return;
-  amax = block_max(amax, red);
+  const float amax = block_max(bmax_halves(am), red);
   const float sc = quant_scale(amax), rq = quant_recip(sc);
 #pragma unroll
   for (int j = 0; j < VPT; ++j) {
     const int e = (j * kRowThreads + threadIdx.x) * 8;
-    if (e < H) store8_i8(q + base + e, v[j], sc, rq);
+    if (e < H) {
+      float f[8];
+      unpack8(hv[j], f);
+      *reinterpret_cast<uint2*>(q + base + e) = quant8(f, sc, rq);
+    }
   }
   if (threadIdx.x == 0) s_out[row] = sc;
 }
@@ -279,14 +346,16 @@ __global__ void embed_i8_kernel(const int64_t* __restrict__ ids, const int8_t* _
 
 // ---------------------------------------------------------------------------------------------- gate + quant
 // sigmoid(g) = 1 / (1 + exp(-g)) in fp32 (expf, IEEE division), rounded to bf16. A fast value from the hardware
-// exp2 / reciprocal approximations (relative error below 1.4e-6 for |g| < 16) rounds to the same bf16 unless it lies
-// within 64 fp32 ulps (relative 3.8e-6) of a bf16 rounding boundary; then, and for |g| >= 16, the fp32 formula decides.
+// exp2 / reciprocal approximations (relative error below 1.4e-6 for |g| < 16) rounds to the same bf16 unless a bf16
+// rounding boundary - a tie, low 16 bits 0x8000 - lies between the two: so only a fast value within 64 fp32 ulps
+// (relative 3.8e-6) of a tie, or |g| >= 16, takes the fp32 formula. (Crossing a bf16-representable value changes
+// the upper bits but both sides round to that value.)
 __device__ __forceinline__ float sigmoid_bf16(float g) {
   float e, v;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(g * -1.4426950408889634f));
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(v) : "f"(1.0f + e));
   const int lo = static_cast<int>(__float_as_uint(v) & 0xFFFFu);
-  if (fabsf(g) >= 16.0f || abs(lo - 0x8000) < 64 || lo < 64 || lo > 0xFFFF - 64) v = __fdiv_rn(1.0f, 1.0f + expf(-g));
+  if (fabsf(g) >= 16.0f || abs(lo - 0x8000) < 64) v = __fdiv_rn(1.0f, 1.0f + expf(-g));
   return rbf(v);
 }
 
@@ -299,30 +368,35 @@ __global__ void __launch_bounds__(kRowThreads) gate_quant_kernel(const __nv_bflo
   __shared__ float red[kRowThreads / 32];
   const int64_t row = blockIdx.x;
   const int W = Hq * D;
-  float v[VPT][8];
-  float amax = 0.f;
+  uint4 vv[VPT];                                      // bf16(o * sigmoid(gate)), packed
+  uint32_t am = 0u;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int e = (j * kRowThreads + threadIdx.x) * 8;
+    vv[j] = make_uint4(0, 0, 0, 0);
+    if (e < W) {
+      const int h = e / D, d = e - h * D;
+      const uint4 ov = __ldg(reinterpret_cast<const uint4*>(o + row * W + e));
+      const uint4 gv = __ldg(reinterpret_cast<const uint4*>(qkv + row * ldqkv + static_cast<int64_t>(h) * 2 * D + D + d));
+      float g[8];
+      unpack8(gv, g);
+      vv[j] = make_uint4(bmul2(ov.x, pack_rn(sigmoid_bf16(g[0]), sigmoid_bf16(g[1]))),
+                         bmul2(ov.y, pack_rn(sigmoid_bf16(g[2]), sigmoid_bf16(g[3]))),
+                         bmul2(ov.z, pack_rn(sigmoid_bf16(g[4]), sigmoid_bf16(g[5]))),
+                         bmul2(ov.w, pack_rn(sigmoid_bf16(g[6]), sigmoid_bf16(g[7]))));
+      am = babsmax4(vv[j], am);
+    }
+  }
+  const float amax = block_max(bmax_halves(am), red);
+  const float sc = quant_scale(amax), rq = quant_recip(sc);
 #pragma unroll
   for (int j = 0; j < VPT; ++j) {
     const int e = (j * kRowThreads + threadIdx.x) * 8;
     if (e < W) {
-      const int h = e / D, d = e % D;
-      float g[8];
-      load8<__nv_bfloat16>(o + row * W + e, v[j]);
-      load8<__nv_bfloat16>(qkv + row * ldqkv + static_cast<int64_t>(h) * 2 * D + D + d, g);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float sg = sigmoid_bf16(g[i]);
-        v[j][i] = rbf(v[j][i] * sg);
-        amax = fmaxf(amax, fabsf(v[j][i]));
-      }
+      float f[8];
+      unpack8(vv[j], f);
+      *reinterpret_cast<uint2*>(q + row * W + e) = quant8(f, sc, rq);
     }
-  }
-  amax = block_max(amax, red);
-  const float sc = quant_scale(amax), rs = quant_recip(sc);
-#pragma unroll
-  for (int j = 0; j < VPT; ++j) {
-    const int e = (j * kRowThreads + threadIdx.x) * 8;
-    if (e < W) store8_i8(q + row * W + e, v[j], sc, rs);
   }
   if (threadIdx.x == 0) s_out[row] = sc;
 }
@@ -422,13 +496,17 @@ extern "C" int od_kv_append_i8(const void* k, const void* v, int kv_dtype, int64
   OD_REQUIRE(D == 64 || D == 128 || D == 256, "od_kv_append_i8: head_dim %d not in {64, 128, 256}", D);
   if (S == 0 || t == 0) return ok();
   cudaStream_t st = as_stream(stream);
-  const int64_t rows = S * t * Hkv;
+  OD_REQUIRE(S < 65536 && t * Hkv < (1LL << 26), "od_kv_append_i8: too many states or tokens in one call");
   const int threads = 256;
-  const unsigned blocks = static_cast<unsigned>((rows * 32 + threads - 1) / threads);
+  const dim3 blocks(static_cast<unsigned>((t * Hkv * 32 + threads - 1) / threads), static_cast<unsigned>(S));
+  // 8-byte loads / 4-byte stores per lane when every row start allows them (element strides multiples of 4)
+  const auto a = [](const void* p, uintptr_t n) { return (reinterpret_cast<uintptr_t>(p) & (n - 1)) == 0; };
+  const bool vec = a(k, 8) && a(v, 8) && a(kq, 4) && a(vq, 4) && ks_s % 4 == 0 && ks_t % 4 == 0 && ks_h % 4 == 0 &&
+                   vs_s % 4 == 0 && vs_t % 4 == 0 && vs_h % 4 == 0;
 #define OD_KV(T_, E)                                                                                           \
   kv_append_kernel<T_, E><<<blocks, threads, 0, st>>>(static_cast<const T_*>(k), static_cast<const T_*>(v), S, t, \
                                                       Hkv, ks_s, ks_t, ks_h, vs_s, vs_t, vs_h, kq, vq,          \
-                                                      static_cast<T_*>(ksc), static_cast<T_*>(vsc), T_cap, t0)
+                                                      static_cast<T_*>(ksc), static_cast<T_*>(vsc), T_cap, t0, vec)
   if (kv_dtype == OD_BF16) {
     if (D == 64) OD_KV(__nv_bfloat16, 2); else if (D == 128) OD_KV(__nv_bfloat16, 4); else OD_KV(__nv_bfloat16, 8);
   } else if (kv_dtype == OD_F16) {

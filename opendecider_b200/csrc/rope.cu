@@ -1,7 +1,7 @@
 // Attention pre-processing on the fused q/k/v projection output: gated-q split, per-head q/k RMSNorm (1 + w) and
 // rotate-half RoPE, with the rounding points of the bf16 reference (Qwen3_5Attention.forward, prefix_attn._forward).
-// One warp per (token, head slot); each lane holds D/32 contiguous elements, so rotate_half's partner element
-// (d +- D/2) sits in lane ^ 16 and is exchanged with one shuffle.
+// One CTA per token, one warp per head slot at a time; each lane holds D/32 contiguous elements, so rotate_half's
+// partner element (d +- D/2) sits in lane ^ 16 and is exchanged with one shuffle.
 #include "common.cuh"
 
 namespace od {
@@ -10,10 +10,13 @@ namespace {
 template <int EPL>
 __device__ __forceinline__ void load_lane(const __nv_bfloat16* p, float (&x)[EPL]) {
   if constexpr (EPL == 4) {
-    uint2 raw = *reinterpret_cast<const uint2*>(p);
+    uint2 raw = __ldg(reinterpret_cast<const uint2*>(p));
     const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
     float2 a = __bfloat1622float2(h[0]), b = __bfloat1622float2(h[1]);
     x[0] = a.x; x[1] = a.y; x[2] = b.x; x[3] = b.y;
+  } else if constexpr (EPL == 2) {
+    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
+    x[0] = a.x; x[1] = a.y;
   } else {
 #pragma unroll
     for (int i = 0; i < EPL; ++i) x[i] = __bfloat162float(p[i]);
@@ -33,60 +36,113 @@ __device__ __forceinline__ void store_lane(__nv_bfloat16* p, const float (&x)[EP
   }
 }
 
+// One CTA of kWarps warps per token: the token's cos / sin rows and the two (1 + w) norm factors are loaded once
+// per lane and serve all of the token's q and k heads; each warp takes head slots warp, warp + kWarps, ... and issues
+// the loads of all of them before the math. A lane holds NW = EPL / 2 bf16 pairs of each head.
+constexpr int kWarps = 8;
+constexpr int kMaxSlotsPerWarp = 8;   // Hq + 2 Hkv <= 64
+
 template <int EPL>
-__global__ void qk_norm_rope_kernel(const __nv_bfloat16* __restrict__ qkv, int64_t ld, const int32_t* __restrict__ pos,
-                                    const __nv_bfloat16* __restrict__ cos_t, const __nv_bfloat16* __restrict__ sin_t,
-                                    int64_t P, const __nv_bfloat16* __restrict__ qw, const __nv_bfloat16* __restrict__ kw,
-                                    float eps, int64_t M, int Hq, int Hkv, __nv_bfloat16* __restrict__ qo,
-                                    __nv_bfloat16* __restrict__ ko, __nv_bfloat16* __restrict__ vo, int32_t* err) {
+__device__ __forceinline__ void load_pairs(const __nv_bfloat16* p, uint32_t (&w)[EPL / 2]) {
+  if constexpr (EPL == 4) {
+    const uint2 r = __ldg(reinterpret_cast<const uint2*>(p));
+    w[0] = r.x;
+    w[1] = r.y;
+  } else if constexpr (EPL == 8) {
+    const uint4 r = __ldg(reinterpret_cast<const uint4*>(p));
+    w[0] = r.x; w[1] = r.y; w[2] = r.z; w[3] = r.w;
+  } else {
+    w[0] = __ldg(reinterpret_cast<const uint32_t*>(p));
+  }
+}
+template <int EPL>
+__device__ __forceinline__ void store_pairs(__nv_bfloat16* p, const uint32_t (&w)[EPL / 2]) {
+  if constexpr (EPL == 4) {
+    *reinterpret_cast<uint2*>(p) = make_uint2(w[0], w[1]);
+  } else if constexpr (EPL == 8) {
+    *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+  } else {
+    *reinterpret_cast<uint32_t*>(p) = w[0];
+  }
+}
+
+template <int EPL>
+__global__ void __launch_bounds__(32 * kWarps) qk_norm_rope_kernel(
+    const __nv_bfloat16* __restrict__ qkv, int64_t ld, const int32_t* __restrict__ pos,
+    const __nv_bfloat16* __restrict__ cos_t, const __nv_bfloat16* __restrict__ sin_t, int64_t P,
+    const __nv_bfloat16* __restrict__ qw, const __nv_bfloat16* __restrict__ kw, float eps, int64_t M, int Hq, int Hkv,
+    __nv_bfloat16* __restrict__ qo, __nv_bfloat16* __restrict__ ko, __nv_bfloat16* __restrict__ vo, int32_t* err) {
   constexpr int D = EPL * 32;
-  const int64_t item = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
+  constexpr int NW = EPL / 2;
+  const int64_t tok = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int slots = Hq + 2 * Hkv;
-  if (item >= M * slots) return;
-  const int64_t tok = item / slots;
-  const int slot = static_cast<int>(item % slots);
   const __nv_bfloat16* row = qkv + tok * ld;
-  float x[EPL];
-  if (slot >= Hq + Hkv) {  // value head: plain copy
-    const int h = slot - Hq - Hkv;
-    load_lane<EPL>(row + static_cast<int64_t>(Hq) * 2 * D + static_cast<int64_t>(Hkv) * D + h * D + lane * EPL, x);
-    store_lane<EPL>(vo + (tok * Hkv + h) * D + lane * EPL, x);
-    return;
-  }
-  const bool is_q = slot < Hq;
-  const int h = is_q ? slot : slot - Hq;
-  const __nv_bfloat16* src = is_q ? row + static_cast<int64_t>(h) * 2 * D : row + static_cast<int64_t>(Hq) * 2 * D + h * D;
-  const __nv_bfloat16* w = is_q ? qw : kw;
-  load_lane<EPL>(src + lane * EPL, x);
-  // Qwen3_5RMSNorm over the head dimension
-  float ss = 0.f;
+  // the slot's source: q head h at h * 2D (its gate follows), k head at Hq * 2D + h * D, v head after the k heads
+  uint32_t x[kMaxSlotsPerWarp][NW];
 #pragma unroll
-  for (int i = 0; i < EPL; ++i) ss += x[i] * x[i];
-  ss = warp_sum(ss);
-  const float rs = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(D)), eps)));
-#pragma unroll
-  for (int i = 0; i < EPL; ++i) {
-    const float wi = __bfloat162float(w[lane * EPL + i]);
-    x[i] = rbf(__fmul_rn(__fmul_rn(x[i], rs), __fadd_rn(1.0f, wi)));
+  for (int i = 0; i < kMaxSlotsPerWarp; ++i) {
+    const int slot = warp + i * kWarps;
+    if (slot < slots) {
+      const __nv_bfloat16* src = slot < Hq ? row + static_cast<int64_t>(slot) * 2 * D
+                                           : row + static_cast<int64_t>(Hq) * 2 * D + static_cast<int64_t>(slot - Hq) * D;
+      load_pairs<EPL>(src + lane * EPL, x[i]);
+    }
   }
-  // RoPE: q*cos + rotate_half(q)*sin, each product and the sum rounded to bf16
   int p = pos[tok];
   if (p < 0 || p >= P) {
-    if (lane == 0) atomicCAS(err, 0, 0x7E0000 | 1);
+    if (threadIdx.x == 0) atomicCAS(err, 0, 0x7E0000 | 1);
     p = 0;
   }
-  const __nv_bfloat16* c = cos_t + static_cast<int64_t>(p) * D + lane * EPL;
-  const __nv_bfloat16* s = sin_t + static_cast<int64_t>(p) * D + lane * EPL;
-  float y[EPL];
+  uint32_t c[NW], sn[NW], wq[NW], wk[NW];
+  load_pairs<EPL>(cos_t + static_cast<int64_t>(p) * D + lane * EPL, c);
+  load_pairs<EPL>(sin_t + static_cast<int64_t>(p) * D + lane * EPL, sn);
+  load_pairs<EPL>(qw + lane * EPL, wq);
+  load_pairs<EPL>(kw + lane * EPL, wk);
+  float2 q1[NW], k1[NW];                              // 1 + w in fp32 (Qwen3_5RMSNorm's weight offset)
 #pragma unroll
-  for (int i = 0; i < EPL; ++i) {
-    const float partner = __shfl_xor_sync(0xffffffffu, x[i], 16);
-    const float rh = lane < 16 ? -partner : partner;
-    y[i] = rbf(rbf(x[i] * __bfloat162float(c[i])) + rbf(rh * __bfloat162float(s[i])));
+  for (int e = 0; e < NW; ++e) {
+    q1[e] = __fadd2_rn(make_float2(1.0f, 1.0f), unpack2(wq[e]));
+    k1[e] = __fadd2_rn(make_float2(1.0f, 1.0f), unpack2(wk[e]));
   }
-  __nv_bfloat16* dst = is_q ? qo + (tok * Hq + h) * D : ko + (tok * Hkv + h) * D;
-  store_lane<EPL>(dst + lane * EPL, y);
+  const uint32_t neg = lane < 16 ? 0x80008000u : 0u;  // rotate_half negates the first half's partners
+#pragma unroll
+  for (int i = 0; i < kMaxSlotsPerWarp; ++i) {
+    const int slot = warp + i * kWarps;
+    if (slot >= slots) break;
+    if (slot >= Hq + Hkv) {                           // value head: plain copy
+      store_pairs<EPL>(vo + (tok * Hkv + (slot - Hq - Hkv)) * D + lane * EPL, x[i]);
+      continue;
+    }
+    const bool is_q = slot < Hq;
+    // Qwen3_5RMSNorm over the head dimension: mean of squares in fp32 (/ D is exact: D is a power of two),
+    // y = bf16((x * rs) * (1 + w))
+    float ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < NW; ++e) {
+      const float2 f = unpack2(x[i][e]);
+      ss += f.x * f.x;
+      ss += f.y * f.y;
+    }
+    ss = warp_sum(ss);
+    const float rs = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(ss, 1.0f / D), eps)));
+    const float2 rs2 = make_float2(rs, rs);
+    uint32_t y[NW];
+#pragma unroll
+    for (int e = 0; e < NW; ++e) {
+      const float2 v = __fmul2_rn(__fmul2_rn(unpack2(x[i][e]), rs2), is_q ? q1[e] : k1[e]);
+      y[e] = pack_rn(v.x, v.y);
+    }
+    // RoPE: q*cos + rotate_half(q)*sin, each product and the sum rounded to bf16; the partner element d +- D/2
+    // sits in lane ^ 16
+#pragma unroll
+    for (int e = 0; e < NW; ++e) {
+      const uint32_t rh = __shfl_xor_sync(0xffffffffu, y[e], 16) ^ neg;
+      x[i][e] = badd2(bmul2(y[e], c[e]), bmul2(rh, sn[e]));
+    }
+    __nv_bfloat16* dst = is_q ? qo + (tok * Hq + slot) * D : ko + (tok * Hkv + (slot - Hq)) * D;
+    store_pairs<EPL>(dst + lane * EPL, x[i]);
+  }
 }
 
 }  // namespace
@@ -100,13 +156,18 @@ extern "C" int od_qk_norm_rope(const void* qkv, const int32_t* pos, const void* 
   OD_REQUIRE(qkv && pos && cos && sin && qnorm_w && knorm_w && q_out && k_out && v_out, "od_qk_norm_rope: null pointer");
   OD_REQUIRE(M >= 0 && Hq > 0 && Hkv > 0 && Hq % Hkv == 0 && P > 0, "od_qk_norm_rope: bad shape");
   OD_REQUIRE(D == 64 || D == 128 || D == 256, "od_qk_norm_rope: head_dim %d not in {64, 128, 256}", D);
+  OD_REQUIRE(aligned8(qkv) && aligned8(cos) && aligned8(sin) && aligned8(qnorm_w) && aligned8(knorm_w) &&
+                 aligned8(q_out) && aligned8(k_out) && aligned8(v_out),
+             "od_qk_norm_rope: pointers must be 8-byte aligned");
   if (M == 0) return ok();
   int32_t* err = device_error_word();
   if (!err) return fail(OD_ECUDA, "od_qk_norm_rope: no device error word");
   const int64_t ld = static_cast<int64_t>(Hq) * 2 * D + 2LL * Hkv * D;
-  const int64_t warps = M * (Hq + 2 * Hkv);
-  const int threads = 256;
-  const unsigned blocks = static_cast<unsigned>((warps * 32 + threads - 1) / threads);
+  OD_REQUIRE(Hq + 2 * Hkv <= kWarps * kMaxSlotsPerWarp, "od_qk_norm_rope: more than %d head slots",
+             kWarps * kMaxSlotsPerWarp);
+  OD_REQUIRE(M < (1LL << 31), "od_qk_norm_rope: too many tokens");
+  const int threads = 32 * kWarps;
+  const unsigned blocks = static_cast<unsigned>(M);
   cudaStream_t st = as_stream(stream);
   auto Q = static_cast<const __nv_bfloat16*>(qkv);
   auto C = static_cast<const __nv_bfloat16*>(cos);
