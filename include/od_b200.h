@@ -139,9 +139,11 @@ OD_API int od_gate_quant(const void* o, const void* qkv, int64_t ldqkv, int64_t 
 /* ---------------------------------------------------------------------------------------------------------------
  * A9/A10: branched shared-prefix attention (Hydragen split, prefix_attn.py:43-76, merged exactly by log-sum-exp).
  * Every query row r (a question or option row, t tokens, Hq heads) attends, in ONE online softmax:
- *   1. the int8 state prefix of state st = row_state[r]: keys p in [p_lo[st], p_hi[st]) of Kp/Vp (S, Hkv, T, D) int8
- *      with per-token scales ksc/vsc (S, Hkv, T); keys with pmask[st, p] == 0 are skipped (pmask may be NULL).
- *      Dequantised in shared memory exactly as materialize() does (bf16(q * s); fp16 scales: bf16(fp16(q * s))).
+ *   1. the state prefix of state st = row_state[r]: keys p in [p_lo[st], p_hi[st]) of Kp/Vp (S, Hkv, T, D); keys
+ *      with pmask[st, p] == 0 are skipped (pmask may be NULL). Either int8 with per-token scales ksc/vsc
+ *      (S, Hkv, T), dequantised in shared memory exactly as materialize() does (bf16(q * s); fp16 scales:
+ *      bf16(fp16(q * s))), or (dims.prefix_bf16 = 1) the already materialised bf16 cache (prefix_attn.py:146-149),
+ *      ksc/vsc unused.
  *   2. optionally a second bf16 prefix level (the question cache, prefix_attn.py:94-99): keys j < q_len[qr] of
  *      Kq/Vq (NQ, Lq, Hkv, D) for question qr = row_q[r].
  *   3. its own k/v (R, t, Hkv, D) bf16 causally: key j visible to query i iff j <= i and
@@ -161,9 +163,10 @@ typedef struct {
   float sm_scale;               /* softmax scale (head_dim ** -0.5) */
   int64_t G;                    /* number of row groups (used when row_groups != NULL) */
   int max_group_rows;           /* largest group (used when row_groups != NULL) */
+  int prefix_bf16;              /* 1: Kp/Vp are bf16 (materialised), 0: int8 + ksc/vsc */
 } od_attn_dims;
 
-OD_API int od_prefix_attn(const void* q, const int8_t* Kp, const int8_t* Vp, const void* ksc, const void* vsc,
+OD_API int od_prefix_attn(const void* q, const void* Kp, const void* Vp, const void* ksc, const void* vsc,
                           const int32_t* row_state, const int32_t* p_lo, const int32_t* p_hi, const uint8_t* pmask,
                           const void* Kq, const void* Vq, const int32_t* row_q, const int32_t* q_len,
                           const void* k_own, const void* v_own, const int32_t* own_lo, const int32_t* own_hi,

@@ -28,7 +28,7 @@ class ODError(RuntimeError):
 class AttnDims(ctypes.Structure):
     _fields_ = [("R", c_int64), ("t", c_int64), ("S", c_int64), ("T", c_int64), ("NQ", c_int64), ("Lq", c_int64),
                 ("Hq", c_int), ("Hkv", c_int), ("D", c_int), ("scale_dtype", c_int), ("sm_scale", c_float),
-                ("G", c_int64), ("max_group_rows", c_int)]
+                ("G", c_int64), ("max_group_rows", c_int), ("prefix_bf16", c_int)]
 
 
 # exported symbol -> argument types (the declarations of include/od_b200.h)
@@ -155,10 +155,12 @@ def quant_rows(x: torch.Tensor, scale_dtype: torch.dtype | None = None, inv_s: t
 
 
 @_probed
-def dequant_rows(q: torch.Tensor, scale: torch.Tensor, out_dtype: torch.dtype) -> torch.Tensor:
+def dequant_rows(q: torch.Tensor, scale: torch.Tensor, out_dtype: torch.dtype, out: torch.Tensor | None = None):
+    """Int8Tensor.dequantize: bf16/f16/f32 (q * scale) per row of the last dim; into `out` when given."""
     dev = _need_cuda(q, scale)
     M, K = q.reshape(-1, q.shape[-1]).shape
-    y = torch.empty(q.shape, dtype=out_dtype, device=dev)
+    y = torch.empty(q.shape, dtype=out_dtype, device=dev) if out is None else out
+    assert y.dtype == out_dtype and y.numel() == q.numel() and y.is_contiguous()
     _check(load().od_dequant_rows_i8(_p(q), _p(scale), _DT[scale.dtype], M, K, _p(y), _DT[out_dtype], _stream(dev)),
            "od_dequant_rows_i8")
     return y
@@ -261,7 +263,8 @@ def prefix_attn(q: torch.Tensor, k_own: torch.Tensor, v_own: torch.Tensor, sm_sc
                 Kp=None, Vp=None, ksc=None, vsc=None, row_state=None, p_lo=None, p_hi=None, pmask=None,
                 Kq=None, Vq=None, row_q=None, q_len=None, own_lo=None, own_hi=None, row_groups=None,
                 max_group_rows: int = 1, out=None, want_lse: bool = False):
-    """q (R, t, Hq, D), own k/v (R, t, Hkv, D) bf16; int8 prefix Kp/Vp (S, Hkv, T, D) + scales (S, Hkv, T[, 1]);
+    """q (R, t, Hq, D), own k/v (R, t, Hkv, D) bf16; state prefix Kp/Vp (S, Hkv, T, D): int8 + scales ksc/vsc
+    (S, Hkv, T[, 1]), or bf16 (the materialised cache, scales unused);
     optional bf16 question prefix Kq/Vq (NQ, Lq, Hkv, D); own keys valid in [own_lo[r], own_hi[r]) and causal;
     row_groups (G, 2) int32 [first row, rows] of consecutive rows sharing state and question, processed together
     (max_group_rows = the largest). Returns o (R, t, Hq, D) [, lse (R, Hq, t)]."""
@@ -272,10 +275,13 @@ def prefix_attn(q: torch.Tensor, k_own: torch.Tensor, v_own: torch.Tensor, sm_sc
     lse = torch.empty(R, Hq, t, dtype=torch.float32, device=dev) if want_lse else None
     S, T = (Kp.shape[0], Kp.shape[2]) if Kp is not None else (0, 0)
     NQ, Lq = (Kq.shape[0], Kq.shape[1]) if Kq is not None else (0, 0)
-    sdt = _DT[ksc.dtype] if ksc is not None else OD_BF16
+    pbf16 = Kp is not None and Kp.dtype == torch.bfloat16
+    assert Kp is None or pbf16 or Kp.dtype == torch.int8, "the state prefix is int8 (+ scales) or bf16"
+    sdt = _DT[ksc.dtype] if (ksc is not None and not pbf16) else OD_BF16
     G = row_groups.shape[0] if row_groups is not None else R
-    dims = AttnDims(R, t, S, T, NQ, Lq, Hq, Hkv, D, sdt, sm_scale, G, max_group_rows if row_groups is not None else 1)
-    _check(load().od_prefix_attn(_p(q), _p(Kp), _p(Vp), _p(ksc), _p(vsc), _p(row_state), _p(p_lo), _p(p_hi),
+    dims = AttnDims(R, t, S, T, NQ, Lq, Hq, Hkv, D, sdt, sm_scale, G, max_group_rows if row_groups is not None else 1,
+                    1 if pbf16 else 0)
+    _check(load().od_prefix_attn(_p(q), _p(Kp), _p(Vp), _p(None if pbf16 else ksc), _p(None if pbf16 else vsc), _p(row_state), _p(p_lo), _p(p_hi),
                                  _p(pmask), _p(Kq), _p(Vq), _p(row_q), _p(q_len), _p(k_own), _p(v_own), _p(own_lo),
                                  _p(own_hi), _p(row_groups),
                                  _p(out), _p(lse), dims, _stream(dev)), "od_prefix_attn")

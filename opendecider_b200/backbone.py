@@ -123,13 +123,15 @@ class KVCache:
     p_lo: torch.Tensor       # (S,) int32: first real token of each state (left padding)
     T: int
     lens: list = field(default_factory=list)   # real tokens per state (CPU ints)
+    kb: list | None = None   # per layer bf16 (S, Hkv, T, D): the materialised K (prefix_attn.py:146-149), or None
+    vb: list | None = None
 
     @property
     def S(self) -> int:
         return self.p_lo.numel()
 
     def nbytes(self) -> int:
-        return sum(t.nbytes() for t in self.k + self.v)
+        return sum(t.nbytes() for t in self.k + self.v) + sum(t.nbytes for t in (self.kb or []) + (self.vb or []))
 
 
 @dataclass
@@ -162,6 +164,11 @@ class Backbone:
         from .rope import rope_tables
         self.cos, self.sin = rope_tables(cfg.head_dim, cfg.rope_theta, cfg.max_pos, cfg.dtype, device)
         self.pad_id = 0
+        # the state pass also writes the dequantised bf16 K/V (what materialize() gives the reference's attention,
+        # prefix_attn.py:146-149) when it fits this budget, so the question / option passes stream the prefix by TMA
+        # instead of dequantising it in every attention tile; 0 disables it
+        total = torch.cuda.get_device_properties(device).total_memory if torch.device(device).type == "cuda" else 0
+        self.materialize_budget = total // 4
 
     # ------------------------------------------------------------------------------------------ construction
     @classmethod
@@ -250,14 +257,23 @@ class Backbone:
             if spec.write_cache is not None:
                 wc = spec.write_cache
                 _lib.kv_append(k4, v4, wc.k[li].q, wc.v[li].q, wc.k[li].scale, wc.v[li].scale, t0=0)
+                if wc.kb is not None:                       # materialise once: bf16(q * s) per cached row
+                    D_ = wc.k[li].q.shape[-1]
+                    _lib.dequant_rows(wc.k[li].q.view(-1, D_), wc.k[li].scale.view(-1, 1), torch.bfloat16,
+                                      out=wc.kb[li].view(-1, D_))
+                    _lib.dequant_rows(wc.v[li].q.view(-1, D_), wc.v[li].scale.view(-1, 1), torch.bfloat16,
+                                      out=wc.vb[li].view(-1, D_))
             if captured is not None:
                 captured.append((k4, v4))
             if last and spec.kv_only_last:
                 break
+            mat = cache is not None and cache.kb is not None
             o = _lib.prefix_attn(
                 q.view(R, t, Hq, D), k4, v4, D ** -0.5,
-                Kp=cache.k[li].q if cache else None, Vp=cache.v[li].q if cache else None,
-                ksc=cache.k[li].scale if cache else None, vsc=cache.v[li].scale if cache else None,
+                Kp=(cache.kb[li] if mat else cache.k[li].q) if cache else None,
+                Vp=(cache.vb[li] if mat else cache.v[li].q) if cache else None,
+                ksc=cache.k[li].scale if cache and not mat else None,
+                vsc=cache.v[li].scale if cache and not mat else None,
                 row_state=spec.row_state, p_lo=cache.p_lo if cache else None,
                 Kq=spec.qkv_prefix[li][0] if spec.qkv_prefix else None,
                 Vq=spec.qkv_prefix[li][1] if spec.qkv_prefix else None, row_q=spec.row_q, q_len=spec.q_len,
@@ -284,8 +300,14 @@ class Backbone:
         cfg, dev = self.cfg, self.device
         mk = lambda: Int8Tensor(torch.empty(S, cfg.kv_heads, T, cfg.head_dim, dtype=torch.int8, device=dev),
                                 torch.empty(S, cfg.kv_heads, T, dtype=cfg.dtype, device=dev), cfg.dtype)
-        return KVCache([mk() for _ in range(cfg.layers)], [mk() for _ in range(cfg.layers)],
-                       torch.zeros(S, dtype=torch.int32, device=dev), T)
+        cache = KVCache([mk() for _ in range(cfg.layers)], [mk() for _ in range(cfg.layers)],
+                        torch.zeros(S, dtype=torch.int32, device=dev), T)
+        bf16_bytes = 2 * cfg.layers * S * cfg.kv_heads * T * cfg.head_dim * 2
+        if cfg.dtype == torch.bfloat16 and 0 < bf16_bytes <= self.materialize_budget:
+            mb = lambda: torch.empty(S, cfg.kv_heads, T, cfg.head_dim, dtype=torch.bfloat16, device=dev)
+            cache.kb = [mb() for _ in range(cfg.layers)]
+            cache.vb = [mb() for _ in range(cfg.layers)]
+        return cache
 
     def plan_state(self, seqs, up=None) -> dict:
         """Host layout of the batched state pass (Backbone.prefix_cache_batch, backbone.py:347-368): states LEFT-padded

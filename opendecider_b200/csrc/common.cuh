@@ -128,6 +128,23 @@ __device__ __forceinline__ uint32_t babsmax4(const uint4& w, uint32_t acc) {
   return babsmax2(acc, babsmax2(babsmax2(w.x, w.y), babsmax2(w.z, w.w)));
 }
 
+// Four int8 (one 32-bit word) -> two bf16 pairs of RN(x * s), s a bf16 pair; equal to rounding float(x) * s to bf16,
+// since the product of two 8-bit significands is exact. Integer path without the conversion pipe: the byte
+// (x ^ 0x80) = x + 128 placed under the exponent of 2^23 gives the float 2^23 + x + 128 exactly; subtracting
+// 2^23 + 128 leaves x, whose upper 16 bits are its exact bf16 (|x| <= 128 has at most 8 significant bits).
+__device__ __forceinline__ void dequant4_bf16(uint32_t w, uint32_t s2, uint32_t& lo, uint32_t& hi) {
+  const uint32_t u = w ^ 0x80808080u;
+  const float2 off = make_float2(-8388736.f, -8388736.f);
+  const float2 f01 = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7650)),
+                                            __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7651))), off);
+  const float2 f23 = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7652)),
+                                            __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7653))), off);
+  const uint32_t x01 = __byte_perm(__float_as_uint(f01.x), __float_as_uint(f01.y), 0x7632);
+  const uint32_t x23 = __byte_perm(__float_as_uint(f23.x), __float_as_uint(f23.y), 0x7632);
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(lo) : "r"(x01), "r"(s2));
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(hi) : "r"(x23), "r"(s2));
+}
+
 // Eight quantised values of a row (quant_int's rounding, two pairs at a time), packed little-endian in two words.
 // The byte of round(y) is the low byte of the bits of y + 1.5 * 2^23. No clamp: every element x of the row whose
 // absmax gave s has |x / s| <= 127 * (1 + 2^-23), which rounds into [-127, 127].

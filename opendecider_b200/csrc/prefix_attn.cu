@@ -69,7 +69,8 @@ struct Layout {
 
 struct Params {
   CUtensorMap map_ko, map_vo, map_kq, map_vq;   // bf16 (rows, Hkv*D) views of own / question K and V, 64x128 boxes
-  CUtensorMap map_kp, map_vp;                   // int8 (S*Hkv*T, D) views of the state prefix, D x 128 boxes
+  CUtensorMap map_kp, map_vp;                   // (S*Hkv*T, D) views of the state prefix: int8 with D x 128 boxes,
+                                                // or bf16 (materialised) with 64x128 boxes in the UMMA swizzle
   const __nv_bfloat16* q;
   const int8_t* Kp;
   const int8_t* Vp;
@@ -93,6 +94,7 @@ struct Params {
   int32_t* err;
   int64_t t, T, Lq;
   int Hq, Hkv, rep, tiles_per_group;
+  int prefix_bf16;
   float scale_log2;
 };
 
@@ -118,23 +120,6 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);
-}
-
-// Four int8 (one 32-bit word) -> two bf16 pairs of RN(x * s), s a bf16 pair; equal to rounding float(x) * s to bf16,
-// since the product of two 8-bit significands is exact. Integer path without the conversion pipe: the byte
-// (x ^ 0x80) = x + 128 placed under the exponent of 2^23 gives the float 2^23 + x + 128 exactly; subtracting
-// 2^23 + 128 leaves x, whose upper 16 bits are its exact bf16 (|x| <= 128 has at most 8 significant bits).
-__device__ __forceinline__ void dequant4_bf16(uint32_t w, uint32_t s2, uint32_t& lo, uint32_t& hi) {
-  const uint32_t u = w ^ 0x80808080u;
-  const float2 off = make_float2(-8388736.f, -8388736.f);
-  const float2 f01 = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7650)),
-                                            __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7651))), off);
-  const float2 f23 = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7652)),
-                                            __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7653))), off);
-  const uint32_t x01 = __byte_perm(__float_as_uint(f01.x), __float_as_uint(f01.y), 0x7632);
-  const uint32_t x23 = __byte_perm(__float_as_uint(f23.x), __float_as_uint(f23.y), 0x7632);
-  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(lo) : "r"(x01), "r"(s2));
-  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(hi) : "r"(x23), "r"(s2));
 }
 
 // A producer thread's share of an int8 block: chunks c = pt + it * kProducers (16 bytes each, key c / (D / 16)).
@@ -313,12 +298,14 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
     if (P.Kp) {
       const int64_t base = (static_cast<int64_t>(st) * P.Hkv + g) * P.T;
       prow = static_cast<int>(base);
-      ks1 = static_cast<const TS*>(P.ksc) + base;
-      vs1 = static_cast<const TS*>(P.vsc) + base;
+      if (!P.prefix_bf16) {
+        ks1 = static_cast<const TS*>(P.ksc) + base;
+        vs1 = static_cast<const TS*>(P.vsc) + base;
+      }
       pm1 = P.pmask ? P.pmask + static_cast<int64_t>(st) * P.T : nullptr;
     }
     uint32_t skc[Piece<D>::N], svc[Piece<D>::N];     // scales of the next int8 K / V piece to convert
-    if (nb1 > 0) {
+    if (nb1 > 0 && !P.prefix_bf16) {
       load_scales<D>(skc, pt, ks1, lo1, hi1);
       load_scales<D>(svc, pt, vs1, lo1, hi1);
       if (pt == 0) {
@@ -329,9 +316,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
       }
     }
     for (int j = 0; j < nblk; ++j) {
-      const bool i8 = j < nb1;
-      const bool q_seg = !i8 && j < nb1 + nb2;
-      const int k0 = i8 ? lo1 + j * BN : q_seg ? (j - nb1) * BN : own_begin + (j - nb1 - nb2) * BN;
+      const bool pre = j < nb1;                       // state prefix block
+      const bool i8 = pre && !P.prefix_bf16;          // ... dequantised here
+      const bool q_seg = !pre && j < nb1 + nb2;
+      const int k0 = pre ? lo1 + j * BN : q_seg ? (j - nb1) * BN : own_begin + (j - nb1 - nb2) * BN;
       // ---- K_j and the block's visibility bits (a mask slot is reused 4 blocks later: by then this producer has
       // passed the V stage wait of block j+3, which follows the softmax of block j+1)
       const int bk = j % KS;
@@ -339,7 +327,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
       bool vis;
       {
         const int idx = k0 + pt;
-        if (i8) {
+        if (pre) {
           vis = idx < hi1 && (!pm1 || pm1[idx]);
         } else if (q_seg) {
           vis = idx < n2;
@@ -370,11 +358,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
         fence_proxy_async_smem();
         mbar_arrive(&kfull[bk]);
       } else if (pt == 0) {
-        const CUtensorMap* mk = q_seg ? &P.map_kq : &P.map_ko;
-        const int y = (q_seg ? qr * static_cast<int>(P.Lq) : row0 * t) + k0;
+        const CUtensorMap* mk = pre ? &P.map_kp : q_seg ? &P.map_kq : &P.map_ko;
+        const int y = pre ? prow + k0 : (q_seg ? qr * static_cast<int>(P.Lq) : row0 * t) + k0;
+        const int x0 = pre ? 0 : g * D;
         mbar_arrive_expect_tx(&kfull[bk], L::TILE);
 #pragma unroll
-        for (int h = 0; h < D / 64; ++h) tma_load_2d(sK + h * L::ATOM, mk, &kfull[bk], g * D + h * 64, y);
+        for (int h = 0; h < D / 64; ++h) tma_load_2d(sK + h * L::ATOM, mk, &kfull[bk], x0 + h * 64, y);
       } else {
         mbar_arrive(&kfull[bk]);
       }
@@ -397,11 +386,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
         fence_proxy_async_smem();
         mbar_arrive(&vfull[bv]);
       } else if (pt == 0) {
-        const CUtensorMap* mv = q_seg ? &P.map_vq : &P.map_vo;
-        const int y = (q_seg ? qr * static_cast<int>(P.Lq) : row0 * t) + k0;
+        const CUtensorMap* mv = pre ? &P.map_vp : q_seg ? &P.map_vq : &P.map_vo;
+        const int y = pre ? prow + k0 : (q_seg ? qr * static_cast<int>(P.Lq) : row0 * t) + k0;
+        const int x0 = pre ? 0 : g * D;
         mbar_arrive_expect_tx(&vfull[bv], L::TILE);
 #pragma unroll
-        for (int h = 0; h < D / 64; ++h) tma_load_2d(sV + h * L::ATOM, mv, &vfull[bv], g * D + h * 64, y);
+        for (int h = 0; h < D / 64; ++h) tma_load_2d(sV + h * L::ATOM, mv, &vfull[bv], x0 + h * 64, y);
       } else {
         mbar_arrive(&vfull[bv]);
       }
@@ -682,7 +672,7 @@ int launch_attn(const Params& P, dim3 grid, cudaStream_t st) {
 
 using namespace od;
 
-extern "C" int od_prefix_attn(const void* q, const int8_t* Kp, const int8_t* Vp, const void* ksc, const void* vsc,
+extern "C" int od_prefix_attn(const void* q, const void* Kp, const void* Vp, const void* ksc, const void* vsc,
                               const int32_t* row_state, const int32_t* p_lo, const int32_t* p_hi, const uint8_t* pmask,
                               const void* Kq, const void* Vq, const int32_t* row_q, const int32_t* q_len,
                               const void* k_own, const void* v_own, const int32_t* own_lo, const int32_t* own_hi,
@@ -692,9 +682,10 @@ extern "C" int od_prefix_attn(const void* q, const int8_t* Kp, const int8_t* Vp,
   OD_REQUIRE(dims.Hq > 0 && dims.Hkv > 0 && dims.Hq % dims.Hkv == 0, "od_prefix_attn: bad head counts");
   const int rep = dims.Hq / dims.Hkv;
   OD_REQUIRE(dims.R >= 0 && dims.t >= 0 && dims.t < (1 << 24), "od_prefix_attn: bad R/t");
-  OD_REQUIRE(!Kp || (Vp && ksc && vsc && row_state && dims.S > 0 && dims.T > 0 && dims.T < (1 << 30)),
-             "od_prefix_attn: the int8 prefix needs Vp, scales, row_state, S, T");
-  OD_REQUIRE(!Kp || dims.scale_dtype == OD_BF16 || dims.scale_dtype == OD_F16, "od_prefix_attn: scale dtype");
+  const bool pbf16 = dims.prefix_bf16 != 0;
+  OD_REQUIRE(!Kp || (Vp && (pbf16 || (ksc && vsc)) && row_state && dims.S > 0 && dims.T > 0 && dims.T < (1 << 30)),
+             "od_prefix_attn: the state prefix needs Vp, row_state, S, T (and ksc/vsc when int8)");
+  OD_REQUIRE(!Kp || pbf16 || dims.scale_dtype == OD_BF16 || dims.scale_dtype == OD_F16, "od_prefix_attn: scale dtype");
   OD_REQUIRE(!Kq || (Vq && row_q && q_len && dims.NQ > 0 && dims.Lq > 0), "od_prefix_attn: bad question prefix");
   OD_REQUIRE(aligned16(q) && aligned16(k_own) && aligned16(v_own) && aligned16(o) &&
                  (!Kp || (aligned16(Kp) && aligned16(Vp))) && (!Kq || (aligned16(Kq) && aligned16(Vq))),
@@ -711,8 +702,9 @@ extern "C" int od_prefix_attn(const void* q, const int8_t* Kp, const int8_t* Vp,
   Params P;
   memset(&P, 0, sizeof(P));
   P.q = static_cast<const __nv_bfloat16*>(q);
-  P.Kp = Kp;
-  P.Vp = Vp;
+  P.Kp = static_cast<const int8_t*>(Kp);
+  P.Vp = static_cast<const int8_t*>(Vp);
+  P.prefix_bf16 = pbf16 ? 1 : 0;
   P.ksc = ksc;
   P.vsc = vsc;
   P.row_state = row_state;
@@ -753,8 +745,13 @@ extern "C" int od_prefix_attn(const void* q, const int8_t* Kp, const int8_t* Vp,
     if (!rc && Kp) {
       const uint64_t prows = static_cast<uint64_t>(dims.S) * dims.Hkv * dims.T;
       OD_REQUIRE(prows < (1ULL << 31), "od_prefix_attn: S * Hkv * T must be below 2^31");
-      rc = make_map_i8(&P.map_kp, Kp, static_cast<uint64_t>(dims.D), prows);
-      if (!rc) rc = make_map_i8(&P.map_vp, Vp, static_cast<uint64_t>(dims.D), prows);
+      if (pbf16) {
+        rc = make_map_bf16(&P.map_kp, Kp, static_cast<uint64_t>(dims.D), prows);
+        if (!rc) rc = make_map_bf16(&P.map_vp, Vp, static_cast<uint64_t>(dims.D), prows);
+      } else {
+        rc = make_map_i8(&P.map_kp, Kp, static_cast<uint64_t>(dims.D), prows);
+        if (!rc) rc = make_map_i8(&P.map_vp, Vp, static_cast<uint64_t>(dims.D), prows);
+      }
     }
     if (rc) return rc;
   }
@@ -762,7 +759,7 @@ extern "C" int od_prefix_attn(const void* q, const int8_t* Kp, const int8_t* Vp,
   OD_REQUIRE(gx < (1LL << 31) && dims.Hkv < 65536, "od_prefix_attn: grid too large");
   dim3 grid(static_cast<unsigned>(gx), dims.Hkv);
   cudaStream_t st = as_stream(stream);
-  const bool half_scale = Kp && dims.scale_dtype == OD_F16;
+  const bool half_scale = Kp && !pbf16 && dims.scale_dtype == OD_F16;
   if (dims.D == 128) {
     if (half_scale) return launch_attn<__half, 128>(P, grid, st);
     return launch_attn<__nv_bfloat16, 128>(P, grid, st);

@@ -197,6 +197,25 @@ __global__ void dequant_rows_kernel(const int8_t* __restrict__ q, const void* sc
   }
 }
 
+// bf16 output with bf16 scales and rows of a multiple of 16: one 16-byte int8 chunk per thread and step, the exact
+// integer-path conversion (RN(q * s) in bf16, as the scalar kernel rounds); 32-bit chunk indices.
+__global__ void dequant_rows_bf16_kernel(const int8_t* __restrict__ q, const uint16_t* __restrict__ scale, uint32_t K16,
+                                         uint32_t n, __nv_bfloat16* __restrict__ y) {
+  for (uint32_t c = blockIdx.x * blockDim.x + threadIdx.x; c < n; c += gridDim.x * blockDim.x) {
+    const uint32_t sb = __ldg(scale + c / K16);
+    const uint32_t s2 = sb | (sb << 16);
+    const uint4 w = __ldg(reinterpret_cast<const uint4*>(q) + c);
+    uint32_t o[8];
+    dequant4_bf16(w.x, s2, o[0], o[1]);
+    dequant4_bf16(w.y, s2, o[2], o[3]);
+    dequant4_bf16(w.z, s2, o[4], o[5]);
+    dequant4_bf16(w.w, s2, o[6], o[7]);
+    uint4* dst = reinterpret_cast<uint4*>(y) + 2 * static_cast<uint64_t>(c);
+    dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+    dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+  }
+}
+
 // ---------------------------------------------------------------------------------------------- KV append
 // One warp per (state, new token, head) row of D elements; EPL = D / 32 contiguous elements per lane. The grid's y
 // index is the state, x covers the (token, head) rows of one state (32-bit index arithmetic).
@@ -477,6 +496,16 @@ extern "C" int od_dequant_rows_i8(const int8_t* q, const void* scale, int scale_
   if (M == 0) return ok();
   cudaStream_t st = as_stream(stream);
   const int64_t n = M * K;
+  if (out_dtype == OD_BF16 && scale_dtype == OD_BF16 && K % 16 == 0 && n / 16 < (1LL << 32) - 65536 && aligned16(q) &&
+      aligned16(y)) {
+    const int64_t n16 = n / 16;
+    const unsigned blocks = static_cast<unsigned>(n16 / 256 + 1 < 148 * 16 ? n16 / 256 + 1 : 148 * 16);
+    dequant_rows_bf16_kernel<<<blocks, 256, 0, st>>>(q, static_cast<const uint16_t*>(scale),
+                                                     static_cast<uint32_t>(K / 16), static_cast<uint32_t>(n16),
+                                                     static_cast<__nv_bfloat16*>(y));
+    OD_LAUNCH_CHECK();
+    return ok();
+  }
   const int blocks = static_cast<int>(n / 256 + 1 < 148 * 32 ? n / 256 + 1 : 148 * 32);
   switch (out_dtype) {
     case OD_BF16: dequant_rows_kernel<<<blocks, 256, 0, st>>>(q, scale, scale_dtype, M, K, static_cast<__nv_bfloat16*>(y)); break;

@@ -80,3 +80,14 @@ def test_batch_invariance(cuda):
     ans = dec.decide_many(reqs)
     one = dec.decide_many(reqs[1:2])
     assert np.abs(np.array(ans[1]["q0"]["probs_list"]) - np.array(one[0]["q0"]["probs_list"])).max() < 1e-3
+
+
+def test_materialised_cache_same_decisions(cuda):
+    """The state pass's bf16 materialisation of the int8 cache (taken when it fits the memory budget) changes no
+    decision: probabilities equal those of the int8 cache dequantised inside attention, bit for bit."""
+    dec, reqs = make_decider(cuda, True)
+    assert dec.model.backbone.materialize_budget > 0
+    p_mat, n_mat = _collect(dec.decide_many(reqs))
+    dec.model.backbone.materialize_budget = 0
+    p_i8, n_i8 = _collect(dec.decide_many(reqs))
+    assert np.array_equal(p_mat, p_i8) and np.array_equal(n_mat, n_i8)

@@ -407,3 +407,53 @@ def test_prefix_attn_int8_dequant_exact(cuda):
         want = deq[s, :, int(p_lo[s]), :].repeat_interleave(rep, 0)           # (Hq, D)
         for i in range(t):
             assert torch.equal(o[r, i].view(torch.int16), want.view(torch.int16)), (r, i)
+
+
+def test_dequant_rows_bf16_exact(cuda):
+    """Int8Tensor.dequantize (quant.py:43-45) into bf16 with bf16 per-row scales (the KV-cache materialisation):
+    every int8 value, scales over 40 binades, bit for bit against bf16(fp32(q) * fp32(s))."""
+    g = torch.Generator().manual_seed(41)
+    M, K = 1000, 128
+    q = torch.randint(-128, 128, (M, K), generator=g, dtype=torch.int8)
+    s = (torch.rand(M, 1, generator=g) * torch.pow(2.0, torch.randint(-30, 10, (M, 1), generator=g).float()))
+    s = s.to(torch.bfloat16)
+    y = _lib.dequant_rows(q.to(cuda), s.to(cuda), torch.bfloat16).cpu()
+    ref = (q.float() * s.float()).to(torch.bfloat16)
+    assert torch.equal(y.view(torch.int16), ref.view(torch.int16))
+
+
+def test_prefix_attn_materialised_prefix_identical(cuda):
+    """The state prefix given as the materialised bf16 cache (dequant_rows of the int8 cache, prefix_attn.py:146-149)
+    produces bit-identical outputs and LSE to the int8 prefix dequantised inside the kernel: left pads, a hole,
+    a question level and row groups."""
+    g = syn.gen(57)
+    S, T, Hq, Hkv, D, t = 2, 300, 32, 8, 128, 6
+    ac = syn.attn_case(S=S, T=T, rows=4, t=t, Hq=Hq, Hkv=Hkv, D=D, seed=57)
+    Kq, Vq, ks, vs = _attn_inputs(cuda, ac)
+    ks, vs = ks.to(torch.bfloat16), vs.to(torch.bfloat16)           # the backbone's cache: bf16 scales
+    Kb = _lib.dequant_rows(Kq.view(-1, D), ks.reshape(-1, 1), torch.bfloat16).view(Kq.shape)
+    Vb = _lib.dequant_rows(Vq.view(-1, D), vs.reshape(-1, 1), torch.bfloat16).view(Vq.shape)
+    pmask = torch.ones(S, T, dtype=torch.uint8)
+    pmask[1, 40:77] = 0
+    NQ, Lq = 2, 30
+    Kqn = torch.randn(NQ, Lq, Hkv, D, generator=g).to(torch.bfloat16).to(cuda)
+    Vqn = torch.randn(NQ, Lq, Hkv, D, generator=g).to(torch.bfloat16).to(cuda)
+    R = ac.q.shape[0]
+    row_q = torch.tensor([r % 2 for r in range(R)], dtype=torch.int32)
+    order = torch.argsort(row_q * 16 + ac.row_state, stable=True)        # groups need shared state and question
+    q, k, v = ac.q[order].to(cuda), ac.k[order].to(cuda), ac.v[order].to(cuda)
+    rs, rq = ac.row_state[order].to(cuda), row_q[order].to(cuda)
+    groups, i = [], 0
+    while i < R:
+        j = i
+        while j < R and j - i < 2 and rs[j] == rs[i] and rq[j] == rq[i]:
+            j += 1
+        groups.append((i, j - i))
+        i = j
+    common = dict(row_state=rs, p_lo=torch.tensor([0, 9], dtype=torch.int32, device=cuda), pmask=pmask.to(cuda),
+                  Kq=Kqn, Vq=Vqn, row_q=rq, q_len=torch.tensor([30, 11], dtype=torch.int32, device=cuda),
+                  row_groups=torch.tensor(groups, dtype=torch.int32, device=cuda), max_group_rows=2, want_lse=True)
+    o8, l8 = _lib.prefix_attn(q, k, v, D ** -0.5, Kp=Kq, Vp=Vq, ksc=ks, vsc=vs, **common)
+    ob, lb = _lib.prefix_attn(q, k, v, D ** -0.5, Kp=Kb, Vp=Vb, **common)
+    assert torch.equal(o8, ob)
+    assert torch.equal(l8, lb)
