@@ -12,8 +12,9 @@ decision forward of that batch (state pass, question-cache row passes, trunk, re
 N GPUs run N batches (weak scaling) and gather the probabilities over NCCL.
 
 Printed: one JSON line on rank 0. `value` = decisions/s over all GPUs with the batch's inputs resident in HBM
-(device time, CUDA events, max over ranks); `e2e` = the same metric through the public API Decider.decide_many
-(tokenisation, one pinned host->device copy, kernels, the device->host read of the answers); `roofline` = the W8A8
+(device time, CUDA events, max over ranks); `e2e` = the same metric through the public API Decider.decide_stream
+(one batch per step: tokenisation, one pinned host->device copy, kernels, the device->host read of the answers, the
+next batch planned while the previous one runs); `roofline` = the W8A8
 GEMM (the dominant kernel) timed per launch with CUDA events inside the timed region; `cpu_baseline` = the CPU oracle
 of the same path (oracle/model.py) on a bounded sample, extrapolated.
 """
@@ -399,28 +400,25 @@ def main():
             print(f"breakdown {k:20s} launches {n:5d}  {ms:9.2f} ms  {100 * ms / tot:5.1f} %", file=sys.stderr)
         print(f"breakdown step {tot:.2f} ms, kernels {sum(v[1] for v in summ.values()):.2f} ms", file=sys.stderr)
 
-    # ---- e2e: the public API per step (tokenise, plan, one pinned H2D copy, kernels, gather, D2H answers)
-    for _ in range(1):
-        ans = decider.decide_many(reqs)
+    # ---- e2e: the public API, one batch per step (Decider.decide_stream: tokenise + plan on the host, one pinned
+    # H2D copy, kernels, the gather, one D2H read of the results, answers), batch b+1 planned while b runs
+    g_fn = gather if world > 1 else None
+    for _ in decider.decide_stream([reqs], gather=g_fn):
+        pass
     torch.cuda.synchronize()
     barrier()
-    h2d = d2h = 0
+    h2d, d2h = decider.last_io["h2d_bytes"], decider.last_io["d2h_bytes"]
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     f0.record()
-    for _ in range(args.steps):
-        p = decider.plan(reqs)
-        pr, _ = decider.execute(p)
-        g = gather(pr)
-        ans = decider.answers(p, pr)
-        if world > 1:
-            g.cpu()
-        h2d = p["h2d_bytes"]
-        d2h = sum(t.numel() * t.element_size() for t in pr) + (g.numel() * g.element_size() if world > 1 else 0)
+    n_ans = 0
+    for ans, _ in decider.decide_stream((reqs for _ in range(args.steps)), gather=g_fn):
+        assert len(ans) == len(reqs)
+        n_ans += 1
     f1.record()
     torch.cuda.synchronize()
     barrier()
     t_e2e = max_over_ranks(f0.elapsed_time(f1) / 1e3)
-    assert len(ans) == len(reqs)
+    assert n_ans == args.steps
 
     if world > 1:
         dist.destroy_process_group()

@@ -143,3 +143,31 @@ class Decider:
         plan = self.plan(requests)
         probs, _ = self.execute(plan)
         return self.answers(plan, probs)
+
+    def decide_stream(self, batches, gather=None):
+        """decide_many over a sequence of request batches, pipelined: the read-back of batch b's results is enqueued
+        right after its kernels, batch b+1 is planned on the host and its device work enqueued, and only then are
+        b's results awaited, so the GPU runs batch after batch without waiting for the host. `gather(probs)`
+        (optional) runs on the device after a batch's kernels, in stream order (e.g. the data-parallel all-gather of
+        the probabilities), and its result is read back with the answers. Yields (answers, gathered or None) per
+        batch, in order. The KV cache allocation is reused from batch to batch."""
+        pending, cache = None, None
+        for requests in batches:
+            plan = self.plan(requests)
+            probs, cache = self.execute(plan, cache)
+            dev = list(probs) + ([gather(probs)] if gather is not None else [])
+            host = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in dev]
+            for h, d in zip(host, dev):
+                h.copy_(d, non_blocking=True)
+            done = torch.cuda.Event()
+            done.record(torch.cuda.current_stream(self.model.backbone.device))
+            self.last_io = {"h2d_bytes": plan["h2d_bytes"], "d2h_bytes": sum(h.numel() * h.element_size() for h in host)}
+            if pending is not None:
+                yield self._finish(*pending)
+            pending = (plan, host, done, gather is not None)
+        if pending is not None:
+            yield self._finish(*pending)
+
+    def _finish(self, plan: dict, host: list, done, gathered: bool):
+        done.synchronize()
+        return self.answers(plan, host[:3]), (host[3] if gathered else None)

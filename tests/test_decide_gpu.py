@@ -91,3 +91,15 @@ def test_materialised_cache_same_decisions(cuda):
     dec.model.backbone.materialize_budget = 0
     p_i8, n_i8 = _collect(dec.decide_many(reqs))
     assert np.array_equal(p_mat, p_i8) and np.array_equal(n_mat, n_i8)
+
+
+def test_decide_stream_equals_decide_many(cuda):
+    """The pipelined stream (batch b+1 planned and enqueued before b's results are read) answers every batch exactly
+    as decide_many does, in order, with batches of different sizes sharing the stream."""
+    dec, reqs = make_decider(cuda, True)
+    batches = [reqs, reqs[:2], reqs[1:], reqs]
+    want = [_collect(dec.decide_many(b)) for b in batches]
+    got = [_collect(a) for a, g in dec.decide_stream(batches)]
+    assert len(got) == len(want)
+    for (pw, nw), (pg, ng) in zip(want, got):
+        assert np.array_equal(pw, pg) and np.array_equal(nw, ng)
