@@ -12,12 +12,14 @@
 //                        keys arrive by TMA directly; one visibility bit per key (padding, holes, segment ends)
 //                        goes to a 4-deep mask ring
 //   MMA warp (1 thread)  S_{j+1} = Q K_{j+1}^T into the other half of a double-buffered S in TMEM while the softmax
-//                        works on S_j, then O += P_j V_j with P read from TMEM (A operand) and V as an MN-major
-//                        shared-memory operand, O accumulating in TMEM
+//                        works on S_j, then O += P_j V_j; Q and P are A operands in TMEM (shared memory then only
+//                        streams K and V to the tensor core: its operand bandwidth is the limit), V is MN-major,
+//                        O accumulates in TMEM
 //   softmax warps (8)    warp w owns TMEM lane quarter w % 4 and keys [64 (w / 4), +64) of each block: causal and
 //                        same-row masks on own keys, the row max exchanged with the partner warp of the other key
 //                        half, online softmax in the exp2 domain with a lazy rescale of O only when the max grows
-//                        by more than 2^8, P (bf16) into TMEM; at the end O / l and the natural-log LSE
+//                        by more than 2^8, P (bf16) into TMEM; at the start each puts its slot's Q half-row into TMEM,
+//                        at the end O / l and the natural-log LSE
 // Every mbarrier wait is bounded; a time-out ends the kernel with an error code, never a hang.
 // Each slot's math does not depend on the other slots: outputs do not depend on row order.
 #include <cudaTypedefs.h>
@@ -40,22 +42,23 @@ constexpr int kProducers = 32 * kProducerWarps;
 constexpr int kThreads = 32 * (kSoftmaxWarps + 1 + kProducerWarps);
 constexpr int BM = 128;              // query slots per CTA
 constexpr int BN = 128;              // keys per block (one per producer thread)
-constexpr int KS = 2;                // K ring depth
+constexpr int KS = 3;                // K ring depth
 constexpr int VS = 2;                // V ring depth
 constexpr int MS = 4;                // mask ring depth (a block's bits are rewritten only after its softmax ended)
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemS = 0;       // S buffers at columns 0 and BN (BN fp32 each)
-constexpr uint32_t kTmemP = 2 * BN;  // P: BN / 2 columns of bf16 pairs
+constexpr uint32_t kTmemP = 2 * BN;  // P: BN / 2 columns of bf16 pairs (A operand of O += P V)
+constexpr uint32_t kTmemQ = 320;     // Q: D / 2 columns of bf16 pairs (A operand of S = Q K^T)
 constexpr uint32_t kTmemO = 384;     // O: D fp32 columns
+static_assert(kTmemP + BN / 2 <= kTmemQ && kTmemQ + 128 / 2 <= kTmemO, "TMEM columns overlap");
 constexpr int32_t kErrAttn = 0x5A0000;
 static_assert(BN == kProducers, "one key of a block per producer thread");
 
 template <int D>
 struct Layout {
   static constexpr int ATOM = 128 * 128;             // 128 rows x 128 B: one 64-column swizzle atom of a tile
-  static constexpr int TILE = ATOM * (D / 64);       // 128 rows x D bf16 (Q, a K block or a V block)
-  static constexpr int Q = 0;
-  static constexpr int K0 = Q + TILE;
+  static constexpr int TILE = ATOM * (D / 64);       // 128 rows x D bf16 (a K block or a V block)
+  static constexpr int K0 = 0;
   static constexpr int V0 = K0 + KS * TILE;
   static constexpr int RAWK = V0 + VS * TILE;        // int8 K / V block staging: BN rows x D bytes, row-major
   static constexpr int RAWV = RAWK + BN * D;
@@ -199,7 +202,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
   uint64_t* rawk_empty = rawk_full + 1;    // producers (raw K converted) -> the TMA-issuing producer
   uint64_t* rawv_full = rawk_full + 2;
   uint64_t* rawv_empty = rawk_full + 3;
-  uint64_t* drain = rawk_full + 4;
+  uint64_t* q_full = rawk_full + 4;        // softmax warps (Q in TMEM) -> MMA
+  uint64_t* drain = rawk_full + 5;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   uint32_t* masks = reinterpret_cast<uint32_t*>(sm + L::MASK0);
@@ -235,6 +239,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
     mbar_init(rawk_empty, kProducers);
     mbar_init(rawv_full, 1);
     mbar_init(rawv_empty, kProducers);
+    mbar_init(q_full, 32 * kSoftmaxWarps);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -273,24 +278,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
   const int nblk = nb1 + nb2 + nb3;
 
   if (warp > kMmaWarp) {
-    // ================================================================== producers: Q, then K/V blocks
+    // ================================================================== producers: K/V blocks
     const int pt = tid - kProducer0, pw = pt >> 5;
-    {
-      constexpr int CPR = D / 8;
-#pragma unroll 4
-      for (int c = pt; c < BM * CPR; c += kProducers) {
-        const int r = c / CPR, ch = c % CPR;
-        const int s = s0 + r;
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (s < slots) {
-          const int a = s / slots_row, i = (s % slots_row) / rep, hh = s % rep;
-          v = __ldg(reinterpret_cast<const uint4*>(
-                        P.q + ((static_cast<int64_t>(row0 + a) * t + i) * P.Hq + g * rep + hh) * D) + ch);
-        }
-        *reinterpret_cast<uint4*>(sm + L::Q + swz(r, ch, L::ATOM)) = v;
-      }
-      fence_proxy_async_smem();                       // Q is read by the first S MMA
-    }
     const TS* ks1 = nullptr;
     const TS* vs1 = nullptr;
     const uint8_t* pm1 = nullptr;
@@ -401,19 +390,17 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
     if (lane == 0 && nblk > 0) {
       constexpr uint32_t idesc_s = idesc_bf16(BM, BN, false);
       constexpr uint32_t idesc_o = idesc_bf16(BM, D, true);
-      const uint32_t sQ = smem_u32(sm + L::Q);
       auto issue_s = [&](int j) {
         const uint32_t sK = smem_u32(sm + L::K(j % KS));
 #pragma unroll
-        for (int kd = 0; kd < D / 16; ++kd) {
-          const uint32_t off = (kd >> 2) * L::ATOM + (kd & 3) * 32;
-          mma_f16(tmem + kTmemS + (j & 1) * BN, desc_sw128(sQ + off, 16, 1024), desc_sw128(sK + off, 16, 1024),
-                  idesc_s, kd > 0 ? 1u : 0u);
-        }
+        for (int kd = 0; kd < D / 16; ++kd)
+          mma_f16_ts(tmem + kTmemS + (j & 1) * BN, tmem + kTmemQ + kd * 8,
+                     desc_sw128(sK + (kd >> 2) * L::ATOM + (kd & 3) * 32, 16, 1024), idesc_s, kd > 0 ? 1u : 0u);
         mma_commit(&s_full[j & 1]);
         mma_commit(&kempty[j % KS]);
       };
-      bool live = mbar_wait(&kfull[0], 0, abort_flag, P.err, kErrAttn | 3);
+      bool live = mbar_wait(q_full, 0, abort_flag, P.err, kErrAttn | 17) &&
+                  mbar_wait(&kfull[0], 0, abort_flag, P.err, kErrAttn | 3);
       if (live) {
         tc_fence_after();
         issue_s(0);
@@ -454,6 +441,34 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
     const int hh_my = slot % rep;
     const uint32_t lane_off = static_cast<uint32_t>(32 * q4) << 16;
     const float scale = P.scale_log2;
+    {
+      // this slot's Q, the warp's half of the head dimension (D / 4 bf16 pairs), into TMEM lane tt
+      constexpr int NW = D / 4;
+      uint32_t qw[NW];
+      if (my_valid) {
+        const uint4* src = reinterpret_cast<const uint4*>(
+            P.q + ((static_cast<int64_t>(row0 + a_my) * t + i_my) * P.Hq + g * rep + hh_my) * D + h * (D / 2));
+#pragma unroll
+        for (int k = 0; k < NW / 4; ++k) {
+          const uint4 v = __ldg(src + k);
+          qw[4 * k] = v.x;
+          qw[4 * k + 1] = v.y;
+          qw[4 * k + 2] = v.z;
+          qw[4 * k + 3] = v.w;
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < NW; ++k) qw[k] = 0u;
+      }
+      if constexpr (NW == 32) {
+        tmem_st_32x32b_x32(tmem + lane_off + kTmemQ + h * NW, qw);
+      } else {
+        tmem_st_32x32b_x16(tmem + lane_off + kTmemQ + h * NW, qw);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(q_full);
+    }
     float m_used = -INFINITY, l_part = 0.f;
     bool live = true;
     for (int j = 0; j < nblk; ++j) {
