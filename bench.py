@@ -227,6 +227,7 @@ def op_gemm(args):
             if i >= args.warmup:
                 ts.append(a.elapsed_time(b))
                 tc.append(c.elapsed_time(d))
+        assert _lib.device_error(dev) == 0, "a kernel reported a device-side error (a bounded wait ran out)"
         t = statistics.median(ts) / 1e3
         ops = 2.0 * M * N * K
         byts = M * K + N * K + 2 * M * N + 4 * M + 2 * N

@@ -53,6 +53,66 @@ __device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* src, float (&v
   }
 }
 
+// Epilogue of one 128 x 256 accumulator in TMEM (tbase: this warp's lane quarter): this thread's output row m,
+// columns n0 .. n0 + 255 (SwiGLU: outputs tile_n * 128 .. + 127).
+template <int EPI>
+__device__ __forceinline__ void epilogue_tile(uint32_t tbase, int m, bool valid, int n0, int tile_n,
+                                              const float* __restrict__ sa, const __nv_bfloat16* __restrict__ sw,
+                                              void* __restrict__ Y, int N) {
+  const float sam = valid ? sa[m] : 0.f;
+  if constexpr (EPI == OD_EPI_INT32) {
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(tbase + c * 32, r);
+      tmem_ld_wait();
+      if (valid) {
+        uint4* dst = reinterpret_cast<uint4*>(static_cast<int32_t*>(Y) + static_cast<int64_t>(m) * N + n0 + c * 32);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) dst[i] = make_uint4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
+      }
+    }
+  } else if constexpr (EPI == OD_EPI_BF16) {
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(tbase + c * 32, r);
+      tmem_ld_wait();
+      if (valid) {
+        float w[32], y[32];
+        load_bf16x32(sw + n0 + c * 32, w);
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          y[j] = __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(r[j])), sam), w[j]);
+        store_bf16x32(static_cast<__nv_bfloat16*>(Y) + static_cast<int64_t>(m) * N + n0 + c * 32, y);
+      }
+    }
+  } else {  // OD_EPI_SWIGLU: columns [0,128) gate, [128,256) up of the same 128 outputs
+    const int ldy = N / 2;
+    const int j0 = tile_n * (BN / 2);
+#pragma unroll 1
+    for (int c = 0; c < BN / 64; ++c) {
+      uint32_t rg[32], ru[32];
+      tmem_ld_32x32b_x32(tbase + c * 32, rg);
+      tmem_ld_32x32b_x32(tbase + BN / 2 + c * 32, ru);
+      tmem_ld_wait();
+      if (valid) {
+        float wg[32], wu[32], y[32];
+        load_bf16x32(sw + n0 + c * 32, wg);
+        load_bf16x32(sw + n0 + BN / 2 + c * 32, wu);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float g = rbf(__fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(rg[j])), sam), wg[j]));
+          const float u = rbf(__fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(ru[j])), sam), wu[j]));
+          const float a = rbf(__fdiv_rn(g, 1.0f + expf(-g)));  // SiLU in fp32, stored as bf16
+          y[j] = __fmul_rn(a, u);
+        }
+        store_bf16x32(static_cast<__nv_bfloat16*>(Y) + static_cast<int64_t>(m) * ldy + j0 + c * 32, y);
+      }
+    }
+  }
+}
+
 template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -188,59 +248,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int m = (tile / num_n) * BM + row;
       const int n0 = (tile % num_n) * BN;
       const bool valid = m < M;
-      const float sam = valid ? sa[m] : 0.f;
-      const uint32_t tbase = tmem_base + acc * BN + (static_cast<uint32_t>(quarter * 32) << 16);
-      if constexpr (EPI == OD_EPI_INT32) {
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(tbase + c * 32, r);
-          tmem_ld_wait();
-          if (valid) {
-            uint4* dst = reinterpret_cast<uint4*>(static_cast<int32_t*>(Y) + static_cast<int64_t>(m) * N + n0 + c * 32);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) dst[i] = make_uint4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
-          }
-        }
-      } else if constexpr (EPI == OD_EPI_BF16) {
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(tbase + c * 32, r);
-          tmem_ld_wait();
-          if (valid) {
-            float w[32], y[32];
-            load_bf16x32(sw + n0 + c * 32, w);
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              y[j] = __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(r[j])), sam), w[j]);
-            store_bf16x32(static_cast<__nv_bfloat16*>(Y) + static_cast<int64_t>(m) * N + n0 + c * 32, y);
-          }
-        }
-      } else {  // OD_EPI_SWIGLU: columns [0,128) gate, [128,256) up of the same 128 outputs
-        const int ldy = N / 2;
-        const int j0 = (tile % num_n) * (BN / 2);
-#pragma unroll 1
-        for (int c = 0; c < BN / 64; ++c) {
-          uint32_t rg[32], ru[32];
-          tmem_ld_32x32b_x32(tbase + c * 32, rg);
-          tmem_ld_32x32b_x32(tbase + BN / 2 + c * 32, ru);
-          tmem_ld_wait();
-          if (valid) {
-            float wg[32], wu[32], y[32];
-            load_bf16x32(sw + n0 + c * 32, wg);
-            load_bf16x32(sw + n0 + BN / 2 + c * 32, wu);
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const float g = rbf(__fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(rg[j])), sam), wg[j]));
-              const float u = rbf(__fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(ru[j])), sam), wu[j]));
-              const float a = rbf(__fdiv_rn(g, 1.0f + expf(-g)));  // SiLU in fp32, stored as bf16
-              y[j] = __fmul_rn(a, u);
-            }
-            store_bf16x32(static_cast<__nv_bfloat16*>(Y) + static_cast<int64_t>(m) * ldy + j0 + c * 32, y);
-          }
-        }
-      }
+      epilogue_tile<EPI>(tmem_base + acc * BN + (static_cast<uint32_t>(quarter * 32) << 16), m, valid, n0,
+                         tile % num_n, sa, sw, Y, N);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -251,6 +260,185 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+
+// ------------------------------------------------------------------------------------------------ CTA-pair form
+// Large M: a cluster of two CTAs computes a 256 x 256 tile with tcgen05.mma.cta_group::2 (M = 256). Each CTA stages
+// 128 rows of A and 128 rows of W per k-block (32 KB per stage instead of 48 KB for a 128 x 256 tile: the shared-
+// memory operand traffic per MAC, which bounds the single-CTA form, drops by a third) and holds 128 rows x 256
+// columns of the accumulator in its own TMEM. Both CTAs' loads of a stage complete on the even CTA's stage barrier,
+// which the even CTA arms for both CTAs' bytes (a remote arrival per stage from the odd CTA would serialise its
+// loads); its single thread issues the pair's MMAs and multicasts its
+// commits (stage free, accumulator full) to both CTAs; the epilogue warps of both CTAs release an accumulator on the
+// even CTA's barrier. Barriers that complete through the other CTA are polled without a suspend hint. After a
+// time-out the even CTA completes and waits for every stage phase either CTA armed, so no load is in flight when the
+// pair leaves (the final cluster barrier holds the odd CTA until then).
+constexpr int P_STAGES = 6;
+constexpr int P_A_BYTES = 128 * BK, P_B_BYTES = 128 * BK, P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;
+constexpr int kPairSmemBytes = P_STAGES * P_STAGE_BYTES + 1024 /*barriers*/ + 1024 /*alignment slack*/;
+constexpr int PM = 256;   // rows per pair tile
+
+template <int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_w8a8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                          const float* __restrict__ sa, const __nv_bfloat16* __restrict__ sw, void* __restrict__ Y,
+                          int M, int N, int K, int32_t* err) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + P_STAGES * P_STAGE_BYTES);
+  uint64_t* empty = full + P_STAGES;
+  uint64_t* tfull = empty + P_STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int num_m = (M + PM - 1) / PM, num_n = N / BN, num_kb = K / BK;
+  const int num_tiles = num_m * num_n;
+  const int pair = blockIdx.x >> 1, num_pairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < P_STAGES; ++s) {
+      mbar_init(&full[s], 1);                         // (even CTA) armed for both CTAs' bytes
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 8);                       // the 4 epilogue warps of both CTAs (used on the even CTA)
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_holder, kTmemCols);
+    tc_fence_before();
+  }
+  __syncthreads();
+  cluster_sync();                                     // both CTAs' barriers exist before any cross-CTA arrival
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer (both CTAs)
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t armed = 0, armed_par = 0;
+      bool live = true;
+      for (int tile = pair; tile < num_tiles && live; tile += num_pairs) {
+        const int m0 = (tile / num_n) * PM + static_cast<int>(rank) * 128;
+        const int n0 = (tile % num_n) * BN + static_cast<int>(rank) * 128;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait_spin(&empty[stage], phase ^ 1, abort_flag, err, kErrGemm | 0x11)) {
+            live = false;
+            break;
+          }
+          uint8_t* st_ = smem + stage * P_STAGE_BYTES;
+          const uint32_t fb = mapa_shared(&full[stage], 0);
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * P_STAGE_BYTES);
+          tma_load_2d_pair(st_, &tmA, fb, kb * BK, m0);
+          tma_load_2d_pair(st_ + P_A_BYTES, &tmB, fb, kb * BK, n0);
+          armed |= 1u << stage;
+          armed_par = (armed_par & ~(1u << stage)) | (phase << stage);
+          if (++stage == P_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!live && leader) {
+        // aborted: every stage's last armed phase, and the phase after it (for which the odd CTA may have issued its
+        // loads alone: arming it for the odd CTA's bytes lets it complete once they land), must be complete before
+        // the pair leaves
+        constexpr long long kDrainCycles = 4000000;   // about 2 ms: an issued load lands well within it
+        for (int s = 0; s < P_STAGES; ++s) {
+          const uint32_t last = (armed >> s) & 1 ? (armed_par >> s) & 1 : 1;
+          if ((armed >> s) & 1) {
+            const long long t0 = clock64();
+            while (!mbar_try_wait(&full[s], last) && clock64() - t0 < kDrainCycles) {
+            }
+          }
+          mbar_arrive_expect_tx(&full[s], P_STAGE_BYTES);
+          const long long t0 = clock64();
+          while (!mbar_try_wait(&full[s], last ^ 1) && clock64() - t0 < kDrainCycles) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ---------------------------------------------------------------- MMA issuer of the pair (even CTA)
+      constexpr uint32_t idesc = idesc_i8(PM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool live = true;
+      for (int tile = pair; tile < num_tiles && live; tile += num_pairs, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait_spin(&tempty[acc], acc_phase ^ 1, abort_flag, err, kErrGemm | 0x12)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait_spin(&full[stage], phase, abort_flag, err, kErrGemm | 0x13)) {
+            live = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + stage * P_STAGE_BYTES);
+          const uint32_t b_addr = a_addr + P_A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 32; ++k)
+            mma_i8_pair(d_tmem, desc_kmajor_sw128(a_addr + 32 * k), desc_kmajor_sw128(b_addr + 32 * k), idesc,
+                        (kb | k) != 0);
+          mma_commit_pair(&empty[stage], 0x3);
+          if (++stage == P_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (live) mma_commit_pair(&tfull[acc], 0x3);
+      }
+      mma_commit_pair(drain, 0x1);
+      const long long t0 = clock64();
+      while (!mbar_try_wait(drain, 0) && clock64() - t0 < kWaitLimitCycles) {
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue (warps 2..5 of both CTAs)
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t tempty_even[2] = {mapa_shared(&tempty[0], 0), mapa_shared(&tempty[1], 0)};
+    int local = 0;
+    for (int tile = pair; tile < num_tiles; tile += num_pairs, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait_spin(&tfull[acc], acc_phase, abort_flag, err, kErrGemm | 0x15)) break;
+      tc_fence_after();
+      const int m = (tile / num_n) * PM + static_cast<int>(rank) * 128 + row;
+      epilogue_tile<EPI>(tmem_base + acc * BN + (static_cast<uint32_t>(quarter * 32) << 16), m, m < M,
+                         (tile % num_n) * BN, tile % num_n, sa, sw, Y, N);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty_even[acc]);
+    }
+  }
+
+  __syncthreads();
+  cluster_sync();                                     // the pair's MMAs are drained; no cross-CTA access remains
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kTmemCols);
   }
 }
 
@@ -313,6 +501,39 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const float* sa, c
   return ok();
 }
 
+template <int EPI>
+int launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const float* sa, const __nv_bfloat16* sw, void* Y,
+                     int M, int N, int K, int32_t* err, cudaStream_t st) {
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    OD_CUDA_TRY(cudaFuncSetAttribute(gemm_w8a8_pair_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kPairSmemBytes));
+    attr_set[dev] = true;
+  }
+  const int tiles = ((M + PM - 1) / PM) * (N / BN);
+  const int pairs = tiles < num_sms() / 2 ? tiles : num_sms() / 2;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kPairSmemBytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  OD_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm_w8a8_pair_kernel<EPI>, ta, tb, sa, sw, Y, M, N, K, err));
+  OD_LAUNCH_CHECK();
+  return ok();
+}
+
+// rows from which the CTA-pair form is used (below it the single-CTA tiles give more CTAs to small problems)
+constexpr int64_t kPairMinRows = 1024;
+
 }  // namespace
 }  // namespace od
 
@@ -329,16 +550,24 @@ extern "C" int od_gemm_w8a8(const int8_t* A, const float* sa, const int8_t* W, c
   OD_REQUIRE(aligned16(A) && aligned16(W) && aligned16(Y), "od_gemm_w8a8: A, W, Y must be 16-byte aligned");
   OD_REQUIRE(epilogue >= OD_EPI_BF16 && epilogue <= OD_EPI_INT32, "od_gemm_w8a8: bad epilogue %d", epilogue);
   if (M == 0) return ok();
+  const bool pairs = M >= kPairMinRows;
   CUtensorMap ta, tb;
   int rc = make_map_i8(&ta, A, static_cast<uint64_t>(K), static_cast<uint64_t>(M), BK, BM);
   if (rc) return rc;
-  rc = make_map_i8(&tb, W, static_cast<uint64_t>(K), static_cast<uint64_t>(N), BK, BN);
+  rc = make_map_i8(&tb, W, static_cast<uint64_t>(K), static_cast<uint64_t>(N), BK, pairs ? 128 : BN);
   if (rc) return rc;
   int32_t* err = device_error_word();
   if (!err) return fail(OD_ECUDA, "od_gemm_w8a8: no device error word");
   cudaStream_t st = as_stream(stream);
   const auto swp = static_cast<const __nv_bfloat16*>(sw);
   const int m = static_cast<int>(M), n = static_cast<int>(N), k = static_cast<int>(K);
+  if (pairs) {
+    switch (epilogue) {
+      case OD_EPI_BF16: return launch_gemm_pair<OD_EPI_BF16>(ta, tb, sa, swp, Y, m, n, k, err, st);
+      case OD_EPI_SWIGLU: return launch_gemm_pair<OD_EPI_SWIGLU>(ta, tb, sa, swp, Y, m, n, k, err, st);
+      default: return launch_gemm_pair<OD_EPI_INT32>(ta, tb, sa, swp, Y, m, n, k, err, st);
+    }
+  }
   switch (epilogue) {
     case OD_EPI_BF16: return launch_gemm<OD_EPI_BF16>(ta, tb, sa, swp, Y, m, n, k, err, st);
     case OD_EPI_SWIGLU: return launch_gemm<OD_EPI_SWIGLU>(ta, tb, sa, swp, Y, m, n, k, err, st);

@@ -169,8 +169,11 @@ def test_gemm_int32_golden(cuda, golden):
     assert np.array_equal(acc.cpu().numpy(), golden["gemm.acc"])
 
 
-@pytest.mark.parametrize("M,N,K", [(1, 256, 128), (127, 512, 384), (300, 768, 1024), (1000, 1280, 2048)])
+@pytest.mark.parametrize("M,N,K", [(1, 256, 128), (127, 512, 384), (300, 768, 1024), (1000, 1280, 2048),
+                                   (1100, 512, 256), (2000, 256, 128), (1024, 1024, 640)])
 def test_gemm_shapes_vs_oracle(cuda, M, N, K):
+    """Single-CTA tiles (M < 1024) and CTA-pair tiles (M >= 1024, including row tails that leave the odd CTA's
+    rows partly or wholly past M) against the int64 oracle: int32 accumulators and the bf16 epilogue bit for bit."""
     g = syn.gen(M + N + K)
     a = torch.randint(-127, 128, (M, K), generator=g, dtype=torch.int8)
     w = torch.randint(-127, 128, (N, K), generator=g, dtype=torch.int8)
@@ -198,9 +201,10 @@ def test_gemm_config2_int32_exact(cuda, M, N, K):
     assert torch.equal(y, yo)
 
 
-def test_gemm_swiglu(cuda):
+@pytest.mark.parametrize("M", [200, 1300])
+def test_gemm_swiglu(cuda, M):
     g = syn.gen(5)
-    M, F, K = 200, 384, 512
+    F, K = 384, 512
     a = torch.randint(-127, 128, (M, K), generator=g, dtype=torch.int8)
     wg = torch.randint(-127, 128, (F, K), generator=g, dtype=torch.int8)
     wu = torch.randint(-127, 128, (F, K), generator=g, dtype=torch.int8)
