@@ -172,13 +172,14 @@ def run_reference(args, rank: int) -> None:
 
 
 # ------------------------------------------------------------------------------------------------ B200 arm
-def traffic_per_launch():
-    """DRAM bytes per W8A8 GEMM launch from the committed ncu summary (profiles/gemm_w8a8_qkv.md), else None."""
-    path = os.path.join(ROOT, "profiles", "gemm_w8a8_qkv.md")
+def traffic_ratio():
+    """DRAM bytes per algorithmic byte of the W8A8 GEMM, from the committed ncu summary of one launch
+    (profiles/gemm_w8a8_pair_8192x10240x4096.md), else None."""
+    path = os.path.join(ROOT, "profiles", "gemm_w8a8_pair_8192x10240x4096.md")
     if not os.path.exists(path):
         return None
     for line in open(path):
-        if line.startswith("dram_bytes_per_launch_full_size:"):
+        if line.startswith("dram_bytes_per_algorithmic_byte:"):
             try:
                 return float(line.split(":", 1)[1].split()[0])
             except ValueError:
@@ -287,6 +288,38 @@ def op_attn(args):
                           "flop_per_byte": flops / byts}))
 
 
+def op_attn_state(args):
+    """The state pass's attention (causal over each row's own keys, no prefix) at config-4 shapes: R rows x T tokens,
+    32 q / 8 kv heads, D 128 (default 64 x 2048). TFLOP/s of the causal QK + PV FLOPs."""
+    from opendecider_b200 import _lib
+    dev = torch.device("cuda", 0)
+    peaks = _peaks()
+    shapes = [tuple(int(v) for v in x.split("x")) for x in (args.shapes or "64x2048").split(",")]
+    for R, T in shapes:
+        Hq, Hkv, D = 32, 8, 128
+        g = torch.Generator(device=dev).manual_seed(0)
+        q = torch.randn(R, T, Hq, D, generator=g, device=dev).to(torch.bfloat16)
+        k = torch.randn(R, T, Hkv, D, generator=g, device=dev).to(torch.bfloat16)
+        v = torch.randn(R, T, Hkv, D, generator=g, device=dev).to(torch.bfloat16)
+        out = torch.empty_like(q)
+        ts = []
+        for i in range(args.warmup + args.steps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            _lib.prefix_attn(q, k, v, D ** -0.5, out=out)
+            b.record()
+            torch.cuda.synchronize()
+            if i >= args.warmup:
+                ts.append(a.elapsed_time(b))
+        assert _lib.device_error(dev) == 0, "a kernel reported a device-side error"
+        tm = statistics.median(ts) / 1e3
+        flops = R * Hq * T * (T + 1) / 2 * D * 4.0
+        byts = 2 * R * T * Hq * D * 2 + 2 * R * T * Hkv * D * 2
+        print(json.dumps({"op": "prefix_attn_state", "shape": {"rows": R, "tokens": T, "Hq": Hq, "Hkv": Hkv, "D": D},
+                          "ms": tm * 1e3, "tflops": flops / tm / 1e12,
+                          "frac_bf16": flops / tm / 1e12 / peaks.get("bf16_tflops", 1590.0), "gbs": byts / tm / 1e9}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -295,9 +328,11 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--config", type=int, default=4, choices=[1, 4])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--op", default="decide", choices=["decide", "gemm", "attn"],
-                    help="decide: the headline decision throughput; gemm / attn: operator configs 2 / 3")
-    ap.add_argument("--shapes", default="", help="--op gemm: MxNxK list; --op attn: requestsxrowsxt list")
+    ap.add_argument("--op", default="decide", choices=["decide", "gemm", "attn", "attn_state"],
+                    help="decide: the headline decision throughput; gemm / attn: operator configs 2 / 3; "
+                         "attn_state: the state pass's causal attention")
+    ap.add_argument("--shapes", default="", help="--op gemm: MxNxK list; --op attn: requestsxrowsxt list; "
+                                                 "--op attn_state: rowsxtokens list")
     ap.add_argument("--requests", type=int, default=0, help="--op attn: requests (default 32)")
     ap.add_argument("--breakdown", action="store_true", help="print per-kernel device time of one step to stderr")
     args = ap.parse_args()
@@ -305,6 +340,8 @@ def main():
         return op_gemm(args)
     if args.op == "attn":
         return op_attn(args)
+    if args.op == "attn_state":
+        return op_attn_state(args)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -382,6 +419,7 @@ def main():
     t_dev = max_over_ranks(e0.elapsed_time(e1) / 1e3)
     gemm_ms = sum(a.elapsed_time(b) for a, b, _, _ in probe)
     gemm_ops = sum(o for _, _, o, _ in probe)
+    gemm_bytes = sum(b for _, _, _, b in probe)
     gemm_launches = len(probe) // max(1, args.steps)
     decisions = n_dec_local * world * args.steps
     value = decisions / t_dev
@@ -452,7 +490,9 @@ def main():
                 "d2h_bytes_per_step": d2h, "ms_per_step": 1e3 * t_e2e / args.steps},
         "roofline": {"bound": "tensor", "kernel": "od_gemm_w8a8 (tcgen05 kind::i8)", "achieved": achieved,
                      "peak": peak, "unit": "TOP/s (int8)", "frac": (achieved / peak) if achieved else None,
-                     "peak_source": peak_note, "traffic": traffic_per_launch(),
+                     "peak_source": peak_note, "traffic": (traffic_ratio() * gemm_bytes / max(1, len(probe))) if traffic_ratio() and probe else None,
+                     "traffic_unit": "DRAM bytes per launch (step average: measured DRAM / algorithmic bytes of one "
+                                     "ncu launch x the algorithmic bytes of the step's launches)",
                      "launches_per_step": gemm_launches, "share_of_step": gemm_ms / 1e3 / args.steps /
                      (t_dev / args.steps) if t_dev else None},
         "cpu_baseline": cpu, "clocks": clk, "gpu_launches": launches * args.steps,
