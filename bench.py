@@ -1,6 +1,6 @@
 """Benchmark of the B200 decision forward pass (BASELINE config 4 by default).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--config 4|1]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--config 4|1|5]
     python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 --master-port P \\
         bench.py --gpus N --steps K --warmup W
 
@@ -46,6 +46,11 @@ def workload(config: int):
         cfg = DecoderConfig.nine_b(feature_layers=(8, 16, 24, "final"))
         return cfg, dict(d_model=512, n_heads=8, decision_layers=4), 12, \
             "config4: 9B-class dense decoder, 64 requests/GPU x 2048-token state, 3 questions (+none)"
+    if config == 5:
+        cfg = DecoderConfig.nine_b(feature_layers=(8, 16, 24, "final"))
+        return cfg, dict(d_model=512, n_heads=8, decision_layers=4), 12, \
+            ("config5: 9B-class dense decoder, 64 requests/GPU x 16384-token cached int8 state + 512 appended "
+             "tokens, 1 choice question x 255 options (+none)")
     cfg = DecoderConfig.tiny(feature_layers=(1, 3, "final"))
     return cfg, dict(d_model=64, n_heads=4, decision_layers=2), 32, \
         "config1: tiny decoder, 4 requests x 256-token state, 1 choice question x 8 options (+none)"
@@ -145,7 +150,69 @@ class CpuSample:
         return nd / per_request, torch.get_num_threads(), desc
 
 
+class CpuSampleCached:
+    """Config 5 on the CPU oracle: one request whose 16384-token state is already cached (the timed work is the
+    append of 512 tokens and the decision, as in the B200 arm; the cache content does not change the cost, so it is
+    random int8 rows materialised). The oracle runs option rows one at a time, so the request is timed with 2 and
+    with 6 options and the row cost extrapolated linearly to the workload's 256 rows (255 options + none), and the
+    layers sampled extrapolated linearly to all layers."""
+
+    K_SMALL, K_LARGE = 2, 6
+
+    def __init__(self, budget_s: float, seed: int = 0):
+        from oracle.model import OracleDecision
+        from oracle import ops
+        from opendecider_b200 import synthetic as syn
+        from opendecider_b200.backbone import synthetic_weights
+        from opendecider_b200.v3 import TrunkConfig, V3Trunk, trunk_state_dict
+        torch.set_num_threads(os.cpu_count() or 1)
+        cfg, tk, qmin, _ = workload(5)
+        self.cfg, self.n_layers_total = cfg, cfg.layers
+        full, tok = syn.decision_requests(5, seed=seed, n_requests=1)
+        self.rows_full = len(full[0].questions[0].options) + 1
+        self.reqs = {k: syn.decision_requests(5, seed=seed, n_requests=1, n_options=k)[0][0]
+                     for k in (self.K_SMALL, self.K_LARGE)}
+        self.T = len(tok([full[0].state], add_special_tokens=False)["input_ids"][0]) + 3
+        tc = TrunkConfig(d_feat=cfg.hidden, n_feat_layers=len(cfg.feature_layers), **tk)
+        trunk = V3Trunk(tc, trunk_state_dict(tc, seed=0), "cpu")
+        sd = synthetic_weights(cfg, seed=0, layers=1)
+        self.feats = cfg.feature_layers
+        cfg.feature_layers = ("final",) * len(self.feats)
+        g = torch.Generator().manual_seed(seed)
+        shp = (1, cfg.kv_heads, self.T, cfg.head_dim)
+
+        def rnd():
+            q = torch.randint(-127, 128, shp, generator=g, dtype=torch.int8)
+            return ops.materialize_int8(q, torch.full(shp[:-1] + (1,), 0.01, dtype=torch.bfloat16))
+
+        self.kv1 = (rnd(), rnd())
+        mk = lambda n: OracleDecision(cfg, CpuSample._alias(sd, n), trunk, tok, TEMPS, TEMPERATURE, layers=n,
+                                      qcache_min_rows=qmin)
+        t1 = self._time(mk(1), self.K_LARGE)
+        self.n = max(1, min(cfg.layers, int(budget_s / max(2.0 * t1, 1e-3))))
+        self.od = mk(self.n)
+
+    def _time(self, od, k) -> float:
+        pre = ([self.kv1] * od.dec.n, torch.zeros(1, dtype=torch.long), self.T, [self.T])
+        r = self.reqs[k]
+        t0 = time.perf_counter()
+        nxt, _, _ = od.append_pass(pre, [r.append])
+        od.decide([r], prebuilt=nxt)
+        return time.perf_counter() - t0
+
+    def step(self):
+        ts, tl = self._time(self.od, self.K_SMALL), self._time(self.od, self.K_LARGE)
+        per_row = max(0.0, (tl - ts) / (self.K_LARGE - self.K_SMALL))
+        t_req = (ts + per_row * (self.rows_full - self.K_SMALL - 1)) * self.n_layers_total / self.n
+        desc = (f"oracle/model.py (PyTorch CPU) on 1 request with a cached {self.T}-token state: append + decision "
+                f"timed with {self.K_SMALL} and {self.K_LARGE} options ({ts:.1f} s, {tl:.1f} s) over {self.n} of "
+                f"{self.n_layers_total} layers, extrapolated linearly to {self.rows_full} option rows and all layers")
+        return 1.0 / t_req, torch.get_num_threads(), desc
+
+
 def cpu_oracle_sample(config: int, budget_s: float):
+    if config == 5:
+        return CpuSampleCached(budget_s).step()
     return CpuSample(config, budget_s).step()
 
 
@@ -155,7 +222,7 @@ def run_reference(args, rank: int) -> None:
         return
     cfg, _, _, desc = workload(args.config)
     per_step = max(3.0, 120.0 / max(1, args.steps + args.warmup))
-    cs = CpuSample(args.config, per_step)
+    cs = CpuSampleCached(per_step) if args.config == 5 else CpuSample(args.config, per_step)
     vals = []
     for i in range(args.warmup + args.steps):
         v, cores, sample = cs.step()
@@ -326,7 +393,7 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--config", type=int, default=4, choices=[1, 4])
+    ap.add_argument("--config", type=int, default=4, choices=[1, 4, 5])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--op", default="decide", choices=["decide", "gemm", "attn", "attn_state"],
                     help="decide: the headline decision throughput; gemm / attn: operator configs 2 / 3; "
@@ -389,9 +456,19 @@ def main():
         return float(t.item())
 
     # ---- value: device-resident inputs (the plan uploaded once), K timed steps
-    plan = decider.plan(reqs)
+    cache, items = None, None
+    if args.config == 5:
+        # the cached states are the workload's input (built once, untimed, with room for the appended tokens);
+        # every step appends the records and decides (execute() first truncates back to the encoded length)
+        appends = [r.append for r in reqs]
+        n_app = len(tok([appends[0]], add_special_tokens=False)["input_ids"][0])
+        cache = decider.encode_states([r.state for r in reqs], room=n_app)
+        torch.cuda.synchronize()
+        plan = decider.plan(reqs, cache=cache, appends=appends)
+        items = lambda k: ((reqs, appends) for _ in range(k))
+    else:
+        plan = decider.plan(reqs)
     n_dec_local = len(plan["questions"])
-    cache = None
     for _ in range(args.warmup):
         probs, cache = decider.execute(plan, cache)
         gather(probs)
@@ -442,7 +519,8 @@ def main():
     # ---- e2e: the public API, one batch per step (Decider.decide_stream: tokenise + plan on the host, one pinned
     # H2D copy, kernels, the gather, one D2H read of the results, answers), batch b+1 planned while b runs
     g_fn = gather if world > 1 else None
-    for _ in decider.decide_stream([reqs], gather=g_fn):
+    stream_in = items if items is not None else (lambda k: (reqs for _ in range(k)))
+    for _ in decider.decide_stream(stream_in(1), gather=g_fn, cache=cache if items is not None else None):
         pass
     torch.cuda.synchronize()
     barrier()
@@ -450,7 +528,8 @@ def main():
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     f0.record()
     n_ans = 0
-    for ans, _ in decider.decide_stream((reqs for _ in range(args.steps)), gather=g_fn):
+    for ans, _ in decider.decide_stream(stream_in(args.steps), gather=g_fn,
+                                        cache=cache if items is not None else None):
         assert len(ans) == len(reqs)
         n_ans += 1
     f1.record()
@@ -459,6 +538,8 @@ def main():
     t_e2e = max_over_ranks(f0.elapsed_time(f1) / 1e3)
     assert n_ans == args.steps
 
+    if args.config == 5:
+        assert plan["state"]["T"] == cache.T, "the cached plan's appended length"
     if world > 1:
         dist.destroy_process_group()
     if rank != 0:
@@ -479,13 +560,15 @@ def main():
     if world == 1 and not args.no_cpu_baseline:
         v, cores, sample = cpu_oracle_sample(args.config, 20.0)
         cpu = {"value": v, "unit": "decisions/s", "cores": cores, "kind": "port", "sample": sample}
+    kv_gb = sum(t.q.numel() for t in cache.k + cache.v) / 1e9 if cache is not None else 0.0
     out = {
         "metric": METRIC, "value": value, "unit": "decisions/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1e3 * t_dev / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded random-id states, random-init weights)",
         "config": {"workload": desc, "global_batch": n_dec_local * world, "requests_per_gpu": len(reqs),
                    "state_tokens": plan["state"]["T"], "parallelism": f"dp{world} (requests sharded, NCCL gather)",
-                   "l2": "inputs larger than L2 (7.6 GB of int8 weights and a 9.7 GB KV cache stream every step)"},
+                   "l2": f"inputs larger than L2 (7.6 GB of int8 weights and a {kv_gb:.1f} GB int8 KV cache stream "
+                         "every step)"},
         "e2e": {"value": decisions / t_e2e, "unit": "decisions/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": 1e3 * t_e2e / args.steps},
         "roofline": {"bound": "tensor", "kernel": "od_gemm_w8a8 (tcgen05 kind::i8)", "achieved": achieved,

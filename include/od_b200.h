@@ -75,12 +75,16 @@ OD_API int od_dequant_rows_i8(const int8_t* q, const void* scale, int scale_dtyp
  * k[s*ks_s + j*ks_t + h*ks_h + d] (any strides, d contiguous), are quantised per (state, head, token) over D exactly
  * as Int8Tensor.quantize and written at token offset t0 of the cache:
  *     kq[s, h, t0 + j, :], ksc[s, h, t0 + j]    (cache: (S, Hkv, T_cap, D) int8 + (S, Hkv, T_cap) scales)
- * Scales are stored in the dtype of k/v (as Int8Tensor does). Replaces PackedCache.pack's per-layer
- * maybe_quantize (backbone.py:446) and PrefixCache._take's new-slice quantisation (state_cache.py:79).
+ * Scales are stored in the dtype of k/v (as Int8Tensor does). kb, vb (optional, both or neither, 16-byte aligned,
+ * (S, Hkv, T_cap, D) in the dtype of k/v) receive the same rows materialised, q * s rounded once as materialize()
+ * computes it (quant.py:43-45), so a kept bf16 copy of the cache is extended without re-reading the int8 rows.
+ * Replaces PackedCache.pack's per-layer maybe_quantize (backbone.py:446) and PrefixCache._take's new-slice
+ * quantisation (state_cache.py:79).
  */
 OD_API int od_kv_append_i8(const void* k, const void* v, int kv_dtype, int64_t S, int64_t t, int Hkv, int D,
                     int64_t ks_s, int64_t ks_t, int64_t ks_h, int64_t vs_s, int64_t vs_t, int64_t vs_h,
-                    int8_t* kq, int8_t* vq, void* ksc, void* vsc, int64_t T_cap, int64_t t0, void* stream);
+                    int8_t* kq, int8_t* vq, void* ksc, void* vsc, void* kb, void* vb, int64_t T_cap, int64_t t0,
+                    void* stream);
 
 /* ---------------------------------------------------------------------------------------------------------------
  * A3 + A4 + A5: residual add + Qwen3.5 RMSNorm + (optional SmoothQuant multiply) + per-token int8 quantisation.

@@ -39,8 +39,8 @@ SIGNATURES = {
     "od_quant_rows_i8": [c_void_p, c_int, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_int, c_void_p],
     "od_dequant_rows_i8": [c_void_p, c_void_p, c_int, c_int64, c_int64, c_void_p, c_int, c_void_p],
     "od_kv_append_i8": [c_void_p, c_void_p, c_int, c_int64, c_int64, c_int, c_int, c_int64, c_int64, c_int64,
-                        c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64,
-                        c_void_p],
+                        c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                        c_int64, c_int64, c_void_p],
     "od_rmsnorm_res_quant": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_int64, c_int, c_void_p,
                              c_void_p, c_void_p, c_void_p],
     "od_gemm_w8a8": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int, c_void_p],
@@ -168,15 +168,21 @@ def dequant_rows(q: torch.Tensor, scale: torch.Tensor, out_dtype: torch.dtype, o
 
 @_probed
 def kv_append(k: torch.Tensor, v: torch.Tensor, kq: torch.Tensor, vq: torch.Tensor, ksc: torch.Tensor,
-              vsc: torch.Tensor, t0: int) -> None:
+              vsc: torch.Tensor, t0: int, kb: torch.Tensor | None = None, vb: torch.Tensor | None = None) -> None:
     """Quantise new keys/values k, v (S, t, Hkv, D) (any strides, last dim contiguous) into the int8 cache
-    kq/vq (S, Hkv, T_cap, D) + ksc/vsc (S, Hkv, T_cap) at token offset t0."""
+    kq/vq (S, Hkv, T_cap, D) + ksc/vsc (S, Hkv, T_cap) at token offset t0; kb/vb (same shape as kq, dtype of k):
+    the materialised copy of the cache, extended with the same rows."""
     dev = _need_cuda(k, v, kq, vq, ksc, vsc)
     S, t, Hkv, D = k.shape
     assert k.stride(3) == 1 and v.stride(3) == 1 and kq.is_contiguous() and vq.is_contiguous()
     assert ksc.dtype == k.dtype and vsc.dtype == v.dtype and k.dtype == v.dtype
+    assert (kb is None) == (vb is None)
+    if kb is not None:
+        assert kb.shape == kq.shape and vb.shape == vq.shape and kb.is_contiguous() and vb.is_contiguous()
+        assert kb.dtype == k.dtype and vb.dtype == k.dtype
     _check(load().od_kv_append_i8(_p(k), _p(v), _DT[k.dtype], S, t, Hkv, D, k.stride(0), k.stride(1), k.stride(2),
                                   v.stride(0), v.stride(1), v.stride(2), _p(kq), _p(vq), _p(ksc), _p(vsc),
+                                  _p(kb), _p(vb),
                                   kq.shape[2], t0, _stream(dev)), "od_kv_append_i8")
 
 

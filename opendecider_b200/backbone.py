@@ -116,19 +116,43 @@ class Layer:
 
 @dataclass
 class KVCache:
-    """int8 state K/V of every layer in the reference's PackedCache layout: q (S, Hkv, T, D) int8 + scale
-    (S, Hkv, T) in the activation dtype, plus the left padding of each state (p_lo) and the padded length T."""
+    """int8 state K/V of every layer in the reference's PackedCache layout: q (S, Hkv, cap, D) int8 + scale
+    (S, Hkv, cap) in the activation dtype, plus the left padding of each state (p_lo) and the padded length T <= cap
+    (positions [T, cap) are room for appended tokens, invisible to attention)."""
     k: list                  # per layer Int8Tensor
     v: list
     p_lo: torch.Tensor       # (S,) int32: first real token of each state (left padding)
     T: int
     lens: list = field(default_factory=list)   # real tokens per state (CPU ints)
-    kb: list | None = None   # per layer bf16 (S, Hkv, T, D): the materialised K (prefix_attn.py:146-149), or None
+    kb: list | None = None   # per layer bf16 (S, Hkv, cap, D): the materialised K (prefix_attn.py:146-149), or None
     vb: list | None = None
+    cap: int = 0             # capacity (the tensors' token dimension); 0 = T
+    scratch: tuple | None = None   # bf16 (K, V) of one layer, (S, Hkv, cap, D): just-in-time materialisation
 
     @property
     def S(self) -> int:
         return self.p_lo.numel()
+
+    @property
+    def capacity(self) -> int:
+        return self.cap or self.T
+
+    def p_hi(self) -> torch.Tensor | None:
+        """(S,) int32 end of the visible prefix (= T) when the cache has room beyond T, else None (all of it)."""
+        if self.capacity == self.T:
+            return None
+        return torch.full((self.S,), self.T, dtype=torch.int32, device=self.p_lo.device)
+
+    def truncate(self, T: int, lens: list) -> None:
+        """Forget appended tokens: back to padded length T (the K/V beyond it are overwritten by the next append)."""
+        self.T, self.lens = T, list(lens)
+
+    def rows(self, a: int, b: int) -> "KVCache":
+        """View of states [a, b) (same storage)."""
+        sl = lambda t: Int8Tensor(t.q[a:b], t.scale[a:b], t.dtype)
+        return KVCache([sl(t) for t in self.k], [sl(t) for t in self.v], self.p_lo[a:b], self.T, self.lens[a:b],
+                       [t[a:b] for t in self.kb] if self.kb is not None else None,
+                       [t[a:b] for t in self.vb] if self.vb is not None else None, self.cap)
 
     def nbytes(self) -> int:
         return sum(t.nbytes() for t in self.k + self.v) + sum(t.nbytes for t in (self.kb or []) + (self.vb or []))
@@ -149,7 +173,8 @@ class PassSpec:
     q_len: torch.Tensor | None = None      # (NQ,) int32 real tokens of each question
     row_groups: torch.Tensor | None = None # (G, 2) int32 [first row, rows]: consecutive rows sharing state + question
     max_group_rows: int = 1
-    write_cache: KVCache | None = None     # state pass: append this pass's K/V (rows = states) at offset 0
+    write_cache: KVCache | None = None     # state / append pass: write this pass's K/V (rows = states) at write_t0
+    write_t0: int = 0
     capture: bool = False                  # keep every layer's post-RoPE (k, v) (R, t, Hkv, D)
     features: tuple = ()                   # feature layers to return ("final" or 1-based layer numbers)
     kv_only_last: bool = False             # state pass: the last layer only needs its K/V
@@ -169,6 +194,10 @@ class Backbone:
         # instead of dequantising it in every attention tile; 0 disables it
         total = torch.cuda.get_device_properties(device).total_memory if torch.device(device).type == "cuda" else 0
         self.materialize_budget = total // 4
+        self.max_pass_tokens = 1 << 17          # state-pass chunk: 131072 tokens
+        # a pass over an int8-only cache dequantises each layer's prefix once into a reused bf16 buffer when it has
+        # at least this many (query token x query head) slots per state per KV head; None: never
+        self.jit_min_slots = 256
 
     # ------------------------------------------------------------------------------------------ construction
     @classmethod
@@ -243,6 +272,12 @@ class Backbone:
         captured = [] if spec.capture else None
         d = None
         cache = spec.cache
+        p_hi = cache.p_hi() if cache is not None else None
+        # dequantise the prefix once per layer (into a reused bf16 buffer) when the whole-cache copy was not kept
+        # and the pass has at least two 128-slot query tiles per state (each would otherwise dequantise it again)
+        jit = cache is not None and cache.kb is None and self.jit_min_slots is not None and \
+            (M // max(1, cache.S)) * (Hq // Hkv) >= self.jit_min_slots and \
+            self.jit_bytes(cache) <= self.materialize_budget
         for li, L in enumerate(self.layers):
             last = li == cfg.layers - 1
             if li == 0:
@@ -256,25 +291,26 @@ class Backbone:
             k4, v4 = k.view(R, t, Hkv, D), v.view(R, t, Hkv, D)
             if spec.write_cache is not None:
                 wc = spec.write_cache
-                _lib.kv_append(k4, v4, wc.k[li].q, wc.v[li].q, wc.k[li].scale, wc.v[li].scale, t0=0)
-                if wc.kb is not None:                       # materialise once: bf16(q * s) per cached row
-                    D_ = wc.k[li].q.shape[-1]
-                    _lib.dequant_rows(wc.k[li].q.view(-1, D_), wc.k[li].scale.view(-1, 1), torch.bfloat16,
-                                      out=wc.kb[li].view(-1, D_))
-                    _lib.dequant_rows(wc.v[li].q.view(-1, D_), wc.v[li].scale.view(-1, 1), torch.bfloat16,
-                                      out=wc.vb[li].view(-1, D_))
+                # the kept bf16 copy (materialize(): bf16(q * s)) is written by the same kernel, new rows only
+                _lib.kv_append(k4, v4, wc.k[li].q, wc.v[li].q, wc.k[li].scale, wc.v[li].scale, t0=spec.write_t0,
+                               kb=wc.kb[li] if wc.kb is not None else None,
+                               vb=wc.vb[li] if wc.vb is not None else None)
             if captured is not None:
                 captured.append((k4, v4))
             if last and spec.kv_only_last:
                 break
-            mat = cache is not None and cache.kb is not None
+            Kb = Vb = None
+            if cache is not None and cache.kb is not None:
+                Kb, Vb = cache.kb[li], cache.vb[li]
+            elif cache is not None and jit:                 # this layer's cache materialised just for this pass
+                Kb, Vb = self._materialise_layer(cache, li)
             o = _lib.prefix_attn(
                 q.view(R, t, Hq, D), k4, v4, D ** -0.5,
-                Kp=(cache.kb[li] if mat else cache.k[li].q) if cache else None,
-                Vp=(cache.vb[li] if mat else cache.v[li].q) if cache else None,
-                ksc=cache.k[li].scale if cache and not mat else None,
-                vsc=cache.v[li].scale if cache and not mat else None,
-                row_state=spec.row_state, p_lo=cache.p_lo if cache else None,
+                Kp=(Kb if Kb is not None else cache.k[li].q) if cache else None,
+                Vp=(Vb if Vb is not None else cache.v[li].q) if cache else None,
+                ksc=cache.k[li].scale if cache and Kb is None else None,
+                vsc=cache.v[li].scale if cache and Kb is None else None,
+                row_state=spec.row_state, p_lo=cache.p_lo if cache else None, p_hi=p_hi,
                 Kq=spec.qkv_prefix[li][0] if spec.qkv_prefix else None,
                 Vq=spec.qkv_prefix[li][1] if spec.qkv_prefix else None, row_q=spec.row_q, q_len=spec.q_len,
                 own_lo=spec.own_lo, own_hi=spec.own_hi, row_groups=spec.row_groups,
@@ -296,18 +332,37 @@ class Backbone:
         return out, captured
 
     # ------------------------------------------------------------------------------------------ state pass
-    def new_cache(self, S: int, T: int) -> KVCache:
+    def new_cache(self, S: int, T: int, cap: int | None = None) -> KVCache:
+        """Empty cache for S states of padded length T, with room for tokens up to `cap` (default T)."""
         cfg, dev = self.cfg, self.device
-        mk = lambda: Int8Tensor(torch.empty(S, cfg.kv_heads, T, cfg.head_dim, dtype=torch.int8, device=dev),
-                                torch.empty(S, cfg.kv_heads, T, dtype=cfg.dtype, device=dev), cfg.dtype)
+        C = max(T, cap or T)
+        mk = lambda: Int8Tensor(torch.empty(S, cfg.kv_heads, C, cfg.head_dim, dtype=torch.int8, device=dev),
+                                torch.empty(S, cfg.kv_heads, C, dtype=cfg.dtype, device=dev), cfg.dtype)
         cache = KVCache([mk() for _ in range(cfg.layers)], [mk() for _ in range(cfg.layers)],
-                        torch.zeros(S, dtype=torch.int32, device=dev), T)
-        bf16_bytes = 2 * cfg.layers * S * cfg.kv_heads * T * cfg.head_dim * 2
+                        torch.zeros(S, dtype=torch.int32, device=dev), T, cap=C)
+        bf16_bytes = 2 * cfg.layers * S * cfg.kv_heads * C * cfg.head_dim * 2
         if cfg.dtype == torch.bfloat16 and 0 < bf16_bytes <= self.materialize_budget:
-            mb = lambda: torch.empty(S, cfg.kv_heads, T, cfg.head_dim, dtype=torch.bfloat16, device=dev)
+            mb = lambda: torch.empty(S, cfg.kv_heads, C, cfg.head_dim, dtype=torch.bfloat16, device=dev)
             cache.kb = [mb() for _ in range(cfg.layers)]
             cache.vb = [mb() for _ in range(cfg.layers)]
         return cache
+
+    def jit_bytes(self, cache: KVCache) -> int:
+        """bytes of one layer's bf16 K and V (the just-in-time materialisation buffer)."""
+        return 2 * cache.S * self.cfg.kv_heads * cache.capacity * self.cfg.head_dim * 2
+
+    def _materialise_layer(self, cache: KVCache, li: int):
+        """bf16(q * s) of layer li's cached K and V into the cache's reused buffer (exactly what the in-kernel
+        dequantisation and materialize() compute)."""
+        if cache.scratch is None:
+            shp = (cache.S, self.cfg.kv_heads, cache.capacity, self.cfg.head_dim)
+            cache.scratch = (torch.empty(shp, dtype=torch.bfloat16, device=self.device),
+                             torch.empty(shp, dtype=torch.bfloat16, device=self.device))
+        D = self.cfg.head_dim
+        Kb, Vb = cache.scratch
+        _lib.dequant_rows(cache.k[li].q.view(-1, D), cache.k[li].scale.view(-1, 1), torch.bfloat16, out=Kb.view(-1, D))
+        _lib.dequant_rows(cache.v[li].q.view(-1, D), cache.v[li].scale.view(-1, 1), torch.bfloat16, out=Vb.view(-1, D))
+        return Kb, Vb
 
     def plan_state(self, seqs, up=None) -> dict:
         """Host layout of the batched state pass (Backbone.prefix_cache_batch, backbone.py:347-368): states LEFT-padded
@@ -325,12 +380,34 @@ class Backbone:
         Int8Tensor.quantize, backbone.py:446). The last layer stops after its K/V projection: nothing downstream
         reads its attention or MLP output (the state pass keeps no hidden states, v3.py:317)."""
         S, T = plan["S"], plan["T"]
-        if cache is None or cache.S != S or cache.T != T:
-            cache = self.new_cache(S, T)
+        cap = max(T, plan.get("cap") or T)
+        if cache is None or cache.S != S or cache.capacity != cap:
+            cache = self.new_cache(S, T, cap)
+        cache.T = T
         cache.p_lo.copy_(plan["pad"])
         cache.lens = plan["lens"]
-        self.run(PassSpec(ids=plan["ids"], pos=plan["pos"], own_lo=plan["pad"], write_cache=cache,
+        # states in chunks of at most `max_pass_tokens` tokens (bounded activation memory), each written into its
+        # rows of the cache
+        per = max(1, self.max_pass_tokens // max(1, T))
+        for a in range(0, S, per):
+            b = min(S, a + per)
+            self.run(PassSpec(ids=plan["ids"][a:b], pos=plan["pos"][a:b], own_lo=plan["pad"][a:b],
+                              write_cache=cache.rows(a, b), kv_only_last=True))
+        return cache
+
+    def run_append(self, ids: torch.Tensor, cache: KVCache) -> KVCache:
+        """PrefixCache.encode's continuation (state_cache.py:140-146) for every state at once: n new tokens per state
+        (ids (S, n) on the device) at positions T .. T+n-1 attend the cached prefix [p_lo, T) and each other causally;
+        their int8 K/V (Int8Tensor.quantize, the snapshot's quantisation) are written at [T, T+n). Advances T."""
+        S, n = ids.shape
+        assert S == cache.S and cache.T + n <= cache.capacity, "append: cache rows / capacity"
+        T = cache.T
+        pos = (T + torch.arange(n, device=ids.device, dtype=torch.int32)).expand(S, n).contiguous()
+        rows = torch.arange(S, device=ids.device, dtype=torch.int32)
+        self.run(PassSpec(ids=ids, pos=pos, cache=cache, row_state=rows, write_cache=cache, write_t0=T,
                           kv_only_last=True))
+        cache.T = T + n
+        cache.lens = [l + n for l in cache.lens]
         return cache
 
     def prefix_cache_batch(self, seqs) -> KVCache:

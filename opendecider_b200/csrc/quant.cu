@@ -223,7 +223,8 @@ template <typename T, int EPL>
 __global__ void kv_append_kernel(const T* __restrict__ k, const T* __restrict__ v, int64_t S, int64_t t, int Hkv,
                                  int64_t ks_s, int64_t ks_t, int64_t ks_h, int64_t vs_s, int64_t vs_t, int64_t vs_h,
                                  int8_t* __restrict__ kq, int8_t* __restrict__ vq, T* __restrict__ ksc,
-                                 T* __restrict__ vsc, int64_t T_cap, int64_t t0, bool vec) {
+                                 T* __restrict__ vsc, T* __restrict__ kb, T* __restrict__ vb, int64_t T_cap,
+                                 int64_t t0, bool vec) {
   constexpr int D = EPL * 32;
   const int item = static_cast<int>((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
   const int lane = threadIdx.x & 31;
@@ -251,13 +252,39 @@ __global__ void kv_append_kernel(const T* __restrict__ k, const T* __restrict__ 
     amax = warp_max(amax);
     const float sc = quant_scale(amax), rs = quant_recip(sc);
     int8_t* out = (which == 0 ? kq : vq) + dst * D + lane * EPL;
+    int8_t qv[EPL];
     if (EPL == 4 && vec) {                                // one 4-byte store per lane
-      *reinterpret_cast<uint32_t*>(out) = quant4(x[0], x[1], x[2], x[3], sc, rs);
+      const uint32_t w = quant4(x[0], x[1], x[2], x[3], sc, rs);
+      *reinterpret_cast<uint32_t*>(out) = w;
+#pragma unroll
+      for (int i = 0; i < EPL; ++i) qv[i] = static_cast<int8_t>(w >> (8 * i));
     } else {
 #pragma unroll
-      for (int i = 0; i < EPL; ++i) out[i] = quant_val(x[i], sc, rs);
+      for (int i = 0; i < EPL; ++i) {
+        qv[i] = quant_val(x[i], sc, rs);
+        out[i] = qv[i];
+      }
     }
-    if (lane == 0) (which == 0 ? ksc : vsc)[dst] = Elem<T>::from_f(sc);
+    const T sc_t = Elem<T>::from_f(sc);
+    if (lane == 0) (which == 0 ? ksc : vsc)[dst] = sc_t;
+    T* mat = which == 0 ? kb : vb;
+    if (mat != nullptr) {   // materialize(): q * s in the scale's dtype; |q| <= 127 times s is exact in fp32
+      const float sf = Elem<T>::to_f(sc_t);
+      T m[EPL];
+#pragma unroll
+      for (int i = 0; i < EPL; ++i) m[i] = Elem<T>::from_f(static_cast<float>(qv[i]) * sf);
+      T* mo = mat + dst * D + lane * EPL;
+      if constexpr (EPL * sizeof(T) == 16) {
+        *reinterpret_cast<uint4*>(mo) = *reinterpret_cast<const uint4*>(m);
+      } else if constexpr (EPL * sizeof(T) == 8) {
+        *reinterpret_cast<uint2*>(mo) = *reinterpret_cast<const uint2*>(m);
+      } else if constexpr (EPL * sizeof(T) == 4) {
+        *reinterpret_cast<uint32_t*>(mo) = *reinterpret_cast<const uint32_t*>(m);
+      } else {
+#pragma unroll
+        for (int i = 0; i < EPL; ++i) mo[i] = m[i];
+      }
+    }
   }
 }
 
@@ -519,8 +546,12 @@ extern "C" int od_dequant_rows_i8(const int8_t* q, const void* scale, int scale_
 
 extern "C" int od_kv_append_i8(const void* k, const void* v, int kv_dtype, int64_t S, int64_t t, int Hkv, int D,
                                int64_t ks_s, int64_t ks_t, int64_t ks_h, int64_t vs_s, int64_t vs_t, int64_t vs_h,
-                               int8_t* kq, int8_t* vq, void* ksc, void* vsc, int64_t T_cap, int64_t t0, void* stream) {
+                               int8_t* kq, int8_t* vq, void* ksc, void* vsc, void* kb, void* vb, int64_t T_cap,
+                               int64_t t0, void* stream) {
   OD_REQUIRE(k && v && kq && vq && ksc && vsc, "od_kv_append_i8: null pointer");
+  OD_REQUIRE((kb == nullptr) == (vb == nullptr), "od_kv_append_i8: kb and vb go together");
+  OD_REQUIRE(kb == nullptr || ((reinterpret_cast<uintptr_t>(kb) | reinterpret_cast<uintptr_t>(vb)) & 15) == 0,
+             "od_kv_append_i8: materialised outputs must be 16-byte aligned");
   OD_REQUIRE(S >= 0 && t >= 0 && Hkv > 0 && t0 >= 0 && t0 + t <= T_cap, "od_kv_append_i8: bad shape (t0 + t > T_cap?)");
   OD_REQUIRE(D == 64 || D == 128 || D == 256, "od_kv_append_i8: head_dim %d not in {64, 128, 256}", D);
   if (S == 0 || t == 0) return ok();
@@ -535,7 +566,8 @@ extern "C" int od_kv_append_i8(const void* k, const void* v, int kv_dtype, int64
 #define OD_KV(T_, E)                                                                                           \
   kv_append_kernel<T_, E><<<blocks, threads, 0, st>>>(static_cast<const T_*>(k), static_cast<const T_*>(v), S, t, \
                                                       Hkv, ks_s, ks_t, ks_h, vs_s, vs_t, vs_h, kq, vq,          \
-                                                      static_cast<T_*>(ksc), static_cast<T_*>(vsc), T_cap, t0, vec)
+                                                      static_cast<T_*>(ksc), static_cast<T_*>(vsc),            \
+                                                      static_cast<T_*>(kb), static_cast<T_*>(vb), T_cap, t0, vec)
   if (kv_dtype == OD_BF16) {
     if (D == 64) OD_KV(__nv_bfloat16, 2); else if (D == 128) OD_KV(__nv_bfloat16, 4); else OD_KV(__nv_bfloat16, 8);
   } else if (kv_dtype == OD_F16) {

@@ -43,9 +43,13 @@ class Decider:
         q2.none_col = len(q.options)
         return q2
 
-    def encode_states(self, states) -> KVCache:
-        """The batched state pass: state_text() of every request, tokenised, one left-padded pass."""
-        return self.model.backbone.run_state(self._plan_states(states))
+    def encode_states(self, states, cap: int | None = None, room: int = 0) -> KVCache:
+        """The batched state pass: state_text() of every request, tokenised, one left-padded pass (in state chunks
+        for long states). cap (total token capacity) or room (tokens beyond the encoded length): space for appended
+        tokens (decide with `cache=` and `appends=`)."""
+        st = self._plan_states(states)
+        st["cap"] = max(cap or 0, st["T"] + room)
+        return self.model.backbone.run_state(st)
 
     def _plan_states(self, states, up=None) -> dict:
         texts = [state_text(s) for s in states]
@@ -64,12 +68,27 @@ class Decider:
                 owner.append(i)
         return {"questions": batch, "owner": owner, "n_requests": len(requests)}
 
-    def plan(self, requests) -> dict:
+    def plan(self, requests, cache: KVCache | None = None, appends=None) -> dict:
         """Everything host-side of one decide_many call (tokenisation, layouts, readout constants), staged in one
-        pinned buffer and uploaded by one copy. The plan's device views stay valid until the next plan()."""
+        pinned buffer and uploaded by one copy. The plan's device views stay valid until the next plan().
+        With `cache` (row i = request i's encoded state, encode_states) the state pass is skipped; `appends` (one text
+        per request, equal token counts) are first appended to the states - PrefixCache.encode's continuation of a
+        cached state (state_cache.py:116-158) for the whole batch - and the questions read the extended states."""
         self.staging.begin()
         up = self.staging.put
-        st = self._plan_states([r.state for r in requests], up)
+        if cache is None:
+            st = self._plan_states([r.state for r in requests], up)
+        else:
+            assert cache.S == len(requests), "one cached state per request"
+            T0, lens0 = cache.T, list(cache.lens)
+            app, n = None, 0
+            if appends is not None:
+                seqs = self.model.tok(list(appends), add_special_tokens=False)["input_ids"]
+                n = len(seqs[0])
+                assert all(len(q) == n for q in seqs), "appends of one batch have equal token counts"
+                assert T0 + n <= cache.capacity, "the cache has no room for the appended tokens (encode_states cap)"
+                app = up(torch.tensor(seqs, dtype=torch.long))
+            st = {"cached": True, "T0": T0, "lens0": lens0, "append": app, "T": T0 + n, "lens": [l + n for l in lens0]}
         batch, owner = [], []
         for i, r in enumerate(requests):
             for q in r.questions:
@@ -89,7 +108,14 @@ class Decider:
     def execute(self, plan: dict, cache: KVCache | None = None):
         """The device work of one call: state pass, row passes, trunk, od_readout. Returns device tensors
         (probs (N, K) fp32, renorm (N, K) fp64, p_none (N,) fp32) and the cache."""
-        cache = self.model.backbone.run_state(plan["state"], cache)
+        st = plan["state"]
+        if st.get("cached"):
+            assert cache is not None, "the plan reads an encoded cache: pass it to execute()"
+            cache.truncate(st["T0"], st["lens0"])         # a replayed plan appends at the same place again
+            if st["append"] is not None:
+                self.model.backbone.run_append(st["append"], cache)
+        else:
+            cache = self.model.backbone.run_state(st, cache)
         logits, opt_mask = self.model.execute(plan["model"], cache)
         probs = _lib.readout(logits.contiguous(), plan["T"], opt_mask.to(torch.uint8), none_col=plan["none_col"])
         return probs, cache
@@ -144,16 +170,17 @@ class Decider:
         probs, _ = self.execute(plan)
         return self.answers(plan, probs)
 
-    def decide_stream(self, batches, gather=None):
+    def decide_stream(self, batches, gather=None, cache: KVCache | None = None):
         """decide_many over a sequence of request batches, pipelined: the read-back of batch b's results is enqueued
         right after its kernels, batch b+1 is planned on the host and its device work enqueued, and only then are
         b's results awaited, so the GPU runs batch after batch without waiting for the host. `gather(probs)`
         (optional) runs on the device after a batch's kernels, in stream order (e.g. the data-parallel all-gather of
         the probabilities), and its result is read back with the answers. Yields (answers, gathered or None) per
-        batch, in order. The KV cache allocation is reused from batch to batch."""
-        pending, cache = None, None
-        for requests in batches:
-            plan = self.plan(requests)
+        batch, in order. The KV cache allocation is reused from batch to batch. With `cache`, every batch is a
+        (requests, appends) pair over that cache's encoded states (see plan())."""
+        pending, fixed = None, cache is not None
+        for item in batches:
+            plan = self.plan(*item, cache=cache) if fixed else self.plan(item)
             probs, cache = self.execute(plan, cache)
             dev = list(probs) + ([gather(probs)] if gather is not None else [])
             host = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in dev]

@@ -117,9 +117,11 @@ def words(ids) -> str:
 
 @dataclass
 class Request:
-    """One decision request: a state and its questions (the atomic part of the reference's DecideRequest)."""
+    """One decision request: a state and its questions (the atomic part of the reference's DecideRequest); `append`:
+    text appended to an already-encoded state before the questions (config 5's incremental records)."""
     state: str
     questions: list
+    append: str = ""
 
 
 def _ids(g, n, vocab):
@@ -137,13 +139,14 @@ def _distinct_options(g, k, n_tok, vocab):
 
 
 def decision_requests(config: int, seed: int = 0, n_requests: int | None = None, vocab: int | None = None,
-                      state_tokens: int | None = None, n_options: int | None = None):
+                      state_tokens: int | None = None, n_options: int | None = None, append_tokens: int | None = None):
     """Seeded requests of BASELINE configs 1, 4 and 5 (states of random ids; state_text() adds 3 template tokens,
     so the random part is state_tokens - 3 ids and the tokenised state is exactly state_tokens long).
       1: 4 requests, 256-token states, one choice question: prompt 16 ids, 8 options x 8 ids
       4: 64 requests, 2048-token states, three questions: choice 16 options x 12 ids, yes/no, score 5 levels x
          2 ids; prompts 16 ids
-      5: 512 requests, 16384-token states (+512 appended record ids), one choice question 255 options x 12 ids
+      5: 512 requests, 16384-token states (+512 appended record ids, Request.append), one choice question 255
+         options x 12 ids
     Returns (requests, tokenizer)."""
     from .batching import Question
     g = gen(seed)
@@ -153,6 +156,7 @@ def decision_requests(config: int, seed: int = 0, n_requests: int | None = None,
         n, V, T, K = n_requests or 64, vocab or 151936, state_tokens or 2048, n_options or 16
     elif config == 5:
         n, V, T, K = n_requests or 512, vocab or 151936, state_tokens or 16384, n_options or 255
+        A = 512 if append_tokens is None else append_tokens
     else:
         raise ValueError(config)
     tok = SyntheticTokenizer(V)
@@ -168,5 +172,5 @@ def decision_requests(config: int, seed: int = 0, n_requests: int | None = None,
             qs.append(Question.score(words(_ids(g, 16, V)), _distinct_options(g, 5, 2, V), name="score"))
         else:
             qs.append(Question(words(_ids(g, 16, V)), _distinct_options(g, K, 12, V), "choice", name="choice"))
-        reqs.append(Request(state, qs))
+        reqs.append(Request(state, qs, words(_ids(g, A, V)) if config == 5 else ""))
     return reqs, tok

@@ -110,20 +110,32 @@ class OracleDecoder:
         return out, kv
 
 
+def sdpa_flash(q, k, v, ok):
+    """The attention of the reference's own passes over a cache (the transformers sdpa interface, which on the CPU
+    runs torch's flash-attention kernel: aten/src/ATen/native/cpu/FlashAttentionKernel.cpp): fp32 scores
+    (q.k) * D^-0.5, fp32 max and exp-sum, the probabilities rounded to bf16 before the P.V product (fp32
+    accumulation), the sum divided out in fp32, bf16 out. Below 512 keys that kernel takes one key block, so no
+    rescaling enters. q (R, t, Hq, D), k/v (R, Tk, Hkv, D) bf16, ok (R, t, Tk) bool -> (R, t, Hq*D) bf16."""
+    R, t, Hq, D = q.shape
+    g = Hq // k.shape[2]
+    qf = q.float().transpose(1, 2)
+    kf = k.float().repeat_interleave(g, 2).transpose(1, 2)
+    vf = v.float().repeat_interleave(g, 2).transpose(1, 2)
+    s = (qf @ kf.transpose(-1, -2)) * D ** -0.5
+    s = s.masked_fill(~ok[:, None], float("-inf"))
+    m = s.amax(-1, keepdim=True).clamp_min(-3.0e38)
+    p = torch.exp(s - m)
+    o = (p.to(BF).float() @ vf) / p.sum(-1, keepdim=True).clamp_min(1e-30)
+    return o.transpose(1, 2).reshape(R, t, Hq * D).to(BF)
+
+
 def causal_attend(pad):
-    """Causal attention of the state pass with left padding (keys before pad[r] masked), fp32 math."""
+    """Causal attention of the state pass with left padding (keys before pad[r] masked)."""
     def f(i, q, k, v):
-        R, t, Hq, D = q.shape
-        g = Hq // k.shape[2]
-        qf = q.float().transpose(1, 2)
-        kf = k.float().repeat_interleave(g, 2).transpose(1, 2)
-        vf = v.float().repeat_interleave(g, 2).transpose(1, 2)
-        s = qf @ kf.transpose(-1, -2) * D ** -0.5
+        t = q.shape[1]
         j = torch.arange(t)
         ok = (j[None, :] <= j[:, None])[None] & (j[None, None, :] >= pad.view(-1, 1, 1))
-        s = s.masked_fill(~ok[:, None], float("-inf"))
-        o = torch.softmax(s, -1).nan_to_num(0.0) @ vf
-        return o.transpose(1, 2).reshape(R, t, Hq * D).to(BF)
+        return sdpa_flash(q, k, v, ok)
     return f
 
 
@@ -153,11 +165,54 @@ class OracleDecision:
                           ops.materialize_int8(torch.from_numpy(vq), torch.from_numpy(vs).to(BF))))
         return cache, pad, T, lens
 
-    def decide(self, requests):
-        """Returns (probs (N, K), renorm (N, K) fp64, p_none (N,)) numpy, questions in request order."""
+    def append_pass(self, prebuilt, appends):
+        """PrefixCache.encode's continuation of cached states (state_cache.py:116-158, one request at a time there):
+        the appended ids (equal counts) attend the materialised prefix and each other causally at positions T..T+n-1
+        (Backbone.prefill with the restored cache); their K/V are quantised into the next snapshot (_take,
+        state_cache.py:79); PackedCache.pack then quantises the whole cache (the materialised prefix again, and the
+        new K/V) and the rows read it materialised. Returns ((cache, pad, T + n, lens + n), snapshots, packs) with
+        snapshots[layer] = ((k int8 (S, Hkv, n, D), k scale bf16 (S, Hkv, n)), (v ...)) and packs[layer] the same
+        over all T + n tokens."""
+        cache, pad, T, lens = prebuilt
+        seqs = self.tok(list(appends), add_special_tokens=False)["input_ids"]
+        S, n = len(seqs), len(seqs[0])
+        assert all(len(q) == n for q in seqs)
+        ids = torch.tensor(seqs)
+        pos = (T + torch.arange(n)).expand(S, n)
+        pm_state = torch.arange(T)[None, :] >= pad[:, None]
+        D = self.cfg.head_dim
+
+        i_ = torch.arange(n)
+        ok = torch.cat([pm_state[:, None, :].expand(S, n, T), (i_[None, :] <= i_[:, None])[None].expand(S, n, n)], 2)
+
+        def attend(i, q, k, v):
+            Kp, Vp = cache[i]                                             # (S, Hkv, T, D) materialised
+            return sdpa_flash(q, torch.cat([Kp.transpose(1, 2), k], 1), torch.cat([Vp.transpose(1, 2), v], 1), ok)
+
+        _, kv = self.dec.run(ids, pos, attend)
+        new, snaps, packs = [], [], []
+        for (Kp, Vp), (k, v) in zip(cache, kv):
+            pair, snap, pack = [], [], []
+            for P_, x in ((Kp, k), (Vp, v)):
+                xn = x.transpose(1, 2).contiguous()                       # (S, Hkv, n, D) bf16
+                q8, sc, _ = ops.quantize_rows(xn.float().numpy(), "bf16")
+                snap.append((torch.from_numpy(q8), torch.from_numpy(sc).to(BF).reshape(q8.shape[:-1])))
+                full = torch.cat([P_, xn], 2)
+                fq, fs, _ = ops.quantize_rows(full.float().numpy(), "bf16")
+                fq, fs = torch.from_numpy(fq), torch.from_numpy(fs).to(BF).reshape(fq.shape[:-1])
+                pack.append((fq, fs))
+                pair.append(ops.materialize_int8(fq, fs[..., None]))
+            new.append(tuple(pair))
+            snaps.append(tuple(snap))
+            packs.append(tuple(pack))
+        return (new, pad, T + n, [l + n for l in lens]), snaps, packs
+
+    def decide(self, requests, prebuilt=None):
+        """Returns (probs (N, K), renorm (N, K) fp64, p_none (N,)) numpy, questions in request order. prebuilt: the
+        states' (cache, pad, T, lens) from state_pass / append_pass instead of a state pass."""
         import copy
         from opendecider_b200.batching import MAX_OPTIONS, answer_option_text, answer_row_prefix
-        cache, pad, T, lens = self.state_pass([r.state for r in requests])
+        cache, pad, T, lens = prebuilt if prebuilt is not None else self.state_pass([r.state for r in requests])
         qs = []
         for i, r in enumerate(requests):
             for q in r.questions:

@@ -72,8 +72,13 @@ def build_reference(cfg: DecoderConfig, tok):
         layer_types=["full_attention"] * cfg.layers, rms_norm_eps=cfg.eps, tie_word_embeddings=True,
         pad_token_id=tok.pad_token_id,
         rope_parameters={"rope_type": "default", "rope_theta": cfg.rope_theta, "partial_rotary_factor": 1.0})
-    m = Qwen3_5ForCausalLM(c).to(torch.bfloat16).eval()
+    m = Qwen3_5ForCausalLM(c)
+    inv_freq = m.model.rotary_emb.inv_freq.clone()
+    m = m.to(torch.bfloat16).eval()
     lm = m.model
+    # from_pretrained(dtype=bfloat16) - the reference's load path (backbone.py:118) - keeps the rotary inv_freq
+    # buffer in fp32; a whole-module .to(bfloat16) would round it, so the fp32 buffer is put back.
+    lm.rotary_emb.inv_freq = inv_freq
     missing, unexpected = lm.load_state_dict(synthetic_weights(cfg, seed=0), strict=False)
     assert not unexpected and all("rotary" in k for k in missing), (missing, unexpected)
     quantize_int8_(lm.layers)

@@ -123,6 +123,31 @@ def test_kv_append_golden(cuda, golden):
     assert torch.equal(vsc.cpu().view(torch.int16).reshape(-1), torch.from_numpy(golden["kv.vs"]).reshape(-1))
 
 
+@pytest.mark.parametrize("D", [64, 128, 256])
+def test_kv_append_materialised_copy(cuda, D):
+    """The kept bf16 copy written by the append equals materialize() of the int8 rows it wrote (oracle
+    materialize_int8, bit for bit), at a token offset, leaving every other position of the copy untouched."""
+    S, t, Hkv, T_cap, t0 = 3, 37, 2, 96, 50
+    g = syn.gen(D)
+    k = (torch.randn(S, t, Hkv, D, generator=g) * 2).to(torch.bfloat16).to(cuda)
+    v = (torch.randn(S, t, Hkv, D, generator=g) * 0.3).to(torch.bfloat16).to(cuda)
+    kq = torch.zeros(S, Hkv, T_cap, D, dtype=torch.int8, device=cuda)
+    vq = torch.zeros_like(kq)
+    ksc = torch.zeros(S, Hkv, T_cap, dtype=torch.bfloat16, device=cuda)
+    vsc = torch.zeros_like(ksc)
+    kb = torch.full((S, Hkv, T_cap, D), 7.0, dtype=torch.bfloat16, device=cuda)
+    vb = torch.full_like(kb, 7.0)
+    _lib.kv_append(k, v, kq, vq, ksc, vsc, t0=t0, kb=kb, vb=vb)
+    for q8, sc, mat in ((kq, ksc, kb), (vq, vsc, vb)):
+        want = ops.materialize_int8(q8[:, :, t0:t0 + t].cpu(), sc[:, :, t0:t0 + t, None].cpu())
+        assert torch.equal(mat[:, :, t0:t0 + t].cpu().view(torch.int16), want.view(torch.int16))
+        assert bool((mat[:, :, :t0] == 7.0).all()) and bool((mat[:, :, t0 + t:] == 7.0).all())
+        # and the int8 rows are those of the append without the copy
+    kq2, vq2, ksc2, vsc2 = (torch.zeros_like(x) for x in (kq, vq, ksc, vsc))
+    _lib.kv_append(k, v, kq2, vq2, ksc2, vsc2, t0=t0)
+    assert torch.equal(kq2, kq) and torch.equal(vq2, vq) and torch.equal(ksc2, ksc) and torch.equal(vsc2, vsc)
+
+
 # ------------------------------------------------------------------------------------------------ norm + quant
 @pytest.mark.parametrize("M,H", [(40, 256), (333, 4096)])
 def test_rmsnorm_res_quant(cuda, M, H):
