@@ -433,7 +433,8 @@ def main():
     torch.cuda.empty_cache()
     tc = TrunkConfig(d_feat=cfg.hidden, n_feat_layers=len(cfg.feature_layers), **tk)
     trunk = V3Trunk(tc, trunk_state_dict(tc, seed=0), dev)
-    reqs, tok = syn.decision_requests(args.config, seed=rank)
+    # per GPU: config 4's 64 requests; config 5's 512 requests are the 8-GPU batch, 64 per GPU (weak scaling)
+    reqs, tok = syn.decision_requests(args.config, seed=rank, n_requests=64 if args.config == 5 else None)
     decider = Decider(V3Model(bb, trunk, tok, qcache_min_rows=qmin), TEMPERATURE, TEMPS)
 
     def gather(probs):

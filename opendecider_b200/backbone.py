@@ -128,6 +128,8 @@ class KVCache:
     vb: list | None = None
     cap: int = 0             # capacity (the tensors' token dimension); 0 = T
     scratch: tuple | None = None   # bf16 (K, V) of one layer, (S, Hkv, cap, D): just-in-time materialisation
+    enc_T: int = 0           # the encoded states' padded length and real lengths (the snapshot every append of a
+    enc_lens: list = field(default_factory=list)   # decision call starts from, as PrefixCache._restore does)
 
     @property
     def S(self) -> int:
@@ -383,9 +385,9 @@ class Backbone:
         cap = max(T, plan.get("cap") or T)
         if cache is None or cache.S != S or cache.capacity != cap:
             cache = self.new_cache(S, T, cap)
-        cache.T = T
+        cache.T = cache.enc_T = T
         cache.p_lo.copy_(plan["pad"])
-        cache.lens = plan["lens"]
+        cache.lens, cache.enc_lens = list(plan["lens"]), list(plan["lens"])
         # states in chunks of at most `max_pass_tokens` tokens (bounded activation memory), each written into its
         # rows of the cache
         per = max(1, self.max_pass_tokens // max(1, T))

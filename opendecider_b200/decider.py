@@ -80,7 +80,7 @@ class Decider:
             st = self._plan_states([r.state for r in requests], up)
         else:
             assert cache.S == len(requests), "one cached state per request"
-            T0, lens0 = cache.T, list(cache.lens)
+            T0, lens0 = cache.enc_T, list(cache.enc_lens)        # appends of earlier calls are not kept
             app, n = None, 0
             if appends is not None:
                 seqs = self.model.tok(list(appends), add_special_tokens=False)["input_ids"]
