@@ -180,7 +180,7 @@ class Decider:
         (requests, appends) pair over that cache's encoded states (see plan())."""
         pending, fixed = None, cache is not None
         for item in batches:
-            plan = self.plan(*item, cache=cache) if fixed else self.plan(item)
+            plan = self.plan(item[0], cache=cache, appends=item[1]) if fixed else self.plan(item)
             probs, cache = self.execute(plan, cache)
             dev = list(probs) + ([gather(probs)] if gather is not None else [])
             host = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in dev]

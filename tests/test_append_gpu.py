@@ -158,3 +158,19 @@ def test_append_prefix_read_paths_identical(cuda):
         bb.jit_min_slots = 256
     for other in runs[1:]:
         assert all(np.array_equal(x, y) for x, y in zip(runs[0], other))
+
+
+def test_append_decide_stream_equals_execute(cuda):
+    """decide_stream over an encoded cache ((requests, appends) per batch, each batch appending to the encoded
+    states afresh) answers as plan + execute does, batch after batch."""
+    cfg, reqs, tok, dec = make(cuda)
+    cache = dec.encode_states([r.state for r in reqs], room=APPEND)
+    want = _flat(_decide_cached(dec, reqs, cache))
+    other = syn.decision_requests(5, seed=4, n_requests=N_REQ, vocab=cfg.vocab, state_tokens=STATE,
+                                  n_options=OPTIONS, append_tokens=APPEND)[0]
+    appends = [[r.append for r in reqs], [r.append for r in other], [r.append for r in reqs]]
+    got = [_flat(a) for a, _ in dec.decide_stream(((reqs, ap) for ap in appends), cache=cache)]
+    assert len(got) == 3
+    for i in (0, 2):
+        assert all(np.array_equal(x, y) for x, y in zip(want, got[i]))
+    assert not np.array_equal(want[0], got[1][0])        # other records, other answers
