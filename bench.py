@@ -330,7 +330,7 @@ def op_attn(args):
         row_state = torch.arange(S, dtype=torch.int32, device=dev).repeat_interleave(rows)
         kw = dict(Kp=Kq.view(S, Hkv, T, D), Vp=Vq.view(S, Hkv, T, D), ksc=ks.view(S, Hkv, T),
                   vsc=vs.view(S, Hkv, T), row_state=row_state)
-        per = max(1, min(rows, 128 // (t * (Hq // Hkv))))      # rows of one request share a 128-slot tile
+        per = max(1, min(rows, _lib.ATTN_CTA_SLOTS // (t * (Hq // Hkv))))   # rows of a request share a CTA
         starts = [(s * rows + a, min(per, rows - a)) for s in range(S) for a in range(0, rows, per)]
         kw["row_groups"] = torch.tensor(starts, dtype=torch.int32, device=dev)
         kw["max_group_rows"] = per

@@ -264,6 +264,10 @@ def gate_quant(o: torch.Tensor, qkv: torch.Tensor, Hq: int, D: int, q=None, s=No
     return q, s
 
 
+# query slots one od_prefix_attn CTA holds (two 128-slot tensor-core tiles): a row group may fill it
+ATTN_CTA_SLOTS = 256
+
+
 @_probed
 def prefix_attn(q: torch.Tensor, k_own: torch.Tensor, v_own: torch.Tensor, sm_scale: float, *,
                 Kp=None, Vp=None, ksc=None, vsc=None, row_state=None, p_lo=None, p_hi=None, pmask=None,

@@ -34,41 +34,44 @@ namespace od {
 namespace {
 using namespace sm100;
 
-constexpr int kSoftmaxWarps = 8;     // warps 0-7: lane quarter w % 4, key half w / 4
+constexpr int kSoftmaxWarps = 8;     // warps 0-3: query tile 0, warps 4-7: query tile 1 (lane quarter w % 4)
 constexpr int kMmaWarp = 8;          // warp 8: TMEM allocation and the single MMA-issuing thread
-constexpr int kProducerWarps = 4;    // warps 9-12: stage Q, then K/V blocks
+constexpr int kProducerWarps = 4;    // warps 9-12: K/V blocks
 constexpr int kProducer0 = 32 * (kSoftmaxWarps + 1);
 constexpr int kProducers = 32 * kProducerWarps;
 constexpr int kThreads = 32 * (kSoftmaxWarps + 1 + kProducerWarps);
-constexpr int BM = 128;              // query slots per CTA
+constexpr int BM = 128;              // query slots per tile (one per TMEM lane)
+constexpr int kTiles = 2;            // query tiles per CTA, ping-ponged on the tensor core
+constexpr int kCtaSlots = kTiles * BM;
 constexpr int BN = 128;              // keys per block (one per producer thread)
-constexpr int KS = 3;                // K ring depth
+constexpr int KS = 2;                // K ring depth
 constexpr int VS = 2;                // V ring depth
-constexpr int MS = 4;                // mask ring depth (a block's bits are rewritten only after its softmax ended)
+constexpr int MS = 4;                // mask ring depth (a block's bits are rewritten only after both softmaxes)
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kTmemS = 0;       // S buffers at columns 0 and BN (BN fp32 each)
-constexpr uint32_t kTmemP = 2 * BN;  // P: BN / 2 columns of bf16 pairs (A operand of O += P V)
-constexpr uint32_t kTmemQ = 320;     // Q: D / 2 columns of bf16 pairs (A operand of S = Q K^T)
-constexpr uint32_t kTmemO = 384;     // O: D fp32 columns
-static_assert(kTmemP + BN / 2 <= kTmemQ && kTmemQ + 128 / 2 <= kTmemO, "TMEM columns overlap");
+constexpr uint32_t kTmemS = 0;       // S of tile x at column x * BN (BN fp32); its P (bf16 pairs) overwrites the
+                                     // first BN / 2 of those columns
+constexpr uint32_t kTmemO = 2 * BN;  // O of tile x at column kTmemO + x * 128 (D <= 128 fp32)
 constexpr int32_t kErrAttn = 0x5A0000;
 static_assert(BN == kProducers, "one key of a block per producer thread");
+static_assert(kTmemO + kTiles * 128 <= kTmemCols, "TMEM columns");
 
 template <int D>
 struct Layout {
   static constexpr int ATOM = 128 * 128;             // 128 rows x 128 B: one 64-column swizzle atom of a tile
-  static constexpr int TILE = ATOM * (D / 64);       // 128 rows x D bf16 (a K block or a V block)
-  static constexpr int K0 = 0;
+  static constexpr int TILE = ATOM * (D / 64);       // 128 rows x D bf16 (a Q tile, a K block or a V block)
+  static constexpr int Q0 = 0;                       // kTiles query tiles (the A operand of S = Q K^T)
+  static constexpr int K0 = Q0 + kTiles * TILE;
   static constexpr int V0 = K0 + KS * TILE;
   static constexpr int RAWK = V0 + VS * TILE;        // int8 K / V block staging: BN rows x D bytes, row-major
   static constexpr int RAWV = RAWK + BN * D;
   static constexpr int MASK0 = RAWV + BN * D;        // MS x 4 words: bit k of word w = key 32 w + k visible
-  static constexpr int XCH = MASK0 + MS * 16;        // 3 x 2 x BM floats: row max (2 parities), then l
-  static constexpr int BAR = XCH + 3 * 2 * BM * 4;   // mbarriers + TMEM holder + abort flag
+  static constexpr int BAR = MASK0 + MS * 16;        // mbarriers + TMEM holder + abort flag
   static constexpr int BYTES = BAR + 256 + 1024;     // + alignment slack
+  static __host__ __device__ constexpr int Q(int x) { return Q0 + x * TILE; }
   static __host__ __device__ constexpr int K(int b) { return K0 + b * TILE; }
   static __host__ __device__ constexpr int V(int b) { return V0 + b * TILE; }
 };
+static_assert(Layout<128>::BYTES <= 232448, "shared memory");
 
 struct Params {
   CUtensorMap map_ko, map_vo, map_kq, map_vq;   // bf16 (rows, Hkv*D) views of own / question K and V, 64x128 boxes
@@ -190,24 +193,22 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
   uint8_t* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::BAR);
   uint64_t* kfull = bars;                  // [KS] producers (+ TMA bytes) -> MMA
-  uint64_t* kempty = kfull + KS;           // [KS] MMA (S_j complete) -> producers
+  uint64_t* kempty = kfull + KS;           // [KS] MMA (S_j of both tiles complete) -> producers
   uint64_t* vfull = kempty + KS;           // [VS] producers (+ TMA bytes) -> MMA
-  uint64_t* vempty = vfull + VS;           // [VS] MMA (P_j V_j complete) -> producers
+  uint64_t* vempty = vfull + VS;           // [VS] MMA (P_j V_j of both tiles complete) -> producers
   uint64_t* mfull = vempty + VS;           // [MS] producer warps (mask words written) -> softmax
-  uint64_t* s_full = mfull + MS;           // [2] MMA (S_j complete) -> softmax
-  uint64_t* p_full = s_full + 2;           // softmax (P_j in TMEM, O rescaled) -> MMA
-  uint64_t* pv_done = p_full + 1;          // MMA (P_j V_j complete) -> softmax
-  uint64_t* xbar = pv_done + 1;            // [4] the two softmax warps of a lane quarter exchanged their values
-  uint64_t* rawk_full = xbar + 4;          // TMA (raw int8 K block) -> producers
+  uint64_t* s_full = mfull + MS;           // [kTiles] MMA (S_j of the tile complete) -> the tile's softmax
+  uint64_t* p_full = s_full + kTiles;      // [kTiles] the tile's softmax (P_j in TMEM, O rescaled) -> MMA
+  uint64_t* pv_done = p_full + kTiles;     // [kTiles] MMA (P_j V_j of the tile complete) -> MMA, softmax epilogue
+  uint64_t* rawk_full = pv_done + kTiles;  // TMA (raw int8 K block) -> producers
   uint64_t* rawk_empty = rawk_full + 1;    // producers (raw K converted) -> the TMA-issuing producer
   uint64_t* rawv_full = rawk_full + 2;
   uint64_t* rawv_empty = rawk_full + 3;
-  uint64_t* q_full = rawk_full + 4;        // softmax warps (Q in TMEM) -> MMA
+  uint64_t* q_full = rawk_full + 4;        // softmax warps (both Q tiles in shared memory) -> MMA
   uint64_t* drain = rawk_full + 5;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   uint32_t* masks = reinterpret_cast<uint32_t*>(sm + L::MASK0);
-  float* xch = reinterpret_cast<float*>(sm + L::XCH);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int tile = blockIdx.x % P.tiles_per_group;
@@ -218,8 +219,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
   const int t = static_cast<int>(P.t);
   const int slots_row = t * rep;
   const int slots = nr * slots_row;
-  const int s0 = tile * BM;
+  const int s0 = tile * kCtaSlots;
   if (s0 >= slots) return;                            // uniform: before any barrier or allocation
+  const int ntiles = slots - s0 > BM ? 2 : 1;         // the second query tile only when it holds a slot
 
   if (tid == 0) {
     for (int b = 0; b < KS; ++b) {
@@ -231,10 +233,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
       mbar_init(&vempty[b], 1);
     }
     for (int b = 0; b < MS; ++b) mbar_init(&mfull[b], kProducerWarps);
-    for (int b = 0; b < 2; ++b) mbar_init(&s_full[b], 1);
-    mbar_init(p_full, 32 * kSoftmaxWarps);
-    mbar_init(pv_done, 1);
-    for (int b = 0; b < 4; ++b) mbar_init(&xbar[b], 64);
+    for (int x = 0; x < kTiles; ++x) {
+      mbar_init(&s_full[x], 1);
+      mbar_init(&p_full[x], BM);
+      mbar_init(&pv_done[x], 1);
+    }
     mbar_init(rawk_full, 1);
     mbar_init(rawk_empty, kProducers);
     mbar_init(rawv_full, 1);
@@ -266,11 +269,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
     n2 = P.q_len[qr];
     nb2 = (n2 + BN - 1) / BN;
   }
-  // own keys, flattened (row a, token j) -> a * t + j; a single long row only needs keys up to the tile's last token
+  // own keys, flattened (row a, token j) -> a * t + j; a single long row only needs keys up to the CTA's last token
   int own_begin = 0, own_end = nr * t;
   if (nr == 1) {
     const int lo = P.own_lo ? P.own_lo[row0] : 0;
-    const int last_tok = min(t - 1, (min(slots, s0 + BM) - 1) / rep);
+    const int last_tok = min(t - 1, (min(slots, s0 + kCtaSlots) - 1) / rep);
     own_begin = (lo / BN) * BN;
     own_end = last_tok + 1;
   }
@@ -387,42 +390,61 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
     }
   } else if (warp == kMmaWarp) {
     // ================================================================== MMA issue (one thread)
+    // Per block j and tile x: S_x(j) = Q_x K_j^T into the tile's S columns, then (once the tile's softmax has
+    // written P_x(j) over them) O_x += P_x(j) V_j. P aliases S, so S_x(j+1) is issued only after P_x(j) V_j has
+    // completed; the other tile's MMAs fill the tensor core meanwhile (A: P V, S; then B: P V, S).
     if (lane == 0 && nblk > 0) {
       constexpr uint32_t idesc_s = idesc_bf16(BM, BN, false);
       constexpr uint32_t idesc_o = idesc_bf16(BM, D, true);
-      auto issue_s = [&](int j) {
+      auto issue_s = [&](int x, int j) {
+        const uint32_t sQ = smem_u32(sm + L::Q(x));
         const uint32_t sK = smem_u32(sm + L::K(j % KS));
 #pragma unroll
-        for (int kd = 0; kd < D / 16; ++kd)
-          mma_f16_ts(tmem + kTmemS + (j & 1) * BN, tmem + kTmemQ + kd * 8,
-                     desc_sw128(sK + (kd >> 2) * L::ATOM + (kd & 3) * 32, 16, 1024), idesc_s, kd > 0 ? 1u : 0u);
-        mma_commit(&s_full[j & 1]);
-        mma_commit(&kempty[j % KS]);
+        for (int kd = 0; kd < D / 16; ++kd) {
+          const uint32_t off = (kd >> 2) * L::ATOM + (kd & 3) * 32;
+          mma_f16(tmem + kTmemS + x * BN, desc_sw128(sQ + off, 16, 1024), desc_sw128(sK + off, 16, 1024), idesc_s,
+                  kd > 0 ? 1u : 0u);
+        }
+        mma_commit(&s_full[x]);
+      };
+      auto issue_pv = [&](int x, int j) {
+        const uint32_t sV = smem_u32(sm + L::V(j % VS));
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk)
+          mma_f16_ts(tmem + kTmemO + x * 128, tmem + kTmemS + x * BN + kk * 8,
+                     desc_sw128(sV + kk * 16 * 128, L::ATOM, 1024), idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(&pv_done[x]);
       };
       bool live = mbar_wait(q_full, 0, abort_flag, P.err, kErrAttn | 17) &&
                   mbar_wait(&kfull[0], 0, abort_flag, P.err, kErrAttn | 3);
       if (live) {
         tc_fence_after();
-        issue_s(0);
+        for (int x = 0; x < ntiles; ++x) issue_s(x, 0);
+        mma_commit(&kempty[0]);
       }
       for (int j = 0; j < nblk && live; ++j) {
-        // S buffer (j+1) & 1 was last read by the softmax of block j-1, whose P_{j-1} was waited for below
-        if (j + 1 < nblk) {
-          if (!mbar_wait(&kfull[(j + 1) % KS], ((j + 1) / KS) & 1, abort_flag, P.err, kErrAttn | 4)) break;
+        const bool more = j + 1 < nblk;
+        if (!mbar_wait(&vfull[j % VS], (j / VS) & 1, abort_flag, P.err, kErrAttn | 5)) break;
+        if (more && !mbar_wait(&kfull[(j + 1) % KS], ((j + 1) / KS) & 1, abort_flag, P.err, kErrAttn | 4)) break;
+        for (int x = 0; x < ntiles && live; ++x) {
+          if (!mbar_wait(&p_full[x], j & 1, abort_flag, P.err, kErrAttn | 6)) {
+            live = false;
+            break;
+          }
           tc_fence_after();
-          issue_s(j + 1);
+          issue_pv(x, j);
+          if (x == ntiles - 1) mma_commit(&vempty[j % VS]);
+          if (more) {
+            // P_x(j) is read from the columns S_x(j+1) overwrites: wait for the P V above to complete
+            if (!mbar_wait(&pv_done[x], j & 1, abort_flag, P.err, kErrAttn | 18)) {
+              live = false;
+              break;
+            }
+            tc_fence_after();
+            issue_s(x, j + 1);
+            if (x == ntiles - 1) mma_commit(&kempty[(j + 1) % KS]);
+          }
         }
-        if (!mbar_wait(&vfull[j % VS], (j / VS) & 1, abort_flag, P.err, kErrAttn | 5) ||
-            !mbar_wait(p_full, j & 1, abort_flag, P.err, kErrAttn | 6))
-          break;
-        tc_fence_after();
-        const uint32_t sV = smem_u32(sm + L::V(j % VS));
-#pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk)
-          mma_f16_ts(tmem + kTmemO, tmem + kTmemP + kk * 8, desc_sw128(sV + kk * 16 * 128, L::ATOM, 1024), idesc_o,
-                     (j > 0 || kk > 0) ? 1u : 0u);
-        mma_commit(pv_done);
-        mma_commit(&vempty[j % VS]);
       }
       // every MMA issued here has completed before TMEM is released (immediate unless aborted)
       mma_commit(drain);
@@ -431,190 +453,173 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
       }
     }
   } else {
-    // ================================================================== softmax (lane quarter q4, key half h)
-    const int q4 = warp & 3, h = warp >> 2;
+    // ================================================================== softmax (tile x, lane quarter q4)
+    const int q4 = warp & 3, x = warp >> 2;
     const int tt = 32 * q4 + lane;                    // slot of the tile = TMEM lane
-    const int slot = s0 + tt;
+    const int slot = s0 + x * BM + tt;
     const bool my_valid = slot < slots;
     const int a_my = my_valid ? slot / slots_row : 0;
     const int i_my = my_valid ? (slot % slots_row) / rep : 0;
     const int hh_my = slot % rep;
     const uint32_t lane_off = static_cast<uint32_t>(32 * q4) << 16;
+    const uint32_t tS = tmem + lane_off + kTmemS + x * BN;
+    const uint32_t tO = tmem + lane_off + kTmemO + x * 128;
     const float scale = P.scale_log2;
     {
-      // this slot's Q, the warp's half of the head dimension (D / 4 bf16 pairs), into TMEM lane tt
-      constexpr int NW = D / 4;
-      uint32_t qw[NW];
+      // this slot's Q row into the tile's shared-memory A operand (128-byte swizzled, K-major)
+      uint8_t* dq = sm + L::Q(x);
       if (my_valid) {
         const uint4* src = reinterpret_cast<const uint4*>(
-            P.q + ((static_cast<int64_t>(row0 + a_my) * t + i_my) * P.Hq + g * rep + hh_my) * D + h * (D / 2));
+            P.q + ((static_cast<int64_t>(row0 + a_my) * t + i_my) * P.Hq + g * rep + hh_my) * D);
 #pragma unroll
-        for (int k = 0; k < NW / 4; ++k) {
-          const uint4 v = __ldg(src + k);
-          qw[4 * k] = v.x;
-          qw[4 * k + 1] = v.y;
-          qw[4 * k + 2] = v.z;
-          qw[4 * k + 3] = v.w;
-        }
+        for (int ch = 0; ch < D / 8; ++ch) *reinterpret_cast<uint4*>(dq + swz(tt, ch, L::ATOM)) = __ldg(src + ch);
       } else {
 #pragma unroll
-        for (int k = 0; k < NW; ++k) qw[k] = 0u;
+        for (int ch = 0; ch < D / 8; ++ch) *reinterpret_cast<uint4*>(dq + swz(tt, ch, L::ATOM)) = make_uint4(0, 0, 0, 0);
       }
-      if constexpr (NW == 32) {
-        tmem_st_32x32b_x32(tmem + lane_off + kTmemQ + h * NW, qw);
-      } else {
-        tmem_st_32x32b_x16(tmem + lane_off + kTmemQ + h * NW, qw);
-      }
-      tmem_st_wait();
-      tc_fence_before();
+      fence_proxy_async_smem();
       mbar_arrive(q_full);
     }
-    float m_used = -INFINITY, l_part = 0.f;
+    const bool active = x < ntiles;                   // warp-uniform
+    float m_used = -INFINITY, l_sum = 0.f;
     bool live = true;
-    for (int j = 0; j < nblk; ++j) {
-      const int b = j & 1;
-      if (!warp_wait(&s_full[b], (j >> 1) & 1, abort_flag, P.err, kErrAttn | 7) ||
+    for (int j = 0; j < nblk && active; ++j) {
+      if (!warp_wait(&s_full[x], j & 1, abort_flag, P.err, kErrAttn | 7) ||
           !warp_wait(&mfull[j % MS], (j / MS) & 1, abort_flag, P.err, kErrAttn | 8)) {
         live = false;
         break;
       }
       tc_fence_after();
-      float s[64];
-      {
-        uint32_t r0[32], r1[32];
-        tmem_ld_32x32b_x32(tmem + lane_off + kTmemS + b * BN + 64 * h, r0);
-        tmem_ld_32x32b_x32(tmem + lane_off + kTmemS + b * BN + 64 * h + 32, r1);
-        tmem_ld_wait();
+      uint32_t mw[4];
 #pragma unroll
-        for (int k = 0; k < 32; ++k) {
-          s[k] = __uint_as_float(r0[k]);
-          s[k + 32] = __uint_as_float(r1[k]);
-        }
-      }
-      const uint32_t mw0 = masks[4 * (j % MS) + 2 * h], mw1 = masks[4 * (j % MS) + 2 * h + 1];
+      for (int w = 0; w < 4; ++w) mw[w] = masks[4 * (j % MS) + w];
       // own keys visible to this slot form one range of the flattened (row, token) index: its own row's tokens up
-      // to its own position; in block-local key numbers of this warp's half: [vis_lo, vis_hi]
+      // to its own position; in block-local key numbers: [vis_lo, vis_hi]
       int vis_lo = -(1 << 30), vis_hi = 1 << 30;
       if (j >= nb1 + nb2) {
-        const int key0 = own_begin + (j - nb1 - nb2) * BN + 64 * h;
+        const int key0 = own_begin + (j - nb1 - nb2) * BN;
         vis_lo = a_my * t - key0;
         vis_hi = a_my * t + i_my - key0;
       }
-      const bool fast = (mw0 & mw1) == 0xffffffffu && vis_lo <= 0 && vis_hi >= 63;
-      if (!__all_sync(0xffffffffu, fast)) {
+      const bool fast = __all_sync(0xffffffffu, (mw[0] & mw[1] & mw[2] & mw[3]) == 0xffffffffu && vis_lo <= 0 &&
+                                                    vis_hi >= BN - 1);
+      // a 32-key chunk's scores with the invisible keys at -inf
+      auto mask_chunk = [&](uint32_t (&c)[32], int ci) {
+        if (!fast) {
+          const uint32_t w = ci == 0 ? mw[0] : ci == 1 ? mw[1] : ci == 2 ? mw[2] : mw[3];
 #pragma unroll
-        for (int k = 0; k < 64; ++k) {
-          const uint32_t bit = ((k < 32 ? mw0 : mw1) >> (k & 31)) & 1u;
-          if (!bit || k < vis_lo || k > vis_hi) s[k] = -INFINITY;
+          for (int k = 0; k < 32; ++k)
+            if (!((w >> k) & 1u) || k + 32 * ci < vis_lo || k + 32 * ci > vis_hi) c[k] = __float_as_uint(-INFINITY);
         }
-      }
+      };
+      // pass 1: the row max over the block's four 32-key chunks, two at a time
+      uint32_t ca[32], cb[32];
       float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int k = 0; k < 64; k += 8) {
-        mq[0] = fmax3(mq[0], s[k], s[k + 1]);
-        mq[1] = fmax3(mq[1], s[k + 2], s[k + 3]);
-        mq[2] = fmax3(mq[2], s[k + 4], s[k + 5]);
-        mq[3] = fmax3(mq[3], s[k + 6], s[k + 7]);
+      for (int half = 0; half < 2; ++half) {
+        tmem_ld_32x32b_x32(tS + 64 * half, ca);
+        tmem_ld_32x32b_x32(tS + 64 * half + 32, cb);
+        tmem_ld_wait();
+        mask_chunk(ca, 2 * half);
+        mask_chunk(cb, 2 * half + 1);
+#pragma unroll
+        for (int k = 0; k < 32; k += 4) {
+          mq[0] = fmax3(mq[0], __uint_as_float(ca[k]), __uint_as_float(ca[k + 1]));
+          mq[1] = fmax3(mq[1], __uint_as_float(ca[k + 2]), __uint_as_float(ca[k + 3]));
+          mq[2] = fmax3(mq[2], __uint_as_float(cb[k]), __uint_as_float(cb[k + 1]));
+          mq[3] = fmax3(mq[3], __uint_as_float(cb[k + 2]), __uint_as_float(cb[k + 3]));
+        }
       }
       const float mloc = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
-      // the row max of the whole block: exchange with the warp holding the other key half of these slots
-      float* xm = xch + (j & 1) * 2 * BM;
-      xm[h * BM + tt] = mloc;
-      mbar_arrive(&xbar[q4]);
-      if (!warp_wait(&xbar[q4], j & 1, abort_flag, P.err, kErrAttn | 9)) {
-        live = false;
-        break;
-      }
-      const float mb = fmaxf(mloc, xm[(1 - h) * BM + tt]) * scale;
+      const float mb = mloc * scale;
       float alpha = 1.f;
       bool resc = false;
       if (m_used == -INFINITY) {
         m_used = mb;                                   // nothing accumulated yet: O and l are 0
       } else if (mb > m_used + 8.f) {
         alpha = ex2_approx(m_used - mb);
-        l_part *= alpha;
+        l_sum *= alpha;
         m_used = mb;
         resc = true;
       }
-      uint32_t pw[32];
-      float rs = 0.f;
-      if (m_used == -INFINITY) {                       // no visible key so far: every weight is 0
-#pragma unroll
-        for (int c = 0; c < 32; ++c) pw[c] = 0u;
-      } else {
-        const float2 sc2 = make_float2(scale, scale), nm2 = make_float2(-m_used, -m_used);
-        float2 acc[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-#pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const float2 x = __ffma2_rn(make_float2(s[2 * c], s[2 * c + 1]), sc2, nm2);
-          const float2 p = make_float2(ex2_approx(x.x), ex2_approx(x.y));
-          acc[c & 1] = __fadd2_rn(acc[c & 1], p);
-          pw[c] = pack_bf16(p.x, p.y);
-        }
-        rs = (acc[0].x + acc[0].y) + (acc[1].x + acc[1].y);
-      }
-      l_part += rs;
-      // P (one buffer) and O are free once P_{j-1} V_{j-1} completed
-      if (j >= 1 && !warp_wait(pv_done, (j - 1) & 1, abort_flag, P.err, kErrAttn | 10)) {
-        live = false;
-        break;
-      }
-      tc_fence_after();
-      if (__any_sync(0xffffffffu, resc)) {             // lazy rescale of this warp's half of the O row
+      // O_x may be rescaled now: P_x(j-1) V_{j-1} completed before S_x(j) was issued
+      if (__any_sync(0xffffffffu, resc)) {             // lazy rescale of the O row
 #pragma unroll 1
-        for (int dc = 0; dc < D / 64; ++dc) {
+        for (int dc = 0; dc < D / 32; ++dc) {
           uint32_t o[32];
-          const uint32_t ta = tmem + lane_off + kTmemO + h * (D / 2) + dc * 32;
-          tmem_ld_32x32b_x32(ta, o);
+          tmem_ld_32x32b_x32(tO + dc * 32, o);
           tmem_ld_wait();
 #pragma unroll
           for (int k = 0; k < 32; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * alpha);
-          tmem_st_32x32b_x32(ta, o);
+          tmem_st_32x32b_x32(tO + dc * 32, o);
         }
       }
-      tmem_st_32x32b_x32(tmem + lane_off + kTmemP + 32 * h, pw);
+      // pass 2: P = 2^(s * scale - m) in bf16 over the S columns (P chunk c lands on columns 16c..16c+15, which hold
+      // S chunk c / 2: already read), the row sum in fp32. One chunk of scores in registers at a time (the kernel's
+      // 13 warps cap a thread at 128 registers).
+      const bool none = m_used == -INFINITY;           // no visible key so far: every weight is 0
+      const float2 sc2 = make_float2(scale, scale), nm2 = make_float2(-m_used, -m_used);
+      float2 acc[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+      auto chunk = [&](uint32_t (&c)[32], int ci) {
+        mask_chunk(c, ci);
+        uint32_t pw[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+          if (none) {
+            pw[k] = 0u;
+          } else {
+            const float2 y = __ffma2_rn(make_float2(__uint_as_float(c[2 * k]), __uint_as_float(c[2 * k + 1])), sc2,
+                                        nm2);
+            const float2 pp = make_float2(ex2_approx(y.x), ex2_approx(y.y));
+            acc[k & 1] = __fadd2_rn(acc[k & 1], pp);
+            pw[k] = pack_bf16(pp.x, pp.y);
+          }
+        }
+        tmem_st_32x32b_x16(tS + 16 * ci, pw);
+      };
+#pragma unroll 1
+      for (int ci = 0; ci < 4; ++ci) {
+        tmem_ld_32x32b_x32(tS + 32 * ci, ca);
+        tmem_ld_wait();
+        chunk(ca, ci);
+      }
+      l_sum += (acc[0].x + acc[0].y) + (acc[1].x + acc[1].y);
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[x]);
     }
     // ---- epilogue: O / l, natural-log LSE (nothing is written after a time-out; the error word says why).
     // TMEM loads are warp-collective: every lane loads, valid slots store.
-    if (live && nblk > 0)
-      live = warp_wait(pv_done, (nblk - 1) & 1, abort_flag, P.err, kErrAttn | 11);
-    if (live) {
-      float* xl = xch + 4 * BM;
-      xl[h * BM + tt] = l_part;
-      mbar_arrive(&xbar[q4]);
-      live = warp_wait(&xbar[q4], nblk & 1, abort_flag, P.err, kErrAttn | 12);
-    }
-    if (live) {
-      tc_fence_after();
-      const float l_sum = l_part + xch[4 * BM + (1 - h) * BM + tt];
-      const float inv = l_sum > 0.f ? 1.0f / l_sum : 0.f;
-      const int64_t orow = ((static_cast<int64_t>(row0 + a_my) * t + i_my) * P.Hq + g * rep + hh_my) * D;
+    if (active) {
+      if (live && nblk > 0) live = warp_wait(&pv_done[x], (nblk - 1) & 1, abort_flag, P.err, kErrAttn | 11);
+      if (live) {
+        tc_fence_after();
+        const float inv = l_sum > 0.f ? 1.0f / l_sum : 0.f;
+        const int64_t orow = ((static_cast<int64_t>(row0 + a_my) * t + i_my) * P.Hq + g * rep + hh_my) * D;
 #pragma unroll 1
-      for (int dc = 0; dc < D / 64; ++dc) {
-        uint32_t o[32];
-        if (nblk > 0) {
-          tmem_ld_32x32b_x32(tmem + lane_off + kTmemO + h * (D / 2) + dc * 32, o);
-          tmem_ld_wait();
-        } else {
+        for (int dc = 0; dc < D / 32; ++dc) {
+          uint32_t o[32];
+          if (nblk > 0) {
+            tmem_ld_32x32b_x32(tO + dc * 32, o);
+            tmem_ld_wait();
+          } else {
 #pragma unroll
-          for (int k = 0; k < 32; ++k) o[k] = 0u;
+            for (int k = 0; k < 32; ++k) o[k] = 0u;
+          }
+          if (my_valid) {
+            uint32_t w[16];
+#pragma unroll
+            for (int k = 0; k < 16; ++k)
+              w[k] = pack_bf16(__uint_as_float(o[2 * k]) * inv, __uint_as_float(o[2 * k + 1]) * inv);
+            uint4* dst = reinterpret_cast<uint4*>(P.o + orow + dc * 32);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) dst[k] = make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+          }
         }
-        if (my_valid) {
-          uint32_t w[16];
-#pragma unroll
-          for (int k = 0; k < 16; ++k)
-            w[k] = pack_bf16(__uint_as_float(o[2 * k]) * inv, __uint_as_float(o[2 * k + 1]) * inv);
-          uint4* dst = reinterpret_cast<uint4*>(P.o + orow + h * (D / 2) + dc * 32);
-#pragma unroll
-          for (int k = 0; k < 4; ++k) dst[k] = make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
-        }
+        if (P.lse && my_valid)
+          P.lse[(static_cast<int64_t>(row0 + a_my) * P.Hq + g * rep + hh_my) * t + i_my] =
+              l_sum > 0.f ? (m_used + log2f(l_sum)) * 0.6931471805599453f : -INFINITY;
       }
-      if (P.lse && my_valid && h == 0)
-        P.lse[(static_cast<int64_t>(row0 + a_my) * P.Hq + g * rep + hh_my) * t + i_my] =
-            l_sum > 0.f ? (m_used + log2f(l_sum)) * 0.6931471805599453f : -INFINITY;
     }
     tc_fence_before();
   }
@@ -708,9 +713,9 @@ extern "C" int od_prefix_attn(const void* q, const void* Kp, const void* Vp, con
   const int64_t G = row_groups ? dims.G : dims.R;
   const int64_t max_rows = row_groups ? dims.max_group_rows : 1;
   OD_REQUIRE(G >= 0 && max_rows >= 1, "od_prefix_attn: bad row groups");
-  OD_REQUIRE(max_rows == 1 || max_rows * dims.t * rep <= BM,
-             "od_prefix_attn: a group of several rows must fit one %d-slot tile (rows %lld x t %lld x rep %d)", BM,
-             (long long)max_rows, (long long)dims.t, rep);
+  OD_REQUIRE(max_rows == 1 || max_rows * dims.t * rep <= kCtaSlots,
+             "od_prefix_attn: a group of several rows must fit one CTA's %d slots (rows %lld x t %lld x rep %d)",
+             kCtaSlots, (long long)max_rows, (long long)dims.t, rep);
   if (G == 0 || dims.t == 0) return ok();
   int32_t* err = device_error_word();
   if (!err) return fail(OD_ECUDA, "od_prefix_attn: no device error word");
@@ -744,7 +749,7 @@ extern "C" int od_prefix_attn(const void* q, const void* Kp, const void* Vp, con
   P.Hq = dims.Hq;
   P.Hkv = dims.Hkv;
   P.rep = rep;
-  P.tiles_per_group = static_cast<int>((max_rows * dims.t * rep + BM - 1) / BM);
+  P.tiles_per_group = static_cast<int>((max_rows * dims.t * rep + kCtaSlots - 1) / kCtaSlots);
   P.scale_log2 = dims.sm_scale * 1.4426950408889634f;
   {
     const uint64_t cols = static_cast<uint64_t>(dims.Hkv) * dims.D;

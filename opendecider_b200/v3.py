@@ -21,6 +21,7 @@ from dataclasses import dataclass
 import torch
 import torch.nn.functional as F
 
+from . import _lib
 from .backbone import Backbone, KVCache, PassSpec
 from .batching import answer_option_text, answer_row_prefix, segment_layout
 
@@ -308,7 +309,7 @@ def plan_rows(bb: Backbone, tok, questions, T: int, qcache: bool, list_cap: int 
             keep = torch.arange(w)[None, :] < ln[:, None]
             dst = (o_start[rows][:, None] + torch.arange(w)[None, :])[keep]
             # rows of one question (consecutive after the stable length sort) share a tensor-core tile
-            mg = max(1, 128 // (w * rep))
+            mg = max(1, _lib.ATTN_CTA_SLOTS // (w * rep))
             grp = row_groups(rq, mg)
             passes.append(RowPass(PassSpec(ids=up(ids), pos=up(pos), own_hi=up(ln.to(torch.int32)),
                                            row_state=up(sidx[rq]), row_q=up(rq.to(torch.int32)), q_len=q_len_dev,

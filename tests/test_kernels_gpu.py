@@ -408,6 +408,34 @@ def test_prefix_attn_row_groups(cuda):
         assert (together[r, :n].float() - alone[r, :n].float()).abs().max() < 1e-2, r
 
 
+def test_prefix_attn_group_spans_both_query_tiles(cuda):
+    """A group of 4 option rows x 13 tokens x 4 heads (208 slots) fills both 128-slot query tiles of a CTA, one row
+    straddling the tile boundary: every row equals the row processed alone, and the oracle."""
+    g = syn.gen(23)
+    S, T, Hq, Hkv, D, t = 2, 300, 32, 8, 128, 13
+    ac = syn.attn_case(S=S, T=T, rows=4, t=t, Hq=Hq, Hkv=Hkv, D=D, seed=23)
+    Kq, Vq, ks, vs = _attn_inputs(cuda, ac)
+    R = ac.q.shape[0]
+    own_hi = torch.tensor([13, 7, 12, 1, 13, 9, 4, 13][:R], dtype=torch.int32)
+    args = dict(Kp=Kq, Vp=Vq, ksc=ks, vsc=vs, row_state=ac.row_state.to(cuda), own_hi=own_hi.to(cuda))
+    q, k, v = ac.q.to(cuda), ac.k.to(cuda), ac.v.to(cuda)
+    alone = _lib.prefix_attn(q, k, v, D ** -0.5, **args)
+    rs = ac.row_state.tolist()
+    groups = [(i, 4) for i in range(0, R, 4)]
+    assert all(len(set(rs[a:a + n])) == 1 for a, n in groups)
+    together = _lib.prefix_attn(q, k, v, D ** -0.5, row_groups=torch.tensor(groups, dtype=torch.int32, device=cuda),
+                                max_group_rows=4, **args)
+    Kp = ops.materialize_int8(Kq.cpu(), ks.cpu()[..., None].to(torch.float16))
+    Vp = ops.materialize_int8(Vq.cpu(), vs.cpu()[..., None].to(torch.float16))
+    for r in range(R):
+        n = int(own_hi[r])
+        assert (together[r, :n].float() - alone[r, :n].float()).abs().max() < 1e-2, r
+        s = rs[r]
+        ref = ops.split_attention(ac.q[r:r + 1, :n].transpose(1, 2), ac.k[r:r + 1, :n].transpose(1, 2),
+                                  ac.v[r:r + 1, :n].transpose(1, 2), Kp[s], Vp[s], None, D ** -0.5)
+        assert (together[r:r + 1, :n].cpu().float() - ref.transpose(1, 2)).abs().max() < 2e-2, r
+
+
 @pytest.mark.gpu
 def test_prefix_attn_int8_dequant_exact(cuda):
     """One visible prefix key per state (p_hi = p_lo + 1, no own key visible): its softmax weight is exactly 1, so
