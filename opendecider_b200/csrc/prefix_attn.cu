@@ -117,26 +117,6 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
-// 2^x for a pair of values on the FMA pipe (a quarter of the softmax exponentials go here, the rest to the MUFU ex2,
-// so neither unit bounds the block): x = j + f with j = rint(x) (the 1.5 * 2^23 addition rounds to an integer) and
-// f in [-1/2, 1/2]; 2^f by a degree-4 minimax polynomial in relative error (coefficients from fit_exp2.py, max error
-// 2.7e-6 in fp32 Horner); 2^j added into the exponent field. x is clamped to -125 so the result stays a normal
-// number: a masked key (x = -inf) weighs 2^-125 instead of 0, below anything a bf16 P.V or the fp32 row sum keeps.
-__device__ __forceinline__ float2 ex2_poly2(float2 x) {
-  constexpr float kC0 = 0.9999992847442627f, kC1 = 0.6931217908859253f, kC2 = 0.240247443318367f,
-                  kC3 = 0.05591785907745361f, kC4 = 0.009570102207362652f, kRound = 12582912.f;
-  x = make_float2(fmaxf(x.x, -125.f), fmaxf(x.y, -125.f));
-  const float2 t = __fadd2_rn(x, make_float2(kRound, kRound));
-  const float2 r = __fadd2_rn(t, make_float2(-kRound, -kRound));
-  const float2 f = __ffma2_rn(r, make_float2(-1.f, -1.f), x);
-  float2 p = __ffma2_rn(make_float2(kC4, kC4), f, make_float2(kC3, kC3));
-  p = __ffma2_rn(p, f, make_float2(kC2, kC2));
-  p = __ffma2_rn(p, f, make_float2(kC1, kC1));
-  p = __ffma2_rn(p, f, make_float2(kC0, kC0));
-  return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23)),
-                     __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
-}
-
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float r;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
@@ -590,7 +570,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
           } else {
             const float2 y = __ffma2_rn(make_float2(__uint_as_float(c[2 * k]), __uint_as_float(c[2 * k + 1])), sc2,
                                         nm2);
-            const float2 pp = (k & 3) == 3 ? ex2_poly2(y) : make_float2(ex2_approx(y.x), ex2_approx(y.y));
+            const float2 pp = make_float2(ex2_approx(y.x), ex2_approx(y.y));
             acc[k & 1] = __fadd2_rn(acc[k & 1], pp);
             pw[k] = pack_bf16(pp.x, pp.y);
           }
