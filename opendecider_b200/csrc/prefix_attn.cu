@@ -512,76 +512,100 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
             if (!((w >> k) & 1u) || k + 32 * ci < vis_lo || k + 32 * ci > vis_hi) c[k] = __float_as_uint(-INFINITY);
         }
       };
-      // pass 1: the row max over the block's four 32-key chunks, two at a time
-      uint32_t ca[32], cb[32];
-      float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        tmem_ld_32x32b_x32(tS + 64 * half, ca);
-        tmem_ld_32x32b_x32(tS + 64 * half + 32, cb);
-        tmem_ld_wait();
-        mask_chunk(ca, 2 * half);
-        mask_chunk(cb, 2 * half + 1);
-#pragma unroll
-        for (int k = 0; k < 32; k += 4) {
-          mq[0] = fmax3(mq[0], __uint_as_float(ca[k]), __uint_as_float(ca[k + 1]));
-          mq[1] = fmax3(mq[1], __uint_as_float(ca[k + 2]), __uint_as_float(ca[k + 3]));
-          mq[2] = fmax3(mq[2], __uint_as_float(cb[k]), __uint_as_float(cb[k + 1]));
-          mq[3] = fmax3(mq[3], __uint_as_float(cb[k + 2]), __uint_as_float(cb[k + 3]));
-        }
-      }
-      const float mloc = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
-      const float mb = mloc * scale;
-      float alpha = 1.f;
-      bool resc = false;
-      if (m_used == -INFINITY) {
-        m_used = mb;                                   // nothing accumulated yet: O and l are 0
-      } else if (mb > m_used + 8.f) {
-        alpha = ex2_approx(m_used - mb);
-        l_sum *= alpha;
-        m_used = mb;
-        resc = true;
-      }
-      // O_x may be rescaled now: P_x(j-1) V_{j-1} completed before S_x(j) was issued
-      if (__any_sync(0xffffffffu, resc)) {             // lazy rescale of the O row
+      // P = 2^(s * scale - m) in bf16 over the S columns (P chunk c lands on columns 16c..16c+15, which hold S chunk
+      // c / 2: already read), the row sum in fp32; returns the block's row max (scaled). One 32-key chunk of scores
+      // in registers at a time (the kernel's 13 warps cap a thread at 128 registers).
+      float2 acc[2];
+      auto p_pass = [&](float m) -> float {
+        const bool none = m == -INFINITY;              // no visible key so far: every weight is 0
+        const float2 sc2 = make_float2(scale, scale), nm2 = make_float2(-m, -m);
+        acc[0] = acc[1] = make_float2(0.f, 0.f);
+        float mq[2] = {-INFINITY, -INFINITY};
 #pragma unroll 1
-        for (int dc = 0; dc < D / 32; ++dc) {
-          uint32_t o[32];
-          tmem_ld_32x32b_x32(tO + dc * 32, o);
+        for (int ci = 0; ci < 4; ++ci) {
+          uint32_t cc[32];
+          tmem_ld_32x32b_x32(tS + 32 * ci, cc);
           tmem_ld_wait();
+          mask_chunk(cc, ci);
+          uint32_t pw[16];
 #pragma unroll
-          for (int k = 0; k < 32; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * alpha);
-          tmem_st_32x32b_x32(tO + dc * 32, o);
+          for (int k = 0; k < 16; ++k) {
+            const float e0 = __uint_as_float(cc[2 * k]), e1 = __uint_as_float(cc[2 * k + 1]);
+            mq[k & 1] = fmax3(mq[k & 1], e0, e1);
+            if (none) {
+              pw[k] = 0u;
+            } else {
+              const float2 y = __ffma2_rn(make_float2(e0, e1), sc2, nm2);
+              const float2 pp = make_float2(ex2_approx(y.x), ex2_approx(y.y));
+              acc[k & 1] = __fadd2_rn(acc[k & 1], pp);
+              pw[k] = pack_bf16(pp.x, pp.y);
+            }
+          }
+          tmem_st_32x32b_x16(tS + 16 * ci, pw);
         }
-      }
-      // pass 2: P = 2^(s * scale - m) in bf16 over the S columns (P chunk c lands on columns 16c..16c+15, which hold
-      // S chunk c / 2: already read), the row sum in fp32. One chunk of scores in registers at a time (the kernel's
-      // 13 warps cap a thread at 128 registers).
-      const bool none = m_used == -INFINITY;           // no visible key so far: every weight is 0
-      const float2 sc2 = make_float2(scale, scale), nm2 = make_float2(-m_used, -m_used);
-      float2 acc[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-      auto chunk = [&](uint32_t (&c)[32], int ci) {
-        mask_chunk(c, ci);
-        uint32_t pw[16];
+        return fmaxf(mq[0], mq[1]) * scale;
+      };
+      // O_x may be rescaled here: P_x(j-1) V_{j-1} completed before S_x(j) was issued
+      auto rescale_o = [&](float alpha, bool resc) {
+        if (__any_sync(0xffffffffu, resc)) {
+#pragma unroll 1
+          for (int dc = 0; dc < D / 32; ++dc) {
+            uint32_t o[32];
+            tmem_ld_32x32b_x32(tO + dc * 32, o);
+            tmem_ld_wait();
 #pragma unroll
-        for (int k = 0; k < 16; ++k) {
-          if (none) {
-            pw[k] = 0u;
-          } else {
-            const float2 y = __ffma2_rn(make_float2(__uint_as_float(c[2 * k]), __uint_as_float(c[2 * k + 1])), sc2,
-                                        nm2);
-            const float2 pp = make_float2(ex2_approx(y.x), ex2_approx(y.y));
-            acc[k & 1] = __fadd2_rn(acc[k & 1], pp);
-            pw[k] = pack_bf16(pp.x, pp.y);
+            for (int k = 0; k < 32; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * alpha);
+            tmem_st_32x32b_x32(tO + dc * 32, o);
           }
         }
-        tmem_st_32x32b_x16(tS + 16 * ci, pw);
       };
-#pragma unroll 1
-      for (int ci = 0; ci < 4; ++ci) {
-        tmem_ld_32x32b_x32(tS + 32 * ci, ca);
-        tmem_ld_wait();
-        chunk(ca, ci);
+      if (__any_sync(0xffffffffu, m_used == -INFINITY)) {
+        // a lane has no running max yet: the block's row max first (a separate pass over S), then P
+        uint32_t ca[32], cb[32];
+        float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          tmem_ld_32x32b_x32(tS + 64 * half, ca);
+          tmem_ld_32x32b_x32(tS + 64 * half + 32, cb);
+          tmem_ld_wait();
+          mask_chunk(ca, 2 * half);
+          mask_chunk(cb, 2 * half + 1);
+#pragma unroll
+          for (int k = 0; k < 32; k += 4) {
+            mq[0] = fmax3(mq[0], __uint_as_float(ca[k]), __uint_as_float(ca[k + 1]));
+            mq[1] = fmax3(mq[1], __uint_as_float(ca[k + 2]), __uint_as_float(ca[k + 3]));
+            mq[2] = fmax3(mq[2], __uint_as_float(cb[k]), __uint_as_float(cb[k + 1]));
+            mq[3] = fmax3(mq[3], __uint_as_float(cb[k + 2]), __uint_as_float(cb[k + 3]));
+          }
+        }
+        const float mb = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])) * scale;
+        float alpha = 1.f;
+        bool resc = false;
+        if (m_used == -INFINITY) {
+          m_used = mb;                                 // nothing accumulated yet: O and l are 0
+        } else if (mb > m_used + 8.f) {
+          alpha = ex2_approx(m_used - mb);
+          l_sum *= alpha;
+          m_used = mb;
+          resc = true;
+        }
+        rescale_o(alpha, resc);
+        p_pass(m_used);
+      } else {
+        // speculative: P against the running max; kept unless the block's max exceeds it by more than 2^8 (lazy
+        // rescale), in which case O and l are rescaled and P is recomputed (the overwritten P never reached the MMA)
+        const float mb = p_pass(m_used);
+        const bool redo = mb > m_used + 8.f;
+        if (__any_sync(0xffffffffu, redo)) {
+          float alpha = 1.f;
+          if (redo) {
+            alpha = ex2_approx(m_used - mb);
+            l_sum *= alpha;
+            m_used = mb;
+          }
+          rescale_o(alpha, redo);
+          p_pass(m_used);
+        }
       }
       l_sum += (acc[0].x + acc[0].y) + (acc[1].x + acc[1].y);
       tmem_st_wait();
