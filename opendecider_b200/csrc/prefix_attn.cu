@@ -392,7 +392,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
     // ================================================================== MMA issue (one thread)
     // Per block j and tile x: S_x(j) = Q_x K_j^T into the tile's S columns, then (once the tile's softmax has
     // written P_x(j) over them) O_x += P_x(j) V_j. P aliases S, so S_x(j+1) is issued only after P_x(j) V_j has
-    // completed; the other tile's MMAs fill the tensor core meanwhile.
+    // completed; the other tile's MMAs fill the tensor core meanwhile (A: P V, S; then B: P V, S).
     if (lane == 0 && nblk > 0) {
       constexpr uint32_t idesc_s = idesc_bf16(BM, BN, false);
       constexpr uint32_t idesc_o = idesc_bf16(BM, D, true);
@@ -415,65 +415,35 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
                      desc_sw128(sV + kk * 16 * 128, L::ATOM, 1024), idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
         mma_commit(&pv_done[x]);
       };
-      bool live = mbar_wait_spin(q_full, 0, abort_flag, P.err, kErrAttn | 17) &&
-                  mbar_wait_spin(&kfull[0], 0, abort_flag, P.err, kErrAttn | 3);
+      bool live = mbar_wait(q_full, 0, abort_flag, P.err, kErrAttn | 17) &&
+                  mbar_wait(&kfull[0], 0, abort_flag, P.err, kErrAttn | 3);
       if (live) {
         tc_fence_after();
         for (int x = 0; x < ntiles; ++x) issue_s(x, 0);
         mma_commit(&kempty[0]);
       }
-      // Each tile advances on its own as soon as its next step is ready: P V of block j once its softmax wrote P and
-      // V_j is staged; S of block j+1 once that P V completed and K_{j+1} is staged. K_j (V_j) is released after
-      // both tiles' S_j (P_j V_j) were issued. No step waits for the other tile; no progress for the bounded-wait
-      // limit ends the kernel with an error code.
-      int jn[kTiles] = {0, 0};                         // next block whose P V the tile issues
-      bool pend[kTiles] = {false, false};              // P V of block jn - 1 issued, S of block jn not yet
-      int s_cnt[MS] = {0, 0, 0, 0}, v_cnt[MS] = {0, 0, 0, 0};   // tiles that issued S_j / P_j V_j (slot j % MS)
-      long long last = clock64();
-      while (live) {
-        bool moved = false, done = true;
-#pragma unroll
-        for (int x = 0; x < kTiles; ++x) {
-          if (x >= ntiles) continue;
-          const int j = jn[x];
-          if (!pend[x]) {
-            if (j >= nblk) continue;
-            done = false;
-            if (mbar_try_wait(&p_full[x], j & 1) && mbar_try_wait(&vfull[j % VS], (j / VS) & 1)) {
-              tc_fence_after();
-              issue_pv(x, j);
-              if (++v_cnt[j % MS] == ntiles) {
-                v_cnt[j % MS] = 0;
-                mma_commit(&vempty[j % VS]);
-              }
-              jn[x] = j + 1;
-              pend[x] = j + 1 < nblk;
-              moved = true;
-            }
-          } else {
-            done = false;
-            // P_x(j-1) is read from the columns S_x(j) overwrites: that P V must have completed
-            if (mbar_try_wait(&pv_done[x], (j - 1) & 1) && mbar_try_wait(&kfull[j % KS], (j / KS) & 1)) {
-              tc_fence_after();
-              issue_s(x, j);
-              if (++s_cnt[j % MS] == ntiles) {
-                s_cnt[j % MS] = 0;
-                mma_commit(&kempty[j % KS]);
-              }
-              pend[x] = false;
-              moved = true;
-            }
+      for (int j = 0; j < nblk && live; ++j) {
+        const bool more = j + 1 < nblk;
+        if (!mbar_wait(&vfull[j % VS], (j / VS) & 1, abort_flag, P.err, kErrAttn | 5)) break;
+        if (more && !mbar_wait(&kfull[(j + 1) % KS], ((j + 1) / KS) & 1, abort_flag, P.err, kErrAttn | 4)) break;
+        for (int x = 0; x < ntiles && live; ++x) {
+          if (!mbar_wait(&p_full[x], j & 1, abort_flag, P.err, kErrAttn | 6)) {
+            live = false;
+            break;
           }
-        }
-        if (done) break;
-        if (moved) {
-          last = clock64();
-        } else if (*abort_flag) {
-          live = false;
-        } else if (clock64() - last > kWaitLimitCycles) {
-          *abort_flag = 1;
-          atomicCAS(P.err, 0, kErrAttn | 6);
-          live = false;
+          tc_fence_after();
+          issue_pv(x, j);
+          if (x == ntiles - 1) mma_commit(&vempty[j % VS]);
+          if (more) {
+            // P_x(j) is read from the columns S_x(j+1) overwrites: wait for the P V above to complete
+            if (!mbar_wait(&pv_done[x], j & 1, abort_flag, P.err, kErrAttn | 18)) {
+              live = false;
+              break;
+            }
+            tc_fence_after();
+            issue_s(x, j + 1);
+            if (x == ntiles - 1) mma_commit(&kempty[(j + 1) % KS]);
+          }
         }
       }
       // every MMA issued here has completed before TMEM is released (immediate unless aborted)
