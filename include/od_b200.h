@@ -155,8 +155,12 @@ OD_API int od_gate_quant(const void* o, const void* qkv, int64_t ldqkv, int64_t 
  * Output o (R, t, Hq, D) bf16 and optionally lse (R, Hq, t) fp32 (natural log, -inf when no key is visible; such
  * rows output 0, wide_attention.py:62-67). q (R, t, Hq, D) bf16. GQA: query head h reads kv head h / (Hq / Hkv).
  * row_groups (G, 2) int32 [first row, rows] (optional; NULL = every row alone): consecutive rows that share their
- * state and question and are processed together in one 128-slot tensor-core tile (rows x t x Hq/Hkv <= 128 when a
- * group has more than one row); they still attend only their own keys.
+ * state and question and are processed together by one CTA of up to two 128-slot tensor-core tiles
+ * (rows x t x Hq/Hkv <= 256 when a group has more than one row); they still attend only their own keys.
+ * dims.nsplit > 1 divides each state prefix among that many CTAs (for launches with fewer query tiles than SMs): each
+ * writes its partial O / l and LSE (fp32) to `workspace` and a second kernel merges them by log-sum-exp; the
+ * workspace (16-byte aligned) holds nsplit x R x t x Hq x (D + 1) floats. od_prefix_attn_plan picks nsplit for a
+ * GPU of num_sms SMs and returns the workspace size; workspace may be NULL when nsplit <= 1.
  * Every row sees the same key layout whatever its index or group: outputs do not depend on row order.
  * Runs on tcgen05 (S = Q K^T and O += P V in TMEM); head_dim 64 or 128.
  */
@@ -168,13 +172,17 @@ typedef struct {
   int64_t G;                    /* number of row groups (used when row_groups != NULL) */
   int max_group_rows;           /* largest group (used when row_groups != NULL) */
   int prefix_bf16;              /* 1: Kp/Vp are bf16 (materialised), 0: int8 + ksc/vsc */
+  int nsplit;                   /* CTAs per state prefix (0 or 1: one) */
 } od_attn_dims;
 
 OD_API int od_prefix_attn(const void* q, const void* Kp, const void* Vp, const void* ksc, const void* vsc,
                           const int32_t* row_state, const int32_t* p_lo, const int32_t* p_hi, const uint8_t* pmask,
                           const void* Kq, const void* Vq, const int32_t* row_q, const int32_t* q_len,
                           const void* k_own, const void* v_own, const int32_t* own_lo, const int32_t* own_hi,
-                          const int32_t* row_groups, void* o, float* lse, od_attn_dims dims, void* stream);
+                          const int32_t* row_groups, void* o, float* lse, od_attn_dims dims, void* workspace,
+                          int64_t workspace_bytes, void* stream);
+/* The split count for od_prefix_attn on a GPU of num_sms SMs and its workspace size in bytes (0 for one split). */
+OD_API int od_prefix_attn_plan(const od_attn_dims* dims, int num_sms, int* nsplit, int64_t* workspace_bytes);
 
 /* ---------------------------------------------------------------------------------------------------------------
  * A13: option readout, Decider._probs (decider.py:255-257):

@@ -28,7 +28,8 @@ class ODError(RuntimeError):
 class AttnDims(ctypes.Structure):
     _fields_ = [("R", c_int64), ("t", c_int64), ("S", c_int64), ("T", c_int64), ("NQ", c_int64), ("Lq", c_int64),
                 ("Hq", c_int), ("Hkv", c_int), ("D", c_int), ("scale_dtype", c_int), ("sm_scale", c_float),
-                ("G", c_int64), ("max_group_rows", c_int), ("prefix_bf16", c_int)]
+                ("G", c_int64), ("max_group_rows", c_int), ("prefix_bf16", c_int),
+                ("nsplit", c_int)]
 
 
 # exported symbol -> argument types (the declarations of include/od_b200.h)
@@ -48,7 +49,8 @@ SIGNATURES = {
     "od_qk_norm_rope": [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_float, c_int64, c_int,
                         c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p],
     "od_gate_quant": [c_void_p, c_void_p, c_int64, c_int64, c_int, c_int, c_void_p, c_void_p, c_void_p],
-    "od_prefix_attn": [c_void_p] * 20 + [AttnDims, c_void_p],
+    "od_prefix_attn": [c_void_p] * 20 + [AttnDims, c_void_p, c_int64, c_void_p],
+    "od_prefix_attn_plan": [POINTER(AttnDims), c_int, POINTER(c_int), POINTER(c_int64)],
     "od_readout": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p,
                    c_void_p],
 }
@@ -266,18 +268,34 @@ def gate_quant(o: torch.Tensor, qkv: torch.Tensor, Hq: int, D: int, q=None, s=No
 
 # query slots one od_prefix_attn CTA holds (two 128-slot tensor-core tiles): a row group may fill it
 ATTN_CTA_SLOTS = 256
+_PLANS: dict = {}
+
+
+def _attn_plan(dims: AttnDims, dev) -> tuple[int, int]:
+    """od_prefix_attn_plan for this GPU's SM count, cached per shape."""
+    key = (dev.index, dims.R, dims.t, dims.S, dims.T, dims.Hq, dims.Hkv, dims.D, dims.G, dims.max_group_rows)
+    got = _PLANS.get(key)
+    if got is None:
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        n, b = ctypes.c_int(1), ctypes.c_int64(0)
+        _check(load().od_prefix_attn_plan(ctypes.byref(dims), sms, ctypes.byref(n), ctypes.byref(b)),
+               "od_prefix_attn_plan")
+        got = _PLANS[key] = (n.value, b.value)
+    return got
 
 
 @_probed
 def prefix_attn(q: torch.Tensor, k_own: torch.Tensor, v_own: torch.Tensor, sm_scale: float, *,
                 Kp=None, Vp=None, ksc=None, vsc=None, row_state=None, p_lo=None, p_hi=None, pmask=None,
                 Kq=None, Vq=None, row_q=None, q_len=None, own_lo=None, own_hi=None, row_groups=None,
-                max_group_rows: int = 1, out=None, want_lse: bool = False):
+                max_group_rows: int = 1, out=None, want_lse: bool = False, nsplit: int | None = None):
     """q (R, t, Hq, D), own k/v (R, t, Hkv, D) bf16; state prefix Kp/Vp (S, Hkv, T, D): int8 + scales ksc/vsc
     (S, Hkv, T[, 1]), or bf16 (the materialised cache, scales unused);
     optional bf16 question prefix Kq/Vq (NQ, Lq, Hkv, D); own keys valid in [own_lo[r], own_hi[r]) and causal;
     row_groups (G, 2) int32 [first row, rows] of consecutive rows sharing state and question, processed together
-    (max_group_rows = the largest). Returns o (R, t, Hq, D) [, lse (R, Hq, t)]."""
+    (max_group_rows = the largest). nsplit: CTAs per state prefix (None: od_prefix_attn_plan's choice for this
+    GPU; the partial results then merge in a second kernel through a workspace from torch's allocator).
+    Returns o (R, t, Hq, D) [, lse (R, Hq, t)]."""
     dev = _need_cuda(q, k_own, v_own, Kp, Kq)
     R, t, Hq, D = q.shape
     Hkv = k_own.shape[2]
@@ -290,11 +308,20 @@ def prefix_attn(q: torch.Tensor, k_own: torch.Tensor, v_own: torch.Tensor, sm_sc
     sdt = _DT[ksc.dtype] if (ksc is not None and not pbf16) else OD_BF16
     G = row_groups.shape[0] if row_groups is not None else R
     dims = AttnDims(R, t, S, T, NQ, Lq, Hq, Hkv, D, sdt, sm_scale, G, max_group_rows if row_groups is not None else 1,
-                    1 if pbf16 else 0)
+                    1 if pbf16 else 0, 0)
+    ws, ws_bytes = None, 0
+    if Kp is not None:
+        if nsplit is None:
+            nsplit, ws_bytes = _attn_plan(dims, dev)
+        else:
+            ws_bytes = 4 * nsplit * R * t * Hq * (D + 1) if nsplit > 1 else 0
+        dims.nsplit = nsplit
+        if nsplit > 1:
+            ws = torch.empty(ws_bytes // 4, dtype=torch.float32, device=dev)
     _check(load().od_prefix_attn(_p(q), _p(Kp), _p(Vp), _p(None if pbf16 else ksc), _p(None if pbf16 else vsc), _p(row_state), _p(p_lo), _p(p_hi),
                                  _p(pmask), _p(Kq), _p(Vq), _p(row_q), _p(q_len), _p(k_own), _p(v_own), _p(own_lo),
                                  _p(own_hi), _p(row_groups),
-                                 _p(out), _p(lse), dims, _stream(dev)), "od_prefix_attn")
+                                 _p(out), _p(lse), dims, _p(ws), ws_bytes, _stream(dev)), "od_prefix_attn")
     return (out, lse) if want_lse else out
 
 

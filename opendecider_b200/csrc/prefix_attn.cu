@@ -41,8 +41,7 @@ constexpr int kProducer0 = 32 * (kSoftmaxWarps + 1);
 constexpr int kProducers = 32 * kProducerWarps;
 constexpr int kThreads = 32 * (kSoftmaxWarps + 1 + kProducerWarps);
 constexpr int BM = 128;              // query slots per tile (one per TMEM lane)
-constexpr int kTiles = 2;            // query tiles per CTA, ping-ponged on the tensor core
-constexpr int kCtaSlots = kTiles * BM;
+constexpr int kMaxTiles = 2;         // query tiles per CTA (NT = 1 or 2), ping-ponged on the tensor core
 constexpr int BN = 128;              // keys per block (one per producer thread)
 constexpr int KS = 2;                // K ring depth
 constexpr int VS = 2;                // V ring depth
@@ -53,25 +52,27 @@ constexpr uint32_t kTmemS = 0;       // S of tile x at column x * BN (BN fp32); 
 constexpr uint32_t kTmemO = 2 * BN;  // O of tile x at column kTmemO + x * 128 (D <= 128 fp32)
 constexpr int32_t kErrAttn = 0x5A0000;
 static_assert(BN == kProducers, "one key of a block per producer thread");
-static_assert(kTmemO + kTiles * 128 <= kTmemCols, "TMEM columns");
+static_assert(kTmemO + kMaxTiles * 128 <= kTmemCols, "TMEM columns");
 
-template <int D>
+template <int D, int NT>
 struct Layout {
   static constexpr int ATOM = 128 * 128;             // 128 rows x 128 B: one 64-column swizzle atom of a tile
   static constexpr int TILE = ATOM * (D / 64);       // 128 rows x D bf16 (a Q tile, a K block or a V block)
-  static constexpr int Q0 = 0;                       // kTiles query tiles (the A operand of S = Q K^T)
-  static constexpr int K0 = Q0 + kTiles * TILE;
+  static constexpr int RD = NT == 1 ? 2 : 1;         // raw int8 staging depth (one query tile leaves room for 2)
+  static constexpr int Q0 = 0;                       // NT query tiles (the A operand of S = Q K^T)
+  static constexpr int K0 = Q0 + NT * TILE;
   static constexpr int V0 = K0 + KS * TILE;
-  static constexpr int RAWK = V0 + VS * TILE;        // int8 K / V block staging: BN rows x D bytes, row-major
-  static constexpr int RAWV = RAWK + BN * D;
-  static constexpr int MASK0 = RAWV + BN * D;        // MS x 4 words: bit k of word w = key 32 w + k visible
+  static constexpr int RAW0 = V0 + VS * TILE;        // RD x (int8 K block, int8 V block): BN rows x D bytes each
+  static constexpr int MASK0 = RAW0 + RD * 2 * BN * D;   // MS x 4 words: bit k of word w = key 32 w + k visible
   static constexpr int BAR = MASK0 + MS * 16;        // mbarriers + TMEM holder + abort flag
-  static constexpr int BYTES = BAR + 256 + 1024;     // + alignment slack
+  static constexpr int BYTES = BAR + 512 + 1024;     // + alignment slack
   static __host__ __device__ constexpr int Q(int x) { return Q0 + x * TILE; }
   static __host__ __device__ constexpr int K(int b) { return K0 + b * TILE; }
   static __host__ __device__ constexpr int V(int b) { return V0 + b * TILE; }
+  static __host__ __device__ constexpr int RAWK(int r) { return RAW0 + r * 2 * BN * D; }
+  static __host__ __device__ constexpr int RAWV(int r) { return RAWK(r) + BN * D; }
 };
-static_assert(Layout<128>::BYTES <= 232448, "shared memory");
+static_assert(Layout<128, 1>::BYTES <= 232448 && Layout<128, 2>::BYTES <= 232448, "shared memory");
 
 struct Params {
   CUtensorMap map_ko, map_vo, map_kq, map_vq;   // bf16 (rows, Hkv*D) views of own / question K and V, 64x128 boxes
@@ -98,9 +99,12 @@ struct Params {
   __nv_bfloat16* o;
   float* lse;
   int32_t* err;
-  int64_t t, T, Lq;
+  int64_t R, t, T, Lq;
   int Hq, Hkv, rep, tiles_per_group;
   int prefix_bf16;
+  int nsplit;                                   // CTAs sharing one query tile's state prefix (grid z)
+  float* part_o;                                // nsplit > 1: per split, O / l (fp32, the layout of o) ...
+  float* part_lse;                              // ... and the natural-log LSE (the layout of lse)
   float scale_log2;
 };
 
@@ -152,7 +156,7 @@ template <typename TS, int D>
 __device__ __forceinline__ void convert_piece(const uint8_t* raw, const uint32_t (&sc)[Piece<D>::N], uint8_t* dst,
                                               int pt) {
   constexpr int CPR = D / 16;
-  constexpr int ATOM = Layout<D>::ATOM;
+  constexpr int ATOM = Layout<D, 1>::ATOM;
 #pragma unroll
   for (int it = 0; it < Piece<D>::N; ++it) {
     const int c = pt + it * kProducers;
@@ -184,9 +188,11 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
   return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, err, code));
 }
 
-template <typename TS, int D>
+template <typename TS, int D, int NT>
 __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_constant__ Params P) {
-  using L = Layout<D>;
+  using L = Layout<D, NT>;
+  constexpr int RD = L::RD;
+  constexpr int kCtaSlots = NT * BM;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // pointer arithmetic on the shared array (not an integer cast) keeps the shared address space visible to the
   // compiler, so accesses compile to shared-memory instructions rather than generic ones
@@ -197,15 +203,15 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
   uint64_t* vfull = kempty + KS;           // [VS] producers (+ TMA bytes) -> MMA
   uint64_t* vempty = vfull + VS;           // [VS] MMA (P_j V_j of both tiles complete) -> producers
   uint64_t* mfull = vempty + VS;           // [MS] producer warps (mask words written) -> softmax
-  uint64_t* s_full = mfull + MS;           // [kTiles] MMA (S_j of the tile complete) -> the tile's softmax
-  uint64_t* p_full = s_full + kTiles;      // [kTiles] the tile's softmax (P_j in TMEM, O rescaled) -> MMA
-  uint64_t* pv_done = p_full + kTiles;     // [kTiles] MMA (P_j V_j of the tile complete) -> MMA, softmax epilogue
-  uint64_t* rawk_full = pv_done + kTiles;  // TMA (raw int8 K block) -> producers
-  uint64_t* rawk_empty = rawk_full + 1;    // producers (raw K converted) -> the TMA-issuing producer
-  uint64_t* rawv_full = rawk_full + 2;
-  uint64_t* rawv_empty = rawk_full + 3;
-  uint64_t* q_full = rawk_full + 4;        // softmax warps (both Q tiles in shared memory) -> MMA
-  uint64_t* drain = rawk_full + 5;
+  uint64_t* s_full = mfull + MS;           // [NT] MMA (S_j of the tile complete) -> the tile's softmax
+  uint64_t* p_full = s_full + NT;          // [NT] the tile's softmax (P_j in TMEM, O rescaled) -> MMA
+  uint64_t* pv_done = p_full + NT;         // [NT] MMA (P_j V_j of the tile complete) -> MMA, softmax epilogue
+  uint64_t* rawk_full = pv_done + NT;      // [RD] TMA (raw int8 K block) -> producers
+  uint64_t* rawk_empty = rawk_full + RD;   // [RD] producers (raw K converted) -> the TMA-issuing producer
+  uint64_t* rawv_full = rawk_empty + RD;   // [RD]
+  uint64_t* rawv_empty = rawv_full + RD;   // [RD]
+  uint64_t* q_full = rawv_empty + RD;      // softmax warps (the Q tiles in shared memory) -> MMA
+  uint64_t* drain = q_full + 1;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   uint32_t* masks = reinterpret_cast<uint32_t*>(sm + L::MASK0);
@@ -221,7 +227,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
   const int slots = nr * slots_row;
   const int s0 = tile * kCtaSlots;
   if (s0 >= slots) return;                            // uniform: before any barrier or allocation
-  const int ntiles = slots - s0 > BM ? 2 : 1;         // the second query tile only when it holds a slot
+  const int ntiles = NT == 2 && slots - s0 > BM ? 2 : 1;   // the second query tile only when it holds a slot
+  const int split = blockIdx.z;
 
   if (tid == 0) {
     for (int b = 0; b < KS; ++b) {
@@ -233,16 +240,18 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
       mbar_init(&vempty[b], 1);
     }
     for (int b = 0; b < MS; ++b) mbar_init(&mfull[b], kProducerWarps);
-    for (int x = 0; x < kTiles; ++x) {
+    for (int x = 0; x < NT; ++x) {
       mbar_init(&s_full[x], 1);
       mbar_init(&p_full[x], BM);
       mbar_init(&pv_done[x], 1);
     }
-    mbar_init(rawk_full, 1);
-    mbar_init(rawk_empty, kProducers);
-    mbar_init(rawv_full, 1);
-    mbar_init(rawv_empty, kProducers);
-    mbar_init(q_full, 32 * kSoftmaxWarps);
+    for (int r = 0; r < RD; ++r) {
+      mbar_init(&rawk_full[r], 1);
+      mbar_init(&rawk_empty[r], kProducers);
+      mbar_init(&rawv_full[r], 1);
+      mbar_init(&rawv_empty[r], kProducers);
+    }
+    mbar_init(q_full, 32 * 4 * NT);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -256,22 +265,30 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
   const uint32_t tmem = *tmem_holder;
 
   // ---- key segments (the group's rows share their state and question); every role derives the same schedule
+  // with nsplit > 1 the state prefix's blocks are divided among the splits in contiguous runs and the last split
+  // also takes the question prefix and the own keys
   int nb1 = 0, lo1 = 0, hi1 = 0, st = 0;
+  const bool last_split = split == P.nsplit - 1;
   if (P.Kp) {
     st = P.row_state[row0];
     lo1 = P.p_lo ? P.p_lo[st] : 0;
     hi1 = P.p_hi ? P.p_hi[st] : static_cast<int>(P.T);
-    nb1 = hi1 > lo1 ? (hi1 - lo1 + BN - 1) / BN : 0;
+    const int all = hi1 > lo1 ? (hi1 - lo1 + BN - 1) / BN : 0;
+    const int per = (all + P.nsplit - 1) / P.nsplit;
+    const int b0 = min(all, split * per), b1 = min(all, b0 + per);
+    nb1 = b1 - b0;
+    lo1 += b0 * BN;
+    hi1 = min(hi1, lo1 + nb1 * BN);
   }
   int nb2 = 0, n2 = 0, qr = 0;
-  if (P.Kq) {
+  if (P.Kq && last_split) {
     qr = P.row_q[row0];
     n2 = P.q_len[qr];
     nb2 = (n2 + BN - 1) / BN;
   }
   // own keys, flattened (row a, token j) -> a * t + j; a single long row only needs keys up to the CTA's last token
-  int own_begin = 0, own_end = nr * t;
-  if (nr == 1) {
+  int own_begin = 0, own_end = last_split ? nr * t : 0;
+  if (nr == 1 && last_split) {
     const int lo = P.own_lo ? P.own_lo[row0] : 0;
     const int last_tok = min(t - 1, (min(slots, s0 + kCtaSlots) - 1) / rep);
     own_begin = (lo / BN) * BN;
@@ -300,11 +317,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
     if (nb1 > 0 && !P.prefix_bf16) {
       load_scales<D>(skc, pt, ks1, lo1, hi1);
       load_scales<D>(svc, pt, vs1, lo1, hi1);
-      if (pt == 0) {
-        mbar_arrive_expect_tx(rawk_full, BN * D);
-        tma_load_2d(sm + L::RAWK, &P.map_kp, rawk_full, 0, prow + lo1);
-        mbar_arrive_expect_tx(rawv_full, BN * D);
-        tma_load_2d(sm + L::RAWV, &P.map_vp, rawv_full, 0, prow + lo1);
+      if (pt == 0) {                                  // the first RD raw blocks in flight
+        for (int r = 0; r < RD && r < nb1; ++r) {
+          mbar_arrive_expect_tx(&rawk_full[r], BN * D);
+          tma_load_2d(sm + L::RAWK(r), &P.map_kp, &rawk_full[r], 0, prow + lo1 + r * BN);
+          mbar_arrive_expect_tx(&rawv_full[r], BN * D);
+          tma_load_2d(sm + L::RAWV(r), &P.map_vp, &rawv_full[r], 0, prow + lo1 + r * BN);
+        }
       }
     }
     for (int j = 0; j < nblk; ++j) {
@@ -336,16 +355,15 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
       }
       uint8_t* sK = sm + L::K(bk);
       if (i8) {
-        if (!mbar_wait(rawk_full, j & 1, abort_flag, P.err, kErrAttn | 13)) break;
-        convert_piece<TS, D>(sm + L::RAWK, skc, sK, pt);
-        mbar_arrive(rawk_empty);
-        if (j + 1 < nb1) {
-          load_scales<D>(skc, pt, ks1, k0 + BN, hi1);
-          if (pt == 0) {                              // refill the staging once every thread has converted it
-            if (!mbar_wait(rawk_empty, j & 1, abort_flag, P.err, kErrAttn | 14)) break;
-            mbar_arrive_expect_tx(rawk_full, BN * D);
-            tma_load_2d(sm + L::RAWK, &P.map_kp, rawk_full, 0, prow + k0 + BN);
-          }
+        const int r = j % RD;
+        if (!mbar_wait(&rawk_full[r], (j / RD) & 1, abort_flag, P.err, kErrAttn | 13)) break;
+        convert_piece<TS, D>(sm + L::RAWK(r), skc, sK, pt);
+        mbar_arrive(&rawk_empty[r]);
+        if (j + 1 < nb1) load_scales<D>(skc, pt, ks1, k0 + BN, hi1);
+        if (j + RD < nb1 && pt == 0) {                // refill the staging slot once every thread has converted it
+          if (!mbar_wait(&rawk_empty[r], (j / RD) & 1, abort_flag, P.err, kErrAttn | 14)) break;
+          mbar_arrive_expect_tx(&rawk_full[r], BN * D);
+          tma_load_2d(sm + L::RAWK(r), &P.map_kp, &rawk_full[r], 0, prow + k0 + RD * BN);
         }
         fence_proxy_async_smem();
         mbar_arrive(&kfull[bk]);
@@ -364,16 +382,15 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
       if (j >= VS && !mbar_wait(&vempty[bv], ((j / VS) - 1) & 1, abort_flag, P.err, kErrAttn | 2)) break;
       uint8_t* sV = sm + L::V(bv);
       if (i8) {
-        if (!mbar_wait(rawv_full, j & 1, abort_flag, P.err, kErrAttn | 15)) break;
-        convert_piece<TS, D>(sm + L::RAWV, svc, sV, pt);
-        mbar_arrive(rawv_empty);
-        if (j + 1 < nb1) {
-          load_scales<D>(svc, pt, vs1, k0 + BN, hi1);
-          if (pt == 0) {
-            if (!mbar_wait(rawv_empty, j & 1, abort_flag, P.err, kErrAttn | 16)) break;
-            mbar_arrive_expect_tx(rawv_full, BN * D);
-            tma_load_2d(sm + L::RAWV, &P.map_vp, rawv_full, 0, prow + k0 + BN);
-          }
+        const int r = j % RD;
+        if (!mbar_wait(&rawv_full[r], (j / RD) & 1, abort_flag, P.err, kErrAttn | 15)) break;
+        convert_piece<TS, D>(sm + L::RAWV(r), svc, sV, pt);
+        mbar_arrive(&rawv_empty[r]);
+        if (j + 1 < nb1) load_scales<D>(svc, pt, vs1, k0 + BN, hi1);
+        if (j + RD < nb1 && pt == 0) {
+          if (!mbar_wait(&rawv_empty[r], (j / RD) & 1, abort_flag, P.err, kErrAttn | 16)) break;
+          mbar_arrive_expect_tx(&rawv_full[r], BN * D);
+          tma_load_2d(sm + L::RAWV(r), &P.map_vp, &rawv_full[r], 0, prow + k0 + RD * BN);
         }
         fence_proxy_async_smem();
         mbar_arrive(&vfull[bv]);
@@ -465,7 +482,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
     const uint32_t tS = tmem + lane_off + kTmemS + x * BN;
     const uint32_t tO = tmem + lane_off + kTmemO + x * 128;
     const float scale = P.scale_log2;
-    {
+    if (x < NT) {
       // this slot's Q row into the tile's shared-memory A operand (128-byte swizzled, K-major)
       uint8_t* dq = sm + L::Q(x);
       if (my_valid) {
@@ -620,6 +637,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
         tc_fence_after();
         const float inv = l_sum > 0.f ? 1.0f / l_sum : 0.f;
         const int64_t orow = ((static_cast<int64_t>(row0 + a_my) * t + i_my) * P.Hq + g * rep + hh_my) * D;
+        const int64_t lrow = (static_cast<int64_t>(row0 + a_my) * P.Hq + g * rep + hh_my) * t + i_my;
+        const float lse_v = l_sum > 0.f ? (m_used + log2f(l_sum)) * 0.6931471805599453f : -INFINITY;
+        // one split: bf16 O / l (and the LSE); several: this split's fp32 O / l and LSE, merged by od_attn_merge
+        const int64_t n_l = P.R * P.t * P.Hq, n_o = n_l * D;
 #pragma unroll 1
         for (int dc = 0; dc < D / 32; ++dc) {
           uint32_t o[32];
@@ -631,18 +652,29 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
             for (int k = 0; k < 32; ++k) o[k] = 0u;
           }
           if (my_valid) {
-            uint32_t w[16];
+            if (P.nsplit > 1) {
+              float4* dst = reinterpret_cast<float4*>(P.part_o + split * n_o + orow + dc * 32);
 #pragma unroll
-            for (int k = 0; k < 16; ++k)
-              w[k] = pack_bf16(__uint_as_float(o[2 * k]) * inv, __uint_as_float(o[2 * k + 1]) * inv);
-            uint4* dst = reinterpret_cast<uint4*>(P.o + orow + dc * 32);
+              for (int k = 0; k < 8; ++k)
+                dst[k] = make_float4(__uint_as_float(o[4 * k]) * inv, __uint_as_float(o[4 * k + 1]) * inv,
+                                     __uint_as_float(o[4 * k + 2]) * inv, __uint_as_float(o[4 * k + 3]) * inv);
+            } else {
+              uint32_t w[16];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) dst[k] = make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+              for (int k = 0; k < 16; ++k)
+                w[k] = pack_bf16(__uint_as_float(o[2 * k]) * inv, __uint_as_float(o[2 * k + 1]) * inv);
+              uint4* dst = reinterpret_cast<uint4*>(P.o + orow + dc * 32);
+#pragma unroll
+              for (int k = 0; k < 4; ++k) dst[k] = make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+            }
           }
         }
-        if (P.lse && my_valid)
-          P.lse[(static_cast<int64_t>(row0 + a_my) * P.Hq + g * rep + hh_my) * t + i_my] =
-              l_sum > 0.f ? (m_used + log2f(l_sum)) * 0.6931471805599453f : -INFINITY;
+        if (my_valid) {
+          if (P.nsplit > 1)
+            P.part_lse[split * n_l + lrow] = lse_v;
+          else if (P.lse)
+            P.lse[lrow] = lse_v;
+        }
       }
     }
     tc_fence_before();
@@ -696,19 +728,77 @@ int make_map_i8(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows
   return OD_OK;
 }
 
-template <typename TS, int D>
+template <typename TS, int D, int NT>
 int launch_attn(const Params& P, dim3 grid, cudaStream_t st) {
   static bool attr[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr[dev]) {
-    OD_CUDA_TRY(cudaFuncSetAttribute(prefix_attn_kernel<TS, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     Layout<D>::BYTES));
+    OD_CUDA_TRY(cudaFuncSetAttribute(prefix_attn_kernel<TS, D, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     Layout<D, NT>::BYTES));
     attr[dev] = true;
   }
-  prefix_attn_kernel<TS, D><<<grid, kThreads, Layout<D>::BYTES, st>>>(P);
+  prefix_attn_kernel<TS, D, NT><<<grid, kThreads, Layout<D, NT>::BYTES, st>>>(P);
   OD_LAUNCH_CHECK();
   return ok();
+}
+
+// The splits of a query row merged exactly by log-sum-exp (the Hydragen merge of prefix_attn._split_attention):
+// O = sum_s w_s O_s / sum_s w_s, w_s = exp(lse_s - max lse), LSE = max lse + log sum_s w_s. One warp per output
+// row (row, token, head), D / 32 elements per lane.
+template <int D>
+__global__ void __launch_bounds__(256) attn_merge_kernel(const float* __restrict__ part_o,
+                                                         const float* __restrict__ part_lse, int nsplit,
+                                                         int64_t n_rows, int t, int Hq, __nv_bfloat16* __restrict__ o,
+                                                         float* __restrict__ lse) {
+  constexpr int E = D / 32;
+  const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= n_rows) return;
+  const int64_t h = row % Hq, ri = row / Hq;
+  const int64_t lrow = ((ri / t) * Hq + h) * t + ri % t;
+  float m = -INFINITY;
+  for (int sp = 0; sp < nsplit; ++sp) m = fmaxf(m, __ldg(part_lse + sp * n_rows + lrow));
+  float acc[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) acc[e] = 0.f;
+  float wsum = 0.f;
+  if (m != -INFINITY) {
+    for (int sp = 0; sp < nsplit; ++sp) {
+      const float w = expf(__ldg(part_lse + sp * n_rows + lrow) - m);
+      wsum += w;
+      const float* src = part_o + (sp * n_rows + row) * D + lane * E;
+#pragma unroll
+      for (int e = 0; e < E; ++e) acc[e] = fmaf(w, __ldg(src + e), acc[e]);
+    }
+  }
+  const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+  __nv_bfloat16* dst = o + row * D + lane * E;
+#pragma unroll
+  for (int e = 0; e < E; e += 2) *reinterpret_cast<uint32_t*>(dst + e) = pack_bf16(acc[e] * inv, acc[e + 1] * inv);
+  if (lse && lane == 0) lse[lrow] = wsum > 0.f ? m + logf(wsum) : -INFINITY;
+}
+
+// Splits of the state prefix: the count minimising (waves of CTAs) x (blocks per CTA + 2 blocks of fixed cost);
+// 1 when the query tiles alone fill the GPU.
+int plan_splits(int64_t ctas, int64_t prefix_blocks, int num_sms) {
+  if (ctas <= 0 || prefix_blocks < 4 || num_sms <= 0) return 1;
+  int best = 1;
+  double best_t = 1e300;
+  for (int n = 1; n <= 8 && n <= prefix_blocks / 2; ++n) {
+    const double waves = static_cast<double>((ctas * n + num_sms - 1) / num_sms);
+    const double tm = waves * (static_cast<double>((prefix_blocks + n - 1) / n) + 2.0);
+    if (tm < best_t * 0.97) {
+      best_t = tm;
+      best = n;
+    }
+  }
+  return best;
+}
+
+int64_t group_slots(const od_attn_dims& d) {
+  const int64_t rows = d.max_group_rows > 0 ? d.max_group_rows : 1;
+  return rows * d.t * (d.Hq / (d.Hkv > 0 ? d.Hkv : 1));
 }
 
 }  // namespace
@@ -720,7 +810,8 @@ extern "C" int od_prefix_attn(const void* q, const void* Kp, const void* Vp, con
                               const int32_t* row_state, const int32_t* p_lo, const int32_t* p_hi, const uint8_t* pmask,
                               const void* Kq, const void* Vq, const int32_t* row_q, const int32_t* q_len,
                               const void* k_own, const void* v_own, const int32_t* own_lo, const int32_t* own_hi,
-                              const int32_t* row_groups, void* o, float* lse, od_attn_dims dims, void* stream) {
+                              const int32_t* row_groups, void* o, float* lse, od_attn_dims dims, void* workspace,
+                              int64_t workspace_bytes, void* stream) {
   OD_REQUIRE(q && k_own && v_own && o, "od_prefix_attn: null pointer");
   OD_REQUIRE(dims.D == 64 || dims.D == 128, "od_prefix_attn: head_dim %d not in {64, 128}", dims.D);
   OD_REQUIRE(dims.Hq > 0 && dims.Hkv > 0 && dims.Hq % dims.Hkv == 0, "od_prefix_attn: bad head counts");
@@ -737,9 +828,19 @@ extern "C" int od_prefix_attn(const void* q, const void* Kp, const void* Vp, con
   const int64_t G = row_groups ? dims.G : dims.R;
   const int64_t max_rows = row_groups ? dims.max_group_rows : 1;
   OD_REQUIRE(G >= 0 && max_rows >= 1, "od_prefix_attn: bad row groups");
-  OD_REQUIRE(max_rows == 1 || max_rows * dims.t * rep <= kCtaSlots,
+  OD_REQUIRE(max_rows == 1 || max_rows * dims.t * rep <= kMaxTiles * BM,
              "od_prefix_attn: a group of several rows must fit one CTA's %d slots (rows %lld x t %lld x rep %d)",
-             kCtaSlots, (long long)max_rows, (long long)dims.t, rep);
+             kMaxTiles * BM, (long long)max_rows, (long long)dims.t, rep);
+  const int64_t gslots = max_rows * dims.t * rep;
+  const int NT = gslots <= BM ? 1 : 2;                // one query tile per CTA frees room for deeper int8 staging
+  const int nsplit = Kp && dims.nsplit > 1 ? dims.nsplit : 1;
+  OD_REQUIRE(nsplit <= 64, "od_prefix_attn: nsplit %d above 64", nsplit);
+  const int64_t n_part = static_cast<int64_t>(dims.R) * dims.t * dims.Hq;
+  if (nsplit > 1)
+    OD_REQUIRE(workspace && aligned16(workspace) &&
+                   workspace_bytes >= static_cast<int64_t>(sizeof(float)) * nsplit * n_part * (dims.D + 1),
+               "od_prefix_attn: %d splits need a 16-byte aligned workspace of %lld bytes (od_prefix_attn_plan)", nsplit,
+               (long long)(static_cast<int64_t>(sizeof(float)) * nsplit * n_part * (dims.D + 1)));
   if (G == 0 || dims.t == 0) return ok();
   int32_t* err = device_error_word();
   if (!err) return fail(OD_ECUDA, "od_prefix_attn: no device error word");
@@ -767,13 +868,19 @@ extern "C" int od_prefix_attn(const void* q, const void* Kp, const void* Vp, con
   P.o = static_cast<__nv_bfloat16*>(o);
   P.lse = lse;
   P.err = err;
+  P.R = dims.R;
   P.t = dims.t;
   P.T = dims.T;
   P.Lq = dims.Lq;
   P.Hq = dims.Hq;
   P.Hkv = dims.Hkv;
   P.rep = rep;
-  P.tiles_per_group = static_cast<int>((max_rows * dims.t * rep + kCtaSlots - 1) / kCtaSlots);
+  P.tiles_per_group = static_cast<int>((gslots + NT * BM - 1) / (NT * BM));
+  P.nsplit = nsplit;
+  if (nsplit > 1) {
+    P.part_o = static_cast<float*>(workspace);
+    P.part_lse = P.part_o + static_cast<int64_t>(nsplit) * n_part * dims.D;
+  }
   P.scale_log2 = dims.sm_scale * 1.4426950408889634f;
   {
     const uint64_t cols = static_cast<uint64_t>(dims.Hkv) * dims.D;
@@ -801,13 +908,42 @@ extern "C" int od_prefix_attn(const void* q, const void* Kp, const void* Vp, con
   }
   const int64_t gx = G * P.tiles_per_group;
   OD_REQUIRE(gx < (1LL << 31) && dims.Hkv < 65536, "od_prefix_attn: grid too large");
-  dim3 grid(static_cast<unsigned>(gx), dims.Hkv);
+  dim3 grid(static_cast<unsigned>(gx), dims.Hkv, nsplit);
   cudaStream_t st = as_stream(stream);
   const bool half_scale = Kp && !pbf16 && dims.scale_dtype == OD_F16;
-  if (dims.D == 128) {
-    if (half_scale) return launch_attn<__half, 128>(P, grid, st);
-    return launch_attn<__nv_bfloat16, 128>(P, grid, st);
-  }
-  if (half_scale) return launch_attn<__half, 64>(P, grid, st);
-  return launch_attn<__nv_bfloat16, 64>(P, grid, st);
+  int rc = OD_OK;
+#define OD_ATTN(NT_)                                                                                          \
+  (dims.D == 128 ? (half_scale ? launch_attn<__half, 128, NT_>(P, grid, st)                                \
+                               : launch_attn<__nv_bfloat16, 128, NT_>(P, grid, st))                        \
+                 : (half_scale ? launch_attn<__half, 64, NT_>(P, grid, st)                                 \
+                               : launch_attn<__nv_bfloat16, 64, NT_>(P, grid, st)))
+  rc = NT == 1 ? OD_ATTN(1) : OD_ATTN(2);
+#undef OD_ATTN
+  if (rc != OD_OK || nsplit == 1) return rc;
+  const unsigned mb = static_cast<unsigned>((n_part * 32 + 255) / 256);
+  if (dims.D == 128)
+    attn_merge_kernel<128><<<mb, 256, 0, st>>>(P.part_o, P.part_lse, nsplit, n_part, static_cast<int>(dims.t),
+                                                dims.Hq, P.o, lse);
+  else
+    attn_merge_kernel<64><<<mb, 256, 0, st>>>(P.part_o, P.part_lse, nsplit, n_part, static_cast<int>(dims.t),
+                                               dims.Hq, P.o, lse);
+  OD_LAUNCH_CHECK();
+  return ok();
+}
+
+extern "C" int od_prefix_attn_plan(const od_attn_dims* dims, int num_sms, int* nsplit, int64_t* workspace_bytes) {
+  OD_REQUIRE(dims && nsplit && workspace_bytes, "od_prefix_attn_plan: null pointer");
+  *nsplit = 1;
+  *workspace_bytes = 0;
+  if (dims->S <= 0 || dims->T <= 0 || dims->Hkv <= 0) return ok();
+  const int64_t gslots = group_slots(*dims);
+  const int64_t cta_slots = gslots <= BM ? BM : kMaxTiles * BM;
+  const int64_t G = dims->max_group_rows > 1 ? dims->G : dims->R;
+  const int64_t ctas = G * ((gslots + cta_slots - 1) / cta_slots) * dims->Hkv;
+  const int n = plan_splits(ctas, (dims->T + BN - 1) / BN, num_sms);
+  *nsplit = n;
+  if (n > 1)
+    *workspace_bytes = static_cast<int64_t>(sizeof(float)) * n * static_cast<int64_t>(dims->R) * dims->t * dims->Hq *
+                       (dims->D + 1);
+  return ok();
 }

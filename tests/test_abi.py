@@ -42,3 +42,20 @@ def test_cpu_tensors_are_rejected():
     import torch
     with pytest.raises(_lib.ODError):
         _lib.quant_rows(torch.zeros(4, 8, dtype=torch.bfloat16))
+
+
+def test_attention_split_plan_is_host_only():
+    """od_prefix_attn_plan is host arithmetic (no GPU): a launch with fewer query tiles than SMs splits the state
+    prefix and gets a workspace of nsplit x R x t x Hq x (D + 1) floats; a full launch or no prefix does not."""
+    lib = _lib.load()
+
+    def plan(R, t, S, T, Hq=32, Hkv=8, D=128, G=0, mg=1, sms=148):
+        dims = _lib.AttnDims(R, t, S, T, 0, 0, Hq, Hkv, D, _lib.OD_BF16, D ** -0.5, G or R, mg, 0, 0)
+        n, b = ctypes.c_int(0), ctypes.c_int64(-1)
+        assert lib.od_prefix_attn_plan(ctypes.byref(dims), sms, ctypes.byref(n), ctypes.byref(b)) == 0
+        return n.value, b.value
+
+    n, b = plan(R=1, t=2, S=1, T=4096)                       # 8 query tiles on 148 SMs
+    assert n > 1 and b == 4 * n * 1 * 2 * 32 * 129
+    assert plan(R=64 * 64, t=16, S=64, T=4096, G=64 * 16, mg=4) == (1, 0)   # thousands of tiles
+    assert plan(R=8, t=2, S=0, T=0) == (1, 0)                 # no state prefix

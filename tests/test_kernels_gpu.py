@@ -514,3 +514,40 @@ def test_prefix_attn_materialised_prefix_identical(cuda):
     ob, lb = _lib.prefix_attn(q, k, v, D ** -0.5, Kp=Kb, Vp=Vb, **common)
     assert torch.equal(o8, ob)
     assert torch.equal(l8, lb)
+
+
+@pytest.mark.parametrize("nsplit", [2, 3, 5])
+def test_prefix_attn_split_prefix_merges_exactly(cuda, nsplit):
+    """The state prefix divided among several CTAs, partials merged by log-sum-exp: the same outputs and LSE as one
+    CTA per tile (fp32 partials: within bf16 rounding), with a left-padded state, a question prefix and own keys."""
+    g = syn.gen(31)
+    S, T, Hq, Hkv, D, t = 2, 1000, 32, 8, 128, 3
+    ac = syn.attn_case(S=S, T=T, rows=3, t=t, Hq=Hq, Hkv=Hkv, D=D, seed=31)
+    Kq, Vq, ks, vs = _attn_inputs(cuda, ac)
+    NQ, Lq = 2, 20
+    Kqn = torch.randn(NQ, Lq, Hkv, D, generator=g).to(torch.bfloat16).to(cuda)
+    Vqn = torch.randn(NQ, Lq, Hkv, D, generator=g).to(torch.bfloat16).to(cuda)
+    args = dict(Kp=Kq, Vp=Vq, ksc=ks, vsc=vs, row_state=ac.row_state.to(cuda),
+                p_lo=torch.tensor([0, 77], dtype=torch.int32, device=cuda),
+                p_hi=torch.tensor([1000, 905], dtype=torch.int32, device=cuda), Kq=Kqn, Vq=Vqn,
+                row_q=torch.tensor([0, 1, 0, 1, 0, 1], dtype=torch.int32, device=cuda),
+                q_len=torch.tensor([20, 9], dtype=torch.int32, device=cuda), want_lse=True)
+    q, k, v = ac.q.to(cuda), ac.k.to(cuda), ac.v.to(cuda)
+    o1, l1 = _lib.prefix_attn(q, k, v, D ** -0.5, nsplit=1, **args)
+    on, ln = _lib.prefix_attn(q, k, v, D ** -0.5, nsplit=nsplit, **args)
+    assert _lib.device_error(cuda) == 0
+    assert (o1.float() - on.float()).abs().max() < 1.6e-2
+    assert (l1 - ln).abs().max() < 1e-4
+
+
+def test_prefix_attn_plan_splits_small_launches(cuda):
+    """A launch with fewer query tiles than SMs is split (one request, 8 KV heads, a 4096-token state); a full
+    one is not."""
+    ac = syn.attn_case(S=1, T=4096, rows=1, t=2, Hq=32, Hkv=8, D=128, seed=3)
+    Kq, Vq, ks, vs = _attn_inputs(cuda, ac)
+    q, k, v = ac.q.to(cuda), ac.k.to(cuda), ac.v.to(cuda)
+    o = _lib.prefix_attn(q, k, v, 128 ** -0.5, Kp=Kq, Vp=Vq, ksc=ks, vsc=vs, row_state=ac.row_state.to(cuda))
+    o1 = _lib.prefix_attn(q, k, v, 128 ** -0.5, Kp=Kq, Vp=Vq, ksc=ks, vsc=vs, row_state=ac.row_state.to(cuda),
+                          nsplit=1)
+    assert max(n for n, _ in _lib._PLANS.values()) > 1
+    assert (o.float() - o1.float()).abs().max() < 1.6e-2
