@@ -331,28 +331,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
       const bool i8 = pre && !P.prefix_bf16;          // ... dequantised here
       const bool q_seg = !pre && j < nb1 + nb2;
       const int k0 = pre ? lo1 + j * BN : q_seg ? (j - nb1) * BN : own_begin + (j - nb1 - nb2) * BN;
-      // ---- K_j and the block's visibility bits (a mask slot is reused 4 blocks later: by then this producer has
-      // passed the V stage wait of block j+3, which follows the softmax of block j+1)
+      // ---- K_j (a mask slot, written below, is reused 4 blocks later: by then this producer has passed the K stage
+      // wait of block j+4, which follows S of block j+2 in both tiles and so both softmaxes of block j+1)
       const int bk = j % KS;
       if (j >= KS && !mbar_wait(&kempty[bk], ((j / KS) - 1) & 1, abort_flag, P.err, kErrAttn | 1)) break;
-      bool vis;
-      {
-        const int idx = k0 + pt;
-        if (pre) {
-          vis = idx < hi1 && (!pm1 || pm1[idx]);
-        } else if (q_seg) {
-          vis = idx < n2;
-        } else {
-          const int a = idx / t, jj = idx - a * t;
-          const int r = row0 + a;
-          vis = idx < own_end && a < nr && jj >= (P.own_lo ? P.own_lo[r] : 0) && jj < (P.own_hi ? P.own_hi[r] : t);
-        }
-      }
-      const uint32_t word = __ballot_sync(0xffffffffu, vis);
-      if (lane == 0) {
-        masks[4 * (j % MS) + pw] = word;
-        mbar_arrive(&mfull[j % MS]);
-      }
       uint8_t* sK = sm + L::K(bk);
       if (i8) {
         const int r = j % RD;
@@ -376,6 +358,25 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
         for (int h = 0; h < D / 64; ++h) tma_load_2d(sK + h * L::ATOM, mk, &kfull[bk], x0 + h * 64, y);
       } else {
         mbar_arrive(&kfull[bk]);
+      }
+      // ---- the block's visibility bits, after K_j is on its way (their global loads stay off the K path)
+      bool vis;
+      {
+        const int idx = k0 + pt;
+        if (pre) {
+          vis = idx < hi1 && (!pm1 || pm1[idx]);
+        } else if (q_seg) {
+          vis = idx < n2;
+        } else {
+          const int a = idx / t, jj = idx - a * t;
+          const int r = row0 + a;
+          vis = idx < own_end && a < nr && jj >= (P.own_lo ? P.own_lo[r] : 0) && jj < (P.own_hi ? P.own_hi[r] : t);
+        }
+      }
+      const uint32_t word = __ballot_sync(0xffffffffu, vis);
+      if (lane == 0) {
+        masks[4 * (j % MS) + pw] = word;
+        mbar_arrive(&mfull[j % MS]);
       }
       // ---- V_j
       const int bv = j % VS;
@@ -452,12 +453,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
           issue_pv(x, j);
           if (x == ntiles - 1) mma_commit(&vempty[j % VS]);
           if (more) {
-            // P_x(j) is read from the columns S_x(j+1) overwrites: wait for the P V above to complete
-            if (!mbar_wait(&pv_done[x], j & 1, abort_flag, P.err, kErrAttn | 18)) {
-              live = false;
-              break;
-            }
-            tc_fence_after();
+            // S_x(j+1) overwrites the columns P_x(j) V_j reads: the tensor core executes one thread's MMAs in issue
+            // order, so it follows right behind without a wait
             issue_s(x, j + 1);
             if (x == ntiles - 1) mma_commit(&kempty[(j + 1) % KS]);
           }
