@@ -183,6 +183,16 @@ OD_API int od_prefix_attn(const void* q, const void* Kp, const void* Vp, const v
                           int64_t workspace_bytes, void* stream);
 /* The split count for od_prefix_attn on a GPU of num_sms SMs and its workspace size in bytes (0 for one split). */
 OD_API int od_prefix_attn_plan(const od_attn_dims* dims, int num_sms, int* nsplit, int64_t* workspace_bytes);
+/* No reference counterpart (an addition of this library, not a replacement of a reference interface): od_prefix_attn
+ * whose split workspace is a static 16 MiB device array of the library instead of a caller buffer, so the call
+ * allocates nothing. Requests needing more scratch are rejected (OD_EINVAL). The array is shared by all calls on a
+ * device: calls on one device must be ordered (one stream or synchronised streams). */
+OD_API int od_prefix_attn_noalloc(const void* q, const void* Kp, const void* Vp, const void* ksc, const void* vsc,
+                                  const int32_t* row_state, const int32_t* p_lo, const int32_t* p_hi,
+                                  const uint8_t* pmask, const void* Kq, const void* Vq, const int32_t* row_q,
+                                  const int32_t* q_len, const void* k_own, const void* v_own, const int32_t* own_lo,
+                                  const int32_t* own_hi, const int32_t* row_groups, void* o, float* lse,
+                                  od_attn_dims dims, void* stream);
 
 /* ---------------------------------------------------------------------------------------------------------------
  * A13: option readout, Decider._probs (decider.py:255-257):

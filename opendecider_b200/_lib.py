@@ -51,6 +51,7 @@ SIGNATURES = {
     "od_gate_quant": [c_void_p, c_void_p, c_int64, c_int64, c_int, c_int, c_void_p, c_void_p, c_void_p],
     "od_prefix_attn": [c_void_p] * 20 + [AttnDims, c_void_p, c_int64, c_void_p],
     "od_prefix_attn_plan": [POINTER(AttnDims), c_int, POINTER(c_int), POINTER(c_int64)],
+    "od_prefix_attn_noalloc": [c_void_p] * 20 + [AttnDims, c_void_p],
     "od_readout": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p,
                    c_void_p],
 }
@@ -337,3 +338,29 @@ def readout(logits: torch.Tensor, T: torch.Tensor, mask: torch.Tensor, bias: tor
     _check(load().od_readout(_p(logits), _p(T), _p(bias), _p(mask), _p(none_col), N, K, _p(probs), _p(renorm),
                              _p(p_none), _stream(dev)), "od_readout")
     return probs, renorm, p_none
+
+
+@_probed
+def prefix_attn_noalloc(q: torch.Tensor, k_own: torch.Tensor, v_own: torch.Tensor, sm_scale: float, *, nsplit: int,
+                        Kp=None, Vp=None, ksc=None, vsc=None, row_state=None, p_lo=None, p_hi=None, pmask=None,
+                        Kq=None, Vq=None, row_q=None, q_len=None, own_lo=None, own_hi=None, row_groups=None,
+                        max_group_rows: int = 1, out=None, want_lse: bool = False):
+    """prefix_attn through od_prefix_attn_noalloc: the split workspace is the library's static device scratch (no
+    allocation by the call; `out`/`lse` are the caller's). Calls on one device must be stream-ordered."""
+    dev = _need_cuda(q, k_own, v_own, Kp, Kq)
+    R, t, Hq, D = q.shape
+    Hkv = k_own.shape[2]
+    out = torch.empty_like(q) if out is None else out
+    lse = torch.empty(R, Hq, t, dtype=torch.float32, device=dev) if want_lse else None
+    S, T = (Kp.shape[0], Kp.shape[2]) if Kp is not None else (0, 0)
+    NQ, Lq = (Kq.shape[0], Kq.shape[1]) if Kq is not None else (0, 0)
+    pbf16 = Kp is not None and Kp.dtype == torch.bfloat16
+    sdt = _DT[ksc.dtype] if (ksc is not None and not pbf16) else OD_BF16
+    G = row_groups.shape[0] if row_groups is not None else R
+    dims = AttnDims(R, t, S, T, NQ, Lq, Hq, Hkv, D, sdt, sm_scale, G, max_group_rows if row_groups is not None else 1,
+                    1 if pbf16 else 0, nsplit)
+    _check(load().od_prefix_attn_noalloc(
+        _p(q), _p(Kp), _p(Vp), _p(None if pbf16 else ksc), _p(None if pbf16 else vsc), _p(row_state), _p(p_lo),
+        _p(p_hi), _p(pmask), _p(Kq), _p(Vq), _p(row_q), _p(q_len), _p(k_own), _p(v_own), _p(own_lo), _p(own_hi),
+        _p(row_groups), _p(out), _p(lse), dims, _stream(dev)), "od_prefix_attn_noalloc")
+    return (out, lse) if want_lse else out

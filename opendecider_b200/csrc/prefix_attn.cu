@@ -944,3 +944,51 @@ extern "C" int od_prefix_attn_plan(const od_attn_dims* dims, int num_sms, int* n
                        (dims->D + 1);
   return ok();
 }
+
+// ------------------------------------------------------------------------------------------------ no-alloc variant
+// od_prefix_attn with the split workspace in a file-scope device array instead of a caller buffer. The array is
+// part of the module's static device memory (one per device, mapped when the module loads); its address is taken
+// once per device with cudaGetSymbolAddress. Nothing in it has to start at zero: every split writes the partial O
+// and LSE of every slot it covers (a split left without keys writes O = 0, LSE = -inf) before the merge reads them.
+// One array per device means calls on one device must be ordered (one stream, or synchronised streams): two
+// in flight at once would share it.
+namespace od {
+namespace {
+constexpr int64_t kNoAllocScratchBytes = 16LL << 20;
+__device__ __align__(256) unsigned char g_attn_scratch[kNoAllocScratchBytes];
+
+void* attn_scratch() {
+  static void* addr[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (!addr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_attn_scratch) != cudaSuccess) return nullptr;
+    addr[dev] = p;
+  }
+  return addr[dev];
+}
+}  // namespace
+}  // namespace od
+
+extern "C" int od_prefix_attn_noalloc(const void* q, const void* Kp, const void* Vp, const void* ksc, const void* vsc,
+                                      const int32_t* row_state, const int32_t* p_lo, const int32_t* p_hi,
+                                      const uint8_t* pmask, const void* Kq, const void* Vq, const int32_t* row_q,
+                                      const int32_t* q_len, const void* k_own, const void* v_own,
+                                      const int32_t* own_lo, const int32_t* own_hi, const int32_t* row_groups,
+                                      void* o, float* lse, od_attn_dims dims, void* stream) {
+  const int nsplit = Kp && dims.nsplit > 1 ? dims.nsplit : 1;
+  const int64_t need =
+      nsplit > 1 ? static_cast<int64_t>(sizeof(float)) * nsplit * dims.R * dims.t * dims.Hq * (dims.D + 1) : 0;
+  OD_REQUIRE(need <= kNoAllocScratchBytes,
+             "od_prefix_attn_noalloc: %d splits need %lld bytes of scratch, the static scratch holds %lld (lower "
+             "dims.nsplit or call od_prefix_attn with a workspace)",
+             nsplit, (long long)need, (long long)kNoAllocScratchBytes);
+  void* ws = nullptr;
+  if (need > 0) {
+    ws = attn_scratch();
+    OD_REQUIRE(ws, "od_prefix_attn_noalloc: no address for the static scratch on this device");
+  }
+  return od_prefix_attn(q, Kp, Vp, ksc, vsc, row_state, p_lo, p_hi, pmask, Kq, Vq, row_q, q_len, k_own, v_own, own_lo,
+                        own_hi, row_groups, o, lse, dims, ws, need, stream);
+}
