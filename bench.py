@@ -50,7 +50,7 @@ def workload(config: int):
         cfg = DecoderConfig.nine_b(feature_layers=(8, 16, 24, "final"))
         return cfg, dict(d_model=512, n_heads=8, decision_layers=4), 12, \
             ("config5: 9B-class dense decoder, 64 requests/GPU x 16384-token cached int8 state + 512 appended "
-             "tokens, 1 choice question x 255 options (+none)")
+             "tokens, 1 choice question x 255 options (no none option at the 255-option cap)")
     cfg = DecoderConfig.tiny(feature_layers=(1, 3, "final"))
     return cfg, dict(d_model=64, n_heads=4, decision_layers=2), 32, \
         "config1: tiny decoder, 4 requests x 256-token state, 1 choice question x 8 options (+none)"
