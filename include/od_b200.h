@@ -195,6 +195,20 @@ OD_API int od_prefix_attn_noalloc(const void* q, const void* Kp, const void* Vp,
                                   od_attn_dims dims, void* stream);
 
 /* ---------------------------------------------------------------------------------------------------------------
+ * (f.2) LM-head log-probabilities of given tokens: Backbone.token_logprob (backbone.py:165-178), the V3 trunk's
+ * option log-prob feature (v3_lm_feature, v3.py:437-442 and 527-532):
+ *     lp[m] = float(h[m]) . (float(qW[tok[m]]) * float(sW[tok[m]])) - logsumexp_v float(bf16(h[m] . Wb[v]))
+ * h (M, H) bf16 (the final normed hidden state of the position before each token), Wb (V, H) bf16 = bf16(qW * sW)
+ * (the tied head as head_rows() dequantises it, quant.py:202-203), qW (V, H) int8 + sW (V,) bf16 the int8 head,
+ * tok (M,) int64, lp (M,) fp32 (-inf for a token outside [0, V)). H must be a multiple of 64. The vocabulary is
+ * divided into vsplit ranges (od_lm_logprob_plan); workspace holds 8 x M x vsplit bytes of per-split partials.
+ */
+OD_API int od_lm_logprob_plan(int64_t M, int64_t V, int num_sms, int* vsplit, int64_t* workspace_bytes);
+OD_API int od_lm_logprob(const void* h, int64_t M, int H, const void* Wb, const int8_t* qW, const void* sW,
+                         int64_t V, const int64_t* tok, float* lp, void* workspace, int64_t workspace_bytes,
+                         int vsplit, void* stream);
+
+/* ---------------------------------------------------------------------------------------------------------------
  * A13: option readout, Decider._probs (decider.py:255-257):
  *     p[i, :] = softmax(logits[i, :] / T[i] + bias[i, :]) * mask[i, :]
  * logits (N, K) fp32, T (N) fp32, bias (N, K) fp32 or NULL, mask (N, K) uint8; probs (N, K) fp32.

@@ -52,6 +52,9 @@ SIGNATURES = {
     "od_prefix_attn": [c_void_p] * 20 + [AttnDims, c_void_p, c_int64, c_void_p],
     "od_prefix_attn_plan": [POINTER(AttnDims), c_int, POINTER(c_int), POINTER(c_int64)],
     "od_prefix_attn_noalloc": [c_void_p] * 20 + [AttnDims, c_void_p],
+    "od_lm_logprob_plan": [c_int64, c_int64, c_int, POINTER(c_int), POINTER(c_int64)],
+    "od_lm_logprob": [c_void_p, c_int64, c_int, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_void_p,
+                      c_int64, c_int, c_void_p],
     "od_readout": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p,
                    c_void_p],
 }
@@ -364,3 +367,26 @@ def prefix_attn_noalloc(q: torch.Tensor, k_own: torch.Tensor, v_own: torch.Tenso
         _p(p_hi), _p(pmask), _p(Kq), _p(Vq), _p(row_q), _p(q_len), _p(k_own), _p(v_own), _p(own_lo), _p(own_hi),
         _p(row_groups), _p(out), _p(lse), dims, _stream(dev)), "od_prefix_attn_noalloc")
     return (out, lse) if want_lse else out
+
+
+@_probed
+def lm_logprob(h: torch.Tensor, Wb: torch.Tensor, qW: torch.Tensor, sW: torch.Tensor, tok: torch.Tensor,
+               vsplit: int | None = None) -> torch.Tensor:
+    """log softmax(h Wb^T)[tok] as Backbone.token_logprob computes it: h (M, H) bf16, Wb (V, H) bf16 (the dequantised
+    tied head), qW (V, H) int8 + sW (V,) bf16 (the int8 head, for the fp32 target logit), tok (M,) int64 -> (M,)
+    fp32. vsplit: vocabulary ranges per row tile (None: od_lm_logprob_plan's choice for this GPU)."""
+    dev = _need_cuda(h, Wb, qW, sW, tok)
+    M, H = h.shape
+    V = Wb.shape[0]
+    assert h.is_contiguous() and Wb.is_contiguous() and qW.is_contiguous() and tok.dtype == torch.int64
+    assert Wb.shape == qW.shape == (V, H) and sW.numel() == V and h.dtype == Wb.dtype == torch.bfloat16
+    n, b = ctypes.c_int(1), ctypes.c_int64(0)
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    _check(load().od_lm_logprob_plan(M, V, sms, ctypes.byref(n), ctypes.byref(b)), "od_lm_logprob_plan")
+    if vsplit is not None:
+        n.value, b.value = vsplit, 8 * M * vsplit
+    ws = torch.empty(max(1, b.value // 4), dtype=torch.float32, device=dev)
+    lp = torch.empty(M, dtype=torch.float32, device=dev)
+    _check(load().od_lm_logprob(_p(h), M, H, _p(Wb), _p(qW), _p(sW.contiguous()), V, _p(tok.contiguous()), _p(lp),
+                                _p(ws), ws.numel() * 4, n.value, _stream(dev)), "od_lm_logprob")
+    return lp

@@ -193,3 +193,17 @@ def readout(logits, T, mask, bias=None, none_col=None):
         if none_col is not None and int(none_col[i]) >= 0:
             p_none[i] = p[i, int(none_col[i])]
     return p.numpy(), renorm.numpy(), p_none.numpy()
+
+
+# ------------------------------------------------------------------------------------------------ (f.2) LM head
+def token_logprob(h, qW, sW, tok):
+    """Backbone.token_logprob (src/opendecider/backbone.py:165-178) with the tied int8 head (Int8Embedding.dequant_
+    rows, quant.py:202-203): logits = bf16(bf16(h) @ bf16(q * s)^T) as the reference's bf16 matmul returns them,
+    log-sum-exp over the vocabulary in fp32 (its chunked logaddexp is the same sum), the target logit in fp32 from
+    q.float() * s.float(). h (M, H) bf16, qW (V, H) int8, sW (V,) or (V, 1) bf16, tok (M,) long -> (M,) fp32."""
+    s = sW.reshape(-1, 1)
+    Wb = qW.to(torch.bfloat16) * s.to(torch.bfloat16)
+    hb = h.to(torch.bfloat16)
+    lse = torch.logsumexp((hb @ Wb.t()).float(), dim=-1)
+    target = (h.float() * (qW[tok].float() * s[tok].float())).sum(-1)
+    return target - lse

@@ -551,3 +551,25 @@ def test_prefix_attn_plan_splits_small_launches(cuda):
                           nsplit=1)
     assert max(n for n, _ in _lib._PLANS.values()) > 1
     assert (o.float() - o1.float()).abs().max() < 1.6e-2
+
+
+@pytest.mark.parametrize("M,H,V", [(300, 256, 1000), (130, 4096, 4099), (7, 64, 256)])
+def test_lm_logprob_matches_token_logprob(cuda, M, H, V):
+    """Backbone.token_logprob on the tensor cores: bf16 logits, a vocabulary log-sum-exp (padded last tile left
+    out), fp32 target logit. Within 5e-3 of the oracle (a bf16 logit may round the other way after a different
+    summation order); splits of the vocabulary agree to fp32 rounding."""
+    g = syn.gen(M + V)
+    h = (torch.randn(M, H, generator=g) * 1.5).to(torch.bfloat16)
+    w = torch.randn(V, H, generator=g) * 0.05
+    qW, sW, _ = ops.quantize_rows(w.numpy(), "bf16")
+    qW, sW = torch.from_numpy(qW), torch.from_numpy(sW[:, 0]).to(torch.bfloat16)
+    Wb = (qW.to(torch.bfloat16) * sW[:, None])
+    tok = torch.randint(0, V, (M,), generator=g)
+    ref = ops.token_logprob(h, qW, sW, tok)
+    args = [t.to(cuda) for t in (h, Wb, qW, sW, tok)]
+    lp = _lib.lm_logprob(*args)
+    assert (lp.cpu() - ref).abs().max() < 5e-3, (lp.cpu() - ref).abs().max()
+    lp1 = _lib.lm_logprob(*args, vsplit=1)
+    lp5 = _lib.lm_logprob(*args, vsplit=min(5, (V + 255) // 256))
+    assert (lp1 - lp5).abs().max() < 1e-4
+    assert _lib.device_error(cuda) == 0
