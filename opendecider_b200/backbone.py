@@ -412,6 +412,15 @@ class Backbone:
         cache.lens = [l + n for l in cache.lens]
         return cache
 
+    def token_logprob(self, h: torch.Tensor, tok: torch.Tensor) -> torch.Tensor:
+        """Backbone.token_logprob (backbone.py:165-178) with the tied int8 head: log softmax(h W^T)[tok] for h (M, H)
+        bf16 and tok (M,) int64 -> (M,) fp32 (od_lm_logprob). The head's bf16 rows (head_rows(): bf16(q * s)) are
+        materialised once and kept."""
+        if getattr(self, "_head_bf16", None) is None:
+            q, sc = self.embed.q, self.embed.scale
+            self._head_bf16 = _lib.dequant_rows(q, sc.reshape(-1, 1), torch.bfloat16)
+        return _lib.lm_logprob(h, self._head_bf16, self.embed.q, self.embed.scale.reshape(-1), tok)
+
     def prefix_cache_batch(self, seqs) -> KVCache:
         """Backbone.prefix_cache_batch (backbone.py:347-368) on B200: returns the int8 KV cache of all states."""
         return self.run_state(self.plan_state(seqs))

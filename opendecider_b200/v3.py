@@ -36,6 +36,7 @@ class TrunkConfig:
     d_model: int = 512
     n_heads: int = 8
     decision_layers: int = 4
+    lm_feature: bool = False    # v3_lm_feature (v3.py:213-216): the frozen LM's log-prob of each option token
 
 
 def _lin(g, out_f, in_f, bias=True):
@@ -88,6 +89,9 @@ def trunk_state_dict(cfg: TrunkConfig, seed: int = 0) -> dict:
     xatglu("cls_ff")
     put("score", *_lin(g, 1, dm))
     put("rel", *_lin(g, 1, dm))
+    if cfg.lm_feature:                      # drawn last: the other parameters do not depend on the switch
+        put("lp_proj", *_lin(g, dm, 1))
+        sd["lm_skip"] = torch.tensor(0.3)   # the reference initialises the gate at 0; nonzero exercises the path
     return sd
 
 
@@ -174,9 +178,10 @@ class V3Trunk:
                 "opt_mask": up(opt_mask)}
 
     @torch.no_grad()
-    def run(self, plan: dict, q_flat: torch.Tensor, o_flat: torch.Tensor) -> torch.Tensor:
+    def run(self, plan: dict, q_flat: torch.Tensor, o_flat: torch.Tensor, lp_flat: torch.Tensor | None = None):
         """V3.forward's device part (v3.py:627-709): option/context stacks, decision layers, CLS readout, score.
-        q_flat (sum lq, nL*d), o_flat (sum lo, nL*d) token features. Returns logits (N, K) fp32, NEG at pads."""
+        q_flat (sum lq, nL*d), o_flat (sum lo, nL*d) token features; lp_flat (sum lo,) the LM log-prob of each
+        option token (lm_feature). Returns logits (N, K) fp32, NEG at pads."""
         p, dev = self.p, self.device
         h, dm, df = self.cfg.n_heads, self.cfg.d_model, self.cfg.d_feat
         N, K, P, Tc = plan["N"], plan["K"], plan["P"], plan["Tc"]
@@ -192,6 +197,11 @@ class V3Trunk:
         C[plan["qrc"]] = self.mix(q_flat)
         C = C * (~c_pad)[..., None]
         x = F.linear(_scalenorm(X, p["in_norm.g"]), p["proj_option.weight"], p["proj_option.bias"])
+        lpX = None
+        if self.cfg.lm_feature:             # token-level log-prob feature (v3.py:666-672)
+            lpX = torch.zeros(N, P, device=dev)
+            lpX[plan["rc"]] = lp_flat.float()
+            x = x + F.linear(lpX[..., None], p["lp_proj.weight"], p["lp_proj.bias"])
         cin = _scalenorm(C, p["in_norm.g"])
         c = torch.where(plan["in_q"][..., None], F.linear(cin, p["proj_question.weight"], p["proj_question.bias"]),
                         F.linear(cin, p["proj_state.weight"], p["proj_state.bias"]))
@@ -211,6 +221,10 @@ class V3Trunk:
         hc = hc + _xatglu(p, "cls_ff", _scalenorm(hc, p["cls_nf.g"]))
         hc = _scalenorm(hc, p["final_norm.g"])
         logits = F.linear(hc, p["score.weight"], p["score.bias"]).squeeze(-1).float()
+        if lpX is not None:                 # gated skip of the length-normalised log-likelihood (v3.py:702-706)
+            own_f = own.float()
+            ll = (own_f * lpX[:, None, :]).sum(-1) / own_f.sum(-1).clamp_min(1)
+            logits = logits + p["lm_skip"] * ll
         return logits.masked_fill(~plan["opt_mask"], NEG)
 # ------------------------------------------------------------------------------------------------ row plans
 def _rect(tok_lists, pad_id, width=None):
@@ -241,6 +255,10 @@ class RowPlan:
     q_lens: torch.Tensor                # CPU
     o_lens: torch.Tensor                # CPU
     q_src: tuple | None = None          # rows-path: (row, col) of question tokens in the first row of each question
+    lp_osrc: torch.Tensor | None = None # lm_feature: per option token, the o_flat row of the previous token ...
+    lp_first: torch.Tensor | None = None  # ... except an option's first token (these positions of the flat array)
+    lp_qsrc: torch.Tensor | None = None # ... which takes its question's last token from q_flat
+    lp_tok: torch.Tensor | None = None  # the option tokens (targets), int64
 
 
 def width_chunks(lengths: torch.Tensor, chunk: int, waste: float = 0.25) -> list:
@@ -269,8 +287,23 @@ def row_groups(owner: torch.Tensor, max_rows: int) -> torch.Tensor:
     return torch.tensor(groups, dtype=torch.int32).view(-1, 2)
 
 
+def lm_sources(q_tok, o_tok, lq, lo, row_q, up) -> dict:
+    """Where each option token's LM log-prob reads its previous position (v3.py:437-442, 527-532): the option's
+    previous token in o_flat, or for its first token its question's last token in q_flat; and the targets."""
+    q_start = torch.cumsum(lq, 0) - lq
+    o_start = torch.cumsum(lo, 0) - lo
+    n = int(lo.sum())
+    m_of = torch.repeat_interleave(torch.arange(lo.numel()), lo)
+    first = torch.arange(n) == o_start[m_of]
+    osrc = (torch.arange(n) - 1).clamp_min(0)
+    qm = row_q[m_of[first]]
+    targets = torch.tensor([t for ts in o_tok for t in ts], dtype=torch.long)
+    return {"lp_osrc": up(osrc), "lp_first": up(torch.nonzero(first).view(-1)),
+            "lp_qsrc": up(q_start[qm] + lq[qm] - 1), "lp_tok": up(targets)}
+
+
 def plan_rows(bb: Backbone, tok, questions, T: int, qcache: bool, list_cap: int = 16, chunk: int = 4096,
-              up=None) -> RowPlan:
+              up=None, lm: bool = False) -> RowPlan:
     """Host layout of the branched row passes. qcache: V3._branched_feats_qcache (v3.py:446-534) - one right-padded
     question pass continuing each question's state at positions T + j, capturing its K/V, then option rows of
     their own answer tokens (sorted by length, chunks as wide as their longest option, positions after their own
@@ -315,7 +348,8 @@ def plan_rows(bb: Backbone, tok, questions, T: int, qcache: bool, list_cap: int 
                                            row_state=up(sidx[rq]), row_q=up(rq.to(torch.int32)), q_len=q_len_dev,
                                            row_groups=up(grp), max_group_rows=int(grp[:, 1].max()),
                                            features=feats), dst=up(dst), keep=up(keep)))
-        return RowPlan(True, qpass, passes, int(lq.sum()), int(lo.sum()), lq, lo)
+        return RowPlan(True, qpass, passes, int(lq.sum()), int(lo.sum()), lq, lo,
+                       **(lm_sources(q_tok, o_tok, lq, lo, row_q, up) if lm else {}))
     rows_tok = [q_tok[int(row_q[i])] + o_tok[i] for i in range(M)]
     ids, ln = _rect(rows_tok, bb.pad_id)
     W = ids.shape[1]
@@ -334,7 +368,8 @@ def plan_rows(bb: Backbone, tok, questions, T: int, qcache: bool, list_cap: int 
                                        row_state=up(sidx[row_q[sl]]), features=feats), dst=up(dst), keep=up(keep)))
     first = torch.cumsum(n_opt, 0) - n_opt
     qr, qc, _, _, _ = segment_layout(lq, torch.arange(N), N)
-    return RowPlan(False, None, passes, int(lq.sum()), int(lo.sum()), lq, lo, (up(first[qr]), up(qc)))
+    return RowPlan(False, None, passes, int(lq.sum()), int(lo.sum()), lq, lo, (up(first[qr]), up(qc)),
+                   **(lm_sources(q_tok, o_tok, lq, lo, row_q, up) if lm else {}))
 
 
 def run_rows(bb: Backbone, plan: RowPlan, cache: KVCache):
@@ -377,7 +412,8 @@ class V3Model:
 
     def plan(self, questions, T: int, state_lens: list, up=None):
         qc = self.question_cache and sum(len(q.options) for q in questions) >= self.qcache_min_rows
-        rows = plan_rows(self.backbone, self.tok, questions, T, qc, self.list_cap, self.chunk, up)
+        rows = plan_rows(self.backbone, self.tok, questions, T, qc, self.list_cap, self.chunk, up,
+                         lm=self.trunk.cfg.lm_feature)
         n_opt = torch.tensor([len(q.options) for q in questions])
         sl = torch.tensor([state_lens[q.state_idx] for q in questions], dtype=torch.long)
         return rows, self.trunk.prepare(rows.q_lens, rows.o_lens, n_opt, sl, up)
@@ -385,7 +421,16 @@ class V3Model:
     def execute(self, plan, cache: KVCache):
         rows, tplan = plan
         q_flat, o_flat = run_rows(self.backbone, rows, cache)
-        return self.trunk.run(tplan, q_flat, o_flat), tplan["opt_mask"]
+        lp = None
+        if self.trunk.cfg.lm_feature:
+            # the final normed hidden state (the last feature layer) of the position before each option token
+            bb = self.backbone
+            assert bb.cfg.feature_layers[-1] == "final", "the LM feature reads the 'final' feature layer"
+            H = bb.cfg.hidden
+            h_prev = o_flat[rows.lp_osrc, -H:]
+            h_prev[rows.lp_first] = q_flat[rows.lp_qsrc, -H:]
+            lp = bb.token_logprob(h_prev.contiguous(), rows.lp_tok)
+        return self.trunk.run(tplan, q_flat, o_flat, lp), tplan["opt_mask"]
 
     def run(self, questions, cache: KVCache):
         """(logits (N, K) fp32, opt_mask (N, K) bool) for questions reading `cache`."""

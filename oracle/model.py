@@ -274,7 +274,23 @@ class OracleDecision:
             o_flat[o_start[m]: o_start[m] + lo[m]] = fo[0, : lo[m]]
         sl = torch.tensor([lens[q.state_idx] for q in qs])
         tplan = self.trunk.prepare(lq, lo, n_opt, sl)
-        logits = self.trunk.run(tplan, q_flat, o_flat)
+        lp = None
+        if self.trunk.cfg.lm_feature:
+            # V3's LM feature (v3.py:527-532): each option token's log-prob given the final normed hidden state of
+            # the position before it - the previous option token, or for the first its question's last token
+            H = self.cfg.hidden
+            q_start = torch.cumsum(lq, 0) - lq
+            rows_prev = []
+            for m in range(lo.numel()):
+                qj = int(row_q[m])
+                rows_prev.append(q_flat[int(q_start[qj] + lq[qj] - 1), -H:])
+                for c in range(1, int(lo[m])):
+                    rows_prev.append(o_flat[int(o_start[m]) + c - 1, -H:])
+            h_prev = torch.stack(rows_prev)
+            tgt = torch.tensor([t for ts in o_tok for t in ts], dtype=torch.long)
+            qw, sw = self.dec.q["embed_tokens"]
+            lp = ops.token_logprob(h_prev, qw, sw, tgt)
+        logits = self.trunk.run(tplan, q_flat, o_flat, lp)
         Tq = [self.temps.get(q.type, self.temperature) for q in qs]
         nc = [getattr(q, "none_col", -1) for q in qs]
         probs, ren, pn = ops.readout(logits.numpy(), Tq, tplan["opt_mask"].numpy(), none_col=nc)

@@ -91,7 +91,7 @@ def build_reference(cfg: DecoderConfig, tok):
     return Backbone(lm, tok, bcfg)
 
 
-def run(qcache: bool):
+def run(qcache: bool, lm: bool = False):
     from opendecider.models import ModelConfig, build_model
     from opendecider.decider import Decider, prepare_inference_
     from opendecider import v3 as ref_v3
@@ -100,9 +100,10 @@ def run(qcache: bool):
     reqs, tok = syn.decision_requests(1, seed=0)
     bb = build_reference(cfg, tok)
     mcfg = ModelConfig(variant="v3", slot_emb="none", dropout=0.0, v3_features="branched", v3_row_format="answer",
-                       v3_cross="question", v3_layer_combine="mix", **TRUNK)
+                       v3_cross="question", v3_layer_combine="mix", v3_lm_feature=lm, **TRUNK)
     model = build_model(bb, mcfg).eval()
-    sd = trunk_state_dict(TrunkConfig(d_feat=cfg.hidden, n_feat_layers=len(FEATURE_LAYERS), **TRUNK), seed=0)
+    sd = trunk_state_dict(TrunkConfig(d_feat=cfg.hidden, n_feat_layers=len(FEATURE_LAYERS), lm_feature=lm, **TRUNK),
+                          seed=0)
     missing, unexpected = model.load_state_dict(sd, strict=False)
     assert not unexpected, unexpected
     os.environ["OPENDECIDER_QCACHE"] = "1" if qcache else "0"
@@ -137,9 +138,9 @@ def run(qcache: bool):
 def main():
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     out = {}
-    for qc in (True, False):
-        p, n, lg = run(qc)
-        tag = "qcache" if qc else "rows"
+    for qc, lm in ((True, False), (False, False), (True, True), (False, True)):
+        p, n, lg = run(qc, lm)
+        tag = ("lmq" if qc else "lmr") if lm else ("qcache" if qc else "rows")
         out[f"{tag}.probs"], out[f"{tag}.none"], out[f"{tag}.logits"] = p, n, lg
         print(tag, p.round(4), n.round(4))
     path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "e2e_config1.npz")

@@ -17,10 +17,10 @@ TRUNK = dict(d_model=64, n_heads=4, decision_layers=2)
 TEMPS = {"choice": 1.4978350400924683, "noul": 1.2169979810714722, "score": 1.5226973295211792}
 
 
-def make_decider(cuda, qcache=True):
+def make_decider(cuda, qcache=True, lm=False):
     cfg = DecoderConfig.tiny(feature_layers=FEATURE_LAYERS)
     bb = Backbone.random(cfg, seed=0, device=cuda, gen_device="cpu")
-    tc = TrunkConfig(d_feat=cfg.hidden, n_feat_layers=len(FEATURE_LAYERS), **TRUNK)
+    tc = TrunkConfig(d_feat=cfg.hidden, n_feat_layers=len(FEATURE_LAYERS), lm_feature=lm, **TRUNK)
     trunk = V3Trunk(tc, trunk_state_dict(tc, seed=0), cuda)
     reqs, tok = syn.decision_requests(1, seed=0)
     model = V3Model(bb, trunk, tok, question_cache=qcache, qcache_min_rows=32)
@@ -103,3 +103,15 @@ def test_decide_stream_equals_decide_many(cuda):
     assert len(got) == len(want)
     for (pw, nw), (pg, ng) in zip(want, got):
         assert np.array_equal(pw, pg) and np.array_equal(nw, ng)
+
+
+@pytest.mark.parametrize("qcache", [True, False])
+def test_config1_lm_feature_matches_reference(cuda, qcache):
+    """The LM log-prob feature (od_lm_logprob over the tied int8 head, v3_lm_feature) on both row paths against the
+    reference's decide_many with the feature on: probabilities within 1e-3, trunk logits within 2e-2."""
+    g = np.load("tests/golden/e2e_config1.npz")
+    tag = "lmq" if qcache else "lmr"
+    dec, reqs = make_decider(cuda, qcache, lm=True)
+    p, none = _collect(dec.decide_many(reqs))
+    assert np.abs(p - g[f"{tag}.probs"]).max() < 1e-3, np.abs(p - g[f"{tag}.probs"]).max()
+    assert np.abs(none - g[f"{tag}.none"]).max() < 1e-3

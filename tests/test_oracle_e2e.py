@@ -25,3 +25,21 @@ def test_oracle_decide_matches_reference():
     assert np.abs(ren[:, :K] - g["qcache.probs"]).max() < 1e-3
     assert np.abs(pn - g["qcache.none"]).max() < 1e-3
     assert np.abs(logits.numpy() - g["qcache.logits"]).max() < 2e-2
+
+
+def test_oracle_lm_feature_matches_reference():
+    """The V3 trunk's LM log-prob feature (v3_lm_feature): the oracle's token_logprob over the tied int8 head and the
+    trunk's lp_proj / gated skip reproduce the reference's decide_many within 1e-3 (the feature moves the
+    probabilities by up to 1.2e-2 on this case, so the check discriminates)."""
+    cfg = DecoderConfig.tiny(feature_layers=FEATURE_LAYERS)
+    tc = TrunkConfig(d_feat=cfg.hidden, n_feat_layers=len(FEATURE_LAYERS), lm_feature=True, **TRUNK)
+    trunk = V3Trunk(tc, trunk_state_dict(tc, seed=0), "cpu")
+    reqs, tok = syn.decision_requests(1, seed=0)
+    od = OracleDecision(cfg, synthetic_weights(cfg, seed=0), trunk, tok, TEMPS, 1.419344425201416,
+                        qcache_min_rows=32)
+    probs, ren, pn, logits = od.decide(reqs)
+    g = np.load("tests/golden/e2e_config1.npz")
+    K = g["lmq.probs"].shape[1]
+    assert np.abs(ren[:, :K] - g["lmq.probs"]).max() < 1e-3
+    assert np.abs(pn - g["lmq.none"]).max() < 1e-3
+    assert np.abs(logits.numpy() - g["lmq.logits"]).max() < 2e-2
