@@ -387,6 +387,39 @@ def op_attn_state(args):
                           "frac_bf16": flops / tm / 1e12 / peaks.get("bf16_tflops", 1590.0), "gbs": byts / tm / 1e9}))
 
 
+def op_lm_logprob(args):
+    """The LM-head log-prob feature's kernel (od_lm_logprob) at the 9B head: M option tokens x V = 151936 vocabulary
+    rows x H = 4096 (default M = 16384). TFLOP/s of the 2 M V H GEMM FLOPs (the log-sum-exp rides in the epilogue)."""
+    from opendecider_b200 import _lib
+    dev = torch.device("cuda", 0)
+    peaks = _peaks()
+    shapes = [tuple(int(v) for v in x.split("x")) for x in (args.shapes or "16384x151936").split(",")]
+    H = 4096
+    for M, V in shapes:
+        g = torch.Generator(device=dev).manual_seed(0)
+        h = torch.randn(M, H, generator=g, device=dev).to(torch.bfloat16)
+        qW = torch.randint(-127, 128, (V, H), generator=g, device=dev, dtype=torch.int8)
+        sW = (torch.rand(V, generator=g, device=dev) * 1e-3 + 1e-4).to(torch.bfloat16)
+        Wb = _lib.dequant_rows(qW, sW.view(-1, 1), torch.bfloat16)
+        tok = torch.randint(0, V, (M,), generator=g, device=dev)
+        ts = []
+        for i in range(args.warmup + args.steps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            _lib.lm_logprob(h, Wb, qW, sW, tok)
+            b.record()
+            torch.cuda.synchronize()
+            if i >= args.warmup:
+                ts.append(a.elapsed_time(b))
+        assert _lib.device_error(dev) == 0, "a kernel reported a device-side error"
+        tm = statistics.median(ts) / 1e3
+        flops = 2.0 * M * V * H
+        print(json.dumps({"op": "lm_logprob", "shape": {"M": M, "V": V, "H": H}, "ms": tm * 1e3,
+                          "tflops": flops / tm / 1e12,
+                          "frac_bf16": flops / tm / 1e12 / peaks.get("bf16_tflops", 1590.0),
+                          "gbs_head": V * H * 2 / tm / 1e9}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -395,7 +428,9 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--config", type=int, default=4, choices=[1, 4, 5])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--op", default="decide", choices=["decide", "gemm", "attn", "attn_state"],
+    ap.add_argument("--lm-feature", action="store_true",
+                    help="the trunk's LM log-prob feature on (v3_lm_feature, as in the shipped 9B checkpoint)")
+    ap.add_argument("--op", default="decide", choices=["decide", "gemm", "attn", "attn_state", "lm_logprob"],
                     help="decide: the headline decision throughput; gemm / attn: operator configs 2 / 3; "
                          "attn_state: the state pass's causal attention")
     ap.add_argument("--shapes", default="", help="--op gemm: MxNxK list; --op attn: requestsxrowsxt list; "
@@ -409,6 +444,8 @@ def main():
         return op_attn(args)
     if args.op == "attn_state":
         return op_attn_state(args)
+    if args.op == "lm_logprob":
+        return op_lm_logprob(args)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -431,7 +468,7 @@ def main():
     cfg, tk, qmin, desc = workload(args.config)
     bb = Backbone.random(cfg, seed=0, device=dev, gen_device=dev)
     torch.cuda.empty_cache()
-    tc = TrunkConfig(d_feat=cfg.hidden, n_feat_layers=len(cfg.feature_layers), **tk)
+    tc = TrunkConfig(d_feat=cfg.hidden, n_feat_layers=len(cfg.feature_layers), lm_feature=args.lm_feature, **tk)
     trunk = V3Trunk(tc, trunk_state_dict(tc, seed=0), dev)
     # per GPU: config 4's 64 requests; config 5's 512 requests are the 8-GPU batch, 64 per GPU (weak scaling)
     reqs, tok = syn.decision_requests(args.config, seed=rank, n_requests=64 if args.config == 5 else None)
@@ -560,13 +597,15 @@ def main():
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
         v, cores, sample = cpu_oracle_sample(args.config, 20.0)
-        cpu = {"value": v, "unit": "decisions/s", "cores": cores, "kind": "port", "sample": sample}
+        cpu = {"value": v, "unit": "decisions/s", "cores": cores, "kind": "port",
+               "sample": sample + ("; without the LM log-prob feature" if args.lm_feature else "")}
     kv_gb = sum(t.q.numel() for t in cache.k + cache.v) / 1e9 if cache is not None else 0.0
     out = {
         "metric": METRIC, "value": value, "unit": "decisions/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1e3 * t_dev / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded random-id states, random-init weights)",
-        "config": {"workload": desc, "global_batch": n_dec_local * world, "requests_per_gpu": len(reqs),
+        "config": {"workload": desc + (" + LM log-prob feature" if args.lm_feature else ""),
+                   "global_batch": n_dec_local * world, "requests_per_gpu": len(reqs),
                    "state_tokens": plan["state"]["T"], "parallelism": f"dp{world} (requests sharded, NCCL gather)",
                    "l2": f"inputs larger than L2 (7.6 GB of int8 weights and a {kv_gb:.1f} GB int8 KV cache stream "
                          "every step)"},
