@@ -133,6 +133,15 @@ OD_API int od_embed_i8(const int64_t* ids, int64_t n, const int8_t* qweight, con
 OD_API int od_qk_norm_rope(const void* qkv, const int32_t* pos, const void* cos, const void* sin, int64_t P,
                     const void* qnorm_w, const void* knorm_w, float eps, int64_t M, int Hq, int Hkv, int D,
                     void* q_out, void* k_out, void* v_out, void* stream);
+/* (f.1) od_qk_norm_rope that also writes the pass's K/V into the int8 cache (the state pass's fused KV write,
+ * replacing od_kv_append_i8 after it): token m = r * t + j of the pass is cache position t0 + j of state r;
+ * kq/vq (S, Hkv, T_cap, D) int8, ksc/vsc (S, Hkv, T_cap) bf16, bytes and scales exactly as od_kv_append_i8 writes
+ * them (PackedCache.pack's maybe_quantize, backbone.py:446; PrefixCache._take, state_cache.py:79); kb/vb (optional,
+ * both or neither) the materialised bf16 rows. q/k/v outputs as od_qk_norm_rope. */
+OD_API int od_qk_norm_rope_kv_i8(const void* qkv, const int32_t* pos, const void* cos, const void* sin, int64_t P,
+                          const void* qnorm_w, const void* knorm_w, float eps, int64_t M, int Hq, int Hkv, int D,
+                          void* q_out, void* k_out, void* v_out, int64_t t, int8_t* kq, int8_t* vq, void* ksc,
+                          void* vsc, void* kb, void* vb, int64_t T_cap, int64_t t0, void* stream);
 
 /* Output gate + per-token quantisation of the o_proj input (Qwen3_5Attention.forward :666-668):
  *     g = bf16(o * bf16(sigmoid(gate))),  then q, s = quantise(g) (fp32 scales)

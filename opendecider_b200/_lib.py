@@ -48,6 +48,9 @@ SIGNATURES = {
     "od_embed_i8": [c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int, c_void_p, c_void_p],
     "od_qk_norm_rope": [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_float, c_int64, c_int,
                         c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p],
+    "od_qk_norm_rope_kv_i8": [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_float, c_int64,
+                              c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p,
+                              c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p],
     "od_gate_quant": [c_void_p, c_void_p, c_int64, c_int64, c_int, c_int, c_void_p, c_void_p, c_void_p],
     "od_prefix_attn": [c_void_p] * 20 + [AttnDims, c_void_p, c_int64, c_void_p],
     "od_prefix_attn_plan": [POINTER(AttnDims), c_int, POINTER(c_int), POINTER(c_int64)],
@@ -256,6 +259,28 @@ def qk_norm_rope(qkv: torch.Tensor, pos: torch.Tensor, cos: torch.Tensor, sin: t
     v_out = torch.empty(M, Hkv, D, dtype=torch.bfloat16, device=dev) if v_out is None else v_out
     _check(load().od_qk_norm_rope(_p(qkv), _p(pos), _p(cos), _p(sin), cos.shape[0], _p(qnorm_w), _p(knorm_w), eps, M,
                                   Hq, Hkv, D, _p(q_out), _p(k_out), _p(v_out), _stream(dev)), "od_qk_norm_rope")
+    return q_out, k_out, v_out
+
+
+@_probed
+def qk_norm_rope_kv(qkv: torch.Tensor, pos: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                    qnorm_w: torch.Tensor, knorm_w: torch.Tensor, eps: float, Hq: int, Hkv: int, D: int, t: int,
+                    kq: torch.Tensor, vq: torch.Tensor, ksc: torch.Tensor, vsc: torch.Tensor, t0: int,
+                    kb: torch.Tensor | None = None, vb: torch.Tensor | None = None):
+    """qk_norm_rope plus the int8 cache write of the pass's K/V (kv_append's bytes): the M = S x t tokens are rows of
+    t tokens, row r written at positions t0 .. t0 + t - 1 of state r of kq/vq (S, Hkv, T_cap, D) + ksc/vsc; kb/vb:
+    the materialised bf16 copy. Returns (q, k, v) as qk_norm_rope."""
+    dev = _need_cuda(qkv, pos, cos, sin, kq, vq, ksc, vsc)
+    M = qkv.shape[0]
+    assert kq.is_contiguous() and vq.is_contiguous() and ksc.dtype == torch.bfloat16 and vsc.dtype == torch.bfloat16
+    assert (kb is None) == (vb is None) and kq.shape[0] * t == M
+    q_out = torch.empty(M, Hq, D, dtype=torch.bfloat16, device=dev)
+    k_out = torch.empty(M, Hkv, D, dtype=torch.bfloat16, device=dev)
+    v_out = torch.empty(M, Hkv, D, dtype=torch.bfloat16, device=dev)
+    _check(load().od_qk_norm_rope_kv_i8(_p(qkv), _p(pos), _p(cos), _p(sin), cos.shape[0], _p(qnorm_w), _p(knorm_w),
+                                        eps, M, Hq, Hkv, D, _p(q_out), _p(k_out), _p(v_out), t, _p(kq), _p(vq),
+                                        _p(ksc), _p(vsc), _p(kb), _p(vb), kq.shape[2], t0, _stream(dev)),
+           "od_qk_norm_rope_kv_i8")
     return q_out, k_out, v_out
 
 

@@ -200,6 +200,10 @@ class Backbone:
         # a pass over an int8-only cache dequantises each layer's prefix once into a reused bf16 buffer when it has
         # at least this many (query token x query head) slots per state per KV head; None: never
         self.jit_min_slots = 256
+        # write a pass's int8 K/V from the q/k-norm + RoPE kernel (od_qk_norm_rope_kv_i8) instead of a separate
+        # od_kv_append_i8 pass: identical bytes, but measured slower on the config-4 step (65.5 ms against 60.6 ms
+        # per step for the two kernels): off
+        self.fused_kv_write = False
 
     # ------------------------------------------------------------------------------------------ construction
     @classmethod
@@ -289,14 +293,21 @@ class Backbone:
                 if li in want:                              # output of decoder layer li (1-based feature number)
                     feats[li] = r.clone()
             qkv = _lib.gemm_w8a8(hq, hs, L.qkv.q, L.qkv.scale, _lib.OD_EPI_BF16)
-            q, k, v = _lib.qk_norm_rope(qkv, pos, self.cos, self.sin, L.q_norm, L.k_norm, cfg.eps, Hq, Hkv, D)
+            wc = spec.write_cache
+            if wc is not None and self.fused_kv_write and cfg.dtype == torch.bfloat16:
+                # the pass's K/V go into the int8 cache (and its kept bf16 copy) from the same kernel
+                q, k, v = _lib.qk_norm_rope_kv(qkv, pos, self.cos, self.sin, L.q_norm, L.k_norm, cfg.eps, Hq, Hkv, D,
+                                               t, wc.k[li].q, wc.v[li].q, wc.k[li].scale, wc.v[li].scale,
+                                               spec.write_t0, kb=wc.kb[li] if wc.kb is not None else None,
+                                               vb=wc.vb[li] if wc.vb is not None else None)
+            else:
+                q, k, v = _lib.qk_norm_rope(qkv, pos, self.cos, self.sin, L.q_norm, L.k_norm, cfg.eps, Hq, Hkv, D)
+                if wc is not None:
+                    _lib.kv_append(k.view(R, t, Hkv, D), v.view(R, t, Hkv, D), wc.k[li].q, wc.v[li].q,
+                                   wc.k[li].scale, wc.v[li].scale, t0=spec.write_t0,
+                                   kb=wc.kb[li] if wc.kb is not None else None,
+                                   vb=wc.vb[li] if wc.vb is not None else None)
             k4, v4 = k.view(R, t, Hkv, D), v.view(R, t, Hkv, D)
-            if spec.write_cache is not None:
-                wc = spec.write_cache
-                # the kept bf16 copy (materialize(): bf16(q * s)) is written by the same kernel, new rows only
-                _lib.kv_append(k4, v4, wc.k[li].q, wc.v[li].q, wc.k[li].scale, wc.v[li].scale, t0=spec.write_t0,
-                               kb=wc.kb[li] if wc.kb is not None else None,
-                               vb=wc.vb[li] if wc.vb is not None else None)
             if captured is not None:
                 captured.append((k4, v4))
             if last and spec.kv_only_last:

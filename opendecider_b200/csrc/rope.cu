@@ -66,12 +66,75 @@ __device__ __forceinline__ void store_pairs(__nv_bfloat16* p, const uint32_t (&w
   }
 }
 
+// The int8 KV cache rows of a pass (state pass, appended records): token tok = row r x t + j of the pass is cache
+// position t0 + j of state r. Each k / v head row is quantised per (state, head, token) over D exactly as
+// od_kv_append_i8 does it (the same helpers), its scale stored in bf16, and optionally its materialised bf16 copy.
+struct KvOut {
+  int8_t* kq;
+  int8_t* vq;
+  __nv_bfloat16* ksc;
+  __nv_bfloat16* vsc;
+  __nv_bfloat16* kb;        // optional (with vb): bf16(q * s), materialize()'s rounding
+  __nv_bfloat16* vb;
+  int64_t t, T_cap, t0;
+};
+
 template <int EPL>
+__device__ __forceinline__ void write_kv_row(const uint32_t (&w)[EPL / 2], int8_t* q8, __nv_bfloat16* sc,
+                                             __nv_bfloat16* mat, int64_t dst, int lane) {
+  constexpr int D = EPL * 32;
+  float x[EPL];
+#pragma unroll
+  for (int e = 0; e < EPL / 2; ++e) {
+    const float2 f = unpack2(w[e]);
+    x[2 * e] = f.x;
+    x[2 * e + 1] = f.y;
+  }
+  float amax = 0.f;
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) amax = fmaxf(amax, fabsf(x[e]));
+  amax = warp_max(amax);
+  const float s = quant_scale(amax), r = quant_recip(s);
+  int8_t qv[EPL];
+  int8_t* out = q8 + dst * D + lane * EPL;
+  if constexpr (EPL == 4) {
+    const uint32_t word = quant4(x[0], x[1], x[2], x[3], s, r);
+    *reinterpret_cast<uint32_t*>(out) = word;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) qv[e] = static_cast<int8_t>(word >> (8 * e));
+  } else if constexpr (EPL == 8) {
+    const uint32_t w0 = quant4(x[0], x[1], x[2], x[3], s, r), w1 = quant4(x[4], x[5], x[6], x[7], s, r);
+    *reinterpret_cast<uint2*>(out) = make_uint2(w0, w1);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      qv[e] = static_cast<int8_t>(w0 >> (8 * e));
+      qv[4 + e] = static_cast<int8_t>(w1 >> (8 * e));
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+      qv[e] = quant_val(x[e], s, r);
+      out[e] = qv[e];
+    }
+  }
+  const __nv_bfloat16 sb = __float2bfloat16_rn(s);
+  if (lane == 0) sc[dst] = sb;
+  if (mat != nullptr) {
+    const float sf = __bfloat162float(sb);
+    float m[EPL];
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) m[e] = static_cast<float>(qv[e]) * sf;   // exact: |q| <= 127, s has 8 bits
+    store_lane<EPL>(mat + dst * D + lane * EPL, m);
+  }
+}
+
+template <int EPL, bool KV>
 __global__ void __launch_bounds__(32 * kWarps) qk_norm_rope_kernel(
     const __nv_bfloat16* __restrict__ qkv, int64_t ld, const int32_t* __restrict__ pos,
     const __nv_bfloat16* __restrict__ cos_t, const __nv_bfloat16* __restrict__ sin_t, int64_t P,
     const __nv_bfloat16* __restrict__ qw, const __nv_bfloat16* __restrict__ kw, float eps, int64_t M, int Hq, int Hkv,
-    __nv_bfloat16* __restrict__ qo, __nv_bfloat16* __restrict__ ko, __nv_bfloat16* __restrict__ vo, int32_t* err) {
+    __nv_bfloat16* __restrict__ qo, __nv_bfloat16* __restrict__ ko, __nv_bfloat16* __restrict__ vo, int32_t* err,
+    KvOut kv) {
   constexpr int D = EPL * 32;
   constexpr int NW = EPL / 2;
   const int64_t tok = blockIdx.x;
@@ -88,6 +151,12 @@ __global__ void __launch_bounds__(32 * kWarps) qk_norm_rope_kernel(
                                            : row + static_cast<int64_t>(Hq) * 2 * D + static_cast<int64_t>(slot - Hq) * D;
       load_pairs<EPL>(src + lane * EPL, x[i]);
     }
+  }
+  // cache position of this token (fused KV write): row r of the pass, token j, one 32-bit division per token
+  int kv_r = 0, kv_j = 0;
+  if constexpr (KV) {
+    kv_r = static_cast<int>(tok) / static_cast<int>(kv.t);
+    kv_j = static_cast<int>(tok) - kv_r * static_cast<int>(kv.t);
   }
   int p = pos[tok];
   if (p < 0 || p >= P) {
@@ -111,7 +180,11 @@ __global__ void __launch_bounds__(32 * kWarps) qk_norm_rope_kernel(
     const int slot = warp + i * kWarps;
     if (slot >= slots) break;
     if (slot >= Hq + Hkv) {                           // value head: plain copy
-      store_pairs<EPL>(vo + (tok * Hkv + (slot - Hq - Hkv)) * D + lane * EPL, x[i]);
+      const int h = slot - Hq - Hkv;
+      store_pairs<EPL>(vo + (tok * Hkv + h) * D + lane * EPL, x[i]);
+      if constexpr (KV)
+        write_kv_row<EPL>(x[i], kv.vq, kv.vsc, kv.vb,
+                          (static_cast<int64_t>(kv_r) * Hkv + h) * kv.T_cap + kv.t0 + kv_j, lane);
       continue;
     }
     const bool is_q = slot < Hq;
@@ -142,6 +215,11 @@ __global__ void __launch_bounds__(32 * kWarps) qk_norm_rope_kernel(
     }
     __nv_bfloat16* dst = is_q ? qo + (tok * Hq + slot) * D : ko + (tok * Hkv + (slot - Hq)) * D;
     store_pairs<EPL>(dst + lane * EPL, x[i]);
+    if constexpr (KV) {
+      if (!is_q)
+        write_kv_row<EPL>(x[i], kv.kq, kv.ksc, kv.kb,
+                          (static_cast<int64_t>(kv_r) * Hkv + (slot - Hq)) * kv.T_cap + kv.t0 + kv_j, lane);
+    }
   }
 }
 
@@ -150,9 +228,11 @@ __global__ void __launch_bounds__(32 * kWarps) qk_norm_rope_kernel(
 
 using namespace od;
 
-extern "C" int od_qk_norm_rope(const void* qkv, const int32_t* pos, const void* cos, const void* sin, int64_t P,
-                               const void* qnorm_w, const void* knorm_w, float eps, int64_t M, int Hq, int Hkv, int D,
-                               void* q_out, void* k_out, void* v_out, void* stream) {
+namespace od {
+namespace {
+int launch_qk_norm_rope(const void* qkv, const int32_t* pos, const void* cos, const void* sin, int64_t P,
+                        const void* qnorm_w, const void* knorm_w, float eps, int64_t M, int Hq, int Hkv, int D,
+                        void* q_out, void* k_out, void* v_out, const KvOut* kv, void* stream) {
   OD_REQUIRE(qkv && pos && cos && sin && qnorm_w && knorm_w && q_out && k_out && v_out, "od_qk_norm_rope: null pointer");
   OD_REQUIRE(M >= 0 && Hq > 0 && Hkv > 0 && Hq % Hkv == 0 && P > 0, "od_qk_norm_rope: bad shape");
   OD_REQUIRE(D == 64 || D == 128 || D == 256, "od_qk_norm_rope: head_dim %d not in {64, 128, 256}", D);
@@ -177,11 +257,44 @@ extern "C" int od_qk_norm_rope(const void* qkv, const int32_t* pos, const void* 
   auto QO = static_cast<__nv_bfloat16*>(q_out);
   auto KO = static_cast<__nv_bfloat16*>(k_out);
   auto VO = static_cast<__nv_bfloat16*>(v_out);
-#define OD_RP(E) qk_norm_rope_kernel<E><<<blocks, threads, 0, st>>>(Q, ld, pos, C, S, P, QW, KW, eps, M, Hq, Hkv, QO, KO, VO, err)
-  if (D == 64) OD_RP(2);
-  else if (D == 128) OD_RP(4);
-  else OD_RP(8);
+  const KvOut none{};
+#define OD_RP(E, KV_) qk_norm_rope_kernel<E, KV_><<<blocks, threads, 0, st>>>(Q, ld, pos, C, S, P, QW, KW, eps, M, Hq, \
+                                                                              Hkv, QO, KO, VO, err, kv ? *kv : none)
+  if (kv) {
+    if (D == 64) OD_RP(2, true);
+    else if (D == 128) OD_RP(4, true);
+    else OD_RP(8, true);
+  } else {
+    if (D == 64) OD_RP(2, false);
+    else if (D == 128) OD_RP(4, false);
+    else OD_RP(8, false);
+  }
 #undef OD_RP
   OD_LAUNCH_CHECK();
   return ok();
+}
+}  // namespace
+}  // namespace od
+
+extern "C" int od_qk_norm_rope(const void* qkv, const int32_t* pos, const void* cos, const void* sin, int64_t P,
+                               const void* qnorm_w, const void* knorm_w, float eps, int64_t M, int Hq, int Hkv, int D,
+                               void* q_out, void* k_out, void* v_out, void* stream) {
+  return launch_qk_norm_rope(qkv, pos, cos, sin, P, qnorm_w, knorm_w, eps, M, Hq, Hkv, D, q_out, k_out, v_out, nullptr,
+                             stream);
+}
+
+extern "C" int od_qk_norm_rope_kv_i8(const void* qkv, const int32_t* pos, const void* cos, const void* sin, int64_t P,
+                                     const void* qnorm_w, const void* knorm_w, float eps, int64_t M, int Hq, int Hkv,
+                                     int D, void* q_out, void* k_out, void* v_out, int64_t t, int8_t* kq, int8_t* vq,
+                                     void* ksc, void* vsc, void* kb, void* vb, int64_t T_cap, int64_t t0,
+                                     void* stream) {
+  OD_REQUIRE(kq && vq && ksc && vsc, "od_qk_norm_rope_kv_i8: null cache pointer");
+  OD_REQUIRE((kb == nullptr) == (vb == nullptr), "od_qk_norm_rope_kv_i8: kb and vb go together");
+  OD_REQUIRE(t > 0 && M % t == 0 && t0 >= 0 && t0 + t <= T_cap, "od_qk_norm_rope_kv_i8: bad token layout");
+  OD_REQUIRE(aligned8(kq) && aligned8(vq) && (kb == nullptr || (aligned8(kb) && aligned8(vb))),
+             "od_qk_norm_rope_kv_i8: cache pointers must be 8-byte aligned");
+  KvOut kv{kq, vq, static_cast<__nv_bfloat16*>(ksc), static_cast<__nv_bfloat16*>(vsc),
+           static_cast<__nv_bfloat16*>(kb), static_cast<__nv_bfloat16*>(vb), t, T_cap, t0};
+  return launch_qk_norm_rope(qkv, pos, cos, sin, P, qnorm_w, knorm_w, eps, M, Hq, Hkv, D, q_out, k_out, v_out, &kv,
+                             stream);
 }

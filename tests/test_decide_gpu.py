@@ -115,3 +115,21 @@ def test_config1_lm_feature_matches_reference(cuda, qcache):
     p, none = _collect(dec.decide_many(reqs))
     assert np.abs(p - g[f"{tag}.probs"]).max() < 1e-3, np.abs(p - g[f"{tag}.probs"]).max()
     assert np.abs(none - g[f"{tag}.none"]).max() < 1e-3
+
+
+def test_fused_kv_write_same_decisions(cuda):
+    """The state pass's K/V written by od_qk_norm_rope_kv_i8 (fused) or by od_kv_append_i8 (separate) give the same
+    cache bytes and the same decisions, bit for bit."""
+    dec, reqs = make_decider(cuda, True)
+    bb = dec.model.backbone
+    c0 = dec.encode_states([r.state for r in reqs])
+    p0 = _collect(dec.decide_many(reqs))
+    bb.fused_kv_write = True
+    try:
+        c1 = dec.encode_states([r.state for r in reqs])
+        p1 = _collect(dec.decide_many(reqs))
+    finally:
+        bb.fused_kv_write = False
+    for a, b in zip(c0.k + c0.v, c1.k + c1.v):
+        assert torch.equal(a.q, b.q) and torch.equal(a.scale.view(torch.int16), b.scale.view(torch.int16))
+    assert all(np.array_equal(x, y) for x, y in zip(p0, p1))

@@ -573,3 +573,36 @@ def test_lm_logprob_matches_token_logprob(cuda, M, H, V):
     lp5 = _lib.lm_logprob(*args, vsplit=min(5, (V + 255) // 256))
     assert (lp1 - lp5).abs().max() < 1e-4
     assert _lib.device_error(cuda) == 0
+
+
+@pytest.mark.parametrize("D,with_copy", [(128, True), (64, False)])
+def test_qk_norm_rope_fused_kv_write_equals_kv_append(cuda, D, with_copy):
+    """The fused cache write of od_qk_norm_rope_kv_i8 equals od_qk_norm_rope followed by od_kv_append_i8, byte for
+    byte (int8 rows, bf16 scales, the materialised copy) at a token offset, with identical q / k / v outputs."""
+    g = syn.gen(D + 7)
+    S, t, Hq, Hkv, T_cap, t0 = 3, 21, 8, 2, 64, 30
+    M = S * t
+    qkv = (torch.randn(M, Hq * 2 * D + 2 * Hkv * D, generator=g) * 2).to(torch.bfloat16).to(cuda)
+    pos = (t0 + torch.arange(t, dtype=torch.int32)).repeat(S).to(cuda)
+    cos, sin = ops.rope_tables(D, 1e6, 256)
+    qn = (torch.randn(D, generator=g) * 0.1).to(torch.bfloat16).to(cuda)
+    kn = (torch.randn(D, generator=g) * 0.1).to(torch.bfloat16).to(cuda)
+    cos, sin = cos.to(cuda), sin.to(cuda)
+
+    def cache():
+        kq = torch.zeros(S, Hkv, T_cap, D, dtype=torch.int8, device=cuda)
+        sc = torch.zeros(S, Hkv, T_cap, dtype=torch.bfloat16, device=cuda)
+        mat = torch.zeros(S, Hkv, T_cap, D, dtype=torch.bfloat16, device=cuda) if with_copy else None
+        return kq, kq.clone(), sc, sc.clone(), mat, (mat.clone() if with_copy else None)
+
+    a = cache()
+    q1, k1, v1 = _lib.qk_norm_rope(qkv, pos, cos, sin, qn, kn, 1e-6, Hq, Hkv, D)
+    _lib.kv_append(k1.view(S, t, Hkv, D), v1.view(S, t, Hkv, D), a[0], a[1], a[2], a[3], t0=t0, kb=a[4], vb=a[5])
+    b = cache()
+    q2, k2, v2 = _lib.qk_norm_rope_kv(qkv, pos, cos, sin, qn, kn, 1e-6, Hq, Hkv, D, t, b[0], b[1], b[2], b[3], t0,
+                                      kb=b[4], vb=b[5])
+    assert torch.equal(q1, q2) and torch.equal(k1, k2) and torch.equal(v1, v2)
+    for x, y in zip(a, b):
+        if x is not None:
+            assert torch.equal(x.view(torch.int8) if x.dtype == torch.int8 else x.view(torch.int16),
+                               y.view(torch.int8) if y.dtype == torch.int8 else y.view(torch.int16))
