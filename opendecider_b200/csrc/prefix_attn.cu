@@ -170,11 +170,24 @@ __device__ __forceinline__ void convert_piece(const uint8_t* raw, const uint32_t
       dequant4_bf16(q.z, s2, w[4], w[5]);
       dequant4_bf16(q.w, s2, w[6], w[7]);
     } else {
-      const float sf = __half2float(__ushort_as_half(static_cast<unsigned short>(sc[it])));
-      const int8_t* qb = reinterpret_cast<const int8_t*>(&q);
+      // fp16 scales: bf16(fp16(q * s)) without conversion instructions. The byte q + 128 placed under the fp16
+      // exponent of 1024 reads as 1024 + q + 128 (exact), minus 1152 gives q exactly; the packed fp16 multiply
+      // rounds q * s once, as the reference's fp16 multiply does (q * s is exact in fp32); widening to fp32 is exact
+      // and the bf16 pack rounds to nearest even.
+      const uint32_t s2 = sc[it] | (sc[it] << 16);
+      const __half2 sh = *reinterpret_cast<const __half2*>(&s2);
+      const __half2 bias = __float2half2_rn(1152.0f);
+      const uint32_t words[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-      for (int e = 0; e < 8; ++e)
-        w[e] = pack_bf16(rhf(static_cast<float>(qb[2 * e]) * sf), rhf(static_cast<float>(qb[2 * e + 1]) * sf));
+      for (int b = 0; b < 4; ++b) {
+        const uint32_t u = words[b] ^ 0x80808080u;
+        const uint32_t lo = __byte_perm(u, 0x64646464u, 0x4140), hi = __byte_perm(u, 0x64646464u, 0x4342);
+        const __half2 qlo = __hsub2(*reinterpret_cast<const __half2*>(&lo), bias);
+        const __half2 qhi = __hsub2(*reinterpret_cast<const __half2*>(&hi), bias);
+        const float2 plo = __half22float2(__hmul2(qlo, sh)), phi = __half22float2(__hmul2(qhi, sh));
+        w[2 * b] = pack_bf16(plo.x, plo.y);
+        w[2 * b + 1] = pack_bf16(phi.x, phi.y);
+      }
     }
     // the 16 int8 values of chunk ch are bf16 chunks 2ch and 2ch+1 of the row
     *reinterpret_cast<uint4*>(dst + swz(key, 2 * ch, ATOM)) = make_uint4(w[0], w[1], w[2], w[3]);
