@@ -51,6 +51,10 @@ OD_API const char* od_version(void);
 /* Device-side error word written by kernels whose bounded waits give up (0 = none). Reads and clears it.
  * Synchronises `stream`. Not a hot-path call. */
 OD_API int od_device_error(void* stream, int32_t* host_code);
+/* No reference counterpart: a self-test of the kernels' failure detection. One thread waits on a barrier that nothing
+ * completes, gives up after limit_cycles (at most the kernels' own limit), records 0x7F0001 in the device error word
+ * and returns; od_device_error then reads it. Nothing faults or hangs. */
+OD_API int od_selftest_bounded_wait(int64_t limit_cycles, void* stream);
 
 /* ---------------------------------------------------------------------------------------------------------------
  * A1 / A5 / A6: per-row symmetric int8 quantisation, Int8Tensor.quantize (quant.py:37-41) and the weight quantiser

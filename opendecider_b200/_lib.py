@@ -37,6 +37,7 @@ SIGNATURES = {
     "od_last_error": [],
     "od_version": [],
     "od_device_error": [c_void_p, POINTER(c_int32)],
+    "od_selftest_bounded_wait": [c_int64, c_void_p],
     "od_quant_rows_i8": [c_void_p, c_int, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_int, c_void_p],
     "od_dequant_rows_i8": [c_void_p, c_void_p, c_int, c_int64, c_int64, c_void_p, c_int, c_void_p],
     "od_kv_append_i8": [c_void_p, c_void_p, c_int, c_int64, c_int64, c_int, c_int, c_int64, c_int64, c_int64,
@@ -415,3 +416,10 @@ def lm_logprob(h: torch.Tensor, Wb: torch.Tensor, qW: torch.Tensor, sW: torch.Te
     _check(load().od_lm_logprob(_p(h), M, H, _p(Wb), _p(qW), _p(sW.contiguous()), V, _p(tok.contiguous()), _p(lp),
                                 _p(ws), ws.numel() * 4, n.value, _stream(dev)), "od_lm_logprob")
     return lp
+
+
+def selftest_bounded_wait(limit_cycles: int, device=None) -> None:
+    """Launch the failure-detection self-test (od_selftest_bounded_wait): a wait that runs out after limit_cycles and
+    records its code in the device error word (read it with device_error())."""
+    dev = torch.device(device or "cuda")
+    _check(load().od_selftest_bounded_wait(int(limit_cycles), _stream(dev)), "od_selftest_bounded_wait")

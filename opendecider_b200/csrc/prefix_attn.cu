@@ -1005,3 +1005,36 @@ extern "C" int od_prefix_attn_noalloc(const void* q, const void* Kp, const void*
   return od_prefix_attn(q, Kp, Vp, ksc, vsc, row_state, p_lo, p_hi, pmask, Kq, Vq, row_q, q_len, k_own, v_own, own_lo,
                         own_hi, row_groups, o, lse, dims, ws, need, stream);
 }
+
+// ------------------------------------------------------------------------------------------------ failure detection
+// Self-test of the bounded-wait path every kernel here relies on: one thread waits on an mbarrier nothing arrives
+// on, with a caller-chosen cycle limit instead of the kernels' ~2 s, records kErrSelfTest in the device error word
+// when the limit runs out and returns. The context stays usable (nothing faults, nothing keeps waiting).
+namespace od {
+namespace {
+constexpr int32_t kErrSelfTest = 0x7F0001;
+
+__global__ void bounded_wait_selftest_kernel(int64_t limit_cycles, int32_t* err) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x != 0) return;
+  mbar_init(&bar, 1);
+  fence_mbar_init();
+  const long long t0 = clock64();
+  while (!mbar_try_wait(&bar, 0)) {
+    if (clock64() - t0 > limit_cycles) {
+      atomicCAS(err, 0, kErrSelfTest);
+      return;
+    }
+  }
+}
+}  // namespace
+}  // namespace od
+
+extern "C" int od_selftest_bounded_wait(int64_t limit_cycles, void* stream) {
+  OD_REQUIRE(limit_cycles > 0 && limit_cycles <= kWaitLimitCycles, "od_selftest_bounded_wait: limit out of range");
+  int32_t* err = device_error_word();
+  if (!err) return fail(OD_ECUDA, "od_selftest_bounded_wait: no device error word");
+  bounded_wait_selftest_kernel<<<1, 32, 0, as_stream(stream)>>>(limit_cycles, err);
+  OD_LAUNCH_CHECK();
+  return ok();
+}

@@ -45,3 +45,37 @@ def test_gather_rows_gloo_world2():
     for p in procs:
         p.join(timeout=60)
     assert res == {0: True, 1: True}
+
+
+def _failing_worker(rank, world, port, q):
+    """Rank 1 dies before the gather; rank 0's gather must end with an error (a short process-group timeout or the
+    closed connection), never wait for good."""
+    import datetime
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
+    if rank == 1:
+        q.put((rank, "died"))
+        q.close()
+        q.join_thread()                                      # the message is out before the process ends
+        os._exit(3)                                          # leaves without joining the collective
+    try:
+        gather_rows(torch.zeros(2, 3))
+        q.put((rank, "no error"))
+    except Exception as e:                                   # noqa: BLE001 - any error is the expected outcome
+        q.put((rank, "error: " + type(e).__name__))
+
+
+def test_gather_fails_cleanly_when_a_rank_dies():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29500 + (os.getpid() + 500) % 1000
+    procs = [ctx.Process(target=_failing_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert res[1] == "died"
+    assert res[0].startswith("error"), res[0]

@@ -606,3 +606,17 @@ def test_qk_norm_rope_fused_kv_write_equals_kv_append(cuda, D, with_copy):
         if x is not None:
             assert torch.equal(x.view(torch.int8) if x.dtype == torch.int8 else x.view(torch.int16),
                                y.view(torch.int8) if y.dtype == torch.int8 else y.view(torch.int16))
+
+
+def test_bounded_wait_reports_and_context_survives(cuda):
+    """Failure detection on the GPU without a fault: a wait on a barrier nothing completes gives up after ~1 ms
+    (2e6 cycles), the code lands in the device error word, od_device_error reads and clears it, and the next kernel
+    runs normally."""
+    assert _lib.device_error(cuda) == 0
+    _lib.selftest_bounded_wait(2_000_000, cuda)
+    assert _lib.device_error(cuda) == 0x7F0001
+    assert _lib.device_error(cuda) == 0                       # read and cleared
+    x = torch.randn(64, 256, generator=syn.gen(1)).to(torch.bfloat16).to(cuda)
+    q, s = _lib.quant_rows(x, scale_dtype=torch.float32)
+    qo, _, so = ops.quantize_rows(x.cpu().float().numpy(), "f32")
+    assert np.array_equal(q.cpu().numpy(), qo)
