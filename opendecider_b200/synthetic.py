@@ -11,6 +11,9 @@ Operator configurations (shapes of the reference's hot path):
 """
 from __future__ import annotations
 
+import re
+import zlib
+
 from dataclasses import dataclass
 
 import torch
@@ -85,24 +88,27 @@ class SyntheticTokenizer:
 
     pad_token_id = 0
 
+    _WORDS = re.compile(r"\n|[^\s]+")
+
     def __init__(self, vocab: int):
         self.vocab = vocab
+        self._fixed = {"\n": 1}          # template words seen so far -> id
 
     def __len__(self) -> int:
         return self.vocab
 
     def encode(self, text: str) -> list:
-        import re
-        import zlib
         out = []
-        for m in re.finditer(r"\n|[^\s]+", text):
-            w = m.group(0)
-            if w == "\n":
-                out.append(1)
-            elif re.fullmatch(r"t\d+", w):
-                out.append(int(w[1:]) % self.vocab)
+        V, fixed = self.vocab, self._fixed
+        for w in self._WORDS.findall(text):
+            d = w[1:]
+            if w[0] == "t" and d.isdecimal():                # the word t<id> (decimal digits, as t\d+ matches)
+                out.append(int(d) % V)
             else:
-                out.append(2 + zlib.crc32(w.encode()) % 14)
+                i = fixed.get(w)
+                if i is None:
+                    i = fixed[w] = 2 + zlib.crc32(w.encode()) % 14
+                out.append(i)
         return out
 
     def __call__(self, texts, add_special_tokens: bool = False):
