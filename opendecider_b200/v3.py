@@ -241,7 +241,8 @@ class RowPass:
     """One rectangular backbone pass over option (or question) rows, with the scatter of its real tokens."""
     spec: PassSpec
     dst: torch.Tensor | None = None     # destination index of each real token in the flat feature array
-    keep: torch.Tensor | None = None    # (R, w) bool: real tokens of the pass
+    keep: torch.Tensor | None = None    # flat (row * w + token) indices of the pass's real tokens, int64: gathering
+                                        # by index needs no device-to-host read, unlike a boolean mask
 
 
 @dataclass
@@ -259,6 +260,11 @@ class RowPlan:
     lp_first: torch.Tensor | None = None  # ... except an option's first token (these positions of the flat array)
     lp_qsrc: torch.Tensor | None = None # ... which takes its question's last token from q_flat
     lp_tok: torch.Tensor | None = None  # the option tokens (targets), int64
+
+
+def _flat_idx(mask: torch.Tensor) -> torch.Tensor:
+    """Flat indices of the True entries of a host mask (computed at plan time)."""
+    return torch.nonzero(mask.reshape(-1)).view(-1)
 
 
 def width_chunks(lengths: torch.Tensor, chunk: int, waste: float = 0.25) -> list:
@@ -327,7 +333,7 @@ def plan_rows(bb: Backbone, tok, questions, T: int, qcache: bool, list_cap: int 
         qpos = (T + torch.arange(Lq, dtype=torch.int32)).expand(N, Lq).contiguous()
         qkeep = torch.arange(Lq)[None, :] < lq[:, None]
         qpass = RowPass(PassSpec(ids=up(Qids), pos=up(qpos), own_hi=up(lq.to(torch.int32)), row_state=up(sidx),
-                                 capture=True, features=feats), keep=up(qkeep))
+                                 capture=True, features=feats), keep=up(_flat_idx(qkeep)))
         o_start = torch.cumsum(lo, 0) - lo
         order = torch.argsort(lo, stable=True)
         q_len_dev = up(lq.to(torch.int32))
@@ -347,7 +353,7 @@ def plan_rows(bb: Backbone, tok, questions, T: int, qcache: bool, list_cap: int 
             passes.append(RowPass(PassSpec(ids=up(ids), pos=up(pos), own_hi=up(ln.to(torch.int32)),
                                            row_state=up(sidx[rq]), row_q=up(rq.to(torch.int32)), q_len=q_len_dev,
                                            row_groups=up(grp), max_group_rows=int(grp[:, 1].max()),
-                                           features=feats), dst=up(dst), keep=up(keep)))
+                                           features=feats), dst=up(dst), keep=up(_flat_idx(keep))))
         return RowPlan(True, qpass, passes, int(lq.sum()), int(lo.sum()), lq, lo,
                        **(lm_sources(q_tok, o_tok, lq, lo, row_q, up) if lm else {}))
     rows_tok = [q_tok[int(row_q[i])] + o_tok[i] for i in range(M)]
@@ -365,7 +371,8 @@ def plan_rows(bb: Backbone, tok, questions, T: int, qcache: bool, list_cap: int 
         keep = (cols >= lq[row_q[rr]][:, None]) & (cols < (lq[row_q[rr]] + lo[rr])[:, None])
         dst = (o_dst_start[rr][:, None] + cols - lq[row_q[rr]][:, None])[keep]
         passes.append(RowPass(PassSpec(ids=up(ids[sl]), pos=up(pos), own_hi=up(ln[sl].to(torch.int32)),
-                                       row_state=up(sidx[row_q[sl]]), features=feats), dst=up(dst), keep=up(keep)))
+                                       row_state=up(sidx[row_q[sl]]), features=feats), dst=up(dst),
+                              keep=up(_flat_idx(keep))))
     first = torch.cumsum(n_opt, 0) - n_opt
     qr, qc, _, _, _ = segment_layout(lq, torch.arange(N), N)
     return RowPlan(False, None, passes, int(lq.sum()), int(lo.sum()), lq, lo, (up(first[qr]), up(qc)),
@@ -381,18 +388,18 @@ def run_rows(bb: Backbone, plan: RowPlan, cache: KVCache):
         qspec = plan.question.spec
         qspec.cache = cache
         fq, cap = bb.run(qspec)
-        q_flat = fq[plan.question.keep]
+        q_flat = fq.view(-1, fq.shape[-1])[plan.question.keep]
         for rp in plan.options:
             rp.spec.cache, rp.spec.qkv_prefix = cache, cap
             fo, _ = bb.run(rp.spec)
-            o_flat[rp.dst] = fo[rp.keep]
+            o_flat[rp.dst] = fo.view(-1, fo.shape[-1])[rp.keep]
         return q_flat, o_flat
     q_flat = None
     first_rows = []
     for rp in plan.options:
         rp.spec.cache = cache
         fo, _ = bb.run(rp.spec)
-        o_flat[rp.dst] = fo[rp.keep]
+        o_flat[rp.dst] = fo.view(-1, fo.shape[-1])[rp.keep]
         first_rows.append(fo)
     Fr = torch.cat(first_rows, 0) if len(first_rows) > 1 else first_rows[0]
     q_flat = Fr[plan.q_src]
