@@ -165,7 +165,10 @@ class Decider:
 
     def decide_many(self, requests) -> list:
         """Independent requests in one batch: ONE state pass over all states and ONE row pass over all questions,
-        each question reading its own request's state (decider.py:438-484). Returns per request {name: answer}."""
+        each question reading its own request's state (decider.py:438-484). Returns per request {name: answer}
+        (no requests: []; requests without questions: {} each, and no backbone pass)."""
+        if not requests or not any(r.questions for r in requests):
+            return [{} for _ in requests]
         plan = self.plan(requests)
         probs, _ = self.execute(plan)
         return self.answers(plan, probs)
