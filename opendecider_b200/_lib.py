@@ -303,7 +303,8 @@ _PLANS: dict = {}
 
 def _attn_plan(dims: AttnDims, dev) -> tuple[int, int]:
     """od_prefix_attn_plan for this GPU's SM count, cached per shape."""
-    key = (dev.index, dims.R, dims.t, dims.S, dims.T, dims.Hq, dims.Hkv, dims.D, dims.G, dims.max_group_rows)
+    key = (dev.index, dims.R, dims.t, dims.S, dims.T, dims.Hq, dims.Hkv, dims.D, dims.G, dims.max_group_rows,
+           dims.prefix_bf16)
     got = _PLANS.get(key)
     if got is None:
         sms = torch.cuda.get_device_properties(dev).multi_processor_count

@@ -553,6 +553,122 @@ def test_prefix_attn_plan_splits_small_launches(cuda):
     assert (o.float() - o1.float()).abs().max() < 1.6e-2
 
 
+def _few_slot_case(scale_dtype, seed):
+    """24 states x 2 groups (2 and 1 rows of 3 tokens, 32 / 8 heads: 24 and 12 query slots per group and KV head,
+    the few-slot form), 300-token int8 states with left pads, an end (p_hi) and a hole, a right-padded question
+    prefix and ragged own keys: 384 work items, several per CTA."""
+    g = syn.gen(seed)
+    S, T, Hq, Hkv, D, t = 24, 300, 32, 8, 128, 3
+    ac = syn.attn_case(S=S, T=T, rows=3, t=t, Hq=Hq, Hkv=Hkv, D=D, seed=seed)
+    Kq, Vq, ks, vs = ac.Kq, ac.Vq, ac.ks.reshape(S, Hkv, T), ac.vs.reshape(S, Hkv, T)
+    if scale_dtype == torch.bfloat16:                      # the backbone's cache: scales in the activation dtype
+        ks, vs = ks.to(torch.bfloat16), vs.to(torch.bfloat16)
+    R = S * 3
+    p_lo = torch.randint(0, 40, (S,), generator=g, dtype=torch.int32)
+    p_hi = T - torch.randint(0, 30, (S,), generator=g, dtype=torch.int32)
+    pmask = torch.ones(S, T, dtype=torch.uint8)
+    pmask[3, 100:180] = 0
+    NQ, Lq = S, 20
+    q_len = torch.randint(1, Lq + 1, (NQ,), generator=g, dtype=torch.int32)
+    Kqn = torch.randn(NQ, Lq, Hkv, D, generator=g).to(torch.bfloat16)
+    Vqn = torch.randn(NQ, Lq, Hkv, D, generator=g).to(torch.bfloat16)
+    row_q = ac.row_state.clone()                           # one question per state
+    own_hi = torch.randint(1, t + 1, (R,), generator=g, dtype=torch.int32)
+    groups = [(3 * s + a, n) for s in range(S) for a, n in ((0, 2), (2, 1))]
+    args = dict(Kp=Kq, Vp=Vq, ksc=ks, vsc=vs, row_state=ac.row_state, p_lo=p_lo, p_hi=p_hi, pmask=pmask, Kq=Kqn,
+                Vq=Vqn, row_q=row_q, q_len=q_len, own_hi=own_hi)
+    return ac, args, torch.tensor(groups, dtype=torch.int32), own_hi
+
+
+def _few_slot_ref(ac, args, r):
+    """Oracle for row r: the state prefix [p_lo, p_hi) with the hole, then the question's first q_len keys, then the
+    row's own keys (causal, below own_hi)."""
+    s, qr = int(args["row_state"][r]), int(args["row_q"][r])
+    sd = args["ksc"].dtype
+    Kp = ops.materialize_int8(args["Kp"][s], args["ksc"][s][..., None].to(sd))
+    Vp = ops.materialize_int8(args["Vp"][s], args["vsc"][s][..., None].to(sd))
+    T = Kp.shape[1]
+    pm = (torch.arange(T) >= args["p_lo"][s]) & (torch.arange(T) < args["p_hi"][s]) & args["pmask"][s].bool()
+    Lq = args["Kq"].shape[1]
+    Kc = torch.cat([Kp, args["Kq"][qr].transpose(0, 1)], 1)
+    Vc = torch.cat([Vp, args["Vq"][qr].transpose(0, 1)], 1)
+    pm = torch.cat([pm, torch.arange(Lq) < args["q_len"][qr]])
+    n = int(args["own_hi"][r])
+    o = ops.split_attention(ac.q[r:r + 1, :n].transpose(1, 2), ac.k[r:r + 1, :n].transpose(1, 2),
+                            ac.v[r:r + 1, :n].transpose(1, 2), Kc, Vc, pm, 128 ** -0.5)
+    return o.transpose(1, 2)[0], n
+
+
+@pytest.mark.parametrize("scale_dtype", [torch.float16, torch.bfloat16])
+def test_prefix_attn_few_slots_vs_oracle(cuda, scale_dtype):
+    """The few-slot form (keys on the tensor core's M side, persistent CTAs over (group, head, split) items) against
+    the oracle's split attention, with one CTA per state prefix and with the planned and an explicit split; the
+    split results merge to the unsplit ones."""
+    ac, args, groups, own_hi = _few_slot_case(scale_dtype, seed=61)
+    dargs = {k: v.to(cuda) for k, v in args.items()}
+    q, k, v = ac.q.to(cuda), ac.k.to(cuda), ac.v.to(cuda)
+    outs = {}
+    for ns in (1, None, 3):
+        o, lse = _lib.prefix_attn(q, k, v, 128 ** -0.5, row_groups=groups.to(cuda), max_group_rows=2, nsplit=ns,
+                                  want_lse=True, **dargs)
+        torch.cuda.synchronize()
+        assert _lib.device_error(cuda) == 0
+        outs[ns] = (o.cpu().float(), lse.cpu())
+    o1, l1 = outs[1]
+    for r in range(ac.q.shape[0]):
+        ref, n = _few_slot_ref(ac, args, r)
+        assert (o1[r, :n] - ref).abs().max() < 2e-2, r
+    for ns in (None, 3):
+        on, ln = outs[ns]
+        for r in range(ac.q.shape[0]):
+            n = int(own_hi[r])
+            assert (on[r, :n] - o1[r, :n]).abs().max() < 1.6e-2, (ns, r)
+            assert (ln[r, :, :n] - l1[r, :, :n]).abs().max() < 1e-4, (ns, r)
+
+
+def test_prefix_attn_few_slots_row_order_invariant(cuda):
+    """Few-slot form, rows alone (12 slots each): permuting the rows permutes the outputs and LSE bit for bit."""
+    ac = syn.attn_case(S=5, T=700, rows=7, t=3, Hq=32, Hkv=8, D=128, seed=67)
+    Kq, Vq, ks, vs = _attn_inputs(cuda, ac)
+    perm = torch.randperm(ac.q.shape[0], generator=syn.gen(2))
+    args = dict(Kp=Kq, Vp=Vq, ksc=ks, vsc=vs, want_lse=True)
+    o, l = _lib.prefix_attn(ac.q.to(cuda), ac.k.to(cuda), ac.v.to(cuda), 128 ** -0.5,
+                            row_state=ac.row_state.to(cuda), **args)
+    op, lp = _lib.prefix_attn(ac.q[perm].to(cuda), ac.k[perm].to(cuda), ac.v[perm].to(cuda), 128 ** -0.5,
+                              row_state=ac.row_state[perm].to(cuda), **args)
+    assert torch.equal(o[perm.to(cuda)], op)
+    assert torch.equal(l[perm.to(cuda)], lp)
+
+
+def test_prefix_attn_few_slots_fp16_dequant_exact(cuda):
+    """As test_prefix_attn_int8_dequant_exact with fp16 scales (BASELINE config 3's cache): one visible prefix key
+    per state, so each output is bf16(fp16(vq * vs)) bit for bit - over every int8 value and scales across the fp16
+    range, subnormals included."""
+    g = syn.gen(71)
+    S, T, Hq, Hkv, D, t = 4, 256, 8, 2, 128, 3
+    Vq = torch.randint(-128, 128, (S, Hkv, T, D), generator=g, dtype=torch.int8)
+    Kq = torch.randint(-128, 128, (S, Hkv, T, D), generator=g, dtype=torch.int8)
+    vs = (torch.rand(S, Hkv, T, generator=g) *
+          torch.pow(2.0, torch.randint(-24, 8, (S, Hkv, T), generator=g).float())).to(torch.float16)
+    ks = torch.full((S, Hkv, T), 0.01).to(torch.float16)
+    row_state = torch.tensor([0, 1, 2, 3, 1], dtype=torch.int32)
+    R = row_state.shape[0]
+    p_lo = torch.tensor([0, 5, 100, 255], dtype=torch.int32)
+    q = torch.randn(R, t, Hq, D, generator=g).to(torch.bfloat16)
+    k = torch.randn(R, t, Hkv, D, generator=g).to(torch.bfloat16)
+    zeros = torch.zeros(R, dtype=torch.int32, device=cuda)
+    o = _lib.prefix_attn(q.to(cuda), k.to(cuda), k.to(cuda), D ** -0.5, Kp=Kq.to(cuda), Vp=Vq.to(cuda),
+                         ksc=ks.to(cuda), vsc=vs.to(cuda), row_state=row_state.to(cuda), p_lo=p_lo.to(cuda),
+                         p_hi=(p_lo + 1).to(cuda), own_lo=zeros, own_hi=zeros).cpu()
+    deq = ops.materialize_int8(Vq, vs[..., None])                               # bf16(fp16(q * s))
+    rep = Hq // Hkv
+    for r in range(R):
+        s = int(row_state[r])
+        want = deq[s, :, int(p_lo[s]), :].repeat_interleave(rep, 0)
+        for i in range(t):
+            assert torch.equal(o[r, i].view(torch.int16), want.view(torch.int16)), (r, i)
+
+
 @pytest.mark.parametrize("M,H,V", [(300, 256, 1000), (130, 4096, 4099), (7, 64, 256)])
 def test_lm_logprob_matches_token_logprob(cuda, M, H, V):
     """Backbone.token_logprob on the tensor cores: bf16 logits, a vocabulary log-sum-exp (padded last tile left
