@@ -77,6 +77,7 @@ static_assert(Layout<128, 1>::BYTES <= 232448 && Layout<128, 2>::BYTES <= 232448
 
 struct Params {
   CUtensorMap map_ko, map_vo, map_kq, map_vq;   // bf16 (rows, Hkv*D) views of own / question K and V, 64x128 boxes
+  CUtensorMap map_ks, map_vs;                   // few-slot form: 1-D views of the int8 prefix's scales, 136-element boxes
   CUtensorMap map_kp, map_vp;                   // (S*Hkv*T, D) views of the state prefix: int8 with D x 128 boxes,
                                                 // or bf16 (materialised) with 64x128 boxes in the UMMA swizzle
   const __nv_bfloat16* q;
@@ -830,9 +831,9 @@ int64_t group_slots(const od_attn_dims& d) {
 // the int8 stream. Roles (13 warps):
 //   producers (8 warps)  each thread dequantises half of one key's K row (the raw int8 K block arrives 128-byte
 //                        swizzled, so lane i reads row i without bank conflicts) into its TMEM lane, and 4 chunks of
-//                        the V block into the UMMA layout, both exactly as materialize() rounds; the raw K and V
-//                        blocks come by TMA through a 4-deep ring (128 KB in flight per SM) that runs across item
-//                        boundaries; bf16 question-prefix and own keys are read directly
+//                        the V block into a double-buffered UMMA tile, both exactly as materialize() rounds; the raw
+//                        K and V blocks and their scales come by TMA through a 3-deep ring (96 KB in flight per SM)
+//                        that runs across item boundaries; bf16 question-prefix and own keys are read directly
 //   MMA (1 thread)       S^T of block j+1 is issued before P_j V_j, so the softmax of j+1 overlaps the P.V of j
 //   softmax (4 warps)    thread = one key of the block (its TMEM lane): 32 slot scores, the slot-wise running max
 //                        and sum reduced over the 128 keys by shuffle transposes and an exchange in shared memory,
@@ -851,7 +852,7 @@ constexpr int kProdWarps = 8;                // warps 5-12
 constexpr int kProd0 = 32 * (kSmWarps + 1);
 constexpr int kProds = 32 * kProdWarps;
 constexpr int kThreads = 32 * (kSmWarps + 1 + kProdWarps);
-constexpr int RD = 4;                        // raw int8 ring depth (a K block and a V block per stage)
+constexpr int RD = 3;                        // raw int8 ring depth (a K block, a V block and their scales)
 constexpr int MS = 4;                        // mask ring depth
 constexpr int PC = BN * D / 16 / kProds;     // 16-byte V chunks per producer thread and block
 constexpr int kMaxItems = 256;               // items of one CTA (its schedule table)
@@ -865,11 +866,14 @@ constexpr int VTILE = 2 * ATOM;              // 128 keys x 128 d bf16 (MN-major 
 constexpr int QATOM = NQ * 128;              // NQ rows x 128 B
 constexpr int QTILE = 2 * QATOM;             // NQ rows x 128 bf16 (K-major B operands Q and P^T)
 constexpr int RAWB = BN * D;                 // one raw int8 block
-constexpr int OFF_V = 0;
-constexpr int OFF_Q = OFF_V + VTILE;         // 2 buffers (item parity)
+constexpr int SCB = 136;                     // scales loaded per block: from the 8-aligned index below the first
+constexpr int SCBYTES = SCB * 2;             // (272 B, a multiple of 16)
+constexpr int OFF_V = 0;                     // 2 buffers (block parity)
+constexpr int OFF_Q = OFF_V + 2 * VTILE;     // 2 buffers (item parity)
 constexpr int OFF_P = OFF_Q + 2 * QTILE;     // 2 buffers (block parity)
 constexpr int OFF_RAW = OFF_P + 2 * QTILE;   // RD x (K block, V block)
-constexpr int OFF_TAB = OFF_RAW + RD * 2 * RAWB;
+constexpr int OFF_SC = OFF_RAW + RD * 2 * RAWB;   // RD x (K scales, V scales), 512 B each
+constexpr int OFF_TAB = OFF_SC + RD * 1024;
 constexpr int OFF_MASK = OFF_TAB + kMaxItems * kRec * 4;
 constexpr int OFF_XCH = OFF_MASK + MS * 16;  // 2 x (4 warps x 32 floats)
 constexpr int OFF_BAR = OFF_XCH + 2 * 128 * 4;
@@ -887,7 +891,7 @@ struct FqItem {
   int row0, nr, slots, g, split;
   int lo1, hi1, nb1;
   int qr, n2, nb2;
-  int own_begin, own_end, nb3, nblk;
+  int own_begin, own_end, nb3, nblk, st;
   int64_t prow;                                // row of key 0 of (state, head) in the (S*Hkv*T, D) views
 };
 
@@ -901,6 +905,7 @@ __device__ __forceinline__ void fq_item(const Params& P, const int* rec, int it,
   const bool last = I.split == P.nsplit - 1;
   I.nb1 = I.lo1 = I.hi1 = 0;
   I.prow = 0;
+  I.st = rec[2];
   if (P.Kp) {
     const int lo = rec[3], hi = rec[4];
     const int all = hi > lo ? (hi - lo + BN - 1) / BN : 0;
@@ -995,9 +1000,9 @@ __global__ void __launch_bounds__(fq::kThreads, 1) prefix_attn_fq_kernel(const _
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + fq::OFF_BAR);
   uint64_t* kfull = bars;                    // [2] producers (K_f in TMEM) -> MMA
   uint64_t* kempty = kfull + 2;              // [2] MMA (S_f complete: K_f read) -> producers
-  uint64_t* vfull = kempty + 2;              // producers (+ TMA bytes) -> MMA
-  uint64_t* vempty = vfull + 1;              // MMA (P_f V_f complete) -> producers
-  uint64_t* mfull = vempty + 1;              // [MSD] producer warps 0-3 (mask words) -> softmax
+  uint64_t* vfull = kempty + 2;              // [2] producers (+ TMA bytes) -> MMA
+  uint64_t* vempty = vfull + 2;              // [2] MMA (P_f V_f complete) -> producers
+  uint64_t* mfull = vempty + 2;              // [MSD] producer warps 0-3 (mask words) -> softmax
   uint64_t* s_full = mfull + MSD;            // [2] MMA (S_f in TMEM) -> softmax
   uint64_t* s_free = s_full + 2;             // [2] softmax (S_f read) -> MMA
   uint64_t* p_full = s_free + 2;             // [2] softmax (P_f in shared memory, O rescaled) -> MMA
@@ -1016,7 +1021,7 @@ __global__ void __launch_bounds__(fq::kThreads, 1) prefix_attn_fq_kernel(const _
   uint32_t* masks = reinterpret_cast<uint32_t*>(sm + fq::OFF_MASK);
   float* xch = reinterpret_cast<float*>(sm + fq::OFF_XCH);
   int* tab = reinterpret_cast<int*>(sm + fq::OFF_TAB);
-  static_assert(2 + 2 + 1 + 1 + MSD + 2 + 2 + 2 + 2 + 1 + 2 + 2 + 4 * RD + 1 + 1 <= fq::kBars, "barriers");
+  static_assert(2 + 2 + 2 + 2 + MSD + 2 + 2 + 2 + 2 + 1 + 2 + 2 + 4 * RD + 1 + 1 <= fq::kBars, "barriers");
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nk = P.n_items > static_cast<int>(blockIdx.x)
@@ -1036,8 +1041,10 @@ __global__ void __launch_bounds__(fq::kThreads, 1) prefix_attn_fq_kernel(const _
       mbar_init(&q_full[b], kProds);
       mbar_init(&q_empty[b], 1);
     }
-    mbar_init(vfull, kProds);
-    mbar_init(vempty, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&vfull[b], kProds);
+      mbar_init(&vempty[b], 1);
+    }
     for (int b = 0; b < MSD; ++b) mbar_init(&mfull[b], 4);
     mbar_init(pv_done, 1);
     for (int r = 0; r < RD; ++r) {
@@ -1084,44 +1091,27 @@ __global__ void __launch_bounds__(fq::kThreads, 1) prefix_attn_fq_kernel(const _
     const int quarter = warp & 3, half = pw >> 2;   // this warp's TMEM lane quarter; the d half of its K rows
     const int kkey = 32 * quarter + lane;           // the key (TMEM lane) whose K row half this thread converts
     const bool i8 = P.Kp != nullptr;
-    // scales (raw 16-bit patterns) and the visibility byte of the next int8 block, loaded one block ahead
-    uint32_t skc = 0, svc[PC];
-#pragma unroll
-    for (int it = 0; it < PC; ++it) svc[it] = 0u;
-    uint32_t pmk = 1;
-    FqCursor sc, ld;                                // next int8 block to convert; next one to load (pt == 0)
-    sc.valid = ld.valid = false;
-    auto prefetch = [&]() {
-      if (!sc.valid) return;
-      const int k0 = sc.lo1 + sc.j * BN;
-      const unsigned short* ks = static_cast<const unsigned short*>(P.ksc) + sc.prow;
-      const unsigned short* vs = static_cast<const unsigned short*>(P.vsc) + sc.prow;
-      skc = k0 + kkey < sc.hi1 ? static_cast<uint32_t>(__ldg(ks + k0 + kkey)) : 0u;
-#pragma unroll
-      for (int it = 0; it < PC; ++it) {
-        const int p = k0 + (pt >> 3) + 32 * it;
-        svc[it] = p < sc.hi1 ? static_cast<uint32_t>(__ldg(vs + p)) : 0u;
-      }
-      if (pt < BN && P.pmask)
-        pmk = k0 + pt < sc.hi1 ? P.pmask[static_cast<int64_t>(sc.st) * P.T + k0 + pt] : 0u;
-    };
+    FqCursor ld;                                    // next int8 block to load (pt == 0)
+    ld.valid = false;
     int nk_iss = 0, nv_iss = 0;                     // raw K / V loads issued (pt == 0)
+    // a raw block and the scales of its keys, from the 8-aligned index at or below its first key (the scale TMA's
+    // start must be 16-byte aligned; indices past the tensor read as 0)
     auto load_k = [&](int r) {
-      mbar_arrive_expect_tx(&rawk_full[r], RAWB);
-      tma_load_2d(sm + fq::OFF_RAW + r * 2 * RAWB, &P.map_kp, &rawk_full[r], 0,
-                  static_cast<int>(ld.prow + ld.lo1 + ld.j * BN));
+      const int row = static_cast<int>(ld.prow + ld.lo1 + ld.j * BN);
+      mbar_arrive_expect_tx(&rawk_full[r], RAWB + fq::SCBYTES);
+      tma_load_2d(sm + fq::OFF_RAW + r * 2 * RAWB, &P.map_kp, &rawk_full[r], 0, row);
+      tma_load_1d(sm + fq::OFF_SC + r * 1024, &P.map_ks, &rawk_full[r], row & ~7);
       ++nk_iss;
     };
     auto load_v = [&](int r) {
-      mbar_arrive_expect_tx(&rawv_full[r], RAWB);
-      tma_load_2d(sm + fq::OFF_RAW + r * 2 * RAWB + RAWB, &P.map_vp, &rawv_full[r], 0,
-                  static_cast<int>(ld.prow + ld.lo1 + ld.j * BN));
+      const int row = static_cast<int>(ld.prow + ld.lo1 + ld.j * BN);
+      mbar_arrive_expect_tx(&rawv_full[r], RAWB + fq::SCBYTES);
+      tma_load_2d(sm + fq::OFF_RAW + r * 2 * RAWB + RAWB, &P.map_vp, &rawv_full[r], 0, row);
+      tma_load_1d(sm + fq::OFF_SC + r * 1024 + 512, &P.map_vs, &rawv_full[r], row & ~7);
       ++nv_iss;
       fq_next(P, tab, nk, ld);
     };
     if (i8) {
-      fq_seek(P, tab, nk, sc, 0);
-      prefetch();
       if (pt == 0) {
         fq_seek(P, tab, nk, ld, 0);
         for (int r = 0; r < RD && ld.valid; ++r) {
@@ -1184,6 +1174,11 @@ __global__ void __launch_bounds__(fq::kThreads, 1) prefix_attn_fq_kernel(const _
             break;
           }
           const uint8_t* row = sm + fq::OFF_RAW + r * 2 * RAWB + kkey * D;
+          const int sofs = static_cast<int>((I.prow + k0) & 7);   // first key's index in the staged scales
+          const uint32_t skc =
+              k0 + kkey < I.hi1
+                  ? static_cast<uint32_t>(reinterpret_cast<const unsigned short*>(sm + fq::OFF_SC + r * 1024)[sofs + kkey])
+                  : 0u;
 #pragma unroll
           for (int c4 = 0; c4 < 4; ++c4) {
             const int ch = 4 * half + c4;
@@ -1232,7 +1227,7 @@ __global__ void __launch_bounds__(fq::kThreads, 1) prefix_attn_fq_kernel(const _
           const int idx = k0 + pt;
           bool vis;
           if (pre) {
-            vis = idx < I.hi1 && pmk != 0;
+            vis = idx < I.hi1 && (!P.pmask || P.pmask[static_cast<int64_t>(I.st) * P.T + idx] != 0);
           } else if (qseg) {
             vis = idx < I.n2;
           } else {
@@ -1248,7 +1243,7 @@ __global__ void __launch_bounds__(fq::kThreads, 1) prefix_attn_fq_kernel(const _
           }
         }
         // ---- V_f into the shared-memory A operand
-        if (f >= 1 && !warp_wait(vempty, (f - 1) & 1, abort_flag, P.err, kErrFq | 5)) {
+        if (f >= 2 && !warp_wait(&vempty[f & 1], ((f >> 1) - 1) & 1, abort_flag, P.err, kErrFq | 5)) {
           live = false;
           break;
         }
@@ -1258,18 +1253,22 @@ __global__ void __launch_bounds__(fq::kThreads, 1) prefix_attn_fq_kernel(const _
             break;
           }
           const uint8_t* raw = sm + fq::OFF_RAW + r * 2 * RAWB + RAWB;
+          const unsigned short* vsc_s = reinterpret_cast<const unsigned short*>(sm + fq::OFF_SC + r * 1024 + 512) +
+                                        ((I.prow + k0) & 7);
+          uint8_t* vt = sm + fq::OFF_V + (f & 1) * VTILE;
 #pragma unroll
           for (int it = 0; it < PC; ++it) {
             const int c = pt + it * kProds, key = c >> 3, ch = c & 7;
             const uint4 q = *reinterpret_cast<const uint4*>(raw + key * D + ch * 16);
+            const uint32_t svk = k0 + key < I.hi1 ? static_cast<uint32_t>(vsc_s[key]) : 0u;
             uint32_t w8[8];
-            dequant16<TS>(q, svc[it], w8);
+            dequant16<TS>(q, svk, w8);
             // chunks 2ch and 2ch+1 of the row; threads with ch >= 4 store their odd chunk first, so the 8 threads
             // of a row hit 8 distinct bank groups in each store
             const uint4 lo = make_uint4(w8[0], w8[1], w8[2], w8[3]), hi = make_uint4(w8[4], w8[5], w8[6], w8[7]);
             const bool sw = ch >= 4;
-            *reinterpret_cast<uint4*>(sm + fq::OFF_V + swz(key, 2 * ch + (sw ? 1 : 0), ATOM)) = sw ? hi : lo;
-            *reinterpret_cast<uint4*>(sm + fq::OFF_V + swz(key, 2 * ch + (sw ? 0 : 1), ATOM)) = sw ? lo : hi;
+            *reinterpret_cast<uint4*>(vt + swz(key, 2 * ch + (sw ? 1 : 0), ATOM)) = sw ? hi : lo;
+            *reinterpret_cast<uint4*>(vt + swz(key, 2 * ch + (sw ? 0 : 1), ATOM)) = sw ? lo : hi;
           }
           mbar_arrive(&rawv_empty[r]);
           bool ok_ = true;
@@ -1281,19 +1280,18 @@ __global__ void __launch_bounds__(fq::kThreads, 1) prefix_attn_fq_kernel(const _
             live = false;
             break;
           }
-          fq_next(P, tab, nk, sc);
-          prefetch();
           ++u;
           fence_proxy_async_smem();
-          mbar_arrive(vfull);
+          mbar_arrive(&vfull[f & 1]);
         } else if (pt == 0) {
           const CUtensorMap* mv = qseg ? &P.map_vq : &P.map_vo;
           const int y = (qseg ? I.qr * static_cast<int>(P.Lq) : I.row0 * t) + k0;
-          mbar_arrive_expect_tx(vfull, VTILE);
+          mbar_arrive_expect_tx(&vfull[f & 1], VTILE);
 #pragma unroll
-          for (int h = 0; h < 2; ++h) tma_load_2d(sm + fq::OFF_V + h * ATOM, mv, vfull, I.g * D + h * 64, y);
+          for (int h = 0; h < 2; ++h)
+            tma_load_2d(sm + fq::OFF_V + (f & 1) * VTILE + h * ATOM, mv, &vfull[f & 1], I.g * D + h * 64, y);
         } else {
-          mbar_arrive(vfull);
+          mbar_arrive(&vfull[f & 1]);
         }
       }
     }
@@ -1318,17 +1316,18 @@ __global__ void __launch_bounds__(fq::kThreads, 1) prefix_attn_fq_kernel(const _
       int f = 0, pf = 0, pob = 0;
       bool live = true, pend = false, pfirst = false;
       auto issue_pv = [&]() -> bool {
-        if (!mbar_wait(vfull, pf & 1, abort_flag, P.err, kErrFq | 8) ||
+        if (!mbar_wait(&vfull[pf & 1], (pf >> 1) & 1, abort_flag, P.err, kErrFq | 8) ||
             !mbar_wait(&p_full[pf & 1], (pf >> 1) & 1, abort_flag, P.err, kErrFq | 9))
           return false;
         tc_fence_after();
-        const uint32_t sV = smem_u32(sm + fq::OFF_V), sP = smem_u32(sm + fq::OFF_P + (pf & 1) * QTILE);
+        const uint32_t sV = smem_u32(sm + fq::OFF_V + (pf & 1) * VTILE);
+        const uint32_t sP = smem_u32(sm + fq::OFF_P + (pf & 1) * QTILE);
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk)
           mma_f16(tmem + fq::kTmemO + pob * NQ, desc_sw128(sV + kk * 16 * 128, ATOM, 1024),
                   desc_sw128(sP + (kk >> 2) * QATOM + (kk & 3) * 32, 16, 1024), idesc_o,
                   (pfirst && kk == 0) ? 0u : 1u);
-        mma_commit(vempty);
+        mma_commit(&vempty[pf & 1]);
         mma_commit(&p_empty[pf & 1]);
         mma_commit(pv_done);
         return true;
@@ -1597,6 +1596,21 @@ int make_map_i8_sw128(CUtensorMap* map, const void* base, uint64_t rows) {
   return OD_OK;
 }
 
+// 1-D view of n 16-bit scales (fp16 or bf16 bit patterns) tiled into 136-element boxes (zero past the end)
+int make_map_scales(CUtensorMap* map, const void* base, uint64_t n) {
+  auto fn = encode_fn();
+  if (!fn) return fail(OD_ECUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[1] = {n};
+  cuuint64_t strides[1] = {0};
+  cuuint32_t box[1] = {static_cast<cuuint32_t>(fq::SCB)};
+  cuuint32_t estr[1] = {1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 1, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(OD_ECUDA, "cuTensorMapEncodeTiled (scales) failed (%d)", static_cast<int>(r));
+  return OD_OK;
+}
+
 int num_sms_current() {
   static int sms[64] = {0};
   int dev = 0;
@@ -1674,7 +1688,8 @@ extern "C" int od_prefix_attn(const void* q, const void* Kp, const void* Vp, con
                (long long)(static_cast<int64_t>(sizeof(float)) * nsplit * n_part * (dims.D + 1)));
   if (G == 0 || dims.t == 0) return ok();
   // at most 32 query slots per group and KV head: the few-slot form
-  const bool fewq = dims.D == fq::D && gslots <= fq::NQ && !(Kp && pbf16);
+  // (its scale tensor maps need 16-byte aligned scale arrays)
+  const bool fewq = dims.D == fq::D && gslots <= fq::NQ && !(Kp && pbf16) && (!Kp || (aligned16(ksc) && aligned16(vsc)));
   int32_t* err = device_error_word();
   if (!err) return fail(OD_ECUDA, "od_prefix_attn: no device error word");
   Params P;
@@ -1735,6 +1750,8 @@ extern "C" int od_prefix_attn(const void* q, const void* Kp, const void* Vp, con
       } else {
         rc = fewq ? make_map_i8_sw128(&P.map_kp, Kp, prows)
                   : make_map_i8(&P.map_kp, Kp, static_cast<uint64_t>(dims.D), prows);
+        if (!rc && fewq) rc = make_map_scales(&P.map_ks, ksc, prows);
+        if (!rc && fewq) rc = make_map_scales(&P.map_vs, vsc, prows);
         if (!rc) rc = make_map_i8(&P.map_vp, Vp, static_cast<uint64_t>(dims.D), prows);
       }
     }

@@ -661,6 +661,9 @@ def test_prefix_attn_few_slots_fp16_dequant_exact(cuda):
                          ksc=ks.to(cuda), vsc=vs.to(cuda), row_state=row_state.to(cuda), p_lo=p_lo.to(cuda),
                          p_hi=(p_lo + 1).to(cuda), own_lo=zeros, own_hi=zeros).cpu()
     deq = ops.materialize_int8(Vq, vs[..., None])                               # bf16(fp16(q * s))
+    # an fp16 product that underflows is -0 for a negative q; a weighted sum started from +0 (here, as in the
+    # reference's softmax(S) @ V) returns +0 there, so zeros compare without their sign
+    deq = torch.where(deq == 0, torch.zeros_like(deq), deq)
     rep = Hq // Hkv
     for r in range(R):
         s = int(row_state[r])
