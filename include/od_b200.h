@@ -175,10 +175,7 @@ OD_API int od_gate_quant(const void* o, const void* qkv, int64_t ldqkv, int64_t 
  * workspace (16-byte aligned) holds nsplit x R x t x Hq x (D + 1) floats. od_prefix_attn_plan picks nsplit for a
  * GPU of num_sms SMs and returns the workspace size; workspace may be NULL when nsplit <= 1.
  * Every row sees the same key layout whatever its index or group: outputs do not depend on row order.
- * Runs on tcgen05 (S = Q K^T and O += P V in TMEM); head_dim 64 or 128. Launches whose groups hold at most 32
- * query slots per KV head (rows x t x Hq/Hkv <= 32, head_dim 128, an int8 state prefix or none) take a bandwidth
- * form with the block's keys on the tensor core's M side (S^T = K Q^T, O^T += V^T P^T) and persistent CTAs over
- * (group, KV head, split) items; same results within bf16 rounding, same workspace contract.
+ * Runs on tcgen05 (S = Q K^T and O += P V in TMEM); head_dim 64 or 128.
  */
 typedef struct {
   int64_t R, t, S, T, NQ, Lq;   /* rows, tokens per row, states, prefix capacity, questions, question length */

@@ -26,7 +26,6 @@
 
 #include <string.h>
 
-#include <algorithm>
 #include <type_traits>
 
 #include "sm100.cuh"
@@ -77,7 +76,6 @@ static_assert(Layout<128, 1>::BYTES <= 232448 && Layout<128, 2>::BYTES <= 232448
 
 struct Params {
   CUtensorMap map_ko, map_vo, map_kq, map_vq;   // bf16 (rows, Hkv*D) views of own / question K and V, 64x128 boxes
-  CUtensorMap map_ks, map_vs;                   // few-slot form: 1-D views of the int8 prefix's scales, 136-element boxes
   CUtensorMap map_kp, map_vp;                   // (S*Hkv*T, D) views of the state prefix: int8 with D x 128 boxes,
                                                 // or bf16 (materialised) with 64x128 boxes in the UMMA swizzle
   const __nv_bfloat16* q;
@@ -108,7 +106,6 @@ struct Params {
   float* part_o;                                // nsplit > 1: per split, O / l (fp32, the layout of o) ...
   float* part_lse;                              // ... and the natural-log LSE (the layout of lse)
   float scale_log2;
-  int n_items;                                  // few-slot form: (group, KV head, split) work items
 };
 
 // byte offset of 16-byte chunk `ch` of row `row` in a 128B-swizzled tile made of `atom`-byte column atoms
@@ -154,37 +151,6 @@ __device__ __forceinline__ void load_scales(uint32_t (&sc)[Piece<D>::N], int pt,
   }
 }
 
-// 16 int8 values of one key (one 16-byte chunk) dequantised exactly as materialize() rounds, with the key's scale
-// `sc` (raw 16-bit pattern): eight bf16 pairs, lower element in the low half.
-template <typename TS>
-__device__ __forceinline__ void dequant16(const uint4 q, uint32_t sc, uint32_t (&w)[8]) {
-  const uint32_t s2 = sc | (sc << 16);
-  if (std::is_same<TS, __nv_bfloat16>::value) {
-    dequant4_bf16(q.x, s2, w[0], w[1]);
-    dequant4_bf16(q.y, s2, w[2], w[3]);
-    dequant4_bf16(q.z, s2, w[4], w[5]);
-    dequant4_bf16(q.w, s2, w[6], w[7]);
-  } else {
-    // fp16 scales: bf16(fp16(q * s)) without conversion instructions. The byte q + 128 placed under the fp16
-    // exponent of 1024 reads as 1024 + q + 128 (exact), minus 1152 gives q exactly; the packed fp16 multiply
-    // rounds q * s once, as the reference's fp16 multiply does (q * s is exact in fp32); widening to fp32 is exact
-    // and the bf16 pack rounds to nearest even.
-    const __half2 sh = *reinterpret_cast<const __half2*>(&s2);
-    const __half2 bias = __float2half2_rn(1152.0f);
-    const uint32_t words[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-    for (int b = 0; b < 4; ++b) {
-      const uint32_t u = words[b] ^ 0x80808080u;
-      const uint32_t lo = __byte_perm(u, 0x64646464u, 0x4140), hi = __byte_perm(u, 0x64646464u, 0x4342);
-      const __half2 qlo = __hsub2(*reinterpret_cast<const __half2*>(&lo), bias);
-      const __half2 qhi = __hsub2(*reinterpret_cast<const __half2*>(&hi), bias);
-      const float2 plo = __half22float2(__hmul2(qlo, sh)), phi = __half22float2(__hmul2(qhi, sh));
-      w[2 * b] = pack_bf16(plo.x, plo.y);
-      w[2 * b + 1] = pack_bf16(phi.x, phi.y);
-    }
-  }
-}
-
 // Dequantise a staged int8 block (row-major, D bytes per key) into a bf16 stage exactly as materialize() rounds.
 template <typename TS, int D>
 __device__ __forceinline__ void convert_piece(const uint8_t* raw, const uint32_t (&sc)[Piece<D>::N], uint8_t* dst,
@@ -197,7 +163,32 @@ __device__ __forceinline__ void convert_piece(const uint8_t* raw, const uint32_t
     const int key = c / CPR, ch = c % CPR;
     const uint4 q = *reinterpret_cast<const uint4*>(raw + key * D + ch * 16);
     uint32_t w[8];
-    dequant16<TS>(q, sc[it], w);
+    if (std::is_same<TS, __nv_bfloat16>::value) {
+      const uint32_t s2 = sc[it] | (sc[it] << 16);
+      dequant4_bf16(q.x, s2, w[0], w[1]);
+      dequant4_bf16(q.y, s2, w[2], w[3]);
+      dequant4_bf16(q.z, s2, w[4], w[5]);
+      dequant4_bf16(q.w, s2, w[6], w[7]);
+    } else {
+      // fp16 scales: bf16(fp16(q * s)) without conversion instructions. The byte q + 128 placed under the fp16
+      // exponent of 1024 reads as 1024 + q + 128 (exact), minus 1152 gives q exactly; the packed fp16 multiply
+      // rounds q * s once, as the reference's fp16 multiply does (q * s is exact in fp32); widening to fp32 is exact
+      // and the bf16 pack rounds to nearest even.
+      const uint32_t s2 = sc[it] | (sc[it] << 16);
+      const __half2 sh = *reinterpret_cast<const __half2*>(&s2);
+      const __half2 bias = __float2half2_rn(1152.0f);
+      const uint32_t words[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        const uint32_t u = words[b] ^ 0x80808080u;
+        const uint32_t lo = __byte_perm(u, 0x64646464u, 0x4140), hi = __byte_perm(u, 0x64646464u, 0x4342);
+        const __half2 qlo = __hsub2(*reinterpret_cast<const __half2*>(&lo), bias);
+        const __half2 qhi = __hsub2(*reinterpret_cast<const __half2*>(&hi), bias);
+        const float2 plo = __half22float2(__hmul2(qlo, sh)), phi = __half22float2(__hmul2(qhi, sh));
+        w[2 * b] = pack_bf16(plo.x, plo.y);
+        w[2 * b + 1] = pack_bf16(phi.x, phi.y);
+      }
+    }
     // the 16 int8 values of chunk ch are bf16 chunks 2ch and 2ch+1 of the row
     *reinterpret_cast<uint4*>(dst + swz(key, 2 * ch, ATOM)) = make_uint4(w[0], w[1], w[2], w[3]);
     *reinterpret_cast<uint4*>(dst + swz(key, 2 * ch + 1, ATOM)) = make_uint4(w[4], w[5], w[6], w[7]);
@@ -820,832 +811,6 @@ int64_t group_slots(const od_attn_dims& d) {
   return rows * d.t * (d.Hq / (d.Hkv > 0 ? d.Hkv : 1));
 }
 
-// ================================================================================================ few-slot form
-// Launches whose row groups hold at most 32 query slots per KV head (a few short rows over a long int8 state: a
-// yes/no question, a short record batch) read every state block for little math: with the slots on the M side of a
-// 128-row tensor-core tile most of it is padding, and the int8 stream is bound by the latency of each block's chain.
-// This form puts the block's 128 keys on M and the group's slots on N = 32:
-//   S^T  = K_j Q^T       A = dequantised K block in TMEM (written by the producers), B = Q (shared, K-major)
-//   O^T += V_j^T P^T     A = dequantised V block (shared, MN-major), B = P^T (shared, K-major)
-// so each tensor-core op is a quarter of the form above and shared memory carries only the V block, Q and P next to
-// the int8 stream. Roles (13 warps):
-//   producers (8 warps)  each thread dequantises half of one key's K row (the raw int8 K block arrives 128-byte
-//                        swizzled, so lane i reads row i without bank conflicts) into its TMEM lane, and 4 chunks of
-//                        the V block into a double-buffered UMMA tile, both exactly as materialize() rounds; the raw
-//                        K and V blocks and their scales come by TMA through a 3-deep ring (96 KB in flight per SM)
-//                        that runs across item boundaries; bf16 question-prefix and own keys are read directly
-//   MMA (1 thread)       S^T of block j+1 is issued before P_j V_j, so the softmax of j+1 overlaps the P.V of j
-//   softmax (4 warps)    thread = one key of the block (its TMEM lane): 32 slot scores, the slot-wise running max
-//                        and sum reduced over the 128 keys by shuffle transposes and an exchange in shared memory,
-//                        lazy rescale (only when a slot's max grows by more than 2^8), P^T (bf16) to shared memory;
-//                        at an item's end O^T / l per slot (thread = one of the 128 output dimensions)
-// CTAs are persistent: CTA c takes items c, c + grid, ... of (row group, KV head, prefix split); their schedules are
-// decoded once into a shared-memory table when the CTA starts. Slots are independent of each other, so outputs do
-// not depend on row order. Every wait is bounded, and every warp-wide instruction runs on a converged warp (waits
-// and refill outcomes are agreed across the warp before it).
-namespace fq {
-constexpr int NQ = 32;                       // query slots of an item (the N of both MMAs)
-constexpr int D = 128;
-constexpr int kSmWarps = 4;                  // warps 0-3: softmax / epilogue (TMEM lane quarter = warp)
-constexpr int kMmaWarp = 4;                  // warp 4: TMEM allocation, MMA issue
-constexpr int kProdWarps = 8;                // warps 5-12
-constexpr int kProd0 = 32 * (kSmWarps + 1);
-constexpr int kProds = 32 * kProdWarps;
-constexpr int kThreads = 32 * (kSmWarps + 1 + kProdWarps);
-constexpr int RD = 3;                        // raw int8 ring depth (a K block, a V block and their scales)
-constexpr int MS = 4;                        // mask ring depth
-constexpr int PC = BN * D / 16 / kProds;     // 16-byte V chunks per producer thread and block
-constexpr int kMaxItems = 256;               // items of one CTA (its schedule table)
-constexpr int kRec = 8;                      // ints per table record
-constexpr uint32_t kTmemCols = 256;
-constexpr uint32_t kTmemS = 0;               // S^T of block f at column (f & 1) * NQ
-constexpr uint32_t kTmemO = 2 * NQ;          // O^T of item k at column kTmemO + (k & 1) * NQ
-constexpr uint32_t kTmemK = 4 * NQ;          // K of block f (bf16 pairs) at column kTmemK + (f & 1) * D / 2
-constexpr int ATOM = 128 * 128;              // 128 rows x 128 B
-constexpr int VTILE = 2 * ATOM;              // 128 keys x 128 d bf16 (MN-major A operand)
-constexpr int QATOM = NQ * 128;              // NQ rows x 128 B
-constexpr int QTILE = 2 * QATOM;             // NQ rows x 128 bf16 (K-major B operands Q and P^T)
-constexpr int RAWB = BN * D;                 // one raw int8 block
-constexpr int SCB = 136;                     // scales loaded per block: from the 8-aligned index below the first
-constexpr int SCBYTES = SCB * 2;             // (272 B, a multiple of 16)
-constexpr int OFF_V = 0;                     // 2 buffers (block parity)
-constexpr int OFF_Q = OFF_V + 2 * VTILE;     // 2 buffers (item parity)
-constexpr int OFF_P = OFF_Q + 2 * QTILE;     // 2 buffers (block parity)
-constexpr int OFF_RAW = OFF_P + 2 * QTILE;   // RD x (K block, V block)
-constexpr int OFF_SC = OFF_RAW + RD * 2 * RAWB;   // RD x (K scales, V scales), 512 B each
-constexpr int OFF_TAB = OFF_SC + RD * 1024;
-constexpr int OFF_MASK = OFF_TAB + kMaxItems * kRec * 4;
-constexpr int OFF_XCH = OFF_MASK + MS * 16;  // 2 x (4 warps x 32 floats)
-constexpr int OFF_BAR = OFF_XCH + 2 * 128 * 4;
-constexpr int kBars = 44;
-constexpr int BYTES = OFF_BAR + kBars * 8 + 16 + 1024;
-constexpr int32_t kErrFq = kErrAttn | 0x100;
-static_assert(PC * kProds * 16 == BN * D, "V chunks");
-static_assert(OFF_RAW % 1024 == 0 && RAWB % 1024 == 0, "swizzled raw K blocks need 1024-byte alignment");
-static_assert(BYTES <= 232448, "shared memory");
-static_assert(kTmemK + 2 * D / 2 <= kTmemCols, "TMEM columns");
-}  // namespace fq
-
-// One work item's schedule, from its table record (row0, rows, state, p_lo, p_hi, question, q_len, own_lo of row0).
-struct FqItem {
-  int row0, nr, slots, g, split;
-  int lo1, hi1, nb1;
-  int qr, n2, nb2;
-  int own_begin, own_end, nb3, nblk, st;
-  int64_t prow;                                // row of key 0 of (state, head) in the (S*Hkv*T, D) views
-};
-
-__device__ __forceinline__ void fq_item(const Params& P, const int* rec, int it, FqItem& I) {
-  I.split = it % P.nsplit;
-  I.g = (it / P.nsplit) % P.Hkv;
-  I.row0 = rec[0];
-  I.nr = rec[1];
-  const int t = static_cast<int>(P.t);
-  I.slots = I.nr * t * P.rep;
-  const bool last = I.split == P.nsplit - 1;
-  I.nb1 = I.lo1 = I.hi1 = 0;
-  I.prow = 0;
-  I.st = rec[2];
-  if (P.Kp) {
-    const int lo = rec[3], hi = rec[4];
-    const int all = hi > lo ? (hi - lo + BN - 1) / BN : 0;
-    const int per = (all + P.nsplit - 1) / P.nsplit;
-    const int b0 = min(all, I.split * per), b1 = min(all, b0 + per);
-    I.nb1 = b1 - b0;
-    I.lo1 = lo + b0 * BN;
-    I.hi1 = min(hi, I.lo1 + I.nb1 * BN);
-    I.prow = (static_cast<int64_t>(rec[2]) * P.Hkv + I.g) * P.T;
-  }
-  I.qr = rec[5];
-  I.n2 = P.Kq && last ? rec[6] : 0;
-  I.nb2 = (I.n2 + BN - 1) / BN;
-  I.own_begin = 0;
-  I.own_end = last ? I.nr * t : 0;
-  if (I.nr == 1 && last) {
-    I.own_begin = (rec[7] / BN) * BN;
-    I.own_end = t;
-  }
-  I.nb3 = I.own_end > I.own_begin ? (I.own_end - I.own_begin + BN - 1) / BN : 0;
-  I.nblk = I.nb1 + I.nb2 + I.nb3;
-}
-
-// Position in the sequence of int8 state-prefix blocks a CTA consumes (items in order, their prefix blocks in order).
-struct FqCursor {
-  int k, j, nb1, lo1, hi1, st;
-  int64_t prow;
-  bool valid;
-};
-
-__device__ __forceinline__ void fq_seek(const Params& P, const int* tab, int nk, FqCursor& c, int k) {
-  c.valid = false;
-  for (; k < nk; ++k) {
-    FqItem I;
-    fq_item(P, tab + fq::kRec * k, blockIdx.x + k * gridDim.x, I);
-    if (I.nb1 > 0) {
-      c.k = k;
-      c.j = 0;
-      c.nb1 = I.nb1;
-      c.lo1 = I.lo1;
-      c.hi1 = I.hi1;
-      c.st = tab[fq::kRec * k + 2];
-      c.prow = I.prow;
-      c.valid = true;
-      return;
-    }
-  }
-}
-__device__ __forceinline__ void fq_next(const Params& P, const int* tab, int nk, FqCursor& c) {
-  if (++c.j >= c.nb1) fq_seek(P, tab, nk, c, c.k + 1);
-}
-
-// In lane l: op over the warp's 32 lanes of v[l] (a transpose-reduce: 31 shuffles for 32 values; every lane
-// shuffles at every step).
-template <bool kMax>
-__device__ __forceinline__ float transpose_reduce(const float (&v)[32], int lane) {
-  auto op = [](float a, float b) { return kMax ? fmaxf(a, b) : a + b; };
-  float a[16], b[8], c[4], d[2];
-  const bool h4 = lane & 16, h3 = lane & 8, h2 = lane & 4, h1 = lane & 2, h0 = lane & 1;
-#pragma unroll
-  for (int i = 0; i < 16; ++i)
-    a[i] = op(h4 ? v[i + 16] : v[i], __shfl_xor_sync(0xffffffffu, h4 ? v[i] : v[i + 16], 16));
-#pragma unroll
-  for (int i = 0; i < 8; ++i) b[i] = op(h3 ? a[i + 8] : a[i], __shfl_xor_sync(0xffffffffu, h3 ? a[i] : a[i + 8], 8));
-#pragma unroll
-  for (int i = 0; i < 4; ++i) c[i] = op(h2 ? b[i + 4] : b[i], __shfl_xor_sync(0xffffffffu, h2 ? b[i] : b[i + 4], 4));
-#pragma unroll
-  for (int i = 0; i < 2; ++i) d[i] = op(h1 ? c[i + 2] : c[i], __shfl_xor_sync(0xffffffffu, h1 ? c[i] : c[i + 2], 2));
-  return op(h0 ? d[1] : d[0], __shfl_xor_sync(0xffffffffu, h0 ? d[0] : d[1], 1));
-}
-
-template <typename TS>
-__global__ void __launch_bounds__(fq::kThreads, 1) prefix_attn_fq_kernel(const __grid_constant__ Params P) {
-  using fq::NQ;
-  using fq::D;
-  using fq::kSmWarps;
-  using fq::kProd0;
-  using fq::kProds;
-  using fq::RD;
-  using fq::PC;
-  using fq::kRec;
-  using fq::kTmemK;
-  using fq::ATOM;
-  using fq::VTILE;
-  using fq::QATOM;
-  using fq::QTILE;
-  using fq::RAWB;
-  using fq::kErrFq;
-  constexpr int MSD = fq::MS;
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + fq::OFF_BAR);
-  uint64_t* kfull = bars;                    // [2] producers (K_f in TMEM) -> MMA
-  uint64_t* kempty = kfull + 2;              // [2] MMA (S_f complete: K_f read) -> producers
-  uint64_t* vfull = kempty + 2;              // [2] producers (+ TMA bytes) -> MMA
-  uint64_t* vempty = vfull + 2;              // [2] MMA (P_f V_f complete) -> producers
-  uint64_t* mfull = vempty + 2;              // [MSD] producer warps 0-3 (mask words) -> softmax
-  uint64_t* s_full = mfull + MSD;            // [2] MMA (S_f in TMEM) -> softmax
-  uint64_t* s_free = s_full + 2;             // [2] softmax (S_f read) -> MMA
-  uint64_t* p_full = s_free + 2;             // [2] softmax (P_f in shared memory, O rescaled) -> MMA
-  uint64_t* p_empty = p_full + 2;            // [2] MMA (P_f V_f complete) -> softmax
-  uint64_t* pv_done = p_empty + 2;           // MMA (P_f V_f complete) -> softmax (rescale, epilogue)
-  uint64_t* q_full = pv_done + 1;            // [2] producers (Q of item k) -> MMA
-  uint64_t* q_empty = q_full + 2;            // [2] MMA (every S of item k complete) -> producers
-  uint64_t* rawk_full = q_empty + 2;         // [RD] TMA -> producers
-  uint64_t* rawk_empty = rawk_full + RD;     // [RD] producers -> the TMA-issuing producer
-  uint64_t* rawv_full = rawk_empty + RD;     // [RD]
-  uint64_t* rawv_empty = rawv_full + RD;     // [RD]
-  uint64_t* xsync = rawv_empty + RD;         // softmax threads: one phase per exchange
-  uint64_t* drain = xsync + 1;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
-  uint32_t* masks = reinterpret_cast<uint32_t*>(sm + fq::OFF_MASK);
-  float* xch = reinterpret_cast<float*>(sm + fq::OFF_XCH);
-  int* tab = reinterpret_cast<int*>(sm + fq::OFF_TAB);
-  static_assert(2 + 2 + 2 + 2 + MSD + 2 + 2 + 2 + 2 + 1 + 2 + 2 + 4 * RD + 1 + 1 <= fq::kBars, "barriers");
-
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int nk = P.n_items > static_cast<int>(blockIdx.x)
-                     ? (P.n_items - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
-                           static_cast<int>(gridDim.x)
-                     : 0;                    // <= kMaxItems (the grid is sized for it)
-  const int t = static_cast<int>(P.t), rep = P.rep, slots_row = t * rep;
-
-  if (tid == 0) {
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&kfull[b], kProds);
-      mbar_init(&kempty[b], 1);
-      mbar_init(&s_full[b], 1);
-      mbar_init(&s_free[b], 32 * kSmWarps);
-      mbar_init(&p_full[b], 32 * kSmWarps);
-      mbar_init(&p_empty[b], 1);
-      mbar_init(&q_full[b], kProds);
-      mbar_init(&q_empty[b], 1);
-    }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&vfull[b], kProds);
-      mbar_init(&vempty[b], 1);
-    }
-    for (int b = 0; b < MSD; ++b) mbar_init(&mfull[b], 4);
-    mbar_init(pv_done, 1);
-    for (int r = 0; r < RD; ++r) {
-      mbar_init(&rawk_full[r], 1);
-      mbar_init(&rawk_empty[r], kProds);
-      mbar_init(&rawv_full[r], 1);
-      mbar_init(&rawv_empty[r], kProds);
-    }
-    mbar_init(xsync, 32 * kSmWarps);
-    mbar_init(drain, 1);
-    *abort_flag = 0;
-    fence_mbar_init();
-  }
-  // the CTA's item schedules, one record per item
-  for (int k = tid; k < nk; k += fq::kThreads) {
-    const int it = blockIdx.x + k * gridDim.x;
-    const int grp = it / P.nsplit / P.Hkv;
-    int* rec = tab + kRec * k;
-    const int row0 = P.row_groups ? P.row_groups[2 * grp] : grp;
-    const int st = P.Kp ? P.row_state[row0] : 0;
-    const int qr = P.Kq ? P.row_q[row0] : 0;
-    rec[0] = row0;
-    rec[1] = P.row_groups ? P.row_groups[2 * grp + 1] : 1;
-    rec[2] = st;
-    rec[3] = P.Kp && P.p_lo ? P.p_lo[st] : 0;
-    rec[4] = P.Kp ? (P.p_hi ? P.p_hi[st] : static_cast<int>(P.T)) : 0;
-    rec[5] = qr;
-    rec[6] = P.Kq ? P.q_len[qr] : 0;
-    rec[7] = P.own_lo ? P.own_lo[row0] : 0;
-  }
-  if (warp == fq::kMmaWarp) {
-    tmem_alloc(tmem_holder, fq::kTmemCols);
-    tc_fence_before();
-  }
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_holder;
-
-  if (warp > fq::kMmaWarp) {
-    // ================================================================== producers
-    // Every wait here is agreed across the warp (warp_wait, or a refill outcome folded through __all_sync), so
-    // the warp is converged at its warp-wide TMEM stores and leaves the loops together on a time-out.
-    const int pt = tid - kProd0, pw = pt >> 5;
-    const int quarter = warp & 3, half = pw >> 2;   // this warp's TMEM lane quarter; the d half of its K rows
-    const int kkey = 32 * quarter + lane;           // the key (TMEM lane) whose K row half this thread converts
-    const bool i8 = P.Kp != nullptr;
-    FqCursor ld;                                    // next int8 block to load (pt == 0)
-    ld.valid = false;
-    int nk_iss = 0, nv_iss = 0;                     // raw K / V loads issued (pt == 0)
-    // a raw block and the scales of its keys, from the 8-aligned index at or below its first key (the scale TMA's
-    // start must be 16-byte aligned; indices past the tensor read as 0)
-    auto load_k = [&](int r) {
-      const int row = static_cast<int>(ld.prow + ld.lo1 + ld.j * BN);
-      mbar_arrive_expect_tx(&rawk_full[r], RAWB + fq::SCBYTES);
-      tma_load_2d(sm + fq::OFF_RAW + r * 2 * RAWB, &P.map_kp, &rawk_full[r], 0, row);
-      tma_load_1d(sm + fq::OFF_SC + r * 1024, &P.map_ks, &rawk_full[r], row & ~7);
-      ++nk_iss;
-    };
-    auto load_v = [&](int r) {
-      const int row = static_cast<int>(ld.prow + ld.lo1 + ld.j * BN);
-      mbar_arrive_expect_tx(&rawv_full[r], RAWB + fq::SCBYTES);
-      tma_load_2d(sm + fq::OFF_RAW + r * 2 * RAWB + RAWB, &P.map_vp, &rawv_full[r], 0, row);
-      tma_load_1d(sm + fq::OFF_SC + r * 1024 + 512, &P.map_vs, &rawv_full[r], row & ~7);
-      ++nv_iss;
-      fq_next(P, tab, nk, ld);
-    };
-    if (i8) {
-      if (pt == 0) {
-        fq_seek(P, tab, nk, ld, 0);
-        for (int r = 0; r < RD && ld.valid; ++r) {
-          load_k(r);
-          load_v(r);
-        }
-      }
-    }
-    // this thread's two 16-byte chunks of the next item's Q rows (row c >> 4, chunk c & 15), one item ahead
-    uint4 qreg[2];
-    auto load_q = [&](int k) {
-      FqItem I;
-      fq_item(P, tab + kRec * k, blockIdx.x + k * gridDim.x, I);
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int c = pt + e * kProds, row = c >> 4, ch = c & 15;
-        qreg[e] = make_uint4(0u, 0u, 0u, 0u);
-        if (row < I.slots) {
-          const int a = row / slots_row, i = (row - a * slots_row) / rep, hh = row % rep;
-          qreg[e] = __ldg(reinterpret_cast<const uint4*>(
-                              P.q + ((static_cast<int64_t>(I.row0 + a) * t + i) * P.Hq + I.g * rep + hh) * D) +
-                          ch);
-        }
-      }
-    };
-    if (nk > 0) load_q(0);
-    const uint32_t tk = tmem + (static_cast<uint32_t>(32 * quarter) << 16) + kTmemK + 32 * half;
-    int f = 0, u = 0;                               // flattened block; int8 blocks converted
-    bool live = true;
-    for (int k = 0; k < nk && live; ++k) {
-      FqItem I;
-      fq_item(P, tab + kRec * k, blockIdx.x + k * gridDim.x, I);
-      const int qb = k & 1;
-      if (k >= 2 && !warp_wait(&q_empty[qb], ((k >> 1) - 1) & 1, abort_flag, P.err, kErrFq | 1)) {
-        live = false;
-        break;
-      }
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int c = pt + e * kProds;
-        *reinterpret_cast<uint4*>(sm + fq::OFF_Q + qb * QTILE + swz(c >> 4, c & 15, QATOM)) = qreg[e];
-      }
-      fence_proxy_async_smem();
-      mbar_arrive(&q_full[qb]);
-      if (k + 1 < nk) load_q(k + 1);
-      for (int j = 0; j < I.nblk; ++j, ++f) {
-        const bool pre = j < I.nb1;
-        const bool qseg = !pre && j < I.nb1 + I.nb2;
-        const int k0 = pre ? I.lo1 + j * BN : qseg ? (j - I.nb1) * BN : I.own_begin + (j - I.nb1 - I.nb2) * BN;
-        // ---- K_f: half a key row into this thread's TMEM lane (bf16 pairs, lower d in the low half)
-        if (f >= 2 && !warp_wait(&kempty[f & 1], ((f >> 1) - 1) & 1, abort_flag, P.err, kErrFq | 2)) {
-          live = false;
-          break;
-        }
-        uint32_t kw[32];
-        const int r = u % RD;
-        if (pre) {
-          if (!warp_wait(&rawk_full[r], (u / RD) & 1, abort_flag, P.err, kErrFq | 3)) {
-            live = false;
-            break;
-          }
-          const uint8_t* row = sm + fq::OFF_RAW + r * 2 * RAWB + kkey * D;
-          const int sofs = static_cast<int>((I.prow + k0) & 7);   // first key's index in the staged scales
-          const uint32_t skc =
-              k0 + kkey < I.hi1
-                  ? static_cast<uint32_t>(reinterpret_cast<const unsigned short*>(sm + fq::OFF_SC + r * 1024)[sofs + kkey])
-                  : 0u;
-#pragma unroll
-          for (int c4 = 0; c4 < 4; ++c4) {
-            const int ch = 4 * half + c4;
-            const uint4 q = *reinterpret_cast<const uint4*>(row + ((ch ^ (kkey & 7)) << 4));
-            uint32_t w8[8];
-            dequant16<TS>(q, skc, w8);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) kw[8 * c4 + e] = w8[e];
-          }
-          mbar_arrive(&rawk_empty[r]);
-          bool ok_ = true;
-          if (pt == 0 && ld.valid) {                // refill the slot with the K block RD ahead
-            ok_ = mbar_wait(&rawk_empty[r], (u / RD) & 1, abort_flag, P.err, kErrFq | 4);
-            if (ok_) load_k(r);
-          }
-          if (!__all_sync(0xffffffffu, ok_)) {      // the warp reconverges before its warp-wide TMEM store
-            live = false;
-            break;
-          }
-        } else {
-          // bf16 question-prefix / own keys straight from global memory (zeros past the segment)
-          const int idx = k0 + kkey;
-          const __nv_bfloat16* src = nullptr;
-          if (qseg) {
-            if (idx < I.n2) src = P.Kq + ((static_cast<int64_t>(I.qr) * P.Lq + idx) * P.Hkv + I.g) * D;
-          } else {
-            const int64_t orow = static_cast<int64_t>(I.row0) * t + idx;
-            if (idx < I.own_end && orow < P.R * P.t) src = P.k_own + (orow * P.Hkv + I.g) * D;
-          }
-#pragma unroll
-          for (int c4 = 0; c4 < 8; ++c4) {
-            const uint4 v = src ? __ldg(reinterpret_cast<const uint4*>(src + 64 * half) + c4) : make_uint4(0, 0, 0, 0);
-            kw[4 * c4] = v.x;
-            kw[4 * c4 + 1] = v.y;
-            kw[4 * c4 + 2] = v.z;
-            kw[4 * c4 + 3] = v.w;
-          }
-        }
-        __syncwarp();
-        tmem_st_32x32b_x32(tk + (f & 1) * (D / 2), kw);
-        tmem_st_wait();
-        tc_fence_before();
-        mbar_arrive(&kfull[f & 1]);
-        // ---- the block's visibility bits (keys k0 + pt, pt < 128: producer warps 0-3)
-        if (pt < BN) {
-          const int idx = k0 + pt;
-          bool vis;
-          if (pre) {
-            vis = idx < I.hi1 && (!P.pmask || P.pmask[static_cast<int64_t>(I.st) * P.T + idx] != 0);
-          } else if (qseg) {
-            vis = idx < I.n2;
-          } else {
-            const int a = idx / t, jj = idx - a * t;
-            const int rr = I.row0 + a;
-            vis = idx < I.own_end && a < I.nr && jj >= (P.own_lo ? P.own_lo[rr] : 0) &&
-                  jj < (P.own_hi ? P.own_hi[rr] : t);
-          }
-          const uint32_t word = __ballot_sync(0xffffffffu, vis);
-          if (lane == 0) {
-            masks[4 * (f % MSD) + pw] = word;
-            mbar_arrive(&mfull[f % MSD]);
-          }
-        }
-        // ---- V_f into the shared-memory A operand
-        if (f >= 2 && !warp_wait(&vempty[f & 1], ((f >> 1) - 1) & 1, abort_flag, P.err, kErrFq | 5)) {
-          live = false;
-          break;
-        }
-        if (pre) {
-          if (!warp_wait(&rawv_full[r], (u / RD) & 1, abort_flag, P.err, kErrFq | 6)) {
-            live = false;
-            break;
-          }
-          const uint8_t* raw = sm + fq::OFF_RAW + r * 2 * RAWB + RAWB;
-          const unsigned short* vsc_s = reinterpret_cast<const unsigned short*>(sm + fq::OFF_SC + r * 1024 + 512) +
-                                        ((I.prow + k0) & 7);
-          uint8_t* vt = sm + fq::OFF_V + (f & 1) * VTILE;
-#pragma unroll
-          for (int it = 0; it < PC; ++it) {
-            const int c = pt + it * kProds, key = c >> 3, ch = c & 7;
-            const uint4 q = *reinterpret_cast<const uint4*>(raw + key * D + ch * 16);
-            const uint32_t svk = k0 + key < I.hi1 ? static_cast<uint32_t>(vsc_s[key]) : 0u;
-            uint32_t w8[8];
-            dequant16<TS>(q, svk, w8);
-            // chunks 2ch and 2ch+1 of the row; threads with ch >= 4 store their odd chunk first, so the 8 threads
-            // of a row hit 8 distinct bank groups in each store
-            const uint4 lo = make_uint4(w8[0], w8[1], w8[2], w8[3]), hi = make_uint4(w8[4], w8[5], w8[6], w8[7]);
-            const bool sw = ch >= 4;
-            *reinterpret_cast<uint4*>(vt + swz(key, 2 * ch + (sw ? 1 : 0), ATOM)) = sw ? hi : lo;
-            *reinterpret_cast<uint4*>(vt + swz(key, 2 * ch + (sw ? 0 : 1), ATOM)) = sw ? lo : hi;
-          }
-          mbar_arrive(&rawv_empty[r]);
-          bool ok_ = true;
-          if (pt == 0 && ld.valid) {
-            ok_ = mbar_wait(&rawv_empty[r], (u / RD) & 1, abort_flag, P.err, kErrFq | 7);
-            if (ok_) load_v(r);
-          }
-          if (!__all_sync(0xffffffffu, ok_)) {
-            live = false;
-            break;
-          }
-          ++u;
-          fence_proxy_async_smem();
-          mbar_arrive(&vfull[f & 1]);
-        } else if (pt == 0) {
-          const CUtensorMap* mv = qseg ? &P.map_vq : &P.map_vo;
-          const int y = (qseg ? I.qr * static_cast<int>(P.Lq) : I.row0 * t) + k0;
-          mbar_arrive_expect_tx(&vfull[f & 1], VTILE);
-#pragma unroll
-          for (int h = 0; h < 2; ++h)
-            tma_load_2d(sm + fq::OFF_V + (f & 1) * VTILE + h * ATOM, mv, &vfull[f & 1], I.g * D + h * 64, y);
-        } else {
-          mbar_arrive(&vfull[f & 1]);
-        }
-      }
-    }
-    if (pt == 0 && (nk_iss > u || nv_iss > u)) {
-      // aborted: let the raw loads still in flight land before the CTA's shared memory is released
-      for (int v = u; v < nk_iss; ++v) {
-        const long long c0 = clock64();
-        while (!mbar_try_wait(&rawk_full[v % RD], (v / RD) & 1) && clock64() - c0 < 2000000) {
-        }
-      }
-      for (int v = u; v < nv_iss; ++v) {
-        const long long c0 = clock64();
-        while (!mbar_try_wait(&rawv_full[v % RD], (v / RD) & 1) && clock64() - c0 < 2000000) {
-        }
-      }
-    }
-  } else if (warp == fq::kMmaWarp) {
-    // ================================================================== MMA issue (one thread)
-    if (lane == 0) {
-      constexpr uint32_t idesc_s = idesc_bf16(128, NQ, false);
-      constexpr uint32_t idesc_o = idesc_bf16_amn(128, NQ);
-      int f = 0, pf = 0, pob = 0;
-      bool live = true, pend = false, pfirst = false;
-      auto issue_pv = [&]() -> bool {
-        if (!mbar_wait(&vfull[pf & 1], (pf >> 1) & 1, abort_flag, P.err, kErrFq | 8) ||
-            !mbar_wait(&p_full[pf & 1], (pf >> 1) & 1, abort_flag, P.err, kErrFq | 9))
-          return false;
-        tc_fence_after();
-        const uint32_t sV = smem_u32(sm + fq::OFF_V + (pf & 1) * VTILE);
-        const uint32_t sP = smem_u32(sm + fq::OFF_P + (pf & 1) * QTILE);
-#pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk)
-          mma_f16(tmem + fq::kTmemO + pob * NQ, desc_sw128(sV + kk * 16 * 128, ATOM, 1024),
-                  desc_sw128(sP + (kk >> 2) * QATOM + (kk & 3) * 32, 16, 1024), idesc_o,
-                  (pfirst && kk == 0) ? 0u : 1u);
-        mma_commit(&vempty[pf & 1]);
-        mma_commit(&p_empty[pf & 1]);
-        mma_commit(pv_done);
-        return true;
-      };
-      for (int k = 0; k < nk && live; ++k) {
-        FqItem I;
-        fq_item(P, tab + kRec * k, blockIdx.x + k * gridDim.x, I);
-        const int qb = k & 1;
-        if (!mbar_wait(&q_full[qb], (k >> 1) & 1, abort_flag, P.err, kErrFq | 10)) {
-          live = false;
-          break;
-        }
-        for (int j = 0; j < I.nblk; ++j, ++f) {
-          if (!mbar_wait(&kfull[f & 1], (f >> 1) & 1, abort_flag, P.err, kErrFq | 11) ||
-              (f >= 2 && !mbar_wait(&s_free[f & 1], ((f >> 1) - 1) & 1, abort_flag, P.err, kErrFq | 12))) {
-            live = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t sQ = smem_u32(sm + fq::OFF_Q + qb * QTILE);
-#pragma unroll
-          for (int kd = 0; kd < D / 16; ++kd)
-            mma_f16_ts(tmem + fq::kTmemS + (f & 1) * NQ, tmem + kTmemK + (f & 1) * (D / 2) + kd * 8,
-                       desc_sw128(sQ + (kd >> 2) * QATOM + (kd & 3) * 32, 16, 1024), idesc_s, kd > 0 ? 1u : 0u);
-          mma_commit(&s_full[f & 1]);
-          mma_commit(&kempty[f & 1]);
-          // the previous block's P.V behind this block's S (the softmax of this block overlaps it)
-          if (pend && !issue_pv()) {
-            live = false;
-            break;
-          }
-          pend = true;
-          pf = f;
-          pob = qb;
-          pfirst = j == 0;
-        }
-        if (live) mma_commit(&q_empty[qb]);
-      }
-      if (live && pend) issue_pv();
-      mma_commit(drain);
-      const long long c0 = clock64();
-      while (!mbar_try_wait(drain, 0) && clock64() - c0 < kWaitLimitCycles) {
-      }
-    }
-  } else {
-    // ================================================================== softmax and epilogue
-    // Control flow is identical across the 32 lanes (every condition below is warp-uniform, and every lane takes
-    // part in every shuffle).
-    const int w = warp, kl = 32 * w + lane;        // key of a block (TMEM lane of S^T); d row of O^T
-    const uint32_t lane_off = static_cast<uint32_t>(32 * w) << 16;
-    const float scale = P.scale_log2;
-    int f = 0, xs = 0;
-    bool live = true;
-    // all 128 softmax threads have written their value of exchange xs; its buffer is readable after this
-    auto exchange = [&]() -> bool {
-      mbar_arrive(xsync);
-      const bool ok_ = warp_wait(xsync, xs & 1, abort_flag, P.err, kErrFq | 13);
-      ++xs;
-      return ok_;
-    };
-    const int cc = (kl & 63) >> 3;                  // this key's 16-byte chunk in a P^T row (before the swizzle)
-    for (int k = 0; k < nk && live; ++k) {
-      FqItem I;
-      fq_item(P, tab + kRec * k, blockIdx.x + k * gridDim.x, I);
-      const int ob = k & 1;
-      // slot `lane` of the item: row a, token i, head hh of the GQA group
-      const bool qv = lane < I.slots;
-      const int a_l = qv ? lane / slots_row : 0;
-      const int i_l = qv ? (lane - a_l * slots_row) / rep : 0;
-      const int hh_l = lane % rep;
-      float m_l = -INFINITY;                        // running max of slot `lane` (log2 units)
-      float lp[NQ];                                 // this key lane's share of every slot's sum
-#pragma unroll
-      for (int q = 0; q < NQ; ++q) lp[q] = 0.f;
-      for (int j = 0; j < I.nblk; ++j, ++f) {
-        if (!warp_wait(&s_full[f & 1], (f >> 1) & 1, abort_flag, P.err, kErrFq | 14) ||
-            !warp_wait(&mfull[f % MSD], (f / MSD) & 1, abort_flag, P.err, kErrFq | 15)) {
-          live = false;
-          break;
-        }
-        const bool vis = (masks[4 * (f % MSD) + w] >> lane) & 1u;
-        tc_fence_after();
-        float x[NQ];
-        {
-          uint32_t s[NQ];
-          tmem_ld_32x32b_x32(tmem + lane_off + fq::kTmemS + (f & 1) * NQ, s);
-          tmem_ld_wait();
-#pragma unroll
-          for (int q = 0; q < NQ; ++q) x[q] = __uint_as_float(s[q]);
-        }
-        tc_fence_before();
-        mbar_arrive(&s_free[f & 1]);
-        const bool own = j >= I.nb1 + I.nb2;        // warp-uniform
-        int ak = -1, jk = 0;
-        if (own) {
-          const int idx = I.own_begin + (j - I.nb1 - I.nb2) * BN + kl;
-          ak = idx / t;
-          jk = idx - ak * t;
-        }
-        const float thr_l = m_l + 8.f;
-        bool over = false;
-#pragma unroll
-        for (int q = 0; q < NQ; ++q) {
-          bool v = vis && q < I.slots;
-          if (own) {                                // every lane shuffles (no short-circuit around a shuffle)
-            const int aq = __shfl_sync(0xffffffffu, a_l, q), iq = __shfl_sync(0xffffffffu, i_l, q);
-            v = v && aq == ak && jk <= iq;
-          }
-          x[q] = v ? x[q] * scale : -INFINITY;
-          const float th = __shfl_sync(0xffffffffu, thr_l, q);
-          over = over || x[q] > th;
-        }
-        // does any slot's block max exceed its running max by more than 2^8 (all four warps decide alike)?
-        {
-          const bool wover = __any_sync(0xffffffffu, over);
-          float* xb = xch + (xs & 1) * 128;
-          if (lane == 0) xb[32 * w] = wover ? 1.f : 0.f;
-          if (!exchange()) {
-            live = false;
-            break;
-          }
-          if (xb[0] + xb[32] + xb[64] + xb[96] > 0.f) {
-            const float bmw = transpose_reduce<true>(x, lane);
-            float* xb2 = xch + (xs & 1) * 128;
-            xb2[32 * w + lane] = bmw;
-            if (!exchange()) {
-              live = false;
-              break;
-            }
-            const float bm = fmaxf(fmaxf(xb2[lane], xb2[32 + lane]), fmaxf(xb2[64 + lane], xb2[96 + lane]));
-            const float m_new = bm > m_l + 8.f ? bm : m_l;
-            const float alpha = (m_l == -INFINITY || m_new == m_l) ? 1.f : ex2_approx(m_l - m_new);
-            m_l = m_new;
-            if (__any_sync(0xffffffffu, alpha != 1.f)) {
-#pragma unroll
-              for (int q = 0; q < NQ; ++q) lp[q] *= __shfl_sync(0xffffffffu, alpha, q);
-              if (j > 0) {                          // O^T holds this item's earlier blocks: rescale its columns
-                if (!warp_wait(pv_done, (f - 1) & 1, abort_flag, P.err, kErrFq | 16)) {
-                  live = false;
-                  break;
-                }
-                tc_fence_after();
-                uint32_t o[NQ];
-                tmem_ld_32x32b_x32(tmem + lane_off + fq::kTmemO + ob * NQ, o);
-                tmem_ld_wait();
-#pragma unroll
-                for (int q = 0; q < NQ; ++q)
-                  o[q] = __float_as_uint(__uint_as_float(o[q]) * __shfl_sync(0xffffffffu, alpha, q));
-                tmem_st_32x32b_x32(tmem + lane_off + fq::kTmemO + ob * NQ, o);
-                tmem_st_wait();
-              }
-            }
-          }
-        }
-        // ---- P^T (bf16): row q (slot), column kl (key) of the K-major B operand
-        if (f >= 2 && !warp_wait(&p_empty[f & 1], ((f >> 1) - 1) & 1, abort_flag, P.err, kErrFq | 17)) {
-          live = false;
-          break;
-        }
-        uint8_t* sp = sm + fq::OFF_P + (f & 1) * QTILE + (kl >> 6) * QATOM + (kl & 7) * 2;
-#pragma unroll
-        for (int q = 0; q < NQ; ++q) {
-          const float mq = __shfl_sync(0xffffffffu, m_l, q);
-          const float p = x[q] == -INFINITY ? 0.f : ex2_approx(x[q] - mq);
-          lp[q] += p;
-          *reinterpret_cast<__nv_bfloat16*>(sp + q * 128 + ((cc ^ (q & 7)) << 4)) = __float2bfloat16_rn(p);
-        }
-        tc_fence_before();
-        fence_proxy_async_smem();
-        mbar_arrive(&p_full[f & 1]);
-      }
-      if (!live) break;
-      // ---- item epilogue: slot sums over the 128 key lanes, O^T / l (thread = output dimension kl), LSE
-      const float lw = transpose_reduce<false>(lp, lane);
-      float* xb = xch + (xs & 1) * 128;
-      xb[32 * w + lane] = lw;
-      if (!exchange()) {
-        live = false;
-        break;
-      }
-      const float L = (xb[lane] + xb[32 + lane]) + (xb[64 + lane] + xb[96 + lane]);
-      const float inv_l = L > 0.f ? 1.0f / L : 0.f;
-      uint32_t o[NQ];
-      if (I.nblk > 0) {
-        if (!warp_wait(pv_done, (f - 1) & 1, abort_flag, P.err, kErrFq | 18)) {
-          live = false;
-          break;
-        }
-        tc_fence_after();
-        tmem_ld_32x32b_x32(tmem + lane_off + fq::kTmemO + ob * NQ, o);
-        tmem_ld_wait();
-      } else {
-#pragma unroll
-        for (int q = 0; q < NQ; ++q) o[q] = 0u;
-      }
-      // output row (row, token, head) of slot `lane`, in units of D
-      const int64_t orow_l = (static_cast<int64_t>(I.row0 + a_l) * t + i_l) * P.Hq + I.g * rep + hh_l;
-      const int orow_hi = static_cast<int>(orow_l >> 32), orow_lo = static_cast<int>(orow_l & 0xFFFFFFFF);
-      const int64_t n_l = P.R * P.t * P.Hq;
-#pragma unroll
-      for (int q = 0; q < NQ; ++q) {
-        // all lanes shuffle; only the item's slots store
-        const uint32_t hi_q = static_cast<uint32_t>(__shfl_sync(0xffffffffu, orow_hi, q));
-        const uint32_t lo_q = static_cast<uint32_t>(__shfl_sync(0xffffffffu, orow_lo, q));
-        const float val = __uint_as_float(o[q]) * __shfl_sync(0xffffffffu, inv_l, q);
-        if (q < I.slots) {
-          const int64_t orow = static_cast<int64_t>((static_cast<uint64_t>(hi_q) << 32) | lo_q);
-          if (P.nsplit > 1)
-            P.part_o[(I.split * n_l + orow) * D + kl] = val;
-          else
-            P.o[orow * D + kl] = __float2bfloat16_rn(val);
-        }
-      }
-      if (w == 0 && qv) {
-        const int64_t lrow = (static_cast<int64_t>(I.row0 + a_l) * P.Hq + I.g * rep + hh_l) * t + i_l;
-        const float lse_v = L > 0.f ? (m_l + log2f(L)) * 0.6931471805599453f : -INFINITY;
-        if (P.nsplit > 1)
-          P.part_lse[I.split * n_l + lrow] = lse_v;
-        else if (P.lse)
-          P.lse[lrow] = lse_v;
-      }
-      tc_fence_before();
-    }
-  }
-  __syncthreads();
-  if (warp == fq::kMmaWarp) {
-    tc_fence_after();
-    tmem_dealloc(tmem, fq::kTmemCols);
-  }
-}
-
-// Splits of the state prefix for the few-slot form: the count minimising (items per CTA) x (blocks per item + half a
-// block of per-item cost) over a persistent grid of num_sms CTAs, plus one block for the merge when split.
-int plan_splits_fq(int64_t units, int64_t prefix_blocks, int num_sms) {
-  if (units <= 0 || prefix_blocks < 2 || num_sms <= 0) return 1;
-  int best = 1;
-  double best_t = 1e300;
-  for (int n = 1; n <= 64 && n <= prefix_blocks; ++n) {
-    const double per_cta = static_cast<double>((units * n + num_sms - 1) / num_sms);
-    const double tm = per_cta * (static_cast<double>((prefix_blocks + n - 1) / n) + 0.5) + (n > 1 ? 1.0 : 0.0);
-    if (tm < best_t * 0.97) {
-      best_t = tm;
-      best = n;
-    }
-  }
-  return best;
-}
-
-bool use_fq(const od_attn_dims& d, bool has_prefix) {
-  return d.D == fq::D && group_slots(d) <= fq::NQ && !(has_prefix && d.prefix_bf16);
-}
-
-// (rows, 128) int8 row-major view tiled into 128 x BN boxes with the 128-byte swizzle (16-byte chunk c of row r at
-// chunk position c ^ (r & 7)), for the few-slot form's K blocks
-int make_map_i8_sw128(CUtensorMap* map, const void* base, uint64_t rows) {
-  auto fn = encode_fn();
-  if (!fn) return fail(OD_ECUDA, "cuTensorMapEncodeTiled is unavailable");
-  cuuint64_t dims[2] = {128, rows};
-  cuuint64_t strides[1] = {128};
-  cuuint32_t box[2] = {128, static_cast<cuuint32_t>(BN)};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(OD_ECUDA, "cuTensorMapEncodeTiled (int8, swizzled) failed (%d)", static_cast<int>(r));
-  return OD_OK;
-}
-
-// 1-D view of n 16-bit scales (fp16 or bf16 bit patterns) tiled into 136-element boxes (zero past the end)
-int make_map_scales(CUtensorMap* map, const void* base, uint64_t n) {
-  auto fn = encode_fn();
-  if (!fn) return fail(OD_ECUDA, "cuTensorMapEncodeTiled is unavailable");
-  cuuint64_t dims[1] = {n};
-  cuuint64_t strides[1] = {0};
-  cuuint32_t box[1] = {static_cast<cuuint32_t>(fq::SCB)};
-  cuuint32_t estr[1] = {1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 1, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(OD_ECUDA, "cuTensorMapEncodeTiled (scales) failed (%d)", static_cast<int>(r));
-  return OD_OK;
-}
-
-int num_sms_current() {
-  static int sms[64] = {0};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-  if (!sms[dev]) {
-    int n = 0;
-    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-    sms[dev] = n;
-  }
-  return sms[dev];
-}
-
-template <typename TS>
-int launch_fq(const Params& P, cudaStream_t st) {
-  static bool attr[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr[dev]) {
-    OD_CUDA_TRY(cudaFuncSetAttribute(prefix_attn_fq_kernel<TS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     fq::BYTES));
-    cudaFuncAttributes fa;
-    OD_CUDA_TRY(cudaFuncGetAttributes(&fa, prefix_attn_fq_kernel<TS>));
-    OD_REQUIRE(fa.maxThreadsPerBlock >= fq::kThreads,
-               "od_prefix_attn: the few-slot kernel fits %d threads per block (%d registers each), needs %d",
-               fa.maxThreadsPerBlock, fa.numRegs, fq::kThreads);
-    attr[dev] = true;
-  }
-  int grid = std::min(P.n_items, num_sms_current());
-  grid = std::max(grid, (P.n_items + fq::kMaxItems - 1) / fq::kMaxItems);
-  prefix_attn_fq_kernel<TS><<<grid, fq::kThreads, fq::BYTES, st>>>(P);
-  OD_LAUNCH_CHECK();
-  return ok();
-}
-
-
 }  // namespace
 }  // namespace od
 
@@ -1687,9 +852,6 @@ extern "C" int od_prefix_attn(const void* q, const void* Kp, const void* Vp, con
                "od_prefix_attn: %d splits need a 16-byte aligned workspace of %lld bytes (od_prefix_attn_plan)", nsplit,
                (long long)(static_cast<int64_t>(sizeof(float)) * nsplit * n_part * (dims.D + 1)));
   if (G == 0 || dims.t == 0) return ok();
-  // at most 32 query slots per group and KV head: the few-slot form
-  // (its scale tensor maps need 16-byte aligned scale arrays)
-  const bool fewq = dims.D == fq::D && gslots <= fq::NQ && !(Kp && pbf16) && (!Kp || (aligned16(ksc) && aligned16(vsc)));
   int32_t* err = device_error_word();
   if (!err) return fail(OD_ECUDA, "od_prefix_attn: no device error word");
   Params P;
@@ -1748,33 +910,24 @@ extern "C" int od_prefix_attn(const void* q, const void* Kp, const void* Vp, con
         rc = make_map_bf16(&P.map_kp, Kp, static_cast<uint64_t>(dims.D), prows);
         if (!rc) rc = make_map_bf16(&P.map_vp, Vp, static_cast<uint64_t>(dims.D), prows);
       } else {
-        rc = fewq ? make_map_i8_sw128(&P.map_kp, Kp, prows)
-                  : make_map_i8(&P.map_kp, Kp, static_cast<uint64_t>(dims.D), prows);
-        if (!rc && fewq) rc = make_map_scales(&P.map_ks, ksc, prows);
-        if (!rc && fewq) rc = make_map_scales(&P.map_vs, vsc, prows);
+        rc = make_map_i8(&P.map_kp, Kp, static_cast<uint64_t>(dims.D), prows);
         if (!rc) rc = make_map_i8(&P.map_vp, Vp, static_cast<uint64_t>(dims.D), prows);
       }
     }
     if (rc) return rc;
   }
-  cudaStream_t st = as_stream(stream);
-  const bool half_scale = Kp && !pbf16 && dims.scale_dtype == OD_F16;
-  int rc = OD_OK;
-  if (fewq) {
-    const int64_t items = G * dims.Hkv * nsplit;
-    OD_REQUIRE(items < (1LL << 30), "od_prefix_attn: too many work items");
-    P.n_items = static_cast<int>(items);
-    rc = half_scale ? launch_fq<__half>(P, st) : launch_fq<__nv_bfloat16>(P, st);
-  }
   const int64_t gx = G * P.tiles_per_group;
   OD_REQUIRE(gx < (1LL << 31) && dims.Hkv < 65536, "od_prefix_attn: grid too large");
   dim3 grid(static_cast<unsigned>(gx), dims.Hkv, nsplit);
+  cudaStream_t st = as_stream(stream);
+  const bool half_scale = Kp && !pbf16 && dims.scale_dtype == OD_F16;
+  int rc = OD_OK;
 #define OD_ATTN(NT_)                                                                                          \
   (dims.D == 128 ? (half_scale ? launch_attn<__half, 128, NT_>(P, grid, st)                                \
                                : launch_attn<__nv_bfloat16, 128, NT_>(P, grid, st))                        \
                  : (half_scale ? launch_attn<__half, 64, NT_>(P, grid, st)                                 \
                                : launch_attn<__nv_bfloat16, 64, NT_>(P, grid, st)))
-  if (!fewq) rc = NT == 1 ? OD_ATTN(1) : OD_ATTN(2);
+  rc = NT == 1 ? OD_ATTN(1) : OD_ATTN(2);
 #undef OD_ATTN
   if (rc != OD_OK || nsplit == 1) return rc;
   const unsigned mb = static_cast<unsigned>((n_part * 32 + 255) / 256);
@@ -1797,8 +950,7 @@ extern "C" int od_prefix_attn_plan(const od_attn_dims* dims, int num_sms, int* n
   const int64_t cta_slots = gslots <= BM ? BM : kMaxTiles * BM;
   const int64_t G = dims->max_group_rows > 1 ? dims->G : dims->R;
   const int64_t ctas = G * ((gslots + cta_slots - 1) / cta_slots) * dims->Hkv;
-  const int n = use_fq(*dims, true) ? plan_splits_fq(G * dims->Hkv, (dims->T + BN - 1) / BN, num_sms)
-                                    : plan_splits(ctas, (dims->T + BN - 1) / BN, num_sms);
+  const int n = plan_splits(ctas, (dims->T + BN - 1) / BN, num_sms);
   *nsplit = n;
   if (n > 1)
     *workspace_bytes = static_cast<int64_t>(sizeof(float)) * n * static_cast<int64_t>(dims->R) * dims->t * dims->Hq *

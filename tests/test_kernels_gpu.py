@@ -554,9 +554,9 @@ def test_prefix_attn_plan_splits_small_launches(cuda):
 
 
 def _few_slot_case(scale_dtype, seed):
-    """24 states x 2 groups (2 and 1 rows of 3 tokens, 32 / 8 heads: 24 and 12 query slots per group and KV head,
-    the few-slot form), 300-token int8 states with left pads, an end (p_hi) and a hole, a right-padded question
-    prefix and ragged own keys: 384 work items, several per CTA."""
+    """24 states x 2 groups (2 and 1 rows of 3 tokens, 32 / 8 heads: 24 and 12 query slots per group and KV head, the
+    bandwidth-bound shape of a yes/no question), 300-token int8 states with left pads, an end (p_hi) and a hole, a
+    right-padded question prefix and ragged own keys: 384 (group, KV head) tiles."""
     g = syn.gen(seed)
     S, T, Hq, Hkv, D, t = 24, 300, 32, 8, 128, 3
     ac = syn.attn_case(S=S, T=T, rows=3, t=t, Hq=Hq, Hkv=Hkv, D=D, seed=seed)
@@ -600,10 +600,10 @@ def _few_slot_ref(ac, args, r):
 
 
 @pytest.mark.parametrize("scale_dtype", [torch.float16, torch.bfloat16])
-def test_prefix_attn_few_slots_vs_oracle(cuda, scale_dtype):
-    """The few-slot form (keys on the tensor core's M side, persistent CTAs over (group, head, split) items) against
-    the oracle's split attention, with one CTA per state prefix and with the planned and an explicit split; the
-    split results merge to the unsplit ones."""
+def test_prefix_attn_few_slot_groups_vs_oracle(cuda, scale_dtype):
+    """Groups of a few short rows (at most 24 query slots per KV head, one mostly empty query tile) against the
+    oracle's split attention, with one CTA per state prefix and with the planned and an explicit split; the split
+    results merge to the unsplit ones."""
     ac, args, groups, own_hi = _few_slot_case(scale_dtype, seed=61)
     dargs = {k: v.to(cuda) for k, v in args.items()}
     q, k, v = ac.q.to(cuda), ac.k.to(cuda), ac.v.to(cuda)
@@ -626,8 +626,9 @@ def test_prefix_attn_few_slots_vs_oracle(cuda, scale_dtype):
             assert (ln[r, :, :n] - l1[r, :, :n]).abs().max() < 1e-4, (ns, r)
 
 
-def test_prefix_attn_few_slots_row_order_invariant(cuda):
-    """Few-slot form, rows alone (12 slots each): permuting the rows permutes the outputs and LSE bit for bit."""
+def test_prefix_attn_short_rows_row_order_invariant(cuda):
+    """Rows of 3 tokens alone (12 query slots per KV head): permuting the rows permutes the outputs and LSE bit for
+    bit."""
     ac = syn.attn_case(S=5, T=700, rows=7, t=3, Hq=32, Hkv=8, D=128, seed=67)
     Kq, Vq, ks, vs = _attn_inputs(cuda, ac)
     perm = torch.randperm(ac.q.shape[0], generator=syn.gen(2))
@@ -640,7 +641,7 @@ def test_prefix_attn_few_slots_row_order_invariant(cuda):
     assert torch.equal(l[perm.to(cuda)], lp)
 
 
-def test_prefix_attn_few_slots_fp16_dequant_exact(cuda):
+def test_prefix_attn_fp16_dequant_exact(cuda):
     """As test_prefix_attn_int8_dequant_exact with fp16 scales (BASELINE config 3's cache): one visible prefix key
     per state, so each output is bf16(fp16(vq * vs)) bit for bit - over every int8 value and scales across the fp16
     range, subnormals included."""
