@@ -216,9 +216,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
   uint64_t* vfull = kempty + KS;           // [VS] producers (+ TMA bytes) -> MMA
   uint64_t* vempty = vfull + VS;           // [VS] MMA (P_j V_j of both tiles complete) -> producers
   uint64_t* mfull = vempty + VS;           // [MS] producer warps (mask words written) -> softmax
-  uint64_t* s_full = mfull + MS;           // [NT] MMA (S_j of the tile complete) -> the tile's softmax
-  uint64_t* p_full = s_full + NT;          // [NT] the tile's softmax (P_j in TMEM, O rescaled) -> MMA
-  uint64_t* pv_done = p_full + NT;         // [NT] MMA (P_j V_j of the tile complete) -> MMA, softmax epilogue
+  // s_full / p_full: per query tile (NT = 2), or per S buffer (NT = 1: S double-buffered in TMEM, buffer j & 1)
+  uint64_t* s_full = mfull + MS;           // [2] MMA (S_j complete) -> softmax
+  uint64_t* p_full = s_full + 2;           // [2] softmax (P_j in TMEM, O rescaled) -> MMA
+  uint64_t* pv_done = p_full + 2;          // [NT] MMA (P_j V_j of the tile complete) -> softmax rescale, epilogue
   uint64_t* rawk_full = pv_done + NT;      // [RD] TMA (raw int8 K block) -> producers
   uint64_t* rawk_empty = rawk_full + RD;   // [RD] producers (raw K converted) -> the TMA-issuing producer
   uint64_t* rawv_full = rawk_empty + RD;   // [RD]
@@ -253,9 +254,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
       mbar_init(&vempty[b], 1);
     }
     for (int b = 0; b < MS; ++b) mbar_init(&mfull[b], kProducerWarps);
-    for (int x = 0; x < NT; ++x) {
+    for (int x = 0; x < 2; ++x) {
       mbar_init(&s_full[x], 1);
       mbar_init(&p_full[x], BM);
+    }
+    for (int x = 0; x < NT; ++x) {
       mbar_init(&pv_done[x], 1);
     }
     for (int r = 0; r < RD; ++r) {
@@ -424,7 +427,56 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
     // Per block j and tile x: S_x(j) = Q_x K_j^T into the tile's S columns, then (once the tile's softmax has
     // written P_x(j) over them) O_x += P_x(j) V_j. P aliases S, so S_x(j+1) is issued only after P_x(j) V_j has
     // completed; the other tile's MMAs fill the tensor core meanwhile (A: P V, S; then B: P V, S).
-    if (lane == 0 && nblk > 0) {
+    // One query tile (NT = 1): the second tile's S columns hold a second S buffer, so S(j+1) is computed while the
+    // softmax works on block j and the softmax runs block after block; S(j+2) follows P(j) V(j) into buffer j & 1.
+    if constexpr (NT == 1) {
+      if (lane == 0 && nblk > 0) {
+        constexpr uint32_t idesc_s = idesc_bf16(BM, BN, false);
+        constexpr uint32_t idesc_o = idesc_bf16(BM, D, true);
+        const uint32_t sQ = smem_u32(sm + L::Q(0));
+        auto issue_s = [&](int j) {
+          const uint32_t sK = smem_u32(sm + L::K(j % KS));
+#pragma unroll
+          for (int kd = 0; kd < D / 16; ++kd) {
+            const uint32_t off = (kd >> 2) * L::ATOM + (kd & 3) * 32;
+            mma_f16(tmem + kTmemS + (j & 1) * BN, desc_sw128(sQ + off, 16, 1024), desc_sw128(sK + off, 16, 1024),
+                    idesc_s, kd > 0 ? 1u : 0u);
+          }
+          mma_commit(&s_full[j & 1]);
+          mma_commit(&kempty[j % KS]);
+        };
+        bool live = mbar_wait(q_full, 0, abort_flag, P.err, kErrAttn | 17);
+        for (int j = 0; j < 2 && j < nblk && live; ++j) {
+          live = mbar_wait(&kfull[j % KS], (j / KS) & 1, abort_flag, P.err, kErrAttn | 3);
+          if (live) {
+            tc_fence_after();
+            issue_s(j);
+          }
+        }
+        for (int j = 0; j < nblk && live; ++j) {
+          if (!mbar_wait(&vfull[j % VS], (j / VS) & 1, abort_flag, P.err, kErrAttn | 5) ||
+              !mbar_wait(&p_full[j & 1], (j >> 1) & 1, abort_flag, P.err, kErrAttn | 6))
+            break;
+          tc_fence_after();
+          const uint32_t sV = smem_u32(sm + L::V(j % VS));
+#pragma unroll
+          for (int kk = 0; kk < BN / 16; ++kk)
+            mma_f16_ts(tmem + kTmemO, tmem + kTmemS + (j & 1) * BN + kk * 8,
+                       desc_sw128(sV + kk * 16 * 128, L::ATOM, 1024), idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+          mma_commit(&pv_done[0]);
+          mma_commit(&vempty[j % VS]);
+          if (j + 2 < nblk) {
+            if (!mbar_wait(&kfull[(j + 2) % KS], ((j + 2) / KS) & 1, abort_flag, P.err, kErrAttn | 4)) break;
+            tc_fence_after();
+            issue_s(j + 2);                         // in issue order behind the P.V that reads buffer j & 1
+          }
+        }
+        mma_commit(drain);
+        const long long c0 = clock64();
+        while (!mbar_try_wait(drain, 0) && clock64() - c0 < kWaitLimitCycles) {
+        }
+      }
+    } else if (lane == 0 && nblk > 0) {
       constexpr uint32_t idesc_s = idesc_bf16(BM, BN, false);
       constexpr uint32_t idesc_o = idesc_bf16(BM, D, true);
       auto issue_s = [&](int x, int j) {
@@ -489,7 +541,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
     const int i_my = my_valid ? (slot % slots_row) / rep : 0;
     const int hh_my = slot % rep;
     const uint32_t lane_off = static_cast<uint32_t>(32 * q4) << 16;
-    const uint32_t tS = tmem + lane_off + kTmemS + x * BN;
+    const uint32_t tS0 = tmem + lane_off + kTmemS + x * BN;
     const uint32_t tO = tmem + lane_off + kTmemO + x * 128;
     const float scale = P.scale_log2;
     if (x < NT) {
@@ -511,11 +563,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
     float m_used = -INFINITY, l_sum = 0.f;
     bool live = true;
     for (int j = 0; j < nblk && active; ++j) {
-      if (!warp_wait(&s_full[x], j & 1, abort_flag, P.err, kErrAttn | 7) ||
+      const int sb = NT == 1 ? (j & 1) : x;          // S buffer of this block
+      if (!warp_wait(&s_full[sb], NT == 1 ? (j >> 1) & 1 : j & 1, abort_flag, P.err, kErrAttn | 7) ||
           !warp_wait(&mfull[j % MS], (j / MS) & 1, abort_flag, P.err, kErrAttn | 8)) {
         live = false;
         break;
       }
+      const uint32_t tS = NT == 1 ? tS0 + (j & 1) * BN : tS0;
       tc_fence_after();
       uint32_t mw[4];
 #pragma unroll
@@ -572,9 +626,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
         }
         return fmaxf(mq[0], mq[1]) * scale;
       };
-      // O_x may be rescaled here: P_x(j-1) V_{j-1} completed before S_x(j) was issued
-      auto rescale_o = [&](float alpha, bool resc) {
+      // O_x may be rescaled once P_x(j-1) V_{j-1} has completed: with two tiles it did before S_x(j) was issued;
+      // with one (S double-buffered) the softmax waits for it here
+      auto rescale_o = [&](float alpha, bool resc) -> bool {
         if (__any_sync(0xffffffffu, resc)) {
+          if (NT == 1 && j > 0 && !warp_wait(&pv_done[0], (j - 1) & 1, abort_flag, P.err, kErrAttn | 18))
+            return false;
+          tc_fence_after();
 #pragma unroll 1
           for (int dc = 0; dc < D / 32; ++dc) {
             uint32_t o[32];
@@ -585,6 +643,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
             tmem_st_32x32b_x32(tO + dc * 32, o);
           }
         }
+        return true;
       };
       if (__any_sync(0xffffffffu, m_used == -INFINITY)) {
         // a lane has no running max yet: the block's row max first (a separate pass over S), then P
@@ -616,7 +675,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
           m_used = mb;
           resc = true;
         }
-        rescale_o(alpha, resc);
+        if (!rescale_o(alpha, resc)) {
+          live = false;
+          break;
+        }
         p_pass(m_used);
       } else {
         // speculative: P against the running max; kept unless the block's max exceeds it by more than 2^8 (lazy
@@ -630,14 +692,17 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
             l_sum *= alpha;
             m_used = mb;
           }
-          rescale_o(alpha, redo);
+          if (!rescale_o(alpha, redo)) {
+            live = false;
+            break;
+          }
           p_pass(m_used);
         }
       }
       l_sum += (acc[0].x + acc[0].y) + (acc[1].x + acc[1].y);
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&p_full[x]);
+      mbar_arrive(&p_full[sb]);
     }
     // ---- epilogue: O / l, natural-log LSE (nothing is written after a time-out; the error word says why).
     // TMEM loads are warp-collective: every lane loads, valid slots store.
