@@ -186,12 +186,6 @@ typedef struct {
   int max_group_rows;           /* largest group (used when row_groups != NULL) */
   int prefix_bf16;              /* 1: Kp/Vp are bf16 (materialised), 0: int8 + ksc/vsc */
   int nsplit;                   /* CTAs per state prefix (0 or 1: one) */
-  const void* gate;             /* optional (NULL = none): the output gate of Qwen3.5's gated attention, bf16; the D
-                                   gate values of (row r, token i, head h) at gate[(r*t + i)*ld_gate + h*2*D + D + d]
-                                   (q_proj's [q | gate] per-head layout). When given, o receives
-                                   bf16(o * bf16(sigmoid(gate))), the value Qwen3_5Attention.forward feeds o_proj
-                                   (prefix_attn.py:129-131, modeling_qwen3_5.py:666-668); 16-byte aligned */
-  int64_t ld_gate;              /* row stride of gate in elements (a multiple of 8) */
 } od_attn_dims;
 
 OD_API int od_prefix_attn(const void* q, const void* Kp, const void* Vp, const void* ksc, const void* vsc,

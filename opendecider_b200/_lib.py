@@ -29,7 +29,7 @@ class AttnDims(ctypes.Structure):
     _fields_ = [("R", c_int64), ("t", c_int64), ("S", c_int64), ("T", c_int64), ("NQ", c_int64), ("Lq", c_int64),
                 ("Hq", c_int), ("Hkv", c_int), ("D", c_int), ("scale_dtype", c_int), ("sm_scale", c_float),
                 ("G", c_int64), ("max_group_rows", c_int), ("prefix_bf16", c_int),
-                ("nsplit", c_int), ("gate", c_void_p), ("ld_gate", c_int64)]
+                ("nsplit", c_int)]
 
 
 # exported symbol -> argument types (the declarations of include/od_b200.h)
@@ -296,16 +296,6 @@ def gate_quant(o: torch.Tensor, qkv: torch.Tensor, Hq: int, D: int, q=None, s=No
     return q, s
 
 
-def _set_gate(dims: AttnDims, gate, rows: int, Hq: int, D: int) -> None:
-    """od_attn_dims.gate / ld_gate from a (rows, >= 2 * Hq * D) bf16 tensor with unit column stride, or none."""
-    if gate is None:
-        return
-    assert gate.dtype == torch.bfloat16 and gate.dim() == 2 and gate.shape[0] == rows and gate.stride(1) == 1 \
-        and gate.shape[1] >= 2 * Hq * D, "gate: (R * t, >= 2 * Hq * D) bf16 rows"
-    dims.gate = gate.data_ptr()
-    dims.ld_gate = gate.stride(0)
-
-
 # query slots one od_prefix_attn CTA holds (two 128-slot tensor-core tiles): a row group may fill it
 ATTN_CTA_SLOTS = 256
 _PLANS: dict = {}
@@ -329,15 +319,13 @@ def _attn_plan(dims: AttnDims, dev) -> tuple[int, int]:
 def prefix_attn(q: torch.Tensor, k_own: torch.Tensor, v_own: torch.Tensor, sm_scale: float, *,
                 Kp=None, Vp=None, ksc=None, vsc=None, row_state=None, p_lo=None, p_hi=None, pmask=None,
                 Kq=None, Vq=None, row_q=None, q_len=None, own_lo=None, own_hi=None, row_groups=None,
-                max_group_rows: int = 1, out=None, want_lse: bool = False, nsplit: int | None = None, gate=None):
+                max_group_rows: int = 1, out=None, want_lse: bool = False, nsplit: int | None = None):
     """q (R, t, Hq, D), own k/v (R, t, Hkv, D) bf16; state prefix Kp/Vp (S, Hkv, T, D): int8 + scales ksc/vsc
     (S, Hkv, T[, 1]), or bf16 (the materialised cache, scales unused);
     optional bf16 question prefix Kq/Vq (NQ, Lq, Hkv, D); own keys valid in [own_lo[r], own_hi[r]) and causal;
     row_groups (G, 2) int32 [first row, rows] of consecutive rows sharing state and question, processed together
     (max_group_rows = the largest). nsplit: CTAs per state prefix (None: od_prefix_attn_plan's choice for this
     GPU; the partial results then merge in a second kernel through a workspace from torch's allocator).
-    gate (R * t, >= 2 * Hq * D) bf16, optional: the QKV projection output whose per-head [q | gate] columns hold the
-    output gate; o is then bf16(o * bf16(sigmoid(gate))), the o_proj input of Qwen3.5's gated attention.
     Returns o (R, t, Hq, D) [, lse (R, Hq, t)]."""
     dev = _need_cuda(q, k_own, v_own, Kp, Kq)
     R, t, Hq, D = q.shape
@@ -352,7 +340,6 @@ def prefix_attn(q: torch.Tensor, k_own: torch.Tensor, v_own: torch.Tensor, sm_sc
     G = row_groups.shape[0] if row_groups is not None else R
     dims = AttnDims(R, t, S, T, NQ, Lq, Hq, Hkv, D, sdt, sm_scale, G, max_group_rows if row_groups is not None else 1,
                     1 if pbf16 else 0, 0)
-    _set_gate(dims, gate, R * t, Hq, D)
     ws, ws_bytes = None, 0
     if Kp is not None:
         if nsplit is None:
@@ -387,7 +374,7 @@ def readout(logits: torch.Tensor, T: torch.Tensor, mask: torch.Tensor, bias: tor
 def prefix_attn_noalloc(q: torch.Tensor, k_own: torch.Tensor, v_own: torch.Tensor, sm_scale: float, *, nsplit: int,
                         Kp=None, Vp=None, ksc=None, vsc=None, row_state=None, p_lo=None, p_hi=None, pmask=None,
                         Kq=None, Vq=None, row_q=None, q_len=None, own_lo=None, own_hi=None, row_groups=None,
-                        max_group_rows: int = 1, out=None, want_lse: bool = False, gate=None):
+                        max_group_rows: int = 1, out=None, want_lse: bool = False):
     """prefix_attn through od_prefix_attn_noalloc: the split workspace is the library's static device scratch (no
     allocation by the call; `out`/`lse` are the caller's). Calls on one device must be stream-ordered."""
     dev = _need_cuda(q, k_own, v_own, Kp, Kq)
@@ -402,7 +389,6 @@ def prefix_attn_noalloc(q: torch.Tensor, k_own: torch.Tensor, v_own: torch.Tenso
     G = row_groups.shape[0] if row_groups is not None else R
     dims = AttnDims(R, t, S, T, NQ, Lq, Hq, Hkv, D, sdt, sm_scale, G, max_group_rows if row_groups is not None else 1,
                     1 if pbf16 else 0, nsplit)
-    _set_gate(dims, gate, R * t, Hq, D)
     _check(load().od_prefix_attn_noalloc(
         _p(q), _p(Kp), _p(Vp), _p(None if pbf16 else ksc), _p(None if pbf16 else vsc), _p(row_state), _p(p_lo),
         _p(p_hi), _p(pmask), _p(Kq), _p(Vq), _p(row_q), _p(q_len), _p(k_own), _p(v_own), _p(own_lo), _p(own_hi),

@@ -11,10 +11,9 @@ Per decoder layer (Qwen3_5DecoderLayer, modeling_qwen3_5.py:744-783) on M tokens
     od_rmsnorm_res_quant   residual add + input RMSNorm + per-token int8         (A3/A4/A5)
     od_gemm_w8a8           fused q/k/v projection (the reference's three Int8Linear weights stacked by rows)
     od_qk_norm_rope        gated-q split, q/k RMSNorm, RoPE
-    od_prefix_attn         causal / shared-prefix attention (int8 state prefix, bf16 question prefix, own keys),
-                           with the output gate o * sigmoid(gate) in its epilogue
+    od_prefix_attn         causal / shared-prefix attention (int8 state prefix, bf16 question prefix, own keys)
     od_kv_append_i8        int8 KV cache write (state pass)                      (A6)
-    od_quant_rows_i8       per-token int8 of the gated attention output (what od_gate_quant computes in one kernel)
+    od_gate_quant          o * sigmoid(gate) + per-token int8
     od_gemm_w8a8           o_proj
     od_rmsnorm_res_quant   residual add + post-attention RMSNorm + int8
     od_gemm_w8a8 SWIGLU    gate/up (rows interleaved in blocks of 128) with SiLU(gate)*up in the epilogue
@@ -328,10 +327,8 @@ class Backbone:
                 Kq=spec.qkv_prefix[li][0] if spec.qkv_prefix else None,
                 Vq=spec.qkv_prefix[li][1] if spec.qkv_prefix else None, row_q=spec.row_q, q_len=spec.q_len,
                 own_lo=spec.own_lo, own_hi=spec.own_hi, row_groups=spec.row_groups,
-                max_group_rows=spec.max_group_rows, gate=qkv)
-            # the output gate is applied in the attention epilogue; o_proj's per-token quantisation follows
-            oq, os_ = _lib.quant_rows(o.view(M, Hq * D), scale_dtype=torch.float32)
-            os_ = os_.view(-1)
+                max_group_rows=spec.max_group_rows)
+            oq, os_ = _lib.gate_quant(o.view(M, Hq * D), qkv, Hq, D)
             a = _lib.gemm_w8a8(oq, os_, L.o.q, L.o.scale, _lib.OD_EPI_BF16)
             mq, ms = _lib.rmsnorm_res_quant(a, L.ln2, cfg.eps, res_in=r, res_out=r)
             hm = _lib.gemm_w8a8(mq, ms, L.gate_up.q, L.gate_up.scale, _lib.OD_EPI_SWIGLU)

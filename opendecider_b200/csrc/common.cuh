@@ -167,20 +167,6 @@ __device__ __forceinline__ uint2 quant8(const float (&v)[8], float s, float r) {
                     __byte_perm(__byte_perm(b[4], b[5], 0x0040), __byte_perm(b[6], b[7], 0x0040), 0x5410));
 }
 
-// sigmoid(g) = 1 / (1 + exp(-g)) in fp32 (expf, IEEE division), rounded to bf16. A fast value from the hardware
-// exp2 / reciprocal approximations (relative error below 1.4e-6 for |g| < 16) rounds to the same bf16 unless a bf16
-// rounding boundary - a tie, low 16 bits 0x8000 - lies between the two: so only a fast value within 64 fp32 ulps
-// (relative 3.8e-6) of a tie, or |g| >= 16, takes the fp32 formula. (Crossing a bf16-representable value changes
-// the upper bits but both sides round to that value.)
-__device__ __forceinline__ float sigmoid_bf16(float g) {
-  float e, v;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(g * -1.4426950408889634f));
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(v) : "f"(1.0f + e));
-  const int lo = static_cast<int>(__float_as_uint(v) & 0xFFFFu);
-  if (fabsf(g) >= 16.0f || abs(lo - 0x8000) < 64) v = __fdiv_rn(1.0f, 1.0f + expf(-g));
-  return rbf(v);
-}
-
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));

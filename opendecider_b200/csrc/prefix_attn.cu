@@ -106,8 +106,6 @@ struct Params {
   float* part_o;                                // nsplit > 1: per split, O / l (fp32, the layout of o) ...
   float* part_lse;                              // ... and the natural-log LSE (the layout of lse)
   float scale_log2;
-  const __nv_bfloat16* gate;                    // optional output gate (od_attn_dims.gate), row stride ld_gate
-  int64_t ld_gate;
 };
 
 // byte offset of 16-byte chunk `ch` of row `row` in a 128B-swizzled tile made of `atom`-byte column atoms
@@ -740,21 +738,6 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
 #pragma unroll
               for (int k = 0; k < 16; ++k)
                 w[k] = pack_bf16(__uint_as_float(o[2 * k]) * inv, __uint_as_float(o[2 * k + 1]) * inv);
-              if (P.gate) {                             // bf16(o * bf16(sigmoid(gate))), as od_gate_quant forms it
-                const uint4* gp = reinterpret_cast<const uint4*>(
-                    P.gate + (static_cast<int64_t>(row0 + a_my) * t + i_my) * P.ld_gate +
-                    static_cast<int64_t>(g * rep + hh_my) * 2 * D + D + dc * 32);
-#pragma unroll
-                for (int k4 = 0; k4 < 4; ++k4) {
-                  const uint4 gv = __ldg(gp + k4);
-                  const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
-#pragma unroll
-                  for (int e = 0; e < 4; ++e) {
-                    const float2 gf = unpack2(gw[e]);
-                    w[4 * k4 + e] = bmul2(w[4 * k4 + e], pack_rn(sigmoid_bf16(gf.x), sigmoid_bf16(gf.y)));
-                  }
-                }
-              }
               uint4* dst = reinterpret_cast<uint4*>(P.o + orow + dc * 32);
 #pragma unroll
               for (int k = 0; k < 4; ++k) dst[k] = make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
@@ -842,8 +825,7 @@ template <int D>
 __global__ void __launch_bounds__(256) attn_merge_kernel(const float* __restrict__ part_o,
                                                          const float* __restrict__ part_lse, int nsplit,
                                                          int64_t n_rows, int t, int Hq, __nv_bfloat16* __restrict__ o,
-                                                         float* __restrict__ lse, const __nv_bfloat16* __restrict__ gate,
-                                                         int64_t ld_gate) {
+                                                         float* __restrict__ lse) {
   constexpr int E = D / 32;
   const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -867,17 +849,8 @@ __global__ void __launch_bounds__(256) attn_merge_kernel(const float* __restrict
   }
   const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
   __nv_bfloat16* dst = o + row * D + lane * E;
-  // the output gate of token ri, head h (od_attn_dims.gate)
-  const __nv_bfloat16* gp = gate ? gate + ri * ld_gate + h * 2 * D + D + lane * E : nullptr;
 #pragma unroll
-  for (int e = 0; e < E; e += 2) {
-    uint32_t w = pack_bf16(acc[e] * inv, acc[e + 1] * inv);
-    if (gp) {
-      const float2 gf = unpack2(*reinterpret_cast<const uint32_t*>(gp + e));
-      w = bmul2(w, pack_rn(sigmoid_bf16(gf.x), sigmoid_bf16(gf.y)));
-    }
-    *reinterpret_cast<uint32_t*>(dst + e) = w;
-  }
+  for (int e = 0; e < E; e += 2) *reinterpret_cast<uint32_t*>(dst + e) = pack_bf16(acc[e] * inv, acc[e + 1] * inv);
   if (lse && lane == 0) lse[lrow] = wsum > 0.f ? m + logf(wsum) : -INFINITY;
 }
 
@@ -984,13 +957,6 @@ extern "C" int od_prefix_attn(const void* q, const void* Kp, const void* Vp, con
     P.part_lse = P.part_o + static_cast<int64_t>(nsplit) * n_part * dims.D;
   }
   P.scale_log2 = dims.sm_scale * 1.4426950408889634f;
-  if (dims.gate) {
-    OD_REQUIRE(aligned16(dims.gate) && dims.ld_gate % 8 == 0 && dims.ld_gate >= 2LL * dims.Hq * dims.D,
-               "od_prefix_attn: the gate must be 16-byte aligned with a row stride that is a multiple of 8 and at "
-               "least 2 * Hq * D");
-    P.gate = static_cast<const __nv_bfloat16*>(dims.gate);
-    P.ld_gate = dims.ld_gate;
-  }
   {
     const uint64_t cols = static_cast<uint64_t>(dims.Hkv) * dims.D;
     OD_REQUIRE((cols * 2) % 16 == 0, "od_prefix_attn: Hkv * D * 2 must be a multiple of 16");
@@ -1032,10 +998,10 @@ extern "C" int od_prefix_attn(const void* q, const void* Kp, const void* Vp, con
   const unsigned mb = static_cast<unsigned>((n_part * 32 + 255) / 256);
   if (dims.D == 128)
     attn_merge_kernel<128><<<mb, 256, 0, st>>>(P.part_o, P.part_lse, nsplit, n_part, static_cast<int>(dims.t),
-                                                dims.Hq, P.o, lse, P.gate, P.ld_gate);
+                                                dims.Hq, P.o, lse);
   else
     attn_merge_kernel<64><<<mb, 256, 0, st>>>(P.part_o, P.part_lse, nsplit, n_part, static_cast<int>(dims.t),
-                                               dims.Hq, P.o, lse, P.gate, P.ld_gate);
+                                               dims.Hq, P.o, lse);
   OD_LAUNCH_CHECK();
   return ok();
 }

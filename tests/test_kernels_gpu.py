@@ -673,28 +673,6 @@ def test_prefix_attn_fp16_dequant_exact(cuda):
             assert torch.equal(o[r, i].view(torch.int16), want.view(torch.int16)), (r, i)
 
 
-@pytest.mark.parametrize("rows,t,nsplit", [(3, 5, 1), (3, 5, 3), (1, 200, 1), (2, 40, 2)])
-def test_prefix_attn_output_gate_matches_gate_quant(cuda, rows, t, nsplit):
-    """The output gate applied in the attention epilogue (and in the split merge) then od_quant_rows_i8 gives the
-    same int8 bytes and scales as the ungated attention followed by od_gate_quant (bf16(o * bf16(sigmoid(gate))),
-    then the per-token quantiser), on one-tile (rows of 5 tokens), two-tile (200-token rows) and split launches."""
-    g = syn.gen(83 + t)
-    S, T, Hq, Hkv, D = 2, 400, 32, 8, 128
-    ac = syn.attn_case(S=S, T=T, rows=rows, t=t, Hq=Hq, Hkv=Hkv, D=D, seed=83 + t)
-    Kq, Vq, ks, vs = _attn_inputs(cuda, ac)
-    R = ac.q.shape[0]
-    qkv = (torch.randn(R * t, Hq * 2 * D + 2 * Hkv * D, generator=g) * 3).to(torch.bfloat16).to(cuda)
-    args = dict(Kp=Kq, Vp=Vq, ksc=ks, vsc=vs, row_state=ac.row_state.to(cuda), nsplit=nsplit)
-    q, k, v = ac.q.to(cuda), ac.k.to(cuda), ac.v.to(cuda)
-    o = _lib.prefix_attn(q, k, v, D ** -0.5, **args)
-    og = _lib.prefix_attn(q, k, v, D ** -0.5, gate=qkv, **args)
-    q1, s1 = _lib.gate_quant(o.view(R * t, Hq * D), qkv, Hq, D)
-    q2, s2 = _lib.quant_rows(og.view(R * t, Hq * D), scale_dtype=torch.float32)
-    assert _lib.device_error(cuda) == 0
-    assert torch.equal(q1, q2)
-    assert torch.equal(s1.view(-1), s2.view(-1))
-
-
 @pytest.mark.parametrize("M,H,V", [(300, 256, 1000), (130, 4096, 4099), (7, 64, 256)])
 def test_lm_logprob_matches_token_logprob(cuda, M, H, V):
     """Backbone.token_logprob on the tensor cores: bf16 logits, a vocabulary log-sum-exp (padded last tile left
