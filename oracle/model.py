@@ -9,8 +9,12 @@ the transformers Qwen3.5 modules on a bf16 CPU model):
                  bf16((acc * s_x) * s_w); weights quantised as Int8Linear does (quant.py:124-127)
   state pass     Backbone.prefix_cache_batch (backbone.py:347-368): left-padded, causal, the cache quantised per
                  (state, head, token) by Int8Tensor.quantize (backbone.py:446)
-  row passes     V3._branched_feats_qcache / _branched_feats (v3.py:393-534) with shared_prefix_attention's
-                 _split_attention CPU branch (prefix_attn.py:58-76) over the materialised int8 state K/V
+  row passes     V3._branched_feats_qcache (v3.py:446-534): one right-padded question pass over every question, then
+                 option rows sorted by length in chunks of 64; each attention call routed as shared_prefix_attention
+                 routes it (prefix_attn.py:135-175): one masked scaled_dot_product_attention call for rows of several
+                 states (prefix_attn.py:102-117), else _split_attention's CPU branch per state (prefix_attn.py:58-76)
+  attention      the reference's own CPU calls: torch's scaled_dot_product_attention (its flash kernel on the CPU) for
+                 the state pass and the one-call path, so the oracle equals the reference bit for bit end to end
   trunk/readout  the trunk of opendecider_b200.v3 on the CPU (plain PyTorch, the same code the GPU path runs, pinned
                  to the reference by tests/golden/e2e_config1.npz) and Decider._probs' softmax (decider.py:255-257)
 Only tests/, __graft_entry__.smoke() and bench.py (cpu_baseline, --impl reference) may import this module.
@@ -111,22 +115,22 @@ class OracleDecoder:
 
 
 def sdpa_flash(q, k, v, ok):
-    """The attention of the reference's own passes over a cache (the transformers sdpa interface, which on the CPU
-    runs torch's flash-attention kernel: aten/src/ATen/native/cpu/FlashAttentionKernel.cpp): fp32 scores
-    (q.k) * D^-0.5, fp32 max and exp-sum, the probabilities rounded to bf16 before the P.V product (fp32
-    accumulation), the sum divided out in fp32, bf16 out. Below 512 keys that kernel takes one key block, so no
-    rescaling enters. q (R, t, Hq, D), k/v (R, Tk, Hkv, D) bf16, ok (R, t, Tk) bool -> (R, t, Hq*D) bf16."""
+    """The attention of every batched pass the reference runs through torch's scaled_dot_product_attention with a
+    boolean mask - the transformers sdpa interface of its state pass (modeling_qwen3_5.py:676-686 ->
+    integrations/sdpa_attention.py) and shared_prefix_attention's one-call multi-state path (prefix_attn.py:102-117).
+    On the CPU that call runs torch's flash-attention kernel (fp32 scores, probabilities rounded to bf16 before the
+    P.V product, key blocks of 512 with running-max rescaling); the oracle makes the same call on the CPU, so its
+    arithmetic is the reference's own, bit for bit. Query rows with no visible key attend every key instead, as
+    transformers' sdpa mask does for them (their outputs feed no real token). q (R, t, Hq, D), k/v (R, Tk, Hkv, D)
+    bf16, ok (R, t, Tk) bool -> (R, t, Hq*D) bf16."""
     R, t, Hq, D = q.shape
     g = Hq // k.shape[2]
-    qf = q.float().transpose(1, 2)
-    kf = k.float().repeat_interleave(g, 2).transpose(1, 2)
-    vf = v.float().repeat_interleave(g, 2).transpose(1, 2)
-    s = (qf @ kf.transpose(-1, -2)) * D ** -0.5
-    s = s.masked_fill(~ok[:, None], float("-inf"))
-    m = s.amax(-1, keepdim=True).clamp_min(-3.0e38)
-    p = torch.exp(s - m)
-    o = (p.to(BF).float() @ vf) / p.sum(-1, keepdim=True).clamp_min(1e-30)
-    return o.transpose(1, 2).reshape(R, t, Hq * D).to(BF)
+    ok = ok | ~ok.any(-1, keepdim=True)
+    qq = q.transpose(1, 2)
+    kk = k.repeat_interleave(g, 2).transpose(1, 2)
+    vv = v.repeat_interleave(g, 2).transpose(1, 2)
+    o = torch.nn.functional.scaled_dot_product_attention(qq, kk, vv, attn_mask=ok[:, None], scale=D ** -0.5)
+    return o.transpose(1, 2).reshape(R, t, Hq * D)
 
 
 def causal_attend(pad):
@@ -139,14 +143,38 @@ def causal_attend(pad):
     return f
 
 
+BATCHED_BYTES = 1 << 30     # prefix_attn.py:27: the one-call multi-state path's bound on gathered prefix K/V
+
+
+def uses_batched_call(n_rows: int, n_states: int, hkv: int, d: int, prefix_len: int) -> bool:
+    """shared_prefix_attention's choice (prefix_attn.py:159-167): rows reading more than one state go through ONE
+    masked scaled_dot_product_attention call per layer when rows x (Hkv * D * prefix length) bf16 values x 4 stays
+    within BATCHED_BYTES; otherwise (and always for a single state) through _split_attention, one state at a time."""
+    return n_states > 1 and n_rows * hkv * d * prefix_len * 2 * 4 <= BATCHED_BYTES
+
+
+def split_rows(q, k, v, Kp, Vp, pm):
+    """_forward's per-state branch (prefix_attn.py:118-129) for rows of one state: the prefix from its first real key
+    (leading pads sliced off), later pads masked, then _split_attention's CPU branch (fp32 throughout).
+    q (n, t, Hq, D), k/v (n, t, Hkv, D), Kp/Vp (Hkv, P, D), pm (P,) bool -> (n, t, Hq*D) bf16."""
+    n, t, Hq, D = q.shape
+    off = int(pm.int().argmax())
+    holes = bool((~pm).sum() > off)
+    o = ops.split_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), Kp[:, off:], Vp[:, off:],
+                            pm[off:] if holes else None, D ** -0.5)
+    return o.to(BF).transpose(1, 2).reshape(n, t, Hq * D)
+
+
 class OracleDecision:
     """decide_many on the CPU: state pass, question-cache row passes, trunk, readout."""
 
     def __init__(self, cfg, sd, trunk, tok, temps: dict, temperature: float, layers: int | None = None,
-                 list_cap: int = 16, qcache_min_rows: int = 12, none_text: str = "none of the above"):
+                 list_cap: int = 16, qcache_min_rows: int = 12, none_text: str = "none of the above",
+                 branch_chunk: int = 64):
         self.dec = OracleDecoder(cfg, sd, layers)
         self.cfg, self.trunk, self.tok, self.temps, self.temperature = cfg, trunk, tok, temps, temperature
         self.list_cap, self.qcache_min_rows, self.none_text = list_cap, qcache_min_rows, none_text
+        self.branch_chunk = branch_chunk                  # v3_branch_chunk (models.py:66)
 
     def state_pass(self, states):
         from opendecider_b200.batching import state_text
@@ -236,42 +264,62 @@ class OracleDecision:
         for j, t in enumerate(q_tok):
             Qids[j, : len(t)] = torch.tensor(t)
         pm_state = torch.arange(T)[None, :] >= pad[:, None]
+        Hkv, D = self.cfg.kv_heads, self.cfg.head_dim
+        qmask = torch.arange(Lq)[None, :] < lq[:, None]
+        causal = lambda t: torch.arange(t)[None, :] <= torch.arange(t)[:, None]
 
-        def attend_q(i, q, k, v):                         # question pass: state prefix + own (causal)
-            Kp, Vp = cache[i]
-            out = torch.empty(q.shape[0], q.shape[1], q.shape[2] * q.shape[3], dtype=BF)
-            for j in range(q.shape[0]):
-                s = int(sidx[j])
-                o = ops.split_attention(q[j:j + 1].transpose(1, 2), k[j:j + 1].transpose(1, 2),
-                                        v[j:j + 1].transpose(1, 2), Kp[s], Vp[s], pm_state[s], q.shape[3] ** -0.5)
-                out[j] = o.to(BF).transpose(1, 2).reshape(q.shape[1], -1)
+        # the question pass: ONE right-padded pass over every question (v3_question_batch, v3.py:484-499), reading
+        # the state prefix through shared_prefix_attention (one masked call, or one state at a time)
+        batched_q = uses_batched_call(N, len(set(sidx.tolist())), Hkv, D, T)
+
+        def attend_q(i, q, k, v):
+            Kp, Vp = cache[i]                                             # (S, Hkv, T, D) materialised
+            if batched_q:
+                ok = torch.cat([pm_state[sidx][:, None, :].expand(N, Lq, T), causal(Lq)[None].expand(N, Lq, Lq)], 2)
+                return sdpa_flash(q, torch.cat([Kp[sidx].transpose(1, 2), k], 1),
+                                  torch.cat([Vp[sidx].transpose(1, 2), v], 1), ok)
+            out = torch.empty(N, Lq, q.shape[2] * D, dtype=BF)
+            for st in sorted(set(sidx.tolist())):
+                r = (sidx == st).nonzero().squeeze(1)
+                out[r] = split_rows(q[r], k[r], v[r], Kp[st], Vp[st], pm_state[st])
             return out
 
         qpos = (T + torch.arange(Lq)).expand(N, Lq)
         fq, qkv = self.dec.run(Qids, qpos, attend_q, feats)
-        q_flat = fq[torch.arange(Lq)[None, :] < lq[:, None]]
+        q_flat = fq[qmask]
         o_flat = torch.empty(int(lo.sum()), fq.shape[-1], dtype=fq.dtype)
         o_start = torch.cumsum(lo, 0) - lo
-        for m in range(lo.numel()):                       # option rows, one at a time (width >= 2)
-            w = max(2, int(lo[m]))
-            ids = torch.zeros(1, w, dtype=torch.long)
-            ids[0, : lo[m]] = torch.tensor(o_tok[m])
-            qj = int(row_q[m])
-            s = int(sidx[qj])
+        # option rows (v3.py:500-519): every question's rows sorted by option length (stable), chunks of
+        # v3_branch_chunk rows, each as wide as its longest option (>= 2), right-padded; a row's tokens continue at its
+        # own question's end; the prefix is [state ; question] (pmq masks both levels' pads)
+        pmq = torch.cat([pm_state[sidx], qmask], 1)                       # (N, T + Lq)
+        order = torch.argsort(lo, stable=True)
+        for a in range(0, order.numel(), self.branch_chunk):
+            rs = order[a: a + self.branch_chunk]
+            n, w = rs.numel(), max(2, int(lo[rs].max()))
+            ids = torch.zeros(n, w, dtype=torch.long)
+            for j, m in enumerate(rs.tolist()):
+                ids[j, : lo[m]] = torch.tensor(o_tok[m])
+            qr = row_q[rs]
+            batched = uses_batched_call(n, len(set(qr.tolist())), Hkv, D, T + Lq)
 
-            def attend_o(i, q, k, v, qj=qj, s=s):
+            def attend_o(i, q, k, v, qr=qr, batched=batched):
                 Kp, Vp = cache[i]
-                Kq, Vq = qkv[i]
-                Kc = torch.cat([Kp[s], Kq[qj].transpose(0, 1)], 1)
-                Vc = torch.cat([Vp[s], Vq[qj].transpose(0, 1)], 1)
-                pmc = torch.cat([pm_state[s], torch.arange(Lq) < lq[qj]])
-                o = ops.split_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), Kc, Vc, pmc,
-                                        q.shape[3] ** -0.5)
-                return o.to(BF).transpose(1, 2).reshape(1, q.shape[1], -1)
+                Kq, Vq = qkv[i]                                           # (N, Lq, Hkv, D) captured
+                Kc = torch.cat([Kp[sidx].transpose(1, 2), Kq], 1)         # (N, T + Lq, Hkv, D)
+                Vc = torch.cat([Vp[sidx].transpose(1, 2), Vq], 1)
+                if batched:
+                    t = q.shape[1]
+                    ok = torch.cat([pmq[qr][:, None, :].expand(len(qr), t, T + Lq),
+                                    causal(t)[None].expand(len(qr), t, t)], 2)
+                    return sdpa_flash(q, torch.cat([Kc[qr], k], 1), torch.cat([Vc[qr], v], 1), ok)
+                qj = int(qr[0])
+                return split_rows(q, k, v, Kc[qj].transpose(0, 1), Vc[qj].transpose(0, 1), pmq[qj])
 
-            pos = (T + lq[qj] + torch.arange(w))[None, :]
+            pos = (T + lq[qr])[:, None] + torch.arange(w)[None, :]
             fo, _ = self.dec.run(ids, pos, attend_o, feats)
-            o_flat[o_start[m]: o_start[m] + lo[m]] = fo[0, : lo[m]]
+            for j, m in enumerate(rs.tolist()):
+                o_flat[o_start[m]: o_start[m] + lo[m]] = fo[j, : lo[m]]
         sl = torch.tensor([lens[q.state_idx] for q in qs])
         tplan = self.trunk.prepare(lq, lo, n_opt, sl)
         lp = None

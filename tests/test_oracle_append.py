@@ -2,13 +2,9 @@
 (tests/golden/append_config5.npz, made by tests/golden/make_golden_append.py): 2 requests, 96-token states, 24
 appended ids, the tiny backbone of the e2e fixture.
 
-What is bit-exact and what is not: everything before a layer's attention (A8W8 projections, q/k RMSNorm, RoPE at the
-continued positions, the per-token int8 quantisation of the new K/V) is integer or correctly-rounded bf16 work and
-is compared byte for byte - for layer 0 on the oracle's own chained pass, and for every layer on the hidden state
-the reference itself fed that layer. The attention output is float work whose summation order differs between
-implementations (the reference's CPU flash kernel, the oracle's matmuls, the tensor-core kernel); a one-ulp change in
-it moves the next layer's int8 activations by a step, so the chained K/V of layers >= 1 are compared within a
-dequantised tolerance."""
+Everything is compared byte for byte: the oracle's attention over the restored prefix is the reference's own CPU
+call (torch's scaled_dot_product_attention, as transformers makes it), so the chained layers' K/V, the snapshots and
+the packed cache equal the reference's exactly in every layer, on the machine that made the fixture."""
 from __future__ import annotations
 
 import os
@@ -28,10 +24,6 @@ from oracle import ops  # noqa: E402
 from oracle.model import BF, OracleDecision  # noqa: E402
 from opendecider_b200 import synthetic as syn  # noqa: E402
 from opendecider_b200.backbone import DecoderConfig, synthetic_weights  # noqa: E402
-
-# chained layers >= 1: max |dequantised difference| / max |golden value| per (request, layer, K|V)
-CHAIN_REL_TOL = 0.06
-
 
 @pytest.fixture(scope="module")
 def setup():
@@ -85,21 +77,17 @@ def test_every_layer_kv_write_bit_exact_on_reference_input(setup):
                 np.testing.assert_array_equal(_bits(torch.from_numpy(sc[..., 0]).to(BF)), g[f"snap.{r}.{li}.{a}.s"])
 
 
-def _deq(q, s_bits):
-    s = torch.from_numpy(s_bits).view(BF).float().numpy()
-    return q.astype(np.float32) * s[..., None]
-
-
-def test_chained_layers_within_tolerance(setup):
+def test_chained_layers_bit_exact(setup):
+    """Every layer's appended K/V after the chained continuation (each layer's attention reads the restored prefix
+    and the earlier appended tokens): the snapshot bytes and scales and the packed cache, equal to the reference's."""
     cfg, reqs, tok, g, od, runs = setup
     for r, (_, snaps, packs) in enumerate(runs):
         for li in range(cfg.layers):
             for ai, a in enumerate("kv"):
                 for name, (q8, sc) in (("snap", snaps[li][ai]), ("pack", packs[li][ai])):
-                    ref = _deq(g[f"{name}.{r}.{li}.{a}.q"], g[f"{name}.{r}.{li}.{a}.s"])
-                    got = _deq(q8[0].numpy(), _bits(sc[0]))
-                    rel = float(np.abs(ref - got).max() / np.abs(ref).max())
-                    assert rel <= CHAIN_REL_TOL, (name, r, li, a, rel)
+                    np.testing.assert_array_equal(q8[0].numpy(), g[f"{name}.{r}.{li}.{a}.q"],
+                                                  err_msg=f"{name} req {r} layer {li} {a}")
+                    np.testing.assert_array_equal(_bits(sc[0]), g[f"{name}.{r}.{li}.{a}.s"])
 
 
 def test_pack_layer0_bit_exact(setup):
