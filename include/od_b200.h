@@ -176,6 +176,8 @@ OD_API int od_gate_quant(const void* o, const void* qkv, int64_t ldqkv, int64_t 
  * GPU of num_sms SMs and returns the workspace size; workspace may be NULL when nsplit <= 1.
  * Every row sees the same key layout whatever its index or group: outputs do not depend on row order.
  * Runs on tcgen05 (S = Q K^T and O += P V in TMEM); head_dim 64 or 128.
+ * o and lse are undefined whenever od_device_error reports a code (a bounded wait gave up); with nsplit > 1 the
+ * merge then writes NaN. An empty problem (R, t or G = 0) returns OD_OK without a launch or a workspace.
  */
 typedef struct {
   int64_t R, t, S, T, NQ, Lq;   /* rows, tokens per row, states, prefix capacity, questions, question length */

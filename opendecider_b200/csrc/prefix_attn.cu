@@ -820,18 +820,27 @@ int launch_attn(const Params& P, dim3 grid, cudaStream_t st) {
 
 // The splits of a query row merged exactly by log-sum-exp (the Hydragen merge of prefix_attn._split_attention):
 // O = sum_s w_s O_s / sum_s w_s, w_s = exp(lse_s - max lse), LSE = max lse + log sum_s w_s. One warp per output
-// row (row, token, head), D / 32 elements per lane.
+// row (row, token, head), D / 32 elements per lane. When the device error word is set (a split gave up a bounded
+// wait and may have left its partials unwritten, so the workspace can hold an earlier call's values), every output
+// is NaN instead of a plausible mix.
 template <int D>
 __global__ void __launch_bounds__(256) attn_merge_kernel(const float* __restrict__ part_o,
                                                          const float* __restrict__ part_lse, int nsplit,
                                                          int64_t n_rows, int t, int Hq, __nv_bfloat16* __restrict__ o,
-                                                         float* __restrict__ lse) {
+                                                         float* __restrict__ lse, const int32_t* __restrict__ err) {
   constexpr int E = D / 32;
   const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (row >= n_rows) return;
   const int64_t h = row % Hq, ri = row / Hq;
   const int64_t lrow = ((ri / t) * Hq + h) * t + ri % t;
+  if (*reinterpret_cast<const volatile int32_t*>(err) != 0) {
+    __nv_bfloat16* dst = o + row * D + lane * E;
+#pragma unroll
+    for (int e = 0; e < E; e += 2) *reinterpret_cast<uint32_t*>(dst + e) = pack_bf16(NAN, NAN);
+    if (lse && lane == 0) lse[lrow] = NAN;
+    return;
+  }
   float m = -INFINITY;
   for (int sp = 0; sp < nsplit; ++sp) m = fmaxf(m, __ldg(part_lse + sp * n_rows + lrow));
   float acc[E];
@@ -887,11 +896,14 @@ extern "C" int od_prefix_attn(const void* q, const void* Kp, const void* Vp, con
                               const void* k_own, const void* v_own, const int32_t* own_lo, const int32_t* own_hi,
                               const int32_t* row_groups, void* o, float* lse, od_attn_dims dims, void* workspace,
                               int64_t workspace_bytes, void* stream) {
-  OD_REQUIRE(q && k_own && v_own && o, "od_prefix_attn: null pointer");
   OD_REQUIRE(dims.D == 64 || dims.D == 128, "od_prefix_attn: head_dim %d not in {64, 128}", dims.D);
   OD_REQUIRE(dims.Hq > 0 && dims.Hkv > 0 && dims.Hq % dims.Hkv == 0, "od_prefix_attn: bad head counts");
   const int rep = dims.Hq / dims.Hkv;
   OD_REQUIRE(dims.R >= 0 && dims.t >= 0 && dims.t < (1 << 24), "od_prefix_attn: bad R/t");
+  OD_REQUIRE(!row_groups || dims.G >= 0, "od_prefix_attn: bad row groups");
+  // an empty problem needs no buffers (empty tensors may carry null pointers), no workspace and no launch
+  if ((row_groups ? dims.G : dims.R) == 0 || dims.t == 0) return ok();
+  OD_REQUIRE(q && k_own && v_own && o, "od_prefix_attn: null pointer");
   const bool pbf16 = dims.prefix_bf16 != 0;
   OD_REQUIRE(!Kp || (Vp && (pbf16 || (ksc && vsc)) && row_state && dims.S > 0 && dims.T > 0 && dims.T < (1 << 30)),
              "od_prefix_attn: the state prefix needs Vp, row_state, S, T (and ksc/vsc when int8)");
@@ -916,7 +928,6 @@ extern "C" int od_prefix_attn(const void* q, const void* Kp, const void* Vp, con
                    workspace_bytes >= static_cast<int64_t>(sizeof(float)) * nsplit * n_part * (dims.D + 1),
                "od_prefix_attn: %d splits need a 16-byte aligned workspace of %lld bytes (od_prefix_attn_plan)", nsplit,
                (long long)(static_cast<int64_t>(sizeof(float)) * nsplit * n_part * (dims.D + 1)));
-  if (G == 0 || dims.t == 0) return ok();
   int32_t* err = device_error_word();
   if (!err) return fail(OD_ECUDA, "od_prefix_attn: no device error word");
   Params P;
@@ -998,10 +1009,10 @@ extern "C" int od_prefix_attn(const void* q, const void* Kp, const void* Vp, con
   const unsigned mb = static_cast<unsigned>((n_part * 32 + 255) / 256);
   if (dims.D == 128)
     attn_merge_kernel<128><<<mb, 256, 0, st>>>(P.part_o, P.part_lse, nsplit, n_part, static_cast<int>(dims.t),
-                                                dims.Hq, P.o, lse);
+                                                dims.Hq, P.o, lse, P.err);
   else
     attn_merge_kernel<64><<<mb, 256, 0, st>>>(P.part_o, P.part_lse, nsplit, n_part, static_cast<int>(dims.t),
-                                               dims.Hq, P.o, lse);
+                                               dims.Hq, P.o, lse, P.err);
   OD_LAUNCH_CHECK();
   return ok();
 }
@@ -1036,6 +1047,8 @@ constexpr int64_t kNoAllocScratchBytes = 16LL << 20;
 __device__ __align__(256) unsigned char g_attn_scratch[kNoAllocScratchBytes];
 
 void* attn_scratch() {
+  // Filled without a lock: threads that race on a device's first call all store the same address (the symbol's
+  // address on that device), so a duplicate lookup is the only effect of the race.
   static void* addr[64] = {nullptr};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;

@@ -54,7 +54,9 @@ def gather_rows(x: torch.Tensor, group=None) -> list[torch.Tensor]:
 
 class DistributedDecider:
     """decide_many over all ranks: every rank receives the full request list, runs its contiguous block and gets
-    every request's answers back (renormalised probabilities and P(none) gathered once)."""
+    every request's answers back. One gather per call carries, per question, the raw option probabilities (the
+    softmax over the options and `none`, against which P(none) decides the value, decider.py:345), the caller-option
+    renormalisation and P(none), so every rank answers exactly as one rank deciding the whole list would."""
 
     def __init__(self, decider, group=None):
         self.decider, self.group = decider, group
@@ -65,10 +67,12 @@ class DistributedDecider:
         blocks = shard([request_weight(r, tok) for r in requests], world)
         a, b = blocks[rank]
         mine = requests[a:b]
-        if mine:
+        if mine and any(r.questions for r in mine):
             plan = self.decider.plan(mine)
             (probs, renorm, p_none), _ = self.decider.execute(plan)
-            local = torch.cat([renorm, p_none.double()[:, None]], 1)
+            # [raw probs (K) | renormalised (K) | P(none)] in float64: fp32 values and the fp64 renormalisation
+            # travel exactly
+            local = torch.cat([probs.double(), renorm.double(), p_none.double()[:, None]], 1)
         else:
             local = torch.zeros(0, 1, dtype=torch.float64, device=self.decider.model.backbone.device)
         parts = gather_rows(local, self.group)
@@ -77,8 +81,10 @@ class DistributedDecider:
             if e <= s:
                 continue
             reqs = requests[s:e]
+            if part.shape[0] == 0:                       # a block whose requests ask nothing
+                out += [{} for _ in reqs]
+                continue
             p = self.decider.plan_questions(reqs)
-            K = part.shape[1] - 1
-            ren, pn = part[:, :K], part[:, K].float()
-            out += self.decider.answers(p, (ren.float(), ren, pn))
+            K = (part.shape[1] - 1) // 2
+            out += self.decider.answers(p, (part[:, :K].float(), part[:, K:2 * K], part[:, 2 * K].float()))
         return out

@@ -19,7 +19,10 @@ import torch
 
 ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 sys.path.insert(0, ROOT)
-sys.path.insert(0, os.environ.get("OPENDECIDER_REF", "/root/reference/src"))
+if __name__ == "__main__":
+    if not os.environ.get("OPENDECIDER_REF"):     # the reference's src/ directory (this generator imports it)
+        sys.exit("set OPENDECIDER_REF to the reference checkout's src/ directory")
+    sys.path.insert(0, os.environ["OPENDECIDER_REF"])
 
 from opendecider_b200 import synthetic as syn  # noqa: E402
 

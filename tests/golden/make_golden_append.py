@@ -24,7 +24,7 @@ import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, HERE)
-from make_golden_e2e import FEATURE_LAYERS, build_reference  # noqa: E402
+from make_golden_e2e import FEATURE_LAYERS, build_reference, use_reference  # noqa: E402
 
 from opendecider_b200 import synthetic as syn  # noqa: E402
 from opendecider_b200.backbone import DecoderConfig  # noqa: E402
@@ -38,6 +38,7 @@ def bits(t: torch.Tensor) -> np.ndarray:
 
 
 def main():
+    use_reference()
     from opendecider.state_cache import PrefixCache
     torch.manual_seed(0)
     cfg = DecoderConfig.tiny(feature_layers=tuple(FEATURE_LAYERS))

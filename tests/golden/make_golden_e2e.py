@@ -29,7 +29,6 @@ import torch
 
 ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 sys.path.insert(0, ROOT)
-sys.path.insert(0, os.environ.get("OPENDECIDER_REF", "/root/reference/src"))
 
 from opendecider_b200 import synthetic as syn  # noqa: E402
 from opendecider_b200.backbone import DecoderConfig, synthetic_weights  # noqa: E402
@@ -59,7 +58,17 @@ class A8W8:
         return (self.q.float() * self.s.float()).to(torch.bfloat16).t()
 
 
+def use_reference() -> None:
+    """Put the reference's src/ directory (OPENDECIDER_REF, required) on sys.path; the generators import it."""
+    ref = os.environ.get("OPENDECIDER_REF")
+    if not ref:
+        sys.exit("set OPENDECIDER_REF to the reference checkout's src/ directory")
+    if ref not in sys.path:
+        sys.path.insert(0, ref)
+
+
 def build_reference(cfg: DecoderConfig, tok):
+    use_reference()
     from transformers.models.qwen3_5.configuration_qwen3_5 import Qwen3_5TextConfig
     from transformers.models.qwen3_5.modeling_qwen3_5 import Qwen3_5ForCausalLM, Qwen3_5TextModel
     from opendecider.backbone import Backbone, BackboneConfig, use_reference_kernels
@@ -92,6 +101,7 @@ def build_reference(cfg: DecoderConfig, tok):
 
 
 def run(qcache: bool, lm: bool = False):
+    use_reference()
     from opendecider.models import ModelConfig, build_model
     from opendecider.decider import Decider, prepare_inference_
     from opendecider import v3 as ref_v3

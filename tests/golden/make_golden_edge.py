@@ -13,7 +13,7 @@ import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, HERE)
-from make_golden_e2e import FEATURE_LAYERS, TEMPS, TRUNK, build_reference  # noqa: E402
+from make_golden_e2e import FEATURE_LAYERS, TEMPS, TRUNK, build_reference, use_reference  # noqa: E402
 
 from opendecider_b200 import synthetic as syn  # noqa: E402
 from opendecider_b200.backbone import DecoderConfig  # noqa: E402
@@ -35,6 +35,7 @@ def edge_requests():
 
 
 def main():
+    use_reference()
     from opendecider.decider import Decider, prepare_inference_
     from opendecider.models import ModelConfig, build_model
     torch.manual_seed(0)

@@ -79,3 +79,91 @@ def test_gather_fails_cleanly_when_a_rank_dies():
             p.kill()
     assert res[1] == "died"
     assert res[0].startswith("error"), res[0]
+
+
+class _StubModel:
+    """Stands in for V3Model on CPU: a tokenizer and a device; the stub decider computes its probabilities itself."""
+
+    def __init__(self):
+        from opendecider_b200.synthetic import SyntheticTokenizer
+        self.tok = SyntheticTokenizer(1024)
+        self.backbone = type("BB", (), {"device": torch.device("cpu")})()
+
+
+def _stub_decider():
+    """Decider whose device work is replaced by a deterministic CPU function of each question (the host logic -
+    plans, `none`, answers - is the real Decider's). The question 'tie' gets raw probabilities [0.3, 0.3 | none 0.4]:
+    P(none) beats the raw option maximum (0.3) but not the renormalised one (0.5)."""
+    from opendecider_b200.decider import Decider
+
+    class StubDecider(Decider):
+        def __init__(self):
+            self.model, self.temperature, self.temperature_by_type = _StubModel(), 1.0, {}
+            self.none_text = "none of the above"
+
+        def plan(self, requests, cache=None, appends=None):
+            return self.plan_questions(requests)
+
+        def execute(self, plan, cache=None):
+            qs = plan["questions"]
+            Kmax = max(len(q.options) for q in qs)
+            probs = torch.zeros(len(qs), Kmax, dtype=torch.float32)
+            for i, q in enumerate(qs):
+                K = len(q.options)
+                if q.prompt == "tie":
+                    probs[i, :K] = torch.tensor([0.3, 0.3, 0.4])
+                else:
+                    w = torch.tensor([1.0 + (sum(map(ord, q.prompt + o)) % 7) for o in q.options])
+                    probs[i, :K] = w / w.sum()
+            renorm = torch.zeros(len(qs), Kmax, dtype=torch.float64)
+            p_none = torch.zeros(len(qs), dtype=torch.float32)
+            for i, q in enumerate(qs):
+                K = getattr(q, "none_col", len(q.options))
+                renorm[i, :K] = probs[i, :K].double() / probs[i, :K].double().sum()
+                p_none[i] = probs[i, K] if hasattr(q, "none_col") else 0.0
+            return (probs, renorm, p_none), None
+
+    return StubDecider()
+
+
+def _requests():
+    from opendecider_b200.batching import Question
+    from opendecider_b200.synthetic import Request
+    reqs = []
+    for i in range(7):
+        qs = [Question(f"t{10 + i} t{11 + i}", [f"t{20 + j}" for j in range(2 + i % 3)], name="a")]
+        if i % 2:
+            qs.append(Question.noul(f"t{30 + i}", name="b"))
+        reqs.append(Request(" ".join(f"t{40 + j}" for j in range(3 + 5 * i)), qs))
+    reqs[3] = Request("t1 t2", [Question("tie", ["t5", "t6"], name="a")])
+    reqs.append(Request("t3", []))                           # a request without questions
+    return reqs
+
+
+def _decider_worker(rank, world, port, q):
+    from opendecider_b200.distributed import DistributedDecider
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        got = DistributedDecider(_stub_decider()).decide_many(_requests())
+        q.put((rank, got))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_distributed_decider_equals_single_rank():
+    """DistributedDecider.decide_many on two gloo ranks answers every request exactly as one rank's decide_many:
+    same values, probabilities and P(none), in request order, on both ranks - including the question whose P(none)
+    beats the raw option maximum but not the renormalised one (value 'none')."""
+    want = _stub_decider().decide_many(_requests())
+    assert want[3]["a"]["value"] == "none" and want[-1] == {}
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29500 + (os.getpid() + 250) % 1000
+    procs = [ctx.Process(target=_decider_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    assert res[0] == want and res[1] == want

@@ -42,6 +42,19 @@ def test_no_alloc_without_split_needs_no_scratch(cuda):
     assert torch.equal(o1, o2) and torch.equal(l1, l2)
 
 
+def test_no_alloc_empty_problem(cuda):
+    """No rows (or no tokens) with a split requested: both variants return without a launch and without scratch."""
+    q, k, v, args = _case(cuda, 45)
+    no_rows = (q[:0], k[:0], v[:0])
+    no_tokens = (q[:, :0].contiguous(), k[:, :0].contiguous(), v[:, :0].contiguous())
+    for qe, ke, ve in (no_rows, no_tokens):
+        o1, l1 = _lib.prefix_attn(qe, ke, ve, 128 ** -0.5, nsplit=3, **args)
+        o2, l2 = _lib.prefix_attn_noalloc(qe, ke, ve, 128 ** -0.5, nsplit=3, **args)
+        assert o1.numel() == o2.numel() == 0 and l1.numel() == l2.numel() == 0
+    torch.cuda.synchronize()
+    assert _lib.device_error(cuda) == 0
+
+
 def test_no_alloc_rejects_oversize_scratch(cuda):
     """64 splits of 6 rows x 4 tokens x 32 heads x 129 floats need 25 MB > the 16 MiB scratch: refused on the
     host, nothing launched."""
