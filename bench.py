@@ -101,11 +101,13 @@ class Clocks:
 
 # ------------------------------------------------------------------------------------------------ CPU oracle
 class CpuSample:
-    """The CPU oracle (oracle/model.py) timed on one request of the workload with as many decoder layers as fit a
-    time budget, extrapolated linearly to all layers. With fewer layers than the feature layers need, the last
-    sampled layer's normed output stands in for each feature layer (same shapes and trunk work)."""
+    """The CPU oracle (oracle/model.py: bit-exact with the reference's own decide_many on config 1 and the edge batch)
+    timed on one request of the workload at two depths, n_lo and n_hi decoder layers (layers past the first reuse
+    layer 0's weights: timing only). The slope between the two is the cost of one layer, the intercept the fixed cost
+    (embedding, trunk, readout); one request = intercept + all layers x slope. The decoder's feature layers are read
+    from the last sampled layer (same shapes and trunk work)."""
 
-    def __init__(self, config: int, budget_s: float, seed: int = 0):
+    def __init__(self, config: int, n_lo: int = 2, n_hi: int = 8, seed: int = 0):
         from oracle.model import OracleDecision
         from opendecider_b200 import synthetic as syn
         from opendecider_b200.backbone import synthetic_weights
@@ -113,41 +115,46 @@ class CpuSample:
         torch.set_num_threads(os.cpu_count() or 1)
         cfg, tk, qmin, _ = workload(config)
         self.cfg, self.n_layers_total = cfg, cfg.layers
+        self.n_lo, self.n_hi = min(n_lo, cfg.layers), min(n_hi, cfg.layers)
         self.reqs, tok = syn.decision_requests(config, seed=seed, n_requests=1)
         tc = TrunkConfig(d_feat=cfg.hidden, n_feat_layers=len(cfg.feature_layers), **tk)
         trunk = V3Trunk(tc, trunk_state_dict(tc, seed=0), "cpu")
         sd = synthetic_weights(cfg, seed=0, layers=1)
         self.feats = cfg.feature_layers
         cfg.feature_layers = ("final",) * len(self.feats)
-        mk = lambda n: OracleDecision(cfg, self._alias(sd, n), trunk, tok, TEMPS, TEMPERATURE, layers=n,
-                                      qcache_min_rows=qmin)
-        t1 = self._time(mk(1))                      # calibration with one layer
-        self.n = max(1, min(cfg.layers, int(budget_s / max(t1, 1e-3))))
-        self.od = mk(self.n)
+        self.od = OracleDecision(cfg, sd, trunk, tok, TEMPS, TEMPERATURE, layers=1, qcache_min_rows=qmin)
+        for table in (self.od.dec.q, self.od.dec.norm):   # layers 1..n_hi-1 alias layer 0's quantised weights
+            table.update(self._alias(table, self.n_hi))   # (runs its first n layers when od.dec.n = n)
+        self._time(self.n_lo)                         # warm-up: allocator, thread pool, kernel selection
 
     @staticmethod
     def _alias(sd, n):
         """Layers 1..n-1 reuse layer 0's weights (timing only: the sample is not checked for parity)."""
         out = dict(sd)
         for k, v in sd.items():
-            if k.startswith("layers.0."):
+            if k.startswith("layers.0"):
                 for i in range(1, n):
                     out[k.replace("layers.0.", f"layers.{i}.", 1)] = v
         return out
 
-    def _time(self, od) -> float:
+    def _time(self, n: int) -> float:
+        self.od.dec.n = n
         t0 = time.perf_counter()
-        od.decide(self.reqs)
+        self.od.decide(self.reqs)
         return time.perf_counter() - t0
 
     def step(self):
-        """One timed sample. Returns (decisions/s extrapolated, threads, description)."""
-        t = self._time(self.od)
+        """One timed sample. Returns (decisions/s of the whole-depth request, threads, description)."""
+        t_lo, t_hi = self._time(self.n_lo), self._time(self.n_hi)
+        per_layer = max(0.0, (t_hi - t_lo) / max(1, self.n_hi - self.n_lo))
+        fixed = max(0.0, t_lo - self.n_lo * per_layer)
+        t_req = fixed + self.n_layers_total * per_layer
         nd = sum(len(r.questions) for r in self.reqs)
-        per_request = t * self.n_layers_total / self.n
-        desc = (f"oracle/model.py (PyTorch CPU, bf16 + int8 _int_mm) on 1 request ({nd} decisions): {self.n} of "
-                f"{self.n_layers_total} decoder layers timed ({t:.1f} s), extrapolated linearly to all layers")
-        return nd / per_request, torch.get_num_threads(), desc
+        desc = (f"oracle/model.py (PyTorch CPU: int8 _int_mm projections, torch's CPU attention) on 1 request "
+                f"({nd} decisions) timed at {self.n_lo} and {self.n_hi} of {self.n_layers_total} decoder layers "
+                f"({t_lo:.1f} s, {t_hi:.1f} s): {per_layer:.2f} s per layer + {fixed:.2f} s fixed, extrapolated to "
+                f"all layers ({t_req:.1f} s per request)")
+        return nd / t_req, torch.get_num_threads(), desc
 
 
 class CpuSampleCached:
@@ -213,7 +220,7 @@ class CpuSampleCached:
 def cpu_oracle_sample(config: int, budget_s: float):
     if config == 5:
         return CpuSampleCached(budget_s).step()
-    return CpuSample(config, budget_s).step()
+    return CpuSample(config).step()
 
 
 def run_reference(args, rank: int) -> None:
@@ -222,7 +229,7 @@ def run_reference(args, rank: int) -> None:
         return
     cfg, _, _, desc = workload(args.config)
     per_step = max(3.0, 120.0 / max(1, args.steps + args.warmup))
-    cs = CpuSampleCached(per_step) if args.config == 5 else CpuSample(args.config, per_step)
+    cs = CpuSampleCached(per_step) if args.config == 5 else CpuSample(args.config)
     vals = []
     for i in range(args.warmup + args.steps):
         v, cores, sample = cs.step()

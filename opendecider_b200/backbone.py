@@ -61,13 +61,14 @@ class DecoderConfig:
     @classmethod
     def tiny(cls, **kw) -> "DecoderConfig":
         """4 layers, hidden 256, 4 q / 2 kv heads, head_dim 64, SwiGLU 688, vocab 1024."""
-        return cls(vocab=1024, hidden=256, layers=4, heads=4, kv_heads=2, head_dim=64, ffn=688, max_pos=4096, **kw)
+        return cls(**{**dict(vocab=1024, hidden=256, layers=4, heads=4, kv_heads=2, head_dim=64, ffn=688,
+                             max_pos=4096), **kw})
 
     @classmethod
     def nine_b(cls, **kw) -> "DecoderConfig":
         """BASELINE configs 4/5: 36 layers, hidden 4096, 32 q / 8 kv heads, head_dim 128, SwiGLU 12288, vocab 151936."""
-        return cls(vocab=151936, hidden=4096, layers=36, heads=32, kv_heads=8, head_dim=128, ffn=12288,
-                   max_pos=32768, **kw)
+        return cls(**{**dict(vocab=151936, hidden=4096, layers=36, heads=32, kv_heads=8, head_dim=128, ffn=12288,
+                             max_pos=32768), **kw})
 
 
 def hf_weight_names(cfg: DecoderConfig) -> list[tuple[str, tuple]]:

@@ -133,14 +133,32 @@ def sdpa_flash(q, k, v, ok):
     return o.transpose(1, 2).reshape(R, t, Hq * D)
 
 
-def causal_attend(pad):
+def causal_attend(pad, sdpa=None):
     """Causal attention of the state pass with left padding (keys before pad[r] masked)."""
     def f(i, q, k, v):
         t = q.shape[1]
         j = torch.arange(t)
         ok = (j[None, :] <= j[:, None])[None] & (j[None, None, :] >= pad.view(-1, 1, 1))
-        return sdpa_flash(q, k, v, ok)
+        return (sdpa or sdpa_flash)(q, k, v, ok)
     return f
+
+
+def sdpa_exp_variant(q, k, v, ok):
+    """sdpa_flash with ONE change, for measuring how sensitive a decision is to the last bit of attention: torch.exp
+    in place of the CPU flash kernel's own vectorised exponential and a division in place of its reciprocal
+    multiply. Scores, masks, the bf16 rounding of the probabilities and the fp32 accumulation are unchanged; about 9 %
+    of the bf16 outputs move by one ulp. Any attention not bit-identical to torch's CPU kernel (a tensor-core kernel
+    with its own exponential and summation order) differs from the reference by perturbations of this size."""
+    R, t, Hq, D = q.shape
+    g = Hq // k.shape[2]
+    ok = ok | ~ok.any(-1, keepdim=True)
+    qf = q.float().transpose(1, 2)
+    kf = k.float().repeat_interleave(g, 2).transpose(1, 2)
+    vf = v.float().repeat_interleave(g, 2).transpose(1, 2)
+    s = ((qf @ kf.transpose(-1, -2)) * D ** -0.5).masked_fill(~ok[:, None], float("-inf"))
+    p = torch.exp(s - s.amax(-1, keepdim=True))
+    o = (p.to(BF).float() @ vf) / p.sum(-1, keepdim=True)
+    return o.transpose(1, 2).reshape(R, t, Hq * D).to(BF)
 
 
 BATCHED_BYTES = 1 << 30     # prefix_attn.py:27: the one-call multi-state path's bound on gathered prefix K/V
@@ -170,11 +188,12 @@ class OracleDecision:
 
     def __init__(self, cfg, sd, trunk, tok, temps: dict, temperature: float, layers: int | None = None,
                  list_cap: int = 16, qcache_min_rows: int = 12, none_text: str = "none of the above",
-                 branch_chunk: int = 64):
+                 branch_chunk: int = 64, sdpa=None):
         self.dec = OracleDecoder(cfg, sd, layers)
         self.cfg, self.trunk, self.tok, self.temps, self.temperature = cfg, trunk, tok, temps, temperature
         self.list_cap, self.qcache_min_rows, self.none_text = list_cap, qcache_min_rows, none_text
         self.branch_chunk = branch_chunk                  # v3_branch_chunk (models.py:66)
+        self.sdpa = sdpa or sdpa_flash                    # sdpa_exp_variant: the sensitivity probe
 
     def state_pass(self, states):
         from opendecider_b200.batching import state_text
@@ -184,7 +203,7 @@ class OracleDecision:
         ids = torch.tensor([[0] * (T - n) + list(s) for s, n in zip(seqs, lens)])
         pad = torch.tensor([T - n for n in lens])
         pos = torch.arange(T).expand(S, T)
-        _, kv = self.dec.run(ids, pos, causal_attend(pad))
+        _, kv = self.dec.run(ids, pos, causal_attend(pad, self.sdpa))
         cache = []
         for k, v in kv:                                   # Int8Tensor.quantize then materialize(): bf16 prefix
             kq, ks, _ = ops.quantize_rows(k.transpose(1, 2).float().numpy(), "bf16")
@@ -215,7 +234,7 @@ class OracleDecision:
 
         def attend(i, q, k, v):
             Kp, Vp = cache[i]                                             # (S, Hkv, T, D) materialised
-            return sdpa_flash(q, torch.cat([Kp.transpose(1, 2), k], 1), torch.cat([Vp.transpose(1, 2), v], 1), ok)
+            return self.sdpa(q, torch.cat([Kp.transpose(1, 2), k], 1), torch.cat([Vp.transpose(1, 2), v], 1), ok)
 
         _, kv = self.dec.run(ids, pos, attend)
         new, snaps, packs = [], [], []
@@ -276,7 +295,7 @@ class OracleDecision:
             Kp, Vp = cache[i]                                             # (S, Hkv, T, D) materialised
             if batched_q:
                 ok = torch.cat([pm_state[sidx][:, None, :].expand(N, Lq, T), causal(Lq)[None].expand(N, Lq, Lq)], 2)
-                return sdpa_flash(q, torch.cat([Kp[sidx].transpose(1, 2), k], 1),
+                return self.sdpa(q, torch.cat([Kp[sidx].transpose(1, 2), k], 1),
                                   torch.cat([Vp[sidx].transpose(1, 2), v], 1), ok)
             out = torch.empty(N, Lq, q.shape[2] * D, dtype=BF)
             for st in sorted(set(sidx.tolist())):
@@ -312,7 +331,7 @@ class OracleDecision:
                     t = q.shape[1]
                     ok = torch.cat([pmq[qr][:, None, :].expand(len(qr), t, T + Lq),
                                     causal(t)[None].expand(len(qr), t, t)], 2)
-                    return sdpa_flash(q, torch.cat([Kc[qr], k], 1), torch.cat([Vc[qr], v], 1), ok)
+                    return self.sdpa(q, torch.cat([Kc[qr], k], 1), torch.cat([Vc[qr], v], 1), ok)
                 qj = int(qr[0])
                 return split_rows(q, k, v, Kc[qj].transpose(0, 1), Vc[qj].transpose(0, 1), pmq[qj])
 

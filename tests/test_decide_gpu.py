@@ -138,13 +138,19 @@ def test_fused_kv_write_same_decisions(cuda):
 def test_edge_cases_match_reference(cuda):
     """Ragged states (7, 300 and 45 tokens: a left-padded state pass), a question at the 255-option cap (no `none`
     column), a two-option choice, a yes/no question and a three-option choice, against the reference's own
-    decide_many on the same batch (tests/golden/edge_cases.npz): probabilities and P(none) within 3e-3. That bound,
-    not 1e-3, is the reference's own: decided with torch's math SDPA backend instead of its flash one, the reference
-    moves yes/no and choice probabilities of this tiny random-init model by up to 2.7e-3 (measured on CPU), and the
-    B200 path is within 1.5e-3 here. A request without questions answers {}, an empty batch []."""
+    decide_many on the same batch (tests/golden/edge_cases.npz). A request without questions answers {}, an empty
+    batch [].
+
+    Bound per question: 1e-3 absolute, or 1.5 x the move that the reference's own arithmetic makes when only the
+    exponential inside its attention is swapped (the CPU oracle, bit-exact with the reference, run with
+    oracle.model.sdpa_exp_variant), whichever is larger. Questions whose answer stays within 6.7e-4 under that swap
+    are held to 1e-3; the two-option questions near p = 0.5 move by up to 2.3e-3 under it, and no attention that is
+    not bit-identical to torch's CPU kernel can be held closer than that."""
     import sys
     sys.path.insert(0, "tests/golden")
     from make_golden_edge import NAMES, edge_requests
+    from oracle.model import OracleDecision, sdpa_exp_variant
+    from opendecider_b200.backbone import synthetic_weights
     g = np.load("tests/golden/edge_cases.npz")
     dec, _ = make_decider(cuda, True)
     reqs = edge_requests() + [syn.Request("t20 t21", [])]
@@ -152,8 +158,23 @@ def test_edge_cases_match_reference(cuda):
     assert dec.decide_many([]) == [] and ans[3] == {}
     got = {**ans[0], **ans[1], **ans[2]}
     assert "none" not in got["big"]                              # 255 options: no none option
-    for name in NAMES:
+    cfg = DecoderConfig.tiny(feature_layers=FEATURE_LAYERS)
+    tc = TrunkConfig(d_feat=cfg.hidden, n_feat_layers=len(FEATURE_LAYERS), **TRUNK)
+    od = OracleDecision(cfg, synthetic_weights(cfg, seed=0), V3Trunk(tc, trunk_state_dict(tc, seed=0), "cpu"),
+                        syn.SyntheticTokenizer(cfg.vocab), TEMPS, 1.419344425201416, qcache_min_rows=32,
+                        sdpa=sdpa_exp_variant)
+    _, ren_x, pn_x, _ = od.decide(edge_requests())
+    held = []
+    for i, name in enumerate(NAMES):
+        ref = g[f"{name}.probs"]
+        sens = float(np.abs(ren_x[i, : ref.size] - ref).max())
+        if not np.isnan(g[f"{name}.none"]):
+            sens = max(sens, abs(float(pn_x[i]) - float(g[f"{name}.none"])))
+        bound = max(1e-3, 1.5 * sens)
+        if bound == 1e-3:
+            held.append(name)
         pl = np.array(got[name]["probs_list"])
-        assert np.abs(pl - g[f"{name}.probs"]).max() < 3e-3, (name, np.abs(pl - g[f"{name}.probs"]).max())
+        assert np.abs(pl - ref).max() < bound, (name, np.abs(pl - ref).max(), bound)
         if "none" in got[name]:
-            assert abs(got[name]["none"] - float(g[f"{name}.none"])) < 3e-3, name
+            assert abs(got[name]["none"] - float(g[f"{name}.none"])) < bound, name
+    assert {"big", "two", "small"} <= set(held), held            # held to 1e-3: all but the yes/no question

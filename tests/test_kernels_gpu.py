@@ -740,3 +740,35 @@ def test_bounded_wait_reports_and_context_survives(cuda):
     q, s = _lib.quant_rows(x, scale_dtype=torch.float32)
     qo, _, so = ops.quantize_rows(x.cpu().float().numpy(), "f32")
     assert np.array_equal(q.cpu().numpy(), qo)
+
+
+@pytest.mark.parametrize("prefix", ["int8", "bf16"])
+def test_prefix_attn_config3_full_shape(cuda, prefix):
+    """BASELINE config 3 at its full per-request shape on 2 requests: a 4096-token int8 state (fp16 scales), 64
+    option rows x 16 tokens, 32 / 8 heads, D 128, rows grouped 4 per CTA and the state prefix split as
+    od_prefix_attn_plan chooses - against the oracle's _split_attention (prefix_attn.py:58-76, fp32). The prefix is
+    read as int8 (dequantised in the kernel) or as the materialised bf16 cache. Tolerance: 2e-2 absolute, the
+    reference's own GPU test bound for bf16 P.V; 5e-3 relative in norm."""
+    S, T, rows, t, Hq, Hkv, D = 2, 4096, 64, 16, 32, 8, 128
+    ac = syn.attn_case(S=S, T=T, rows=rows, t=t, Hq=Hq, Hkv=Hkv, D=D, seed=31)
+    Kq, Vq, ks, vs = _attn_inputs(cuda, ac)
+    Kp = ops.materialize_int8(ac.Kq, ac.ks)                       # (S, Hkv, T, D) bf16, as materialize() gives it
+    Vp = ops.materialize_int8(ac.Vq, ac.vs)
+    if prefix == "int8":
+        kw = dict(Kp=Kq, Vp=Vq, ksc=ks, vsc=vs)
+    else:
+        kw = dict(Kp=Kp.to(cuda), Vp=Vp.to(cuda))
+    per = 4                                                       # 4 rows x 16 tokens x 4 heads = 256 slots
+    groups = torch.tensor([(a, per) for a in range(0, S * rows, per)], dtype=torch.int32, device=cuda)
+    o = _lib.prefix_attn(ac.q.to(cuda), ac.k.to(cuda), ac.v.to(cuda), D ** -0.5, row_state=ac.row_state.to(cuda),
+                         row_groups=groups, max_group_rows=per, **kw).cpu().float()
+    torch.cuda.synchronize()
+    assert _lib.device_error(cuda) == 0
+    for s in range(S):
+        for a in range(s * rows, (s + 1) * rows, 16):             # 16 rows at a time bound the CPU score tensor
+            r = slice(a, a + 16)
+            ref = ops.split_attention(ac.q[r].transpose(1, 2), ac.k[r].transpose(1, 2), ac.v[r].transpose(1, 2),
+                                      Kp[s], Vp[s], None, D ** -0.5).transpose(1, 2)
+            got = o[r]
+            assert (got - ref).abs().max() < 2e-2, (s, a)
+            assert (got - ref).norm() / ref.norm() < 5e-3, (s, a)

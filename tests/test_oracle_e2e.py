@@ -54,24 +54,17 @@ def test_oracle_lm_feature_matches_reference():
     assert np.abs(logits.numpy() - g["lmq.logits"]).max() < 1e-5
 
 
-def _edge_oracle(attn=None):
+def _edge_oracle(sdpa=None):
     import sys
     sys.path.insert(0, "tests/golden")
-    import oracle.model as om
     from make_golden_edge import NAMES, edge_requests
     cfg = DecoderConfig.tiny(feature_layers=FEATURE_LAYERS)
     tc = TrunkConfig(d_feat=cfg.hidden, n_feat_layers=len(FEATURE_LAYERS), **TRUNK)
     trunk = V3Trunk(tc, trunk_state_dict(tc, seed=0), "cpu")
     tok = syn.SyntheticTokenizer(cfg.vocab)
     od = OracleDecision(cfg, synthetic_weights(cfg, seed=0), trunk, tok, TEMPS, 1.419344425201416,
-                        qcache_min_rows=32)
-    keep = om.sdpa_flash
-    if attn is not None:
-        om.sdpa_flash = attn
-    try:
-        _, ren, pn, _ = od.decide(edge_requests())
-    finally:
-        om.sdpa_flash = keep
+                        qcache_min_rows=32, sdpa=sdpa)
+    _, ren, pn, _ = od.decide(edge_requests())
     g = np.load("tests/golden/edge_cases.npz")
     return {name: float(np.abs(ren[i, : g[f"{name}.probs"].size] - g[f"{name}.probs"]).max())
             for i, name in enumerate(NAMES)}
@@ -85,24 +78,11 @@ def test_oracle_edge_cases_match_reference():
 
 
 def test_edge_yes_no_is_sensitive_to_the_last_bit_of_attention():
-    """The oracle with one change inside its attention calls (torch.exp for the CPU kernel's exponential, a
-    division for its reciprocal multiply; scores, masks and the bf16 rounding of the probabilities unchanged) moves
-    the yes/no question of the edge batch by more than 1e-3 from the reference - so 1e-3 on that question demands
-    an attention bit-identical to torch's CPU kernel - while the 255-option question stays within 1e-4."""
-    import torch
-
-    def attn(q, k, v, ok):
-        R, t, Hq, D = q.shape
-        g = Hq // k.shape[2]
-        ok = ok | ~ok.any(-1, keepdim=True)
-        qf = q.float().transpose(1, 2)
-        kf = k.float().repeat_interleave(g, 2).transpose(1, 2)
-        vf = v.float().repeat_interleave(g, 2).transpose(1, 2)
-        s = ((qf @ kf.transpose(-1, -2)) * D ** -0.5).masked_fill(~ok[:, None], float("-inf"))
-        p = torch.exp(s - s.amax(-1, keepdim=True))
-        o = (p.to(torch.bfloat16).float() @ vf) / p.sum(-1, keepdim=True)
-        return o.transpose(1, 2).reshape(R, t, Hq * D).to(torch.bfloat16)
-
-    d = _edge_oracle(attn)
+    """The oracle with one change inside its attention calls (oracle.model.sdpa_exp_variant: torch.exp for the CPU
+    kernel's exponential, a division for its reciprocal multiply) moves the yes/no question of the edge batch by
+    more than 1e-3 from the reference - so 1e-3 on that question demands an attention bit-identical to torch's CPU
+    kernel - while the 255-option question stays within 1e-4."""
+    from oracle.model import sdpa_exp_variant
+    d = _edge_oracle(sdpa_exp_variant)
     assert d["yn"] > 1e-3, d
     assert d["big"] < 1e-4, d
