@@ -466,6 +466,7 @@ def main():
     from opendecider_b200 import synthetic as syn
     from opendecider_b200.backbone import Backbone
     from opendecider_b200.decider import Decider
+    from opendecider_b200.distributed import DistributedDecider
     from opendecider_b200.v3 import TrunkConfig, V3Model, V3Trunk, trunk_state_dict
 
     torch.cuda.set_device(local)
@@ -477,16 +478,21 @@ def main():
     torch.cuda.empty_cache()
     tc = TrunkConfig(d_feat=cfg.hidden, n_feat_layers=len(cfg.feature_layers), lm_feature=args.lm_feature, **tk)
     trunk = V3Trunk(tc, trunk_state_dict(tc, seed=0), dev)
-    # per GPU: config 4's 64 requests; config 5's 512 requests are the 8-GPU batch, 64 per GPU (weak scaling)
-    reqs, tok = syn.decision_requests(args.config, seed=rank, n_requests=64 if args.config == 5 else None)
+    # ONE global batch of 64 requests per GPU (weak scaling; config 5's 512 requests are the 8-GPU batch), the same on
+    # every rank; each rank decides its contiguous token-balanced block (distributed.shard) and every rank gets every
+    # request's probabilities back through one all_gather per step (DistributedDecider)
+    reqs_all, tok = syn.decision_requests(args.config, seed=0, n_requests=64 * world)
     decider = Decider(V3Model(bb, trunk, tok, qcache_min_rows=qmin), TEMPERATURE, TEMPS)
+    dd = DistributedDecider(decider) if world > 1 else None
+    blocks = dd.blocks(reqs_all) if dd else [(0, len(reqs_all))]
+    shapes = dd.layouts(reqs_all, blocks) if dd else None
+    a_blk, b_blk = blocks[rank]
+    reqs = reqs_all[a_blk:b_blk]
 
     def gather(probs):
-        if world > 1:
-            p = probs[0]
-            out = torch.empty(world * p.shape[0], p.shape[1], dtype=p.dtype, device=dev)
-            dist.all_gather_into_tensor(out, p.contiguous())
-            return out
+        """Every rank's [probs | renorm | P(none)] block, one NCCL all_gather_into_tensor, no host sync."""
+        if dd is not None:
+            return dd.gather(dd.pack(*probs), shapes)
         return probs[0]
 
     def barrier():
@@ -505,12 +511,13 @@ def main():
     if args.config == 5:
         # the cached states are the workload's input (built once, untimed, with room for the appended tokens);
         # every step appends the records and decides (execute() first truncates back to the encoded length)
-        appends = [r.append for r in reqs]
+        appends_all = [r.append for r in reqs_all]
+        appends = appends_all[a_blk:b_blk]
         n_app = len(tok([appends[0]], add_special_tokens=False)["input_ids"][0])
         cache = decider.encode_states([r.state for r in reqs], room=n_app)
         torch.cuda.synchronize()
         plan = decider.plan(reqs, cache=cache, appends=appends)
-        items = lambda k: ((reqs, appends) for _ in range(k))
+        items = lambda k: ((reqs_all, appends_all) for _ in range(k))
     else:
         plan = decider.plan(reqs)
     n_dec_local = len(plan["questions"])
@@ -543,7 +550,8 @@ def main():
     gemm_ops = sum(o for _, _, o, _ in probe)
     gemm_bytes = sum(b for _, _, _, b in probe)
     gemm_launches = len(probe) // max(1, args.steps)
-    decisions = n_dec_local * world * args.steps
+    n_dec_total = sum(h for h, _ in shapes) if dd else n_dec_local
+    decisions = n_dec_total * args.steps
     value = decisions / t_dev
 
     if args.breakdown and rank == 0:
@@ -563,9 +571,17 @@ def main():
 
     # ---- e2e: the public API, one batch per step (Decider.decide_stream: tokenise + plan on the host, one pinned
     # H2D copy, kernels, the gather, one D2H read of the results, answers), batch b+1 planned while b runs
-    g_fn = gather if world > 1 else None
-    stream_in = items if items is not None else (lambda k: (reqs for _ in range(k)))
-    for _ in decider.decide_stream(stream_in(1), gather=g_fn, cache=cache if items is not None else None):
+    # with N ranks: DistributedDecider.decide_stream (each rank plans and runs its block, one all_gather, and every
+    # rank builds every request's answers)
+    stream_in = items if items is not None else (lambda k: (reqs_all for _ in range(k)))
+    cache_in = cache if items is not None else None
+
+    def stream(k):
+        if dd is not None:
+            return dd.decide_stream(stream_in(k), cache=cache_in)
+        return (ans for ans, _ in decider.decide_stream(stream_in(k), cache=cache_in))
+
+    for _ in stream(1):
         pass
     torch.cuda.synchronize()
     barrier()
@@ -573,9 +589,8 @@ def main():
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     f0.record()
     n_ans = 0
-    for ans, _ in decider.decide_stream(stream_in(args.steps), gather=g_fn,
-                                        cache=cache if items is not None else None):
-        assert len(ans) == len(reqs)
+    for ans in stream(args.steps):
+        assert len(ans) == len(reqs_all)
         n_ans += 1
     f1.record()
     torch.cuda.synchronize()
@@ -612,8 +627,11 @@ def main():
         "warmup": args.warmup, "ms_per_step": 1e3 * t_dev / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded random-id states, random-init weights)",
         "config": {"workload": desc + (" + LM log-prob feature" if args.lm_feature else ""),
-                   "global_batch": n_dec_local * world, "requests_per_gpu": len(reqs),
-                   "state_tokens": plan["state"]["T"], "parallelism": f"dp{world} (requests sharded, NCCL gather)",
+                   "global_batch": n_dec_total, "requests": len(reqs_all), "requests_per_gpu": len(reqs),
+                   "state_tokens": plan["state"]["T"],
+                   "parallelism": f"dp{world}: one global batch of {len(reqs_all)} requests in contiguous "
+                                  "token-balanced blocks per GPU, replicated weights, one NCCL all_gather of the "
+                                  "probabilities per step",
                    "l2": f"inputs larger than L2 (7.6 GB of int8 weights and a {kv_gb:.1f} GB int8 KV cache stream "
                          "every step)"},
         "e2e": {"value": decisions / t_e2e, "unit": "decisions/s", "h2d_bytes_per_step": h2d,

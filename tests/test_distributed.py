@@ -123,6 +123,15 @@ def _stub_decider():
                 p_none[i] = probs[i, K] if hasattr(q, "none_col") else 0.0
             return (probs, renorm, p_none), None
 
+        def decide_stream(self, batches, gather=None, cache=None):
+            # Decider.decide_stream's contract without CUDA events or pinned buffers: gather() right after a
+            # batch's device work, before the next batch is planned
+            for item in batches:
+                plan = self.plan(item)
+                probs, _ = self.execute(plan)
+                g = gather(probs) if gather is not None else None
+                yield self.answers(plan, probs), g
+
     return StubDecider()
 
 
@@ -145,8 +154,11 @@ def _decider_worker(rank, world, port, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        got = DistributedDecider(_stub_decider()).decide_many(_requests())
-        q.put((rank, got))
+        dd = DistributedDecider(_stub_decider())
+        reqs = _requests()
+        got = dd.decide_many(reqs)
+        streamed = list(dd.decide_stream([reqs[:-1], reqs[2:6], reqs[:-1]]))
+        q.put((rank, (got, streamed)))
     finally:
         dist.destroy_process_group()
 
@@ -154,7 +166,8 @@ def _decider_worker(rank, world, port, q):
 def test_distributed_decider_equals_single_rank():
     """DistributedDecider.decide_many on two gloo ranks answers every request exactly as one rank's decide_many:
     same values, probabilities and P(none), in request order, on both ranks - including the question whose P(none)
-    beats the raw option maximum but not the renormalised one (value 'none')."""
+    beats the raw option maximum but not the renormalised one (value 'none'). decide_stream over three batches of
+    different sizes answers each as decide_many does."""
     want = _stub_decider().decide_many(_requests())
     assert want[3]["a"]["value"] == "none" and want[-1] == {}
     ctx = mp.get_context("spawn")
@@ -166,4 +179,9 @@ def test_distributed_decider_equals_single_rank():
     res = dict(q.get(timeout=120) for _ in procs)
     for p in procs:
         p.join(timeout=60)
-    assert res[0] == want and res[1] == want
+    single = _stub_decider()
+    want_stream = [single.decide_many(b) for b in ([*_requests()[:-1]], _requests()[2:6], [*_requests()[:-1]])]
+    for r in (0, 1):
+        got, streamed = res[r]
+        assert got == want
+        assert streamed == want_stream             # the pipelined form: every batch, in order, on every rank
