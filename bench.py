@@ -394,6 +394,65 @@ def op_attn_state(args):
                           "frac_bf16": flops / tm / 1e12 / peaks.get("bf16_tflops", 1590.0), "gbs": byts / tm / 1e9}))
 
 
+def op_rows(args):
+    """The bandwidth-bound row kernels of a decoder layer at the 9B widths (hidden 4096, 32 / 8 heads, D 128, SwiGLU
+    12288) over M tokens (default 131072, one state-pass chunk): GB/s of each kernel's algorithmic bytes (every input
+    read once, every output written once; the RoPE tables and norm weights stay in L2 and are not counted) and the
+    fraction of the measured HBM copy rate. Inputs are larger than L2 (126 MB), so every launch streams from HBM."""
+    from opendecider_b200 import _lib
+    from opendecider_b200.rope import rope_tables
+    dev = torch.device("cuda", 0)
+    hbm = _peaks().get("hbm_gbs", 6650.0)
+    M = int(args.shapes or 131072)
+    H, Hq, Hkv, D, F = 4096, 32, 8, 128, 12288
+    W = Hq * D
+    g = torch.Generator(device=dev).manual_seed(0)
+    bf = lambda *shape: torch.randn(*shape, generator=g, device=dev).to(torch.bfloat16)
+    x, res, w = bf(M, H), bf(M, H), bf(H) * 0.1
+    hm = bf(M, F)
+    qkv = bf(M, 2 * W + 2 * Hkv * D)
+    o = bf(M, W)
+    cos, sin = rope_tables(D, 1e6, 32768, torch.bfloat16, dev)
+    pos = torch.randint(0, 4096, (M,), generator=g, device=dev, dtype=torch.int32)
+    qn, kn = bf(D) * 0.1, bf(D) * 0.1
+    S, t = M // 2048, 2048
+    kq = torch.empty(S, Hkv, t, D, dtype=torch.int8, device=dev)
+    vq = torch.empty_like(kq)
+    ksc = torch.empty(S, Hkv, t, dtype=torch.bfloat16, device=dev)
+    vsc = torch.empty_like(ksc)
+    kb = torch.empty(S, Hkv, t, D, dtype=torch.bfloat16, device=dev)
+    vb = torch.empty_like(kb)
+    kk, vv = bf(S, t, Hkv, D), bf(S, t, Hkv, D)
+    res_out = torch.empty_like(res)
+    cases = [
+        ("rmsnorm_res_quant", lambda: _lib.rmsnorm_res_quant(x, w, 1e-6, res_in=res, res_out=res_out),
+         M * (7 * H + 4)),
+        ("quant_rows", lambda: _lib.quant_rows(hm, scale_dtype=torch.float32), M * (3 * F + 4)),
+        ("gate_quant", lambda: _lib.gate_quant(o, qkv, Hq, D), M * (5 * W + 4)),
+        ("qk_norm_rope", lambda: _lib.qk_norm_rope(qkv, pos, cos, sin, qn, kn, 1e-6, Hq, Hkv, D),
+         M * (4 * (W + 2 * Hkv * D) + 4)),
+        ("kv_append", lambda: _lib.kv_append(kk, vv, kq, vq, ksc, vsc, t0=0, kb=kb, vb=vb),
+         M * Hkv * (2 * D * 2 + 2 * D + 2 * 2 + 2 * D * 2)),
+    ]
+    only = set(args.kernels.split(",")) if args.kernels else None
+    for name, fn, byts in cases:
+        if only and name not in only:
+            continue
+        ts = []
+        for i in range(args.warmup + args.steps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize()
+            if i >= args.warmup:
+                ts.append(a.elapsed_time(b))
+        assert _lib.device_error(dev) == 0, "a kernel reported a device-side error"
+        tm = statistics.median(ts) / 1e3
+        print(json.dumps({"op": name, "tokens": M, "ms": tm * 1e3, "bytes": byts, "gbs": byts / tm / 1e9,
+                          "frac_hbm": byts / tm / 1e9 / hbm}))
+
+
 def op_lm_logprob(args):
     """The LM-head log-prob feature's kernel (od_lm_logprob) at the 9B head: M option tokens x V = 151936 vocabulary
     rows x H = 4096 (default M = 16384). TFLOP/s of the 2 M V H GEMM FLOPs (the log-sum-exp rides in the epilogue)."""
@@ -437,12 +496,13 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--lm-feature", action="store_true",
                     help="the trunk's LM log-prob feature on (v3_lm_feature, as in the shipped 9B checkpoint)")
-    ap.add_argument("--op", default="decide", choices=["decide", "gemm", "attn", "attn_state", "lm_logprob"],
+    ap.add_argument("--op", default="decide", choices=["decide", "gemm", "attn", "attn_state", "lm_logprob", "rows"],
                     help="decide: the headline decision throughput; gemm / attn: operator configs 2 / 3; "
                          "attn_state: the state pass's causal attention")
     ap.add_argument("--shapes", default="", help="--op gemm: MxNxK list; --op attn: requestsxrowsxt list; "
                                                  "--op attn_state: rowsxtokens list")
     ap.add_argument("--requests", type=int, default=0, help="--op attn: requests (default 32)")
+    ap.add_argument("--kernels", default="", help="--op rows: comma-separated subset of the row kernels")
     ap.add_argument("--breakdown", action="store_true", help="print per-kernel device time of one step to stderr")
     args = ap.parse_args()
     if args.op == "gemm":
@@ -453,6 +513,8 @@ def main():
         return op_attn_state(args)
     if args.op == "lm_logprob":
         return op_lm_logprob(args)
+    if args.op == "rows":
+        return op_rows(args)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))

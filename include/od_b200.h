@@ -111,12 +111,18 @@ OD_API int od_rmsnorm_res_quant(const void* x, const void* res_in, void* res_out
  *                         (Qwen3_5MLP.forward: act_fn(gate_proj(x)) * up_proj(x)), Y (M, N/2) bf16
  * epilogue OD_EPI_INT32:  Y[m, n] = acc (int32) - the bit-exact parity mode
  * A (M, K) int8 row-major, sa (M) fp32 (per-token activation scales), W (N, K) int8 row-major (Int8Linear.qweight),
- * sw (N) bf16 (Int8Linear.scale). K % 128 == 0, N % 256 == 0 (OD_EPI_SWIGLU: N % 256 == 0), M >= 1 (any).
+ * sw (N) bf16 (Int8Linear.scale). K % 128 == 0, N % 32 == 0 (OD_EPI_SWIGLU: N % 256 == 0), M >= 0 (any).
  * A, W 16-byte aligned. Replaces GemLite A8W8 (quant.py:302-314) and the dequant+cuBLAS path (quant.py:149-157).
  */
 enum { OD_EPI_BF16 = 0, OD_EPI_SWIGLU = 1, OD_EPI_INT32 = 2 };
 OD_API int od_gemm_w8a8(const int8_t* A, const float* sa, const int8_t* W, const void* sw, void* Y,
                  int64_t M, int64_t N, int64_t K, int epilogue, void* stream);
+/* od_gemm_w8a8 writing rows of Y ldy elements apart (ldy >= the output width, a multiple of one 16-byte store),
+ * so several projections of one layer can fill column ranges of one stacked output: the SmoothQuant path's separate
+ * q / k / v GEMMs (each input smoothed by its own vector, SmoothedLinear quant.py:317-329) write the same fused
+ * (M, Hq*2D + 2*Hkv*D) layout the single stacked GEMM writes. */
+OD_API int od_gemm_w8a8_ld(const int8_t* A, const float* sa, const int8_t* W, const void* sw, void* Y,
+                    int64_t M, int64_t N, int64_t K, int epilogue, int64_t ldy, void* stream);
 
 /* ---------------------------------------------------------------------------------------------------------------
  * Embedding lookup of an int8 table, Int8Embedding.forward (quant.py:199-200):
@@ -148,10 +154,19 @@ OD_API int od_qk_norm_rope_kv_i8(const void* qkv, const int32_t* pos, const void
                           void* vsc, void* kb, void* vb, int64_t T_cap, int64_t t0, void* stream);
 
 /* Output gate + per-token quantisation of the o_proj input (Qwen3_5Attention.forward :666-668):
- *     g = bf16(o * bf16(sigmoid(gate))),  then q, s = quantise(g) (fp32 scales)
- * o (M, Hq*D) bf16; gate read from qkv (M, ldqkv) at column h*2D + D + d for head h. */
+ *     g = bf16(o * bf16(sigmoid(gate))),  g' = inv_s ? bf16(g * inv_s) : g,  then q, s = quantise(g') (fp32 scales)
+ * o (M, Hq*D) bf16; gate read from qkv (M, ldqkv) at column h*2D + D + d for head h; inv_s (Hq*D) bf16 or NULL
+ * (the o_proj SmoothedLinear multiply, quant.py:328-329). */
 OD_API int od_gate_quant(const void* o, const void* qkv, int64_t ldqkv, int64_t M, int Hq, int D,
-                  int8_t* q, float* s, void* stream);
+                  const void* inv_s, int8_t* q, float* s, void* stream);
+/* SwiGLU of separate gate / up projections + the down projection's input quantisation (Qwen3_5MLP.forward, with a
+ * SmoothedLinear on each of gate_proj, up_proj and down_proj, quant.py:317-350, whose vectors differ so gate and up
+ * cannot share the interleaved SwiGLU GEMM):
+ *     a = bf16(g / (1 + exp(-g))),  h = bf16(a * u),  h' = inv_s ? bf16(h * inv_s) : h,  q, s = quantise(h')
+ * g, u (M, F) bf16 (F % 8 == 0), inv_s (F) bf16 or NULL, q (M, F) int8, s (M) fp32. Same rounding points as the
+ * OD_EPI_SWIGLU epilogue. */
+OD_API int od_swiglu_quant(const void* g, const void* u, int64_t M, int64_t F, const void* inv_s, int8_t* q,
+                    float* s, void* stream);
 
 /* ---------------------------------------------------------------------------------------------------------------
  * A9/A10: branched shared-prefix attention (Hydragen split, prefix_attn.py:43-76, merged exactly by log-sum-exp).

@@ -46,13 +46,16 @@ SIGNATURES = {
     "od_rmsnorm_res_quant": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_int64, c_int, c_void_p,
                              c_void_p, c_void_p, c_void_p],
     "od_gemm_w8a8": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int, c_void_p],
+    "od_gemm_w8a8_ld": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int, c_int64,
+                        c_void_p],
     "od_embed_i8": [c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int, c_void_p, c_void_p],
     "od_qk_norm_rope": [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_float, c_int64, c_int,
                         c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p],
     "od_qk_norm_rope_kv_i8": [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_float, c_int64,
                               c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p,
                               c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p],
-    "od_gate_quant": [c_void_p, c_void_p, c_int64, c_int64, c_int, c_int, c_void_p, c_void_p, c_void_p],
+    "od_gate_quant": [c_void_p, c_void_p, c_int64, c_int64, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p],
+    "od_swiglu_quant": [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p],
     "od_prefix_attn": [c_void_p] * 20 + [AttnDims, c_void_p, c_int64, c_void_p],
     "od_prefix_attn_plan": [POINTER(AttnDims), c_int, POINTER(c_int), POINTER(c_int64)],
     "od_prefix_attn_noalloc": [c_void_p] * 20 + [AttnDims, c_void_p],
@@ -216,7 +219,8 @@ def rmsnorm_res_quant(x: torch.Tensor, w: torch.Tensor, eps: float, res_in: torc
 @_probed
 def gemm_w8a8(a: torch.Tensor, sa: torch.Tensor | None, w: torch.Tensor, sw: torch.Tensor | None,
               epilogue: int = OD_EPI_BF16, out: torch.Tensor | None = None) -> torch.Tensor:
-    """int8 (M, K) x int8 (N, K)^T on tcgen05: bf16 (M, N) / SwiGLU bf16 (M, N/2) / int32 (M, N)."""
+    """int8 (M, K) x int8 (N, K)^T on tcgen05: bf16 (M, N) / SwiGLU bf16 (M, N/2) / int32 (M, N). `out` may be a
+    column slice of a wider row-major buffer (its row stride is passed as the output leading dimension)."""
     dev = _need_cuda(a, w, sa, sw)
     M, K = a.shape
     N = w.shape[0]
@@ -231,8 +235,9 @@ def gemm_w8a8(a: torch.Tensor, sa: torch.Tensor | None, w: torch.Tensor, sw: tor
     if probe is not None:
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-    _check(load().od_gemm_w8a8(_p(a), _p(sa), _p(w), _p(sw), _p(out), M, N, K, epilogue, _stream(dev)),
-           "od_gemm_w8a8")
+    assert out.dim() == 2 and out.stride(1) == 1 and out.shape[0] == M, "out: (M, cols) with contiguous rows"
+    _check(load().od_gemm_w8a8_ld(_p(a), _p(sa), _p(w), _p(sw), _p(out), M, N, K, epilogue, out.stride(0),
+                                  _stream(dev)), "od_gemm_w8a8")
     if probe is not None:
         e1.record()
         probe.append((e0, e1, 2 * M * N * K, M * K + N * K + out.numel() * out.element_size() + 4 * M + 2 * N))
@@ -286,13 +291,27 @@ def qk_norm_rope_kv(qkv: torch.Tensor, pos: torch.Tensor, cos: torch.Tensor, sin
 
 
 @_probed
-def gate_quant(o: torch.Tensor, qkv: torch.Tensor, Hq: int, D: int, q=None, s=None):
-    dev = _need_cuda(o, qkv)
+def gate_quant(o: torch.Tensor, qkv: torch.Tensor, Hq: int, D: int, q=None, s=None, inv_s=None):
+    """bf16(o * bf16(sigmoid(gate))) [x inv_s, the o_proj SmoothedLinear] -> per-token int8 q (M, Hq*D), fp32 s (M,)."""
+    dev = _need_cuda(o, qkv, inv_s)
     M = o.shape[0]
     q = torch.empty(M, Hq * D, dtype=torch.int8, device=dev) if q is None else q
     s = torch.empty(M, dtype=torch.float32, device=dev) if s is None else s
-    _check(load().od_gate_quant(_p(o), _p(qkv), qkv.stride(0), M, Hq, D, _p(q), _p(s), _stream(dev)),
+    _check(load().od_gate_quant(_p(o), _p(qkv), qkv.stride(0), M, Hq, D, _p(inv_s), _p(q), _p(s), _stream(dev)),
            "od_gate_quant")
+    return q, s
+
+
+@_probed
+def swiglu_quant(g: torch.Tensor, u: torch.Tensor, inv_s: torch.Tensor | None = None, q=None, s=None):
+    """bf16(bf16(silu(g)) * u) [x inv_s, the down_proj SmoothedLinear] -> per-token int8 q (M, F), fp32 s (M,):
+    the MLP of a layer whose gate_proj and up_proj are smoothed by different vectors (two GEMMs)."""
+    dev = _need_cuda(g, u, inv_s)
+    assert g.shape == u.shape and g.is_contiguous() and u.is_contiguous()
+    M, F = g.shape
+    q = torch.empty(M, F, dtype=torch.int8, device=dev) if q is None else q
+    s = torch.empty(M, dtype=torch.float32, device=dev) if s is None else s
+    _check(load().od_swiglu_quant(_p(g), _p(u), M, F, _p(inv_s), _p(q), _p(s), _stream(dev)), "od_swiglu_quant")
     return q, s
 
 

@@ -21,6 +21,15 @@ Per decoder layer (Qwen3_5DecoderLayer, modeling_qwen3_5.py:744-783) on M tokens
     od_gemm_w8a8           down_proj
 Stacking q/k/v (and gate/up) rows is exact: per-output-channel scales and int32 dot products of a row do not depend
 on the other rows, and all three projections quantise the same normalised activation.
+
+SmoothQuant (the reference's a8w8sq path: smooth_a8w8_ + SmoothedLinear, quant.py:317-350): a smoothed linear holds
+int8(W * s) and multiplies its input by inv_s = bf16(1 / s) before the per-token quantisation. The multiply runs inside
+the quantising kernel (od_rmsnorm_res_quant, od_quant_rows_i8, od_gate_quant, od_swiglu_quant). When q, k and v (or gate
+and up) carry one shared vector, the stacked GEMMs run unchanged on the one smoothed activation. When their vectors
+differ - the reference's calibration (scripts/smoothquant_calibrate.py) computes one per linear - each projection
+quantises its own smoothed copy of the normalised activation and runs its own GEMM: q, k, v into their column ranges
+of the same stacked output (od_gemm_w8a8_ld), gate and up into two outputs that od_swiglu_quant combines. Exact either
+way: every smoothed input is quantised exactly as the reference quantises it.
 """
 from __future__ import annotations
 
@@ -104,6 +113,25 @@ def synthetic_weights(cfg: DecoderConfig, seed: int = 0, device="cpu", layers: i
 
 
 @dataclass
+class Smooth:
+    """SmoothQuant inverse scales of one decoder layer, inv_s = bf16(1 / s) per input channel (SmoothedLinear,
+    quant.py:317-329); None for a linear that is not smoothed."""
+    qkv: tuple               # (q_proj, k_proj, v_proj) inv_s, each (H,) or None
+    gu: tuple                # (gate_proj, up_proj)
+    o: torch.Tensor | None   # o_proj (Hq*D,)
+    down: torch.Tensor | None  # down_proj (F_pad,): ones past F (those activations are 0)
+    qkv_shared: bool = True  # one vector (or none) for q, k, v: the stacked GEMM runs on one smoothed activation
+    gu_shared: bool = True
+
+
+def _same(vs) -> bool:
+    """True when every entry is None or all are equal tensors."""
+    if all(v is None for v in vs):
+        return True
+    return all(v is not None for v in vs) and all(torch.equal(vs[0], v) for v in vs[1:])
+
+
+@dataclass
 class Layer:
     ln1: torch.Tensor
     ln2: torch.Tensor
@@ -111,8 +139,20 @@ class Layer:
     q_norm: torch.Tensor
     k_norm: torch.Tensor
     o: Int8Tensor            # (H, Hq*D)
-    gate_up: Int8Tensor      # (2*F_pad, H) rows interleaved in blocks of GU_BLOCK
+    gate_up: Int8Tensor | None   # (2*F_pad, H) rows interleaved in blocks of GU_BLOCK (None: separate gate / up)
     down: Int8Tensor         # (H, F_pad) columns >= F are zero
+    sq: Smooth | None = None
+    gate: Int8Tensor | None = None   # (F_pad, H): gate_proj alone, when gate / up are smoothed by different vectors
+    up: Int8Tensor | None = None
+
+    def qkv_parts(self, cfg: "DecoderConfig") -> list:
+        """Row ranges of the stacked q/k/v weight: [(first column, Int8Tensor view)] for q_proj, k_proj, v_proj."""
+        nq, nk = cfg.heads * cfg.head_dim * 2, cfg.kv_heads * cfg.head_dim
+        out, c = [], 0
+        for n in (nq, nk, nk):
+            out.append((c, Int8Tensor(self.qkv.q[c:c + n], self.qkv.scale[c:c + n], self.qkv.dtype)))
+            c += n
+        return out
 
 
 @dataclass
@@ -208,16 +248,28 @@ class Backbone:
 
     # ------------------------------------------------------------------------------------------ construction
     @classmethod
-    def from_int8(cls, cfg: DecoderConfig, q: dict, norms: dict, device) -> "Backbone":
+    def from_int8(cls, cfg: DecoderConfig, q: dict, norms: dict, device, inv_s: dict | None = None) -> "Backbone":
         """From the reference's int8 layout: q maps 'embed_tokens' and every 'layers.{i}.{self_attn|mlp}.{proj}' to
-        (qweight int8 (N, K), scale (N,) or (N, 1)); norms maps the RMSNorm weight names to float tensors."""
+        (qweight int8 (N, K), scale (N,) or (N, 1)); norms maps the RMSNorm weight names to float tensors. inv_s: the
+        SmoothQuant inverse scales {'layers.{i}.{self_attn|mlp}.{proj}': bf16 (K,)} of the smoothed linears, whose
+        q entries then hold int8(W * s) (smooth_a8w8_, quant.py:333-350)."""
         dev = torch.device(device)
         D, F, Fp, H = cfg.head_dim, cfg.ffn, cfg.ffn_pad, cfg.hidden
         dt = cfg.dtype
+        inv_s = inv_s or {}
 
         def qt(name):
             w, s = q[name]
             return w.to(dev).contiguous(), s.reshape(-1).to(dev, dt).contiguous()
+
+        def iv(name, pad_to=None):
+            v = inv_s.get(name)
+            if v is None:
+                return None
+            v = v.reshape(-1).to(dev, torch.bfloat16)
+            if pad_to is not None and v.numel() < pad_to:
+                v = torch.cat([v, v.new_ones(pad_to - v.numel())])
+            return v.contiguous()
 
         layers = []
         for i in range(cfg.layers):
@@ -229,36 +281,59 @@ class Backbone:
             if Fp != F:                                   # zero rows: SiLU(0) * 0 = 0 outputs, exact padding
                 gw = torch.cat([gw, gw.new_zeros(Fp - F, H)]); uw = torch.cat([uw, uw.new_zeros(Fp - F, H)])
                 gs = torch.cat([gs, gs.new_ones(Fp - F)]); us = torch.cat([us, us.new_ones(Fp - F)])
-            gu_w = torch.stack([gw.view(Fp // GU_BLOCK, GU_BLOCK, H), uw.view(Fp // GU_BLOCK, GU_BLOCK, H)], 1)
-            gu_s = torch.stack([gs.view(-1, GU_BLOCK), us.view(-1, GU_BLOCK)], 1)
             dw, ds = qt(p + "mlp.down_proj")
             if Fp != F:                                   # zero columns: the padded activations contribute 0
                 dw = torch.cat([dw, dw.new_zeros(H, Fp - F)], 1)
             ow, os_ = qt(p + "self_attn.o_proj")
-            layers.append(Layer(
+            sq = None
+            names = [p + n for n in ("self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj", "mlp.gate_proj",
+                                     "mlp.up_proj", "self_attn.o_proj", "mlp.down_proj")]
+            if any(n in inv_s for n in names):
+                v = [iv(n) for n in names[:6]] + [iv(names[6], Fp)]
+                sq = Smooth(qkv=tuple(v[:3]), gu=tuple(v[3:5]), o=v[5], down=v[6], qkv_shared=_same(v[:3]),
+                            gu_shared=_same(v[3:5]))
+            layer = Layer(
                 ln1=norms[p + "input_layernorm.weight"].to(dev, dt).contiguous(),
                 ln2=norms[p + "post_attention_layernorm.weight"].to(dev, dt).contiguous(),
                 qkv=qkv,
                 q_norm=norms[p + "self_attn.q_norm.weight"].to(dev, dt).contiguous(),
                 k_norm=norms[p + "self_attn.k_norm.weight"].to(dev, dt).contiguous(),
-                o=Int8Tensor(ow, os_, dt),
-                gate_up=Int8Tensor(gu_w.reshape(2 * Fp, H).contiguous(), gu_s.reshape(-1).contiguous(), dt),
-                down=Int8Tensor(dw.contiguous(), ds, dt)))
+                o=Int8Tensor(ow, os_, dt), gate_up=None,
+                down=Int8Tensor(dw.contiguous(), ds, dt), sq=sq)
+            if sq is None or sq.gu_shared:
+                gu_w = torch.stack([gw.view(Fp // GU_BLOCK, GU_BLOCK, H), uw.view(Fp // GU_BLOCK, GU_BLOCK, H)], 1)
+                gu_s = torch.stack([gs.view(-1, GU_BLOCK), us.view(-1, GU_BLOCK)], 1)
+                layer.gate_up = Int8Tensor(gu_w.reshape(2 * Fp, H).contiguous(), gu_s.reshape(-1).contiguous(), dt)
+            else:                                         # two GEMMs on two differently smoothed activations
+                layer.gate, layer.up = Int8Tensor(gw.contiguous(), gs, dt), Int8Tensor(uw.contiguous(), us, dt)
+            layers.append(layer)
         ew, es = qt("embed_tokens")
         return cls(cfg, Int8Tensor(ew, es, dt), layers, norms["norm.weight"].to(dev, dt).contiguous(), dev)
 
     @classmethod
-    def from_float_weights(cls, cfg: DecoderConfig, sd: dict, device) -> "Backbone":
+    def from_float_weights(cls, cfg: DecoderConfig, sd: dict, device, smooth: dict | None = None) -> "Backbone":
         """Quantise float weights exactly as the reference does at load (quantize_int8_ / Int8Embedding,
-        quant.py:122-127, 186-191: per-output-row absmax int8, scale in the weight dtype), on the device."""
+        quant.py:122-127, 186-191: per-output-row absmax int8, scale in the weight dtype), on the device.
+        smooth: SmoothQuant scales s (K,) per linear, keyed as the reference's scale files key them (relative to the
+        decoder's layer list: '{i}.self_attn.q_proj', ...); each such weight becomes W * s per input channel in fp32,
+        stored in the weight dtype, before quantisation, and its input is multiplied by bf16(1 / s) (smooth_a8w8_ and
+        SmoothedLinear, quant.py:317-350)."""
         dev = torch.device(device)
-        q, norms = {}, {}
+        q, norms, inv_s = {}, {}, {}
+        smooth = smooth or {}
         for name, w in sd.items():
             if name.endswith("norm.weight"):
                 norms[name] = w
-            else:
-                q[name[: -len(".weight")]] = quantize_weight(w.to(dev))
-        return cls.from_int8(cfg, q, norms, dev)
+                continue
+            base = name[: -len(".weight")]
+            sv = smooth.get(base[len("layers."):]) if base.startswith("layers.") else None
+            w = w.to(dev)
+            if sv is not None:
+                sv = sv.to(dev, torch.float32)
+                w = (w.float() * sv[None, :]).to(w.dtype)
+                inv_s[base] = (1.0 / sv).to(torch.bfloat16)
+            q[base] = quantize_weight(w)
+        return cls.from_int8(cfg, q, norms, dev, inv_s)
 
     @classmethod
     def random(cls, cfg: DecoderConfig, seed: int = 0, device="cuda", gen_device="cpu") -> "Backbone":
@@ -287,13 +362,22 @@ class Backbone:
             self.jit_bytes(cache) <= self.materialize_budget
         for li, L in enumerate(self.layers):
             last = li == cfg.layers - 1
-            if li == 0:
-                hq, hs = _lib.rmsnorm_res_quant(r, L.ln1, cfg.eps)
-            else:
-                hq, hs = _lib.rmsnorm_res_quant(d, L.ln1, cfg.eps, res_in=r, res_out=r)
-                if li in want:                              # output of decoder layer li (1-based feature number)
-                    feats[li] = r.clone()
-            qkv = _lib.gemm_w8a8(hq, hs, L.qkv.q, L.qkv.scale, _lib.OD_EPI_BF16)
+            sq = L.sq
+            nk = {} if li == 0 else dict(res_in=r, res_out=r)
+            if sq is None or sq.qkv_shared:
+                hq, hs = _lib.rmsnorm_res_quant(r if li == 0 else d, L.ln1, cfg.eps,
+                                                inv_s=sq.qkv[0] if sq is not None else None, **nk)
+                qkv = _lib.gemm_w8a8(hq, hs, L.qkv.q, L.qkv.scale, _lib.OD_EPI_BF16)
+            else:                                           # q, k, v smoothed by different vectors
+                y = torch.empty(M, H, dtype=cfg.dtype, device=dev)
+                _lib.rmsnorm_res_quant(r if li == 0 else d, L.ln1, cfg.eps, y_out=y, want_q=False, **nk)
+                qkv = torch.empty(M, cfg.qkv_out, dtype=cfg.dtype, device=dev)
+                for (c, W), inv in zip(L.qkv_parts(cfg), sq.qkv):
+                    xq, xs = _lib.quant_rows(y, scale_dtype=torch.float32, inv_s=inv)
+                    _lib.gemm_w8a8(xq, xs.view(-1), W.q, W.scale, _lib.OD_EPI_BF16,
+                                   out=qkv[:, c:c + W.q.shape[0]])
+            if li > 0 and li in want:                       # output of decoder layer li (1-based feature number)
+                feats[li] = r.clone()
             wc = spec.write_cache
             if wc is not None and self.fused_kv_write and cfg.dtype == torch.bfloat16:
                 # the pass's K/V go into the int8 cache (and its kept bf16 copy) from the same kernel
@@ -329,11 +413,21 @@ class Backbone:
                 Vq=spec.qkv_prefix[li][1] if spec.qkv_prefix else None, row_q=spec.row_q, q_len=spec.q_len,
                 own_lo=spec.own_lo, own_hi=spec.own_hi, row_groups=spec.row_groups,
                 max_group_rows=spec.max_group_rows)
-            oq, os_ = _lib.gate_quant(o.view(M, Hq * D), qkv, Hq, D)
+            oq, os_ = _lib.gate_quant(o.view(M, Hq * D), qkv, Hq, D, inv_s=sq.o if sq is not None else None)
             a = _lib.gemm_w8a8(oq, os_, L.o.q, L.o.scale, _lib.OD_EPI_BF16)
-            mq, ms = _lib.rmsnorm_res_quant(a, L.ln2, cfg.eps, res_in=r, res_out=r)
-            hm = _lib.gemm_w8a8(mq, ms, L.gate_up.q, L.gate_up.scale, _lib.OD_EPI_SWIGLU)
-            dq, dsc = _lib.quant_rows(hm, scale_dtype=torch.float32)
+            if L.gate_up is not None:
+                mq, ms = _lib.rmsnorm_res_quant(a, L.ln2, cfg.eps, res_in=r, res_out=r,
+                                                inv_s=sq.gu[0] if sq is not None else None)
+                hm = _lib.gemm_w8a8(mq, ms, L.gate_up.q, L.gate_up.scale, _lib.OD_EPI_SWIGLU)
+                dq, dsc = _lib.quant_rows(hm, scale_dtype=torch.float32, inv_s=sq.down if sq is not None else None)
+            else:                                           # gate and up smoothed by different vectors
+                y2 = torch.empty(M, H, dtype=cfg.dtype, device=dev)
+                _lib.rmsnorm_res_quant(a, L.ln2, cfg.eps, res_in=r, res_out=r, y_out=y2, want_q=False)
+                gq, gs = _lib.quant_rows(y2, scale_dtype=torch.float32, inv_s=sq.gu[0])
+                g = _lib.gemm_w8a8(gq, gs.view(-1), L.gate.q, L.gate.scale, _lib.OD_EPI_BF16)
+                uq, us = _lib.quant_rows(y2, scale_dtype=torch.float32, inv_s=sq.gu[1])
+                u = _lib.gemm_w8a8(uq, us.view(-1), L.up.q, L.up.scale, _lib.OD_EPI_BF16)
+                dq, dsc = _lib.swiglu_quant(g, u, inv_s=sq.down)
             d = _lib.gemm_w8a8(dq, dsc.view(-1), L.down.q, L.down.scale, _lib.OD_EPI_BF16)
         out = None
         if want and not spec.kv_only_last:

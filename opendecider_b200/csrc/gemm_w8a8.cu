@@ -54,27 +54,28 @@ __device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* src, float (&v
 }
 
 // Epilogue of one 128 x 256 accumulator in TMEM (tbase: this warp's lane quarter): this thread's output row m,
-// columns n0 .. n0 + 255 (SwiGLU: outputs tile_n * 128 .. + 127).
+// columns n0 .. n0 + 255 (SwiGLU: outputs tile_n * 128 .. + 127); rows of Y are ldy elements apart. Columns at or
+// beyond N (a last tile wider than the weight: its rows were zero-filled by TMA) are not stored.
 template <int EPI>
 __device__ __forceinline__ void epilogue_tile(uint32_t tbase, int m, bool valid, int n0, int tile_n,
                                               const float* __restrict__ sa, const __nv_bfloat16* __restrict__ sw,
-                                              void* __restrict__ Y, int N) {
+                                              void* __restrict__ Y, int64_t ldy, int N) {
   const float sam = valid ? sa[m] : 0.f;
   if constexpr (EPI == OD_EPI_INT32) {
 #pragma unroll 1
-    for (int c = 0; c < BN / 32; ++c) {
+    for (int c = 0; c < BN / 32 && n0 + c * 32 < N; ++c) {        // warp-uniform bound (tcgen05.ld is collective)
       uint32_t r[32];
       tmem_ld_32x32b_x32(tbase + c * 32, r);
       tmem_ld_wait();
       if (valid) {
-        uint4* dst = reinterpret_cast<uint4*>(static_cast<int32_t*>(Y) + static_cast<int64_t>(m) * N + n0 + c * 32);
+        uint4* dst = reinterpret_cast<uint4*>(static_cast<int32_t*>(Y) + static_cast<int64_t>(m) * ldy + n0 + c * 32);
 #pragma unroll
         for (int i = 0; i < 8; ++i) dst[i] = make_uint4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
       }
     }
   } else if constexpr (EPI == OD_EPI_BF16) {
 #pragma unroll 1
-    for (int c = 0; c < BN / 32; ++c) {
+    for (int c = 0; c < BN / 32 && n0 + c * 32 < N; ++c) {
       uint32_t r[32];
       tmem_ld_32x32b_x32(tbase + c * 32, r);
       tmem_ld_wait();
@@ -84,11 +85,10 @@ __device__ __forceinline__ void epilogue_tile(uint32_t tbase, int m, bool valid,
 #pragma unroll
         for (int j = 0; j < 32; ++j)
           y[j] = __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(r[j])), sam), w[j]);
-        store_bf16x32(static_cast<__nv_bfloat16*>(Y) + static_cast<int64_t>(m) * N + n0 + c * 32, y);
+        store_bf16x32(static_cast<__nv_bfloat16*>(Y) + static_cast<int64_t>(m) * ldy + n0 + c * 32, y);
       }
     }
   } else {  // OD_EPI_SWIGLU: columns [0,128) gate, [128,256) up of the same 128 outputs
-    const int ldy = N / 2;
     const int j0 = tile_n * (BN / 2);
 #pragma unroll 1
     for (int c = 0; c < BN / 64; ++c) {
@@ -117,7 +117,7 @@ template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const float* __restrict__ sa, const __nv_bfloat16* __restrict__ sw, void* __restrict__ Y, int M,
-                     int N, int K, int32_t* err) {
+                     int N, int K, int64_t ldy, int32_t* err) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // pointer arithmetic on the shared array (not an integer cast) keeps the shared address space visible
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -130,7 +130,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int num_m = (M + BM - 1) / BM, num_n = N / BN, num_kb = K / BK;
+  const int num_m = (M + BM - 1) / BM, num_n = (N + BN - 1) / BN, num_kb = K / BK;
   const int num_tiles = num_m * num_n;
 
   if (threadIdx.x == 0) {
@@ -249,7 +249,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int n0 = (tile % num_n) * BN;
       const bool valid = m < M;
       epilogue_tile<EPI>(tmem_base + acc * BN + (static_cast<uint32_t>(quarter * 32) << 16), m, valid, n0,
-                         tile % num_n, sa, sw, Y, N);
+                         tile % num_n, sa, sw, Y, ldy, N);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -284,7 +284,7 @@ template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_w8a8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                           const float* __restrict__ sa, const __nv_bfloat16* __restrict__ sw, void* __restrict__ Y,
-                          int M, int N, int K, int32_t* err) {
+                          int M, int N, int K, int64_t ldy, int32_t* err) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + P_STAGES * P_STAGE_BYTES);
@@ -298,7 +298,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
-  const int num_m = (M + PM - 1) / PM, num_n = N / BN, num_kb = K / BK;
+  const int num_m = (M + PM - 1) / PM, num_n = (N + BN - 1) / BN, num_kb = K / BK;
   const int num_tiles = num_m * num_n;
   const int pair = blockIdx.x >> 1, num_pairs = gridDim.x >> 1;
 
@@ -427,7 +427,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int m = (tile / num_n) * PM + static_cast<int>(rank) * 128 + row;
       epilogue_tile<EPI>(tmem_base + acc * BN + (static_cast<uint32_t>(quarter * 32) << 16), m, m < M,
-                         (tile % num_n) * BN, tile % num_n, sa, sw, Y, N);
+                         (tile % num_n) * BN, tile % num_n, sa, sw, Y, ldy, N);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_even[acc]);
@@ -486,7 +486,7 @@ int num_sms() {
 
 template <int EPI>
 int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const float* sa, const __nv_bfloat16* sw, void* Y,
-                int M, int N, int K, int32_t* err, cudaStream_t st) {
+                int M, int N, int K, int64_t ldy, int32_t* err, cudaStream_t st) {
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -494,16 +494,16 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const float* sa, c
     OD_CUDA_TRY(cudaFuncSetAttribute(gemm_w8a8_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
     attr_set[dev] = true;
   }
-  const int tiles = ((M + BM - 1) / BM) * (N / BN);
+  const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const int grid = tiles < num_sms() ? tiles : num_sms();
-  gemm_w8a8_kernel<EPI><<<grid, kThreads, kSmemBytes, st>>>(ta, tb, sa, sw, Y, M, N, K, err);
+  gemm_w8a8_kernel<EPI><<<grid, kThreads, kSmemBytes, st>>>(ta, tb, sa, sw, Y, M, N, K, ldy, err);
   OD_LAUNCH_CHECK();
   return ok();
 }
 
 template <int EPI>
 int launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const float* sa, const __nv_bfloat16* sw, void* Y,
-                     int M, int N, int K, int32_t* err, cudaStream_t st) {
+                     int M, int N, int K, int64_t ldy, int32_t* err, cudaStream_t st) {
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -512,7 +512,7 @@ int launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const float* 
                                      kPairSmemBytes));
     attr_set[dev] = true;
   }
-  const int tiles = ((M + PM - 1) / PM) * (N / BN);
+  const int tiles = ((M + PM - 1) / PM) * ((N + BN - 1) / BN);
   const int pairs = tiles < num_sms() / 2 ? tiles : num_sms() / 2;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
@@ -526,7 +526,7 @@ int launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const float* 
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  OD_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm_w8a8_pair_kernel<EPI>, ta, tb, sa, sw, Y, M, N, K, err));
+  OD_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm_w8a8_pair_kernel<EPI>, ta, tb, sa, sw, Y, M, N, K, ldy, err));
   OD_LAUNCH_CHECK();
   return ok();
 }
@@ -539,16 +539,21 @@ constexpr int64_t kPairMinRows = 1024;
 
 using namespace od;
 
-extern "C" int od_gemm_w8a8(const int8_t* A, const float* sa, const int8_t* W, const void* sw, void* Y, int64_t M,
-                            int64_t N, int64_t K, int epilogue, void* stream) {
+extern "C" int od_gemm_w8a8_ld(const int8_t* A, const float* sa, const int8_t* W, const void* sw, void* Y, int64_t M,
+                               int64_t N, int64_t K, int epilogue, int64_t ldy, void* stream) {
   OD_REQUIRE(A && W && Y, "od_gemm_w8a8: null pointer");
   OD_REQUIRE(epilogue == OD_EPI_INT32 || (sa && sw), "od_gemm_w8a8: scales are required for this epilogue");
-  OD_REQUIRE(M >= 0 && M < (1LL << 31) && N > 0 && N % BN == 0 && N < (1LL << 31) && K > 0 && K % BK == 0 &&
-                 K < (1LL << 31),
-             "od_gemm_w8a8: need N %% 256 == 0 and K %% 128 == 0 (M=%lld N=%lld K=%lld)", (long long)M, (long long)N,
-             (long long)K);
+  OD_REQUIRE(M >= 0 && M < (1LL << 31) && N > 0 && N % (epilogue == OD_EPI_SWIGLU ? BN : 32) == 0 &&
+                 N < (1LL << 31) && K > 0 && K % BK == 0 && K < (1LL << 31),
+             "od_gemm_w8a8: need N %% 32 == 0 (SwiGLU: N %% 256 == 0) and K %% 128 == 0 (M=%lld N=%lld K=%lld)",
+             (long long)M, (long long)N, (long long)K);
   OD_REQUIRE(aligned16(A) && aligned16(W) && aligned16(Y), "od_gemm_w8a8: A, W, Y must be 16-byte aligned");
   OD_REQUIRE(epilogue >= OD_EPI_BF16 && epilogue <= OD_EPI_INT32, "od_gemm_w8a8: bad epilogue %d", epilogue);
+  const int64_t cols = epilogue == OD_EPI_SWIGLU ? N / 2 : N;
+  const int64_t vec = epilogue == OD_EPI_INT32 ? 4 : 8;          // elements of one 16-byte store
+  OD_REQUIRE(ldy >= cols && ldy % vec == 0 && ldy < (1LL << 40),
+             "od_gemm_w8a8: output row stride %lld must be >= %lld and a multiple of %lld elements", (long long)ldy,
+             (long long)cols, (long long)vec);
   if (M == 0) return ok();
   const bool pairs = M >= kPairMinRows;
   CUtensorMap ta, tb;
@@ -563,14 +568,19 @@ extern "C" int od_gemm_w8a8(const int8_t* A, const float* sa, const int8_t* W, c
   const int m = static_cast<int>(M), n = static_cast<int>(N), k = static_cast<int>(K);
   if (pairs) {
     switch (epilogue) {
-      case OD_EPI_BF16: return launch_gemm_pair<OD_EPI_BF16>(ta, tb, sa, swp, Y, m, n, k, err, st);
-      case OD_EPI_SWIGLU: return launch_gemm_pair<OD_EPI_SWIGLU>(ta, tb, sa, swp, Y, m, n, k, err, st);
-      default: return launch_gemm_pair<OD_EPI_INT32>(ta, tb, sa, swp, Y, m, n, k, err, st);
+      case OD_EPI_BF16: return launch_gemm_pair<OD_EPI_BF16>(ta, tb, sa, swp, Y, m, n, k, ldy, err, st);
+      case OD_EPI_SWIGLU: return launch_gemm_pair<OD_EPI_SWIGLU>(ta, tb, sa, swp, Y, m, n, k, ldy, err, st);
+      default: return launch_gemm_pair<OD_EPI_INT32>(ta, tb, sa, swp, Y, m, n, k, ldy, err, st);
     }
   }
   switch (epilogue) {
-    case OD_EPI_BF16: return launch_gemm<OD_EPI_BF16>(ta, tb, sa, swp, Y, m, n, k, err, st);
-    case OD_EPI_SWIGLU: return launch_gemm<OD_EPI_SWIGLU>(ta, tb, sa, swp, Y, m, n, k, err, st);
-    default: return launch_gemm<OD_EPI_INT32>(ta, tb, sa, swp, Y, m, n, k, err, st);
+    case OD_EPI_BF16: return launch_gemm<OD_EPI_BF16>(ta, tb, sa, swp, Y, m, n, k, ldy, err, st);
+    case OD_EPI_SWIGLU: return launch_gemm<OD_EPI_SWIGLU>(ta, tb, sa, swp, Y, m, n, k, ldy, err, st);
+    default: return launch_gemm<OD_EPI_INT32>(ta, tb, sa, swp, Y, m, n, k, ldy, err, st);
   }
+}
+
+extern "C" int od_gemm_w8a8(const int8_t* A, const float* sa, const int8_t* W, const void* sw, void* Y, int64_t M,
+                            int64_t N, int64_t K, int epilogue, void* stream) {
+  return od_gemm_w8a8_ld(A, sa, W, sw, Y, M, N, K, epilogue, epilogue == OD_EPI_SWIGLU ? N / 2 : N, stream);
 }

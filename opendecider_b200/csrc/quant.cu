@@ -405,11 +405,13 @@ __device__ __forceinline__ float sigmoid_bf16(float g) {
   return rbf(v);
 }
 
-// o * sigmoid(gate) (Qwen3_5Attention.forward) then per-token quantisation of the o_proj input.
+// o * sigmoid(gate) (Qwen3_5Attention.forward), the o_proj SmoothedLinear multiply when inv_s is given, then
+// per-token quantisation of the o_proj input.
 template <int VPT>
 __global__ void __launch_bounds__(kRowThreads) gate_quant_kernel(const __nv_bfloat16* __restrict__ o,
                                                                  const __nv_bfloat16* __restrict__ qkv,
                                                                  int64_t ldqkv, int Hq, int D,
+                                                                 const __nv_bfloat16* __restrict__ inv_s,
                                                                  int8_t* __restrict__ q, float* __restrict__ s_out) {
   __shared__ float red[kRowThreads / 32];
   const int64_t row = blockIdx.x;
@@ -430,6 +432,10 @@ __global__ void __launch_bounds__(kRowThreads) gate_quant_kernel(const __nv_bflo
                          bmul2(ov.y, pack_rn(sigmoid_bf16(g[2]), sigmoid_bf16(g[3]))),
                          bmul2(ov.z, pack_rn(sigmoid_bf16(g[4]), sigmoid_bf16(g[5]))),
                          bmul2(ov.w, pack_rn(sigmoid_bf16(g[6]), sigmoid_bf16(g[7]))));
+      if (inv_s) {                                   // SmoothedLinear: bf16(x * inv_s)
+        const uint4 is = __ldg(reinterpret_cast<const uint4*>(inv_s + e));
+        vv[j] = make_uint4(bmul2(vv[j].x, is.x), bmul2(vv[j].y, is.y), bmul2(vv[j].z, is.z), bmul2(vv[j].w, is.w));
+      }
       am = babsmax4(vv[j], am);
     }
   }
@@ -442,6 +448,55 @@ __global__ void __launch_bounds__(kRowThreads) gate_quant_kernel(const __nv_bflo
       float f[8];
       unpack8(vv[j], f);
       *reinterpret_cast<uint2*>(q + row * W + e) = quant8(f, sc, rq);
+    }
+  }
+  if (threadIdx.x == 0) s_out[row] = sc;
+}
+
+// SwiGLU of separately computed gate and up projections (Qwen3_5MLP.forward: act_fn(gate_proj(x)) * up_proj(x)),
+// with the rounding points of the GEMM's fused SwiGLU epilogue: a = bf16(g / (1 + exp(-g))), h = bf16(a * u); then
+// the down projection's SmoothedLinear multiply when inv_s is given and per-token quantisation (its input). Used
+// when gate_proj and up_proj are smoothed by different vectors and so cannot share one interleaved GEMM.
+template <int VPT>
+__global__ void __launch_bounds__(kRowThreads) swiglu_quant_kernel(const __nv_bfloat16* __restrict__ g,
+                                                                   const __nv_bfloat16* __restrict__ u, int64_t F,
+                                                                   const __nv_bfloat16* __restrict__ inv_s,
+                                                                   int8_t* __restrict__ q, float* __restrict__ s_out) {
+  __shared__ float red[kRowThreads / 32];
+  const int64_t row = blockIdx.x;
+  uint4 hv[VPT];
+  uint32_t am = 0u;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int64_t e = (static_cast<int64_t>(j) * kRowThreads + threadIdx.x) * 8;
+    hv[j] = make_uint4(0, 0, 0, 0);
+    if (e < F) {
+      const uint4 gv = __ldg(reinterpret_cast<const uint4*>(g + row * F + e));
+      const uint4 uv = __ldg(reinterpret_cast<const uint4*>(u + row * F + e));
+      float gf[8];
+      unpack8(gv, gf);
+      uint32_t a[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        a[i] = pack_rn(__fdiv_rn(gf[2 * i], 1.0f + expf(-gf[2 * i])),
+                       __fdiv_rn(gf[2 * i + 1], 1.0f + expf(-gf[2 * i + 1])));
+      hv[j] = make_uint4(bmul2(a[0], uv.x), bmul2(a[1], uv.y), bmul2(a[2], uv.z), bmul2(a[3], uv.w));
+      if (inv_s) {
+        const uint4 is = __ldg(reinterpret_cast<const uint4*>(inv_s + e));
+        hv[j] = make_uint4(bmul2(hv[j].x, is.x), bmul2(hv[j].y, is.y), bmul2(hv[j].z, is.z), bmul2(hv[j].w, is.w));
+      }
+      am = babsmax4(hv[j], am);
+    }
+  }
+  const float amax = block_max(bmax_halves(am), red);
+  const float sc = quant_scale(amax), rq = quant_recip(sc);
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int64_t e = (static_cast<int64_t>(j) * kRowThreads + threadIdx.x) * 8;
+    if (e < F) {
+      float f[8];
+      unpack8(hv[j], f);
+      *reinterpret_cast<uint2*>(q + row * F + e) = quant8(f, sc, rq);
     }
   }
   if (threadIdx.x == 0) s_out[row] = sc;
@@ -630,11 +685,12 @@ extern "C" int od_embed_i8(const int64_t* ids, int64_t n, const int8_t* qweight,
   return ok();
 }
 
-extern "C" int od_gate_quant(const void* o, const void* qkv, int64_t ldqkv, int64_t M, int Hq, int D, int8_t* q,
-                             float* s, void* stream) {
+extern "C" int od_gate_quant(const void* o, const void* qkv, int64_t ldqkv, int64_t M, int Hq, int D,
+                             const void* inv_s, int8_t* q, float* s, void* stream) {
   OD_REQUIRE(o && qkv && q && s, "od_gate_quant: null pointer");
   OD_REQUIRE(M >= 0 && Hq > 0 && D % 8 == 0 && ldqkv % 8 == 0 && ldqkv >= 2LL * Hq * D, "od_gate_quant: bad shape");
-  OD_REQUIRE(aligned16(o) && aligned16(qkv) && aligned16(q), "od_gate_quant: pointers must be 16-byte aligned");
+  OD_REQUIRE(aligned16(o) && aligned16(qkv) && aligned16(q) && (!inv_s || aligned16(inv_s)),
+             "od_gate_quant: pointers must be 16-byte aligned");
   if (M == 0) return ok();
   cudaStream_t st = as_stream(stream);
   const int W = Hq * D;
@@ -642,7 +698,8 @@ extern "C" int od_gate_quant(const void* o, const void* qkv, int64_t ldqkv, int6
   dim3 grid(static_cast<unsigned>(M)), block(kRowThreads);
   auto O = static_cast<const __nv_bfloat16*>(o);
   auto G = static_cast<const __nv_bfloat16*>(qkv);
-#define OD_GQ(V) gate_quant_kernel<V><<<grid, block, 0, st>>>(O, G, ldqkv, Hq, D, q, s)
+  auto IS = static_cast<const __nv_bfloat16*>(inv_s);
+#define OD_GQ(V) gate_quant_kernel<V><<<grid, block, 0, st>>>(O, G, ldqkv, Hq, D, IS, q, s)
   if (vecs <= 1) OD_GQ(1);
   else if (vecs <= 2) OD_GQ(2);
   else if (vecs <= 3) OD_GQ(3);
@@ -652,6 +709,32 @@ extern "C" int od_gate_quant(const void* o, const void* qkv, int64_t ldqkv, int6
   else if (vecs <= 16) OD_GQ(16);
   else return fail(OD_EUNSUPPORTED, "od_gate_quant: Hq*D=%d above %d", W, 16 * 8 * kRowThreads);
 #undef OD_GQ
+  OD_LAUNCH_CHECK();
+  return ok();
+}
+
+extern "C" int od_swiglu_quant(const void* g, const void* u, int64_t M, int64_t F, const void* inv_s, int8_t* q,
+                               float* s, void* stream) {
+  OD_REQUIRE(g && u && q && s, "od_swiglu_quant: null pointer");
+  OD_REQUIRE(M >= 0 && F > 0 && F % 8 == 0, "od_swiglu_quant: bad shape (F %% 8 == 0)");
+  OD_REQUIRE(aligned16(g) && aligned16(u) && aligned16(q) && (!inv_s || aligned16(inv_s)),
+             "od_swiglu_quant: pointers must be 16-byte aligned");
+  if (M == 0) return ok();
+  cudaStream_t st = as_stream(stream);
+  const int64_t vecs = (F / 8 + kRowThreads - 1) / kRowThreads;
+  dim3 grid(static_cast<unsigned>(M)), block(kRowThreads);
+  auto Gp = static_cast<const __nv_bfloat16*>(g);
+  auto Up = static_cast<const __nv_bfloat16*>(u);
+  auto IS = static_cast<const __nv_bfloat16*>(inv_s);
+#define OD_SQ(V) swiglu_quant_kernel<V><<<grid, block, 0, st>>>(Gp, Up, F, IS, q, s)
+  if (vecs <= 1) OD_SQ(1);
+  else if (vecs <= 2) OD_SQ(2);
+  else if (vecs <= 4) OD_SQ(4);
+  else if (vecs <= 6) OD_SQ(6);
+  else if (vecs <= 8) OD_SQ(8);
+  else if (vecs <= 12) OD_SQ(12);
+  else return fail(OD_EUNSUPPORTED, "od_swiglu_quant: F=%lld above %d", (long long)F, 12 * 8 * kRowThreads);
+#undef OD_SQ
   OD_LAUNCH_CHECK();
   return ok();
 }

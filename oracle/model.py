@@ -60,17 +60,34 @@ def _rot(x, cos, sin):
 
 class OracleDecoder:
     """The int8 decoder on the CPU. sd: float (bf16) weights under HF's Qwen3_5TextModel names; `layers` limits the
-    pass to the first n layers (the timed baseline samples a few layers and extrapolates)."""
+    pass to the first n layers (the timed baseline samples a few layers and extrapolates). smooth: SmoothQuant scales
+    s (K,) per linear keyed relative to the layer list ('{i}.self_attn.q_proj', as the reference's scale files are):
+    smooth_a8w8_ (quant.py:333-350) stores W * s (fp32 product, weight dtype) and SmoothedLinear.forward
+    (quant.py:328-329) multiplies the input by inv_s = bf16(1 / s) in the activation dtype before the A8W8 product."""
 
-    def __init__(self, cfg, sd: dict, layers: int | None = None):
+    def __init__(self, cfg, sd: dict, layers: int | None = None, smooth: dict | None = None):
         self.cfg = cfg
         self.n = layers or cfg.layers
-        self.q = {}
+        self.q, self.inv = {}, {}
+        smooth = smooth or {}
         for name, w in sd.items():
             if not name.endswith("norm.weight"):
-                self.q[name[: -len(".weight")]] = _quant_w(w)
+                base = name[: -len(".weight")]
+                sv = smooth.get(base[len("layers."):]) if base.startswith("layers.") else None
+                if sv is not None:
+                    sv = sv.float()
+                    w = (w.float() * sv[None, :]).to(w.dtype)
+                    self.inv[base] = (1.0 / sv).to(BF)
+                self.q[base] = _quant_w(w)
         self.norm = {k: v for k, v in sd.items() if k.endswith("norm.weight")}
         self.cos, self.sin = ops.rope_tables(cfg.head_dim, cfg.rope_theta, cfg.max_pos)
+
+    def lin(self, name: str, x: torch.Tensor) -> torch.Tensor:
+        """One projection: [SmoothedLinear's bf16(x * inv_s)] then the A8W8 arithmetic. x (M, K) bf16."""
+        inv = self.inv.get(name)
+        if inv is not None:
+            x = x * inv
+        return a8w8(x, *self.q[name])
 
     def embed(self, ids):
         qw, s = self.q["embed_tokens"]
@@ -82,21 +99,21 @@ class OracleDecoder:
         R, t, H = x.shape
         D, Hq, Hkv = cfg.head_dim, cfg.heads, cfg.kv_heads
         h = rmsnorm(x, self.norm[p + "input_layernorm.weight"], cfg.eps).reshape(R * t, H)
-        qg = a8w8(h, *self.q[p + "self_attn.q_proj"]).view(R, t, Hq, 2 * D)
+        qg = self.lin(p + "self_attn.q_proj", h).view(R, t, Hq, 2 * D)
         q, gate = qg[..., :D], qg[..., D:].reshape(R, t, Hq * D)
-        k = a8w8(h, *self.q[p + "self_attn.k_proj"]).view(R, t, Hkv, D)
-        v = a8w8(h, *self.q[p + "self_attn.v_proj"]).view(R, t, Hkv, D)
+        k = self.lin(p + "self_attn.k_proj", h).view(R, t, Hkv, D)
+        v = self.lin(p + "self_attn.v_proj", h).view(R, t, Hkv, D)
         q = rmsnorm(q, self.norm[p + "self_attn.q_norm.weight"], cfg.eps)
         k = rmsnorm(k, self.norm[p + "self_attn.k_norm.weight"], cfg.eps)
         c, s = self.cos[pos][:, :, None, :], self.sin[pos][:, :, None, :]
         q, k = _rot(q, c, s), _rot(k, c, s)
         o = attend(i, q, k, v) * torch.sigmoid(gate)
-        x = x + a8w8(o.reshape(R * t, Hq * D), *self.q[p + "self_attn.o_proj"]).view(R, t, H)
+        x = x + self.lin(p + "self_attn.o_proj", o.reshape(R * t, Hq * D)).view(R, t, H)
         h2 = rmsnorm(x, self.norm[p + "post_attention_layernorm.weight"], cfg.eps).reshape(R * t, H)
-        g = a8w8(h2, *self.q[p + "mlp.gate_proj"])
-        u = a8w8(h2, *self.q[p + "mlp.up_proj"])
+        g = self.lin(p + "mlp.gate_proj", h2)
+        u = self.lin(p + "mlp.up_proj", h2)
         m = torch.nn.functional.silu(g) * u
-        x = x + a8w8(m, *self.q[p + "mlp.down_proj"]).view(R, t, H)
+        x = x + self.lin(p + "mlp.down_proj", m).view(R, t, H)
         return x, k, v
 
     def run(self, ids, pos, attend, features=()):
@@ -188,8 +205,8 @@ class OracleDecision:
 
     def __init__(self, cfg, sd, trunk, tok, temps: dict, temperature: float, layers: int | None = None,
                  list_cap: int = 16, qcache_min_rows: int = 12, none_text: str = "none of the above",
-                 branch_chunk: int = 64, sdpa=None):
-        self.dec = OracleDecoder(cfg, sd, layers)
+                 branch_chunk: int = 64, sdpa=None, smooth: dict | None = None):
+        self.dec = OracleDecoder(cfg, sd, layers, smooth)
         self.cfg, self.trunk, self.tok, self.temps, self.temperature = cfg, trunk, tok, temps, temperature
         self.list_cap, self.qcache_min_rows, self.none_text = list_cap, qcache_min_rows, none_text
         self.branch_chunk = branch_chunk                  # v3_branch_chunk (models.py:66)

@@ -67,7 +67,12 @@ def use_reference() -> None:
         sys.path.insert(0, ref)
 
 
-def build_reference(cfg: DecoderConfig, tok):
+def build_reference(cfg: DecoderConfig, tok, quantize: bool = True, smooth: dict | None = None):
+    """The reference's tiny backbone. quantize=False: the bf16 model (weight_quant none, the SmoothQuant calibration
+    model). smooth {'{i}.self_attn.q_proj': s, ...}: the reference's a8w8sq load (smooth_a8w8_, quant.py:333-350)
+    restated around its own classes: W *= s per input channel (fp32 product, bf16 weight), the weight quantised by
+    the reference's Int8Linear with the A8W8 arithmetic at its _fused seam (GemLite's A8W8 is not installed), and
+    the reference's SmoothedLinear(inner, s) in the linear's place (x * inv_s before the product)."""
     use_reference()
     from transformers.models.qwen3_5.configuration_qwen3_5 import Qwen3_5TextConfig
     from transformers.models.qwen3_5.modeling_qwen3_5 import Qwen3_5ForCausalLM, Qwen3_5TextModel
@@ -90,13 +95,25 @@ def build_reference(cfg: DecoderConfig, tok):
     lm.rotary_emb.inv_freq = inv_freq
     missing, unexpected = lm.load_state_dict(synthetic_weights(cfg, seed=0), strict=False)
     assert not unexpected and all("rotary" in k for k in missing), (missing, unexpected)
-    quantize_int8_(lm.layers)
-    lm.embed_tokens = Int8Embedding(lm.embed_tokens)
-    for mod in lm.layers.modules():
-        if isinstance(mod, Int8Linear):
-            mod.__dict__["_fused"] = A8W8(mod)
-    bcfg = BackboneConfig(path="synthetic", dtype="bfloat16", weight_quant="int8", kv_quant="int8",
-                          feature_layers=list(FEATURE_LAYERS), device="cpu")
+    if quantize:
+        smooth = smooth or {}
+        for name, mod in lm.layers.named_modules():
+            if isinstance(mod, torch.nn.Linear) and name in smooth:
+                s = smooth[name].to(torch.float32)
+                mod.weight.data = (mod.weight.data.float() * s[None, :]).to(mod.weight.dtype)
+        quantize_int8_(lm.layers)
+        lm.embed_tokens = Int8Embedding(lm.embed_tokens)
+        for mod in lm.layers.modules():
+            if isinstance(mod, Int8Linear):
+                mod.__dict__["_fused"] = A8W8(mod)
+        if smooth:
+            from opendecider.quant import SmoothedLinear
+            for name, s in smooth.items():
+                parent_name, attr = name.rsplit(".", 1)
+                parent = lm.layers.get_submodule(parent_name)
+                setattr(parent, attr, SmoothedLinear(getattr(parent, attr), s.to(torch.float32)))
+    bcfg = BackboneConfig(path="synthetic", dtype="bfloat16", weight_quant="int8" if quantize else "none",
+                          kv_quant="int8", feature_layers=list(FEATURE_LAYERS), device="cpu")
     return Backbone(lm, tok, bcfg)
 
 

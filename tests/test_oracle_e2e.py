@@ -86,3 +86,31 @@ def test_edge_yes_no_is_sensitive_to_the_last_bit_of_attention():
     d = _edge_oracle(sdpa_exp_variant)
     assert d["yn"] > 1e-3, d
     assert d["big"] < 1e-4, d
+
+
+def smooth_scales_from_golden(g) -> dict:
+    """The SmoothQuant scales the golden was made with ({'{i}.self_attn.q_proj': s, ...}, fp32)."""
+    import torch
+    return {k[len("scale."):]: torch.from_numpy(g[k]) for k in g.files if k.startswith("scale.")}
+
+
+def test_oracle_smoothquant_matches_reference():
+    """A8 row A3: a SmoothQuant model (the reference's smooth_a8w8_ folding + SmoothedLinear, calibrated scales per
+    linear, alpha 0.65: tests/golden/smooth_config1.npz) decided by the oracle equals the reference's decide_many."""
+    g = np.load("tests/golden/smooth_config1.npz")
+    scales = smooth_scales_from_golden(g)
+    assert len(scales) == 28                               # 7 linears x 4 layers, each its own vector
+    cfg = DecoderConfig.tiny(feature_layers=FEATURE_LAYERS)
+    tc = TrunkConfig(d_feat=cfg.hidden, n_feat_layers=len(FEATURE_LAYERS), **TRUNK)
+    trunk = V3Trunk(tc, trunk_state_dict(tc, seed=0), "cpu")
+    reqs, tok = syn.decision_requests(1, seed=0)
+    od = OracleDecision(cfg, synthetic_weights(cfg, seed=0), trunk, tok, TEMPS, 1.419344425201416,
+                        qcache_min_rows=32, smooth=scales)
+    _, ren, pn, logits = od.decide(reqs)
+    K = g["probs"].shape[1]
+    assert np.abs(ren[:, :K] - g["probs"]).max() < 1e-6
+    assert np.abs(pn - g["none"]).max() < 1e-6
+    assert np.abs(logits.numpy() - g["logits"]).max() < 1e-5
+    # the smoothing moves the trunk logits by 1e-2 (this random-init model has no activation outliers to move)
+    base = np.load("tests/golden/e2e_config1.npz")["qcache.logits"]
+    assert np.abs(g["logits"] - base).max() > 5e-3
