@@ -67,12 +67,14 @@ def use_reference() -> None:
         sys.path.insert(0, ref)
 
 
-def build_reference(cfg: DecoderConfig, tok, quantize: bool = True, smooth: dict | None = None):
+def build_reference(cfg: DecoderConfig, tok, quantize: bool = True, smooth: dict | None = None, device: str = "cpu"):
     """The reference's tiny backbone. quantize=False: the bf16 model (weight_quant none, the SmoothQuant calibration
     model). smooth {'{i}.self_attn.q_proj': s, ...}: the reference's a8w8sq load (smooth_a8w8_, quant.py:333-350)
     restated around its own classes: W *= s per input channel (fp32 product, bf16 weight), the weight quantised by
     the reference's Int8Linear with the A8W8 arithmetic at its _fused seam (GemLite's A8W8 is not installed), and
-    the reference's SmoothedLinear(inner, s) in the linear's place (x * inv_s before the product)."""
+    the reference's SmoothedLinear(inner, s) in the linear's place (x * inv_s before the product). device: where the
+    model is placed after it is built and quantised (the goldens are made on the CPU; the drop-in test runs it on
+    CUDA)."""
     use_reference()
     from transformers.models.qwen3_5.configuration_qwen3_5 import Qwen3_5TextConfig
     from transformers.models.qwen3_5.modeling_qwen3_5 import Qwen3_5ForCausalLM, Qwen3_5TextModel
@@ -112,8 +114,9 @@ def build_reference(cfg: DecoderConfig, tok, quantize: bool = True, smooth: dict
                 parent_name, attr = name.rsplit(".", 1)
                 parent = lm.layers.get_submodule(parent_name)
                 setattr(parent, attr, SmoothedLinear(getattr(parent, attr), s.to(torch.float32)))
+    lm = lm.to(device)
     bcfg = BackboneConfig(path="synthetic", dtype="bfloat16", weight_quant="int8" if quantize else "none",
-                          kv_quant="int8", feature_layers=list(FEATURE_LAYERS), device="cpu")
+                          kv_quant="int8", feature_layers=list(FEATURE_LAYERS), device=device)
     return Backbone(lm, tok, bcfg)
 
 
