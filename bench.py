@@ -433,6 +433,9 @@ def op_rows(args):
          M * (4 * (W + 2 * Hkv * D) + 4)),
         ("kv_append", lambda: _lib.kv_append(kk, vv, kq, vq, ksc, vsc, t0=0, kb=kb, vb=vb),
          M * Hkv * (2 * D * 2 + 2 * D + 2 * 2 + 2 * D * 2)),
+        ("qk_norm_rope_kv", lambda: _lib.qk_norm_rope_kv(qkv, pos, cos, sin, qn, kn, 1e-6, Hq, Hkv, D, t, kq, vq, ksc,
+                                                         vsc, 0, kb=kb, vb=vb),
+         M * (4 * (W + 2 * Hkv * D) + 4) + M * Hkv * (2 * D + 2 * 2 + 2 * D * 2)),
     ]
     only = set(args.kernels.split(",")) if args.kernels else None
     for name, fn, byts in cases:

@@ -158,8 +158,10 @@ __device__ __forceinline__ uint2 quant8(const float (&v)[8], float s, float r) {
     float2 t = __fadd2_rn(y, m2);
     const float2 n = __fadd2_rn(t, nm2);
     const float2 d = __fadd2_rn(y, make_float2(-n.x, -n.y));
-    if (fabsf(d.x) > 0.4999f) t.x = __fadd_rn(__fdiv_rn(v[2 * i], s), kMagic);
-    if (fabsf(d.y) > 0.4999f) t.y = __fadd_rn(__fdiv_rn(v[2 * i + 1], s), kMagic);
+    if (fmaxf(fabsf(d.x), fabsf(d.y)) > 0.4999f) {     // rare: one of the pair is near a half-integer
+      if (fabsf(d.x) > 0.4999f) t.x = __fadd_rn(__fdiv_rn(v[2 * i], s), kMagic);
+      if (fabsf(d.y) > 0.4999f) t.y = __fadd_rn(__fdiv_rn(v[2 * i + 1], s), kMagic);
+    }
     b[2 * i] = __float_as_uint(t.x);
     b[2 * i + 1] = __float_as_uint(t.y);
   }

@@ -396,13 +396,22 @@ __global__ void embed_i8_kernel(const int64_t* __restrict__ ids, const int8_t* _
 // rounding boundary - a tie, low 16 bits 0x8000 - lies between the two: so only a fast value within 64 fp32 ulps
 // (relative 3.8e-6) of a tie, or |g| >= 16, takes the fp32 formula. (Crossing a bf16-representable value changes
 // the upper bits but both sides round to that value.)
-__device__ __forceinline__ float sigmoid_bf16(float g) {
-  float e, v;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(g * -1.4426950408889634f));
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(v) : "f"(1.0f + e));
-  const int lo = static_cast<int>(__float_as_uint(v) & 0xFFFFu);
-  if (fabsf(g) >= 16.0f || abs(lo - 0x8000) < 64) v = __fdiv_rn(1.0f, 1.0f + expf(-g));
-  return rbf(v);
+// Two sigmoids packed as a bf16 pair (lo = g.x), the pair's arithmetic in packed fp32 operations. A value is near a
+// tie when its low 16 bits lie within 64 of 0x8000: (bits + 0x803F) mod 2^16 below 0x80.
+__device__ __forceinline__ uint32_t sigmoid2_bf16(float2 g) {
+  const float2 y = __fmul2_rn(g, make_float2(-1.4426950408889634f, -1.4426950408889634f));
+  float e0, e1, v0, v1;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e0) : "f"(y.x));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e1) : "f"(y.y));
+  const float2 d = __fadd2_rn(make_float2(1.0f, 1.0f), make_float2(e0, e1));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(v0) : "f"(d.x));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(v1) : "f"(d.y));
+  const uint32_t t0 = (__float_as_uint(v0) + 0x803Fu) & 0xFF80u, t1 = (__float_as_uint(v1) + 0x803Fu) & 0xFF80u;
+  if (min(t0, t1) == 0u || fmaxf(fabsf(g.x), fabsf(g.y)) >= 16.0f) {
+    v0 = __fdiv_rn(1.0f, 1.0f + expf(-g.x));
+    v1 = __fdiv_rn(1.0f, 1.0f + expf(-g.y));
+  }
+  return pack_rn(v0, v1);
 }
 
 // o * sigmoid(gate) (Qwen3_5Attention.forward), the o_proj SmoothedLinear multiply when inv_s is given, then
@@ -426,12 +435,8 @@ __global__ void __launch_bounds__(kRowThreads) gate_quant_kernel(const __nv_bflo
       const int h = e / D, d = e - h * D;
       const uint4 ov = __ldg(reinterpret_cast<const uint4*>(o + row * W + e));
       const uint4 gv = __ldg(reinterpret_cast<const uint4*>(qkv + row * ldqkv + static_cast<int64_t>(h) * 2 * D + D + d));
-      float g[8];
-      unpack8(gv, g);
-      vv[j] = make_uint4(bmul2(ov.x, pack_rn(sigmoid_bf16(g[0]), sigmoid_bf16(g[1]))),
-                         bmul2(ov.y, pack_rn(sigmoid_bf16(g[2]), sigmoid_bf16(g[3]))),
-                         bmul2(ov.z, pack_rn(sigmoid_bf16(g[4]), sigmoid_bf16(g[5]))),
-                         bmul2(ov.w, pack_rn(sigmoid_bf16(g[6]), sigmoid_bf16(g[7]))));
+      vv[j] = make_uint4(bmul2(ov.x, sigmoid2_bf16(unpack2(gv.x))), bmul2(ov.y, sigmoid2_bf16(unpack2(gv.y))),
+                         bmul2(ov.z, sigmoid2_bf16(unpack2(gv.z))), bmul2(ov.w, sigmoid2_bf16(unpack2(gv.w))));
       if (inv_s) {                                   // SmoothedLinear: bf16(x * inv_s)
         const uint4 is = __ldg(reinterpret_cast<const uint4*>(inv_s + e));
         vv[j] = make_uint4(bmul2(vv[j].x, is.x), bmul2(vv[j].y, is.y), bmul2(vv[j].z, is.z), bmul2(vv[j].w, is.w));
