@@ -266,6 +266,33 @@ def _peaks():
     return json.load(open(pk)) if os.path.exists(pk) else {}
 
 
+def int8_peak(dev, seconds: float = 2.0) -> dict:
+    """The dense int8 tensor rate measured here: cuBLASLt's int8 GEMM (torch._int_mm) at 8192^3, best of 5 single
+    launches (burst) and back to back for `seconds` (sustained, as a GEMM inside a long step runs), TOP/s."""
+    a = torch.randint(-127, 128, (8192, 8192), dtype=torch.int8, device=dev)
+    b = torch.randint(-127, 128, (8192, 8192), dtype=torch.int8, device=dev)
+    ops = 2.0 * 8192 ** 3
+    for _ in range(3):
+        torch._int_mm(a, b)
+    burst = []
+    for _ in range(5):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        torch._int_mm(a, b)
+        e1.record()
+        torch.cuda.synchronize()
+        burst.append(ops / (e0.elapsed_time(e1) / 1e3) / 1e12)
+    n = max(1, int(seconds * min(burst) * 1e12 / ops))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(n):
+        torch._int_mm(a, b)
+    e1.record()
+    torch.cuda.synchronize()
+    return {"burst": max(burst), "sustained": n * ops / (e0.elapsed_time(e1) / 1e3) / 1e12,
+            "how": f"torch._int_mm (cuBLASLt int8) 8192^3: best of 5 launches, and {n} back to back"}
+
+
 def _flush_l2(buf):
     buf.add_(1)                                                # writes 256 MB: more than the 126 MB L2
 
@@ -280,6 +307,8 @@ def op_gemm(args):
     shapes = [tuple(int(v) for v in x.split("x")) for x in args.shapes.split(",")] if args.shapes else \
         [(m, n, k) for m in (512, 2048, 8192) for (k, n) in ((4096, 4096), (4096, 12288), (12288, 4096))]
     peak = 2.0 * _peaks().get("bf16_tflops", 1590.0)            # burst: a kernel timed alone
+    i8 = int8_peak(dev)
+    print(json.dumps({"op": "int8_peak", **i8}))
     flush = torch.zeros(64 << 20, dtype=torch.float32, device=dev)
     for (M, N, K) in shapes:
         gc = syn.gemm_case(M, N, K, seed=0)
@@ -308,6 +337,7 @@ def op_gemm(args):
         byts = M * K + N * K + 2 * M * N + 4 * M + 2 * N
         print(json.dumps({"op": "gemm_w8a8", "shape": {"M": M, "N": N, "K": K}, "ms": t * 1e3,
                           "tops": ops / t / 1e12, "peak_tops": peak, "frac": ops / t / 1e12 / peak,
+                          "frac_of_int8_burst": ops / t / 1e12 / i8["burst"],
                           "gbs": byts / t / 1e9, "cublaslt_int8_tops": ops / (statistics.median(tc) / 1e3) / 1e12,
                           "l2": "flushed between iterations"}))
 
@@ -681,6 +711,7 @@ def main():
         peak = 2.0 * 1400.0
         peak_note = "2 x fallback sustained bf16 1.4 PFLOP/s"
     achieved = gemm_ops / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else None
+    i8 = int8_peak(dev)
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
         v, cores, sample = cpu_oracle_sample(args.config, 20.0)
@@ -703,9 +734,13 @@ def main():
                 "d2h_bytes_per_step": d2h, "ms_per_step": 1e3 * t_e2e / args.steps},
         "roofline": {"bound": "tensor", "kernel": "od_gemm_w8a8 (tcgen05 kind::i8)", "achieved": achieved,
                      "peak": peak, "unit": "TOP/s (int8)", "frac": (achieved / peak) if achieved else None,
-                     "peak_source": peak_note, "traffic": (traffic_ratio() * gemm_bytes / max(1, len(probe))) if traffic_ratio() and probe else None,
+                     "peak_source": peak_note,
+                     "int8_measured": i8, "frac_of_int8_sustained": (achieved / i8["sustained"]) if achieved else None,
+                     "traffic": (traffic_ratio() * gemm_bytes / max(1, len(probe))) if traffic_ratio() and probe else None,
                      "traffic_unit": "DRAM bytes per launch (step average: measured DRAM / algorithmic bytes of one "
                                      "ncu launch x the algorithmic bytes of the step's launches)",
+                     "traffic_source": "scaled from the committed ncu capture of one launch "
+                                       "(profiles/gemm_w8a8_pair_8192x10240x4096.md); not measured in this run",
                      "launches_per_step": gemm_launches, "share_of_step": gemm_ms / 1e3 / args.steps /
                      (t_dev / args.steps) if t_dev else None},
         "cpu_baseline": cpu, "clocks": clk, "gpu_launches": launches * args.steps,

@@ -33,6 +33,10 @@ class Decider:
         self.none_text = os.environ.get("OPENDECIDER_NONE_TEXT", "none of the above") if none_text is None \
             else none_text
         self.staging = Staging(model.backbone.device)
+        self._graphs = {}                         # execute_graph: plan layout -> (CUDA graph, its outputs)
+        self._graph_pool = None
+        if torch.device(model.backbone.device).type == "cuda":
+            self._graph_pool = torch.cuda.graph_pool_handle()
 
     def _with_none(self, q: Question) -> Question:
         """Copy of q with `none` appended, unless at the 255-option cap (decider.py:296-303)."""
@@ -120,6 +124,36 @@ class Decider:
         probs = _lib.readout(logits.contiguous(), plan["T"], opt_mask.to(torch.uint8), none_col=plan["none_col"])
         return probs, cache
 
+    def execute_graph(self, plan: dict, cache: KVCache | None = None):
+        """execute() as ONE CUDA graph per plan layout: the first call with a layout runs execute() eagerly (setting
+        up the kernels' one-time attributes and the cache), then captures it; later calls with the same layout - the
+        same shapes and the same staging offsets, so a new batch of the same structure whose plan has just been
+        staged - replay it. Every kernel of the state pass, the row passes, the trunk and the readout is in the graph;
+        the plan's inputs live in the staging arena's device buffer, whose addresses the graph captured, and the
+        outputs in the graph's memory pool (read them before the next replay). The cache must be the one of the
+        capture (the plan layout includes its buffers)."""
+        if cache is None:
+            probs, cache = self.execute(plan, cache)       # allocates the cache outside any graph
+            torch.cuda.synchronize(self.model.backbone.device)
+        key = (_layout(plan), _layout(cache))
+        hit = self._graphs.get(key)
+        if hit is None:
+            dev = self.model.backbone.device
+            side = torch.cuda.Stream(dev)
+            side.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(side):
+                self.execute(plan, cache)                  # warm-up: one-time kernel attributes, allocator pools
+            torch.cuda.current_stream(dev).wait_stream(side)
+            torch.cuda.synchronize(dev)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, pool=self._graph_pool):
+                out, c2 = self.execute(plan, cache)
+            assert c2 is cache, "the captured pass must write the given cache"
+            hit = self._graphs[key] = (graph, out)
+        graph, out = hit
+        graph.replay()
+        return out, cache
+
     def probs(self, questions, cache: KVCache):
         """Decider._probs (decider.py:236-284) without calibration profiles / sampler for questions reading
         `cache`: logits / T -> softmax * mask, caller-option renormalisation (fp64) and P(none) in od_readout."""
@@ -201,3 +235,26 @@ class Decider:
     def _finish(self, plan: dict, host: list, done, gathered: bool):
         done.synchronize()
         return self.answers(plan, host[:3]), (host[3] if gathered else None)
+
+
+def _layout(x):
+    """Hashable layout of a plan or cache: device tensors by (address, shape, dtype), host tensors and scalars by
+    value, host-only objects (questions, owners) skipped. Two plans with the same layout launch the same kernels on
+    the same buffers."""
+    import dataclasses
+    if isinstance(x, torch.Tensor):
+        if x.device.type == "cpu":                       # host-side plan data: its values shape the launches
+            return ("C", tuple(x.reshape(-1).tolist()), tuple(x.shape), str(x.dtype))
+        return ("T", x.data_ptr(), tuple(x.shape), str(x.dtype), x.device.type)
+    if isinstance(x, (int, float, bool, str, type(None))):
+        return x
+    if isinstance(x, dict):
+        return tuple((k, _layout(v)) for k, v in x.items() if k not in ("questions", "owner", "h2d_bytes"))
+    if isinstance(x, (list, tuple)):
+        return tuple(_layout(v) for v in x)
+    if dataclasses.is_dataclass(x):
+        # a pass's cache and question-level K/V are bound when the pass runs (run_rows): not part of the plan's layout
+        skip = ("cache", "qkv_prefix") if type(x).__name__ == "PassSpec" else ()
+        return (type(x).__name__,) + tuple(_layout(getattr(x, f.name)) for f in dataclasses.fields(x)
+                                           if f.name not in skip)
+    return ("obj", type(x).__name__)

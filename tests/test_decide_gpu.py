@@ -118,18 +118,19 @@ def test_config1_lm_feature_matches_reference(cuda, qcache):
 
 
 def test_fused_kv_write_same_decisions(cuda):
-    """The state pass's K/V written by od_qk_norm_rope_kv_i8 (fused) or by od_kv_append_i8 (separate) give the same
-    cache bytes and the same decisions, bit for bit."""
+    """The state pass's K/V written by od_qk_norm_rope_kv_i8 (fused, the default) or by od_kv_append_i8 (separate)
+    give the same cache bytes and the same decisions, bit for bit."""
     dec, reqs = make_decider(cuda, True)
     bb = dec.model.backbone
+    assert bb.fused_kv_write
     c0 = dec.encode_states([r.state for r in reqs])
     p0 = _collect(dec.decide_many(reqs))
-    bb.fused_kv_write = True
+    bb.fused_kv_write = False
     try:
         c1 = dec.encode_states([r.state for r in reqs])
         p1 = _collect(dec.decide_many(reqs))
     finally:
-        bb.fused_kv_write = False
+        bb.fused_kv_write = True
     for a, b in zip(c0.k + c0.v, c1.k + c1.v):
         assert torch.equal(a.q, b.q) and torch.equal(a.scale.view(torch.int16), b.scale.view(torch.int16))
     assert all(np.array_equal(x, y) for x, y in zip(p0, p1))
@@ -178,3 +179,36 @@ def test_edge_cases_match_reference(cuda):
         if "none" in got[name]:
             assert abs(got[name]["none"] - float(g[f"{name}.none"])) < bound, name
     assert {"big", "two", "small"} <= set(held), held            # held to 1e-3: all but the yes/no question
+
+
+def test_execute_graph_equals_eager(cuda):
+    """The whole decision call captured as one CUDA graph (Decider.execute_graph) gives the eager path's outputs bit
+    for bit, and a second batch of the same structure (new token ids, same lengths) staged into the same arena is
+    answered by replaying the graph, again equal to eager."""
+    dec, reqs = make_decider(cuda, True)
+    reqs2, _ = syn.decision_requests(1, seed=9)
+    plan = dec.plan(reqs)
+    want, cache = dec.execute(plan)
+    want = [t.clone() for t in want]
+    got, cache = dec.execute_graph(plan, cache)
+    assert all(torch.equal(a, b) for a, b in zip(want, got))
+    assert len(dec._graphs) == 1
+    plan2 = dec.plan(reqs2)
+    want2, _ = dec.execute(plan2, cache)
+    want2 = [t.clone() for t in want2]
+    from opendecider_b200.decider import _layout
+
+    def first_diff(a, b, path="plan"):
+        if type(a) is not type(b) or not isinstance(a, tuple) or len(a) != len(b):
+            return None if a == b else (path, str(a)[:200], str(b)[:200])
+        for i, (x, y) in enumerate(zip(a, b)):
+            d = first_diff(x, y, f"{path}[{i}]")
+            if d is not None:
+                return d
+        return None
+    assert _layout(plan) == _layout(plan2), first_diff(_layout(plan), _layout(plan2))
+    got2, _ = dec.execute_graph(plan2, cache)
+    assert len(dec._graphs) == 1                          # replayed, not captured again
+    assert all(torch.equal(a, b) for a, b in zip(want2, got2))
+    assert not all(torch.equal(a, b) for a, b in zip(want, want2))
+    torch.cuda.synchronize()
