@@ -336,6 +336,7 @@ def op_gemm(args):
         ops = 2.0 * M * N * K
         byts = M * K + N * K + 2 * M * N + 4 * M + 2 * N
         print(json.dumps({"op": "gemm_w8a8", "shape": {"M": M, "N": N, "K": K}, "ms": t * 1e3,
+                          "splits": _lib._gemm_plan(M, N, K, dev),
                           "tops": ops / t / 1e12, "peak_tops": peak, "frac": ops / t / 1e12 / peak,
                           "frac_of_int8_burst": ops / t / 1e12 / i8["burst"],
                           "gbs": byts / t / 1e9, "cublaslt_int8_tops": ops / (statistics.median(tc) / 1e3) / 1e12,

@@ -123,6 +123,16 @@ OD_API int od_gemm_w8a8(const int8_t* A, const float* sa, const int8_t* W, const
  * (M, Hq*2D + 2*Hkv*D) layout the single stacked GEMM writes. */
 OD_API int od_gemm_w8a8_ld(const int8_t* A, const float* sa, const int8_t* W, const void* sw, void* Y,
                     int64_t M, int64_t N, int64_t K, int epilogue, int64_t ldy, void* stream);
+/* Split-K for small M (M < 1024, the single-CTA form): the K range of each 128 x 256 tile is divided among `splits`
+ * work items (1..8, at most K / 128), each writing its int32 partial tile to `workspace` (tiles x splits x 128 x 256
+ * int32, no initial contents needed); a second kernel sums the partials (exact integer addition) and runs the
+ * epilogue: results identical to od_gemm_w8a8. Calls sharing a workspace must be stream-ordered.
+ * od_gemm_w8a8_plan returns the split count this GPU's SM count favours (1: no split, no workspace) and the
+ * workspace size. Same reference interfaces as od_gemm_w8a8. */
+OD_API int od_gemm_w8a8_plan(int64_t M, int64_t N, int64_t K, int num_sms, int* splits, int64_t* workspace_bytes);
+OD_API int od_gemm_w8a8_splitk(const int8_t* A, const float* sa, const int8_t* W, const void* sw, void* Y,
+                        int64_t M, int64_t N, int64_t K, int epilogue, int64_t ldy, int splits, void* workspace,
+                        int64_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------------------------------------------
  * Embedding lookup of an int8 table, Int8Embedding.forward (quant.py:199-200):

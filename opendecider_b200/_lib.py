@@ -48,6 +48,9 @@ SIGNATURES = {
     "od_gemm_w8a8": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int, c_void_p],
     "od_gemm_w8a8_ld": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int, c_int64,
                         c_void_p],
+    "od_gemm_w8a8_plan": [c_int64, c_int64, c_int64, c_int, POINTER(c_int), POINTER(c_int64)],
+    "od_gemm_w8a8_splitk": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int,
+                            c_int64, c_int, c_void_p, c_int64, c_void_p],
     "od_embed_i8": [c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int, c_void_p, c_void_p],
     "od_qk_norm_rope": [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_float, c_int64, c_int,
                         c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p],
@@ -216,11 +219,42 @@ def rmsnorm_res_quant(x: torch.Tensor, w: torch.Tensor, eps: float, res_in: torc
     return (q, s) if want_q else (None, None)
 
 
+_GEMM_PLANS: dict = {}
+_SPLITK_WS: dict = {}
+
+
+def _gemm_plan(M: int, N: int, K: int, dev) -> int:
+    """od_gemm_w8a8_plan's split count for this shape on this GPU (cached per shape)."""
+    key = (M, N, K, dev.index)
+    if key not in _GEMM_PLANS:
+        n, b = ctypes.c_int(1), ctypes.c_int64(0)
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        _check(load().od_gemm_w8a8_plan(M, N, K, sms, ctypes.byref(n), ctypes.byref(b)), "od_gemm_w8a8_plan")
+        _GEMM_PLANS[key] = n.value
+    return _GEMM_PLANS[key]
+
+
+def _splitk_bytes(M: int, N: int, splits: int) -> int:
+    tiles = -(-M // 128) * -(-N // 256)
+    return tiles * splits * 128 * 256 * 4
+
+
+def _splitk_workspace(dev, nbytes: int) -> torch.Tensor:
+    """The split-K partials' workspace of a device (grown on demand). Calls are stream-ordered on the device's current
+    stream, so two never use it at the same time."""
+    ws = _SPLITK_WS.get(dev.index)
+    if ws is None or ws.numel() * 4 < nbytes:
+        ws = torch.empty(-(-nbytes // 4), dtype=torch.int32, device=dev)
+        _SPLITK_WS[dev.index] = ws
+    return ws
+
+
 @_probed
 def gemm_w8a8(a: torch.Tensor, sa: torch.Tensor | None, w: torch.Tensor, sw: torch.Tensor | None,
-              epilogue: int = OD_EPI_BF16, out: torch.Tensor | None = None) -> torch.Tensor:
+              epilogue: int = OD_EPI_BF16, out: torch.Tensor | None = None, splits: int | None = None) -> torch.Tensor:
     """int8 (M, K) x int8 (N, K)^T on tcgen05: bf16 (M, N) / SwiGLU bf16 (M, N/2) / int32 (M, N). `out` may be a
-    column slice of a wider row-major buffer (its row stride is passed as the output leading dimension)."""
+    column slice of a wider row-major buffer (its row stride is passed as the output leading dimension). splits: the
+    K range split over work items for small M (None: od_gemm_w8a8_plan's choice; 1: none)."""
     dev = _need_cuda(a, w, sa, sw)
     M, K = a.shape
     N = w.shape[0]
@@ -236,8 +270,15 @@ def gemm_w8a8(a: torch.Tensor, sa: torch.Tensor | None, w: torch.Tensor, sw: tor
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
     assert out.dim() == 2 and out.stride(1) == 1 and out.shape[0] == M, "out: (M, cols) with contiguous rows"
-    _check(load().od_gemm_w8a8_ld(_p(a), _p(sa), _p(w), _p(sw), _p(out), M, N, K, epilogue, out.stride(0),
-                                  _stream(dev)), "od_gemm_w8a8")
+    if splits is None:
+        splits = _gemm_plan(M, N, K, dev)
+    if splits > 1:                                  # small M: the K range split over CTAs (exact int32 sums)
+        ws = _splitk_workspace(dev, _splitk_bytes(M, N, splits))
+        _check(load().od_gemm_w8a8_splitk(_p(a), _p(sa), _p(w), _p(sw), _p(out), M, N, K, epilogue, out.stride(0),
+                                          splits, _p(ws), ws.numel() * 4, _stream(dev)), "od_gemm_w8a8")
+    else:
+        _check(load().od_gemm_w8a8_ld(_p(a), _p(sa), _p(w), _p(sw), _p(out), M, N, K, epilogue, out.stride(0),
+                                      _stream(dev)), "od_gemm_w8a8")
     if probe is not None:
         e1.record()
         probe.append((e0, e1, 2 * M * N * K, M * K + N * K + out.numel() * out.element_size() + 4 * M + 2 * N))

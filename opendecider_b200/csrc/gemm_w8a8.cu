@@ -113,11 +113,73 @@ __device__ __forceinline__ void epilogue_tile(uint32_t tbase, int m, bool valid,
   }
 }
 
+// Split-K (single-CTA form, small M): the K range of a tile is divided among `splits` work items, each of which
+// writes its int32 partial tile to the workspace (tiles x splits x BM x BN); a second kernel sums the partials -
+// exact, integer addition - and runs the epilogue, one thread per 8 outputs. No CTA waits for another.
+struct SplitK {
+  int splits;
+  int32_t* part;
+};
+
+template <int EPI>
+__global__ void __launch_bounds__(256) gemm_splitk_reduce_kernel(const int32_t* __restrict__ part, int splits, int M,
+                                                                 int N, const float* __restrict__ sa,
+                                                                 const __nv_bfloat16* __restrict__ sw,
+                                                                 void* __restrict__ Y, int64_t ldy) {
+  const int num_n = (N + BN - 1) / BN;
+  const int groups = EPI == OD_EPI_SWIGLU ? N / 16 : N / 8;     // 8-output groups per row
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= static_cast<int64_t>(M) * groups) return;
+  const int m = static_cast<int>(idx / groups), gi = static_cast<int>(idx % groups);
+  const int row = m % BM;
+  // accumulator columns of this group: BF16 / INT32 output n = 8 gi .. + 7; SwiGLU outputs j = 8 gi .. + 7 read the
+  // gate columns c and the up columns BN / 2 + c of their tile
+  const int n = EPI == OD_EPI_SWIGLU ? (gi * 8 / (BN / 2)) * BN + (gi * 8) % (BN / 2) : gi * 8;
+  const int tile = (m / BM) * num_n + n / BN, col = n % BN;
+  int32_t a[8] = {0, 0, 0, 0, 0, 0, 0, 0}, u[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  for (int sp = 0; sp < splits; ++sp) {
+    const int32_t* src = part + ((static_cast<int64_t>(tile) * splits + sp) * BM + row) * BN + col;
+    const int4 x0 = __ldcg(reinterpret_cast<const int4*>(src)), x1 = __ldcg(reinterpret_cast<const int4*>(src) + 1);
+    a[0] += x0.x; a[1] += x0.y; a[2] += x0.z; a[3] += x0.w; a[4] += x1.x; a[5] += x1.y; a[6] += x1.z; a[7] += x1.w;
+    if constexpr (EPI == OD_EPI_SWIGLU) {
+      const int4 y0 = __ldcg(reinterpret_cast<const int4*>(src + BN / 2));
+      const int4 y1 = __ldcg(reinterpret_cast<const int4*>(src + BN / 2) + 1);
+      u[0] += y0.x; u[1] += y0.y; u[2] += y0.z; u[3] += y0.w; u[4] += y1.x; u[5] += y1.y; u[6] += y1.z; u[7] += y1.w;
+    }
+  }
+  if constexpr (EPI == OD_EPI_INT32) {
+    int4* dst = reinterpret_cast<int4*>(static_cast<int32_t*>(Y) + static_cast<int64_t>(m) * ldy + n);
+    dst[0] = make_int4(a[0], a[1], a[2], a[3]);
+    dst[1] = make_int4(a[4], a[5], a[6], a[7]);
+  } else {
+    const float sam = sa[m];
+    float y[8];
+    if constexpr (EPI == OD_EPI_BF16) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        y[j] = __fmul_rn(__fmul_rn(static_cast<float>(a[j]), sam), __bfloat162float(sw[n + j]));
+    } else {                                           // the OD_EPI_SWIGLU epilogue's rounding points
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float g = rbf(__fmul_rn(__fmul_rn(static_cast<float>(a[j]), sam), __bfloat162float(sw[n + j])));
+        const float v = rbf(__fmul_rn(__fmul_rn(static_cast<float>(u[j]), sam), __bfloat162float(sw[n + BN / 2 + j])));
+        y[j] = __fmul_rn(rbf(__fdiv_rn(g, 1.0f + expf(-g))), v);
+      }
+    }
+    uint4 w;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&w);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) h[j] = __floats2bfloat162_rn(y[2 * j], y[2 * j + 1]);
+    const int64_t out_col = EPI == OD_EPI_SWIGLU ? static_cast<int64_t>(gi) * 8 : n;
+    *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(Y) + static_cast<int64_t>(m) * ldy + out_col) = w;
+  }
+}
+
 template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const float* __restrict__ sa, const __nv_bfloat16* __restrict__ sw, void* __restrict__ Y, int M,
-                     int N, int K, int64_t ldy, int32_t* err) {
+                     int N, int K, int64_t ldy, int32_t* err, SplitK sk) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // pointer arithmetic on the shared array (not an integer cast) keeps the shared address space visible
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -132,6 +194,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_m = (M + BM - 1) / BM, num_n = (N + BN - 1) / BN, num_kb = K / BK;
   const int num_tiles = num_m * num_n;
+  const int splits = sk.splits;
+  const int num_items = num_tiles * splits;               // item = tile x splits + split
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -166,9 +230,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t armed = 0;  // bit s: stage s holds a load issued with parity bit (armed_par >> s) & 1
       uint32_t armed_par = 0;
       bool live = true;
-      for (int tile = blockIdx.x; tile < num_tiles && live; tile += gridDim.x) {
+      for (int item = blockIdx.x; item < num_items && live; item += gridDim.x) {
+        const int tile = item / splits, sp = item - tile * splits;
         const int m0 = (tile / num_n) * BM, n0 = (tile % num_n) * BN;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        const int kb0 = sp * num_kb / splits, kb1 = (sp + 1) * num_kb / splits;
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, err, kErrGemm | 1)) {
             live = false;
             break;
@@ -203,13 +269,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       int local = 0;
       bool live = true;
-      for (int tile = blockIdx.x; tile < num_tiles && live; tile += gridDim.x, ++local) {
+      for (int item = blockIdx.x; item < num_items && live; item += gridDim.x, ++local) {
+        const int sp = item % splits;
+        const int kb0 = sp * num_kb / splits, kb1 = (sp + 1) * num_kb / splits;
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, err, kErrGemm | 2)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, err, kErrGemm | 3)) {
             live = false;
             break;
@@ -220,7 +288,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int k = 0; k < BK / 32; ++k)
             mma_i8(d_tmem, desc_kmajor_sw128(a_addr + 32 * k), desc_kmajor_sw128(b_addr + 32 * k), idesc,
-                   (kb | k) != 0);
+                   (kb != kb0 || k != 0));
           mma_commit(&empty[stage]);
           if (++stage == STAGES) {
             stage = 0;
@@ -240,7 +308,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter + 32) = tile rows
     const int row = quarter * 32 + lane;
     int local = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+    for (int item = blockIdx.x; item < num_items; item += gridDim.x, ++local) {
+      const int tile = item / splits, sp = item - tile * splits;
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, err, kErrGemm | 4)) break;
@@ -248,8 +317,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int m = (tile / num_n) * BM + row;
       const int n0 = (tile % num_n) * BN;
       const bool valid = m < M;
-      epilogue_tile<EPI>(tmem_base + acc * BN + (static_cast<uint32_t>(quarter * 32) << 16), m, valid, n0,
-                         tile % num_n, sa, sw, Y, ldy, N);
+      const uint32_t tacc = tmem_base + acc * BN + (static_cast<uint32_t>(quarter * 32) << 16);
+      if (splits == 1) {
+        epilogue_tile<EPI>(tacc, m, valid, n0, tile % num_n, sa, sw, Y, ldy, N);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[acc]);
+        continue;
+      }
+      // split-K: this item's partial accumulator row into the workspace (summed by gemm_splitk_reduce_kernel)
+      int32_t* mine = sk.part + ((static_cast<int64_t>(tile) * splits + sp) * BM + row) * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tacc + c * 32, r);
+        tmem_ld_wait();
+        uint4* dst = reinterpret_cast<uint4*>(mine + c * 32);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) __stcg(dst + i, make_uint4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]));
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -486,7 +572,7 @@ int num_sms() {
 
 template <int EPI>
 int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const float* sa, const __nv_bfloat16* sw, void* Y,
-                int M, int N, int K, int64_t ldy, int32_t* err, cudaStream_t st) {
+                int M, int N, int K, int64_t ldy, int32_t* err, cudaStream_t st, SplitK sk = SplitK{1, nullptr}) {
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -494,9 +580,9 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const float* sa, c
     OD_CUDA_TRY(cudaFuncSetAttribute(gemm_w8a8_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
     attr_set[dev] = true;
   }
-  const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
-  const int grid = tiles < num_sms() ? tiles : num_sms();
-  gemm_w8a8_kernel<EPI><<<grid, kThreads, kSmemBytes, st>>>(ta, tb, sa, sw, Y, M, N, K, ldy, err);
+  const int items = ((M + BM - 1) / BM) * ((N + BN - 1) / BN) * sk.splits;
+  const int grid = items < num_sms() ? items : num_sms();
+  gemm_w8a8_kernel<EPI><<<grid, kThreads, kSmemBytes, st>>>(ta, tb, sa, sw, Y, M, N, K, ldy, err, sk);
   OD_LAUNCH_CHECK();
   return ok();
 }
@@ -539,8 +625,37 @@ constexpr int64_t kPairMinRows = 1024;
 
 using namespace od;
 
-extern "C" int od_gemm_w8a8_ld(const int8_t* A, const float* sa, const int8_t* W, const void* sw, void* Y, int64_t M,
-                               int64_t N, int64_t K, int epilogue, int64_t ldy, void* stream) {
+namespace od {
+namespace {
+// Split count of the single-CTA form for a small-M problem, in units of one k-block per wave of CTAs: (waves of work
+// items) x (k-blocks per item + about 2 of fixed cost), plus, when split, the partial tiles' round trip through L2 and
+// the reduction launch (measured on B200 at about 4 units + 0.17 per partial tile: 17 us for 128). Splitting pays
+// only for long K (M = 512, K = 12288: 45.7 us against 51.8); at most 8 splits and at most the k-blocks.
+int plan_splits_gemm(int64_t M, int64_t N, int64_t K, int sms) {
+  if (M >= kPairMinRows || sms <= 0) return 1;
+  const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  const int64_t kb = K / BK;
+  int best = 1;
+  double best_t = 1e300;
+  for (int s = 1; s <= 8 && s <= kb; ++s) {
+    const double waves = static_cast<double>((tiles * s + sms - 1) / sms);
+    const double t = waves * (static_cast<double>((kb + s - 1) / s) + 2.0) + (s > 1 ? 4.0 + 0.17 * tiles * s : 0.0);
+    if (t < best_t * 0.97) {
+      best_t = t;
+      best = s;
+    }
+  }
+  return best;
+}
+
+int64_t splitk_bytes(int64_t M, int64_t N, int splits) {
+  const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  return tiles * splits * BM * BN * static_cast<int64_t>(sizeof(int32_t));
+}
+
+int gemm_entry(const int8_t* A, const float* sa, const int8_t* W, const void* sw, void* Y, int64_t M, int64_t N,
+               int64_t K, int epilogue, int64_t ldy, int splits, void* workspace, int64_t workspace_bytes,
+               void* stream) {
   OD_REQUIRE(A && W && Y, "od_gemm_w8a8: null pointer");
   OD_REQUIRE(epilogue == OD_EPI_INT32 || (sa && sw), "od_gemm_w8a8: scales are required for this epilogue");
   OD_REQUIRE(M >= 0 && M < (1LL << 31) && N > 0 && N % (epilogue == OD_EPI_SWIGLU ? BN : 32) == 0 &&
@@ -554,8 +669,16 @@ extern "C" int od_gemm_w8a8_ld(const int8_t* A, const float* sa, const int8_t* W
   OD_REQUIRE(ldy >= cols && ldy % vec == 0 && ldy < (1LL << 40),
              "od_gemm_w8a8: output row stride %lld must be >= %lld and a multiple of %lld elements", (long long)ldy,
              (long long)cols, (long long)vec);
-  if (M == 0) return ok();
   const bool pairs = M >= kPairMinRows;
+  OD_REQUIRE(splits >= 1 && splits <= 8 && splits <= K / BK, "od_gemm_w8a8: splits %d must be in [1, min(8, K/128)]",
+             splits);
+  OD_REQUIRE(splits == 1 || !pairs, "od_gemm_w8a8: split-K is for M < %lld (the single-CTA form)",
+             (long long)kPairMinRows);
+  if (splits > 1)
+    OD_REQUIRE(workspace && aligned16(workspace) && workspace_bytes >= splitk_bytes(M, N, splits),
+               "od_gemm_w8a8: %d splits need a 16-byte aligned workspace of %lld bytes (od_gemm_w8a8_plan)",
+               splits, (long long)splitk_bytes(M, N, splits));
+  if (M == 0) return ok();
   CUtensorMap ta, tb;
   int rc = make_map_i8(&ta, A, static_cast<uint64_t>(K), static_cast<uint64_t>(M), BK, BM);
   if (rc) return rc;
@@ -573,11 +696,43 @@ extern "C" int od_gemm_w8a8_ld(const int8_t* A, const float* sa, const int8_t* W
       default: return launch_gemm_pair<OD_EPI_INT32>(ta, tb, sa, swp, Y, m, n, k, ldy, err, st);
     }
   }
+  SplitK sk{splits, static_cast<int32_t*>(workspace)};
   switch (epilogue) {
-    case OD_EPI_BF16: return launch_gemm<OD_EPI_BF16>(ta, tb, sa, swp, Y, m, n, k, ldy, err, st);
-    case OD_EPI_SWIGLU: return launch_gemm<OD_EPI_SWIGLU>(ta, tb, sa, swp, Y, m, n, k, ldy, err, st);
-    default: return launch_gemm<OD_EPI_INT32>(ta, tb, sa, swp, Y, m, n, k, ldy, err, st);
+    case OD_EPI_BF16: rc = launch_gemm<OD_EPI_BF16>(ta, tb, sa, swp, Y, m, n, k, ldy, err, st, sk); break;
+    case OD_EPI_SWIGLU: rc = launch_gemm<OD_EPI_SWIGLU>(ta, tb, sa, swp, Y, m, n, k, ldy, err, st, sk); break;
+    default: rc = launch_gemm<OD_EPI_INT32>(ta, tb, sa, swp, Y, m, n, k, ldy, err, st, sk); break;
   }
+  if (rc != OD_OK || splits == 1) return rc;
+  const int64_t threads = M * (epilogue == OD_EPI_SWIGLU ? N / 16 : N / 8);
+  const unsigned blocks = static_cast<unsigned>((threads + 255) / 256);
+  const int32_t* part = static_cast<const int32_t*>(workspace);
+  switch (epilogue) {
+    case OD_EPI_BF16: gemm_splitk_reduce_kernel<OD_EPI_BF16><<<blocks, 256, 0, st>>>(part, splits, m, n, sa, swp, Y, ldy); break;
+    case OD_EPI_SWIGLU: gemm_splitk_reduce_kernel<OD_EPI_SWIGLU><<<blocks, 256, 0, st>>>(part, splits, m, n, sa, swp, Y, ldy); break;
+    default: gemm_splitk_reduce_kernel<OD_EPI_INT32><<<blocks, 256, 0, st>>>(part, splits, m, n, sa, swp, Y, ldy); break;
+  }
+  OD_LAUNCH_CHECK();
+  return ok();
+}
+}  // namespace
+}  // namespace od
+
+extern "C" int od_gemm_w8a8_ld(const int8_t* A, const float* sa, const int8_t* W, const void* sw, void* Y, int64_t M,
+                               int64_t N, int64_t K, int epilogue, int64_t ldy, void* stream) {
+  return gemm_entry(A, sa, W, sw, Y, M, N, K, epilogue, ldy, 1, nullptr, 0, stream);
+}
+
+extern "C" int od_gemm_w8a8_plan(int64_t M, int64_t N, int64_t K, int num_sms, int* splits, int64_t* workspace_bytes) {
+  OD_REQUIRE(splits && workspace_bytes && M >= 0 && N > 0 && K > 0, "od_gemm_w8a8_plan: bad arguments");
+  *splits = plan_splits_gemm(M, N, K, num_sms);
+  *workspace_bytes = *splits > 1 ? splitk_bytes(M, N, *splits) : 0;
+  return ok();
+}
+
+extern "C" int od_gemm_w8a8_splitk(const int8_t* A, const float* sa, const int8_t* W, const void* sw, void* Y,
+                                   int64_t M, int64_t N, int64_t K, int epilogue, int64_t ldy, int splits,
+                                   void* workspace, int64_t workspace_bytes, void* stream) {
+  return gemm_entry(A, sa, W, sw, Y, M, N, K, epilogue, ldy, splits, workspace, workspace_bytes, stream);
 }
 
 extern "C" int od_gemm_w8a8(const int8_t* A, const float* sa, const int8_t* W, const void* sw, void* Y, int64_t M,

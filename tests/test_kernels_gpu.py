@@ -772,3 +772,26 @@ def test_prefix_attn_config3_full_shape(cuda, prefix):
             got = o[r]
             assert (got - ref).abs().max() < 2e-2, (s, a)
             assert (got - ref).norm() / ref.norm() < 5e-3, (s, a)
+
+
+@pytest.mark.parametrize("M,N,K", [(512, 4096, 4096), (200, 768, 1024), (1000, 512, 1536), (1, 256, 512)])
+def test_gemm_splitk_equals_unsplit(cuda, M, N, K):
+    """Split-K (small M): the K range divided over 2..4 work items whose int32 partials a second kernel sums - bf16,
+    SwiGLU and int32 epilogues identical to the unsplit GEMM, the int32 accumulators to the oracle's, twice in a
+    row on the same workspace."""
+    gc = syn.gemm_case(M=M, N=N, K=K, seed=6)
+    xq, sx = _lib.quant_rows(gc.x.to(cuda), scale_dtype=torch.float32)
+    W, sw = gc.qweight.to(cuda), gc.wscale.to(cuda).view(-1)
+    ref32 = torch.from_numpy(ops.gemm_i32(xq.cpu().numpy(), gc.qweight.numpy()))
+    for epi in (_lib.OD_EPI_BF16, _lib.OD_EPI_SWIGLU, _lib.OD_EPI_INT32):
+        base = _lib.gemm_w8a8(xq, sx.view(-1), W, sw, epi, splits=1)
+        for s in (2, 3, 4):
+            if s > K // 128:
+                continue
+            for _ in range(2):
+                got = _lib.gemm_w8a8(xq, sx.view(-1), W, sw, epi, splits=s)
+                assert torch.equal(got, base), (epi, s)
+        if epi == _lib.OD_EPI_INT32:
+            assert torch.equal(base.cpu(), ref32)
+    torch.cuda.synchronize()
+    assert _lib.device_error(cuda) == 0
