@@ -9,14 +9,16 @@ Workload (config 4): a 9B-class dense Qwen3.5-style decoder (36 layers, hidden 4
 layers 8/16/24/final); per GPU 64 requests, each a 2048-token random-id state with three questions (choice 16 x 12
 tokens, yes/no, score 5 x 2 tokens), each + the `none` option: 192 decisions per GPU per step. One step = the whole
 decision forward of that batch (state pass, question-cache row passes, trunk, readout). Requests are independent:
-N GPUs run N batches (weak scaling) and gather the probabilities over NCCL.
+N GPUs decide one global batch of 64 x N requests, each its contiguous size-balanced block (weak scaling), and gather
+the probabilities over NCCL.
 
 Printed: one JSON line on rank 0. `value` = decisions/s over all GPUs with the batch's inputs resident in HBM
 (device time, CUDA events, max over ranks); `e2e` = the same metric through the public API Decider.decide_stream
 (one batch per step: tokenisation, one pinned host->device copy, kernels, the device->host read of the answers, the
 next batch planned while the previous one runs); `roofline` = the W8A8
-GEMM (the dominant kernel) timed per launch with CUDA events inside the timed region; `cpu_baseline` = the CPU oracle
-of the same path (oracle/model.py) on a bounded sample, extrapolated.
+GEMM (the dominant kernel) timed per launch with CUDA events inside the timed region; `cpu_baseline` = the reference's
+own Decider.decide_many on the host cores (the reference package installed in baseline/_ref; the bit-exact CPU port,
+oracle/model.py, for config 5 or without the install) on a bounded sample, extrapolated.
 """
 from __future__ import annotations
 
@@ -217,32 +219,178 @@ class CpuSampleCached:
         return 1.0 / t_req, torch.get_num_threads(), desc
 
 
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
+
+
+def reference_installed() -> bool:
+    return os.path.isdir(os.path.join(REF_DIR, "opendecider"))
+
+
+class RefCpuSample:
+    """The reference's OWN code timed on the host cores: `opendecider.decider.Decider.decide_many` from the unmodified
+    reference package installed in baseline/_ref, on its stock CPU path (int8 weight-only linears dequantised per
+    call, `Int8Linear.forward` quant.py:149-157; the state pass, question cache and option rows of decide_many,
+    decider.py:438-484; torch's CPU attention). Set-up only, none of which changes the arithmetic: a Qwen3.5 text
+    model built from the workload's configuration (every layer full attention, HF random init, bf16) instead of a
+    checkpoint, the reference's quantize_int8_ / Int8Embedding, its use_reference_kernels(True), a no-op
+    `_update_linear_attn_mask` (transformers 5.5 raises on an all-attention cache), the word-level synthetic tokenizer.
+    One request of the workload is decided at n_lo and n_hi decoder layers (layers past the first share its int8
+    weights: timing only); the slope is one layer's cost and the intercept the fixed cost, extrapolated to all layers.
+    The trunk reads its feature layers from the last sampled layer (same shapes and work)."""
+
+    def __init__(self, config: int, n_lo: int = 2, n_hi: int = 8, seed: int = 0):
+        import copy
+        if not reference_installed():
+            raise RuntimeError("the reference package is not installed in baseline/_ref")
+        if REF_DIR not in sys.path:
+            sys.path.insert(0, REF_DIR)
+        from transformers.models.qwen3_5.configuration_qwen3_5 import Qwen3_5TextConfig
+        from transformers.models.qwen3_5.modeling_qwen3_5 import Qwen3_5ForCausalLM, Qwen3_5TextModel
+        from opendecider.backbone import Backbone, BackboneConfig, use_reference_kernels
+        from opendecider.decider import Decider, prepare_inference_
+        from opendecider.models import ModelConfig, build_model
+        from opendecider.quant import Int8Embedding, quantize_int8_
+        from opendecider_b200 import synthetic as syn
+        from opendecider_b200.backbone import synthetic_weights
+        torch.set_num_threads(os.cpu_count() or 1)
+        cfg, tk, _, _ = workload(config)
+        self.n_layers_total = cfg.layers
+        self.n_lo, self.n_hi = min(n_lo, cfg.layers), min(n_hi, cfg.layers)
+        reqs, tok = syn.decision_requests(config, seed=seed, n_requests=1)
+        self.nd = sum(len(r.questions) for r in reqs)
+        self.reqs = [{"state": r.state, "questions": {q.name: self._question(q) for q in r.questions}} for r in reqs]
+        use_reference_kernels(True)
+        Qwen3_5TextModel._update_linear_attn_mask = lambda self, am, pkv: None
+        c = Qwen3_5TextConfig(
+            vocab_size=cfg.vocab, hidden_size=cfg.hidden, intermediate_size=cfg.ffn, num_hidden_layers=1,
+            num_attention_heads=cfg.heads, num_key_value_heads=cfg.kv_heads, head_dim=cfg.head_dim,
+            layer_types=["full_attention"], rms_norm_eps=cfg.eps, tie_word_embeddings=True,
+            pad_token_id=tok.pad_token_id,
+            rope_parameters={"rope_type": "default", "rope_theta": cfg.rope_theta, "partial_rotary_factor": 1.0})
+        # built on the meta device and filled with the seeded synthetic weights (HF's own random init of the 0.6 G
+        # embedding takes a minute on the CPU); the rotary table is built on the CPU in fp32, as from_pretrained keeps it
+        dt = torch.get_default_dtype()
+        torch.set_default_dtype(torch.bfloat16)
+        try:
+            with torch.device("meta"):
+                lm = Qwen3_5ForCausalLM(c).model
+        finally:
+            torch.set_default_dtype(dt)
+        lm = lm.to_empty(device="cpu").eval()
+        lm.rotary_emb = type(lm.rotary_emb)(config=c)
+        missing, unexpected = lm.load_state_dict(synthetic_weights(cfg, seed=seed, layers=1), strict=False)
+        assert not unexpected and not missing, (missing, unexpected)
+        quantize_int8_(lm.layers)
+        lm.embed_tokens = Int8Embedding(lm.embed_tokens)
+        self.lm, self.layer0 = lm, lm.layers[0]
+        self.share = {id(t): t for t in list(self.layer0.parameters()) + list(self.layer0.buffers())}
+        self.tok, self.Backbone, self.BackboneConfig = tok, Backbone, BackboneConfig
+        self.mcfg = lambda: ModelConfig(variant="v3", slot_emb="none", dropout=0.0, v3_features="branched",
+                                        v3_row_format="answer", v3_cross="question", v3_layer_combine="mix",
+                                        v3_lm_feature=False, **tk)
+        self.build_model, self.prepare_inference_, self.Decider = build_model, prepare_inference_, Decider
+        self.n_feat = len(cfg.feature_layers)
+        self.deciders = {n: self._decider(n) for n in (self.n_lo, self.n_hi)}
+        self._time(self.n_lo)                          # warm-up: allocator, thread pool, kernel selection
+
+    @staticmethod
+    def _question(q) -> dict:
+        """A synthetic question in the reference's request schema (schema.py: choice options, noul, score levels)."""
+        if q.type == "noul":
+            return {"type": "noul", "prompt": q.prompt}
+        if q.type == "score":
+            return {"type": "score", "prompt": q.prompt, "levels": list(q.options)}
+        return {"type": q.type, "prompt": q.prompt, "options": list(q.options)}
+
+    def _decider(self, n: int):
+        import copy
+        layers = [self.layer0]
+        for i in range(1, n):
+            lay = copy.deepcopy(self.layer0, dict(self.share))
+            lay.self_attn.layer_idx = i
+            layers.append(lay)
+        self.lm.layers = torch.nn.ModuleList(layers)
+        self.lm.config.num_hidden_layers = n
+        self.lm.config.layer_types = ["full_attention"] * n
+        bcfg = self.BackboneConfig(path="synthetic", dtype="bfloat16", weight_quant="int8", kv_quant="int8",
+                                   feature_layers=["final"] * self.n_feat, device="cpu")
+        lm = copy.copy(self.lm)                        # its own layer list and config; shared weights
+        lm._modules = dict(self.lm._modules)
+        lm.config = copy.copy(self.lm.config)
+        bb = self.Backbone(lm, self.tok, bcfg)
+        torch.manual_seed(0)
+        model = self.build_model(bb, self.mcfg()).eval()
+        self.prepare_inference_(model)
+        return self.Decider(model, temperature=TEMPERATURE, temperature_by_type=TEMPS)
+
+    def _time(self, n: int) -> float:
+        t0 = time.perf_counter()
+        with torch.inference_mode():
+            ans = self.deciders[n].decide_many(self.reqs)
+        dt = time.perf_counter() - t0
+        assert len(ans) == len(self.reqs)
+        return dt
+
+    def step(self):
+        """One timed sample. Returns (decisions/s of the whole-depth request, threads, description)."""
+        t_lo, t_hi = self._time(self.n_lo), self._time(self.n_hi)
+        per_layer = max(0.0, (t_hi - t_lo) / max(1, self.n_hi - self.n_lo))
+        fixed = max(0.0, t_lo - self.n_lo * per_layer)
+        t_req = fixed + self.n_layers_total * per_layer
+        desc = (f"the reference's own Decider.decide_many (baseline/_ref, stock CPU path: int8 weight-only linears, "
+                f"torch CPU attention) on 1 request ({self.nd} decisions) timed at {self.n_lo} and {self.n_hi} of "
+                f"{self.n_layers_total} decoder layers ({t_lo:.1f} s, {t_hi:.1f} s): {per_layer:.2f} s per layer + "
+                f"{fixed:.2f} s fixed, extrapolated to all layers ({t_req:.1f} s per request)")
+        return self.nd / t_req, torch.get_num_threads(), desc
+
+
 def cpu_oracle_sample(config: int, budget_s: float):
     if config == 5:
         return CpuSampleCached(budget_s).step()
     return CpuSample(config).step()
 
 
+def cpu_baseline_sample(config: int, budget_s: float, samples: int = 3):
+    """(value, threads, description, kind): the reference's own code where it is installed and the configuration is
+    a plain decide_many (configs 1 and 4; the mean of `samples` timed samples), else the bit-exact port (config 5's
+    cached-state append)."""
+    if config != 5 and reference_installed():
+        rs = RefCpuSample(config)
+        got = [rs.step() for _ in range(samples)]
+        return statistics.mean(g[0] for g in got), got[0][1], got[-1][2] + f"; mean of {samples} samples", "reference"
+    return (*cpu_oracle_sample(config, budget_s), "port")
+
+
 def run_reference(args, rank: int) -> None:
-    """--impl reference: the reference path's CPU implementation (the oracle port) on the host cores."""
+    """--impl reference: the reference's own CPU implementation of the path on the host cores - its Decider.decide_many
+    from the installed reference package (RefCpuSample) for configs 1 and 4, with the bit-exact port timed once beside
+    it as a cross-check; config 5 (the cached-state append) and a missing install time the port."""
     if rank != 0:
         return
     cfg, _, _, desc = workload(args.config)
-    per_step = max(3.0, 120.0 / max(1, args.steps + args.warmup))
-    cs = CpuSampleCached(per_step) if args.config == 5 else CpuSample(args.config)
+    use_ref = args.config != 5 and reference_installed()
+    if use_ref:
+        cs, kind = RefCpuSample(args.config), "reference"
+    else:
+        per_step = max(3.0, 120.0 / max(1, args.steps + args.warmup))
+        cs, kind = (CpuSampleCached(per_step) if args.config == 5 else CpuSample(args.config)), "port"
     vals = []
     for i in range(args.warmup + args.steps):
         v, cores, sample = cs.step()
         if i >= args.warmup:
             vals.append(v)
     value = statistics.mean(vals)
-    print(json.dumps({
+    line = {
         "metric": METRIC, "value": value, "unit": "decisions/s", "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "int8", "data": "synthetic", "impl": "reference",
         "config": {"workload": desc, "global_batch": None},
-        "cpu_baseline": {"value": value, "unit": "decisions/s", "cores": cores, "kind": "port", "sample": sample},
-        "e2e": {"value": value, "unit": "decisions/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+        "cpu_baseline": {"value": value, "unit": "decisions/s", "cores": cores, "kind": kind, "sample": sample},
+        "e2e": {"value": value, "unit": "decisions/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    if use_ref:
+        pv, pc, ps = CpuSample(args.config).step()
+        line["port_cross_check"] = {"value": pv, "unit": "decisions/s", "cores": pc, "kind": "port", "sample": ps}
+    print(json.dumps(line))
 
 
 # ------------------------------------------------------------------------------------------------ B200 arm
@@ -715,8 +863,8 @@ def main():
     i8 = int8_peak(dev)
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
-        v, cores, sample = cpu_oracle_sample(args.config, 20.0)
-        cpu = {"value": v, "unit": "decisions/s", "cores": cores, "kind": "port",
+        v, cores, sample, kind = cpu_baseline_sample(args.config, 20.0)
+        cpu = {"value": v, "unit": "decisions/s", "cores": cores, "kind": kind,
                "sample": sample + ("; without the LM log-prob feature" if args.lm_feature else "")}
     kv_gb = sum(t.q.numel() for t in cache.k + cache.v) / 1e9 if cache is not None else 0.0
     out = {

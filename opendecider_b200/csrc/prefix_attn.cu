@@ -15,11 +15,12 @@
 //                        works on S_j, then O += P_j V_j; Q and P are A operands in TMEM (shared memory then only
 //                        streams K and V to the tensor core: its operand bandwidth is the limit), V is MN-major,
 //                        O accumulates in TMEM
-//   softmax warps (8)    warp w owns TMEM lane quarter w % 4 and keys [64 (w / 4), +64) of each block: causal and
-//                        same-row masks on own keys, the row max exchanged with the partner warp of the other key
-//                        half, online softmax in the exp2 domain with a lazy rescale of O only when the max grows
-//                        by more than 2^8, P (bf16) into TMEM; at the start each puts its slot's Q half-row into TMEM,
-//                        at the end O / l and the natural-log LSE
+//   softmax warps (8)    warps 0-3 serve query tile 0 and warps 4-7 tile 1; warp w owns TMEM lane quarter w % 4, so
+//                        one thread owns one query slot and all 128 keys of each block (no cross-warp exchange):
+//                        causal and same-row masks on own keys, online softmax in the exp2 domain with a lazy
+//                        rescale of O only when the max grows by more than 2^8, P (bf16) into TMEM; at the start each
+//                        puts its slot's Q row into the tile's shared-memory operand, at the end O / l and the
+//                        natural-log LSE
 // Every mbarrier wait is bounded; a time-out ends the kernel with an error code, never a hang.
 // Each slot's math does not depend on the other slots: outputs do not depend on row order.
 #include <cudaTypedefs.h>
