@@ -79,6 +79,8 @@ struct Params {
   CUtensorMap map_ko, map_vo, map_kq, map_vq;   // bf16 (rows, Hkv*D) views of own / question K and V, 64x128 boxes
   CUtensorMap map_kp, map_vp;                   // (S*Hkv*T, D) views of the state prefix: int8 with D x 128 boxes,
                                                 // or bf16 (materialised) with 64x128 boxes in the UMMA swizzle
+  CUtensorMap map_q, map_o;                     // (R*t, Hq, D) views of q and o, boxes of 64 x rep x 128 / rep: one
+                                                // box = 128 consecutive slots (token, head of the group) x 64 columns
   const __nv_bfloat16* q;
   const int8_t* Kp;
   const int8_t* Vp;
@@ -104,6 +106,8 @@ struct Params {
   int Hq, Hkv, rep, tiles_per_group;
   int prefix_bf16;
   int nsplit;                                   // CTAs sharing one query tile's state prefix (grid z)
+  int q_tma;                                    // the query tiles arrive by TMA and full output tiles leave by TMA
+                                                // (map_q / map_o valid: rep divides 128)
   float* part_o;                                // nsplit > 1: per split, O / l (fp32, the layout of o) ...
   float* part_lse;                              // ... and the natural-log LSE (the layout of lse)
   float scale_log2;
@@ -227,7 +231,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
   uint64_t* rawv_empty = rawv_full + RD;   // [RD]
   uint64_t* q_full = rawv_empty + RD;      // softmax warps (the Q tiles in shared memory) -> MMA
   uint64_t* drain = q_full + 1;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* o_ready = drain + 1;           // [2] the tile's softmax threads (O rows staged) -> the TMA-store thread
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(o_ready + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   uint32_t* masks = reinterpret_cast<uint32_t*>(sm + L::MASK0);
 
@@ -268,8 +273,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
       mbar_init(&rawv_full[r], 1);
       mbar_init(&rawv_empty[r], kProducers);
     }
-    mbar_init(q_full, 32 * 4 * NT);
+    mbar_init(q_full, P.q_tma ? 1 : 32 * 4 * NT);
     mbar_init(drain, 1);
+    mbar_init(&o_ready[0], BM);
+    mbar_init(&o_ready[1], BM);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -317,6 +324,16 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
   if (warp > kMmaWarp) {
     // ================================================================== producers: K/V blocks
     const int pt = tid - kProducer0, pw = pt >> 5;
+    if (P.q_tma && pt == 0 && nblk > 0) {
+      // the CTA's query tiles: tile x = slots s0 + x BM .. + BM - 1 of the group = tokens row0 t + (s0 + x BM) / rep ..
+      // (all heads of the GQA group per token); tokens past the last row read as zero, slots past the group's last
+      // read the next group's rows (finite; never stored)
+      mbar_arrive_expect_tx(q_full, ntiles * L::TILE);
+      for (int x = 0; x < ntiles; ++x)
+#pragma unroll
+        for (int h = 0; h < D / 64; ++h)
+          tma_load_3d(sm + L::Q(x) + h * L::ATOM, &P.map_q, q_full, h * 64, g * rep, row0 * t + (s0 + x * BM) / rep);
+    }
     const TS* ks1 = nullptr;
     const TS* vs1 = nullptr;
     const uint8_t* pm1 = nullptr;
@@ -545,17 +562,33 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
     const uint32_t tS0 = tmem + lane_off + kTmemS + x * BN;
     const uint32_t tO = tmem + lane_off + kTmemO + x * 128;
     const float scale = P.scale_log2;
-    if (x < NT) {
-      // this slot's Q row into the tile's shared-memory A operand (128-byte swizzled, K-major)
+    if (x < NT && !P.q_tma) {
+      // the warp's 32 Q rows (tile rows 32 q4 ..) into the tile's shared-memory A operand (128-byte swizzled,
+      // K-major), row by row across the warp: each load instruction reads 32 / CPR whole rows (contiguous 16-byte
+      // chunks), so every fetched line is used at once. (One thread per row, 16 strided loads each, re-fetched the
+      // lines from L2 up to 8 times once the small L1 beside ~200 KB of shared memory had evicted them.)
+      // Slots past the group's last are zero.
       uint8_t* dq = sm + L::Q(x);
-      if (my_valid) {
-        const uint4* src = reinterpret_cast<const uint4*>(
-            P.q + ((static_cast<int64_t>(row0 + a_my) * t + i_my) * P.Hq + g * rep + hh_my) * D);
+      constexpr int CPR = D / 8;                      // 16-byte chunks per row
+      constexpr int RPI = 32 / CPR;                   // rows per instruction
+      constexpr int HALF = CPR / 2;                   // loads in flight per batch
+      const int ch = lane % CPR;
 #pragma unroll
-        for (int ch = 0; ch < D / 8; ++ch) *reinterpret_cast<uint4*>(dq + swz(tt, ch, L::ATOM)) = __ldg(src + ch);
-      } else {
+      for (int b = 0; b < 2; ++b) {
+        uint4 val[HALF];
 #pragma unroll
-        for (int ch = 0; ch < D / 8; ++ch) *reinterpret_cast<uint4*>(dq + swz(tt, ch, L::ATOM)) = make_uint4(0, 0, 0, 0);
+        for (int it = 0; it < HALF; ++it) {
+          const int sl = s0 + x * BM + 32 * q4 + (b * HALF + it) * RPI + lane / CPR;
+          val[it] = make_uint4(0, 0, 0, 0);
+          if (sl < slots) {
+            const int a = sl / slots_row, i = (sl % slots_row) / rep, hh = sl % rep;
+            val[it] = __ldg(reinterpret_cast<const uint4*>(
+                              P.q + ((static_cast<int64_t>(row0 + a) * t + i) * P.Hq + g * rep + hh) * D) + ch);
+          }
+        }
+#pragma unroll
+        for (int it = 0; it < HALF; ++it)
+          *reinterpret_cast<uint4*>(dq + swz(32 * q4 + (b * HALF + it) * RPI + lane / CPR, ch, L::ATOM)) = val[it];
       }
       fence_proxy_async_smem();
       mbar_arrive(q_full);
@@ -735,13 +768,42 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
                 dst[k] = make_float4(__uint_as_float(o[4 * k]) * inv, __uint_as_float(o[4 * k + 1]) * inv,
                                      __uint_as_float(o[4 * k + 2]) * inv, __uint_as_float(o[4 * k + 3]) * inv);
             } else {
+              // bf16 O / l into this slot's row of the tile's Q buffer (free: every MMA of the tile has completed),
+              // in the same swizzled layout; the warp stores its 32 rows below, whole rows per instruction
               uint32_t w[16];
 #pragma unroll
               for (int k = 0; k < 16; ++k)
                 w[k] = pack_bf16(__uint_as_float(o[2 * k]) * inv, __uint_as_float(o[2 * k + 1]) * inv);
-              uint4* dst = reinterpret_cast<uint4*>(P.o + orow + dc * 32);
 #pragma unroll
-              for (int k = 0; k < 4; ++k) dst[k] = make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+              for (int k = 0; k < 4; ++k)
+                *reinterpret_cast<uint4*>(sm + L::Q(x) + swz(tt, dc * 4 + k, L::ATOM)) =
+                    make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+            }
+          }
+        }
+        if (P.nsplit == 1 && P.q_tma && s0 + x * BM + BM <= slots) {
+          // a full tile (every slot in the group): one TMA store per 64 columns once all 128 rows are staged
+          fence_proxy_async_smem();
+          mbar_arrive(&o_ready[x]);
+          if (q4 == 0 && lane == 0 && mbar_wait(&o_ready[x], 0, abort_flag, P.err, kErrAttn | 19)) {
+#pragma unroll
+            for (int h = 0; h < D / 64; ++h)
+              tma_store_3d(&P.map_o, sm + L::Q(x) + h * L::ATOM, h * 64, g * rep, row0 * t + (s0 + x * BM) / rep);
+            tma_store_commit();
+            tma_store_wait_read();
+          }
+        } else if (P.nsplit == 1) {
+          __syncwarp();
+          constexpr int CPR = D / 8, RPI = 32 / CPR;
+          const int ch = lane % CPR;
+#pragma unroll 4
+          for (int it = 0; it < CPR; ++it) {
+            const int rr = 32 * q4 + it * RPI + lane / CPR;
+            const int sl = s0 + x * BM + rr;
+            if (sl < slots) {
+              const int a = sl / slots_row, i = (sl % slots_row) / rep, hh = sl % rep;
+              reinterpret_cast<uint4*>(P.o + ((static_cast<int64_t>(row0 + a) * t + i) * P.Hq + g * rep + hh) * D)[ch] =
+                  *reinterpret_cast<const uint4*>(sm + L::Q(x) + swz(rr, ch, L::ATOM));
             }
           }
         }
@@ -786,6 +848,22 @@ int make_map_bf16(CUtensorMap* map, const void* base, uint64_t cols, uint64_t ro
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(OD_ECUDA, "cuTensorMapEncodeTiled (bf16) failed (%d)", static_cast<int>(r));
+  return OD_OK;
+}
+
+// (rows, Hq, D) bf16 view (q or o: token-major, heads, head_dim) tiled into 64 x rep x (BM / rep) boxes with the
+// 128-byte swizzle: a box is BM consecutive (token, head) rows of 128 bytes, the UMMA layout of a query tile
+int make_map_slots(CUtensorMap* map, const void* base, uint64_t D, uint64_t H, uint64_t rows, int rep) {
+  auto fn = encode_fn();
+  if (!fn) return fail(OD_ECUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[3] = {D, H, rows};
+  cuuint64_t strides[2] = {D * 2, H * D * 2};
+  cuuint32_t box[3] = {64, static_cast<cuuint32_t>(rep), static_cast<cuuint32_t>(BM / rep)};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(OD_ECUDA, "cuTensorMapEncodeTiled (slots) failed (%d)", static_cast<int>(r));
   return OD_OK;
 }
 
@@ -979,6 +1057,14 @@ extern "C" int od_prefix_attn(const void* q, const void* Kp, const void* Vp, con
     if (!Kq) {
       P.map_kq = P.map_ko;
       P.map_vq = P.map_vo;
+    }
+    const int64_t tokens = static_cast<int64_t>(dims.R) * dims.t;
+    if (!rc && BM % rep == 0 && tokens < (1LL << 31)) {
+      rc = make_map_slots(&P.map_q, q, static_cast<uint64_t>(dims.D), static_cast<uint64_t>(dims.Hq),
+                          static_cast<uint64_t>(tokens), rep);
+      if (!rc) rc = make_map_slots(&P.map_o, o, static_cast<uint64_t>(dims.D), static_cast<uint64_t>(dims.Hq),
+                                   static_cast<uint64_t>(tokens), rep);
+      P.q_tma = 1;
     }
     if (!rc && Kp) {
       const uint64_t prows = static_cast<uint64_t>(dims.S) * dims.Hkv * dims.T;
