@@ -191,20 +191,22 @@ class V3Trunk:
         b_cross = torch.zeros(c_pad.shape, device=dev).masked_fill(c_pad, NEG)[:, None, None, :]
         own = opt_id[:, None, :] == torch.arange(K, device=dev)[None, :, None]
         b_cls = torch.zeros(own.shape, device=dev).masked_fill(~own, NEG)[:, None]
-        X = torch.zeros(N, P, df, device=dev)
-        X[plan["rc"]] = self.mix(o_flat)
-        C = torch.zeros(N, Tc, df, device=dev)
-        C[plan["qrc"]] = self.mix(q_flat)
-        C = C * (~c_pad)[..., None]
-        x = F.linear(_scalenorm(X, p["in_norm.g"]), p["proj_option.weight"], p["proj_option.bias"])
+        # The input projections run on the real tokens only and are scattered into the padded (N, P) / (N, Tc)
+        # layouts: ScaleNorm and the projection act row by row, and a padding row (zeros in the reference) projects to
+        # the bias alone - proj_option's for option pads, proj_state's for context pads (V3.forward applies
+        # proj_state wherever the context is not question text). The padded tensors of the reference's layout
+        # (N x P x d_feat fp32, about 0.6 GB at config 4) are never built.
+        x = p["proj_option.bias"].expand(N, P, dm).clone()
+        x[plan["rc"]] = F.linear(_scalenorm(self.mix(o_flat), p["in_norm.g"]), p["proj_option.weight"],
+                                 p["proj_option.bias"])
         lpX = None
         if self.cfg.lm_feature:             # token-level log-prob feature (v3.py:666-672)
             lpX = torch.zeros(N, P, device=dev)
             lpX[plan["rc"]] = lp_flat.float()
             x = x + F.linear(lpX[..., None], p["lp_proj.weight"], p["lp_proj.bias"])
-        cin = _scalenorm(C, p["in_norm.g"])
-        c = torch.where(plan["in_q"][..., None], F.linear(cin, p["proj_question.weight"], p["proj_question.bias"]),
-                        F.linear(cin, p["proj_state.weight"], p["proj_state.bias"]))
+        c = p["proj_state.bias"].expand(N, Tc, dm).clone()
+        c[plan["qrc"]] = F.linear(_scalenorm(self.mix(q_flat), p["in_norm.g"]), p["proj_question.weight"],
+                                  p["proj_question.bias"])
         opos, cpos = plan["opos"], plan["cpos"]
         for i in range(self.cfg.decision_layers):
             L = f"layers.{i}."
