@@ -1,9 +1,10 @@
 """Requests data-parallel over the GPUs of one box: one process per GPU (torchrun), replicated weights, no
 data-path collective; the per-question probabilities are gathered once per batch over NCCL (gloo on CPU in tests).
 
-shard(): contiguous blocks balanced by request size (request_weight: characters of the state, records, prompts and
-options), so gathering in rank order restores the request order. gather_blocks(): every rank's (n_i, W_i) block when all ranks know every block's shape on the host
-(they all hold the full request list): padded to the largest, ONE all_gather_into_tensor, no host synchronisation.
+shard(): contiguous blocks balanced by request size (request_weight: words of the state, records, prompts and
+options), so gathering in rank order restores the request order. gather_blocks(): every rank's (n_i, W_i) block when
+all ranks know every block's shape on the host (they all hold the full request list): padded to the largest, ONE
+all_gather_into_tensor, no host synchronisation.
 gather_rows(): the same when the shapes are only known locally (one extra all_gather of the shapes).
 """
 from __future__ import annotations
@@ -28,13 +29,19 @@ def shard(weights, world: int) -> list[tuple[int, int]]:
     return [(bounds[i], bounds[i + 1]) for i in range(world)]
 
 
+def _words(text: str) -> int:
+    return text.count(" ") + 1 if text else 0
+
+
 def request_weight(req) -> int:
-    """What a request costs, for balancing: the characters of its state, appended records, prompts and options (a
-    proxy for their tokens that needs no tokenizer pass over every request of the global batch on every rank)."""
+    """What a request costs, for balancing: the words of its state, appended records, prompts and options - a proxy
+    for their tokens that needs no tokenizer pass over every request of the global batch on every rank (a word-level
+    tokenizer gives exactly one token per word; characters would weight a long token id or a long word more than the
+    work it causes)."""
     from .batching import state_text
-    n = len(state_text(req.state)) + len(getattr(req, "append", "") or "")
+    n = _words(state_text(req.state)) + _words(getattr(req, "append", "") or "")
     for q in req.questions:
-        n += len(q.prompt) + sum(len(o) for o in q.options)
+        n += _words(q.prompt) + sum(_words(o) for o in q.options)
     return n
 
 
