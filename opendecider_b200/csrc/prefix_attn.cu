@@ -451,14 +451,21 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
       if (lane == 0 && nblk > 0) {
         constexpr uint32_t idesc_s = idesc_bf16(BM, BN, false);
         constexpr uint32_t idesc_o = idesc_bf16(BM, D, true);
-        const uint32_t sQ = smem_u32(sm + L::Q(0));
+        // descriptors computed once; each MMA then costs its issuing thread one add and the instruction
+        static_assert(KS == 2 && VS == 2, "two stages");
+        const uint64_t qd = desc_sw128(smem_u32(sm + L::Q(0)), 16, 1024);
+        const uint64_t kd0 = desc_sw128(smem_u32(sm + L::K(0)), 16, 1024);
+        const uint64_t kd1 = desc_sw128(smem_u32(sm + L::K(1)), 16, 1024);
+        const uint64_t vd0 = desc_sw128(smem_u32(sm + L::V(0)), L::ATOM, 1024);
+        const uint64_t vd1 = desc_sw128(smem_u32(sm + L::V(1)), L::ATOM, 1024);
         auto issue_s = [&](int j) {
-          const uint32_t sK = smem_u32(sm + L::K(j % KS));
+          const uint64_t kd = (j % KS) ? kd1 : kd0;
+          const uint32_t dS = tmem + kTmemS + (j & 1) * BN;
+          mma_f16(dS, qd, kd, idesc_s, 0u);
 #pragma unroll
-          for (int kd = 0; kd < D / 16; ++kd) {
-            const uint32_t off = (kd >> 2) * L::ATOM + (kd & 3) * 32;
-            mma_f16(tmem + kTmemS + (j & 1) * BN, desc_sw128(sQ + off, 16, 1024), desc_sw128(sK + off, 16, 1024),
-                    idesc_s, kd > 0 ? 1u : 0u);
+          for (int k = 1; k < D / 16; ++k) {
+            const uint32_t off = (k >> 2) * L::ATOM + (k & 3) * 32;
+            mma_f16_accum(dS, desc_advance(qd, off), desc_advance(kd, off), idesc_s);
           }
           mma_commit(&s_full[j & 1]);
           mma_commit(&kempty[j % KS]);
@@ -476,11 +483,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
               !mbar_wait(&p_full[j & 1], (j >> 1) & 1, abort_flag, P.err, kErrAttn | 6))
             break;
           tc_fence_after();
-          const uint32_t sV = smem_u32(sm + L::V(j % VS));
+          const uint64_t vd = (j % VS) ? vd1 : vd0;
+          const uint32_t aP = tmem + kTmemS + (j & 1) * BN;
+          mma_f16_ts(tmem + kTmemO, aP, vd, idesc_o, j > 0 ? 1u : 0u);
 #pragma unroll
-          for (int kk = 0; kk < BN / 16; ++kk)
-            mma_f16_ts(tmem + kTmemO, tmem + kTmemS + (j & 1) * BN + kk * 8,
-                       desc_sw128(sV + kk * 16 * 128, L::ATOM, 1024), idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 1; kk < BN / 16; ++kk)
+            mma_f16_ts_accum(tmem + kTmemO, aP + kk * 8, desc_advance(vd, kk * 16 * 128), idesc_o);
           mma_commit(&pv_done[0]);
           mma_commit(&vempty[j % VS]);
           if (j + 2 < nblk) {
@@ -497,23 +505,31 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
     } else if (lane == 0 && nblk > 0) {
       constexpr uint32_t idesc_s = idesc_bf16(BM, BN, false);
       constexpr uint32_t idesc_o = idesc_bf16(BM, D, true);
+      // descriptors computed once; each MMA then costs its issuing thread one add and the instruction
+      static_assert(KS == 2 && VS == 2, "two stages");
+      const uint64_t qd0 = desc_sw128(smem_u32(sm + L::Q(0)), 16, 1024);
+      const uint64_t qd1 = desc_sw128(smem_u32(sm + L::Q(NT - 1)), 16, 1024);
+      const uint64_t kd0 = desc_sw128(smem_u32(sm + L::K(0)), 16, 1024);
+      const uint64_t kd1 = desc_sw128(smem_u32(sm + L::K(1)), 16, 1024);
+      const uint64_t vd0 = desc_sw128(smem_u32(sm + L::V(0)), L::ATOM, 1024);
+      const uint64_t vd1 = desc_sw128(smem_u32(sm + L::V(1)), L::ATOM, 1024);
       auto issue_s = [&](int x, int j) {
-        const uint32_t sQ = smem_u32(sm + L::Q(x));
-        const uint32_t sK = smem_u32(sm + L::K(j % KS));
+        const uint64_t qd = x ? qd1 : qd0, kd = (j % KS) ? kd1 : kd0;
+        const uint32_t dS = tmem + kTmemS + x * BN;
+        mma_f16(dS, qd, kd, idesc_s, 0u);
 #pragma unroll
-        for (int kd = 0; kd < D / 16; ++kd) {
-          const uint32_t off = (kd >> 2) * L::ATOM + (kd & 3) * 32;
-          mma_f16(tmem + kTmemS + x * BN, desc_sw128(sQ + off, 16, 1024), desc_sw128(sK + off, 16, 1024), idesc_s,
-                  kd > 0 ? 1u : 0u);
+        for (int k = 1; k < D / 16; ++k) {
+          const uint32_t off = (k >> 2) * L::ATOM + (k & 3) * 32;
+          mma_f16_accum(dS, desc_advance(qd, off), desc_advance(kd, off), idesc_s);
         }
         mma_commit(&s_full[x]);
       };
       auto issue_pv = [&](int x, int j) {
-        const uint32_t sV = smem_u32(sm + L::V(j % VS));
+        const uint64_t vd = (j % VS) ? vd1 : vd0;
+        const uint32_t dO = tmem + kTmemO + x * 128, aP = tmem + kTmemS + x * BN;
+        mma_f16_ts(dO, aP, vd, idesc_o, j > 0 ? 1u : 0u);
 #pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk)
-          mma_f16_ts(tmem + kTmemO + x * 128, tmem + kTmemS + x * BN + kk * 8,
-                     desc_sw128(sV + kk * 16 * 128, L::ATOM, 1024), idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 1; kk < BN / 16; ++kk) mma_f16_ts_accum(dO, aP + kk * 8, desc_advance(vd, kk * 16 * 128), idesc_o);
         mma_commit(&pv_done[x]);
       };
       bool live = mbar_wait(q_full, 0, abort_flag, P.err, kErrAttn | 17) &&

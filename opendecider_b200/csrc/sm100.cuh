@@ -250,6 +250,22 @@ __device__ __forceinline__ void mma_commit_pair(uint64_t* bar, uint16_t cta_mask
 }
 
 // Arrive once on `bar` when every tcgen05.mma issued so far by this thread has completed.
+// The same MMAs accumulating into D unconditionally (the enable-input-d predicate an immediate): one instruction
+// less per MMA for the single issuing thread, whose per-MMA instruction count, not the tensor core, otherwise sets
+// the rate of short (N <= 128) bf16 MMAs.
+__device__ __forceinline__ void mma_f16_accum(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc) {
+  asm volatile("tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, 1;" ::"r"(d_tmem), "l"(a_desc), "l"(b_desc),
+               "r"(idesc)
+               : "memory");
+}
+__device__ __forceinline__ void mma_f16_ts_accum(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc) {
+  asm volatile("tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, 1;" ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc),
+               "r"(idesc)
+               : "memory");
+}
+// A shared-memory descriptor advanced by `off_bytes` (a multiple of 16): the 14-bit start-address field holds
+// address >> 4, and shared-memory addresses stay below 2^18, so the addition never carries out of the field.
+__device__ __forceinline__ uint64_t desc_advance(uint64_t d, uint32_t off_bytes) { return d + (off_bytes >> 4); }
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
