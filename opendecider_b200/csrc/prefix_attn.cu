@@ -646,12 +646,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
       // P = 2^(s * scale - m) in bf16 over the S columns (P chunk c lands on columns 16c..16c+15, which hold S chunk
       // c / 2: already read), the row sum in fp32; returns the block's row max (scaled). One 32-key chunk of scores
       // in registers at a time (the kernel's 13 warps cap a thread at 128 registers).
-      float2 acc[4];                                   // four partial sums and maxima: shorter dependency chains
+      float2 acc[2];
       auto p_pass = [&](float m) -> float {
         const bool none = m == -INFINITY;              // no visible key so far: every weight is 0
         const float2 sc2 = make_float2(scale, scale), nm2 = make_float2(-m, -m);
-        acc[0] = acc[1] = acc[2] = acc[3] = make_float2(0.f, 0.f);
-        float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        acc[0] = acc[1] = make_float2(0.f, 0.f);
+        float mq[2] = {-INFINITY, -INFINITY};
 #pragma unroll 1
         for (int ci = 0; ci < 4; ++ci) {
           uint32_t cc[32];
@@ -662,19 +662,19 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
 #pragma unroll
           for (int k = 0; k < 16; ++k) {
             const float e0 = __uint_as_float(cc[2 * k]), e1 = __uint_as_float(cc[2 * k + 1]);
-            mq[k & 3] = fmax3(mq[k & 3], e0, e1);
+            mq[k & 1] = fmax3(mq[k & 1], e0, e1);
             if (none) {
               pw[k] = 0u;
             } else {
               const float2 y = __ffma2_rn(make_float2(e0, e1), sc2, nm2);
               const float2 pp = make_float2(ex2_approx(y.x), ex2_approx(y.y));
-              acc[k & 3] = __fadd2_rn(acc[k & 3], pp);
+              acc[k & 1] = __fadd2_rn(acc[k & 1], pp);
               pw[k] = pack_bf16(pp.x, pp.y);
             }
           }
           tmem_st_32x32b_x16(tS + 16 * ci, pw);
         }
-        return fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])) * scale;
+        return fmaxf(mq[0], mq[1]) * scale;
       };
       // O_x may be rescaled once P_x(j-1) V_{j-1} has completed: with two tiles it did before S_x(j) was issued;
       // with one (S double-buffered) the softmax waits for it here
@@ -749,7 +749,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_attn_kernel(const __grid_c
           p_pass(m_used);
         }
       }
-      l_sum += ((acc[0].x + acc[0].y) + (acc[1].x + acc[1].y)) + ((acc[2].x + acc[2].y) + (acc[3].x + acc[3].y));
+      l_sum += (acc[0].x + acc[0].y) + (acc[1].x + acc[1].y);
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&p_full[sb]);
