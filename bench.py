@@ -238,7 +238,7 @@ class RefCpuSample:
     weights: timing only); the slope is one layer's cost and the intercept the fixed cost, extrapolated to all layers.
     The trunk reads its feature layers from the last sampled layer (same shapes and work)."""
 
-    def __init__(self, config: int, n_lo: int = 2, n_hi: int = 8, seed: int = 0):
+    def __init__(self, config: int, n_lo: int = 2, n_hi: int = 10, seed: int = 0):
         import copy
         if not reference_installed():
             raise RuntimeError("the reference package is not installed in baseline/_ref")
@@ -292,6 +292,7 @@ class RefCpuSample:
         self.n_feat = len(cfg.feature_layers)
         self.deciders = {n: self._decider(n) for n in (self.n_lo, self.n_hi)}
         self._time(self.n_lo)                          # warm-up: allocator, thread pool, kernel selection
+        self._time(self.n_hi)
 
     @staticmethod
     def _question(q) -> dict:
@@ -331,16 +332,18 @@ class RefCpuSample:
         assert len(ans) == len(self.reqs)
         return dt
 
-    def step(self):
-        """One timed sample. Returns (decisions/s of the whole-depth request, threads, description)."""
-        t_lo, t_hi = self._time(self.n_lo), self._time(self.n_hi)
+    def step(self, reps: int = 3):
+        """One timed sample: the median of `reps` timings at each depth. Returns (decisions/s of the whole-depth
+        request, threads, description)."""
+        t_lo = statistics.median(self._time(self.n_lo) for _ in range(reps))
+        t_hi = statistics.median(self._time(self.n_hi) for _ in range(reps))
         per_layer = max(0.0, (t_hi - t_lo) / max(1, self.n_hi - self.n_lo))
         fixed = max(0.0, t_lo - self.n_lo * per_layer)
         t_req = fixed + self.n_layers_total * per_layer
         desc = (f"the reference's own Decider.decide_many (baseline/_ref, stock CPU path: int8 weight-only linears, "
                 f"torch CPU attention) on 1 request ({self.nd} decisions) timed at {self.n_lo} and {self.n_hi} of "
-                f"{self.n_layers_total} decoder layers ({t_lo:.1f} s, {t_hi:.1f} s): {per_layer:.2f} s per layer + "
-                f"{fixed:.2f} s fixed, extrapolated to all layers ({t_req:.1f} s per request)")
+                f"{self.n_layers_total} decoder layers (medians of 3: {t_lo:.2f} s, {t_hi:.2f} s): {per_layer:.3f} s per "
+                f"layer + {fixed:.2f} s fixed, extrapolated to all layers ({t_req:.1f} s per request)")
         return self.nd / t_req, torch.get_num_threads(), desc
 
 
