@@ -270,12 +270,13 @@ def _flat_idx(mask: torch.Tensor) -> torch.Tensor:
 
 
 def width_chunks(lengths: torch.Tensor, chunk: int, waste: float = 0.25) -> list:
-    """Split rows sorted by length (ascending) into chunks: a new chunk starts at `chunk` rows or when padding the
-    chunk to a longer row would waste more than `waste` of its tokens. Returns [(start, end)] over the sorted rows."""
+    """Split rows sorted by length (ascending) into chunks: a new chunk starts when it would exceed `chunk` tokens
+    (rows x its width) or when padding the chunk to a longer row would waste more than `waste` of its tokens.
+    Returns [(start, end)] over the sorted rows."""
     out, a, w = [], 0, 0
     for i, L in enumerate(lengths.tolist()):
         n = i - a
-        if n and (n >= chunk or (L > w and (L - w) * n > waste * n * w)):
+        if n and ((n + 1) * max(w, L, 2) > chunk or (L > w and (L - w) * n > waste * n * w)):
             out.append((a, i))
             a, n, w = i, 0, 0
         w = max(w, L)
@@ -310,12 +311,13 @@ def lm_sources(q_tok, o_tok, lq, lo, row_q, up) -> dict:
             "lp_qsrc": up(q_start[qm] + lq[qm] - 1), "lp_tok": up(targets)}
 
 
-def plan_rows(bb: Backbone, tok, questions, T: int, qcache: bool, list_cap: int = 16, chunk: int = 4096,
+def plan_rows(bb: Backbone, tok, questions, T: int, qcache: bool, list_cap: int = 16, chunk: int = 1 << 18,
               up=None, lm: bool = False) -> RowPlan:
     """Host layout of the branched row passes. qcache: V3._branched_feats_qcache (v3.py:446-534) - one right-padded
     question pass continuing each question's state at positions T + j, capturing its K/V, then option rows of
     their own answer tokens (sorted by length, chunks as wide as their longest option, positions after their own
-    question). Otherwise V3._branched_feats (v3.py:393-444) - one row [question ; option] per option."""
+    question). Otherwise V3._branched_feats (v3.py:393-444) - one row [question ; option] per option. chunk: the most
+    tokens one row pass holds (its activations; fewer passes re-read the cached state less often)."""
     dev = bb.device
     up = up or (lambda x: x.to(dev, non_blocking=True))
     N = len(questions)
@@ -363,8 +365,9 @@ def plan_rows(bb: Backbone, tok, questions, T: int, qcache: bool, list_cap: int 
     W = ids.shape[1]
     passes = []
     o_dst_start = torch.cumsum(lo, 0) - lo
-    for a in range(0, M, chunk):
-        sl = slice(a, min(a + chunk, M))
+    rows_per = max(1, chunk // max(1, W))
+    for a in range(0, M, rows_per):
+        sl = slice(a, min(a + rows_per, M))
         R = sl.stop - sl.start
         pos = (T + torch.arange(W, dtype=torch.int32)).expand(R, W).contiguous()
         # option tokens of these rows: columns [lq, lq + lo) of each row
@@ -414,7 +417,7 @@ class V3Model:
     configuration. question_cache / qcache_min_rows: the serving switch of prepare_inference_ (decider.py:111-116)."""
 
     def __init__(self, backbone: Backbone, trunk: V3Trunk, tokenizer, list_cap: int = 16,
-                 question_cache: bool = True, qcache_min_rows: int = 12, chunk: int = 4096):
+                 question_cache: bool = True, qcache_min_rows: int = 12, chunk: int = 1 << 18):
         self.backbone, self.trunk, self.tok = backbone, trunk, tokenizer
         self.list_cap, self.question_cache, self.qcache_min_rows, self.chunk = (list_cap, question_cache,
                                                                                 qcache_min_rows, chunk)
