@@ -7,7 +7,7 @@
 namespace od {
 namespace {
 
-constexpr int kWarps = 8;
+constexpr int kWarps = 2;              // small CTAs, 16 per SM: more tokens' loads in flight per SM
 
 // The int8 KV cache rows of a pass (state pass, appended records): token tok = row r x t + j of the pass is cache
 // position t0 + j of state r. Each k / v head row is quantised per (state, head, token) over D exactly as
@@ -57,7 +57,7 @@ __device__ __forceinline__ void write_kv_unit(const uint4& w, int8_t* q8, __nv_b
 }
 
 template <int D, bool KV>
-__global__ void __launch_bounds__(32 * kWarps, 4) qk_norm_rope_kernel(
+__global__ void __launch_bounds__(32 * kWarps, 16) qk_norm_rope_kernel(
     const __nv_bfloat16* __restrict__ qkv, int64_t ld, const int32_t* __restrict__ pos,
     const __nv_bfloat16* __restrict__ cos_t, const __nv_bfloat16* __restrict__ sin_t, int64_t P,
     const __nv_bfloat16* __restrict__ qw, const __nv_bfloat16* __restrict__ kw, float eps, int64_t M, int Hq, int Hkv,
