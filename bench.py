@@ -239,7 +239,6 @@ class RefCpuSample:
     The trunk reads its feature layers from the last sampled layer (same shapes and work)."""
 
     def __init__(self, config: int, n_lo: int = 2, n_hi: int = 10, seed: int = 0):
-        import copy
         if not reference_installed():
             raise RuntimeError("the reference package is not installed in baseline/_ref")
         if REF_DIR not in sys.path:

@@ -183,7 +183,7 @@ class V3Trunk:
         q_flat (sum lq, nL*d), o_flat (sum lo, nL*d) token features; lp_flat (sum lo,) the LM log-prob of each
         option token (lm_feature). Returns logits (N, K) fp32, NEG at pads."""
         p, dev = self.p, self.device
-        h, dm, df = self.cfg.n_heads, self.cfg.d_model, self.cfg.d_feat
+        h, dm = self.cfg.n_heads, self.cfg.d_model
         N, K, P, Tc = plan["N"], plan["K"], plan["P"], plan["Tc"]
         opt_id, c_pad = plan["opt_id"], plan["c_pad"]
         x_pad = opt_id < 0
