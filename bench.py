@@ -113,14 +113,15 @@ class CpuSample:
         from oracle.model import OracleDecision
         from opendecider_b200 import synthetic as syn
         from opendecider_b200.backbone import synthetic_weights
-        from opendecider_b200.v3 import TrunkConfig, V3Trunk, trunk_state_dict
+        from opendecider_b200.v3 import TrunkConfig, trunk_state_dict
+        from oracle.trunk import OracleTrunk
         torch.set_num_threads(os.cpu_count() or 1)
         cfg, tk, qmin, _ = workload(config)
         self.cfg, self.n_layers_total = cfg, cfg.layers
         self.n_lo, self.n_hi = min(n_lo, cfg.layers), min(n_hi, cfg.layers)
         self.reqs, tok = syn.decision_requests(config, seed=seed, n_requests=1)
         tc = TrunkConfig(d_feat=cfg.hidden, n_feat_layers=len(cfg.feature_layers), **tk)
-        trunk = V3Trunk(tc, trunk_state_dict(tc, seed=0), "cpu")
+        trunk = OracleTrunk(tc, trunk_state_dict(tc, seed=0))
         sd = synthetic_weights(cfg, seed=0, layers=1)
         self.feats = cfg.feature_layers
         cfg.feature_layers = ("final",) * len(self.feats)
@@ -173,7 +174,8 @@ class CpuSampleCached:
         from oracle import ops
         from opendecider_b200 import synthetic as syn
         from opendecider_b200.backbone import synthetic_weights
-        from opendecider_b200.v3 import TrunkConfig, V3Trunk, trunk_state_dict
+        from opendecider_b200.v3 import TrunkConfig, trunk_state_dict
+        from oracle.trunk import OracleTrunk
         torch.set_num_threads(os.cpu_count() or 1)
         cfg, tk, qmin, _ = workload(5)
         self.cfg, self.n_layers_total = cfg, cfg.layers
@@ -183,7 +185,7 @@ class CpuSampleCached:
                      for k in (self.K_SMALL, self.K_LARGE)}
         self.T = len(tok([full[0].state], add_special_tokens=False)["input_ids"][0]) + 3
         tc = TrunkConfig(d_feat=cfg.hidden, n_feat_layers=len(cfg.feature_layers), **tk)
-        trunk = V3Trunk(tc, trunk_state_dict(tc, seed=0), "cpu")
+        trunk = OracleTrunk(tc, trunk_state_dict(tc, seed=0))
         sd = synthetic_weights(cfg, seed=0, layers=1)
         self.feats = cfg.feature_layers
         cfg.feature_layers = ("final",) * len(self.feats)

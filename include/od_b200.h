@@ -249,6 +249,50 @@ OD_API int od_lm_logprob(const void* h, int64_t M, int H, const void* Wb, const 
                          int vsplit, void* stream);
 
 /* ---------------------------------------------------------------------------------------------------------------
+ * A12: the V3 decision trunk in fp32 (V3.forward, v3.py:606-709). Every trunk linear (nn.Linear in fp32, v3.py's
+ * MHA :82-100 and XATGLU :53-67, the input projections) runs through od_gemm_f32 on operands held as a pair
+ * hi = x rounded to tf32, lo = x - hi ("3xTF32" on the tensor cores: fp32-level results); the kernels that produce
+ * a linear's input write that pair directly.
+ *
+ * od_split_tf32: x (M, K) fp32 (row stride ldx) -> hi, lo (M, K) (row stride ldo). Used for weights, once.
+ * od_scalenorm_split: ScaleNorm (v3.py:43-50) of each row, g * x / max(||x||_2, eps), g a device fp32 scalar; with
+ *   mix_w (n_mix fp32 weights, the softmax of layer_mix) the row is first the mix of n_mix feature layers stored
+ *   side by side (V3._mix_wide, v3.py:328-341: x = sum_l mix_w[l] * float(row[l * K:(l + 1) * K])). x in dtype
+ *   OD_BF16 / OD_F16 / OD_F32, K <= 8192. Writes hi, lo (M, K).
+ * od_gemm_f32: y[out_rows[r]] = x[r] . W^T (+ bias) (+ res[out_rows[r]]), x = x_hi + x_lo (M, K), W = w_hi + w_lo
+ *   (N, K) (nn.Linear's layout), bias (N,) or NULL, res rows at res + out_row * ldres (ldres 0: one row for every
+ *   output row; res may be y: x = x + layer(x)) or NULL, out_rows (M,) int64 or NULL (identity). K % 4 == 0; row
+ *   strides in elements, multiples of 4 for x and W; operands 16-byte aligned.
+ * od_xatglu_split: zv (M, 2F) = [wg x + bg | wv x + bv] -> the XATGLU product (v3.py:65-66)
+ *   (((atan z + pi/2) / pi) * (1 + 2a) - a) * value as hi, lo (M, F); alpha a device fp32 scalar.
+ * od_trunk_attn: scaled_dot_product_attention (v3.py:97, scale 1/sqrt(Dh)) of one MHA call with its additive mask
+ *   built from ids instead of an (N, h, P, T) tensor, q / k RoPE'd (v3.py:70-79) by positions when given:
+ *     OD_TRUNK_SELF  keys with k_grp < 0 masked, + bonus[h] where q_grp == k_grp >= 0 (the option self-attention:
+ *                    same_bias * same, masked_fill of padded keys, V3.forward :676-681)
+ *     OD_TRUNK_KEYS  keys with k_grp < 0 masked (the cross-attention to the question, c_pad)
+ *     OD_TRUNK_CLS   query i sees only keys with k_grp == i (the CLS readout of option i, :690-697)
+ *   q row (b, i) at q + b * q_bstride + i * ldq + h * Dh (q_bstride = ldq = 0: one row shared by every query),
+ *   k / v row (b, j) at + b * kv_bstride + j * ldkv + h * Dh; positions / groups (B, Lq) and (B, Lk) int32.
+ *   Output row (b, i) at o + (b * Lq + i) * ldo + h * Dh (heads side by side, the layout of the o projection's
+ *   input), as fp32 (o) and / or as the hi / lo pair. Dh in {16, 32, 64}. A query with no visible key gets zeros
+ *   (only padded CLS options, whose logits are masked).
+ */
+enum { OD_TRUNK_SELF = 0, OD_TRUNK_KEYS = 1, OD_TRUNK_CLS = 2 };
+OD_API int od_split_tf32(const float* x, int64_t ldx, int64_t M, int64_t K, float* hi, float* lo, int64_t ldo,
+                         void* stream);
+OD_API int od_scalenorm_split(const void* x, int dtype, int64_t ldx, int64_t M, int64_t K, const float* mix_w,
+                              int n_mix, const float* g, float eps, float* hi, float* lo, int64_t ldo, void* stream);
+OD_API int od_gemm_f32(const float* x_hi, const float* x_lo, int64_t ldx, const float* w_hi, const float* w_lo,
+                       int64_t ldw, const float* bias, const float* res, int64_t ldres, const int64_t* out_rows,
+                       float* y, int64_t ldy, int64_t M, int64_t N, int64_t K, void* stream);
+OD_API int od_xatglu_split(const float* zv, int64_t ldzv, int64_t M, int64_t F, const float* alpha, float* hi,
+                           float* lo, int64_t ldo, void* stream);
+OD_API int od_trunk_attn(const float* q, int64_t ldq, int64_t q_bstride, const float* k, const float* v, int64_t ldkv,
+                         int64_t kv_bstride, const int32_t* q_pos, const int32_t* k_pos, const int32_t* q_grp,
+                         const int32_t* k_grp, const float* bonus, int mode, int64_t B, int64_t Lq, int64_t Lk, int H,
+                         int Dh, float* o, float* o_hi, float* o_lo, int64_t ldo, void* stream);
+
+/* ---------------------------------------------------------------------------------------------------------------
  * A13: option readout, Decider._probs (decider.py:255-257):
  *     p[i, :] = softmax(logits[i, :] / T[i] + bias[i, :]) * mask[i, :]
  * logits (N, K) fp32, T (N) fp32, bias (N, K) fp32 or NULL, mask (N, K) uint8; probs (N, K) fp32.

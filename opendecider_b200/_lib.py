@@ -18,6 +18,7 @@ HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))
 
 OD_BF16, OD_F16, OD_F32 = 0, 1, 2
 OD_EPI_BF16, OD_EPI_SWIGLU, OD_EPI_INT32 = 0, 1, 2
+OD_TRUNK_SELF, OD_TRUNK_KEYS, OD_TRUNK_CLS = 0, 1, 2
 _DT = {torch.bfloat16: OD_BF16, torch.float16: OD_F16, torch.float32: OD_F32}
 
 
@@ -67,6 +68,15 @@ SIGNATURES = {
                       c_int64, c_int, c_void_p],
     "od_readout": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p,
                    c_void_p],
+    "od_split_tf32": [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_void_p],
+    "od_scalenorm_split": [c_void_p, c_int, c_int64, c_int64, c_int64, c_void_p, c_int, c_void_p, c_float, c_void_p,
+                           c_void_p, c_int64, c_void_p],
+    "od_gemm_f32": [c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_void_p,
+                    c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p],
+    "od_xatglu_split": [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_int64, c_void_p],
+    "od_trunk_attn": [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p,
+                      c_void_p, c_void_p, c_int, c_int64, c_int64, c_int64, c_int, c_int, c_void_p, c_void_p, c_void_p,
+                      c_int64, c_void_p],
 }
 
 _lib = None
@@ -477,6 +487,110 @@ def lm_logprob(h: torch.Tensor, Wb: torch.Tensor, qW: torch.Tensor, sW: torch.Te
     _check(load().od_lm_logprob(_p(h), M, H, _p(Wb), _p(qW), _p(sW.contiguous()), V, _p(tok.contiguous()), _p(lp),
                                 _p(ws), ws.numel() * 4, n.value, _stream(dev)), "od_lm_logprob")
     return lp
+
+
+# ------------------------------------------------------------------------------------------------ V3 trunk (fp32)
+# An fp32 GEMM operand travels as a pair (hi, lo) of (M, K) fp32 tensors with hi = x rounded to tf32 and lo = x - hi:
+# od_gemm_f32 multiplies such pairs on the tensor cores (3 tf32 products per k-step) with fp32-level accuracy.
+
+
+def _pair(M: int, K: int, dev) -> tuple:
+    return (torch.empty(M, K, dtype=torch.float32, device=dev), torch.empty(M, K, dtype=torch.float32, device=dev))
+
+
+@_probed
+def split_tf32(x: torch.Tensor) -> tuple:
+    """x (M, K) fp32 -> the operand pair (hi, lo) of gemm_f32."""
+    dev = _need_cuda(x)
+    assert x.dtype == torch.float32 and x.dim() == 2 and x.stride(1) == 1
+    M, K = x.shape
+    hi, lo = _pair(M, K, dev)
+    _check(load().od_split_tf32(_p(x), x.stride(0), M, K, _p(hi), _p(lo), K, _stream(dev)), "od_split_tf32")
+    return hi, lo
+
+
+@_probed
+def scalenorm_split(x: torch.Tensor, g: torch.Tensor, eps: float = 1e-5, mix_w: torch.Tensor | None = None) -> tuple:
+    """ScaleNorm g * x / max(||x||, eps) per row (v3.py:43-50) as an operand pair; g a 0-dim fp32 device tensor.
+    With mix_w (n,) fp32 the row is first sum_l mix_w[l] * x[:, l K:(l + 1) K] (the layer mix, v3.py:328-341).
+    x (M, K) or (M, n K) in bf16 / fp16 / fp32, rows contiguous; a 1-D x is one row."""
+    dev = _need_cuda(x, g, mix_w)
+    x2 = x.view(1, -1) if x.dim() == 1 else x
+    assert x2.stride(1) == 1 and g.dtype == torch.float32 and g.numel() == 1
+    n = 1 if mix_w is None else mix_w.numel()
+    M, K = x2.shape[0], x2.shape[1] // n
+    hi, lo = _pair(M, K, dev)
+    _check(load().od_scalenorm_split(_p(x2), _DT[x2.dtype], x2.stride(0), M, K, _p(mix_w), n, _p(g), eps, _p(hi),
+                                     _p(lo), K, _stream(dev)), "od_scalenorm_split")
+    return hi, lo
+
+
+@_probed
+def gemm_f32(x: tuple, w: tuple, bias: torch.Tensor | None = None, res: torch.Tensor | None = None,
+             out: torch.Tensor | None = None, out_rows: torch.Tensor | None = None) -> torch.Tensor:
+    """y[out_rows[r]] = x[r] . W^T (+ bias) (+ res[out_rows[r]]) in fp32: x = (hi, lo) (M, K), w = (hi, lo) (N, K)
+    (nn.Linear's layout), bias (N,), res (rows, N) - may be `out` itself (x = x + layer(x)) - or (N,) (one row for
+    every output row), out_rows (M,) int64 (default: row r). Returns out ((M, N) fp32 when not given)."""
+    xh, xl = x
+    wh, wl = w
+    dev = _need_cuda(xh, xl, wh, wl, bias, res, out, out_rows)
+    M, K = xh.shape
+    N = wh.shape[0]
+    assert xl.shape == xh.shape and xl.stride(0) == xh.stride(0) and wl.shape == wh.shape
+    assert wl.stride(0) == wh.stride(0) and wh.shape[1] == K and xh.stride(1) == 1 and wh.stride(1) == 1
+    if out is None:
+        out = torch.empty(M, N, dtype=torch.float32, device=dev)
+    assert out.dtype == torch.float32 and out.stride(-1) == 1 and out.shape[-1] == N
+    ldres = 0
+    if res is not None:
+        assert res.dtype == torch.float32 and res.stride(-1) == 1
+        ldres = 0 if res.dim() == 1 else res.stride(0)
+    if out_rows is not None:
+        assert out_rows.dtype == torch.int64 and out_rows.numel() == M
+    _check(load().od_gemm_f32(_p(xh), _p(xl), xh.stride(0), _p(wh), _p(wl), wh.stride(0), _p(bias), _p(res), ldres,
+                              _p(out_rows), _p(out), out.stride(0), M, N, K, _stream(dev)), "od_gemm_f32")
+    return out
+
+
+@_probed
+def xatglu_split(zv: torch.Tensor, alpha: torch.Tensor) -> tuple:
+    """zv (M, 2F) = [wg x + bg | wv x + bv] -> the XATGLU product (((atan z + pi/2) / pi)(1 + 2a) - a) * value
+    (v3.py:65-66) as an operand pair (M, F); alpha a 0-dim fp32 device tensor."""
+    dev = _need_cuda(zv, alpha)
+    assert zv.dtype == torch.float32 and zv.stride(1) == 1 and zv.shape[1] % 2 == 0
+    M, F = zv.shape[0], zv.shape[1] // 2
+    hi, lo = _pair(M, F, dev)
+    _check(load().od_xatglu_split(_p(zv), zv.stride(0), M, F, _p(alpha), _p(hi), _p(lo), F, _stream(dev)),
+           "od_xatglu_split")
+    return hi, lo
+
+
+@_probed
+def trunk_attn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mode: int, B: int, Lq: int, Lk: int, H: int,
+               k_grp: torch.Tensor, q_grp: torch.Tensor | None = None, bonus: torch.Tensor | None = None,
+               q_pos: torch.Tensor | None = None, k_pos: torch.Tensor | None = None, q_shared: bool = False,
+               pair: bool = True):
+    """One trunk MHA's attention (v3.py:97) with its mask from ids (od_trunk_attn): q (B * Lq, H * Dh) rows (or one
+    row shared by every query when q_shared), k / v (B * Lk, H * Dh) rows (column slices of a wider buffer allowed),
+    groups / positions (B, L) int32. Returns the output (B * Lq, H * Dh) as an operand pair (pair=True) or fp32."""
+    dev = _need_cuda(q, k, v, k_grp, q_grp, bonus, q_pos, k_pos)
+    D = q.shape[-1]
+    Dh = D // H
+    assert q.stride(-1) == 1 and k.stride(-1) == 1 and v.stride(-1) == 1 and k.stride(0) == v.stride(0)
+    for t in (k_grp, q_grp, q_pos, k_pos):
+        assert t is None or (t.dtype == torch.int32 and t.is_contiguous())
+    ldq = 0 if q_shared else q.stride(0)
+    qbs = 0 if q_shared else Lq * q.stride(0)
+    if pair:
+        o = None
+        hi, lo = _pair(B * Lq, D, dev)
+    else:
+        o = torch.empty(B * Lq, D, dtype=torch.float32, device=dev)
+        hi = lo = None
+    _check(load().od_trunk_attn(_p(q), ldq, qbs, _p(k), _p(v), k.stride(0), Lk * k.stride(0), _p(q_pos), _p(k_pos),
+                                _p(q_grp), _p(k_grp), _p(bonus), mode, B, Lq, Lk, H, Dh, _p(o), _p(hi), _p(lo), D,
+                                _stream(dev)), "od_trunk_attn")
+    return (hi, lo) if pair else o
 
 
 def selftest_bounded_wait(limit_cycles: int, device=None) -> None:

@@ -15,7 +15,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libod_b200.so")
-SOURCES = ["common.cu", "quant.cu", "rope.cu", "gemm_w8a8.cu", "prefix_attn.cu", "lm_head.cu"]
+SOURCES = ["common.cu", "quant.cu", "rope.cu", "gemm_w8a8.cu", "prefix_attn.cu", "lm_head.cu", "trunk.cu"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",

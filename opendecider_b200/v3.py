@@ -10,8 +10,8 @@ Row passes (the hot part, all in libod_b200 through Backbone.run):
                           state, used below the question-cache threshold (decider.QCACHE_MIN_ROWS).
 Trunk (small, d_model 512): V3.forward (v3.py:606-709) with the serving configuration of the shipped 9B checkpoint
 (v3_cross="question" so the trunk never reads state tokens, slot_emb="none", readout "last", no context layers) and
-a softmax layer mix of the multi-layer features. It runs as PyTorch fp32 ops on the GPU (cuBLAS for its small
-GEMMs); its parameter names are the reference V3's, so a reference checkpoint's trunk loads unchanged.
+a softmax layer mix of the multi-layer features. It runs in fp32 on the library's trunk kernels (V3Trunk); its
+parameter names are the reference V3's, so a reference checkpoint's trunk loads unchanged.
 """
 from __future__ import annotations
 
@@ -19,7 +19,6 @@ import math
 from dataclasses import dataclass
 
 import torch
-import torch.nn.functional as F
 
 from . import _lib
 from .backbone import Backbone, KVCache, PassSpec
@@ -95,139 +94,140 @@ def trunk_state_dict(cfg: TrunkConfig, seed: int = 0) -> dict:
     return sd
 
 
-def _scalenorm(x, g, eps=1e-5):
-    """ScaleNorm (v3.py:43-50): g * x / max(||x||, eps)."""
-    return g * x / x.norm(dim=-1, keepdim=True).clamp_min(eps)
-
-
-def _xatglu(p, prefix, x):
-    """First-order xATGLU (v3.py:53-67): wo(g_a(wg x) * wv x), g_a(z) = ((atan z + pi/2) / pi)(1 + 2a) - a."""
-    a = p[prefix + ".alpha"]
-    z = F.linear(x, p[prefix + ".wg.weight"], p[prefix + ".wg.bias"])
-    gate = (torch.atan(z) + math.pi / 2) / math.pi * (1 + 2 * a) - a
-    return F.linear(gate * F.linear(x, p[prefix + ".wv.weight"], p[prefix + ".wv.bias"]), p[prefix + ".wo.weight"],
-                    p[prefix + ".wo.bias"])
-
-
-def _rope_pairs(x, pos):
-    """Interleaved-pair RoPE of the trunk (v3.py:70-79), base 10000; pos (N, L) or None (= no rotation)."""
-    if pos is None:
-        return x
-    dh = x.shape[-1]
-    inv = 1.0 / (10000 ** (torch.arange(0, dh, 2, device=x.device, dtype=torch.float32) / dh))
-    ang = pos.to(x.device).float()[:, None, :, None] * inv
-    c, s = ang.cos().to(x.dtype), ang.sin().to(x.dtype)
-    x1, x2 = x[..., 0::2], x[..., 1::2]
-    return torch.stack([x1 * c - x2 * s, x1 * s + x2 * c], -1).flatten(-2)
-
-
-def _mha(p, prefix, h, x, ctx, bias, q_pos=None, k_pos=None):
-    """MHA (v3.py:82-100): RoPE'd q/k, additive float mask, SDPA."""
-    N, P, d = x.shape
-    T = ctx.shape[1]
-    dh = d // h
-    q = _rope_pairs(F.linear(x, p[prefix + ".q.weight"]).view(N, P, h, dh).transpose(1, 2), q_pos)
-    k = _rope_pairs(F.linear(ctx, p[prefix + ".k.weight"]).view(N, T, h, dh).transpose(1, 2), k_pos)
-    v = F.linear(ctx, p[prefix + ".v.weight"]).view(N, T, h, dh).transpose(1, 2)
-    o = F.scaled_dot_product_attention(q, k, v, attn_mask=bias)
-    return F.linear(o.transpose(1, 2).reshape(N, P, d), p[prefix + ".o.weight"])
+def trunk_plan(q_lens, o_lens, n_opt, state_lens, up) -> dict:
+    """Host-side layout of V3.forward (v3.py:606-662) for the state-free trunk: option-token and question-token
+    destinations, option ids and positions, masks; `up` moves each tensor where it is used. q_lens / o_lens /
+    n_opt / state_lens are CPU longs (state_lens: the real length of each question's state). The int32 copies and
+    the flat destination rows are the kernels' forms of the same layout."""
+    N = n_opt.numel()
+    K = int(n_opt.max())
+    opt_mask = torch.arange(K)[None, :] < n_opt[:, None]
+    opt_q = torch.repeat_interleave(torch.arange(N), n_opt)
+    opt_k = torch.arange(int(n_opt.sum())) - torch.repeat_interleave(torch.cumsum(n_opt, 0) - n_opt, n_opt)
+    row, col, seg, pos, row_len = segment_layout(o_lens, opt_q, N)
+    P = int(row_len.max())
+    opt_id = torch.full((N, P), -1, dtype=torch.long)
+    opt_id[row, col] = opt_k[seg]
+    opos = torch.zeros(N, P, dtype=torch.long)
+    opos[row, col] = pos
+    Tc = int(q_lens.max())
+    qrow, qcol, _, _, _ = segment_layout(q_lens, torch.arange(N), N)
+    t = torch.arange(Tc)[None, :]
+    in_q = t < q_lens[:, None]
+    cpos = t + state_lens[:, None]
+    c_pad = ~in_q
+    return {"N": N, "K": K, "P": P, "Tc": Tc, "rc": (up(row), up(col)), "qrc": (up(qrow), up(qcol)),
+            "opt_id": up(opt_id), "opos": up(opos), "in_q": up(in_q), "cpos": up(cpos), "c_pad": up(c_pad),
+            "opt_mask": up(opt_mask),
+            "rc_flat": up(row * P + col), "qrc_flat": up(qrow * Tc + qcol), "gid32": up(opt_id.int()),
+            "cgid32": up(torch.where(c_pad, -1, 0).int()), "opos32": up(opos.int()), "cpos32": up(cpos.int())}
 
 
 class V3Trunk:
-    """The decision trunk on the GPU (fp32). `params` under the reference V3 state-dict names."""
+    """The decision trunk on the GPU in fp32 (V3.forward, v3.py:606-709), every op a libod_b200 kernel:
+    od_gemm_f32 for every linear (3xTF32 operand pairs on the tensor cores; the projections that read the same input
+    stacked into one GEMM: q/k/v of the self-attention, k/v of the cross-attention and of the CLS attention, wg/wv of
+    each xATGLU), od_scalenorm_split for each ScaleNorm (with the layer mix for the input projections),
+    od_xatglu_split for the xATGLU gate, od_trunk_attn for each attention with its mask from option ids (no
+    (N, h, P, P) bias tensor). Residual adds happen in the GEMM epilogues, in place. `params` under the reference
+    V3 state-dict names."""
 
     def __init__(self, cfg: TrunkConfig, params: dict, device):
         self.cfg = cfg
-        self.p = {k: v.to(device=device, dtype=torch.float32) for k, v in params.items()}
         self.device = torch.device(device)
+        if self.device.type != "cuda":
+            raise _lib.ODError("V3Trunk runs on a CUDA device (libod_b200 has no CPU path)")
+        p = {k: v.to(device=self.device, dtype=torch.float32).contiguous() for k, v in params.items()}
+        self.p = p
 
-    def mix(self, f: torch.Tensor) -> torch.Tensor:
-        """Softmax layer mix of multi-layer token features (V3._mix_wide, v3.py:328-341): (m, nL*d) -> (m, d)."""
-        n, d = self.cfg.n_feat_layers, self.cfg.d_feat
-        if n == 1:
-            return f.float()
-        w = torch.softmax(self.p["layer_mix"].float(), 0)
-        return torch.einsum("l,mld->md", w, f.float().view(f.shape[0], n, d)).float()
+        def w(*names):
+            return _lib.split_tf32(torch.cat([p[n + ".weight"] for n in names], 0).contiguous())
+
+        def b(*names):
+            return torch.cat([p[n + ".bias"] for n in names], 0).contiguous()
+
+        self.w, self.b = {}, {}
+        for n in ("proj_option", "proj_question", "score"):
+            self.w[n] = w(n)
+        blocks = [f"layers.{i}." for i in range(cfg.decision_layers)] + [""]
+        for L in blocks:
+            ff = L + "ff" if L else "cls_ff"
+            self.w[ff + ".wgv"], self.b[ff + ".wgv"] = w(ff + ".wg", ff + ".wv"), b(ff + ".wg", ff + ".wv")
+            self.w[ff + ".wo"] = w(ff + ".wo")
+        for i in range(cfg.decision_layers):
+            L = f"layers.{i}."
+            self.w[L + "self_attn.qkv"] = w(L + "self_attn.q", L + "self_attn.k", L + "self_attn.v")
+            self.w[L + "self_attn.o"] = w(L + "self_attn.o")
+            self.w[L + "cross.q"] = w(L + "cross.q")
+            self.w[L + "cross.kv"] = w(L + "cross.k", L + "cross.v")
+            self.w[L + "cross.o"] = w(L + "cross.o")
+        self.w["cls_attn.q"] = w("cls_attn.q")
+        self.w["cls_attn.kv"] = w("cls_attn.k", "cls_attn.v")
+        self.w["cls_attn.o"] = w("cls_attn.o")
+        # the layer mix's weights, softmax(layer_mix) as V3._mix_wide (v3.py:328-341) forms them on every call
+        self.mix_w = torch.softmax(p["layer_mix"], 0).contiguous() if cfg.n_feat_layers > 1 else None
 
     def prepare(self, q_lens, o_lens, n_opt, state_lens, up=None) -> dict:
-        """Host-side layout of V3.forward (v3.py:606-662) for the state-free trunk, uploaded once: option-token and
-        question-token destinations, option ids and positions, masks and additive biases. q_lens / o_lens / n_opt /
-        state_lens are CPU longs (state_lens: the real length of each question's state)."""
-        dev = self.device
-        N = n_opt.numel()
-        K = int(n_opt.max())
-        opt_mask = torch.arange(K)[None, :] < n_opt[:, None]
-        opt_q = torch.repeat_interleave(torch.arange(N), n_opt)
-        opt_k = torch.arange(int(n_opt.sum())) - torch.repeat_interleave(torch.cumsum(n_opt, 0) - n_opt, n_opt)
-        row, col, seg, pos, row_len = segment_layout(o_lens, opt_q, N)
-        P = int(row_len.max())
-        opt_id = torch.full((N, P), -1, dtype=torch.long)
-        opt_id[row, col] = opt_k[seg]
-        opos = torch.zeros(N, P, dtype=torch.long)
-        opos[row, col] = pos
-        x_pad = opt_id < 0
-        Tc = int(q_lens.max())
-        qrow, qcol, _, _, _ = segment_layout(q_lens, torch.arange(N), N)
-        t = torch.arange(Tc)[None, :]
-        in_q = t < q_lens[:, None]
-        cpos = t + state_lens[:, None]
-        c_pad = ~in_q
-        up = up or (lambda x: x.to(dev, non_blocking=True))
-        return {"N": N, "K": K, "P": P, "Tc": Tc, "rc": (up(row), up(col)), "qrc": (up(qrow), up(qcol)),
-                "opt_id": up(opt_id), "opos": up(opos), "in_q": up(in_q), "cpos": up(cpos), "c_pad": up(c_pad),
-                "opt_mask": up(opt_mask)}
+        """trunk_plan uploaded to the trunk's device (once per plan)."""
+        return trunk_plan(q_lens, o_lens, n_opt, state_lens, up or (lambda x: x.to(self.device, non_blocking=True)))
 
     @torch.no_grad()
     def run(self, plan: dict, q_flat: torch.Tensor, o_flat: torch.Tensor, lp_flat: torch.Tensor | None = None):
         """V3.forward's device part (v3.py:627-709): option/context stacks, decision layers, CLS readout, score.
         q_flat (sum lq, nL*d), o_flat (sum lo, nL*d) token features; lp_flat (sum lo,) the LM log-prob of each
         option token (lm_feature). Returns logits (N, K) fp32, NEG at pads."""
-        p, dev = self.p, self.device
+        p, W, B = self.p, self.w, self.b
+        L_ = _lib
         h, dm = self.cfg.n_heads, self.cfg.d_model
         N, K, P, Tc = plan["N"], plan["K"], plan["P"], plan["Tc"]
-        opt_id, c_pad = plan["opt_id"], plan["c_pad"]
-        x_pad = opt_id < 0
-        same = ((opt_id[:, :, None] == opt_id[:, None, :]) & ~x_pad[:, :, None]).float()
-        b_cross = torch.zeros(c_pad.shape, device=dev).masked_fill(c_pad, NEG)[:, None, None, :]
-        own = opt_id[:, None, :] == torch.arange(K, device=dev)[None, :, None]
-        b_cls = torch.zeros(own.shape, device=dev).masked_fill(~own, NEG)[:, None]
-        # The input projections run on the real tokens only and are scattered into the padded (N, P) / (N, Tc)
-        # layouts: ScaleNorm and the projection act row by row, and a padding row (zeros in the reference) projects to
-        # the bias alone - proj_option's for option pads, proj_state's for context pads (V3.forward applies
-        # proj_state wherever the context is not question text). The padded tensors of the reference's layout
-        # (N x P x d_feat fp32, about 0.6 GB at config 4) are never built.
-        x = p["proj_option.bias"].expand(N, P, dm).clone()
-        x[plan["rc"]] = F.linear(_scalenorm(self.mix(o_flat), p["in_norm.g"]), p["proj_option.weight"],
-                                 p["proj_option.bias"])
+        gid, cgid, opos, cpos = plan["gid32"], plan["cgid32"], plan["opos32"], plan["cpos32"]
+        # The input projections run on the real tokens only and are scattered into the padded (N*P) / (N*Tc) row
+        # layouts: ScaleNorm and the projection act row by row, and a padding row (zeros in the reference) projects
+        # to the bias alone - proj_option's for option pads, proj_state's for context pads (V3.forward applies
+        # proj_state wherever the context is not question text).
+        x = p["proj_option.bias"].expand(N * P, dm).contiguous()
+        L_.gemm_f32(L_.scalenorm_split(o_flat, p["in_norm.g"], mix_w=self.mix_w), W["proj_option"],
+                    bias=p["proj_option.bias"], out=x, out_rows=plan["rc_flat"])
         lpX = None
-        if self.cfg.lm_feature:             # token-level log-prob feature (v3.py:666-672)
-            lpX = torch.zeros(N, P, device=dev)
+        if self.cfg.lm_feature:             # token-level log-prob feature (v3.py:666-672): x + lp_proj(lp)
+            lpX = torch.zeros(N, P, device=self.device)
             lpX[plan["rc"]] = lp_flat.float()
-            x = x + F.linear(lpX[..., None], p["lp_proj.weight"], p["lp_proj.bias"])
-        c = p["proj_state.bias"].expand(N, Tc, dm).clone()
-        c[plan["qrc"]] = F.linear(_scalenorm(self.mix(q_flat), p["in_norm.g"]), p["proj_question.weight"],
-                                  p["proj_question.bias"])
-        opos, cpos = plan["opos"], plan["cpos"]
+            x.add_((lpX.view(-1, 1) * p["lp_proj.weight"].view(1, -1)).add_(p["lp_proj.bias"]))
+        c = p["proj_state.bias"].expand(N * Tc, dm).contiguous()
+        L_.gemm_f32(L_.scalenorm_split(q_flat, p["in_norm.g"], mix_w=self.mix_w), W["proj_question"],
+                    bias=p["proj_question.bias"], out=c, out_rows=plan["qrc_flat"])
         for i in range(self.cfg.decision_layers):
             L = f"layers.{i}."
-            b_self = p[L + "same_bias"].view(1, h, 1, 1) * same[:, None]
-            b_self = b_self.masked_fill(x_pad[:, None, None, :], NEG)
-            hx = _scalenorm(x, p[L + "n1.g"])
-            x = x + _mha(p, L + "self_attn", h, hx, hx, b_self, opos, opos)
-            x = x + _mha(p, L + "cross", h, _scalenorm(x, p[L + "n2.g"]), _scalenorm(c, p[L + "n2c.g"]),
-                         b_cross, None, cpos)
-            x = x + _xatglu(p, L + "ff", _scalenorm(x, p[L + "n3.g"]))
-        hc = p["cls.weight"].expand(N, K, dm)
-        hc = hc + _mha(p, "cls_attn", h, _scalenorm(hc, p["cls_nq.g"]), _scalenorm(x, p["cls_nkv.g"]),
-                       b_cls, None, opos)
-        hc = hc + _xatglu(p, "cls_ff", _scalenorm(hc, p["cls_nf.g"]))
-        hc = _scalenorm(hc, p["final_norm.g"])
-        logits = F.linear(hc, p["score.weight"], p["score.bias"]).squeeze(-1).float()
+            # x = x + self_attn(n1(x)): RoPE'd within each option, + same_bias[h] between tokens of one option
+            qkv = L_.gemm_f32(L_.scalenorm_split(x, p[L + "n1.g"]), W[L + "self_attn.qkv"])
+            o = L_.trunk_attn(qkv[:, :dm], qkv[:, dm:2 * dm], qkv[:, 2 * dm:], L_.OD_TRUNK_SELF, N, P, P, h,
+                              k_grp=gid, q_grp=gid, bonus=p[L + "same_bias"], q_pos=opos, k_pos=opos)
+            L_.gemm_f32(o, W[L + "self_attn.o"], res=x, out=x)
+            # x = x + cross(n2(x), n2c(c)): the question tokens, keys RoPE'd at their positions after the state
+            qc = L_.gemm_f32(L_.scalenorm_split(x, p[L + "n2.g"]), W[L + "cross.q"])
+            kv = L_.gemm_f32(L_.scalenorm_split(c, p[L + "n2c.g"]), W[L + "cross.kv"])
+            o = L_.trunk_attn(qc, kv[:, :dm], kv[:, dm:], L_.OD_TRUNK_KEYS, N, P, Tc, h, k_grp=cgid, k_pos=cpos)
+            L_.gemm_f32(o, W[L + "cross.o"], res=x, out=x)
+            # x = x + ff(n3(x))
+            zv = L_.gemm_f32(L_.scalenorm_split(x, p[L + "n3.g"]), W[L + "ff.wgv"], bias=B[L + "ff.wgv"])
+            L_.gemm_f32(L_.xatglu_split(zv, p[L + "ff.alpha"]), W[L + "ff.wo"], bias=p[L + "ff.wo.bias"], res=x,
+                        out=x)
+        # CLS readout: every option's query is the same row (cls.weight, no RoPE); option k sees its own tokens
+        qcls = L_.gemm_f32(L_.scalenorm_split(p["cls.weight"], p["cls_nq.g"]), W["cls_attn.q"])
+        kv = L_.gemm_f32(L_.scalenorm_split(x, p["cls_nkv.g"]), W["cls_attn.kv"])
+        o = L_.trunk_attn(qcls, kv[:, :dm], kv[:, dm:], L_.OD_TRUNK_CLS, N, K, P, h, k_grp=gid, k_pos=opos,
+                          q_shared=True)
+        hc = L_.gemm_f32(o, W["cls_attn.o"], res=p["cls.weight"].view(-1))
+        zv = L_.gemm_f32(L_.scalenorm_split(hc, p["cls_nf.g"]), W["cls_ff.wgv"], bias=B["cls_ff.wgv"])
+        L_.gemm_f32(L_.xatglu_split(zv, p["cls_ff.alpha"]), W["cls_ff.wo"], bias=p["cls_ff.wo.bias"], res=hc, out=hc)
+        logits = L_.gemm_f32(L_.scalenorm_split(hc, p["final_norm.g"]), W["score"], bias=p["score.bias"]).view(N, K)
         if lpX is not None:                 # gated skip of the length-normalised log-likelihood (v3.py:702-706)
-            own_f = own.float()
+            own_f = (plan["opt_id"][:, None, :] == torch.arange(K, device=self.device)[None, :, None]).float()
             ll = (own_f * lpX[:, None, :]).sum(-1) / own_f.sum(-1).clamp_min(1)
             logits = logits + p["lm_skip"] * ll
         return logits.masked_fill(~plan["opt_mask"], NEG)
+
+
 # ------------------------------------------------------------------------------------------------ row plans
 def _rect(tok_lists, pad_id, width=None):
     lens = torch.tensor([len(t) for t in tok_lists], dtype=torch.long)

@@ -15,8 +15,8 @@ the transformers Qwen3.5 modules on a bf16 CPU model):
                  states (prefix_attn.py:102-117), else _split_attention's CPU branch per state (prefix_attn.py:58-76)
   attention      the reference's own CPU calls: torch's scaled_dot_product_attention (its flash kernel on the CPU) for
                  the state pass and the one-call path, so the oracle equals the reference bit for bit end to end
-  trunk/readout  the trunk of opendecider_b200.v3 on the CPU (plain PyTorch, the same code the GPU path runs, pinned
-                 to the reference by tests/golden/e2e_config1.npz) and Decider._probs' softmax (decider.py:255-257)
+  trunk/readout  oracle/trunk.py's fp32 restatement of the V3 trunk (pinned to the reference by
+                 tests/golden/e2e_config1.npz) and Decider._probs' softmax (decider.py:255-257)
 Only tests/, __graft_entry__.smoke() and bench.py (cpu_baseline, --impl reference) may import this module.
 """
 from __future__ import annotations

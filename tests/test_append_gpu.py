@@ -115,9 +115,10 @@ def _flat(ans):
 
 def test_append_decisions_match_oracle(cuda):
     from oracle.model import OracleDecision
+    from oracle.trunk import OracleTrunk
     cfg, reqs, tok, dec = make(cuda)
     tc = TrunkConfig(d_feat=cfg.hidden, n_feat_layers=len(FEATURE_LAYERS), **TRUNK)
-    od = OracleDecision(cfg, synthetic_weights(cfg, seed=0), V3Trunk(tc, trunk_state_dict(tc, seed=0), "cpu"), tok,
+    od = OracleDecision(cfg, synthetic_weights(cfg, seed=0), OracleTrunk(tc, trunk_state_dict(tc, seed=0)), tok,
                         TEMPS, TEMPERATURE, qcache_min_rows=32)
     nxt, _, _ = od.append_pass(od.state_pass([r.state for r in reqs]), [r.append for r in reqs])
     _, ren, pn, _ = od.decide(reqs, prebuilt=nxt)

@@ -13,6 +13,7 @@ import pytest
 import torch
 
 from oracle.model import OracleDecision, sdpa_exp_variant
+from oracle.trunk import OracleTrunk
 from opendecider_b200 import synthetic as syn
 from opendecider_b200.backbone import Backbone, DecoderConfig, synthetic_weights
 from opendecider_b200.decider import Decider
@@ -35,7 +36,7 @@ def test_nine_b_width_two_layers_matches_oracle(cuda):
     dec = Decider(V3Model(Backbone.from_float_weights(cfg, sd, cuda), V3Trunk(tc, sd_trunk, cuda), tok,
                           qcache_min_rows=12), TEMPERATURE, TEMPS)
     ans = dec.decide_many(reqs)
-    od = OracleDecision(cfg, sd, V3Trunk(tc, sd_trunk, "cpu"), tok, TEMPS, TEMPERATURE, qcache_min_rows=12)
+    od = OracleDecision(cfg, sd, OracleTrunk(tc, sd_trunk), tok, TEMPS, TEMPERATURE, qcache_min_rows=12)
     _, ren, pn, _ = od.decide(reqs)
     od.sdpa = sdpa_exp_variant
     _, ren_x, pn_x, _ = od.decide(reqs)

@@ -151,6 +151,7 @@ def test_edge_cases_match_reference(cuda):
     sys.path.insert(0, "tests/golden")
     from make_golden_edge import NAMES, edge_requests
     from oracle.model import OracleDecision, sdpa_exp_variant
+    from oracle.trunk import OracleTrunk
     from opendecider_b200.backbone import synthetic_weights
     g = np.load("tests/golden/edge_cases.npz")
     dec, _ = make_decider(cuda, True)
@@ -161,7 +162,7 @@ def test_edge_cases_match_reference(cuda):
     assert "none" not in got["big"]                              # 255 options: no none option
     cfg = DecoderConfig.tiny(feature_layers=FEATURE_LAYERS)
     tc = TrunkConfig(d_feat=cfg.hidden, n_feat_layers=len(FEATURE_LAYERS), **TRUNK)
-    od = OracleDecision(cfg, synthetic_weights(cfg, seed=0), V3Trunk(tc, trunk_state_dict(tc, seed=0), "cpu"),
+    od = OracleDecision(cfg, synthetic_weights(cfg, seed=0), OracleTrunk(tc, trunk_state_dict(tc, seed=0)),
                         syn.SyntheticTokenizer(cfg.vocab), TEMPS, 1.419344425201416, qcache_min_rows=32,
                         sdpa=sdpa_exp_variant)
     _, ren_x, pn_x, _ = od.decide(edge_requests())

@@ -12,9 +12,10 @@ tensor-core kernel, cannot be held to 1e-3 there."""
 import numpy as np
 
 from oracle.model import OracleDecision
+from oracle.trunk import OracleTrunk
 from opendecider_b200 import synthetic as syn
 from opendecider_b200.backbone import DecoderConfig, synthetic_weights
-from opendecider_b200.v3 import TrunkConfig, V3Trunk, trunk_state_dict
+from opendecider_b200.v3 import TrunkConfig, trunk_state_dict
 
 FEATURE_LAYERS = (1, 3, "final")
 TRUNK = dict(d_model=64, n_heads=4, decision_layers=2)
@@ -24,7 +25,7 @@ TEMPS = {"choice": 1.4978350400924683, "noul": 1.2169979810714722, "score": 1.52
 def test_oracle_decide_matches_reference():
     cfg = DecoderConfig.tiny(feature_layers=FEATURE_LAYERS)
     tc = TrunkConfig(d_feat=cfg.hidden, n_feat_layers=len(FEATURE_LAYERS), **TRUNK)
-    trunk = V3Trunk(tc, trunk_state_dict(tc, seed=0), "cpu")
+    trunk = OracleTrunk(tc, trunk_state_dict(tc, seed=0))
     reqs, tok = syn.decision_requests(1, seed=0)
     od = OracleDecision(cfg, synthetic_weights(cfg, seed=0), trunk, tok, TEMPS, 1.419344425201416,
                         qcache_min_rows=32)
@@ -42,7 +43,7 @@ def test_oracle_lm_feature_matches_reference():
     1.2e-2 on this case, so the check discriminates)."""
     cfg = DecoderConfig.tiny(feature_layers=FEATURE_LAYERS)
     tc = TrunkConfig(d_feat=cfg.hidden, n_feat_layers=len(FEATURE_LAYERS), lm_feature=True, **TRUNK)
-    trunk = V3Trunk(tc, trunk_state_dict(tc, seed=0), "cpu")
+    trunk = OracleTrunk(tc, trunk_state_dict(tc, seed=0))
     reqs, tok = syn.decision_requests(1, seed=0)
     od = OracleDecision(cfg, synthetic_weights(cfg, seed=0), trunk, tok, TEMPS, 1.419344425201416,
                         qcache_min_rows=32)
@@ -60,7 +61,7 @@ def _edge_oracle(sdpa=None):
     from make_golden_edge import NAMES, edge_requests
     cfg = DecoderConfig.tiny(feature_layers=FEATURE_LAYERS)
     tc = TrunkConfig(d_feat=cfg.hidden, n_feat_layers=len(FEATURE_LAYERS), **TRUNK)
-    trunk = V3Trunk(tc, trunk_state_dict(tc, seed=0), "cpu")
+    trunk = OracleTrunk(tc, trunk_state_dict(tc, seed=0))
     tok = syn.SyntheticTokenizer(cfg.vocab)
     od = OracleDecision(cfg, synthetic_weights(cfg, seed=0), trunk, tok, TEMPS, 1.419344425201416,
                         qcache_min_rows=32, sdpa=sdpa)
@@ -102,7 +103,7 @@ def test_oracle_smoothquant_matches_reference():
     assert len(scales) == 28                               # 7 linears x 4 layers, each its own vector
     cfg = DecoderConfig.tiny(feature_layers=FEATURE_LAYERS)
     tc = TrunkConfig(d_feat=cfg.hidden, n_feat_layers=len(FEATURE_LAYERS), **TRUNK)
-    trunk = V3Trunk(tc, trunk_state_dict(tc, seed=0), "cpu")
+    trunk = OracleTrunk(tc, trunk_state_dict(tc, seed=0))
     reqs, tok = syn.decision_requests(1, seed=0)
     od = OracleDecision(cfg, synthetic_weights(cfg, seed=0), trunk, tok, TEMPS, 1.419344425201416,
                         qcache_min_rows=32, smooth=scales)

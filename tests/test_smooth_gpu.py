@@ -16,6 +16,7 @@ import torch
 
 from oracle import ops
 from oracle.model import OracleDecision
+from oracle.trunk import OracleTrunk
 from opendecider_b200 import synthetic as syn
 from opendecider_b200.backbone import Backbone, DecoderConfig, synthetic_weights
 from opendecider_b200.decider import Decider
@@ -49,7 +50,7 @@ def _deciders(cuda, smooth):
     bb = Backbone.from_float_weights(cfg, sd, cuda, smooth=smooth)
     dec = Decider(V3Model(bb, V3Trunk(tc, trunk_state_dict(tc, seed=0), cuda), tok, qcache_min_rows=32),
                   TEMPERATURE, TEMPS)
-    od = OracleDecision(cfg, sd, V3Trunk(tc, trunk_state_dict(tc, seed=0), "cpu"), tok, TEMPS, TEMPERATURE,
+    od = OracleDecision(cfg, sd, OracleTrunk(tc, trunk_state_dict(tc, seed=0)), tok, TEMPS, TEMPERATURE,
                         qcache_min_rows=32, smooth=smooth)
     return dec, od, reqs
 
