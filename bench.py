@@ -577,6 +577,83 @@ def op_attn_state(args):
                           "frac_bf16": flops / tm / 1e12 / peaks.get("bf16_tflops", 1590.0), "gbs": byts / tm / 1e9}))
 
 
+def op_trunk(args):
+    """The V3 trunk's kernels at the config-4 trunk shapes (d_model 512, 8 heads, xATGLU width 1368, features 4096):
+    od_gemm_f32 (3xTF32: three tf32 tensor-core products per fp32 product; `tf32_frac` = 3 x 2MNK / t against half the
+    measured bf16 burst rate, the tf32 dense rate of B200) beside PyTorch's fp32 GEMM on the same operands (cuBLAS,
+    TF32 off), and od_trunk_attn on the option self-attention (192 questions x 200 option-token slots) beside PyTorch's
+    SDPA with the materialised (N, h, P, P) float mask it replaces. L2 flushed between launches."""
+    from opendecider_b200 import _lib
+    dev = torch.device("cuda", 0)
+    tf32_peak = 0.5 * _peaks().get("bf16_tflops", 1590.0)
+    flush = torch.zeros(64 << 20, dtype=torch.float32, device=dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    torch.backends.cuda.matmul.allow_tf32 = False
+
+    def timed(fn):
+        ts = []
+        for i in range(args.warmup + args.steps):
+            _flush_l2(flush)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize()
+            if i >= args.warmup:
+                ts.append(a.elapsed_time(b))
+        return statistics.median(ts) / 1e3
+
+    shapes = [tuple(int(v) for v in x.split("x")) for x in args.shapes.split(",")] if args.shapes else \
+        [(16384, 512, 4096), (38400, 1536, 512), (38400, 2736, 512), (38400, 512, 1368)]
+    for (M, N, K) in shapes:
+        x = torch.randn(M, K, generator=g, device=dev)
+        w = torch.randn(N, K, generator=g, device=dev) / K ** 0.5
+        b = torch.randn(N, generator=g, device=dev)
+        xp, wp = _lib.split_tf32(x), _lib.split_tf32(w)
+        y = torch.empty(M, N, device=dev)
+        t = timed(lambda: _lib.gemm_f32(xp, wp, bias=b, out=y))
+        tl = timed(lambda: torch.nn.functional.linear(x, w, b))
+        fl = 2.0 * M * N * K
+        print(json.dumps({"op": "gemm_f32", "shape": {"M": M, "N": N, "K": K}, "ms": t * 1e3,
+                          "fp32_tflops": fl / t / 1e12, "tf32_tflops": 3 * fl / t / 1e12,
+                          "tf32_frac": 3 * fl / t / 1e12 / tf32_peak, "torch_fp32_ms": tl * 1e3}))
+    B, P, H, Dh = 192, 200, 8, 64
+    D = H * Dh
+    gid = torch.full((B, P), -1, dtype=torch.int32)
+    gc = torch.Generator().manual_seed(0)
+    for q in range(B):
+        c = 0
+        for k in range(17):
+            n = int(torch.randint(1, 12, (1,), generator=gc))
+            if c + n > P:
+                break
+            gid[q, c:c + n] = k
+            c += n
+    gid_d = gid.to(dev)
+    qkv = torch.randn(B * P, 3 * D, generator=g, device=dev)
+    bonus = torch.randn(H, generator=g, device=dev)
+    olen = (gid >= 0).sum(1).int().to(dev)
+    t = timed(lambda: _lib.trunk_attn(qkv[:, :D], qkv[:, D:2 * D], qkv[:, 2 * D:], _lib.OD_TRUNK_SELF, B, P, P, H,
+                                      k_grp=gid_d, q_grp=gid_d, bonus=bonus))
+    t_len = timed(lambda: _lib.trunk_attn(qkv[:, :D], qkv[:, D:2 * D], qkv[:, 2 * D:], _lib.OD_TRUNK_SELF, B, P, P,
+                                          H, k_grp=gid_d, q_grp=gid_d, bonus=bonus, q_len=olen, k_len=olen))
+    gl = gid_d.long()
+    x_pad = gl < 0
+    same = ((gl[:, :, None] == gl[:, None, :]) & ~x_pad[:, :, None]).float()
+    q4 = qkv.view(B, P, 3, H, Dh)
+
+    def sdpa():
+        bias = (bonus.view(1, H, 1, 1) * same[:, None]).masked_fill(x_pad[:, None, None, :], -1e9)
+        return torch.nn.functional.scaled_dot_product_attention(q4[:, :, 0].transpose(1, 2), q4[:, :, 1].transpose(1, 2),
+                                                                q4[:, :, 2].transpose(1, 2), attn_mask=bias)
+    ts_ = timed(sdpa)
+    fl = 4.0 * B * H * P * P * Dh
+    print(json.dumps({"op": "trunk_attn_self", "shape": {"questions": B, "P": P, "heads": H, "Dh": Dh},
+                      "ms": t * 1e3, "tflops": fl / t / 1e12, "ms_with_row_lengths": t_len * 1e3,
+                      "torch_sdpa_with_mask_ms": ts_ * 1e3}))
+    assert _lib.device_error(dev) == 0, "a kernel reported a device-side error"
+
+
 def op_rows(args):
     """The bandwidth-bound row kernels of a decoder layer at the 9B widths (hidden 4096, 32 / 8 heads, D 128, SwiGLU
     12288) over M tokens (default 131072, one state-pass chunk): GB/s of each kernel's algorithmic bytes (every input
@@ -682,7 +759,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--lm-feature", action="store_true",
                     help="the trunk's LM log-prob feature on (v3_lm_feature, as in the shipped 9B checkpoint)")
-    ap.add_argument("--op", default="decide", choices=["decide", "gemm", "attn", "attn_state", "lm_logprob", "rows"],
+    ap.add_argument("--op", default="decide",
+                    choices=["decide", "gemm", "attn", "attn_state", "lm_logprob", "rows", "trunk"],
                     help="decide: the headline decision throughput; gemm / attn: operator configs 2 / 3; "
                          "attn_state: the state pass's causal attention")
     ap.add_argument("--shapes", default="", help="--op gemm: MxNxK list; --op attn: requestsxrowsxt list; "
@@ -701,6 +779,8 @@ def main():
         return op_lm_logprob(args)
     if args.op == "rows":
         return op_rows(args)
+    if args.op == "trunk":
+        return op_trunk(args)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))

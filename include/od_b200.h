@@ -261,21 +261,26 @@ OD_API int od_lm_logprob(const void* h, int64_t M, int H, const void* Wb, const 
  *   OD_BF16 / OD_F16 / OD_F32, K <= 8192. Writes hi, lo (M, K).
  * od_gemm_f32: y[out_rows[r]] = x[r] . W^T (+ bias) (+ res[out_rows[r]]), x = x_hi + x_lo (M, K), W = w_hi + w_lo
  *   (N, K) (nn.Linear's layout), bias (N,) or NULL, res rows at res + out_row * ldres (ldres 0: one row for every
- *   output row; res may be y: x = x + layer(x)) or NULL, out_rows (M,) int64 or NULL (identity). K % 4 == 0; row
+ *   output row; res may be y: x = x + layer(x)) or NULL, out_rows (M,) int64 or NULL (identity). With rope_pos (M,)
+ *   int32 the columns [0, rope_cols) - the q and / or k of MHA's projections - leave RoPE'd (v3.py:70-79) at row r's
+ *   position: pairs (2i, 2i+1) of each rope_dh-wide head rotated by the angle fp32(pos * rope_inv[i]), rope_inv
+ *   (rope_dh / 2,) fp32 = 1 / 10000^(2i / rope_dh) as the reference's formula evaluates it. K % 4 == 0; row
  *   strides in elements, multiples of 4 for x and W; operands 16-byte aligned.
  * od_xatglu_split: zv (M, 2F) = [wg x + bg | wv x + bv] -> the XATGLU product (v3.py:65-66)
  *   (((atan z + pi/2) / pi) * (1 + 2a) - a) * value as hi, lo (M, F); alpha a device fp32 scalar.
  * od_trunk_attn: scaled_dot_product_attention (v3.py:97, scale 1/sqrt(Dh)) of one MHA call with its additive mask
- *   built from ids instead of an (N, h, P, T) tensor, q / k RoPE'd (v3.py:70-79) by positions when given:
+ *   built from ids instead of an (N, h, P, T) tensor; q and k arrive RoPE'd (od_gemm_f32's rope_pos):
  *     OD_TRUNK_SELF  keys with k_grp < 0 masked, + bonus[h] where q_grp == k_grp >= 0 (the option self-attention:
  *                    same_bias * same, masked_fill of padded keys, V3.forward :676-681)
  *     OD_TRUNK_KEYS  keys with k_grp < 0 masked (the cross-attention to the question, c_pad)
  *     OD_TRUNK_CLS   query i sees only keys with k_grp == i (the CLS readout of option i, :690-697)
  *   q row (b, i) at q + b * q_bstride + i * ldq + h * Dh (q_bstride = ldq = 0: one row shared by every query),
- *   k / v row (b, j) at + b * kv_bstride + j * ldkv + h * Dh; positions / groups (B, Lq) and (B, Lk) int32.
+ *   k / v row (b, j) at + b * kv_bstride + j * ldkv + h * Dh; groups (B, Lq) and (B, Lk) int32.
  *   Output row (b, i) at o + (b * Lq + i) * ldo + h * Dh (heads side by side, the layout of the o projection's
- *   input), as fp32 (o) and / or as the hi / lo pair. Dh in {16, 32, 64}. A query with no visible key gets zeros
- *   (only padded CLS options, whose logits are masked).
+ *   input), as fp32 (o) and / or as the hi / lo pair. Dh in {16, 32, 64}. q_len / k_len (B,) int32 or NULL: the
+ *   real queries / keys of each batch row are a prefix of that length (the rest padding: keys past k_len are not
+ *   read, queries past q_len get zeros - the reference computes values there that reach no logit). A query with no
+ *   visible key gets zeros (only padded CLS options, whose logits are masked).
  */
 enum { OD_TRUNK_SELF = 0, OD_TRUNK_KEYS = 1, OD_TRUNK_CLS = 2 };
 OD_API int od_split_tf32(const float* x, int64_t ldx, int64_t M, int64_t K, float* hi, float* lo, int64_t ldo,
@@ -284,13 +289,14 @@ OD_API int od_scalenorm_split(const void* x, int dtype, int64_t ldx, int64_t M, 
                               int n_mix, const float* g, float eps, float* hi, float* lo, int64_t ldo, void* stream);
 OD_API int od_gemm_f32(const float* x_hi, const float* x_lo, int64_t ldx, const float* w_hi, const float* w_lo,
                        int64_t ldw, const float* bias, const float* res, int64_t ldres, const int64_t* out_rows,
-                       float* y, int64_t ldy, int64_t M, int64_t N, int64_t K, void* stream);
+                       const int32_t* rope_pos, const float* rope_inv, int rope_cols, int rope_dh, float* y,
+                       int64_t ldy, int64_t M, int64_t N, int64_t K, void* stream);
 OD_API int od_xatglu_split(const float* zv, int64_t ldzv, int64_t M, int64_t F, const float* alpha, float* hi,
                            float* lo, int64_t ldo, void* stream);
 OD_API int od_trunk_attn(const float* q, int64_t ldq, int64_t q_bstride, const float* k, const float* v, int64_t ldkv,
-                         int64_t kv_bstride, const int32_t* q_pos, const int32_t* k_pos, const int32_t* q_grp,
-                         const int32_t* k_grp, const float* bonus, int mode, int64_t B, int64_t Lq, int64_t Lk, int H,
-                         int Dh, float* o, float* o_hi, float* o_lo, int64_t ldo, void* stream);
+                         int64_t kv_bstride, const int32_t* q_grp, const int32_t* k_grp, const float* bonus,
+                         const int32_t* q_len, const int32_t* k_len, int mode, int64_t B, int64_t Lq, int64_t Lk,
+                         int H, int Dh, float* o, float* o_hi, float* o_lo, int64_t ldo, void* stream);
 
 /* ---------------------------------------------------------------------------------------------------------------
  * A13: option readout, Decider._probs (decider.py:255-257):

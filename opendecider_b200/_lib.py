@@ -72,7 +72,7 @@ SIGNATURES = {
     "od_scalenorm_split": [c_void_p, c_int, c_int64, c_int64, c_int64, c_void_p, c_int, c_void_p, c_float, c_void_p,
                            c_void_p, c_int64, c_void_p],
     "od_gemm_f32": [c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_void_p,
-                    c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p],
+                    c_void_p, c_void_p, c_int, c_int, c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p],
     "od_xatglu_split": [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_int64, c_void_p],
     "od_trunk_attn": [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p,
                       c_void_p, c_void_p, c_int, c_int64, c_int64, c_int64, c_int, c_int, c_void_p, c_void_p, c_void_p,
@@ -527,13 +527,17 @@ def scalenorm_split(x: torch.Tensor, g: torch.Tensor, eps: float = 1e-5, mix_w: 
 
 @_probed
 def gemm_f32(x: tuple, w: tuple, bias: torch.Tensor | None = None, res: torch.Tensor | None = None,
-             out: torch.Tensor | None = None, out_rows: torch.Tensor | None = None) -> torch.Tensor:
+             out: torch.Tensor | None = None, out_rows: torch.Tensor | None = None,
+             rope_pos: torch.Tensor | None = None, rope_inv: torch.Tensor | None = None,
+             rope_cols: int = 0) -> torch.Tensor:
     """y[out_rows[r]] = x[r] . W^T (+ bias) (+ res[out_rows[r]]) in fp32: x = (hi, lo) (M, K), w = (hi, lo) (N, K)
     (nn.Linear's layout), bias (N,), res (rows, N) - may be `out` itself (x = x + layer(x)) - or (N,) (one row for
-    every output row), out_rows (M,) int64 (default: row r). Returns out ((M, N) fp32 when not given)."""
+    every output row), out_rows (M,) int64 (default: row r). rope_pos (M,) int32 with rope_inv (dh / 2,) fp32 (the
+    frequencies, rope_table()): columns [0, rope_cols) leave RoPE'd in dh-wide heads (v3.py:70-79). Returns out
+    ((M, N) fp32 when not given)."""
     xh, xl = x
     wh, wl = w
-    dev = _need_cuda(xh, xl, wh, wl, bias, res, out, out_rows)
+    dev = _need_cuda(xh, xl, wh, wl, bias, res, out, out_rows, rope_pos, rope_inv)
     M, K = xh.shape
     N = wh.shape[0]
     assert xl.shape == xh.shape and xl.stride(0) == xh.stride(0) and wl.shape == wh.shape
@@ -547,9 +551,22 @@ def gemm_f32(x: tuple, w: tuple, bias: torch.Tensor | None = None, res: torch.Te
         ldres = 0 if res.dim() == 1 else res.stride(0)
     if out_rows is not None:
         assert out_rows.dtype == torch.int64 and out_rows.numel() == M
+    rope_dh = 0
+    if rope_pos is not None:
+        assert rope_pos.dtype == torch.int32 and rope_pos.is_contiguous() and rope_pos.numel() == M
+        assert rope_inv is not None and rope_inv.dtype == torch.float32 and rope_inv.is_contiguous()
+        rope_dh = 2 * rope_inv.numel()
     _check(load().od_gemm_f32(_p(xh), _p(xl), xh.stride(0), _p(wh), _p(wl), wh.stride(0), _p(bias), _p(res), ldres,
-                              _p(out_rows), _p(out), out.stride(0), M, N, K, _stream(dev)), "od_gemm_f32")
+                              _p(out_rows), _p(rope_pos), _p(rope_inv), rope_cols, rope_dh, _p(out), out.stride(0),
+                              M, N, K, _stream(dev)), "od_gemm_f32")
     return out
+
+
+def rope_table(dh: int, device) -> torch.Tensor:
+    """The trunk RoPE's frequencies 1 / 10000^(2i / dh), i < dh / 2, evaluated in fp32 by torch on the host exactly
+    as the reference's rope() writes them (v3.py:75), for gemm_f32's RoPE epilogue."""
+    inv = 1.0 / (10000 ** (torch.arange(0, dh, 2, dtype=torch.float32) / dh))
+    return inv.to(device)
 
 
 @_probed
@@ -568,16 +585,17 @@ def xatglu_split(zv: torch.Tensor, alpha: torch.Tensor) -> tuple:
 @_probed
 def trunk_attn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mode: int, B: int, Lq: int, Lk: int, H: int,
                k_grp: torch.Tensor, q_grp: torch.Tensor | None = None, bonus: torch.Tensor | None = None,
-               q_pos: torch.Tensor | None = None, k_pos: torch.Tensor | None = None, q_shared: bool = False,
+               q_shared: bool = False, q_len: torch.Tensor | None = None, k_len: torch.Tensor | None = None,
                pair: bool = True):
     """One trunk MHA's attention (v3.py:97) with its mask from ids (od_trunk_attn): q (B * Lq, H * Dh) rows (or one
     row shared by every query when q_shared), k / v (B * Lk, H * Dh) rows (column slices of a wider buffer allowed),
-    groups / positions (B, L) int32. Returns the output (B * Lq, H * Dh) as an operand pair (pair=True) or fp32."""
-    dev = _need_cuda(q, k, v, k_grp, q_grp, bonus, q_pos, k_pos)
+    q and k already RoPE'd, groups (B, L) int32, q_len / k_len (B,) int32 the real (prefix) lengths or None. Returns
+    the output (B * Lq, H * Dh) as an operand pair (pair=True) or fp32; padding queries get zeros."""
+    dev = _need_cuda(q, k, v, k_grp, q_grp, bonus, q_len, k_len)
     D = q.shape[-1]
     Dh = D // H
     assert q.stride(-1) == 1 and k.stride(-1) == 1 and v.stride(-1) == 1 and k.stride(0) == v.stride(0)
-    for t in (k_grp, q_grp, q_pos, k_pos):
+    for t in (k_grp, q_grp, q_len, k_len):
         assert t is None or (t.dtype == torch.int32 and t.is_contiguous())
     ldq = 0 if q_shared else q.stride(0)
     qbs = 0 if q_shared else Lq * q.stride(0)
@@ -587,8 +605,9 @@ def trunk_attn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mode: int, B: 
     else:
         o = torch.empty(B * Lq, D, dtype=torch.float32, device=dev)
         hi = lo = None
-    _check(load().od_trunk_attn(_p(q), ldq, qbs, _p(k), _p(v), k.stride(0), Lk * k.stride(0), _p(q_pos), _p(k_pos),
-                                _p(q_grp), _p(k_grp), _p(bonus), mode, B, Lq, Lk, H, Dh, _p(o), _p(hi), _p(lo), D,
+    _check(load().od_trunk_attn(_p(q), ldq, qbs, _p(k), _p(v), k.stride(0), Lk * k.stride(0), _p(q_grp),
+                                _p(k_grp), _p(bonus), _p(q_len), _p(k_len), mode, B, Lq, Lk, H, Dh, _p(o), _p(hi),
+                                _p(lo), D,
                                 _stream(dev)), "od_trunk_attn")
     return (hi, lo) if pair else o
 

@@ -51,6 +51,9 @@ struct GemmF32Args {
   const float* res;          // residual rows (row r at res + out_row(r) * ldres; ldres 0 = one broadcast row) or null
   int64_t ldres;
   const int64_t* out_rows;   // (M,) output row of each x row, or null (identity)
+  const int32_t* rope_pos;   // (M,) RoPE position of each x row, or null
+  const float* rope_inv;     // (rope_dh / 2,) the rotation frequencies 1 / 10000^(2i / rope_dh)
+  int rope_cols, rope_dh;    // columns [0, rope_cols) rotated in pairs (2i, 2i+1) of rope_dh-wide heads
   int M, N, K;
   int vec;                   // y / res rows allow 16-byte accesses
 };
@@ -69,9 +72,11 @@ __global__ void __launch_bounds__(kFThreads, 1)
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
+  __shared__ float rope_inv[64];                     // the RoPE epilogue's frequencies
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_n = (a.N + FB - 1) / FB, num_kb = (a.K + FK - 1) / FK;
   const int num_tiles = ((a.M + FB - 1) / FB) * num_n;
+  if (a.rope_pos && static_cast<int>(threadIdx.x) < a.rope_dh / 2) rope_inv[threadIdx.x] = a.rope_inv[threadIdx.x];
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < F_STAGES; ++s) {
@@ -187,6 +192,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
       const int m0 = (tile / num_n) * FB, n0 = (tile % num_n) * FB;
       const int row = m0 + quarter * 32 + lane;
       const int64_t orow = row < a.M ? (a.out_rows ? a.out_rows[row] : row) : -1;
+      const float rpos = a.rope_pos && row < a.M ? static_cast<float>(a.rope_pos[row]) : 0.f;
       const uint32_t tb = tmem_base + acc * FB + (static_cast<uint32_t>(quarter * 32) << 16);
 #pragma unroll 1
       for (int c = 0; c < FB / 32; ++c) {
@@ -209,6 +215,16 @@ __global__ void __launch_bounds__(kFThreads, 1)
 #pragma unroll
               for (int i = 0; i < 4; ++i)
                 if (col + i < a.N) v[i] = __fadd_rn(v[i], __ldg(a.bias + col + i));
+            }
+            if (a.rope_pos && col < a.rope_cols) {   // RoPE (v3.py:70-79) of the pairs (col, col+1), (col+2, col+3)
+#pragma unroll
+              for (int i = 0; i < 4; i += 2) {
+                const float ang = __fmul_rn(rpos, rope_inv[((col + i) % a.rope_dh) >> 1]);
+                const float cs = cosf(ang), sn = sinf(ang);
+                const float x1 = v[i], x2 = v[i + 1];
+                v[i] = __fsub_rn(__fmul_rn(x1, cs), __fmul_rn(x2, sn));
+                v[i + 1] = __fadd_rn(__fmul_rn(x1, sn), __fmul_rn(x2, cs));
+              }
             }
             if (rr) {
               if (full4) {
@@ -340,11 +356,11 @@ struct TrunkAttnArgs {
   const float* k;
   const float* v;
   int64_t ldkv, kv_bs;       // key (b, j) at k + b * kv_bs + j * ldkv + head * DH
-  const int32_t* q_pos;      // (B, Lq) RoPE positions of the queries or null (no rotation)
-  const int32_t* k_pos;      // (B, Lk) of the keys or null
   const int32_t* q_grp;      // (B, Lq) option id of each query (OD_TRUNK_SELF)
   const int32_t* k_grp;      // (B, Lk) option id (SELF, CLS) or 0 (KEYS) per key; < 0 = padding
   const float* bonus;        // (H,) same-option bias (SELF)
+  const int32_t* q_len;      // (B,) real queries / keys of each batch row (a prefix; the rest is padding), or null
+  const int32_t* k_len;
   int mode, Lq, Lk, H, nqb;
   float scale;
   float* o;                  // (B * Lq, ldo) or null
@@ -355,23 +371,62 @@ struct TrunkAttnArgs {
 
 constexpr int TQ = 32;       // queries per CTA
 constexpr int TSUB = 4;      // threads per query, each taking every 4th key
-constexpr int TKB = 64;      // keys staged per step
+constexpr int TKB = 64;      // keys per staged tile
 
+template <int DH>
+constexpr int attn_smem_bytes() { return 2 * 2 * TKB * (DH + 4) * 4; }   // K and V tiles, double-buffered
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// q and k arrive RoPE'd (od_gemm_f32's epilogue rotates them as it writes them). K / V tiles of TKB keys are copied
+// into shared memory with cp.async one tile ahead of the one being used; keys past the row's real length are
+// zero-filled and masked.
 template <int DH>
 __global__ void __launch_bounds__(TQ * TSUB) trunk_attn_kernel(const TrunkAttnArgs a) {
   constexpr int LDS = DH + 4;                      // padded rows: the 4 threads of a query read 4 banks apart
   constexpr int KPT = TKB / TSUB;
-  __shared__ __align__(16) float ks[TKB * LDS];
-  __shared__ __align__(16) float vs[TKB * LDS];
-  __shared__ int kg[TKB];
-  __shared__ float inv_freq[DH / 2];
+  constexpr int CH = DH / 4;                       // 16-byte chunks per row
+  extern __shared__ __align__(16) float smem_f[];
   const int b = blockIdx.x / a.nqb, qb = blockIdx.x - b * a.nqb, h = blockIdx.y;
   const int t = threadIdx.x, sub = t % TSUB;
   const int qi = qb * TQ + t / TSUB;
-  const bool qvalid = qi < a.Lq;
-  if (t < DH / 2)   // the rope table: 1 / 10000^(2i / dh)
-    inv_freq[t] = __frcp_rn(powf(10000.0f, __fdiv_rn(static_cast<float>(2 * t), static_cast<float>(DH))));
-  __syncthreads();
+  const int lq = a.q_len ? min(max(a.q_len[b], 0), a.Lq) : a.Lq;   // padding queries past lq get zeros
+  const int lk = a.k_len ? min(max(a.k_len[b], 0), a.Lk) : a.Lk;   // padding keys past lk are not read
+  const bool qvalid = qi < lq;
+  const int64_t orow = (static_cast<int64_t>(b) * a.Lq + qi) * a.ldo + h * DH;
+  if (qb * TQ >= lq) {          // a block of padding queries (uniform over the CTA)
+    if (qi < a.Lq) {
+      for (int d = sub * (DH / TSUB); d < (sub + 1) * (DH / TSUB); ++d) {
+        if (a.o) a.o[orow + d] = 0.f;
+        if (a.o_hi) {
+          a.o_hi[orow + d] = 0.f;
+          a.o_lo[orow + d] = 0.f;
+        }
+      }
+    }
+    return;
+  }
+  const uint32_t sbase = smem_u32(smem_f);
+  const float* kb0 = a.k + b * a.kv_bs + h * DH;
+  const float* vb0 = a.v + b * a.kv_bs + h * DH;
+  auto stage = [&](int k0, int buf) {                 // issue the copies of keys k0 .. k0 + TKB - 1 into buffer buf
+    const uint32_t ks = sbase + buf * (2 * TKB * LDS * 4), vs = ks + TKB * LDS * 4;
+    for (int idx = t; idx < TKB * CH; idx += TQ * TSUB) {
+      const int j = idx / CH, c = (idx % CH) * 4;
+      const int jg = k0 + j;
+      const bool ok = jg < lk;
+      const int64_t off = static_cast<int64_t>(ok ? jg : 0) * a.ldkv + c;
+      cp_async16(ks + (j * LDS + c) * 4, kb0 + off, ok);
+      cp_async16(vs + (j * LDS + c) * 4, vb0 + off, ok);
+    }
+    cp_async_commit();
+  };
+  if (lk > 0) stage(0, 0);
 
   float q[DH];
   {
@@ -384,70 +439,49 @@ __global__ void __launch_bounds__(TQ * TSUB) trunk_attn_kernel(const TrunkAttnAr
       q[c + 2] = x.z;
       q[c + 3] = x.w;
     }
-    if (a.q_pos && qvalid) {
-      const float pos = static_cast<float>(a.q_pos[static_cast<int64_t>(b) * a.Lq + qi]);
-#pragma unroll
-      for (int i = 0; i < DH / 2; ++i) {
-        const float ang = __fmul_rn(pos, inv_freq[i]);
-        const float cs = cosf(ang), sn = sinf(ang);
-        const float x1 = q[2 * i], x2 = q[2 * i + 1];
-        q[2 * i] = __fsub_rn(__fmul_rn(x1, cs), __fmul_rn(x2, sn));
-        q[2 * i + 1] = __fadd_rn(__fmul_rn(x1, sn), __fmul_rn(x2, cs));
-      }
-    }
   }
   const int qg = a.mode == OD_TRUNK_SELF ? (qvalid ? a.q_grp[static_cast<int64_t>(b) * a.Lq + qi] : -1) : qi;
   const float bonus = a.mode == OD_TRUNK_SELF ? __ldg(a.bonus + h) : 0.f;
+  const int32_t* kgrp = a.k_grp + static_cast<int64_t>(b) * a.Lk;
 
   float m = -INFINITY, l = 0.f;
   float acc[DH];
 #pragma unroll
   for (int d = 0; d < DH; ++d) acc[d] = 0.f;
 
-  for (int k0 = 0; k0 < a.Lk; k0 += TKB) {
-    // stage the next keys (RoPE'd) and values; rows past Lk are zeros with group INT_MIN
-    for (int idx = t; idx < TKB * (DH / 4); idx += TQ * TSUB) {
-      const int j = idx / (DH / 4), c = (idx % (DH / 4)) * 4;
-      const int jg = k0 + j;
-      float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
-      if (jg < a.Lk) {
-        const int64_t off = b * a.kv_bs + static_cast<int64_t>(jg) * a.ldkv + h * DH + c;
-        kv = *reinterpret_cast<const float4*>(a.k + off);
-        vv = *reinterpret_cast<const float4*>(a.v + off);
-        if (a.k_pos) {
-          const float pos = static_cast<float>(a.k_pos[static_cast<int64_t>(b) * a.Lk + jg]);
-          const float a0 = __fmul_rn(pos, inv_freq[c / 2]), a1 = __fmul_rn(pos, inv_freq[c / 2 + 1]);
-          const float c0 = cosf(a0), s0 = sinf(a0), c1 = cosf(a1), s1 = sinf(a1);
-          kv = make_float4(__fsub_rn(__fmul_rn(kv.x, c0), __fmul_rn(kv.y, s0)),
-                           __fadd_rn(__fmul_rn(kv.x, s0), __fmul_rn(kv.y, c0)),
-                           __fsub_rn(__fmul_rn(kv.z, c1), __fmul_rn(kv.w, s1)),
-                           __fadd_rn(__fmul_rn(kv.z, s1), __fmul_rn(kv.w, c1)));
-        }
-      }
-      *reinterpret_cast<float4*>(ks + j * LDS + c) = kv;
-      *reinterpret_cast<float4*>(vs + j * LDS + c) = vv;
+  for (int k0 = 0, buf = 0; k0 < lk; k0 += TKB, buf ^= 1) {
+    if (k0 + TKB < lk) {
+      stage(k0 + TKB, buf ^ 1);                       // the next tile streams in while this one is used
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
     }
-    if (t < TKB) kg[t] = k0 + t < a.Lk ? a.k_grp[static_cast<int64_t>(b) * a.Lk + k0 + t] : INT_MIN;
     __syncthreads();
+    const float* ks = smem_f + buf * (2 * TKB * LDS);
+    const float* vs = ks + TKB * LDS;
 
+    // q . k of the thread's KPT keys, as KPT independent FMA chains (each over the head dimension in order)
     float s[KPT];
+#pragma unroll
+    for (int jj = 0; jj < KPT; ++jj) s[jj] = 0.f;
+#pragma unroll
+    for (int c = 0; c < DH; c += 4) {
+#pragma unroll
+      for (int jj = 0; jj < KPT; ++jj) {
+        const float4 x = *reinterpret_cast<const float4*>(ks + (jj * TSUB + sub) * LDS + c);
+        s[jj] = fmaf(q[c], x.x, s[jj]);
+        s[jj] = fmaf(q[c + 1], x.y, s[jj]);
+        s[jj] = fmaf(q[c + 2], x.z, s[jj]);
+        s[jj] = fmaf(q[c + 3], x.w, s[jj]);
+      }
+    }
     float tmax = -INFINITY;
 #pragma unroll
     for (int jj = 0; jj < KPT; ++jj) {
-      const int j = jj * TSUB + sub;
-      const int gk = kg[j];
+      const int jg = k0 + jj * TSUB + sub;
+      const int gk = jg < lk ? __ldg(kgrp + jg) : INT_MIN;
       const bool ok = a.mode == OD_TRUNK_CLS ? gk == qg : gk >= 0;
-      const float* kr = ks + j * LDS;
-      float dot = 0.f;
-#pragma unroll
-      for (int c = 0; c < DH; c += 4) {
-        const float4 x = *reinterpret_cast<const float4*>(kr + c);
-        dot = fmaf(q[c], x.x, dot);
-        dot = fmaf(q[c + 1], x.y, dot);
-        dot = fmaf(q[c + 2], x.z, dot);
-        dot = fmaf(q[c + 3], x.w, dot);
-      }
-      float sc = __fmul_rn(dot, a.scale);
+      float sc = __fmul_rn(s[jj], a.scale);
       if (a.mode == OD_TRUNK_SELF && qg >= 0 && gk == qg) sc = __fadd_rn(sc, bonus);
       s[jj] = ok ? sc : -INFINITY;
       tmax = fmaxf(tmax, s[jj]);
@@ -475,7 +509,7 @@ __global__ void __launch_bounds__(TQ * TSUB) trunk_attn_kernel(const TrunkAttnAr
         }
       }
     }
-    __syncthreads();
+    __syncthreads();                                  // the buffer is refilled two tiles later
   }
   // merge the 4 partial softmaxes of the query (adjacent lanes)
 #pragma unroll
@@ -489,13 +523,12 @@ __global__ void __launch_bounds__(TQ * TSUB) trunk_attn_kernel(const TrunkAttnAr
     for (int d = 0; d < DH; ++d) acc[d] = acc[d] * f1 + __shfl_xor_sync(0xffffffffu, acc[d], o) * f2;
     m = mm;
   }
-  if (!qvalid) return;
-  // a row with no visible key (a padded CLS option) gets zeros
-  const int64_t orow = (static_cast<int64_t>(b) * a.Lq + qi) * a.ldo + h * DH;
+  if (qi >= a.Lq) return;
+  // a row with no visible key (a padded CLS option) and a padding query get zeros
 #pragma unroll
   for (int d = 0; d < DH; ++d) {
     if (d / (DH / TSUB) != sub) continue;            // each of the 4 threads writes a quarter of the head
-    const float y = l > 0.f ? __fdiv_rn(acc[d], l) : 0.f;
+    const float y = qvalid && l > 0.f ? __fdiv_rn(acc[d], l) : 0.f;
     if (a.o) a.o[orow + d] = y;
     if (a.o_hi) {
       float hh, ll;
@@ -620,7 +653,8 @@ extern "C" int od_xatglu_split(const float* zv, int64_t ldzv, int64_t M, int64_t
 
 extern "C" int od_gemm_f32(const float* x_hi, const float* x_lo, int64_t ldx, const float* w_hi, const float* w_lo,
                            int64_t ldw, const float* bias, const float* res, int64_t ldres, const int64_t* out_rows,
-                           float* y, int64_t ldy, int64_t M, int64_t N, int64_t K, void* stream) {
+                           const int32_t* rope_pos, const float* rope_inv, int rope_cols, int rope_dh, float* y,
+                           int64_t ldy, int64_t M, int64_t N, int64_t K, void* stream) {
   OD_REQUIRE(x_hi && x_lo && w_hi && w_lo && y, "od_gemm_f32: null pointer");
   OD_REQUIRE(M >= 0 && M < (1LL << 31) && N > 0 && N < (1LL << 31) && K > 0 && K % 4 == 0 && K < (1LL << 31),
              "od_gemm_f32: need K %% 4 == 0 (M=%lld N=%lld K=%lld)", (long long)M, (long long)N, (long long)K);
@@ -629,6 +663,9 @@ extern "C" int od_gemm_f32(const float* x_hi, const float* x_lo, int64_t ldx, co
              (long long)ldy);
   OD_REQUIRE(aligned16(x_hi) && aligned16(x_lo) && aligned16(w_hi) && aligned16(w_lo),
              "od_gemm_f32: operands must be 16-byte aligned");
+  OD_REQUIRE(!rope_pos || (rope_inv && rope_dh >= 4 && rope_dh <= 128 && rope_dh % 4 == 0 && rope_cols >= 0 &&
+                            rope_cols % rope_dh == 0 && rope_cols <= N),
+             "od_gemm_f32: RoPE needs an even head width in [4, 128] (multiple of 4) dividing rope_cols <= N");
   if (M == 0) return ok();
   int32_t* err = device_error_word();
   if (!err) return fail(OD_ECUDA, "od_gemm_f32: no device error word");
@@ -652,6 +689,10 @@ extern "C" int od_gemm_f32(const float* x_hi, const float* x_lo, int64_t ldx, co
   a.res = res;
   a.ldres = ldres;
   a.out_rows = out_rows;
+  a.rope_pos = rope_pos;
+  a.rope_inv = rope_inv;
+  a.rope_cols = rope_pos ? rope_cols : 0;
+  a.rope_dh = rope_pos ? rope_dh : 2;
   a.M = static_cast<int>(M);
   a.N = static_cast<int>(N);
   a.K = static_cast<int>(K);
@@ -664,8 +705,8 @@ extern "C" int od_gemm_f32(const float* x_hi, const float* x_lo, int64_t ldx, co
 }
 
 extern "C" int od_trunk_attn(const float* q, int64_t ldq, int64_t q_bstride, const float* k, const float* v,
-                             int64_t ldkv, int64_t kv_bstride, const int32_t* q_pos, const int32_t* k_pos,
-                             const int32_t* q_grp, const int32_t* k_grp, const float* bonus, int mode, int64_t B,
+                             int64_t ldkv, int64_t kv_bstride, const int32_t* q_grp, const int32_t* k_grp,
+                             const float* bonus, const int32_t* q_len, const int32_t* k_len, int mode, int64_t B,
                              int64_t Lq, int64_t Lk, int H, int Dh, float* o, float* o_hi, float* o_lo, int64_t ldo,
                              void* stream) {
   OD_REQUIRE(q && k && v && k_grp && (o || (o_hi && o_lo)), "od_trunk_attn: null pointer");
@@ -687,11 +728,11 @@ extern "C" int od_trunk_attn(const float* q, int64_t ldq, int64_t q_bstride, con
   a.v = v;
   a.ldkv = ldkv;
   a.kv_bs = kv_bstride;
-  a.q_pos = q_pos;
-  a.k_pos = k_pos;
   a.q_grp = q_grp;
   a.k_grp = k_grp;
   a.bonus = bonus;
+  a.q_len = q_len;
+  a.k_len = k_len;
   a.mode = mode;
   a.Lq = static_cast<int>(Lq);
   a.Lk = static_cast<int>(Lk);
@@ -705,10 +746,22 @@ extern "C" int od_trunk_attn(const float* q, int64_t ldq, int64_t q_bstride, con
   OD_REQUIRE(B * a.nqb < (1LL << 31) && H < 65536, "od_trunk_attn: grid too large");
   const dim3 grid(static_cast<unsigned>(B * a.nqb), static_cast<unsigned>(H));
   cudaStream_t st = as_stream(stream);
+  static bool attr[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr[dev]) {
+    OD_CUDA_TRY(cudaFuncSetAttribute(trunk_attn_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     attn_smem_bytes<64>()));
+    OD_CUDA_TRY(cudaFuncSetAttribute(trunk_attn_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     attn_smem_bytes<32>()));
+    OD_CUDA_TRY(cudaFuncSetAttribute(trunk_attn_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     attn_smem_bytes<16>()));
+    attr[dev] = true;
+  }
   switch (Dh) {
-    case 16: trunk_attn_kernel<16><<<grid, TQ * TSUB, 0, st>>>(a); break;
-    case 32: trunk_attn_kernel<32><<<grid, TQ * TSUB, 0, st>>>(a); break;
-    default: trunk_attn_kernel<64><<<grid, TQ * TSUB, 0, st>>>(a); break;
+    case 16: trunk_attn_kernel<16><<<grid, TQ * TSUB, attn_smem_bytes<16>(), st>>>(a); break;
+    case 32: trunk_attn_kernel<32><<<grid, TQ * TSUB, attn_smem_bytes<32>(), st>>>(a); break;
+    default: trunk_attn_kernel<64><<<grid, TQ * TSUB, attn_smem_bytes<64>(), st>>>(a); break;
   }
   OD_LAUNCH_CHECK();
   return ok();

@@ -120,7 +120,9 @@ def trunk_plan(q_lens, o_lens, n_opt, state_lens, up) -> dict:
             "opt_id": up(opt_id), "opos": up(opos), "in_q": up(in_q), "cpos": up(cpos), "c_pad": up(c_pad),
             "opt_mask": up(opt_mask),
             "rc_flat": up(row * P + col), "qrc_flat": up(qrow * Tc + qcol), "gid32": up(opt_id.int()),
-            "cgid32": up(torch.where(c_pad, -1, 0).int()), "opos32": up(opos.int()), "cpos32": up(cpos.int())}
+            "cgid32": up(torch.where(c_pad, -1, 0).int()), "opos32": up(opos.int().view(-1)),
+            "cpos32": up(cpos.int().view(-1)),
+            "olen32": up(row_len.int()), "qlen32": up(q_lens.int()), "nopt32": up(n_opt.int())}
 
 
 class V3Trunk:
@@ -164,6 +166,7 @@ class V3Trunk:
         self.w["cls_attn.q"] = w("cls_attn.q")
         self.w["cls_attn.kv"] = w("cls_attn.k", "cls_attn.v")
         self.w["cls_attn.o"] = w("cls_attn.o")
+        self.rope_inv = _lib.rope_table(cfg.d_model // cfg.n_heads, self.device)
         # the layer mix's weights, softmax(layer_mix) as V3._mix_wide (v3.py:328-341) forms them on every call
         self.mix_w = torch.softmax(p["layer_mix"], 0).contiguous() if cfg.n_feat_layers > 1 else None
 
@@ -181,6 +184,7 @@ class V3Trunk:
         h, dm = self.cfg.n_heads, self.cfg.d_model
         N, K, P, Tc = plan["N"], plan["K"], plan["P"], plan["Tc"]
         gid, cgid, opos, cpos = plan["gid32"], plan["cgid32"], plan["opos32"], plan["cpos32"]
+        olen, qlen = plan["olen32"], plan["qlen32"]     # real option / question tokens: a prefix of each row
         # The input projections run on the real tokens only and are scattered into the padded (N*P) / (N*Tc) row
         # layouts: ScaleNorm and the projection act row by row, and a padding row (zeros in the reference) projects
         # to the bias alone - proj_option's for option pads, proj_state's for context pads (V3.forward applies
@@ -199,14 +203,17 @@ class V3Trunk:
         for i in range(self.cfg.decision_layers):
             L = f"layers.{i}."
             # x = x + self_attn(n1(x)): RoPE'd within each option, + same_bias[h] between tokens of one option
-            qkv = L_.gemm_f32(L_.scalenorm_split(x, p[L + "n1.g"]), W[L + "self_attn.qkv"])
+            qkv = L_.gemm_f32(L_.scalenorm_split(x, p[L + "n1.g"]), W[L + "self_attn.qkv"], rope_pos=opos,
+                              rope_inv=self.rope_inv, rope_cols=2 * dm)
             o = L_.trunk_attn(qkv[:, :dm], qkv[:, dm:2 * dm], qkv[:, 2 * dm:], L_.OD_TRUNK_SELF, N, P, P, h,
-                              k_grp=gid, q_grp=gid, bonus=p[L + "same_bias"], q_pos=opos, k_pos=opos)
+                              k_grp=gid, q_grp=gid, bonus=p[L + "same_bias"], q_len=olen, k_len=olen)
             L_.gemm_f32(o, W[L + "self_attn.o"], res=x, out=x)
             # x = x + cross(n2(x), n2c(c)): the question tokens, keys RoPE'd at their positions after the state
             qc = L_.gemm_f32(L_.scalenorm_split(x, p[L + "n2.g"]), W[L + "cross.q"])
-            kv = L_.gemm_f32(L_.scalenorm_split(c, p[L + "n2c.g"]), W[L + "cross.kv"])
-            o = L_.trunk_attn(qc, kv[:, :dm], kv[:, dm:], L_.OD_TRUNK_KEYS, N, P, Tc, h, k_grp=cgid, k_pos=cpos)
+            kv = L_.gemm_f32(L_.scalenorm_split(c, p[L + "n2c.g"]), W[L + "cross.kv"], rope_pos=cpos,
+                             rope_inv=self.rope_inv, rope_cols=dm)
+            o = L_.trunk_attn(qc, kv[:, :dm], kv[:, dm:], L_.OD_TRUNK_KEYS, N, P, Tc, h, k_grp=cgid, q_len=olen,
+                              k_len=qlen)
             L_.gemm_f32(o, W[L + "cross.o"], res=x, out=x)
             # x = x + ff(n3(x))
             zv = L_.gemm_f32(L_.scalenorm_split(x, p[L + "n3.g"]), W[L + "ff.wgv"], bias=B[L + "ff.wgv"])
@@ -214,9 +221,10 @@ class V3Trunk:
                         out=x)
         # CLS readout: every option's query is the same row (cls.weight, no RoPE); option k sees its own tokens
         qcls = L_.gemm_f32(L_.scalenorm_split(p["cls.weight"], p["cls_nq.g"]), W["cls_attn.q"])
-        kv = L_.gemm_f32(L_.scalenorm_split(x, p["cls_nkv.g"]), W["cls_attn.kv"])
-        o = L_.trunk_attn(qcls, kv[:, :dm], kv[:, dm:], L_.OD_TRUNK_CLS, N, K, P, h, k_grp=gid, k_pos=opos,
-                          q_shared=True)
+        kv = L_.gemm_f32(L_.scalenorm_split(x, p["cls_nkv.g"]), W["cls_attn.kv"], rope_pos=opos,
+                         rope_inv=self.rope_inv, rope_cols=dm)
+        o = L_.trunk_attn(qcls, kv[:, :dm], kv[:, dm:], L_.OD_TRUNK_CLS, N, K, P, h, k_grp=gid, q_shared=True,
+                          q_len=plan["nopt32"], k_len=olen)
         hc = L_.gemm_f32(o, W["cls_attn.o"], res=p["cls.weight"].view(-1))
         zv = L_.gemm_f32(L_.scalenorm_split(hc, p["cls_nf.g"]), W["cls_ff.wgv"], bias=B["cls_ff.wgv"])
         L_.gemm_f32(L_.xatglu_split(zv, p["cls_ff.alpha"]), W["cls_ff.wo"], bias=p["cls_ff.wo.bias"], res=hc, out=hc)

@@ -87,16 +87,34 @@ def test_xatglu_split(cuda):
     assert (_val((hi, lo)) - ref).abs().max().item() < 2e-6
 
 
-def _attn_ref(q, k, v, bias, q_pos, k_pos):
-    """float64 SDPA of (B, H, L, Dh) tensors as the oracle's MHA computes it (RoPE, additive mask)."""
-    q = ot._rope_pairs(q, q_pos)
-    k = ot._rope_pairs(k, k_pos)
+def test_gemm_f32_rope_epilogue(cuda):
+    """The RoPE the GEMM applies to the q / k columns as it writes them, against the oracle's rotation (v3.py:70-79)
+    of the float64 product."""
+    g = torch.Generator().manual_seed(9)
+    M, K, H, Dh = 300, 512, 8, 64
+    D = H * Dh
+    x, w = torch.randn(M, K, generator=g), torch.randn(3 * D, K, generator=g) / math.sqrt(K)
+    pos = torch.randint(0, 17000, (M,), generator=g)
+    y = _lib.gemm_f32(_pair(x, cuda), _pair(w, cuda), rope_pos=pos.int().to(cuda), rope_inv=_lib.rope_table(Dh, cuda),
+                      rope_cols=2 * D).cpu().double()
+    ref = x.double() @ w.double().T
+    rot = ot._rope_pairs(ref[:, :2 * D].view(1, M, 2 * H, Dh).transpose(1, 2), pos.view(1, M))
+    ref[:, :2 * D] = rot.transpose(1, 2).reshape(M, 2 * D)
+    bound = x.double().abs() @ w.double().abs().T
+    pb = bound[:, :2 * D].view(M, D, 2).amax(-1, keepdim=True).expand(M, D, 2).reshape(M, 2 * D)
+    bound[:, :2 * D] = pb                          # a rotated value mixes the two columns of its pair
+    assert ((y - ref).abs() / bound).max().item() < 5e-6
+
+
+def _attn_ref(q, k, v, bias):
+    """float64 SDPA of (B, H, L, Dh) tensors with an additive mask, as the oracle's MHA calls it."""
     return F.scaled_dot_product_attention(q, k, v, attn_mask=bias)
 
 
+@pytest.mark.parametrize("lens", [False, True])
 @pytest.mark.parametrize("mode", ["self", "keys", "cls"])
 @pytest.mark.parametrize("H,Dh", [(8, 64), (4, 16)])
-def test_trunk_attn_modes(cuda, mode, H, Dh):
+def test_trunk_attn_modes(cuda, mode, H, Dh, lens):
     g = torch.Generator().manual_seed(H * 3 + len(mode))
     B, P, Tc, Kopt = 5, 70, 23, 9
     D = H * Dh
@@ -104,6 +122,7 @@ def test_trunk_attn_modes(cuda, mode, H, Dh):
     gid = torch.full((B, P), -1, dtype=torch.long)
     pos = torch.zeros(B, P, dtype=torch.long)
     n_opt = [3, 9, 1, 6, 4]
+    olen = torch.zeros(B, dtype=torch.long)
     for b in range(B):
         c = 0
         for k in range(n_opt[b]):
@@ -111,6 +130,7 @@ def test_trunk_attn_modes(cuda, mode, H, Dh):
             gid[b, c:c + n] = k
             pos[b, c:c + n] = torch.arange(n)
             c += n
+        olen[b] = c
     x_pad = gid < 0
     qlen = torch.tensor([23, 5, 17, 1, 12])
     c_pad = torch.arange(Tc)[None, :] >= qlen[:, None]
@@ -122,40 +142,46 @@ def test_trunk_attn_modes(cuda, mode, H, Dh):
         same = ((gid[:, :, None] == gid[:, None, :]) & ~x_pad[:, :, None]).double()
         bias = (bonus.double().view(1, H, 1, 1) * same[:, None]).masked_fill(x_pad[:, None, None, :], ot.NEG)
         qp, kp, kg, qg = pos, pos, gid, gid
+        ql, kl = olen, olen
     elif mode == "keys":
         Lq, Lk = P, Tc
         q = torch.randn(B, Lq, D, generator=g)
         bias = torch.zeros(B, 1, 1, Tc, dtype=torch.float64).masked_fill(c_pad[:, None, None, :], ot.NEG)
         qp, kp, kg, qg = None, cpos, torch.where(c_pad, -1, 0), None
+        ql, kl = olen, qlen
     else:
         Lq, Lk = Kopt, P
         q = torch.randn(1, 1, D, generator=g).expand(B, Lq, D)
         own = gid[:, None, :] == torch.arange(Kopt)[None, :, None]
         bias = torch.zeros(B, 1, Kopt, P, dtype=torch.float64).masked_fill(~own[:, None], ot.NEG)
         qp, kp, kg, qg = None, pos, gid, None
+        ql, kl = torch.tensor(n_opt), olen
+    if not lens:
+        ql = kl = None
     k = torch.randn(B, Lk, D, generator=g)
     v = torch.randn(B, Lk, D, generator=g)
+    # q and k arrive RoPE'd (the GEMM's epilogue): rotate them here in fp32 as the oracle does
+    rot = lambda t, L, p: ot._rope_pairs(t.reshape(B, L, H, Dh).transpose(1, 2), p).transpose(1, 2).reshape(B, L, D)  # noqa: E731,E501
+    q, k = rot(q, Lq, qp).contiguous(), rot(k, Lk, kp).contiguous()
     heads = lambda t, L: t.double().reshape(B, L, H, Dh).transpose(1, 2)   # noqa: E731
-    ref = _attn_ref(heads(q, Lq), heads(k, Lk), heads(v, Lk), bias, qp, kp).transpose(1, 2).reshape(B * Lq, D)
+    ref = _attn_ref(heads(q, Lq), heads(k, Lk), heads(v, Lk), bias).transpose(1, 2).reshape(B * Lq, D)
     i32 = lambda t: None if t is None else t.int().contiguous().to(cuda)   # noqa: E731
     mcode = {"self": _lib.OD_TRUNK_SELF, "keys": _lib.OD_TRUNK_KEYS, "cls": _lib.OD_TRUNK_CLS}[mode]
     qd = q[0, :1].contiguous().to(cuda) if mode == "cls" else q.reshape(B * Lq, D).to(cuda)
     kv = torch.cat([k, v], -1).reshape(B * Lk, 2 * D).to(cuda)          # k | v side by side, as the GEMM writes
-    o = _lib.trunk_attn(qd, kv[:, :D], kv[:, D:], mcode, B, Lq, Lk, H, k_grp=i32(kg), q_grp=i32(qg),
-                        bonus=bonus.to(cuda) if mode == "self" else None, q_pos=i32(qp), k_pos=i32(kp),
-                        q_shared=mode == "cls", pair=False).cpu().double()
+    kw = dict(k_grp=i32(kg), q_grp=i32(qg), bonus=bonus.to(cuda) if mode == "self" else None,
+              q_shared=mode == "cls", q_len=i32(ql), k_len=i32(kl))
+    o = _lib.trunk_attn(qd, kv[:, :D], kv[:, D:], mcode, B, Lq, Lk, H, pair=False, **kw).cpu().double()
+    valid = torch.ones(B * Lq, dtype=torch.bool)
     if mode == "cls":   # options past a question's count see no key: zeros here (their logits are masked)
         valid = (torch.arange(Kopt)[None, :] < torch.tensor(n_opt)[:, None]).reshape(-1)
+    if ql is not None:  # padding queries past q_len: zeros
+        valid &= (torch.arange(Lq)[None, :] < ql[:, None]).reshape(-1)
+    if not bool(valid.all()):
         assert o[~valid].abs().max().item() == 0.0
-        o, ref = o[valid], ref[valid]
-    assert (o - ref).abs().max().item() < 2e-6
-    hi, lo = _lib.trunk_attn(qd, kv[:, :D], kv[:, D:], mcode, B, Lq, Lk, H, k_grp=i32(kg), q_grp=i32(qg),
-                             bonus=bonus.to(cuda) if mode == "self" else None, q_pos=i32(qp), k_pos=i32(kp),
-                             q_shared=mode == "cls")
-    o2 = _val((hi, lo))
-    if mode == "cls":
-        o2 = o2[valid]
-    assert (o2 - o).abs().max().item() < 1e-12
+    assert (o[valid] - ref[valid]).abs().max().item() < 2e-6
+    hi, lo = _lib.trunk_attn(qd, kv[:, :D], kv[:, D:], mcode, B, Lq, Lk, H, **kw)
+    assert (_val((hi, lo)) - o).abs().max().item() < 1e-12
 
 
 def _trunk_case(tc, n_q, seed):
