@@ -369,12 +369,18 @@ struct TrunkAttnArgs {
   int64_t ldo;
 };
 
-constexpr int TQ = 32;       // queries per CTA
-constexpr int TSUB = 4;      // threads per query, each taking every 4th key
+constexpr int TQ = 64;       // queries per CTA
 constexpr int TKB = 64;      // keys per staged tile
+constexpr int kAttnThreads = 256;   // 16 x 16: thread (ty, tx) holds rows ty + 16 i and keys tx + 16 j, i, j < 4
 
 template <int DH>
-constexpr int attn_smem_bytes() { return 2 * 2 * TKB * (DH + 4) * 4; }   // K and V tiles, double-buffered
+struct AttnSmem {
+  static constexpr int LD = DH + 4;                 // padded rows: 16 rows 16 apart fall on 8 distinct bank groups
+  static constexpr int LP = TKB + 4;
+  static constexpr int Q = 0, K = TQ * LD, V = K + 2 * TKB * LD, P = V + 2 * TKB * LD;
+  static constexpr int floats = P + TQ * LP;
+  static constexpr int bytes = floats * 4;
+};
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0) : "memory");
@@ -383,159 +389,196 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-// q and k arrive RoPE'd (od_gemm_f32's epilogue rotates them as it writes them). K / V tiles of TKB keys are copied
-// into shared memory with cp.async one tile ahead of the one being used; keys past the row's real length are
-// zero-filled and masked.
+// A SIMT flash attention in fp32 with register tiles (q and k arrive RoPE'd: od_gemm_f32's epilogue rotates them).
+// Per CTA: TQ queries of one (batch row, head); K / V tiles of TKB keys stream through shared memory by cp.async one
+// tile ahead. S = Q K^T and O += P V are 4 x 4 register tiles per thread (8 FMAs per 16-byte shared load); the
+// row max and the rescale of the online softmax are exchanged between the 16 threads of a row by shuffles. Keys past
+// the row's real length are neither loaded nor counted; masked keys get probability 0.
 template <int DH>
-__global__ void __launch_bounds__(TQ * TSUB) trunk_attn_kernel(const TrunkAttnArgs a) {
-  constexpr int LDS = DH + 4;                      // padded rows: the 4 threads of a query read 4 banks apart
-  constexpr int KPT = TKB / TSUB;
-  constexpr int CH = DH / 4;                       // 16-byte chunks per row
+__global__ void __launch_bounds__(kAttnThreads, 2) trunk_attn_kernel(const TrunkAttnArgs a) {
+  using L = AttnSmem<DH>;
+  constexpr int LD = L::LD, LP = L::LP, CH = DH / 4, DPT = DH / 16;
   extern __shared__ __align__(16) float smem_f[];
   const int b = blockIdx.x / a.nqb, qb = blockIdx.x - b * a.nqb, h = blockIdx.y;
-  const int t = threadIdx.x, sub = t % TSUB;
-  const int qi = qb * TQ + t / TSUB;
+  const int t = threadIdx.x, tx = t & 15, ty = t >> 4;
   const int lq = a.q_len ? min(max(a.q_len[b], 0), a.Lq) : a.Lq;   // padding queries past lq get zeros
   const int lk = a.k_len ? min(max(a.k_len[b], 0), a.Lk) : a.Lk;   // padding keys past lk are not read
-  const bool qvalid = qi < lq;
-  const int64_t orow = (static_cast<int64_t>(b) * a.Lq + qi) * a.ldo + h * DH;
-  if (qb * TQ >= lq) {          // a block of padding queries (uniform over the CTA)
-    if (qi < a.Lq) {
-      for (int d = sub * (DH / TSUB); d < (sub + 1) * (DH / TSUB); ++d) {
-        if (a.o) a.o[orow + d] = 0.f;
-        if (a.o_hi) {
-          a.o_hi[orow + d] = 0.f;
-          a.o_lo[orow + d] = 0.f;
-        }
-      }
+  const int q0 = qb * TQ;
+  auto out_row = [&](int i) { return (static_cast<int64_t>(b) * a.Lq + q0 + ty + 16 * i) * a.ldo + h * DH; };
+  auto write = [&](int i, int d, float y) {
+    const int64_t o = out_row(i) + d;
+    if (a.o) a.o[o] = y;
+    if (a.o_hi) {
+      float hh, ll;
+      split_tf32(y, hh, ll);
+      a.o_hi[o] = hh;
+      a.o_lo[o] = ll;
     }
+  };
+  if (q0 >= lq) {               // a block of padding queries (uniform over the CTA)
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      if (q0 + ty + 16 * i < a.Lq)
+#pragma unroll
+        for (int e = 0; e < DPT; ++e) write(i, tx * DPT + e, 0.f);
     return;
   }
   const uint32_t sbase = smem_u32(smem_f);
   const float* kb0 = a.k + b * a.kv_bs + h * DH;
   const float* vb0 = a.v + b * a.kv_bs + h * DH;
-  auto stage = [&](int k0, int buf) {                 // issue the copies of keys k0 .. k0 + TKB - 1 into buffer buf
-    const uint32_t ks = sbase + buf * (2 * TKB * LDS * 4), vs = ks + TKB * LDS * 4;
-    for (int idx = t; idx < TKB * CH; idx += TQ * TSUB) {
+  auto stage = [&](int k0, int buf) {                 // keys k0 .. k0 + TKB - 1 into buffer buf
+    const uint32_t ks = sbase + (L::K + buf * TKB * LD) * 4, vs = sbase + (L::V + buf * TKB * LD) * 4;
+    for (int idx = t; idx < TKB * CH; idx += kAttnThreads) {
       const int j = idx / CH, c = (idx % CH) * 4;
-      const int jg = k0 + j;
-      const bool ok = jg < lk;
-      const int64_t off = static_cast<int64_t>(ok ? jg : 0) * a.ldkv + c;
-      cp_async16(ks + (j * LDS + c) * 4, kb0 + off, ok);
-      cp_async16(vs + (j * LDS + c) * 4, vb0 + off, ok);
+      const bool ok = k0 + j < lk;
+      const int64_t off = static_cast<int64_t>(ok ? k0 + j : 0) * a.ldkv + c;
+      cp_async16(ks + (j * LD + c) * 4, kb0 + off, ok);
+      cp_async16(vs + (j * LD + c) * 4, vb0 + off, ok);
     }
     cp_async_commit();
   };
-  if (lk > 0) stage(0, 0);
-
-  float q[DH];
-  {
-    const float* qr = a.q + b * a.q_bs + static_cast<int64_t>(qvalid ? qi : 0) * a.ldq + h * DH;
-#pragma unroll
-    for (int c = 0; c < DH; c += 4) {
-      const float4 x = *reinterpret_cast<const float4*>(qr + c);
-      q[c] = x.x;
-      q[c + 1] = x.y;
-      q[c + 2] = x.z;
-      q[c + 3] = x.w;
+  {   // the query block (rows past lq: zeros)
+    const float* qb0 = a.q + b * a.q_bs + h * DH;
+    for (int idx = t; idx < TQ * CH; idx += kAttnThreads) {
+      const int r = idx / CH, c = (idx % CH) * 4;
+      const bool ok = q0 + r < lq;
+      cp_async16(sbase + (L::Q + r * LD + c) * 4, qb0 + static_cast<int64_t>(ok ? q0 + r : 0) * a.ldq + c, ok);
     }
   }
-  const int qg = a.mode == OD_TRUNK_SELF ? (qvalid ? a.q_grp[static_cast<int64_t>(b) * a.Lq + qi] : -1) : qi;
+  if (lk > 0) stage(0, 0);    // commits the query block with the first tile
+  else cp_async_commit();
+
+  int qg[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int qi = q0 + ty + 16 * i;
+    qg[i] = a.mode == OD_TRUNK_SELF ? (qi < lq ? a.q_grp[static_cast<int64_t>(b) * a.Lq + qi] : -1) : qi;
+  }
   const float bonus = a.mode == OD_TRUNK_SELF ? __ldg(a.bonus + h) : 0.f;
   const int32_t* kgrp = a.k_grp + static_cast<int64_t>(b) * a.Lk;
 
-  float m = -INFINITY, l = 0.f;
-  float acc[DH];
+  float m[4], l[4], o[4][DPT];
 #pragma unroll
-  for (int d = 0; d < DH; ++d) acc[d] = 0.f;
+  for (int i = 0; i < 4; ++i) {
+    m[i] = -INFINITY;
+    l[i] = 0.f;
+#pragma unroll
+    for (int e = 0; e < DPT; ++e) o[i][e] = 0.f;
+  }
+  const float* Qs = smem_f + L::Q;
+  float* Ps = smem_f + L::P;
 
   for (int k0 = 0, buf = 0; k0 < lk; k0 += TKB, buf ^= 1) {
     if (k0 + TKB < lk) {
-      stage(k0 + TKB, buf ^ 1);                       // the next tile streams in while this one is used
+      stage(k0 + TKB, buf ^ 1);
       cp_async_wait<1>();
     } else {
       cp_async_wait<0>();
     }
     __syncthreads();
-    const float* ks = smem_f + buf * (2 * TKB * LDS);
-    const float* vs = ks + TKB * LDS;
+    const float* Ks = smem_f + L::K + buf * TKB * LD;
+    const float* Vs = smem_f + L::V + buf * TKB * LD;
 
-    // q . k of the thread's KPT keys, as KPT independent FMA chains (each over the head dimension in order)
-    float s[KPT];
+    // S = Q K^T: rows ty + 16 i, keys tx + 16 j, each an FMA chain over the head dimension in order
+    float s[4][4];
 #pragma unroll
-    for (int jj = 0; jj < KPT; ++jj) s[jj] = 0.f;
+    for (int i = 0; i < 4; ++i)
 #pragma unroll
+      for (int j = 0; j < 4; ++j) s[i][j] = 0.f;
+#pragma unroll 4
     for (int c = 0; c < DH; c += 4) {
+      float4 qv[4], kv[4];
 #pragma unroll
-      for (int jj = 0; jj < KPT; ++jj) {
-        const float4 x = *reinterpret_cast<const float4*>(ks + (jj * TSUB + sub) * LDS + c);
-        s[jj] = fmaf(q[c], x.x, s[jj]);
-        s[jj] = fmaf(q[c + 1], x.y, s[jj]);
-        s[jj] = fmaf(q[c + 2], x.z, s[jj]);
-        s[jj] = fmaf(q[c + 3], x.w, s[jj]);
+      for (int i = 0; i < 4; ++i) qv[i] = *reinterpret_cast<const float4*>(Qs + (ty + 16 * i) * LD + c);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) kv[j] = *reinterpret_cast<const float4*>(Ks + (tx + 16 * j) * LD + c);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          s[i][j] = fmaf(qv[i].x, kv[j].x, s[i][j]);
+          s[i][j] = fmaf(qv[i].y, kv[j].y, s[i][j]);
+          s[i][j] = fmaf(qv[i].z, kv[j].z, s[i][j]);
+          s[i][j] = fmaf(qv[i].w, kv[j].w, s[i][j]);
+        }
+    }
+    // scale, bias and mask; the row max over the 16 threads of the row
+    int gk[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) gk[j] = k0 + tx + 16 * j < lk ? __ldg(kgrp + k0 + tx + 16 * j) : INT_MIN;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float rmax = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const bool ok = a.mode == OD_TRUNK_CLS ? gk[j] == qg[i] : gk[j] >= 0;
+        float sc = __fmul_rn(s[i][j], a.scale);
+        if (a.mode == OD_TRUNK_SELF && qg[i] >= 0 && gk[j] == qg[i]) sc = __fadd_rn(sc, bonus);
+        s[i][j] = ok ? sc : -INFINITY;
+        rmax = fmaxf(rmax, s[i][j]);
+      }
+#pragma unroll
+      for (int x = 1; x < 16; x <<= 1) rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, x));
+      const float mn = fmaxf(m[i], rmax);
+      if (mn > m[i]) {                               // the same decision on the row's 16 threads
+        const float f = expf(m[i] - mn);             // 0 while m is -inf
+        l[i] *= f;
+#pragma unroll
+        for (int e = 0; e < DPT; ++e) o[i][e] *= f;
+        m[i] = mn;
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float p = s[i][j] == -INFINITY ? 0.f : expf(s[i][j] - m[i]);
+        l[i] += p;
+        Ps[(ty + 16 * i) * LP + tx + 16 * j] = p;
       }
     }
-    float tmax = -INFINITY;
+    __syncthreads();
+    // O += P V: rows ty + 16 i, dims tx * DPT .. + DPT
+#pragma unroll 4
+    for (int kk = 0; kk < TKB; kk += 4) {
+      float4 pv[4];
 #pragma unroll
-    for (int jj = 0; jj < KPT; ++jj) {
-      const int jg = k0 + jj * TSUB + sub;
-      const int gk = jg < lk ? __ldg(kgrp + jg) : INT_MIN;
-      const bool ok = a.mode == OD_TRUNK_CLS ? gk == qg : gk >= 0;
-      float sc = __fmul_rn(s[jj], a.scale);
-      if (a.mode == OD_TRUNK_SELF && qg >= 0 && gk == qg) sc = __fadd_rn(sc, bonus);
-      s[jj] = ok ? sc : -INFINITY;
-      tmax = fmaxf(tmax, s[jj]);
-    }
-    if (tmax > m) {
-      const float f = expf(m - tmax);               // 0 while m is -inf
-      l *= f;
+      for (int i = 0; i < 4; ++i) pv[i] = *reinterpret_cast<const float4*>(Ps + (ty + 16 * i) * LP + kk);
 #pragma unroll
-      for (int d = 0; d < DH; ++d) acc[d] *= f;
-      m = tmax;
-    }
+      for (int u = 0; u < 4; ++u) {
+        float vv[DPT];
+        const float* vr = Vs + (kk + u) * LD + tx * DPT;
+        if constexpr (DPT == 4) {
+          const float4 x = *reinterpret_cast<const float4*>(vr);
+          vv[0] = x.x;
+          vv[1] = x.y;
+          vv[2] = x.z;
+          vv[3] = x.w;
+        } else if constexpr (DPT == 2) {
+          const float2 x = *reinterpret_cast<const float2*>(vr);
+          vv[0] = x.x;
+          vv[1] = x.y;
+        } else {
+          vv[0] = vr[0];
+        }
 #pragma unroll
-    for (int jj = 0; jj < KPT; ++jj) {
-      if (s[jj] != -INFINITY) {
-        const float p = expf(s[jj] - m);
-        l += p;
-        const float* vr = vs + (jj * TSUB + sub) * LDS;
+        for (int i = 0; i < 4; ++i) {
+          const float p = u == 0 ? pv[i].x : u == 1 ? pv[i].y : u == 2 ? pv[i].z : pv[i].w;
 #pragma unroll
-        for (int c = 0; c < DH; c += 4) {
-          const float4 x = *reinterpret_cast<const float4*>(vr + c);
-          acc[c] = fmaf(p, x.x, acc[c]);
-          acc[c + 1] = fmaf(p, x.y, acc[c + 1]);
-          acc[c + 2] = fmaf(p, x.z, acc[c + 2]);
-          acc[c + 3] = fmaf(p, x.w, acc[c + 3]);
+          for (int e = 0; e < DPT; ++e) o[i][e] = fmaf(p, vv[e], o[i][e]);
         }
       }
     }
-    __syncthreads();                                  // the buffer is refilled two tiles later
+    __syncthreads();                                  // K / V / P buffers are rewritten next
   }
-  // merge the 4 partial softmaxes of the query (adjacent lanes)
+  cp_async_wait<0>();                                 // (no copy is left in flight when lk == 0)
+  // the row sums over the 16 threads of the row, then O / l (a row with no visible key - a padded CLS option -
+  // and a padding query get zeros)
 #pragma unroll
-  for (int o = 1; o < TSUB; o <<= 1) {
-    const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
-    const float l2 = __shfl_xor_sync(0xffffffffu, l, o);
-    const float mm = fmaxf(m, m2);
-    const float f1 = m == -INFINITY ? 0.f : expf(m - mm), f2 = m2 == -INFINITY ? 0.f : expf(m2 - mm);
-    l = l * f1 + l2 * f2;
+  for (int i = 0; i < 4; ++i) {
 #pragma unroll
-    for (int d = 0; d < DH; ++d) acc[d] = acc[d] * f1 + __shfl_xor_sync(0xffffffffu, acc[d], o) * f2;
-    m = mm;
-  }
-  if (qi >= a.Lq) return;
-  // a row with no visible key (a padded CLS option) and a padding query get zeros
+    for (int x = 1; x < 16; x <<= 1) l[i] += __shfl_xor_sync(0xffffffffu, l[i], x);
+    const int qi = q0 + ty + 16 * i;
+    if (qi >= a.Lq) continue;
 #pragma unroll
-  for (int d = 0; d < DH; ++d) {
-    if (d / (DH / TSUB) != sub) continue;            // each of the 4 threads writes a quarter of the head
-    const float y = qvalid && l > 0.f ? __fdiv_rn(acc[d], l) : 0.f;
-    if (a.o) a.o[orow + d] = y;
-    if (a.o_hi) {
-      float hh, ll;
-      split_tf32(y, hh, ll);
-      a.o_hi[orow + d] = hh;
-      a.o_lo[orow + d] = ll;
-    }
+    for (int e = 0; e < DPT; ++e) write(i, tx * DPT + e, qi < lq && l[i] > 0.f ? __fdiv_rn(o[i][e], l[i]) : 0.f);
   }
 }
 
@@ -751,17 +794,17 @@ extern "C" int od_trunk_attn(const float* q, int64_t ldq, int64_t q_bstride, con
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr[dev]) {
     OD_CUDA_TRY(cudaFuncSetAttribute(trunk_attn_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     attn_smem_bytes<64>()));
+                                     AttnSmem<64>::bytes));
     OD_CUDA_TRY(cudaFuncSetAttribute(trunk_attn_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     attn_smem_bytes<32>()));
+                                     AttnSmem<32>::bytes));
     OD_CUDA_TRY(cudaFuncSetAttribute(trunk_attn_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     attn_smem_bytes<16>()));
+                                     AttnSmem<16>::bytes));
     attr[dev] = true;
   }
   switch (Dh) {
-    case 16: trunk_attn_kernel<16><<<grid, TQ * TSUB, attn_smem_bytes<16>(), st>>>(a); break;
-    case 32: trunk_attn_kernel<32><<<grid, TQ * TSUB, attn_smem_bytes<32>(), st>>>(a); break;
-    default: trunk_attn_kernel<64><<<grid, TQ * TSUB, attn_smem_bytes<64>(), st>>>(a); break;
+    case 16: trunk_attn_kernel<16><<<grid, kAttnThreads, AttnSmem<16>::bytes, st>>>(a); break;
+    case 32: trunk_attn_kernel<32><<<grid, kAttnThreads, AttnSmem<32>::bytes, st>>>(a); break;
+    default: trunk_attn_kernel<64><<<grid, kAttnThreads, AttnSmem<64>::bytes, st>>>(a); break;
   }
   OD_LAUNCH_CHECK();
   return ok();
