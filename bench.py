@@ -446,13 +446,17 @@ def int8_peak(dev, seconds: float = 2.0) -> dict:
 
 
 def _flush_l2(buf):
-    buf.add_(1)                                                # writes 256 MB: more than the 126 MB L2
+    """Write 256 MB (more than the 126 MB L2), then read the first half back: the write alone would leave L2 full of
+    dirty lines whose write-back to HBM lands inside the next (timed) kernel; after the read L2 holds clean lines of
+    the flush buffer only, none of the timed kernel's operands."""
+    buf.add_(1)
+    torch.sum(buf[: buf.numel() // 2], dim=0, out=buf[-1:].view(()))
 
 
 def op_gemm(args):
     """the W8A8 GEMM at M in {512, 2048, 8192} x (K, N) in {(4096, 4096), (4096, 12288),
     (12288, 4096)}; one JSON line per shape (TOP/s vs 2 x measured bf16, GB/s of the algorithmic bytes,
-    cuBLASLt's int8 GEMM (torch._int_mm) on the same operands for context). L2 flushed between iterations."""
+    cuBLASLt's int8 GEMM (torch._int_mm) on the same operands for context). L2 flushed between iterations (_flush_l2)."""
     from opendecider_b200 import _lib
     from opendecider_b200 import synthetic as syn
     dev = torch.device("cuda", 0)
