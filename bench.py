@@ -466,7 +466,8 @@ def op_gemm(args):
     i8 = int8_peak(dev)
     print(json.dumps({"op": "int8_peak", **i8}))
     flush = torch.zeros(64 << 20, dtype=torch.float32, device=dev)
-    for (M, N, K) in shapes:
+    split_list = [int(v) for v in args.splits.split(",")] if args.splits else [None]
+    for (M, N, K), sp in ((shape, sp) for shape in shapes for sp in split_list):
         gc = syn.gemm_case(M, N, K, seed=0)
         xq, sx = _lib.quant_rows(gc.x.to(dev), scale_dtype=torch.float32)
         wq, sw = gc.qweight.to(dev), gc.wscale.to(dev).view(-1)
@@ -476,7 +477,7 @@ def op_gemm(args):
             _flush_l2(flush)
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record()
-            _lib.gemm_w8a8(xq, sx.view(-1), wq, sw, _lib.OD_EPI_BF16, out=y)
+            _lib.gemm_w8a8(xq, sx.view(-1), wq, sw, _lib.OD_EPI_BF16, out=y, splits=sp)
             b.record()
             _flush_l2(flush)
             c, d = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -492,7 +493,7 @@ def op_gemm(args):
         ops = 2.0 * M * N * K
         byts = M * K + N * K + 2 * M * N + 4 * M + 2 * N
         print(json.dumps({"op": "gemm_w8a8", "shape": {"M": M, "N": N, "K": K}, "ms": t * 1e3,
-                          "splits": _lib._gemm_plan(M, N, K, dev),
+                          "splits": sp or _lib._gemm_plan(M, N, K, dev),
                           "tops": ops / t / 1e12, "peak_tops": peak, "frac": ops / t / 1e12 / peak,
                           "frac_of_int8_burst": ops / t / 1e12 / i8["burst"],
                           "gbs": byts / t / 1e9, "cublaslt_int8_tops": ops / (statistics.median(tc) / 1e3) / 1e12,
@@ -771,6 +772,8 @@ def main():
                                                  "--op attn_state: rowsxtokens list")
     ap.add_argument("--requests", type=int, default=0, help="--op attn: requests (default 32)")
     ap.add_argument("--kernels", default="", help="--op rows: comma-separated subset of the row kernels")
+    ap.add_argument("--splits", default="", help="--op gemm: comma-separated split-K counts to time per shape "
+                                                 "(default: od_gemm_w8a8_plan's choice)")
     ap.add_argument("--breakdown", action="store_true", help="print per-kernel device time of one step to stderr")
     args = ap.parse_args()
     if args.op == "gemm":
