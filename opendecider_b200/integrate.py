@@ -11,6 +11,10 @@ reference itself defines, next to its prepare_inference_ (decider.py:91-117):
                    int8 prefix dequantised in the kernel, the question level of the question cache as a second
                    prefix, the row's own keys causally) - no materialize() of the state K/V (prefix_attn.py:146-149),
                    no per-state loop, no host synchronisation.
+  trunk seam       a V3 model in the serving configuration (branched answer rows, question cross-attention, readout
+                   "last") gets b200_v3_forward in place of V3.forward (v3.py:606-709): the reference's own feature
+                   passes, then the decision trunk on the library's fp32 kernels (V3Trunk) from the model's own trunk
+                   parameters.
   layouts          unchanged: Int8Linear's qweight/scale, PackedCache.tensors[(layer, "keys"|"values", None)].
 
     from opendecider.decider import Decider, prepare_inference_
@@ -18,8 +22,8 @@ reference itself defines, next to its prepare_inference_ (decider.py:91-117):
     prepare_inference_(model)       # the reference's serving set-up
     prepare_b200_(model)            # then the B200 kernels; undo_b200_(model) restores the reference's paths
 
-Everything else in the reference's forward (embedding, RMSNorm, RoPE, the state pass's SDPA, the V3 trunk, the
-readout) runs as the reference runs it. A CPU model is refused (no CPU fallback).
+Everything else in the reference's forward (embedding, RMSNorm, RoPE, the state pass's SDPA, the readout) runs as
+the reference runs it. A CPU model is refused (no CPU fallback).
 """
 from __future__ import annotations
 
@@ -171,10 +175,65 @@ def b200_shared_prefix_attention(bb, pc, rows: torch.Tensor, pmask: torch.Tensor
             del m.forward
 
 
+_TRUNK_PREFIXES = ("layer_mix", "in_norm.", "proj_", "layers.", "cls", "final_norm.", "score.", "rel.", "lp_proj.",
+                   "lm_skip")
+
+
+def _trunk_config(model):
+    """The TrunkConfig of a reference V3 model whose trunk V3Trunk runs as the reference does - branched answer rows
+    cross-attending the question only, the softmax layer mix, no context layers or context update, readout "last",
+    no `none` sink, no slot embeddings - else None (that model keeps the reference's trunk)."""
+    from .v3 import TrunkConfig
+    cfg, bb = getattr(model, "cfg", None), getattr(model, "backbone", None)
+    ok = (cfg is not None and bb is not None and getattr(cfg, "variant", None) == "v3"
+          and getattr(model, "branched", False) and getattr(model, "state_free", False)
+          and cfg.v3_layer_combine == "mix" and not cfg.v3_context_update and cfg.v3_context_layers == 0
+          and cfg.v3_readout == "last" and not cfg.v3_none and cfg.slot_emb == "none")
+    if not ok:
+        return None
+    return TrunkConfig(d_feat=model.d, n_feat_layers=len(bb.cfg.feature_layers), d_model=cfg.d_model,
+                       n_heads=cfg.n_heads, decision_layers=cfg.decision_layers, lm_feature=bool(cfg.v3_lm_feature))
+
+
+def b200_v3_forward(self, p, mem, questions=None, feats=None):
+    """V3.forward (v3.py:606-709) of a reference model in the configuration _trunk_config accepts, with its trunk on
+    the library's kernels: the reference's own frozen-LLM features (`_conditioned_feats_raw`: state pass, question
+    cache, option rows, the LM feature), then V3Trunk on them - the layout V3.forward builds (option and question
+    tokens, option ids, positions after the state), the layer mix, the decision layers, the CLS readout, `score` and
+    `rel`. Calls with precomputed `feats` take the reference's own forward."""
+    if feats is not None or questions is None:
+        return type(self).forward(self, p, mem, questions, feats)
+    from opendecider.models import DecisionOutput
+    trunk = self.__dict__["_b200_trunk"]
+    _, s_lens, q_flat, q_lens, o_flat, o_lens = self._conditioned_feats_raw(questions, mem)
+    n_opt = torch.tensor([len(q.options) for q in questions])
+    sidx = torch.tensor([q.state_idx for q in questions])
+    plan = trunk.prepare(q_lens, o_lens, n_opt, s_lens[sidx])
+    lp = self._lm_lp if trunk.cfg.lm_feature else None
+    logits, rel = trunk.run(plan, q_flat, o_flat, lp, want_rel=True)
+    return DecisionOutput(logits, p.opt_mask, rel, None)
+
+
+def install_trunk_(model) -> int:
+    """Give a reference V3 model the library's trunk (b200_v3_forward in place of its forward; the weights are the
+    model's own trunk parameters, read once). Returns 1 if installed, 0 if the model's configuration is not one
+    V3Trunk runs."""
+    from .v3 import V3Trunk
+    tc = _trunk_config(model)
+    if tc is None or "_b200_trunk" in model.__dict__:
+        return 0
+    dev = model.backbone.device
+    params = {k: v.detach() for k, v in model.state_dict().items() if k.startswith(_TRUNK_PREFIXES)}
+    model.__dict__["_b200_trunk"] = V3Trunk(tc, params, dev)
+    model.__dict__["forward"] = types.MethodType(b200_v3_forward, model)
+    return 1
+
+
 def prepare_b200_(model) -> dict:
     """Install the B200 kernels into a reference DecisionModel (its `.backbone` a reference Backbone on CUDA): the W8A8
-    GEMM in every int8 linear's `_fused` slot and the int8-KV shared-prefix attention in place of the reference's
-    shared_prefix_attention. Returns {"gemm": linears given a kernel, "attention": seams swapped}."""
+    GEMM in every int8 linear's `_fused` slot, the int8-KV shared-prefix attention in place of the reference's
+    shared_prefix_attention, and - for a V3 model in the serving configuration - the trunk (install_trunk_).
+    Returns {"gemm": linears given a kernel, "attention": seams swapped, "trunk": trunks installed}."""
     import opendecider.v3 as ref_v3
     bb = model.backbone
     n = install_gemm_kernels_(bb.lm.layers)
@@ -183,7 +242,7 @@ def prepare_b200_(model) -> dict:
         model.__dict__["_b200_prev_attention"] = ref_v3.shared_prefix_attention
         ref_v3.shared_prefix_attention = b200_shared_prefix_attention
         swapped = 1
-    return {"gemm": n, "attention": swapped}
+    return {"gemm": n, "attention": swapped, "trunk": install_trunk_(model)}
 
 
 def undo_b200_(model) -> None:
@@ -199,3 +258,5 @@ def undo_b200_(model) -> None:
     prev = model.__dict__.pop("_b200_prev_attention", None)
     if prev is not None:
         ref_v3.shared_prefix_attention = prev
+    if model.__dict__.pop("_b200_trunk", None) is not None:
+        model.__dict__.pop("forward", None)

@@ -149,7 +149,7 @@ class V3Trunk:
             return torch.cat([p[n + ".bias"] for n in names], 0).contiguous()
 
         self.w, self.b = {}, {}
-        for n in ("proj_option", "proj_question", "score"):
+        for n in ("proj_option", "proj_question", "score") + (("rel",) if "rel.weight" in p else ()):
             self.w[n] = w(n)
         blocks = [f"layers.{i}." for i in range(cfg.decision_layers)] + [""]
         for L in blocks:
@@ -175,10 +175,12 @@ class V3Trunk:
         return trunk_plan(q_lens, o_lens, n_opt, state_lens, up or (lambda x: x.to(self.device, non_blocking=True)))
 
     @torch.no_grad()
-    def run(self, plan: dict, q_flat: torch.Tensor, o_flat: torch.Tensor, lp_flat: torch.Tensor | None = None):
+    def run(self, plan: dict, q_flat: torch.Tensor, o_flat: torch.Tensor, lp_flat: torch.Tensor | None = None,
+            want_rel: bool = False):
         """V3.forward's device part (v3.py:627-709): option/context stacks, decision layers, CLS readout, score.
         q_flat (sum lq, nL*d), o_flat (sum lo, nL*d) token features; lp_flat (sum lo,) the LM log-prob of each
-        option token (lm_feature). Returns logits (N, K) fp32, NEG at pads."""
+        option token (lm_feature). Returns logits (N, K) fp32, NEG at pads; with want_rel also the `rel` head's
+        scores of the same final states (v3.py:708), NEG at pads."""
         p, W, B = self.p, self.w, self.b
         L_ = _lib
         h, dm = self.cfg.n_heads, self.cfg.d_model
@@ -228,12 +230,17 @@ class V3Trunk:
         hc = L_.gemm_f32(o, W["cls_attn.o"], res=p["cls.weight"].view(-1))
         zv = L_.gemm_f32(L_.scalenorm_split(hc, p["cls_nf.g"]), W["cls_ff.wgv"], bias=B["cls_ff.wgv"])
         L_.gemm_f32(L_.xatglu_split(zv, p["cls_ff.alpha"]), W["cls_ff.wo"], bias=p["cls_ff.wo.bias"], res=hc, out=hc)
-        logits = L_.gemm_f32(L_.scalenorm_split(hc, p["final_norm.g"]), W["score"], bias=p["score.bias"]).view(N, K)
+        hf = L_.scalenorm_split(hc, p["final_norm.g"])
+        logits = L_.gemm_f32(hf, W["score"], bias=p["score.bias"]).view(N, K)
         if lpX is not None:                 # gated skip of the length-normalised log-likelihood (v3.py:702-706)
             own_f = (plan["opt_id"][:, None, :] == torch.arange(K, device=self.device)[None, :, None]).float()
             ll = (own_f * lpX[:, None, :]).sum(-1) / own_f.sum(-1).clamp_min(1)
             logits = logits + p["lm_skip"] * ll
-        return logits.masked_fill(~plan["opt_mask"], NEG)
+        logits = logits.masked_fill(~plan["opt_mask"], NEG)
+        if not want_rel:
+            return logits
+        rel = L_.gemm_f32(hf, W["rel"], bias=p["rel.bias"]).view(N, K).masked_fill(~plan["opt_mask"], NEG)
+        return logits, rel
 
 
 # ------------------------------------------------------------------------------------------------ row plans

@@ -2,7 +2,7 @@
 (the set-up of tests/golden/make_golden_e2e.py: its Qwen3.5 backbone with Int8Linear / Int8Embedding, its V3 trunk,
 prepare_inference_ with the question cache) built on CUDA, then the B200 kernels installed at the reference's seams -
 the W8A8 GEMM in every Int8Linear's `_fused` slot, the int8-KV shared-prefix attention in place of
-shared_prefix_attention. Its decide_many on BASELINE config 1 must match the golden of the reference's own CPU run
+shared_prefix_attention, the decision trunk in place of V3.forward's (b200_v3_forward). Its decide_many on BASELINE config 1 must match the golden of the reference's own CPU run
 (tests/golden/e2e_config1.npz) within 1e-3, with forward hooks on the int8 linears (how the reference's VeRA adapters
 attach, vera.py:54) still firing, and the library's kernels doing the work.
 
@@ -51,12 +51,14 @@ def test_prepare_b200_on_the_reference_decider(cuda):
     prepare_inference_(model)
     got = prepare_b200_(model)
     try:
-        assert got == {"gemm": 7 * cfg.layers, "attention": 1}
+        assert got == {"gemm": 7 * cfg.layers, "attention": 1, "trunk": 1}
         assert ref_v3.shared_prefix_attention is b200_shared_prefix_attention
+        assert "_b200_trunk" in model.__dict__ and "forward" in model.__dict__
         calls = [0]
         hook = bb.lm.layers[1].self_attn.q_proj.register_forward_hook(
             lambda m, a, out: calls.__setitem__(0, calls[0] + 1))
         l0 = _lib.LAUNCHES[0]
+        _lib.KERNEL_PROBE = {}
         dec = Decider(model, temperature=1.419344425201416, temperature_by_type=TEMPS)
         dreqs = [{"state": r.state, "questions": {q.name: {"type": q.type, "prompt": q.prompt, "options": q.options}
                                                   for q in r.questions}} for r in reqs]
@@ -66,10 +68,14 @@ def test_prepare_b200_on_the_reference_decider(cuda):
         hook.remove()
         assert calls[0] >= 3                           # state pass, question pass, option rows
         assert _lib.LAUNCHES[0] - l0 > 50              # the GEMMs and attention ran in libod_b200
+        ran = set(_lib.KERNEL_PROBE)
+        assert {"gemm_f32", "trunk_attn", "scalenorm_split", "xatglu_split"} <= ran, ran   # the trunk too
         assert _lib.device_error(cuda) == 0
     finally:
+        _lib.KERNEL_PROBE = None
         undo_b200_(model)
     assert ref_v3.shared_prefix_attention is not b200_shared_prefix_attention
+    assert "_b200_trunk" not in model.__dict__ and "forward" not in model.__dict__
     g = np.load(os.path.join(HERE, "golden", "e2e_config1.npz"))
     p = np.array([a["answers"]["q0"]["probs_list"] for a in ans])
     none = np.array([a["answers"]["q0"]["none"] for a in ans])

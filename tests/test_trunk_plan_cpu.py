@@ -50,3 +50,14 @@ def test_v3trunk_has_no_cpu_path():
     tc = TrunkConfig(d_feat=64, n_feat_layers=1, d_model=32, n_heads=2, decision_layers=1)
     with pytest.raises(_lib.ODError):
         V3Trunk(tc, trunk_state_dict(tc, seed=0), "cpu")
+
+
+def test_trunk_seam_reads_every_trunk_parameter():
+    """prepare_b200_'s trunk seam takes a reference model's trunk entries by name prefix: every parameter V3Trunk
+    reads (the reference V3's names, with and without the LM feature) matches one, and the backbone's do not."""
+    from opendecider_b200.integrate import _TRUNK_PREFIXES
+    for lm in (False, True):
+        tc = TrunkConfig(d_feat=64, n_feat_layers=3, d_model=32, n_heads=2, decision_layers=2, lm_feature=lm)
+        assert [k for k in trunk_state_dict(tc) if not k.startswith(_TRUNK_PREFIXES)] == []
+    assert not any(k.startswith(_TRUNK_PREFIXES) for k in ("backbone.lm.layers.0.self_attn.q_proj.qweight",
+                                                            "vera.b.0", "context_layers.0.n1.g", "slots.emb"))
