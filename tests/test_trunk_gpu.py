@@ -3,7 +3,8 @@ of the whole trunk (oracle/trunk.py, pinned to the reference's own decide_many l
 
 Tolerances: od_gemm_f32 (3xTF32 on the tensor cores) within 5e-6 of sum_k |x_k w_k| per output element (fp32
 accumulation of ~2^-21-accurate products); the split operand pairs within 2e-7 relative of their float64 value;
-attention within 2e-6 of the float64 result; the whole trunk's logits within 5e-4 of the oracle's (fp32 summation
+attention within 2e-6 of the float64 result on unit-normal q / k / v (5e-6 over 255-option rows: the fp32 q . k
+over 64 dimensions is accurate to ~1e-6 of |q||k|); the whole trunk's logits within 5e-4 of the oracle's (fp32 summation
 order differences through 4 layers)."""
 import math
 
@@ -217,3 +218,67 @@ def test_trunk_matches_oracle(cuda, size, lm):
     d = (got[mask].double() - ref[mask].double()).abs().max().item()
     assert d < 5e-4, d
     assert np.isfinite(got.numpy()).all()
+
+
+@pytest.mark.parametrize("mode", ["self", "cls"])
+def test_trunk_attn_long_option_lists(cuda, mode):
+    """Many key tiles (P = 700 option-token slots: eleven 64-key tiles through the cp.async double buffer) and many
+    query blocks, against the float64 SDPA with the oracle's mask; 2 questions, 8 heads of 64."""
+    g = torch.Generator().manual_seed(7)
+    B, H, Dh, Kopt = 2, 8, 64, 255
+    D = H * Dh
+    lens = torch.randint(1, 4, (B, Kopt), generator=g)
+    P = int(lens.sum(1).max())
+    gid = torch.full((B, P), -1, dtype=torch.long)
+    for b in range(B):
+        gid[b, : int(lens[b].sum())] = torch.repeat_interleave(torch.arange(Kopt), lens[b])
+    x_pad = gid < 0
+    olen = (~x_pad).sum(1)
+    bonus = torch.randn(H, generator=g)
+    k = torch.randn(B, P, D, generator=g)
+    v = torch.randn(B, P, D, generator=g)
+    if mode == "self":
+        Lq = P
+        q = torch.randn(B, P, D, generator=g)
+        same = ((gid[:, :, None] == gid[:, None, :]) & ~x_pad[:, :, None]).double()
+        bias = (bonus.double().view(1, H, 1, 1) * same[:, None]).masked_fill(x_pad[:, None, None, :], ot.NEG)
+        qd, kw = q.reshape(B * P, D), dict(q_grp=gid.int().to(cuda), bonus=bonus.to(cuda), q_len=olen.int().to(cuda))
+        mcode = _lib.OD_TRUNK_SELF
+    else:
+        Lq = Kopt
+        q = torch.randn(1, 1, D, generator=g).expand(B, Lq, D)
+        own = gid[:, None, :] == torch.arange(Kopt)[None, :, None]
+        bias = torch.zeros(B, 1, Kopt, P, dtype=torch.float64).masked_fill(~own[:, None], ot.NEG)
+        qd, kw = q[0, :1].contiguous(), dict(q_shared=True, q_len=torch.full((B,), Kopt, dtype=torch.int32).to(cuda))
+        mcode = _lib.OD_TRUNK_CLS
+    heads = lambda t, L: t.double().reshape(B, L, H, Dh).transpose(1, 2)   # noqa: E731
+    ref = _attn_ref(heads(q, Lq), heads(k, P), heads(v, P), bias).transpose(1, 2).reshape(B * Lq, D)
+    kv = torch.cat([k, v], -1).reshape(B * P, 2 * D).to(cuda)
+    o = _lib.trunk_attn(qd.to(cuda), kv[:, :D], kv[:, D:], mcode, B, Lq, P, H, k_grp=gid.int().to(cuda),
+                        k_len=olen.int().to(cuda), pair=False, **kw).cpu().double()
+    valid = torch.ones(B * Lq, dtype=torch.bool)
+    if mode == "self":
+        valid = (torch.arange(P)[None, :] < olen[:, None]).reshape(-1)
+    assert (o[valid] - ref[valid]).abs().max().item() < 5e-6
+
+
+def test_trunk_matches_oracle_255_options(cuda):
+    """The whole trunk on config 5's question shape - 255 options of 1-3 tokens per question (P up to 765) - against
+    the CPU oracle; 3 questions, the 9B trunk (d_model 512, 8 heads, 4 layers, 4 feature layers of 4096)."""
+    tc = TrunkConfig(d_feat=4096, n_feat_layers=4, d_model=512, n_heads=8, decision_layers=4)
+    sd = trunk_state_dict(tc, seed=6)
+    g = torch.Generator().manual_seed(13)
+    n_q = 3
+    n_opt = torch.full((n_q,), 255)
+    o_lens = torch.randint(1, 4, (int(n_opt.sum()),), generator=g)
+    q_lens = torch.randint(20, 60, (n_q,), generator=g)
+    sl = torch.tensor([16896, 16000, 900])
+    nf = tc.n_feat_layers * tc.d_feat
+    q_flat = (torch.randn(int(q_lens.sum()), nf, generator=g) * 2).bfloat16()
+    o_flat = (torch.randn(int(o_lens.sum()), nf, generator=g) * 2).bfloat16()
+    oracle = ot.OracleTrunk(tc, sd)
+    ref = oracle.run(oracle.prepare(q_lens, o_lens, n_opt, sl), q_flat, o_flat)
+    gpu = V3Trunk(tc, sd, cuda)
+    got = gpu.run(gpu.prepare(q_lens, o_lens, n_opt, sl), q_flat.to(cuda), o_flat.to(cuda)).cpu()
+    d = (got.double() - ref.double()).abs().max().item()
+    assert d < 5e-4, d
