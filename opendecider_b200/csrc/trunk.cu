@@ -7,7 +7,8 @@
 //                          2^-22 relative, is left out). 128 x 128 tiles, K in 32-element (128-byte) steps through a
 //                          3-stage TMA ring of the four operand halves, two TMEM accumulators, persistent CTAs.
 //                          The epilogue adds the bias and the residual (x = x + layer(x) in place, or a broadcast
-//                          row) and can scatter rows to given output rows (the padded option/context layouts).
+//                          row), can scatter rows to given output rows (the padded option/context layouts) and
+//                          applies RoPE to the q / k columns of an attention's projection as it writes them.
 //   scalenorm_split_kernel ScaleNorm g * x / max(||x||, eps) of each row - of the softmax-weighted mix of the feature
 //                          layers first for the input projections - written as the hi / lo operand pair
 //   xatglu_split_kernel    the first-order xATGLU gate ((atan z + pi/2) / pi)(1 + 2a) - a times the value
@@ -15,7 +16,8 @@
 //   trunk_attn_kernel      softmax(q k^T / sqrt(dh) + bias) v per (question, head) with the trunk's masks built from
 //                          group ids instead of an (N, h, P, T) bias tensor: same-option bonus + key padding (the
 //                          self-attention over option tokens), key padding (the cross-attention to the question),
-//                          keys of the query's own option only (the CLS readout); RoPE of q / k applied as they load
+//                          keys of the query's own option only (the CLS readout); a SIMT flash attention in fp32
+//                          with 4 x 4 register tiles, K / V streamed through shared memory by cp.async
 // Every wait of the GEMM is bounded: a time-out records an error code in the device error word and ends the kernel.
 #include <cudaTypedefs.h>
 #include <math.h>
